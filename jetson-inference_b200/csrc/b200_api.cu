@@ -1,0 +1,95 @@
+// C-ABI wrappers of the engine building blocks (include/jinf/b200.h).
+#include "jinf/b200.h"
+#include "jinf/quant.h"
+
+#include "attn_f16.h"
+#include "common.cuh"
+#include "gemv_q4t.h"
+#include "q4t.cuh"
+
+using namespace jinf;
+
+static int device_sms() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+extern "C" uint64_t jinf_b200_q4t_bytes(int rows, int cols) {
+    Q4TShape sh;
+    return q4t_shape(rows, cols, &sh) ? sh.bytes : 0;
+}
+
+extern "C" jinf_status jinf_b200_q4t_pack(const void* aos, void* q4t, int rows, int cols, cudaStream_t stream) {
+    Q4TShape sh;
+    if (!aos || !q4t || !q4t_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    return q4t_repack(aos, q4t, sh, stream) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
+extern "C" jinf_status jinf_b200_gemv_q4t(const void* q4t, const void* x, int x_type, float* y, int rows, int cols,
+                                          cudaStream_t stream) {
+    Q4TShape sh;
+    if (!q4t || !x || !y || !q4t_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
+    GemvParams p{};
+    gemv_params_for(p, q4t, sh);
+    p.x = x;
+    p.y = y;
+    const int xm = x_type == JINF_TYPE_F32 ? X_PLAIN_F32 : X_PLAIN_F16;
+    const int grid = gemv_grid(p, xm, EPI_STORE, device_sms());
+    return gemv_launch(p, xm, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
+extern "C" jinf_status jinf_b200_gemv_q4t_rmsnorm(const void* q4t, const float* h, const float* gain, float eps,
+                                                  float* y, int rows, int cols, cudaStream_t stream) {
+    Q4TShape sh;
+    if (!q4t || !h || !gain || !y || !q4t_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    GemvParams p{};
+    gemv_params_for(p, q4t, sh);
+    p.hin = h;
+    p.norm_w = gain;
+    p.eps = eps;
+    p.y = y;
+    const int grid = gemv_grid(p, X_RMSNORM, EPI_STORE, device_sms());
+    return gemv_launch(p, X_RMSNORM, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
+extern "C" size_t jinf_b200_attention_workspace_bytes(int n_kv_heads, int head_dim, int max_ctx) {
+    int n_split = (max_ctx + 63) / 64;
+    if (n_split < 1) n_split = 1;
+    if (n_split > 64) n_split = 64;
+    return sizeof(DeviceState) + 256 + sizeof(float) * attn_partial_floats(n_kv_heads, n_split, head_dim);
+}
+
+extern "C" jinf_status jinf_b200_attention_f16(float* out, const float* q, const void* k_cache, const void* v_cache,
+                                               int head_dim, int n_heads, int n_kv_heads, int n_pos, int max_ctx,
+                                               void* workspace, cudaStream_t stream) {
+    if (!out || !q || !k_cache || !v_cache || !workspace || n_pos <= 0 || n_pos > max_ctx || n_heads <= 0 ||
+        n_kv_heads <= 0 || n_heads % n_kv_heads || n_kv_heads > 64 || n_heads / n_kv_heads > 8)
+        return JINF_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128) return JINF_ERR_INVALID;
+    int n_split = (max_ctx + 63) / 64;
+    if (n_split < 1) n_split = 1;
+    if (n_split > 64) n_split = 64;
+    DeviceState* st = (DeviceState*)workspace;
+    const int pos = n_pos - 1;
+    if (cudaMemcpyAsync(&st->pos, &pos, sizeof(int), cudaMemcpyHostToDevice, stream) != cudaSuccess)
+        return JINF_ERR_CUDA;
+    AttnParams p{};
+    p.q = q;
+    p.kcache = (const __half*)k_cache;
+    p.vcache = (const __half*)v_cache;
+    p.out = out;
+    p.partial = (float*)((uint8_t*)workspace + ((sizeof(DeviceState) + 255) & ~(size_t)255));
+    p.n_heads = n_heads;
+    p.n_kv_heads = n_kv_heads;
+    p.head_dim = head_dim;
+    p.max_ctx = max_ctx;
+    p.n_split = n_split;
+    p.st = st;
+    const cudaError_t e = attn_launch(p, stream, false);
+    // the host value of `pos` must stay alive until the copy has been issued: it is a
+    // pageable source, which cudaMemcpyAsync stages before returning.
+    return e == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}

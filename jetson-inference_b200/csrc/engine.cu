@@ -1,0 +1,1116 @@
+// The B200 decode engine behind the reference's jinf_engine_* API
+// (reference src/engine.cpp:41-804, include/jinf/engine.h:161-176).
+//
+// Per token and per layer the reference issues 16 stream operations (7 GEMVs, 2
+// RMSNorms, RoPE, 2 KV memcpys, attention, SiLU-mul, 2 residual adds,
+// reference src/engine.cpp:418-511). Here a layer is 5 fused kernels:
+//   1. QKV GEMV   prologue: h = h + y_down (residual), RMSNorm(attn_norm)
+//                 epilogue: RoPE(q,k) at pos, q -> fp32, k/v -> fp16 KV cache
+//   2. attention  split-K GQA over positions 0..pos
+//   3. o GEMV     -> y_o                       (tensor parallel: allreduce y_o)
+//   4. gate|up    prologue: h = h + y_o, RMSNorm(ffn_norm); epilogue: silu(g)*u
+//   5. down GEMV  -> y_down                    (tensor parallel: allreduce y_down)
+// then LM head (prologue: final residual + output_norm; epilogue: logits + argmax) and
+// a 1-thread finalize (argmax -> token, pos++). The whole step is captured once as a
+// CUDA graph and replayed every token: the position and the token live in device
+// memory. Residual adds are folded into the next prologue (ping-pong h buffers), so the
+// reference's fp32 order "h += proj; rmsnorm(h)" is kept exactly.
+//
+// Weights: every projection is repacked (losslessly) into the Q4T layout in one HBM
+// arena laid out in consumption order; each GEMV prefetches the next matrix into L2
+// (cp.async.bulk.prefetch.L2) before it waits on its inputs, so HBM keeps streaming
+// across kernel boundaries.
+#include "jinf/engine.h"
+#include "jinf/kernels.h"
+#include "jinf/quant.h"
+#include "jinf/splitter.h"
+
+#include "attn_f16.h"
+#include "common.cuh"
+#include "gemv_q4t.h"
+#include "nccl_shim.h"
+#include "q4t.cuh"
+#include "synth_internal.h"
+
+#include <fcntl.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <memory>
+#include <string>
+#include <vector>
+
+using namespace jinf;
+
+// ------------------------------------------------------------------ model sources
+
+namespace {
+
+struct TensorMeta {
+    int type = -1;
+    int n_dims = 0;
+    int64_t shape[4] = {1, 1, 1, 1};
+    int64_t rows() const { return n_dims > 1 ? shape[1] : 1; }
+    int64_t cols() const { return shape[0]; }
+    uint64_t row_bytes() const { return jinf_tensor_nbytes((jinf_qtype)type, cols()); }
+};
+
+// Host-side view of a model: tensor metadata + row reads in file (AoS) layout.
+struct ModelSource {
+    virtual ~ModelSource() {}
+    virtual bool meta(const char* name, TensorMeta* m) const = 0;
+    virtual jinf_status read_rows(const char* name, int64_t row0, int64_t n, void* dst) const = 0;
+    // Optional device-side generation (synthetic models): Q4_0 rows [r0, r0+nr) x columns
+    // [c0, c0+nc) into device rows dst_row0 + i*dst_step of pitch dst_row_bytes, or the
+    // whole f32 tensor. Return false when the source has no device path.
+    virtual bool device_q4_0(const char*, int64_t, int64_t, int64_t, int64_t, uint8_t*, int64_t, int64_t, int64_t,
+                             cudaStream_t, jinf_status*) const { return false; }
+    virtual bool device_f32(const char*, float*, cudaStream_t, jinf_status*) const { return false; }
+    jinf_model_hparams hp{};
+    int primary_type = JINF_TYPE_Q4_0;
+};
+
+struct SynthSource : ModelSource {
+    const jinf_synth_model* m;
+    explicit SynthSource(const jinf_synth_model* mm) : m(mm) {
+        hp = jinf_synth_get_config(m)->hp;
+        primary_type = jinf_synth_get_config(m)->weight_type;
+    }
+    bool meta(const char* name, TensorMeta* t) const override {
+        uint64_t nbytes;
+        return jinf_synth_tensor_info(m, name, &t->type, t->shape, &t->n_dims, &nbytes) == JINF_OK;
+    }
+    jinf_status read_rows(const char* name, int64_t row0, int64_t n, void* dst) const override {
+        return jinf_synth_read_rows(m, name, row0, n, dst);
+    }
+    bool device_q4_0(const char* name, int64_t r0, int64_t nr, int64_t c0, int64_t nc, uint8_t* dst,
+                     int64_t dst_row_bytes, int64_t dst_row0, int64_t dst_step, cudaStream_t s,
+                     jinf_status* st) const override {
+        uint64_t key;
+        float stdv;
+        int role;
+        TensorMeta t;
+        if (!synth_tensor_params(m, name, &key, &stdv, &role) || !meta(name, &t) || t.type != JINF_TYPE_Q4_0)
+            return false;
+        *st = synth_fill_q4_0(key, stdv, t.cols(), r0, nr, c0, nc, dst, dst_row_bytes, dst_row0, dst_step, s) ==
+                      cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+        return true;
+    }
+    bool device_f32(const char* name, float* dst, cudaStream_t s, jinf_status* st) const override {
+        uint64_t key;
+        float stdv;
+        int role;
+        TensorMeta t;
+        if (!synth_tensor_params(m, name, &key, &stdv, &role) || !meta(name, &t) || t.type != JINF_TYPE_F32)
+            return false;
+        const int64_t n = t.rows() * t.cols();
+        cudaError_t e = role == 1 ? fill_f32(dst, n, 1.0f, s) : synth_fill_f32(key, stdv, t.cols(), 0, t.rows(), dst, s);
+        *st = e == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+        return true;
+    }
+};
+
+struct NvmwSource : ModelSource {
+    jinf_nvmw_reader* r = nullptr;
+    int fd = -1;
+    ~NvmwSource() override {
+        if (fd >= 0) close(fd);
+        if (r) jinf_nvmw_close(r);
+    }
+    bool meta(const char* name, TensorMeta* t) const override {
+        const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, name);
+        if (!te) return false;
+        t->type = te->type;
+        t->n_dims = (int)te->n_dims;
+        for (int i = 0; i < 4; ++i) t->shape[i] = i < (int)te->n_dims ? te->shape[i] : 1;
+        return true;
+    }
+    jinf_status read_rows(const char* name, int64_t row0, int64_t n, void* dst) const override {
+        const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, name);
+        if (!te) return JINF_ERR_INVALID;
+        TensorMeta t;
+        meta(name, &t);
+        const uint64_t rb = t.row_bytes();
+        if ((uint64_t)(row0 + n) * rb > te->n_bytes) return JINF_ERR_PARSE;
+        uint64_t off = jinf_nvmw_tensor_file_offset(r, te) + (uint64_t)row0 * rb;
+        uint64_t left = (uint64_t)n * rb;
+        uint8_t* p = (uint8_t*)dst;
+        while (left) {
+            const ssize_t got = pread(fd, p, left > (1u << 30) ? (1u << 30) : left, (off_t)off);
+            if (got <= 0) return JINF_ERR_IO;
+            p += got;
+            off += (uint64_t)got;
+            left -= (uint64_t)got;
+        }
+        return JINF_OK;
+    }
+};
+
+jinf_status open_nvmw_source(const char* path, std::unique_ptr<ModelSource>* out) {
+    auto s = std::make_unique<NvmwSource>();
+    JINF_CHECK(jinf_nvmw_open(&s->r, path), "open .nvmw");
+    const jinf_nvmw_header* h = jinf_nvmw_get_header(s->r);
+    s->fd = open(path, O_RDONLY);
+    if (s->fd < 0) return JINF_ERR_IO;
+    memset(&s->hp, 0, sizeof s->hp);
+    strcpy(s->hp.arch, "llama");
+    s->hp.n_layers = h->n_layers;
+    s->hp.n_embd = h->n_embd;
+    s->hp.n_heads = h->n_heads;
+    s->hp.n_heads_kv = h->n_heads_kv ? h->n_heads_kv : h->n_heads;
+    s->hp.n_ff = h->n_ff;
+    s->hp.n_vocab = h->n_vocab;
+    s->hp.n_ctx_train = h->n_ctx_train;
+    s->hp.rope_freq_base = h->rope_freq_base;
+    s->hp.rms_norm_eps = h->rms_norm_eps;
+    s->primary_type = h->primary_type;
+    *out = std::move(s);
+    return JINF_OK;
+}
+
+// ------------------------------------------------------------------ small kernels
+
+__global__ void k_finalize(DeviceState* st, int with_argmax) {
+    if (with_argmax) {
+        const unsigned long long b = st->best;
+        st->argmax_token = b ? (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull)) : 0;
+        st->token = st->argmax_token;
+        st->best = 0ull;
+    }
+    st->pos += 1;
+}
+
+__global__ void k_fill_kv_random(__half* k, __half* v, int n_layers, int hkv, int max_ctx, int hd, int n_pos,
+                                 unsigned long long seed) {
+    const int64_t total = (int64_t)n_layers * hkv * n_pos * hd;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t d = i % hd;
+        int64_t r = i / hd;
+        const int64_t p = r % n_pos;
+        r /= n_pos;  // = layer * hkv + head
+        const size_t off = ((size_t)r * max_ctx + p) * hd + d;
+        // two uniforms from a counter hash, Box-Muller
+        unsigned long long z = seed + 0x9E3779B97F4A7C15ull * (unsigned long long)(2 * i + 1);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        z ^= z >> 31;
+        const float u1 = ((float)(z >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        const float u2 = ((float)((z >> 16) & 0xFFFFFF) + 0.5f) * (1.0f / 16777216.0f);
+        const float rr = sqrtf(-2.0f * logf(u1));
+        float s, c;
+        sincospif(2.0f * u2, &s, &c);
+        k[off] = __float2half(rr * c);
+        v[off] = __float2half(rr * s);
+    }
+}
+
+__global__ void k_even_rows(const float* in, float* out, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = in[2 * i];
+}
+
+
+enum OpKind { OP_GEMV = 0, OP_ATTN = 1, OP_ALLREDUCE_F32 = 2, OP_ALLREDUCE_MAXU64 = 3, OP_FINALIZE = 4 };
+enum GemvRole { ROLE_QKV = 0, ROLE_O = 1, ROLE_GATEUP = 2, ROLE_DOWN = 3, ROLE_LM = 4, ROLE_NONE = 5 };
+
+struct Op {
+    int kind;
+    int role = ROLE_NONE;
+    int layer = -1;
+    GemvParams gp{};
+    int xm = 0, epi = 0, grid = 1;
+    AttnParams ap{};
+    void* buf = nullptr;
+    size_t count = 0;
+    int with_argmax = 0;
+    uint64_t bytes = 0;  // algorithmic bytes of the op (weights + vectors)
+};
+
+}  // namespace
+
+struct jinf_engine_impl {
+    int device = 0;
+    int tp_rank = 0, tp_size = 1;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    bool use_graph = true;
+    int eos = 2;
+    // global and local dims
+    int d = 0, hd = 0, H = 0, Hkv = 0, ff = 0, V = 0, L = 0;
+    int Hl = 0, Hkvl = 0, ffl = 0, Vl = 0, vocab_off = 0;
+    float eps = 1e-5f, rope_base = 10000.f;
+    int max_ctx = 0;
+    // weights
+    uint8_t* arena = nullptr;
+    uint64_t arena_bytes = 0;
+    uint64_t weight_bytes_token = 0;  // algorithmic quantized bytes per token (this rank)
+    struct Layer {
+        uint8_t* qkv; Q4TShape qkv_sh;
+        uint8_t* o; Q4TShape o_sh;
+        uint8_t* gu; Q4TShape gu_sh;
+        uint8_t* down; Q4TShape down_sh;
+        float* attn_norm;
+        float* ffn_norm;
+    };
+    std::vector<Layer> layers;
+    uint8_t* lm = nullptr;
+    Q4TShape lm_sh{};
+    float* out_norm = nullptr;
+    float* norms = nullptr;  // all norm gains
+    float* embed = nullptr;  // [V][d] f32
+    // KV cache [L][Hkvl][max_ctx][hd] fp16
+    __half* kc = nullptr;
+    __half* vc = nullptr;
+    // activations
+    float* hA = nullptr;
+    float* hB = nullptr;
+    float* y_o = nullptr;
+    float* y_down = nullptr;
+    float* q = nullptr;
+    float* attn = nullptr;
+    float* act = nullptr;
+    float* gate_raw = nullptr;  // FFN hook buffer
+    float* logits = nullptr;    // local shard [Vl]
+    float* logits_full = nullptr;  // [V] (== logits when tp_size == 1)
+    float* attn_partial = nullptr;
+    int n_split = 1;
+    DeviceState* st = nullptr;
+    int32_t* pinned = nullptr;  // [0] token in, [1] token out
+    int32_t* dev_tokens = nullptr;  // prompt tokens of the current forward() [max_ctx]
+    // ops and graphs
+    std::vector<Op> ops_full, ops_body;
+    cudaGraphExec_t exec_full = nullptr, exec_body = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    ncclComm_t comm = nullptr;
+    bool logits_valid = false;
+};
+
+namespace {
+
+jinf_status run_op(jinf_engine_impl* I, const Op& op, cudaStream_t s) {
+    cudaError_t e = cudaSuccess;
+    switch (op.kind) {
+        case OP_GEMV: e = gemv_launch(op.gp, op.xm, op.epi, op.grid, s, true); break;
+        case OP_ATTN: e = attn_launch(op.ap, s, true); break;
+        case OP_FINALIZE: k_finalize<<<1, 1, 0, s>>>(I->st, op.with_argmax); e = cudaGetLastError(); break;
+        case OP_ALLREDUCE_F32:
+        case OP_ALLREDUCE_MAXU64: {
+            const NcclApi* n = nccl_api();
+            if (!n || !I->comm) return JINF_ERR_CUDA;
+            const ncclResult_t r =
+                op.kind == OP_ALLREDUCE_F32
+                    ? n->AllReduce(op.buf, op.buf, op.count, ncclFloat32, ncclSum, I->comm, s)
+                    : n->AllReduce(op.buf, op.buf, op.count, ncclUint64, ncclMax, I->comm, s);
+            if (r != ncclSuccess) {
+                JINF_LOG("NCCL allreduce failed: %s", n->GetErrorString(r));
+                return JINF_ERR_CUDA;
+            }
+            break;
+        }
+        default: return JINF_ERR_INVALID;
+    }
+    if (e != cudaSuccess) {
+        JINF_LOG("launch failed (op %d): %s", op.kind, cudaGetErrorString(e));
+        return JINF_ERR_CUDA;
+    }
+    return JINF_OK;
+}
+
+jinf_status run_ops(jinf_engine_impl* I, const std::vector<Op>& ops, cudaStream_t s) {
+    for (const Op& op : ops) JINF_CHECK(run_op(I, op, s), "step op");
+    return JINF_OK;
+}
+
+jinf_status capture(jinf_engine_impl* I, const std::vector<Op>& ops, cudaGraphExec_t* exec) {
+    cudaGraph_t g = nullptr;
+    JINF_CUDA_CHECK(cudaStreamBeginCapture(I->stream, cudaStreamCaptureModeThreadLocal));
+    jinf_status st = run_ops(I, ops, I->stream);
+    cudaError_t e = cudaStreamEndCapture(I->stream, &g);
+    if (st != JINF_OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    JINF_CUDA_CHECK(e);
+    e = cudaGraphInstantiate(exec, g, 0);
+    cudaGraphDestroy(g);
+    JINF_CUDA_CHECK(e);
+    return JINF_OK;
+}
+
+// Build the op list of one decode step. `with_head` adds the LM head + argmax.
+void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
+    ops.clear();
+    auto gemv_bytes = [](const Q4TShape& sh, int in_elems, int out_elems) -> uint64_t {
+        return (uint64_t)sh.rows * sh.nb * 18 + 4ull * in_elems + 4ull * out_elems;
+    };
+    for (int L = 0; L < I->L; ++L) {
+        const auto& ly = I->layers[L];
+        const auto* next_qkv = L + 1 < I->L ? &I->layers[L + 1] : nullptr;
+        Op qkv{OP_GEMV};
+        qkv.role = ROLE_QKV;
+        qkv.layer = L;
+        gemv_params_for(qkv.gp, ly.qkv, ly.qkv_sh);
+        qkv.xm = L == 0 ? X_EMBED_NORM : X_RMSNORM;
+        qkv.epi = EPI_QKV;
+        qkv.gp.hin = I->hB;
+        qkv.gp.yres = L == 0 ? nullptr : I->y_down;
+        qkv.gp.hout = I->hA;
+        qkv.gp.embed = I->embed;
+        qkv.gp.norm_w = ly.attn_norm;
+        qkv.gp.eps = I->eps;
+        qkv.gp.y = I->q;
+        qkv.gp.kcache = I->kc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        qkv.gp.vcache = I->vc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        qkv.gp.nq = I->Hl * I->hd;
+        qkv.gp.nk = I->Hkvl * I->hd;
+        qkv.gp.head_dim = I->hd;
+        qkv.gp.max_ctx = I->max_ctx;
+        qkv.gp.rope_base = I->rope_base;
+        qkv.gp.st = I->st;
+        qkv.gp.pf_ptr = ly.o;
+        qkv.gp.pf_bytes = ly.o_sh.bytes;
+        qkv.grid = gemv_grid(qkv.gp, qkv.xm, qkv.epi, I->num_sms);
+        qkv.bytes = gemv_bytes(ly.qkv_sh, I->d, ly.qkv_sh.rows);
+        ops.push_back(qkv);
+
+        Op at{OP_ATTN};
+        at.layer = L;
+        at.ap.q = I->q;
+        at.ap.kcache = qkv.gp.kcache;
+        at.ap.vcache = qkv.gp.vcache;
+        at.ap.out = I->attn;
+        at.ap.partial = I->attn_partial;
+        at.ap.n_heads = I->Hl;
+        at.ap.n_kv_heads = I->Hkvl;
+        at.ap.head_dim = I->hd;
+        at.ap.max_ctx = I->max_ctx;
+        at.ap.n_split = I->n_split;
+        at.ap.st = I->st;
+        ops.push_back(at);
+
+        Op o{OP_GEMV};
+        o.role = ROLE_O;
+        o.layer = L;
+        gemv_params_for(o.gp, ly.o, ly.o_sh);
+        o.xm = X_PLAIN_F32;
+        o.epi = EPI_STORE;
+        o.gp.x = I->attn;
+        o.gp.y = I->y_o;
+        o.gp.st = I->st;
+        o.gp.pf_ptr = ly.gu;
+        o.gp.pf_bytes = ly.gu_sh.bytes;
+        o.grid = gemv_grid(o.gp, o.xm, o.epi, I->num_sms);
+        o.bytes = gemv_bytes(ly.o_sh, ly.o_sh.cols, ly.o_sh.rows);
+        ops.push_back(o);
+        if (I->tp_size > 1) {
+            Op ar{OP_ALLREDUCE_F32};
+            ar.buf = I->y_o;
+            ar.count = (size_t)I->d;
+            ops.push_back(ar);
+        }
+
+        Op gu{OP_GEMV};
+        gu.role = ROLE_GATEUP;
+        gu.layer = L;
+        gemv_params_for(gu.gp, ly.gu, ly.gu_sh);
+        gu.xm = X_RMSNORM;
+        gu.epi = EPI_GATEUP;
+        gu.gp.hin = I->hA;
+        gu.gp.yres = I->y_o;
+        gu.gp.hout = I->hB;
+        gu.gp.norm_w = ly.ffn_norm;
+        gu.gp.eps = I->eps;
+        gu.gp.y = I->act;
+        gu.gp.st = I->st;
+        gu.gp.pf_ptr = ly.down;
+        gu.gp.pf_bytes = ly.down_sh.bytes;
+        gu.grid = gemv_grid(gu.gp, gu.xm, gu.epi, I->num_sms);
+        gu.bytes = gemv_bytes(ly.gu_sh, I->d, ly.gu_sh.rows / 2);
+        ops.push_back(gu);
+
+        Op dn{OP_GEMV};
+        dn.role = ROLE_DOWN;
+        dn.layer = L;
+        gemv_params_for(dn.gp, ly.down, ly.down_sh);
+        dn.xm = X_PLAIN_F32;
+        dn.epi = EPI_STORE;
+        dn.gp.x = I->act;
+        dn.gp.y = I->y_down;
+        dn.gp.st = I->st;
+        if (next_qkv) {
+            dn.gp.pf_ptr = next_qkv->qkv;
+            dn.gp.pf_bytes = next_qkv->qkv_sh.bytes;
+        } else if (with_head) {
+            dn.gp.pf_ptr = I->lm;
+            dn.gp.pf_bytes = I->lm_sh.bytes;
+        }
+        dn.grid = gemv_grid(dn.gp, dn.xm, dn.epi, I->num_sms);
+        dn.bytes = gemv_bytes(ly.down_sh, ly.down_sh.cols, ly.down_sh.rows);
+        ops.push_back(dn);
+        if (I->tp_size > 1) {
+            Op ar{OP_ALLREDUCE_F32};
+            ar.buf = I->y_down;
+            ar.count = (size_t)I->d;
+            ops.push_back(ar);
+        }
+    }
+    if (with_head) {
+        Op lm{OP_GEMV};
+        lm.role = ROLE_LM;
+        gemv_params_for(lm.gp, I->lm, I->lm_sh);
+        lm.xm = X_RMSNORM;
+        lm.epi = EPI_LMHEAD;
+        lm.gp.hin = I->hB;
+        lm.gp.yres = I->y_down;
+        lm.gp.hout = nullptr;
+        lm.gp.norm_w = I->out_norm;
+        lm.gp.eps = I->eps;
+        lm.gp.y = I->logits;
+        lm.gp.vocab_offset = I->vocab_off;
+        lm.gp.st = I->st;
+        lm.gp.pf_ptr = I->layers[0].qkv;
+        lm.gp.pf_bytes = I->layers[0].qkv_sh.bytes;
+        lm.grid = gemv_grid(lm.gp, lm.xm, lm.epi, I->num_sms);
+        lm.bytes = gemv_bytes(I->lm_sh, I->d, I->lm_sh.rows);
+        ops.push_back(lm);
+        if (I->tp_size > 1) {
+            Op ar{OP_ALLREDUCE_MAXU64};
+            ar.buf = &I->st->best;
+            ar.count = 1;
+            ops.push_back(ar);
+        }
+    }
+    Op fin{OP_FINALIZE};
+    fin.with_argmax = with_head ? 1 : 0;
+    ops.push_back(fin);
+}
+
+// ---------------------------------------------------------------- loading
+
+struct Loader {
+    jinf_engine_impl* I;
+    const ModelSource* src;
+    std::vector<uint8_t> host;  // AoS staging on the host
+    uint8_t* dstage = nullptr;  // AoS staging on the device
+    size_t dstage_bytes = 0;
+
+    ~Loader() {
+        if (dstage) cudaFree(dstage);
+    }
+
+    jinf_status ensure_dstage(size_t n) {
+        if (n <= dstage_bytes) return JINF_OK;
+        if (dstage) cudaFree(dstage);
+        dstage = nullptr;
+        JINF_CUDA_CHECK(cudaMalloc(&dstage, n));
+        dstage_bytes = n;
+        return JINF_OK;
+    }
+
+    // Stage rows [r0, r0+nr) x columns [c0, c0+nc) of Q4_0 tensor `name` as AoS blocks into
+    // the device staging buffer, row i at staging row dst_row0 + i*dst_step (pitch
+    // dst_row_bytes). Synthetic models are generated in place on the device; files are
+    // read on the host and copied with one pitched copy.
+    jinf_status stage(const char* name, int64_t r0, int64_t nr, int64_t c0, int64_t nc, int64_t dst_row_bytes,
+                      int64_t dst_row0, int64_t dst_step) {
+        TensorMeta m;
+        if (!src->meta(name, &m)) {
+            JINF_LOG("tensor %s missing", name);
+            return JINF_ERR_PARSE;
+        }
+        if (m.type != JINF_TYPE_Q4_0) {
+            JINF_LOG("tensor %s: type %s not supported by the B200 engine (Q4_0 required)", name,
+                     jinf_qtype_name((jinf_qtype)m.type));
+            return JINF_ERR_INVALID;
+        }
+        if (r0 < 0 || c0 < 0 || r0 + nr > m.rows() || c0 + nc > m.cols() || c0 % 32 || nc % 32) {
+            JINF_LOG("tensor %s: slice [%lld+%lld, %lld+%lld) out of range", name, (long long)r0, (long long)nr,
+                     (long long)c0, (long long)nc);
+            return JINF_ERR_INVALID;
+        }
+        jinf_status st = JINF_OK;
+        if (src->device_q4_0(name, r0, nr, c0, nc, dstage, dst_row_bytes, dst_row0, dst_step, I->stream, &st))
+            return st;
+        const uint64_t rb = m.row_bytes();
+        host.resize((size_t)(nr * rb));
+        JINF_CHECK(src->read_rows(name, r0, nr, host.data()), name);
+        JINF_CUDA_CHECK(cudaMemcpy2DAsync(dstage + dst_row0 * dst_row_bytes, (size_t)(dst_step * dst_row_bytes),
+                                          host.data() + (c0 / 32) * 18, (size_t)rb, (size_t)(nc / 32) * 18,
+                                          (size_t)nr, cudaMemcpyHostToDevice, I->stream));
+        JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));  // `host` is reused by the next call
+        return JINF_OK;
+    }
+
+    // Repack the staged AoS matrix into the arena.
+    jinf_status pack(uint8_t* dst, const Q4TShape& sh) {
+        JINF_CUDA_CHECK(q4t_repack(dstage, dst, sh, I->stream));
+        JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+        return JINF_OK;
+    }
+
+    jinf_status read_f32(const char* name, float* dst_dev, int64_t n_expect) {
+        TensorMeta m;
+        if (!src->meta(name, &m)) {
+            JINF_LOG("tensor %s missing", name);
+            return JINF_ERR_PARSE;
+        }
+        const int64_t n = m.rows() * m.cols();
+        if (n != n_expect) {
+            JINF_LOG("tensor %s: %lld elements, expected %lld", name, (long long)n, (long long)n_expect);
+            return JINF_ERR_PARSE;
+        }
+        jinf_status dst_status = JINF_OK;
+        if (src->device_f32(name, dst_dev, I->stream, &dst_status)) {
+            if (dst_status == JINF_OK) JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+            return dst_status;
+        }
+        const uint64_t bytes = m.row_bytes() * (uint64_t)m.rows();
+        // read in slabs of rows to bound host memory
+        const int64_t rows = m.rows();
+        const int64_t slab = rows > 4096 ? 4096 : rows;
+        std::vector<uint8_t> buf((size_t)(slab * m.row_bytes()));
+        std::vector<float> f32;
+        for (int64_t r = 0; r < rows; r += slab) {
+            const int64_t nr = r + slab <= rows ? slab : rows - r;
+            JINF_CHECK(src->read_rows(name, r, nr, buf.data()), name);
+            const int64_t ne = nr * m.cols();
+            float* dst = dst_dev + r * m.cols();
+            if (m.type == JINF_TYPE_F32) {
+                JINF_CUDA_CHECK(cudaMemcpy(dst, buf.data(), (size_t)ne * 4, cudaMemcpyHostToDevice));
+            } else {
+                f32.resize((size_t)ne);
+                jinf_dequantize(buf.data(), (jinf_qtype)m.type, f32.data(), ne);
+                if (m.type != JINF_TYPE_F16 && m.type != JINF_TYPE_Q4_0 && m.type != JINF_TYPE_Q4_K &&
+                    m.type != JINF_TYPE_Q8_0 && m.type != JINF_TYPE_Q6_K) {
+                    JINF_LOG("tensor %s: unsupported type %d", name, m.type);
+                    return JINF_ERR_INVALID;
+                }
+                JINF_CUDA_CHECK(cudaMemcpy(dst, f32.data(), (size_t)ne * 4, cudaMemcpyHostToDevice));
+            }
+        }
+        (void)bytes;
+        return JINF_OK;
+    }
+};
+
+void free_impl(jinf_engine_impl* I) {
+    if (!I) return;
+    if (I->device >= 0) cudaSetDevice(I->device);
+    if (I->exec_full) cudaGraphExecDestroy(I->exec_full);
+    if (I->exec_body) cudaGraphExecDestroy(I->exec_body);
+    if (I->comm) {
+        const NcclApi* n = nccl_api();
+        if (n) n->CommDestroy(I->comm);
+    }
+    void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
+                    I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);
+    if (I->pinned) cudaFreeHost(I->pinned);
+    if (I->ev0) cudaEventDestroy(I->ev0);
+    if (I->ev1) cudaEventDestroy(I->ev1);
+    if (I->stream) cudaStreamDestroy(I->stream);
+    delete I;
+}
+
+jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg, const ModelSource& src,
+                               const jinf_b200_options* opt_in) {
+    jinf_b200_options opt = opt_in ? *opt_in : jinf_b200_options_default();
+    const jinf_model_hparams& hp = src.hp;
+    if (hp.n_layers == 0 || hp.n_embd == 0 || hp.n_heads == 0 || hp.n_ff == 0 || hp.n_vocab == 0) {
+        JINF_LOG("model hyper-parameters incomplete");
+        return JINF_ERR_PARSE;
+    }
+    const int tp = opt.tp_size > 0 ? opt.tp_size : 1;
+    const int hkv = hp.n_heads_kv ? (int)hp.n_heads_kv : (int)hp.n_heads;
+    if ((int)hp.n_heads % tp || hkv % tp || (int)hp.n_ff % tp || (int)hp.n_vocab % tp || opt.tp_rank < 0 ||
+        opt.tp_rank >= tp) {
+        JINF_LOG("tensor-parallel size %d does not divide the model (heads %u/%d, ff %u, vocab %u)", tp, hp.n_heads,
+                 hkv, hp.n_ff, hp.n_vocab);
+        return JINF_ERR_INVALID;
+    }
+    if (cfg->max_context <= 0) return JINF_ERR_INVALID;
+    if (opt.kv_type != JINF_TYPE_F16) {
+        JINF_LOG("only the fp16 KV cache is implemented on B200");
+        return JINF_ERR_INVALID;
+    }
+
+    jinf_engine_impl* I = new jinf_engine_impl();
+    I->device = opt.device;
+    I->tp_rank = opt.tp_rank;
+    I->tp_size = tp;
+    I->use_graph = opt.use_graph != 0;
+    I->eos = opt.eos_token;
+    I->d = (int)hp.n_embd;
+    I->H = (int)hp.n_heads;
+    I->Hkv = hkv;
+    I->hd = I->d / I->H;
+    I->ff = (int)hp.n_ff;
+    I->V = (int)hp.n_vocab;
+    I->L = (int)hp.n_layers;
+    I->Hl = I->H / tp;
+    I->Hkvl = I->Hkv / tp;
+    I->ffl = I->ff / tp;
+    I->Vl = I->V / tp;
+    I->vocab_off = I->Vl * opt.tp_rank;
+    I->eps = hp.rms_norm_eps;
+    I->rope_base = hp.rope_freq_base;
+    I->max_ctx = cfg->max_context;
+    auto fail = [&](jinf_status s) {
+        free_impl(I);
+        return s;
+    };
+    if (I->hd != 64 && I->hd != 128) {
+        JINF_LOG("head_dim %d not supported (64 or 128)", I->hd);
+        return fail(JINF_ERR_INVALID);
+    }
+    if (I->H / I->Hkv > 8) {
+        JINF_LOG("more than 8 query heads per kv head are not supported");
+        return fail(JINF_ERR_INVALID);
+    }
+    if (cudaSetDevice(I->device) != cudaSuccess) {
+        JINF_LOG("cannot select CUDA device %d", I->device);
+        return fail(JINF_ERR_CUDA);
+    }
+    cudaDeviceGetAttribute(&I->num_sms, cudaDevAttrMultiProcessorCount, I->device);
+    if (cudaStreamCreateWithFlags(&I->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(JINF_ERR_CUDA);
+    cudaEventCreate(&I->ev0);
+    cudaEventCreate(&I->ev1);
+
+    // ---- shapes and arena layout (consumption order)
+    const int d = I->d, hd = I->hd;
+    const int qkv_rows = (I->Hl + 2 * I->Hkvl) * hd;
+    I->layers.resize(I->L);
+    uint64_t off = 0;
+    auto place = [&](Q4TShape& sh, int rows, int cols, uint8_t*& ptr) -> bool {
+        if (!q4t_shape(rows, cols, &sh)) return false;
+        ptr = (uint8_t*)(uintptr_t)off;  // offset for now
+        off += (sh.bytes + 255) & ~255ull;
+        I->weight_bytes_token += (uint64_t)rows * (cols / 32) * 18;
+        return true;
+    };
+    for (int L = 0; L < I->L; ++L) {
+        auto& ly = I->layers[L];
+        if (!place(ly.qkv_sh, qkv_rows, d, ly.qkv) || !place(ly.o_sh, d, I->Hl * hd, ly.o) ||
+            !place(ly.gu_sh, 2 * I->ffl, d, ly.gu) || !place(ly.down_sh, d, I->ffl, ly.down)) {
+            JINF_LOG("matrix shapes not supported by the Q4T layout (columns must be multiples of 128)");
+            return fail(JINF_ERR_INVALID);
+        }
+    }
+    if (!place(I->lm_sh, I->Vl, d, I->lm)) return fail(JINF_ERR_INVALID);
+    I->arena_bytes = off;
+    if (cudaMalloc(&I->arena, I->arena_bytes) != cudaSuccess) {
+        JINF_LOG("cannot allocate %.1f MB of weights", I->arena_bytes / 1048576.0);
+        return fail(JINF_ERR_OOM);
+    }
+    for (auto& ly : I->layers) {
+        ly.qkv = I->arena + (uintptr_t)ly.qkv;
+        ly.o = I->arena + (uintptr_t)ly.o;
+        ly.gu = I->arena + (uintptr_t)ly.gu;
+        ly.down = I->arena + (uintptr_t)ly.down;
+    }
+    I->lm = I->arena + (uintptr_t)I->lm;
+
+    // ---- other buffers
+    const size_t kv_elems = (size_t)I->L * I->Hkvl * I->max_ctx * hd;
+    I->n_split = (I->max_ctx + 63) / 64;
+    const int max_split = (2 * I->num_sms) / I->Hkvl;
+    if (I->n_split > max_split) I->n_split = max_split;
+    if (I->n_split < 1) I->n_split = 1;
+    bool ok = cudaMalloc(&I->norms, sizeof(float) * (size_t)(2 * I->L + 1) * d) == cudaSuccess &&
+              cudaMalloc(&I->embed, sizeof(float) * (size_t)I->V * d) == cudaSuccess &&
+              cudaMalloc(&I->kc, sizeof(__half) * kv_elems) == cudaSuccess &&
+              cudaMalloc(&I->vc, sizeof(__half) * kv_elems) == cudaSuccess &&
+              cudaMalloc(&I->hA, sizeof(float) * d) == cudaSuccess &&
+              cudaMalloc(&I->hB, sizeof(float) * d) == cudaSuccess &&
+              cudaMalloc(&I->y_o, sizeof(float) * d) == cudaSuccess &&
+              cudaMalloc(&I->y_down, sizeof(float) * d) == cudaSuccess &&
+              cudaMalloc(&I->q, sizeof(float) * (size_t)I->Hl * hd) == cudaSuccess &&
+              cudaMalloc(&I->attn, sizeof(float) * (size_t)I->Hl * hd) == cudaSuccess &&
+              cudaMalloc(&I->act, sizeof(float) * (size_t)I->ffl) == cudaSuccess &&
+              cudaMalloc(&I->logits, sizeof(float) * (size_t)I->Vl) == cudaSuccess &&
+              cudaMalloc(&I->attn_partial, sizeof(float) * attn_partial_floats(I->Hkvl, I->n_split, hd)) == cudaSuccess &&
+              cudaMalloc(&I->st, sizeof(DeviceState)) == cudaSuccess &&
+              cudaMalloc(&I->dev_tokens, sizeof(int32_t) * (size_t)I->max_ctx) == cudaSuccess &&
+              cudaHostAlloc(&I->pinned, 4 * sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
+    if (ok && tp > 1) ok = cudaMalloc(&I->logits_full, sizeof(float) * (size_t)I->V) == cudaSuccess;
+    if (!ok) return fail(JINF_ERR_OOM);
+    if (tp == 1) I->logits_full = I->logits;
+    cudaMemset(I->kc, 0, sizeof(__half) * kv_elems);
+    cudaMemset(I->vc, 0, sizeof(__half) * kv_elems);
+    cudaMemset(I->st, 0, sizeof(DeviceState));
+    cudaMemset(I->y_o, 0, sizeof(float) * d);
+    cudaMemset(I->y_down, 0, sizeof(float) * d);
+
+    // ---- load weights (per matrix: stage AoS rows in HBM, then repack into the arena)
+    {
+        Loader ld{I, &src};
+        size_t max_stage = 0;
+        for (const auto& ly : I->layers)
+            for (const Q4TShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh})
+                max_stage = std::max(max_stage, (size_t)sh->rows * sh->nb * 18);
+        max_stage = std::max(max_stage, (size_t)I->lm_sh.rows * I->lm_sh.nb * 18);
+        if (ld.ensure_dstage(max_stage) != JINF_OK) return fail(JINF_ERR_OOM);
+        const int64_t rb_d = (int64_t)(d / 32) * 18;  // AoS row bytes of a d-column matrix
+        char nm[128];
+        jinf_status s = JINF_OK;
+        for (int L = 0; L < I->L && s == JINF_OK; ++L) {
+            auto& ly = I->layers[L];
+            ly.attn_norm = I->norms + (size_t)(2 * L) * d;
+            ly.ffn_norm = I->norms + (size_t)(2 * L + 1) * d;
+            snprintf(nm, sizeof nm, "blk.%d.attn_norm.weight", L);
+            s = ld.read_f32(nm, ly.attn_norm, d);
+            if (s != JINF_OK) break;
+            snprintf(nm, sizeof nm, "blk.%d.ffn_norm.weight", L);
+            s = ld.read_f32(nm, ly.ffn_norm, d);
+            if (s != JINF_OK) break;
+            // QKV: this rank's q heads, then its k heads, then its v heads
+            const int64_t nq = (int64_t)I->Hl * hd, nk = (int64_t)I->Hkvl * hd;
+            snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", L);
+            s = ld.stage(nm, I->tp_rank * nq, nq, 0, d, rb_d, 0, 1);
+            if (s == JINF_OK) {
+                snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", L);
+                s = ld.stage(nm, I->tp_rank * nk, nk, 0, d, rb_d, nq, 1);
+            }
+            if (s == JINF_OK) {
+                snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", L);
+                s = ld.stage(nm, I->tp_rank * nk, nk, 0, d, rb_d, nq + nk, 1);
+            }
+            if (s == JINF_OK) s = ld.pack(ly.qkv, ly.qkv_sh);
+            // o: every output row, this rank's input columns (row split)
+            if (s == JINF_OK) {
+                snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", L);
+                s = ld.stage(nm, 0, d, I->tp_rank * nq, nq, (nq / 32) * 18, 0, 1);
+            }
+            if (s == JINF_OK) s = ld.pack(ly.o, ly.o_sh);
+            // gate|up interleaved by neuron: gate_n -> row 2n, up_n -> row 2n+1
+            if (s == JINF_OK) {
+                snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", L);
+                s = ld.stage(nm, (int64_t)I->tp_rank * I->ffl, I->ffl, 0, d, rb_d, 0, 2);
+            }
+            if (s == JINF_OK) {
+                snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", L);
+                s = ld.stage(nm, (int64_t)I->tp_rank * I->ffl, I->ffl, 0, d, rb_d, 1, 2);
+            }
+            if (s == JINF_OK) s = ld.pack(ly.gu, ly.gu_sh);
+            // down: every output row, this rank's neuron columns (row split)
+            if (s == JINF_OK) {
+                snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", L);
+                s = ld.stage(nm, 0, d, (int64_t)I->tp_rank * I->ffl, I->ffl, (int64_t)(I->ffl / 32) * 18, 0, 1);
+            }
+            if (s == JINF_OK) s = ld.pack(ly.down, ly.down_sh);
+        }
+        I->out_norm = I->norms + (size_t)(2 * I->L) * d;
+        if (s == JINF_OK) s = ld.read_f32("output_norm.weight", I->out_norm, d);
+        if (s == JINF_OK) s = ld.stage("output.weight", I->vocab_off, I->Vl, 0, d, rb_d, 0, 1);
+        if (s == JINF_OK) s = ld.pack(I->lm, I->lm_sh);
+        if (s == JINF_OK) s = ld.read_f32("token_embd.weight", I->embed, (int64_t)I->V * d);
+        if (s != JINF_OK) return fail(s);
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail(JINF_ERR_CUDA);
+
+    // ---- communicator
+    if (tp > 1) {
+        const NcclApi* n = nccl_api();
+        if (!n || !opt.nccl_id) {
+            JINF_LOG("tensor parallelism needs NCCL and a unique id");
+            return fail(n ? JINF_ERR_INVALID : JINF_ERR_CUDA);
+        }
+        ncclUniqueId id;
+        memcpy(&id, opt.nccl_id, sizeof id);
+        const ncclResult_t r = n->CommInitRank(&I->comm, tp, id, opt.tp_rank);
+        if (r != ncclSuccess) {
+            JINF_LOG("ncclCommInitRank failed: %s", n->GetErrorString(r));
+            I->comm = nullptr;
+            return fail(JINF_ERR_CUDA);
+        }
+    }
+
+    // ---- step programs
+    build_ops(I, true, I->ops_full);
+    build_ops(I, false, I->ops_body);
+    if (I->use_graph) {
+        jinf_status s = capture(I, I->ops_full, &I->exec_full);
+        if (s == JINF_OK) s = capture(I, I->ops_body, &I->exec_body);
+        if (s != JINF_OK) return fail(s);
+    }
+
+    jinf_engine* e = (jinf_engine*)calloc(1, sizeof(jinf_engine));
+    if (!e) return fail(JINF_ERR_OOM);
+    e->n_layers = I->L;
+    e->n_embd = I->d;
+    e->n_heads = I->H;
+    e->n_heads_kv = I->Hkv;
+    e->n_ff = I->ff;
+    e->n_vocab = I->V;
+    e->max_context = I->max_ctx;
+    e->head_dim = hd;
+    e->rms_norm_eps = I->eps;
+    e->rope_freq_base = I->rope_base;
+    e->primary_type = src.primary_type;
+    e->logits_buf = I->logits_full;
+    e->compute_stream = I->stream;
+    e->impl = I;
+    *out = e;
+    JINF_LOG("engine ready: %d layers, d=%d, heads %d/%d, ff=%d, vocab=%d, tp %d/%d, weights %.1f MB/rank, "
+             "attention splits %d",
+             I->L, I->d, I->H, I->Hkv, I->ff, I->V, I->tp_rank, tp, I->arena_bytes / 1048576.0, I->n_split);
+    return JINF_OK;
+}
+
+// One decode step for the token already in st->token (device).
+jinf_status step(jinf_engine* e, bool with_head) {
+    jinf_engine_impl* I = e->impl;
+    if (e->n_past >= I->max_ctx) {
+        JINF_LOG("context full (%d positions)", I->max_ctx);
+        return JINF_ERR_INVALID;
+    }
+    if (e->ffn_hook) {
+        // Layer-by-layer path that exposes the raw gate pre-activation of each layer.
+        const std::vector<Op>& ops = with_head ? I->ops_full : I->ops_body;
+        for (const Op& op : ops) {
+            Op o2 = op;
+            JINF_CHECK(run_op(I, o2, I->stream), "op");
+            if (op.kind == OP_GEMV && op.role == ROLE_GATEUP) {
+                // The fused kernel never materialises the raw gate. Re-run the same matrix
+                // as a plain GEMV: its prologue input is hB (= h after the o residual, which
+                // the fused kernel just stored), gate rows are the even interleaved rows.
+                if (!I->gate_raw) JINF_CUDA_CHECK(cudaMalloc(&I->gate_raw, sizeof(float) * 3 * (size_t)I->ffl));
+                GemvParams gp = op.gp;
+                gp.hin = I->hB;
+                gp.yres = nullptr;
+                gp.hout = nullptr;
+                gp.y = I->gate_raw + I->ffl;  // [2*ffl] interleaved gate/up
+                gp.pf_bytes = 0;
+                JINF_CUDA_CHECK(gemv_launch(gp, X_RMSNORM, EPI_STORE, op.grid, I->stream, false));
+                k_even_rows<<<(I->ffl + 255) / 256, 256, 0, I->stream>>>(I->gate_raw + I->ffl, I->gate_raw, I->ffl);
+                JINF_CUDA_CHECK(cudaGetLastError());
+                JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+                e->ffn_hook(e->ffn_hook_data, op.layer, I->gate_raw, I->ffl);
+            }
+        }
+    } else if (I->use_graph) {
+        JINF_CUDA_CHECK(cudaGraphLaunch(with_head ? I->exec_full : I->exec_body, I->stream));
+    } else {
+        JINF_CHECK(run_ops(I, with_head ? I->ops_full : I->ops_body, I->stream), "step");
+    }
+    e->n_past += 1;
+    return JINF_OK;
+}
+
+jinf_status gather_logits(jinf_engine* e) {
+    jinf_engine_impl* I = e->impl;
+    if (I->tp_size == 1) return JINF_OK;
+    const NcclApi* n = nccl_api();
+    if (!n) return JINF_ERR_CUDA;
+    if (n->AllGather(I->logits, I->logits_full, (size_t)I->Vl, ncclFloat32, I->comm, I->stream) != ncclSuccess)
+        return JINF_ERR_CUDA;
+    return JINF_OK;
+}
+
+}  // namespace
+
+// ================================================================== public API
+
+extern "C" jinf_status jinf_engine_create_ex(jinf_engine** e, const jinf_engine_config* config,
+                                             const jinf_b200_options* options) {
+    if (!e || !config || !config->model_path) return JINF_ERR_INVALID;
+    std::unique_ptr<ModelSource> src;
+    JINF_CHECK(open_nvmw_source(config->model_path, &src), "model");
+    return create_from_source(e, config, *src, options);
+}
+
+extern "C" jinf_status jinf_engine_create(jinf_engine** e, const jinf_engine_config* config) {
+    return jinf_engine_create_ex(e, config, nullptr);
+}
+
+extern "C" jinf_status jinf_engine_create_synthetic(jinf_engine** e, const jinf_engine_config* config,
+                                                    const jinf_synth_model* model, const jinf_b200_options* options) {
+    if (!e || !config || !model) return JINF_ERR_INVALID;
+    SynthSource src(model);
+    return create_from_source(e, config, src, options);
+}
+
+extern "C" void jinf_engine_destroy(jinf_engine* e) {
+    if (!e) return;
+    free_impl(e->impl);
+    free(e);
+}
+
+extern "C" void jinf_engine_reset(jinf_engine* e) {
+    if (!e || !e->impl) return;
+    jinf_engine_impl* I = e->impl;
+    cudaSetDevice(I->device);
+    cudaStreamSynchronize(I->stream);
+    const size_t kv_elems = (size_t)I->L * I->Hkvl * I->max_ctx * I->hd;
+    cudaMemsetAsync(I->kc, 0, sizeof(__half) * kv_elems, I->stream);
+    cudaMemsetAsync(I->vc, 0, sizeof(__half) * kv_elems, I->stream);
+    cudaMemsetAsync(I->st, 0, sizeof(DeviceState), I->stream);
+    cudaStreamSynchronize(I->stream);
+    e->n_past = 0;
+    I->logits_valid = false;
+    memset(&e->perf, 0, sizeof e->perf);
+}
+
+extern "C" const jinf_perf_stats* jinf_engine_get_stats(const jinf_engine* e) { return e ? &e->perf : nullptr; }
+
+extern "C" jinf_status jinf_engine_forward(jinf_engine* e, const int32_t* tokens, int n_tokens, float** logits) {
+    if (!e || !tokens || n_tokens <= 0 || !logits || !e->impl) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    for (int t = 0; t < n_tokens; ++t)
+        if (tokens[t] < 0 || tokens[t] >= I->V) return JINF_ERR_INVALID;
+    if (e->n_past + n_tokens > I->max_ctx) return JINF_ERR_INVALID;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    jinf_timer timer;
+    JINF_CUDA_CHECK(cudaEventRecord(I->ev0, I->stream));
+    if (n_tokens == 1) {
+        I->pinned[0] = tokens[0];
+        JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->token, &I->pinned[0], sizeof(int32_t), cudaMemcpyHostToDevice,
+                                        I->stream));
+    } else {
+        JINF_CUDA_CHECK(cudaMemcpyAsync(I->dev_tokens, tokens, sizeof(int32_t) * (size_t)n_tokens,
+                                        cudaMemcpyHostToDevice, I->stream));
+    }
+    for (int t = 0; t < n_tokens; ++t) {
+        if (n_tokens > 1)
+            JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->token, I->dev_tokens + t, sizeof(int32_t),
+                                            cudaMemcpyDeviceToDevice, I->stream));
+        // Only the last token's logits are observable: earlier tokens skip the LM head.
+        JINF_CHECK(step(e, t == n_tokens - 1), "decode step");
+    }
+    JINF_CHECK(gather_logits(e), "logits gather");
+    JINF_CUDA_CHECK(cudaEventRecord(I->ev1, I->stream));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, I->ev0, I->ev1);
+    *logits = I->logits_full;
+    I->logits_valid = true;
+    e->perf.total_ms += timer.elapsed_ms();
+    e->perf.gpu_compute_ms += ms;
+    e->perf.tokens_generated += n_tokens;
+    return JINF_OK;
+}
+
+extern "C" jinf_status jinf_engine_last_argmax(jinf_engine* e, int32_t* token) {
+    if (!e || !token || !e->impl || !e->impl->logits_valid) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->pinned[1], &I->st->argmax_token, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                    I->stream));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    *token = I->pinned[1];
+    return JINF_OK;
+}
+
+extern "C" jinf_status jinf_engine_generate(jinf_engine* e, const int32_t* prompt, int n_prompt, int32_t* output,
+                                            int max_tokens, int* n_generated) {
+    if (!e || !output || !n_generated || !e->impl) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    float* logits = nullptr;
+    if (n_prompt > 0) {
+        if (!prompt) return JINF_ERR_INVALID;
+        JINF_CHECK(jinf_engine_forward(e, prompt, n_prompt, &logits), "prompt");
+    } else if (e->n_past == 0 || !I->logits_valid) {
+        return JINF_ERR_INVALID;
+    }
+    // Same loop as the reference (reference src/engine.cpp:779-800): emit the argmax of
+    // the current logits, stop after EOS, otherwise feed the token back through forward().
+    // Per token 4 bytes cross each way (the reference copied all n_vocab logits D2H).
+    int gen = 0;
+    for (int i = 0; i < max_tokens; ++i) {
+        int32_t best;
+        JINF_CHECK(jinf_engine_last_argmax(e, &best), "argmax");
+        output[gen++] = best;
+        if (I->eos >= 0 && best == I->eos) break;
+        if (jinf_engine_forward(e, &best, 1, &logits) != JINF_OK) break;
+    }
+    *n_generated = gen;
+    return JINF_OK;
+}
+
+extern "C" jinf_status jinf_engine_decode_resident(jinf_engine* e, int n_steps, int32_t* out_tokens) {
+    if (!e || !e->impl || n_steps < 0) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    if (!I->logits_valid || e->n_past + n_steps > I->max_ctx) return JINF_ERR_INVALID;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    // st->token already holds the argmax of the last step (finalize feeds it back)
+    for (int i = 0; i < n_steps; ++i) {
+        JINF_CHECK(step(e, true), "decode step");
+        if (out_tokens)
+            JINF_CUDA_CHECK(cudaMemcpyAsync(&out_tokens[i], &I->st->argmax_token, sizeof(int32_t),
+                                            cudaMemcpyDeviceToHost, I->stream));
+    }
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    return JINF_OK;
+}
+
+extern "C" jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uint64_t seed) {
+    if (!e || !e->impl || n_pos < 0 || n_pos > e->impl->max_ctx) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    if (n_pos > 0) {
+        k_fill_kv_random<<<4 * I->num_sms, 256, 0, I->stream>>>(I->kc, I->vc, I->L, I->Hkvl, I->max_ctx, I->hd, n_pos,
+                                                               (unsigned long long)seed);
+        JINF_CUDA_CHECK(cudaGetLastError());
+    }
+    // set the device position; the token stays whatever was last fed
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->pos, &n_pos, sizeof(int), cudaMemcpyHostToDevice, I->stream));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    e->n_past = n_pos;
+    return JINF_OK;
+}
+
+extern "C" uint64_t jinf_engine_weight_bytes_per_token(const jinf_engine* e) {
+    return e && e->impl ? e->impl->weight_bytes_token : 0;
+}
+
+extern "C" jinf_status jinf_engine_profile_kernels(jinf_engine* e, int reps, double* times_us, double* bytes) {
+    if (!e || !e->impl || reps <= 0 || !times_us || !bytes) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    const int roles[6] = {ROLE_QKV, -1 /* attention */, ROLE_O, ROLE_GATEUP, ROLE_DOWN, ROLE_LM};
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    for (int k = 0; k < 6; ++k) {
+        std::vector<const Op*> sel;
+        for (const Op& op : I->ops_full) {
+            if (k == 1 ? op.kind == OP_ATTN : (op.kind == OP_GEMV && op.role == roles[k])) sel.push_back(&op);
+        }
+        times_us[k] = 0;
+        bytes[k] = 0;
+        if (sel.empty()) continue;
+        double total = 0;
+        for (int r = 0; r < reps; ++r) {
+            Op op = *sel[r % sel.size()];
+            if (op.kind == OP_GEMV) op.gp.pf_bytes = 0;  // time the kernel's own stream only
+            cudaEventRecord(a, I->stream);
+            run_op(I, op, I->stream);
+            cudaEventRecord(b, I->stream);
+            cudaEventSynchronize(b);
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, a, b);
+            total += ms;
+        }
+        times_us[k] = 1000.0 * total / reps;
+        bytes[k] = (double)sel[0]->bytes;
+        if (k == 1) {
+            // K and V rows of positions 0..pos for this rank's kv heads
+            int pos = 0;
+            cudaMemcpy(&pos, &I->st->pos, sizeof(int), cudaMemcpyDeviceToHost);
+            bytes[k] = 2.0 * (pos + 1) * I->Hkvl * I->hd * 2.0;
+        }
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    // The kernels above rewrote the residual stream and the argmax accumulator: the
+    // sequence state is no longer meaningful (callers reset before decoding again).
+    JINF_CUDA_CHECK(cudaMemsetAsync(&I->st->best, 0, sizeof(unsigned long long), I->stream));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    I->logits_valid = false;
+    return JINF_OK;
+}

@@ -1,0 +1,57 @@
+// Host interface of the fused Q4T GEMV kernels (gemv_q4t.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "q4t.cuh"
+
+namespace jinf {
+
+constexpr int GEMV_THREADS = 256;
+
+enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3 };
+enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3 };
+
+struct GemvParams {
+    const uint8_t* w;  // Q4T stream of the matrix
+    int rows, cols, lk, steps, tiles;
+    // prologue
+    const void* x;          // X_PLAIN_*: input vector
+    const float* hin;       // X_RMSNORM: residual stream
+    const float* yres;      // X_RMSNORM: pending residual added to hin (may be null)
+    float* hout;            // X_RMSNORM / X_EMBED_NORM: CTA 0 stores h here (may be null)
+    const float* norm_w;    // RMSNorm gain [cols]
+    float eps;
+    const float* embed;     // X_EMBED_NORM: token_embd [n_vocab][cols] (row read at st->token)
+    // epilogue
+    float* y;               // STORE: y[rows]; QKV: q[nq]; GATEUP: h[rows/2]; LMHEAD: logits[rows]
+    __half* kcache;         // QKV: this layer's K cache [n_kv_heads][max_ctx][head_dim]
+    __half* vcache;
+    int nq, nk, head_dim, max_ctx;
+    float rope_base;
+    int vocab_offset;       // LMHEAD: global id of row 0
+    DeviceState* st;
+    // L2 prefetch of the bytes the next kernel will stream
+    const uint8_t* pf_ptr;
+    uint64_t pf_bytes;
+};
+
+inline void gemv_params_for(GemvParams& p, const void* w, const Q4TShape& sh) {
+    p.w = (const uint8_t*)w;
+    p.rows = sh.rows;
+    p.cols = sh.cols;
+    p.lk = sh.lk;
+    p.steps = sh.steps;
+    p.tiles = sh.tiles;
+}
+
+size_t gemv_smem_bytes(int cols, int lk);
+// Persistent grid size: min(tile groups, resident CTAs per SM * num_sms).
+int gemv_grid(const GemvParams& p, int xm, int epi, int num_sms);
+cudaError_t gemv_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
+// AoS Q4_0 [rows][cols] (device) -> Q4T (device, sh.bytes).
+cudaError_t q4t_repack(const void* aos, void* dst, const Q4TShape& sh, cudaStream_t s);
+
+}  // namespace jinf

@@ -1,0 +1,104 @@
+"""Thin wrappers of the reference kernel ABI (jinf_cuda_*) and the new B200 entry points
+(jinf_b200_*) over torch CUDA tensors: torch provides device memory and the stream, the
+computation is the library's."""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _lib as L
+
+
+def _p(t) -> C.c_void_p:
+    return C.c_void_p(t.data_ptr())
+
+
+def _s(stream=None) -> C.c_void_p:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _raise_last(what: str) -> None:
+    err = L.lib.jinf_cuda_last_error()
+    if err:
+        raise L.JinfError(err, what)
+
+
+def dequant_matvec(weight, x, y, rows: int, cols: int, qtype: int, stream=None) -> None:
+    L.lib.jinf_cuda_dequant_matvec(_p(weight), _p(x), _p(y), rows, cols, qtype, _s(stream))
+    _raise_last("jinf_cuda_dequant_matvec")
+
+
+def dequantize(blocks, out, n_blocks: int, qtype: int, stream=None) -> None:
+    fn = {L.Q4_0: L.lib.jinf_cuda_dequantize_q4_0, L.Q4_K: L.lib.jinf_cuda_dequantize_q4_K,
+          L.Q8_0: L.lib.jinf_cuda_dequantize_q8_0, L.Q6_K: L.lib.jinf_cuda_dequantize_q6_K}[qtype]
+    fn(_p(blocks), _p(out), n_blocks, _s(stream))
+    _raise_last("jinf_cuda_dequantize")
+
+
+def rmsnorm(out, x, w, n: int, eps: float, weight_type: int = 0, stream=None) -> None:
+    L.lib.jinf_cuda_rmsnorm(_p(out), _p(x), _p(w), n, eps, weight_type, _s(stream))
+    _raise_last("jinf_cuda_rmsnorm")
+
+
+def rope(q, k, head_dim: int, n_heads: int, n_heads_kv: int, pos: int, base: float, stream=None) -> None:
+    L.lib.jinf_cuda_rope(_p(q), _p(k), head_dim, n_heads, n_heads_kv, pos, base, _s(stream))
+    _raise_last("jinf_cuda_rope")
+
+
+def silu_mul(out, g, u, n: int, stream=None) -> None:
+    L.lib.jinf_cuda_silu_mul(_p(out), _p(g), _p(u), n, _s(stream))
+    _raise_last("jinf_cuda_silu_mul")
+
+
+def softmax(out, x, n: int, stream=None) -> None:
+    L.lib.jinf_cuda_softmax(_p(out), _p(x), n, _s(stream))
+    _raise_last("jinf_cuda_softmax")
+
+
+def residual_add(a, b, n: int, stream=None) -> None:
+    L.lib.jinf_cuda_residual_add(_p(a), _p(b), n, _s(stream))
+    _raise_last("jinf_cuda_residual_add")
+
+
+def attention(out, q, kc, vc, head_dim: int, n_heads: int, n_heads_kv: int, n_past: int, max_ctx: int,
+              stream=None) -> None:
+    L.lib.jinf_cuda_attention(_p(out), _p(q), _p(kc), _p(vc), head_dim, n_heads, n_heads_kv, n_past, max_ctx,
+                              _s(stream))
+    _raise_last("jinf_cuda_attention")
+
+
+def sparse_ffn(bundles, x, out, offsets, n_act: int, hidden: int, bundle_size: int, qtype: int, gate_up,
+               stream=None) -> None:
+    L.lib.jinf_cuda_sparse_ffn(_p(bundles), _p(x), _p(out), _p(offsets), n_act, hidden, bundle_size, qtype,
+                               _p(gate_up), _s(stream))
+    _raise_last("jinf_cuda_sparse_ffn")
+
+
+def q4t_bytes(rows: int, cols: int) -> int:
+    return int(L.lib.jinf_b200_q4t_bytes(rows, cols))
+
+
+def q4t_pack(aos, q4t, rows: int, cols: int, stream=None) -> None:
+    L.check(L.lib.jinf_b200_q4t_pack(_p(aos), _p(q4t), rows, cols, _s(stream)), "jinf_b200_q4t_pack")
+
+
+def gemv_q4t(q4t, x, y, rows: int, cols: int, stream=None) -> None:
+    import torch
+    xt = L.F32 if x.dtype == torch.float32 else L.F16
+    L.check(L.lib.jinf_b200_gemv_q4t(_p(q4t), _p(x), xt, _p(y), rows, cols, _s(stream)), "jinf_b200_gemv_q4t")
+
+
+def gemv_q4t_rmsnorm(q4t, h, gain, eps: float, y, rows: int, cols: int, stream=None) -> None:
+    L.check(L.lib.jinf_b200_gemv_q4t_rmsnorm(_p(q4t), _p(h), _p(gain), eps, _p(y), rows, cols, _s(stream)),
+            "jinf_b200_gemv_q4t_rmsnorm")
+
+
+def attention_workspace_bytes(n_kv_heads: int, head_dim: int, max_ctx: int) -> int:
+    return int(L.lib.jinf_b200_attention_workspace_bytes(n_kv_heads, head_dim, max_ctx))
+
+
+def attention_f16(out, q, kc, vc, head_dim: int, n_heads: int, n_kv_heads: int, n_pos: int, max_ctx: int,
+                  workspace, stream=None) -> None:
+    L.check(L.lib.jinf_b200_attention_f16(_p(out), _p(q), _p(kc), _p(vc), head_dim, n_heads, n_kv_heads, n_pos,
+                                          max_ctx, _p(workspace), _s(stream)), "jinf_b200_attention_f16")

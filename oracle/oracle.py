@@ -1,0 +1,220 @@
+"""ctypes access to the CPU oracle (liboracle.so) and to the reference's own host code
+compiled from its source tree (_ref/libjinf_ref.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference legs as the checker or the timed CPU baseline. The product
+package never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libjinf_ref.so")
+
+_orc = None
+_ref = None
+
+
+def build() -> None:
+    """Build liboracle.so (and _ref/ when the reference tree is present)."""
+    subprocess.run(["make", "-C", HERE], check=True, stdout=subprocess.DEVNULL)
+
+
+def lib() -> C.CDLL:
+    global _orc
+    if _orc is None:
+        if not os.path.exists(ORACLE_SO):
+            build()
+        o = C.CDLL(ORACLE_SO)
+        vp, i32, i64, f32 = C.c_void_p, C.c_int, C.c_int64, C.c_float
+        sig = {
+            "orc_fp16_to_fp32": (f32, [C.c_uint16]),
+            "orc_fp16_to_fp32_array": (None, [vp, vp, i64]),
+            "orc_dequant_q4_0": (None, [vp, vp, i64]),
+            "orc_dequant_q4_K": (None, [vp, vp, i64]),
+            "orc_dequant_q8_0": (None, [vp, vp, i64]),
+            "orc_dequant_q6_K": (None, [vp, vp, i64]),
+            "orc_matvec": (None, [vp, i32, vp, vp, i32, i32]),
+            "orc_rmsnorm": (None, [vp, vp, vp, i32, f32]),
+            "orc_rope": (None, [vp, vp, i32, i32, i32, i32, f32]),
+            "orc_silu_mul": (None, [vp, vp, vp, i32]),
+            "orc_softmax": (None, [vp, vp, i32]),
+            "orc_attention": (None, [vp, vp, vp, vp, i32, i32, i32, i32]),
+            "orc_sparse_ffn": (None, [vp, vp, vp, vp, i32, i32, i32, vp]),
+            "orc_model_create": (vp, [i32, i32, i32, i32, i32, i32, f32, f32, i32, i32]),
+            "orc_model_destroy": (None, [vp]),
+            "orc_model_bind": (i32, [vp, C.c_char_p, i32, vp]),
+            "orc_model_pos": (i32, [vp]),
+            "orc_forward": (i32, [vp, i32, vp]),
+            "orc_argmax": (i32, [vp, i32]),
+            "orc_fill_kv_random": (i32, [vp, i32, C.c_uint64]),
+            "orc_num_threads": (i32, []),
+        }
+        for n, (r, a) in sig.items():
+            fn = getattr(o, n)
+            fn.restype, fn.argtypes = r, a
+        _orc = o
+    return _orc
+
+
+def ref_lib() -> C.CDLL | None:
+    """The reference's own quant.cpp / gguf.cpp / splitter.cpp, or None if not built."""
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_SO):
+            if os.path.exists("/root/reference/src/quant.cpp"):
+                build()
+            if not os.path.exists(REF_SO):
+                return None
+        r = C.CDLL(REF_SO)
+        vp = C.c_void_p
+        for n in ["ref_dequantize_q4_0", "ref_dequantize_q4_K", "ref_dequantize_q8_0"]:
+            getattr(r, n).restype, getattr(r, n).argtypes = None, [vp, vp, C.c_int]
+        r.ref_dequantize.restype, r.ref_dequantize.argtypes = None, [vp, C.c_int, vp, C.c_longlong]
+        r.ref_gguf_summary.restype, r.ref_gguf_summary.argtypes = C.c_int, [C.c_char_p, C.c_char_p, C.c_int]
+        r.ref_split.restype = C.c_int
+        r.ref_split.argtypes = [C.c_char_p, C.c_ulonglong, C.POINTER(C.c_int), C.POINTER(C.c_ulonglong)]
+        _ref = r
+    return _ref
+
+
+def _vp(a: np.ndarray) -> C.c_void_p:
+    return a.ctypes.data_as(C.c_void_p)
+
+
+BLOCK = {2: (32, 18), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
+
+
+def dequant(blocks: np.ndarray, qtype: int) -> np.ndarray:
+    be, bb = BLOCK[qtype]
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    nb = blocks.size // bb
+    out = np.empty(nb * be, dtype=np.float32)
+    fn = {2: "orc_dequant_q4_0", 8: "orc_dequant_q8_0", 12: "orc_dequant_q4_K", 14: "orc_dequant_q6_K"}[qtype]
+    getattr(lib(), fn)(_vp(blocks), _vp(out), nb)
+    return out
+
+
+def fp16_to_fp32(h: np.ndarray) -> np.ndarray:
+    h = np.ascontiguousarray(h, dtype=np.uint16)
+    out = np.empty(h.size, dtype=np.float32)
+    lib().orc_fp16_to_fp32_array(_vp(h), _vp(out), h.size)
+    return out
+
+
+def matvec(w: np.ndarray, qtype: int, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    w = np.ascontiguousarray(w)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(rows, dtype=np.float32)
+    lib().orc_matvec(_vp(w), qtype, _vp(x), _vp(y), rows, cols)
+    return y
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().orc_rmsnorm(_vp(out), _vp(x), _vp(w), x.size, eps)
+    return out
+
+
+def rope(q: np.ndarray, k: np.ndarray, hd: int, nh: int, nkv: int, pos: int, base: float):
+    q = np.array(q, dtype=np.float32)
+    k = np.array(k, dtype=np.float32)
+    lib().orc_rope(_vp(q), _vp(k), hd, nh, nkv, pos, base)
+    return q, k
+
+
+def silu_mul(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g = np.ascontiguousarray(g, dtype=np.float32)
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    out = np.empty_like(g)
+    lib().orc_silu_mul(_vp(out), _vp(g), _vp(u), g.size)
+    return out
+
+
+def softmax(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().orc_softmax(_vp(out), _vp(x), x.size)
+    return out
+
+
+def attention(q, kc, vc, hd, nh, nkv, n_past) -> np.ndarray:
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    kc = np.ascontiguousarray(kc, dtype=np.float32)
+    vc = np.ascontiguousarray(vc, dtype=np.float32)
+    out = np.empty(nh * hd, dtype=np.float32)
+    lib().orc_attention(_vp(out), _vp(q), _vp(kc), _vp(vc), hd, nh, nkv, n_past)
+    return out
+
+
+def sparse_ffn(bundles, x, offsets, n_act, hidden, qtype) -> tuple[np.ndarray, np.ndarray]:
+    bundles = np.ascontiguousarray(bundles, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    offsets = np.ascontiguousarray(offsets, dtype=np.int32)
+    out = np.empty(hidden, dtype=np.float32)
+    gu = np.empty(max(1, n_act), dtype=np.float32)
+    lib().orc_sparse_ffn(_vp(bundles), _vp(x), _vp(out), _vp(offsets), n_act, hidden, qtype, _vp(gu))
+    return out, gu[:n_act]
+
+
+class OracleModel:
+    """The whole decode step on the CPU, over tensors of a jinf SynthModel (borrowed arrays)."""
+
+    def __init__(self, synth, max_ctx: int, kv_f16: bool = True, layers: int | None = None):
+        sh = synth.shape
+        self.shape = sh
+        self.n_layers = sh.n_layers if layers is None else layers
+        o = lib()
+        self.h = o.orc_model_create(self.n_layers, sh.n_embd, sh.n_heads, sh.n_heads_kv, sh.n_ff, sh.n_vocab,
+                                    sh.rms_norm_eps, sh.rope_freq_base, max_ctx, 1 if kv_f16 else 0)
+        self._keep = []
+        for name in synth.tensor_names():
+            if name.startswith("blk.") and int(name.split(".")[1]) >= self.n_layers:
+                continue
+            t, _, _ = synth.tensor_info(name)
+            arr = np.ascontiguousarray(synth.read_rows(name))
+            self._keep.append(arr)
+            o.orc_model_bind(self.h, name.encode(), t, _vp(arr))
+
+    def close(self):
+        if self.h:
+            lib().orc_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def pos(self) -> int:
+        return lib().orc_model_pos(self.h)
+
+    def forward(self, token: int, want_logits: bool = True) -> np.ndarray | None:
+        logits = np.empty(self.shape.n_vocab, dtype=np.float32) if want_logits else None
+        rc = lib().orc_forward(self.h, int(token), _vp(logits) if want_logits else None)
+        if rc != 0:
+            raise RuntimeError(f"orc_forward failed ({rc})")
+        return logits
+
+    def fill_kv_random(self, n_pos: int, seed: int = 0) -> None:
+        if lib().orc_fill_kv_random(self.h, n_pos, seed) != 0:
+            raise RuntimeError("orc_fill_kv_random failed")
+
+
+def argmax(v: np.ndarray) -> int:
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    return int(lib().orc_argmax(_vp(v), v.size))
+
+
+def num_threads() -> int:
+    return int(lib().orc_num_threads())
