@@ -171,14 +171,17 @@ __device__ __forceinline__ void stage_bytes(uint8_t* dst, const uint8_t* src, si
         const uint32_t* s = reinterpret_cast<const uint32_t*>(src);
         uint32_t* d = reinterpret_cast<uint32_t*>(dst);
         for (size_t i = threadIdx.x; i < n / 4; i += blockDim.x) d[i] = ldg_stream_u1(s + i);
-    } else {
+    } else if ((a & 1) == 0 && (n & 1) == 0) {
         const uint16_t* s = reinterpret_cast<const uint16_t*>(src);
         uint16_t* d = reinterpret_cast<uint16_t*>(dst);
         for (size_t i = threadIdx.x; i < n / 2; i += blockDim.x) d[i] = __ldg(s + i);
+    } else {
+        for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = __ldg(src + i);
     }
 }
 
-// Bytes [off, off+16) of a 2-byte-aligned shared buffer as four words (funnel shift when off % 4 == 2).
+// Bytes [off, off+16) of a shared buffer whose start is 16-byte aligned, `off` even: four
+// aligned word reads (five and a funnel shift when off % 4 == 2).
 __device__ __forceinline__ void smem_16B(const uint8_t* base, int off, uint32_t q[4]) {
     const uint32_t* w = reinterpret_cast<const uint32_t*>(base + (off & ~3));
     if ((off & 3) == 0) {
@@ -236,16 +239,18 @@ __global__ void __launch_bounds__(MV_THREADS) k_matvec_small_blocks(const uint8_
     __syncthreads();
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     for (int r = wid; r < nr; r += MV_THREADS / 32) {
-        const uint8_t* rb = sm + (size_t)r * row_bytes;
+        // Offsets are taken from the (16-byte aligned) start of the staged rows: a row
+        // itself starts at r * row_bytes, which is only 2-byte aligned for odd nb.
+        const int rbase = (int)((size_t)r * row_bytes);
         float acc = 0.f;
         for (int b = lane; b < nb; b += 32) {
-            const int off = b * BB;
-            const float d = jinf_h2f(*reinterpret_cast<const uint16_t*>(rb + off));
+            const int off = rbase + b * BB;
+            const float d = jinf_h2f(*reinterpret_cast<const uint16_t*>(sm + off));
             const float* xb = x + 32 * b;
             float s = 0.f;
             if (QT == JINF_TYPE_Q4_0) {
                 uint32_t q[4];
-                smem_16B(rb, off + 2, q);
+                smem_16B(sm, off + 2, q);
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
                     float xs[8];
@@ -254,8 +259,8 @@ __global__ void __launch_bounds__(MV_THREADS) k_matvec_small_blocks(const uint8_
                 }
             } else {
                 uint32_t q[8];
-                smem_16B(rb, off + 2, q);
-                smem_16B(rb, off + 18, q + 4);
+                smem_16B(sm, off + 2, q);
+                smem_16B(sm, off + 18, q + 4);
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
                     float xs[8];

@@ -4,12 +4,14 @@
 // h -> h / (H/Hkv), max-subtracted softmax, P.V), restated as split-K flash-decoding:
 //   grid = n_kv_heads x n_split CTAs; CTA (h, s) covers positions [s*n/S, (s+1)*n/S)
 //   for ALL query heads of kv head h, so each K/V row is read from HBM once (the
-//   reference re-reads it once per query head). Each warp keeps an online-softmax
-//   state per query head; lanes own positions for q.k and head dims for p.v.
-//   The CTA's (m, l, acc) goes to a partial buffer; the last CTA of a kv head
-//   (arrival counter, self-resetting for graph replay) merges the splits in fixed
-//   order and writes the fp32 output [n_heads * hd].
-// Cache layout: [n_kv_heads][max_ctx][hd] fp16 per layer; n = pos + 1 read from the
+//   reference re-reads it once per query head).
+//   Each warp takes 32-position tiles: the tile's K and V rows are copied into the
+//   warp's shared memory with asynchronous 16-byte copies (all issued at once, one
+//   wait), K chunk-swizzled so that lane-per-position reads are bank-conflict free.
+//   Lanes own positions for q.k (online softmax per query head) and head dims for p.v.
+//   The CTA's (m, l, acc) goes to a partial buffer; the last CTA of a kv head (arrival
+//   counter, reset by that CTA for graph replay) merges the splits in fixed order.
+// Cache layout: [n_kv_heads][max_ctx][hd] fp16 per layer; n = pos + 1 is read from the
 // device state, so one captured graph serves every position.
 #include "common.cuh"
 #include "q4t.cuh"
@@ -19,31 +21,56 @@
 
 namespace jinf {
 
-constexpr int AW = 4;       // warps per CTA
-constexpr int AMAXG = 8;    // max query heads per kv head
+constexpr int AW = 4;      // warps per CTA
+constexpr int AMAXG = 8;   // max query heads per kv head
+constexpr int TP = 32;     // positions per warp tile
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+template <int HD>
+struct AttnSmem {
+    static constexpr int CH = HD / 8;  // 16-byte chunks per K/V row
+    float q[AMAXG * HD];
+    __half k[AW][TP * HD];
+    __half v[AW][TP * HD];
+    float wacc[AW][AMAXG][HD];
+    float wm[AW][AMAXG];
+    float wl[AW][AMAXG];
+    int is_last;
+};
+
+size_t attn_smem_bytes(int head_dim) {
+    return head_dim == 64 ? sizeof(AttnSmem<64>) : sizeof(AttnSmem<128>);
+}
 
 template <int HD>
 __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
     constexpr int NJ = HD / 32;  // dims per lane in p.v
+    constexpr int CH = HD / 8;
+    extern __shared__ __align__(16) uint8_t smraw[];
+    AttnSmem<HD>& sm = *reinterpret_cast<AttnSmem<HD>*>(smraw);
     const int kvh = blockIdx.x / p.n_split, split = blockIdx.x % p.n_split;
     const int G = p.n_heads / p.n_kv_heads;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-
-    __shared__ __align__(16) float qs[AMAXG * HD];
-    __shared__ float wacc[AW][AMAXG][HD];
-    __shared__ float wm[AW][AMAXG], wl[AW][AMAXG];
-    __shared__ int is_last;
 
     pdl_wait();
     pdl_trigger();
     const int n = p.st->pos + 1;
     const float scale = rsqrtf((float)HD);
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) qs[i] = p.q[(size_t)kvh * G * HD + i] * scale;
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) sm.q[i] = p.q[(size_t)kvh * G * HD + i] * scale;
     __syncthreads();
 
     const int start = (int)((int64_t)n * split / p.n_split), end = (int)((int64_t)n * (split + 1) / p.n_split);
     const __half* kb = p.kcache + (size_t)kvh * p.max_ctx * HD;
     const __half* vb = p.vcache + (size_t)kvh * p.max_ctx * HD;
+    __half* ksm = sm.k[wid];
+    __half* vsm = sm.v[wid];
 
     float m[AMAXG], l[AMAXG], acc[AMAXG][NJ];
 #pragma unroll
@@ -54,17 +81,25 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
         for (int j = 0; j < NJ; ++j) acc[g][j] = 0.f;
     }
 
-    for (int t0 = start + 32 * wid; t0 < end; t0 += 32 * AW) {
-        const int t = t0 + lane;
-        const bool valid = t < end;
+    for (int t0 = start + TP * wid; t0 < end; t0 += TP * AW) {
+        const int nt = min(TP, end - t0);
+        // stage the tile: chunk c of row r lands at chunk (c ^ (r % CH)) of row r
+        for (int i = lane; i < nt * CH; i += 32) {
+            const int r = i / CH, c = i % CH;
+            cp_async16(ksm + (r * CH + (c ^ (r % CH))) * 8, kb + (size_t)(t0 + r) * HD + c * 8);
+            cp_async16(vsm + i * 8, vb + (size_t)(t0 + r) * HD + c * 8);
+        }
+        cp_async_wait_all();
+        __syncwarp();
+
+        const bool valid = lane < nt;
         float s[AMAXG];
 #pragma unroll
         for (int g = 0; g < AMAXG; ++g) s[g] = 0.f;
         if (valid) {
-            const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)t * HD);
 #pragma unroll 4
-            for (int c = 0; c < HD / 8; ++c) {
-                const uint4 raw = __ldg(kr + c);
+            for (int c = 0; c < CH; ++c) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(ksm + (lane * CH + (c ^ (lane % CH))) * 8);
                 const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
                 float kf[8];
 #pragma unroll
@@ -76,8 +111,8 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
 #pragma unroll
                 for (int g = 0; g < AMAXG; ++g) {
                     if (g < G) {
-                        const float4 qa = *reinterpret_cast<const float4*>(qs + g * HD + 8 * c);
-                        const float4 qb = *reinterpret_cast<const float4*>(qs + g * HD + 8 * c + 4);
+                        const float4 qa = *reinterpret_cast<const float4*>(sm.q + g * HD + 8 * c);
+                        const float4 qb = *reinterpret_cast<const float4*>(sm.q + g * HD + 8 * c + 4);
                         s[g] = fmaf(qa.x, kf[0], s[g]); s[g] = fmaf(qa.y, kf[1], s[g]);
                         s[g] = fmaf(qa.z, kf[2], s[g]); s[g] = fmaf(qa.w, kf[3], s[g]);
                         s[g] = fmaf(qb.x, kf[4], s[g]); s[g] = fmaf(qb.y, kf[5], s[g]);
@@ -91,7 +126,7 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
         for (int g = 0; g < AMAXG; ++g) {
             if (g >= G) { pr[g] = 0.f; continue; }
             const float sc = valid ? s[g] : -INFINITY;
-            const float mn = fmaxf(m[g], warp_max(sc));
+            const float mn = fmaxf(m[g], warp_max(sc));  // finite: lane 0 is valid
             const float corr = m[g] == -INFINITY ? 0.f : expf(m[g] - mn);
             pr[g] = valid ? expf(sc - mn) : 0.f;
             l[g] = l[g] * corr + warp_sum(pr[g]);
@@ -99,22 +134,14 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
             for (int j = 0; j < NJ; ++j) acc[g][j] *= corr;
             m[g] = mn;
         }
-        const int nt = min(32, end - t0);
         for (int tt = 0; tt < nt; ++tt) {
-            const __half* vr = vb + (size_t)(t0 + tt) * HD + NJ * lane;
+            const __half* vr = vsm + tt * HD + NJ * lane;
             float vv[NJ];
-            if (NJ == 4) {
-                const uint2 raw = __ldg(reinterpret_cast<const uint2*>(vr));
-                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-                vv[0] = a.x; vv[1] = a.y; vv[2 % NJ] = b.x; vv[3 % NJ] = b.y;
-            } else {
 #pragma unroll
-                for (int j = 0; j < NJ; j += 2) {
-                    const float2 a = __half22float2(__ldg(reinterpret_cast<const __half2*>(vr + j)));
-                    vv[j] = a.x;
-                    vv[j + 1] = a.y;
-                }
+            for (int j = 0; j < NJ; j += 2) {
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(vr + j));
+                vv[j] = a.x;
+                vv[j + 1] = a.y;
             }
 #pragma unroll
             for (int g = 0; g < AMAXG; ++g) {
@@ -124,32 +151,34 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
                 for (int j = 0; j < NJ; ++j) acc[g][j] = fmaf(pg, vv[j], acc[g][j]);
             }
         }
+        __syncwarp();  // the next tile's copies overwrite this warp's K/V buffers
     }
 
 #pragma unroll
     for (int g = 0; g < AMAXG; ++g) {
         if (g >= G) continue;
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) wacc[wid][g][NJ * lane + j] = acc[g][j];
+        for (int j = 0; j < NJ; ++j) sm.wacc[wid][g][NJ * lane + j] = acc[g][j];
         if (lane == 0) {
-            wm[wid][g] = m[g];
-            wl[wid][g] = l[g];
+            sm.wm[wid][g] = m[g];
+            sm.wl[wid][g] = l[g];
         }
     }
     __syncthreads();
     // CTA partial -> global
-    float* part = p.partial + ((size_t)kvh * p.n_split + split) * (AMAXG * HD + 2 * AMAXG);
+    const size_t stride = AMAXG * HD + 2 * AMAXG;
+    float* part = p.partial + ((size_t)kvh * p.n_split + split) * stride;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int g = i / HD, d = i % HD;
         float M = -INFINITY;
-        for (int w = 0; w < AW; ++w) M = fmaxf(M, wm[w][g]);
+        for (int w = 0; w < AW; ++w) M = fmaxf(M, sm.wm[w][g]);
         float a = 0.f, L = 0.f;
         if (M != -INFINITY) {
             for (int w = 0; w < AW; ++w) {
-                if (wm[w][g] == -INFINITY) continue;
-                const float f = expf(wm[w][g] - M);
-                a = fmaf(wacc[w][g][d], f, a);
-                L = fmaf(wl[w][g], f, L);
+                if (sm.wm[w][g] == -INFINITY) continue;
+                const float f = expf(sm.wm[w][g] - M);
+                a = fmaf(sm.wacc[w][g][d], f, a);
+                L = fmaf(sm.wl[w][g], f, L);
             }
         }
         part[g * HD + d] = a;
@@ -162,14 +191,13 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
     __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned prev = atomicAdd(&p.st->attn_count[kvh], 1u);
-        is_last = prev == (unsigned)(p.n_split - 1);
+        sm.is_last = prev == (unsigned)(p.n_split - 1);
     }
     __syncthreads();
-    if (!is_last) return;
+    if (!sm.is_last) return;
     __threadfence();
     // merge the n_split partials of this kv head in split order
-    const float* base = p.partial + (size_t)kvh * p.n_split * (AMAXG * HD + 2 * AMAXG);
-    const size_t stride = AMAXG * HD + 2 * AMAXG;
+    const float* base = p.partial + (size_t)kvh * p.n_split * stride;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int g = i / HD, d = i % HD;
         float M = -INFINITY;
@@ -193,20 +221,28 @@ size_t attn_partial_floats(int n_kv_heads, int n_split, int head_dim) {
 
 cudaError_t attn_launch(const AttnParams& p, cudaStream_t s, bool pdl) {
     if (p.n_heads % p.n_kv_heads || p.n_heads / p.n_kv_heads > AMAXG || p.n_kv_heads > 64) return cudaErrorInvalidValue;
+    if (p.head_dim != 64 && p.head_dim != 128) return cudaErrorInvalidValue;
+    const size_t smem = attn_smem_bytes(p.head_dim);
+    static bool configured[2] = {false, false};
+    const int which = p.head_dim == 64 ? 0 : 1;
+    if (!configured[which]) {
+        cudaError_t e = which == 0
+            ? cudaFuncSetAttribute(k_attn_f16<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)
+            : cudaFuncSetAttribute(k_attn_f16<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured[which] = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.n_kv_heads * p.n_split);
     cfg.blockDim = dim3(AW * 32);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    switch (p.head_dim) {
-        case 64: return cudaLaunchKernelEx(&cfg, k_attn_f16<64>, p);
-        case 128: return cudaLaunchKernelEx(&cfg, k_attn_f16<128>, p);
-        default: return cudaErrorInvalidValue;
-    }
+    return p.head_dim == 64 ? cudaLaunchKernelEx(&cfg, k_attn_f16<64>, p) : cudaLaunchKernelEx(&cfg, k_attn_f16<128>, p);
 }
 
 }  // namespace jinf

@@ -10,10 +10,17 @@
 using namespace jinf;
 
 static int device_sms() {
-    int dev = 0, n = 148;
+    // per-device cache (up to 64 devices)
+    static int sms[64] = {0};
+    int dev = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n;
+    if (dev < 0 || dev >= 64) return 148;
+    if (!sms[dev]) {
+        int n = 148;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev] = n;
+    }
+    return sms[dev];
 }
 
 extern "C" uint64_t jinf_b200_q4t_bytes(int rows, int cols) {

@@ -9,7 +9,14 @@
 
 namespace jinf {
 
-constexpr int GEMV_THREADS = 256;
+#ifndef JINF_GEMV_THREADS
+#define JINF_GEMV_THREADS 256
+#endif
+#ifndef JINF_GEMV_NBUF
+#define JINF_GEMV_NBUF 3
+#endif
+constexpr int GEMV_THREADS = JINF_GEMV_THREADS;
+constexpr int GEMV_NBUF = JINF_GEMV_NBUF;  // shared-memory chunk slots per warp (GEMV_NBUF - 1 in flight)
 
 enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3 };
 enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3 };

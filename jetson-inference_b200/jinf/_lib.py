@@ -11,7 +11,8 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG_ROOT = os.path.dirname(HERE)
-LIB_PATH = os.path.join(PKG_ROOT, "libjinf_b200.so")
+# JINF_LIB selects another build of the same library (e.g. a tuning variant)
+LIB_PATH = os.environ.get("JINF_LIB") or os.path.join(PKG_ROOT, "libjinf_b200.so")
 
 # jinf_status values (include/jinf/common.h)
 JINF_OK, JINF_ERR_IO, JINF_ERR_PARSE, JINF_ERR_CUDA, JINF_ERR_OOM, JINF_ERR_INVALID, JINF_ERR_TIMEOUT = range(7)
