@@ -35,6 +35,28 @@ jinf_status jinf_b200_gemv_q4t(const void* q4t, const void* x, int x_type, float
 jinf_status jinf_b200_gemv_q4t_rmsnorm(const void* q4t, const float* h, const float* gain, float eps, float* y,
                                        int rows, int cols, cudaStream_t stream);
 
+// Bytes of the Q4M image of a rows x cols Q4_0 matrix; 0 if cols is not a multiple of 128.
+// Q4M is the layout of the tensor-core GEMV: 16-row tiles x 128-column groups, 1152 bytes
+// per (tile, group), every nibble and scale of the AoS blocks moved, none re-quantised.
+uint64_t jinf_b200_q4m_bytes(int rows, int cols);
+
+// Repack reference AoS Q4_0 blocks [rows][cols/32] (device) into Q4M (device, q4m_bytes).
+jinf_status jinf_b200_q4m_pack(const void* aos, void* q4m, int rows, int cols, cudaStream_t stream);
+
+// Workspace bytes of jinf_b200_gemv_q4m for this shape (any kw up to 32).
+size_t jinf_b200_gemv_q4m_workspace_bytes(int rows, int cols);
+
+// y[rows] = W . x over a Q4M matrix on the tensor cores; x fp32 (JINF_TYPE_F32) or fp16
+// (JINF_TYPE_F16), accumulation fp32. kw = K parts per 16-row tile (0 = chosen for the
+// device). kw > 1 needs `workspace` (gemv_q4m_workspace_bytes, zeroed once before first
+// use, then reusable by calls on the same stream); kw = 1 takes workspace = NULL.
+jinf_status jinf_b200_gemv_q4m(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
+                               void* workspace, int kw, cudaStream_t stream);
+
+// y[rows] = W . (rmsnorm(h) * gain) over a Q4M matrix; workspace and kw as above.
+jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* h, const float* gain, float eps, float* y,
+                                       int rows, int cols, void* workspace, int kw, cudaStream_t stream);
+
 // Workspace bytes needed by jinf_b200_attention_f16 for this shape.
 size_t jinf_b200_attention_workspace_bytes(int n_kv_heads, int head_dim, int max_ctx);
 

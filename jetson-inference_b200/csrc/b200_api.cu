@@ -5,6 +5,7 @@
 #include "attn_f16.h"
 #include "common.cuh"
 #include "gemv_q4t.h"
+#include "q4m.cuh"
 #include "q4t.cuh"
 
 using namespace jinf;
@@ -60,6 +61,65 @@ extern "C" jinf_status jinf_b200_gemv_q4t_rmsnorm(const void* q4t, const float* 
     p.y = y;
     const int grid = gemv_grid(p, X_RMSNORM, EPI_STORE, device_sms());
     return gemv_launch(p, X_RMSNORM, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
+extern "C" uint64_t jinf_b200_q4m_bytes(int rows, int cols) {
+    Q4MShape sh;
+    return q4m_shape(rows, cols, &sh) ? sh.bytes : 0;
+}
+
+extern "C" jinf_status jinf_b200_q4m_pack(const void* aos, void* q4m, int rows, int cols, cudaStream_t stream) {
+    Q4MShape sh;
+    if (!aos || !q4m || !q4m_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    return q4m_repack(aos, q4m, sh, stream) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
+static constexpr int kQ4mMaxKw = 32;
+
+extern "C" size_t jinf_b200_gemv_q4m_workspace_bytes(int rows, int cols) {
+    Q4MShape sh;
+    if (!q4m_shape(rows, cols, &sh)) return 0;
+    return (size_t)sh.tiles * kQ4mMaxKw * 16 * sizeof(float) + (size_t)sh.tiles * sizeof(unsigned int);
+}
+
+static jinf_status gemv_q4m_common(GemvParams& p, const Q4MShape& sh, int xm, void* workspace, int kw,
+                                   cudaStream_t stream) {
+    if (sh.cols > gemvm_max_cols() || kw < 0 || kw > kQ4mMaxKw) return JINF_ERR_INVALID;
+    const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms());
+    if (kw == 0) kw = gemvm_pick_kw(sh.tiles, sh.groups, grid, workspace ? kQ4mMaxKw : 1);
+    if (kw > sh.groups || (kw > 1 && !workspace)) return JINF_ERR_INVALID;
+    p.kw = kw;
+    if (kw > 1) {
+        p.part = (float*)workspace;
+        p.cnt = (unsigned int*)((uint8_t*)workspace + (size_t)sh.tiles * kQ4mMaxKw * 16 * sizeof(float));
+    }
+    return gemvm_launch(p, xm, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
+extern "C" jinf_status jinf_b200_gemv_q4m(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
+                                          void* workspace, int kw, cudaStream_t stream) {
+    Q4MShape sh;
+    if (!q4m || !x || !y || !q4m_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
+    GemvParams p{};
+    gemvm_params_for(p, q4m, sh);
+    p.x = x;
+    p.y = y;
+    return gemv_q4m_common(p, sh, x_type == JINF_TYPE_F32 ? X_PLAIN_F32 : X_PLAIN_F16, workspace, kw, stream);
+}
+
+extern "C" jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* h, const float* gain, float eps,
+                                                  float* y, int rows, int cols, void* workspace, int kw,
+                                                  cudaStream_t stream) {
+    Q4MShape sh;
+    if (!q4m || !h || !gain || !y || !q4m_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    GemvParams p{};
+    gemvm_params_for(p, q4m, sh);
+    p.hin = h;
+    p.norm_w = gain;
+    p.eps = eps;
+    p.y = y;
+    return gemv_q4m_common(p, sh, X_RMSNORM, workspace, kw, stream);
 }
 
 extern "C" size_t jinf_b200_attention_workspace_bytes(int n_kv_heads, int head_dim, int max_ctx) {

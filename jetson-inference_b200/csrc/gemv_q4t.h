@@ -5,6 +5,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "q4m.cuh"
 #include "q4t.cuh"
 
 namespace jinf {
@@ -18,12 +19,25 @@ namespace jinf {
 constexpr int GEMV_THREADS = JINF_GEMV_THREADS;
 constexpr int GEMV_NBUF = JINF_GEMV_NBUF;  // shared-memory chunk slots per warp (GEMV_NBUF - 1 in flight)
 
+// Tensor-core GEMV over the Q4M layout (gemv_q4m.cu): one persistent CTA of 16 warps per
+// SM, each warp with a private ring of GEMV_M_NBUF chunk slots.
+#ifndef JINF_GEMV_M_NBUF
+#define JINF_GEMV_M_NBUF 5
+#endif
+constexpr int GEMV_M_THREADS = 512;
+constexpr int GEMV_M_NBUF = JINF_GEMV_M_NBUF;
+
 enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3 };
 enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3 };
 
 struct GemvParams {
-    const uint8_t* w;  // Q4T stream of the matrix
+    const uint8_t* w;  // Q4T or Q4M stream of the matrix
     int rows, cols, lk, steps, tiles;
+    // Q4M only
+    int groups;             // cols / 128
+    int kw;                 // K parts per tile (tasks per tile)
+    float* part;            // kw > 1: [tiles * kw][16] partial row sums
+    unsigned int* cnt;      // kw > 1: [tiles] arrival counters, zero before the first launch (self-resetting)
     // prologue
     const void* x;          // X_PLAIN_*: input vector
     const float* hin;       // X_RMSNORM: residual stream
@@ -60,5 +74,23 @@ int gemv_grid(const GemvParams& p, int xm, int epi, int num_sms);
 cudaError_t gemv_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
 // AoS Q4_0 [rows][cols] (device) -> Q4T (device, sh.bytes).
 cudaError_t q4t_repack(const void* aos, void* dst, const Q4TShape& sh, cudaStream_t s);
+
+inline void gemvm_params_for(GemvParams& p, const void* w, const Q4MShape& sh) {
+    p.w = (const uint8_t*)w;
+    p.rows = sh.rows;
+    p.cols = sh.cols;
+    p.tiles = sh.tiles;
+    p.groups = sh.groups;
+    p.kw = 1;
+}
+size_t gemvm_smem_bytes(int cols);
+int gemvm_max_cols();
+// Persistent grid: resident CTAs per SM * num_sms.
+int gemvm_grid(int cols, int xm, int epi, int num_sms);
+// K parts per tile for a grid of `grid` CTAs (1 <= kw <= min(groups, max_kw)).
+int gemvm_pick_kw(int tiles, int groups, int grid, int max_kw);
+cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
+// AoS Q4_0 [rows][cols] (device) -> Q4M (device, sh.bytes).
+cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s);
 
 }  // namespace jinf

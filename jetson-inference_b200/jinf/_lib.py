@@ -156,6 +156,11 @@ SIGNATURES = {
     "jinf_b200_q4t_pack": (i32, [vp, vp, i32, i32, vp]),
     "jinf_b200_gemv_q4t": (i32, [vp, vp, i32, vp, i32, i32, vp]),
     "jinf_b200_gemv_q4t_rmsnorm": (i32, [vp, vp, vp, f32, vp, i32, i32, vp]),
+    "jinf_b200_q4m_bytes": (u64, [i32, i32]),
+    "jinf_b200_q4m_pack": (i32, [vp, vp, i32, i32, vp]),
+    "jinf_b200_gemv_q4m_workspace_bytes": (sz, [i32, i32]),
+    "jinf_b200_gemv_q4m": (i32, [vp, vp, i32, vp, i32, i32, vp, i32, vp]),
+    "jinf_b200_gemv_q4m_rmsnorm": (i32, [vp, vp, vp, f32, vp, i32, i32, vp, i32, vp]),
     "jinf_b200_attention_workspace_bytes": (sz, [i32, i32, i32]),
     "jinf_b200_attention_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     # gguf.h

@@ -94,6 +94,34 @@ def gemv_q4t_rmsnorm(q4t, h, gain, eps: float, y, rows: int, cols: int, stream=N
             "jinf_b200_gemv_q4t_rmsnorm")
 
 
+def q4m_bytes(rows: int, cols: int) -> int:
+    return int(L.lib.jinf_b200_q4m_bytes(rows, cols))
+
+
+def q4m_pack(aos, q4m, rows: int, cols: int, stream=None) -> None:
+    L.check(L.lib.jinf_b200_q4m_pack(_p(aos), _p(q4m), rows, cols, _s(stream)), "jinf_b200_q4m_pack")
+
+
+def gemv_q4m_workspace_bytes(rows: int, cols: int) -> int:
+    return int(L.lib.jinf_b200_gemv_q4m_workspace_bytes(rows, cols))
+
+
+def gemv_q4m(q4m, x, y, rows: int, cols: int, workspace=None, kw: int = 0, stream=None) -> None:
+    """kw = 0 picks the K split for the device; kw > 1 needs a zeroed workspace tensor."""
+    import torch
+    xt = L.F32 if x.dtype == torch.float32 else L.F16
+    ws = _p(workspace) if workspace is not None else None
+    L.check(L.lib.jinf_b200_gemv_q4m(_p(q4m), _p(x), xt, _p(y), rows, cols, ws, kw, _s(stream)),
+            "jinf_b200_gemv_q4m")
+
+
+def gemv_q4m_rmsnorm(q4m, h, gain, eps: float, y, rows: int, cols: int, workspace=None, kw: int = 0,
+                     stream=None) -> None:
+    ws = _p(workspace) if workspace is not None else None
+    L.check(L.lib.jinf_b200_gemv_q4m_rmsnorm(_p(q4m), _p(h), _p(gain), eps, _p(y), rows, cols, ws, kw,
+                                             _s(stream)), "jinf_b200_gemv_q4m_rmsnorm")
+
+
 def attention_workspace_bytes(n_kv_heads: int, head_dim: int, max_ctx: int) -> int:
     return int(L.lib.jinf_b200_attention_workspace_bytes(n_kv_heads, head_dim, max_ctx))
 

@@ -1,0 +1,130 @@
+"""The tensor-core Q4M GEMV (jinf_b200_q4m_* / jinf_b200_gemv_q4m*) on the GPU: the device
+repack against the numpy statement of the layout (bit-exact), and the GEMV against the CPU
+oracle (reference cuda/matmul_kernels.cu:8-43) within 1e-3 relative, for every K split."""
+import numpy as np
+import pytest
+import torch
+
+import q4m_ref
+from oracle import oracle
+from test_q4m_layout import q4_0_rows, rel_err
+
+pytestmark = pytest.mark.gpu
+
+REL = 1e-3
+
+SHAPES = [(4096, 4096), (1024, 4096), (6144, 4096), (28672, 4096), (4096, 14336), (4096, 512), (4096, 1792),
+          (768, 512), (2816, 512), (512, 1408), (1, 128), (37, 384), (130, 4096), (128256, 4096)]
+
+
+def packed(w, rows, cols, cuda):
+    from jinf import kernels as K
+    q = torch.empty(K.q4m_bytes(rows, cols), dtype=torch.uint8, device=cuda)
+    K.q4m_pack(torch.from_numpy(np.ascontiguousarray(w)).to(cuda), q, rows, cols)
+    return q
+
+
+def workspace(rows, cols, cuda):
+    from jinf import kernels as K
+    return torch.zeros(K.gemv_q4m_workspace_bytes(rows, cols), dtype=torch.uint8, device=cuda)
+
+
+@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (100, 1408), (4096, 4096)])
+def test_q4m_pack_matches_layout(cuda, rows, cols):
+    w = q4_0_rows(rows, cols, seed=rows)
+    got = packed(w, rows, cols, cuda).cpu().numpy()
+    assert np.array_equal(got, q4m_ref.pack(w, rows, cols))
+
+
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_gemv_q4m_fp32(cuda, rows, cols):
+    from jinf import kernels as K
+    w = q4_0_rows(rows, cols, seed=rows + 3 * cols)
+    x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
+    q = packed(w, rows, cols, cuda)
+    ws = workspace(rows, cols, cuda)
+    xd = torch.from_numpy(x).to(cuda)
+    y1 = torch.empty(rows, dtype=torch.float32, device=cuda)
+    y2 = torch.empty(rows, dtype=torch.float32, device=cuda)
+    K.gemv_q4m(q, xd, y1, rows, cols, workspace=ws)
+    K.gemv_q4m(q, xd, y2, rows, cols, workspace=ws)  # counters reset themselves; deterministic sums
+    torch.cuda.synchronize()
+    want = oracle.matvec(w, 2, x, rows, cols)
+    assert rel_err(y1.cpu().numpy(), want) < REL
+    assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("rows,cols,kw", [(4096, 4096, 1), (4096, 4096, 2), (4096, 4096, 3), (4096, 4096, 32),
+                                          (37, 384, 3), (512, 1408, 11), (130, 4096, 7)])
+def test_gemv_q4m_every_k_split(cuda, rows, cols, kw):
+    from jinf import kernels as K
+    w = q4_0_rows(rows, cols, seed=kw)
+    x = np.random.default_rng(kw).standard_normal(cols).astype(np.float32)
+    q = packed(w, rows, cols, cuda)
+    ws = workspace(rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    ref = None
+    for _ in range(3):
+        K.gemv_q4m(q, torch.from_numpy(x).to(cuda), y, rows, cols, workspace=ws if kw > 1 else None, kw=kw)
+        torch.cuda.synchronize()
+        if ref is None:
+            ref = y.clone()
+        assert torch.equal(y, ref)
+    assert rel_err(y.cpu().numpy(), oracle.matvec(w, 2, x, rows, cols)) < REL
+
+
+def test_gemv_q4m_rejects_bad_split(cuda):
+    import jinf
+    from jinf import kernels as K
+    q = torch.zeros(K.q4m_bytes(16, 256), dtype=torch.uint8, device=cuda)
+    x = torch.zeros(256, dtype=torch.float32, device=cuda)
+    y = torch.zeros(16, dtype=torch.float32, device=cuda)
+    with pytest.raises(jinf.JinfError):
+        K.gemv_q4m(q, x, y, 16, 256, workspace=None, kw=2)   # kw > 1 without a workspace
+    ws = workspace(16, 256, cuda)
+    with pytest.raises(jinf.JinfError):
+        K.gemv_q4m(q, x, y, 16, 256, workspace=ws, kw=3)     # more parts than groups
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (128256, 4096), (4096, 14336)])
+def test_gemv_q4m_fp16_input(cuda, rows, cols):
+    from jinf import kernels as K
+    w = q4_0_rows(rows, cols, seed=11)
+    x16 = np.random.default_rng(2).standard_normal(cols).astype(np.float16)
+    q = packed(w, rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    K.gemv_q4m(q, torch.from_numpy(x16).to(cuda), y, rows, cols, workspace=workspace(rows, cols, cuda))
+    assert rel_err(y.cpu().numpy(), oracle.matvec(w, 2, x16.astype(np.float32), rows, cols)) < REL
+
+
+@pytest.mark.parametrize("xscale", [1e-6, 1.0, 1e5])
+def test_gemv_q4m_extreme_values(cuda, xscale):
+    """Every nibble value, scales from 1e-7 to 65504, inputs from 1e-6 to 1e5."""
+    from jinf import kernels as K
+    rows, cols = 64, 1024
+    rng = np.random.default_rng(0)
+    w = rng.integers(0, 256, size=(rows, cols // 32, 18), dtype=np.uint8)
+    d = np.array([1e-7, 6e-5, 1.0, 300.0, -2.5, 65504.0], dtype=np.float16)
+    w[..., 0:2] = np.frombuffer(rng.choice(d, size=rows * cols // 32).astype(np.float16).tobytes(),
+                                dtype=np.uint8).reshape(rows, cols // 32, 2)
+    w = w.reshape(rows, -1)
+    x = (rng.standard_normal(cols) * xscale).astype(np.float32)
+    q = packed(w, rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    K.gemv_q4m(q, torch.from_numpy(x).to(cuda), y, rows, cols, workspace=workspace(rows, cols, cuda))
+    assert rel_err(y.cpu().numpy(), oracle.matvec(w, 2, x, rows, cols)) < REL
+
+
+@pytest.mark.parametrize("rows,cols", [(6144, 4096), (768, 512)])
+def test_gemv_q4m_rmsnorm_prologue(cuda, rows, cols):
+    from jinf import kernels as K
+    rng = np.random.default_rng(rows)
+    w = q4_0_rows(rows, cols, seed=5)
+    h = rng.standard_normal(cols).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    q = packed(w, rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    K.gemv_q4m_rmsnorm(q, torch.from_numpy(h).to(cuda), torch.from_numpy(g).to(cuda), 1e-5, y, rows, cols,
+                       workspace=workspace(rows, cols, cuda))
+    want = oracle.matvec(w, 2, oracle.rmsnorm(h, g, 1e-5), rows, cols)
+    assert rel_err(y.cpu().numpy(), want) < REL
