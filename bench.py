@@ -4,13 +4,16 @@
 
 A step is one greedy decode token at batch 1 (the reference's per-token decode loop,
 reference src/engine.cpp:684-804), after a 512-token prompt: positions 512+W .. 512+W+K-1.
-  value  tokens/s with everything resident in HBM: K graph replays back to back, the
-         argmax token fed back on the device (CUDA events on the engine stream, max over
-         ranks).
+  value  tokens/s with everything resident in HBM: K decode steps back to back (one
+         persistent kernel per token on one GPU; the captured kernel-per-operation graph
+         under tensor parallelism), the argmax token fed back on the device (CUDA events on
+         the engine stream, max over ranks).
   e2e    the same K tokens through jinf_engine_generate with host buffers: per token a
          4-byte H2D of the fed-back id from pinned memory and a 4-byte D2H of the argmax.
-  roofline  the dominant kernel (gate|up GEMV, 66 MB per launch) timed alone with CUDA
-         events against the measured HBM copy bandwidth.
+  roofline  the dominant kernel against the measured HBM copy bandwidth: on one GPU the
+         persistent step kernel itself (algorithmic bytes per launch = quantized weights +
+         KV rows read per token, timed by the same CUDA events as `value`); under tensor
+         parallelism the costliest per-operation GEMV timed alone.
   cpu_baseline  the CPU oracle (restated reference math, reference dequant conventions)
          on the host cores, a bounded sample of the same decode, rank 0 at N=1 only.
 Under torchrun (N > 1) the model is tensor parallel over the ranks (NCCL allreduce inside
@@ -213,7 +216,8 @@ def run_reference(args, rank, world):
 
 def gemv_microbench(dev, peak):
     """C2: Q4_0 GEMV on the 8B projection shapes, batch 1, fp16 x, rotating weight copies
-    so every launch streams from HBM (>= 4x L2 of weights per shape)."""
+    so every launch streams from HBM (>= 4x L2 of weights per shape); the launches are
+    captured in a CUDA graph so the host launch rate does not cap small shapes."""
     import numpy as np
     import torch
     from jinf import kernels as K
@@ -223,28 +227,37 @@ def gemv_microbench(dev, peak):
     for rows, cols in shapes:
         wbytes = rows * cols // 32 * 18
         copies = max(2, int(4 * 126e6 // wbytes) + 1)
-        nq = K.q4t_bytes(rows, cols)
+        nq = K.q4m_bytes(rows, cols)
         syn = jinf.SynthModel(jinf.LlamaShape(1, cols, 32, 8, 4096, rows), seed=rows)
         aos = torch.empty(wbytes, dtype=torch.uint8, device=dev)
         syn.read_rows_device("output.weight", aos)
         qs = []
         for c in range(copies):
             q = torch.empty(nq, dtype=torch.uint8, device=dev)
-            K.q4t_pack(aos, q, rows, cols)
+            K.q4m_pack(aos, q, rows, cols)
             qs.append(q)
         del aos
+        ws = torch.zeros(K.gemv_q4m_workspace_bytes(rows, cols), dtype=torch.uint8, device=dev)
         x = torch.from_numpy(np.random.default_rng(0).standard_normal(cols).astype(np.float16)).to(dev)
         y = torch.empty(rows, dtype=torch.float32, device=dev)
         for i in range(3):
-            K.gemv_q4t(qs[i % copies], x, y, rows, cols)
-        n = 50
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            K.gemv_q4m(qs[i % copies], x, y, rows, cols, workspace=ws)
         torch.cuda.synchronize()
+        n = copies * max(1, 60 // copies)
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(n):
+                    K.gemv_q4m(qs[i % copies], x, y, rows, cols, workspace=ws)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for i in range(n):
-            K.gemv_q4t(qs[i % copies], x, y, rows, cols)
+        g.replay()
         e1.record()
         torch.cuda.synchronize()
+        del g
         us = e0.elapsed_time(e1) * 1000.0 / n
         gbs = (wbytes + 2 * cols + 4 * rows) / (us * 1e-6) / 1e9
         out[f"{rows}x{cols}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3)}
@@ -310,16 +323,27 @@ def run_ours(args, rank, world, local):
     e2e_s = all_max(dist, t1 - t0)
     e2e = len(out) / e2e_s
 
-    # ---- roofline: dominant kernel timed alone (CUDA events), per-launch algorithmic bytes
-    prof = eng.profile_kernels(reps=max(32, shape.n_layers))
-    top = max(("qkv", "o_proj", "gate_up", "down", "lm_head"), key=lambda k: prof[k]["us"] * (32 if k != "lm_head" else 1))
-    achieved = prof[top]["bytes"] / (prof[top]["us"] * 1e-6) / 1e9
+    # ---- roofline of the dominant kernel, per-launch algorithmic bytes / CUDA-event time
+    persistent = eng.persistent
+    prof = eng.profile_kernels(reps=max(32, shape.n_layers))  # kernel-per-operation form, each timed alone
     wbytes = eng.weight_bytes_per_token()
     kv_bytes = 2 * 2 * shape.n_layers * (shape.n_heads_kv // world) * shape.head_dim * (PROMPT + args.warmup + args.steps / 2)
     step_gbs = (wbytes + kv_bytes) / (dev_s / args.steps) / 1e9
+    if persistent:
+        roof = {"bound": "hbm", "kernel": "k_step (persistent decode step, one launch per token)",
+                "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(step_gbs / peak, 4),
+                "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": int(wbytes + kv_bytes),
+                "us_per_launch": round(1e6 * dev_s / args.steps, 2)}
+    else:
+        top = max(("qkv", "o_proj", "gate_up", "down", "lm_head"),
+                  key=lambda k: prof[k]["us"] * (shape.n_layers if k != "lm_head" else 1))
+        achieved = prof[top]["bytes"] / (prof[top]["us"] * 1e-6) / 1e9
+        roof = {"bound": "hbm", "kernel": f"k_gemv_q4m ({top})", "achieved": round(achieved, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                "bytes_per_launch": prof[top]["bytes"], "us_per_launch": round(prof[top]["us"], 2)}
 
     gemv = gemv_microbench(dev, peak) if (world == 1 and args.config == "8b" and not args.no_gemv) else None
-    launches_per_step = shape.n_layers * 5 + 2
+    launches_per_step = 1 if persistent else shape.n_layers * 5 + 2
     line = None
     if rank == 0:
         cpu = None
@@ -339,14 +363,11 @@ def run_ours(args, rank, world, local):
                        "l2": f"{wbytes / 1e9:.2f} GB of weights streamed per step >> 126 MB L2 (no flush needed)"},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
             "gpu_launches": launches_per_step * args.steps,
-            "roofline": {"bound": "hbm", "kernel": f"q4t_gemv_{top}", "achieved": round(achieved, 1),
-                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": peak_kind, "traffic": None,
-                         "bytes_per_launch": prof[top]["bytes"], "us_per_launch": round(prof[top]["us"], 2)},
+            "roofline": roof,
             "decode_roofline": {"weights_bytes_per_token": wbytes, "kv_bytes_per_token_avg": int(kv_bytes),
                                 "achieved_GBs": round(step_gbs, 1), "frac": round(step_gbs / peak, 4),
                                 "roofline_tok_s": round(peak * 1e9 / (wbytes + kv_bytes), 1)},
-            "kernels_us": {k: round(v["us"], 2) for k, v in prof.items()},
+            "per_op_kernels_us": {k: round(v["us"], 2) for k, v in prof.items()},
             "clocks": clk.summary(),
             "load_s": round(t_load, 1),
         }

@@ -1,8 +1,8 @@
 // jinf-b200: new entry points with no counterpart in the reference ABI.
 //
 // These expose the engine's B200 building blocks so callers and tests can use them
-// outside the engine: the lossless Q4T weight layout, the fused Q4_0 GEMV over it and
-// the fp16-KV split-K decode attention. Same conventions as the reference kernel ABI
+// outside the engine: the lossless Q4M weight layout, the tensor-core Q4_0 GEMV over it
+// and the fp16-KV split-K decode attention. Same conventions as the reference kernel ABI
 // (device pointers owned by the caller, asynchronous on `stream`) except that each
 // returns a jinf_status instead of void.
 #pragma once
@@ -17,23 +17,6 @@ typedef struct CUstream_st* cudaStream_t;
 #ifdef __cplusplus
 extern "C" {
 #endif
-
-// Bytes of the Q4T image of a rows x cols Q4_0 matrix; 0 if cols is not a multiple of 128.
-uint64_t jinf_b200_q4t_bytes(int rows, int cols);
-
-// Repack reference AoS Q4_0 blocks [rows][cols/32] (device) into Q4T (device, q4t_bytes).
-// Lossless: every nibble and scale is moved, none is re-quantised.
-jinf_status jinf_b200_q4t_pack(const void* aos, void* q4t, int rows, int cols, cudaStream_t stream);
-
-// y[rows] = W . x over a Q4T matrix; x is fp32 (x_type = JINF_TYPE_F32) or fp16
-// (x_type = JINF_TYPE_F16), accumulation fp32. The batch-1 decode GEMV of the engine.
-jinf_status jinf_b200_gemv_q4t(const void* q4t, const void* x, int x_type, float* y, int rows, int cols,
-                               cudaStream_t stream);
-
-// y[rows] = W . (rmsnorm(h) * gain), the engine's fused RMSNorm-prologue GEMV; h and
-// gain are fp32 [cols].
-jinf_status jinf_b200_gemv_q4t_rmsnorm(const void* q4t, const float* h, const float* gain, float eps, float* y,
-                                       int rows, int cols, cudaStream_t stream);
 
 // Bytes of the Q4M image of a rows x cols Q4_0 matrix; 0 if cols is not a multiple of 128.
 // Q4M is the layout of the tensor-core GEMV: 16-row tiles x 128-column groups, 1152 bytes

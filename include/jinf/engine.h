@@ -101,6 +101,7 @@ typedef struct jinf_b200_options {
     int   sparse_mode;      // 0 dense FFN (default), 1 predictor top-k, 2 fixed mask
     float sparse_keep;      // fraction of FFN neurons kept in sparse modes (default 0.15)
     uint64_t sparse_seed;   // seed of the predictor weights / fixed masks
+    int   persistent;       // tp_size 1: run each token as one persistent kernel (default 1)
 } jinf_b200_options;
 
 static inline jinf_b200_options jinf_b200_options_default(void) {
@@ -115,6 +116,7 @@ static inline jinf_b200_options jinf_b200_options_default(void) {
     o.sparse_mode = 0;
     o.sparse_keep = 0.15f;
     o.sparse_seed = 0;
+    o.persistent = 1;
     return o;
 }
 
@@ -158,6 +160,8 @@ jinf_status jinf_engine_last_argmax(jinf_engine* e, int32_t* token);
 // Fill the KV cache positions [0, n_pos) of every layer with seeded N(0,1) fp16 values
 // and set n_past = n_pos (timing-only shortcut for long contexts).
 jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uint64_t seed);
+// 1 when each decode token runs as one persistent kernel, 0 for one kernel per operation.
+int         jinf_engine_is_persistent(const jinf_engine* e);
 // Bytes of quantized weights this rank streams per token (algorithmic weight traffic).
 uint64_t    jinf_engine_weight_bytes_per_token(const jinf_engine* e);
 // Time one launch of each fused kernel kind on its own (CUDA events, `reps` repetitions

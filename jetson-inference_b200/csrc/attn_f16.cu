@@ -14,7 +14,7 @@
 // Cache layout: [n_kv_heads][max_ctx][hd] fp16 per layer; n = pos + 1 is read from the
 // device state, so one captured graph serves every position.
 #include "common.cuh"
-#include "q4t.cuh"
+#include "device_state.cuh"
 #include "attn_f16.h"
 
 #include <math.h>

@@ -4,7 +4,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 
-#include "q4t.cuh"
+#include "device_state.cuh"
 
 namespace jinf {
 

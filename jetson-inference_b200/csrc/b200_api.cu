@@ -4,9 +4,9 @@
 
 #include "attn_f16.h"
 #include "common.cuh"
-#include "gemv_q4t.h"
+#include "gemv.h"
+#include "device_state.cuh"
 #include "q4m.cuh"
-#include "q4t.cuh"
 
 using namespace jinf;
 
@@ -22,45 +22,6 @@ static int device_sms() {
         sms[dev] = n;
     }
     return sms[dev];
-}
-
-extern "C" uint64_t jinf_b200_q4t_bytes(int rows, int cols) {
-    Q4TShape sh;
-    return q4t_shape(rows, cols, &sh) ? sh.bytes : 0;
-}
-
-extern "C" jinf_status jinf_b200_q4t_pack(const void* aos, void* q4t, int rows, int cols, cudaStream_t stream) {
-    Q4TShape sh;
-    if (!aos || !q4t || !q4t_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
-    return q4t_repack(aos, q4t, sh, stream) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
-}
-
-extern "C" jinf_status jinf_b200_gemv_q4t(const void* q4t, const void* x, int x_type, float* y, int rows, int cols,
-                                          cudaStream_t stream) {
-    Q4TShape sh;
-    if (!q4t || !x || !y || !q4t_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
-    if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
-    GemvParams p{};
-    gemv_params_for(p, q4t, sh);
-    p.x = x;
-    p.y = y;
-    const int xm = x_type == JINF_TYPE_F32 ? X_PLAIN_F32 : X_PLAIN_F16;
-    const int grid = gemv_grid(p, xm, EPI_STORE, device_sms());
-    return gemv_launch(p, xm, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
-}
-
-extern "C" jinf_status jinf_b200_gemv_q4t_rmsnorm(const void* q4t, const float* h, const float* gain, float eps,
-                                                  float* y, int rows, int cols, cudaStream_t stream) {
-    Q4TShape sh;
-    if (!q4t || !h || !gain || !y || !q4t_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
-    GemvParams p{};
-    gemv_params_for(p, q4t, sh);
-    p.hin = h;
-    p.norm_w = gain;
-    p.eps = eps;
-    p.y = y;
-    const int grid = gemv_grid(p, X_RMSNORM, EPI_STORE, device_sms());
-    return gemv_launch(p, X_RMSNORM, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
 }
 
 extern "C" uint64_t jinf_b200_q4m_bytes(int rows, int cols) {

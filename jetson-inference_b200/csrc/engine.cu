@@ -3,7 +3,10 @@
 //
 // Per token and per layer the reference issues 16 stream operations (7 GEMVs, 2
 // RMSNorms, RoPE, 2 KV memcpys, attention, SiLU-mul, 2 residual adds,
-// reference src/engine.cpp:418-511). Here a layer is 5 fused kernels:
+// reference src/engine.cpp:418-511). On one GPU the whole token is ONE persistent
+// cooperative kernel (step_kernel.cu) that streams every layer's weights without stopping
+// at phase boundaries. Tensor-parallel runs (NCCL allreduce between phases) and the FFN
+// hook use the kernel-per-operation form, where a layer is 5 fused kernels:
 //   1. QKV GEMV   prologue: h = h + y_down (residual), RMSNorm(attn_norm)
 //                 epilogue: RoPE(q,k) at pos, q -> fp32, k/v -> fp16 KV cache
 //   2. attention  split-K GQA over positions 0..pos
@@ -16,10 +19,10 @@
 // memory. Residual adds are folded into the next prologue (ping-pong h buffers), so the
 // reference's fp32 order "h += proj; rmsnorm(h)" is kept exactly.
 //
-// Weights: every projection is repacked (losslessly) into the Q4T layout in one HBM
-// arena laid out in consumption order; each GEMV prefetches the next matrix into L2
-// (cp.async.bulk.prefetch.L2) before it waits on its inputs, so HBM keeps streaming
-// across kernel boundaries.
+// Weights: every projection is repacked (losslessly) into the Q4M layout (q4m.cuh) in one
+// HBM arena laid out in consumption order; in the kernel-per-operation form each GEMV
+// prefetches the next matrix into L2 (cp.async.bulk.prefetch.L2) before it waits on its
+// inputs, so HBM keeps streaming across kernel boundaries.
 #include "jinf/engine.h"
 #include "jinf/kernels.h"
 #include "jinf/quant.h"
@@ -27,9 +30,11 @@
 
 #include "attn_f16.h"
 #include "common.cuh"
-#include "gemv_q4t.h"
+#include "device_state.cuh"
+#include "gemv.h"
 #include "nccl_shim.h"
-#include "q4t.cuh"
+#include "q4m.cuh"
+#include "step.h"
 #include "synth_internal.h"
 
 #include <fcntl.h>
@@ -248,16 +253,16 @@ struct jinf_engine_impl {
     uint64_t arena_bytes = 0;
     uint64_t weight_bytes_token = 0;  // algorithmic quantized bytes per token (this rank)
     struct Layer {
-        uint8_t* qkv; Q4TShape qkv_sh;
-        uint8_t* o; Q4TShape o_sh;
-        uint8_t* gu; Q4TShape gu_sh;
-        uint8_t* down; Q4TShape down_sh;
+        uint8_t* qkv; Q4MShape qkv_sh;
+        uint8_t* o; Q4MShape o_sh;
+        uint8_t* gu; Q4MShape gu_sh;
+        uint8_t* down; Q4MShape down_sh;
         float* attn_norm;
         float* ffn_norm;
     };
     std::vector<Layer> layers;
     uint8_t* lm = nullptr;
-    Q4TShape lm_sh{};
+    Q4MShape lm_sh{};
     float* out_norm = nullptr;
     float* norms = nullptr;  // all norm gains
     float* embed = nullptr;  // [V][d] f32
@@ -280,6 +285,16 @@ struct jinf_engine_impl {
     DeviceState* st = nullptr;
     int32_t* pinned = nullptr;  // [0] token in, [1] token out
     int32_t* dev_tokens = nullptr;  // prompt tokens of the current forward() [max_ctx]
+    // split-K workspace of the stand-alone GEMV kernels
+    float* gemv_part = nullptr;
+    unsigned int* gemv_cnt = nullptr;
+    // persistent step (tp_size == 1): phase tables on the device, counters, partials
+    bool persistent = false;
+    int step_grid = 0;
+    StepPhase* d_phases = nullptr;  // [n_full + n_body]
+    unsigned int* step_done = nullptr;
+    float* step_attn_part = nullptr;
+    StepParams sp_full{}, sp_body{};
     // ops and graphs
     std::vector<Op> ops_full, ops_body;
     cudaGraphExec_t exec_full = nullptr, exec_body = nullptr;
@@ -293,7 +308,7 @@ namespace {
 jinf_status run_op(jinf_engine_impl* I, const Op& op, cudaStream_t s) {
     cudaError_t e = cudaSuccess;
     switch (op.kind) {
-        case OP_GEMV: e = gemv_launch(op.gp, op.xm, op.epi, op.grid, s, true); break;
+        case OP_GEMV: e = gemvm_launch(op.gp, op.xm, op.epi, op.grid, s, true); break;
         case OP_ATTN: e = attn_launch(op.ap, s, true); break;
         case OP_FINALIZE: k_finalize<<<1, 1, 0, s>>>(I->st, op.with_argmax); e = cudaGetLastError(); break;
         case OP_ALLREDUCE_F32:
@@ -340,11 +355,20 @@ jinf_status capture(jinf_engine_impl* I, const std::vector<Op>& ops, cudaGraphEx
     return JINF_OK;
 }
 
+constexpr int kEngineMaxKw = 16;  // K parts per tile of the stand-alone GEMVs
+
 // Build the op list of one decode step. `with_head` adds the LM head + argmax.
 void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
     ops.clear();
-    auto gemv_bytes = [](const Q4TShape& sh, int in_elems, int out_elems) -> uint64_t {
-        return (uint64_t)sh.rows * sh.nb * 18 + 4ull * in_elems + 4ull * out_elems;
+    auto gemv_bytes = [](const Q4MShape& sh, int in_elems, int out_elems) -> uint64_t {
+        return (uint64_t)sh.rows * (sh.cols / 32) * 18 + 4ull * in_elems + 4ull * out_elems;
+    };
+    // grid and K split of a stand-alone GEMV
+    auto finish = [&](Op& op) {
+        op.grid = gemvm_grid(op.gp.cols, op.xm, op.epi, I->num_sms);
+        op.gp.kw = gemvm_pick_kw(op.gp.tiles, op.gp.groups, op.grid, kEngineMaxKw);
+        op.gp.part = I->gemv_part;
+        op.gp.cnt = I->gemv_cnt;
     };
     for (int L = 0; L < I->L; ++L) {
         const auto& ly = I->layers[L];
@@ -352,7 +376,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         Op qkv{OP_GEMV};
         qkv.role = ROLE_QKV;
         qkv.layer = L;
-        gemv_params_for(qkv.gp, ly.qkv, ly.qkv_sh);
+        gemvm_params_for(qkv.gp, ly.qkv, ly.qkv_sh);
         qkv.xm = L == 0 ? X_EMBED_NORM : X_RMSNORM;
         qkv.epi = EPI_QKV;
         qkv.gp.hin = I->hB;
@@ -372,7 +396,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         qkv.gp.st = I->st;
         qkv.gp.pf_ptr = ly.o;
         qkv.gp.pf_bytes = ly.o_sh.bytes;
-        qkv.grid = gemv_grid(qkv.gp, qkv.xm, qkv.epi, I->num_sms);
+        finish(qkv);
         qkv.bytes = gemv_bytes(ly.qkv_sh, I->d, ly.qkv_sh.rows);
         ops.push_back(qkv);
 
@@ -394,7 +418,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         Op o{OP_GEMV};
         o.role = ROLE_O;
         o.layer = L;
-        gemv_params_for(o.gp, ly.o, ly.o_sh);
+        gemvm_params_for(o.gp, ly.o, ly.o_sh);
         o.xm = X_PLAIN_F32;
         o.epi = EPI_STORE;
         o.gp.x = I->attn;
@@ -402,7 +426,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         o.gp.st = I->st;
         o.gp.pf_ptr = ly.gu;
         o.gp.pf_bytes = ly.gu_sh.bytes;
-        o.grid = gemv_grid(o.gp, o.xm, o.epi, I->num_sms);
+        finish(o);
         o.bytes = gemv_bytes(ly.o_sh, ly.o_sh.cols, ly.o_sh.rows);
         ops.push_back(o);
         if (I->tp_size > 1) {
@@ -415,7 +439,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         Op gu{OP_GEMV};
         gu.role = ROLE_GATEUP;
         gu.layer = L;
-        gemv_params_for(gu.gp, ly.gu, ly.gu_sh);
+        gemvm_params_for(gu.gp, ly.gu, ly.gu_sh);
         gu.xm = X_RMSNORM;
         gu.epi = EPI_GATEUP;
         gu.gp.hin = I->hA;
@@ -427,14 +451,14 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         gu.gp.st = I->st;
         gu.gp.pf_ptr = ly.down;
         gu.gp.pf_bytes = ly.down_sh.bytes;
-        gu.grid = gemv_grid(gu.gp, gu.xm, gu.epi, I->num_sms);
+        finish(gu);
         gu.bytes = gemv_bytes(ly.gu_sh, I->d, ly.gu_sh.rows / 2);
         ops.push_back(gu);
 
         Op dn{OP_GEMV};
         dn.role = ROLE_DOWN;
         dn.layer = L;
-        gemv_params_for(dn.gp, ly.down, ly.down_sh);
+        gemvm_params_for(dn.gp, ly.down, ly.down_sh);
         dn.xm = X_PLAIN_F32;
         dn.epi = EPI_STORE;
         dn.gp.x = I->act;
@@ -447,7 +471,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
             dn.gp.pf_ptr = I->lm;
             dn.gp.pf_bytes = I->lm_sh.bytes;
         }
-        dn.grid = gemv_grid(dn.gp, dn.xm, dn.epi, I->num_sms);
+        finish(dn);
         dn.bytes = gemv_bytes(ly.down_sh, ly.down_sh.cols, ly.down_sh.rows);
         ops.push_back(dn);
         if (I->tp_size > 1) {
@@ -460,7 +484,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
     if (with_head) {
         Op lm{OP_GEMV};
         lm.role = ROLE_LM;
-        gemv_params_for(lm.gp, I->lm, I->lm_sh);
+        gemvm_params_for(lm.gp, I->lm, I->lm_sh);
         lm.xm = X_RMSNORM;
         lm.epi = EPI_LMHEAD;
         lm.gp.hin = I->hB;
@@ -473,7 +497,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         lm.gp.st = I->st;
         lm.gp.pf_ptr = I->layers[0].qkv;
         lm.gp.pf_bytes = I->layers[0].qkv_sh.bytes;
-        lm.grid = gemv_grid(lm.gp, lm.xm, lm.epi, I->num_sms);
+        finish(lm);
         lm.bytes = gemv_bytes(I->lm_sh, I->d, I->lm_sh.rows);
         ops.push_back(lm);
         if (I->tp_size > 1) {
@@ -486,6 +510,119 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
     Op fin{OP_FINALIZE};
     fin.with_argmax = with_head ? 1 : 0;
     ops.push_back(fin);
+}
+
+// Phase table of the persistent step (tp_size == 1). Every phase
+// waits for the one before it; the residual stream is hA, updated in place by the o and
+// down epilogues.
+void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph) {
+    ph.clear();
+    auto add_gemv = [&](const uint8_t* w, const Q4MShape& sh, int xm, int epi) -> StepPhase& {
+        StepPhase p{};
+        p.kind = PH_GEMV;
+        p.xm = xm;
+        p.epi = epi;
+        p.w = w;
+        p.rows = sh.rows;
+        p.cols = sh.cols;
+        p.tiles = sh.tiles;
+        p.groups = sh.groups;
+        ph.push_back(p);
+        return ph.back();
+    };
+    for (int L = 0; L < I->L; ++L) {
+        const auto& ly = I->layers[L];
+        __half* kc = I->kc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        __half* vc = I->vc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        StepPhase& qkv = add_gemv(ly.qkv, ly.qkv_sh, L == 0 ? X_EMBED_NORM : X_RMSNORM, EPI_QKV);
+        qkv.hsrc = L == 0 ? I->embed : I->hA;
+        qkv.hout = L == 0 ? I->hA : nullptr;
+        qkv.norm_w = ly.attn_norm;
+        qkv.y = I->q;
+        qkv.kcache = kc;
+        qkv.vcache = vc;
+        StepPhase at{};
+        at.kind = PH_ATTN;
+        at.q = I->q;
+        at.out = I->attn;
+        at.kcache = kc;
+        at.vcache = vc;
+        ph.push_back(at);
+        StepPhase& o = add_gemv(ly.o, ly.o_sh, X_PLAIN_F32, EPI_RESID);
+        o.x = I->attn;
+        o.y = I->hA;
+        StepPhase& gu = add_gemv(ly.gu, ly.gu_sh, X_RMSNORM, EPI_GATEUP);
+        gu.hsrc = I->hA;
+        gu.norm_w = ly.ffn_norm;
+        gu.y = I->act;
+        StepPhase& dn = add_gemv(ly.down, ly.down_sh, X_PLAIN_F32, EPI_RESID);
+        dn.x = I->act;
+        dn.y = I->hA;
+    }
+    if (with_head) {
+        StepPhase& lm = add_gemv(I->lm, I->lm_sh, X_RMSNORM, EPI_LMHEAD);
+        lm.hsrc = I->hA;
+        lm.norm_w = I->out_norm;
+        lm.y = I->logits;
+    }
+    for (size_t i = 0; i < ph.size(); ++i) {
+        ph[i].dep = (int)i - 1;
+        ph[i].dep_target = i == 0 ? 0u : ph[i - 1].kind == PH_GEMV ? (unsigned)ph[i - 1].tiles : (unsigned)I->Hkvl;
+    }
+}
+
+// Set up the persistent step: phase tables on the device, counters and partial buffers.
+// Returns JINF_OK with I->persistent = false when the shape does not fit the kernel.
+jinf_status setup_persistent(jinf_engine_impl* I) {
+    I->persistent = false;
+    const int G = I->Hl / I->Hkvl;
+    int max_cols = I->d;
+    for (const auto& ly : I->layers)
+        for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) max_cols = std::max(max_cols, sh->cols);
+    const unsigned xs = step_xstage_bytes(max_cols, G, I->hd);
+    const size_t smem = step_smem_bytes(xs, 5 * I->L + 1);
+    if (G > ATTN_MAX_GROUP || I->Hkvl > 64 || I->max_ctx > ATTN_POS_PER_CTA * ATTN_MAX_SPLIT || smem > 227 * 1024 ||
+        step_occupancy(smem) < 1) {
+        JINF_LOG("persistent step unavailable for this shape (%zu bytes of shared memory); using one kernel per "
+                 "operation", smem);
+        return JINF_OK;
+    }
+    I->step_grid = I->num_sms;
+    std::vector<StepPhase> full, body;
+    build_step(I, true, full);
+    build_step(I, false, body);
+    const size_t attn_floats = (size_t)I->Hkvl * ATTN_MAX_SPLIT * ATTN_MAX_GROUP * (I->hd + 2);
+    std::vector<StepPhase> all(full);
+    all.insert(all.end(), body.begin(), body.end());
+    JINF_CUDA_CHECK(cudaMalloc(&I->d_phases, sizeof(StepPhase) * all.size()));
+    JINF_CUDA_CHECK(cudaMalloc(&I->step_done, sizeof(unsigned int) * (full.size() + 1)));
+    JINF_CUDA_CHECK(cudaMalloc(&I->step_attn_part, sizeof(float) * attn_floats));
+    JINF_CUDA_CHECK(cudaMemcpy(I->d_phases, all.data(), sizeof(StepPhase) * all.size(), cudaMemcpyHostToDevice));
+    JINF_CUDA_CHECK(cudaMemset(I->step_done, 0, sizeof(unsigned int) * (full.size() + 1)));
+    StepParams sp{};
+    sp.done = I->step_done;
+    sp.attn_part = I->step_attn_part;
+    sp.st = I->st;
+    sp.nq = I->Hl * I->hd;
+    sp.nk = I->Hkvl * I->hd;
+    sp.head_dim = I->hd;
+    sp.max_ctx = I->max_ctx;
+    sp.n_heads = I->Hl;
+    sp.n_kv_heads = I->Hkvl;
+    sp.rope_base = I->rope_base;
+    sp.eps = I->eps;
+    sp.xstage_bytes = xs;
+    sp.spin_limit = 4000000ull;  // about a second of polling: far beyond any phase, never a hang
+    I->sp_full = sp;
+    I->sp_full.phases = I->d_phases;
+    I->sp_full.n_phases = (int)full.size();
+    I->sp_full.with_argmax = 1;
+    I->sp_body = sp;
+    I->sp_body.phases = I->d_phases + full.size();
+    I->sp_body.n_phases = (int)body.size();
+    I->sp_body.with_argmax = 0;
+    I->persistent = true;
+    return JINF_OK;
 }
 
 // ---------------------------------------------------------------- loading
@@ -545,8 +682,8 @@ struct Loader {
     }
 
     // Repack the staged AoS matrix into the arena.
-    jinf_status pack(uint8_t* dst, const Q4TShape& sh) {
-        JINF_CUDA_CHECK(q4t_repack(dstage, dst, sh, I->stream));
+    jinf_status pack(uint8_t* dst, const Q4MShape& sh) {
+        JINF_CUDA_CHECK(q4m_repack(dstage, dst, sh, I->stream));
         JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
         return JINF_OK;
     }
@@ -606,7 +743,8 @@ void free_impl(jinf_engine_impl* I) {
         if (n) n->CommDestroy(I->comm);
     }
     void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
-                    I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens};
+                    I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
+                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);
@@ -686,8 +824,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     const int qkv_rows = (I->Hl + 2 * I->Hkvl) * hd;
     I->layers.resize(I->L);
     uint64_t off = 0;
-    auto place = [&](Q4TShape& sh, int rows, int cols, uint8_t*& ptr) -> bool {
-        if (!q4t_shape(rows, cols, &sh)) return false;
+    auto place = [&](Q4MShape& sh, int rows, int cols, uint8_t*& ptr) -> bool {
+        if (!q4m_shape(rows, cols, &sh) || cols > gemvm_max_cols()) return false;
         ptr = (uint8_t*)(uintptr_t)off;  // offset for now
         off += (sh.bytes + 255) & ~255ull;
         I->weight_bytes_token += (uint64_t)rows * (cols / 32) * 18;
@@ -697,7 +835,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         auto& ly = I->layers[L];
         if (!place(ly.qkv_sh, qkv_rows, d, ly.qkv) || !place(ly.o_sh, d, I->Hl * hd, ly.o) ||
             !place(ly.gu_sh, 2 * I->ffl, d, ly.gu) || !place(ly.down_sh, d, I->ffl, ly.down)) {
-            JINF_LOG("matrix shapes not supported by the Q4T layout (columns must be multiples of 128)");
+            JINF_LOG("matrix shapes not supported by the Q4M layout (columns must be multiples of 128)");
             return fail(JINF_ERR_INVALID);
         }
     }
@@ -737,6 +875,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
               cudaMalloc(&I->st, sizeof(DeviceState)) == cudaSuccess &&
               cudaMalloc(&I->dev_tokens, sizeof(int32_t) * (size_t)I->max_ctx) == cudaSuccess &&
               cudaHostAlloc(&I->pinned, 4 * sizeof(int32_t), cudaHostAllocDefault) == cudaSuccess;
+    if (ok) I->pinned[2] = DEV_OK;
     if (ok && tp > 1) ok = cudaMalloc(&I->logits_full, sizeof(float) * (size_t)I->V) == cudaSuccess;
     if (!ok) return fail(JINF_ERR_OOM);
     if (tp == 1) I->logits_full = I->logits;
@@ -751,9 +890,9 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         Loader ld{I, &src};
         size_t max_stage = 0;
         for (const auto& ly : I->layers)
-            for (const Q4TShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh})
-                max_stage = std::max(max_stage, (size_t)sh->rows * sh->nb * 18);
-        max_stage = std::max(max_stage, (size_t)I->lm_sh.rows * I->lm_sh.nb * 18);
+            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh})
+                max_stage = std::max(max_stage, (size_t)sh->rows * (sh->cols / 32) * 18);
+        max_stage = std::max(max_stage, (size_t)I->lm_sh.rows * (I->lm_sh.cols / 32) * 18);
         if (ld.ensure_dstage(max_stage) != JINF_OK) return fail(JINF_ERR_OOM);
         const int64_t rb_d = (int64_t)(d / 32) * 18;  // AoS row bytes of a d-column matrix
         char nm[128];
@@ -830,6 +969,21 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         }
     }
 
+    // ---- split-K workspace of the stand-alone GEMVs (counters zero, self-resetting)
+    {
+        size_t tiles = I->lm_sh.tiles;
+        for (const auto& ly : I->layers)
+            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) tiles = std::max(tiles, (size_t)sh->tiles);
+        if (cudaMalloc(&I->gemv_part, sizeof(float) * tiles * kEngineMaxKw * 16) != cudaSuccess ||
+            cudaMalloc(&I->gemv_cnt, sizeof(unsigned int) * tiles) != cudaSuccess)
+            return fail(JINF_ERR_OOM);
+        cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * tiles);
+    }
+    if (tp == 1 && opt.persistent) {
+        const jinf_status s = setup_persistent(I);
+        if (s != JINF_OK) return fail(s);
+    }
+
     // ---- step programs
     build_ops(I, true, I->ops_full);
     build_ops(I, false, I->ops_body);
@@ -856,9 +1010,9 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     e->compute_stream = I->stream;
     e->impl = I;
     *out = e;
-    JINF_LOG("engine ready: %d layers, d=%d, heads %d/%d, ff=%d, vocab=%d, tp %d/%d, weights %.1f MB/rank, "
-             "attention splits %d",
-             I->L, I->d, I->H, I->Hkv, I->ff, I->V, I->tp_rank, tp, I->arena_bytes / 1048576.0, I->n_split);
+    JINF_LOG("engine ready: %d layers, d=%d, heads %d/%d, ff=%d, vocab=%d, tp %d/%d, weights %.1f MB/rank, %s",
+             I->L, I->d, I->H, I->Hkv, I->ff, I->V, I->tp_rank, tp, I->arena_bytes / 1048576.0,
+             I->persistent ? "persistent step kernel" : "one kernel per operation");
     return JINF_OK;
 }
 
@@ -886,13 +1040,15 @@ jinf_status step(jinf_engine* e, bool with_head) {
                 gp.hout = nullptr;
                 gp.y = I->gate_raw + I->ffl;  // [2*ffl] interleaved gate/up
                 gp.pf_bytes = 0;
-                JINF_CUDA_CHECK(gemv_launch(gp, X_RMSNORM, EPI_STORE, op.grid, I->stream, false));
+                JINF_CUDA_CHECK(gemvm_launch(gp, X_RMSNORM, EPI_STORE, op.grid, I->stream, false));
                 k_even_rows<<<(I->ffl + 255) / 256, 256, 0, I->stream>>>(I->gate_raw + I->ffl, I->gate_raw, I->ffl);
                 JINF_CUDA_CHECK(cudaGetLastError());
                 JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
                 e->ffn_hook(e->ffn_hook_data, op.layer, I->gate_raw, I->ffl);
             }
         }
+    } else if (I->persistent) {
+        JINF_CUDA_CHECK(step_launch(with_head ? I->sp_full : I->sp_body, I->step_grid, I->stream));
     } else if (I->use_graph) {
         JINF_CUDA_CHECK(cudaGraphLaunch(with_head ? I->exec_full : I->exec_body, I->stream));
     } else {
@@ -900,6 +1056,14 @@ jinf_status step(jinf_engine* e, bool with_head) {
     }
     e->n_past += 1;
     return JINF_OK;
+}
+
+// Device-side error recorded by a step (pinned[2], copied after the step): a dependency
+// wait of the persistent kernel that gave up.
+jinf_status device_error(jinf_engine_impl* I) {
+    if (I->pinned[2] == DEV_OK) return JINF_OK;
+    JINF_LOG("device error %d: a phase of the persistent step timed out waiting for its inputs", I->pinned[2]);
+    return JINF_ERR_TIMEOUT;
 }
 
 jinf_status gather_logits(jinf_engine* e) {
@@ -983,8 +1147,10 @@ extern "C" jinf_status jinf_engine_forward(jinf_engine* e, const int32_t* tokens
         JINF_CHECK(step(e, t == n_tokens - 1), "decode step");
     }
     JINF_CHECK(gather_logits(e), "logits gather");
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->pinned[2], &I->st->error, sizeof(int32_t), cudaMemcpyDeviceToHost, I->stream));
     JINF_CUDA_CHECK(cudaEventRecord(I->ev1, I->stream));
     JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    JINF_CHECK(device_error(I), "decode step");
     float ms = 0.f;
     cudaEventElapsedTime(&ms, I->ev0, I->ev1);
     *logits = I->logits_full;
@@ -999,9 +1165,11 @@ extern "C" jinf_status jinf_engine_last_argmax(jinf_engine* e, int32_t* token) {
     if (!e || !token || !e->impl || !e->impl->logits_valid) return JINF_ERR_INVALID;
     jinf_engine_impl* I = e->impl;
     JINF_CUDA_CHECK(cudaSetDevice(I->device));
-    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->pinned[1], &I->st->argmax_token, sizeof(int32_t), cudaMemcpyDeviceToHost,
+    // argmax_token and error are adjacent in the device state: one 8-byte read
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->pinned[1], &I->st->argmax_token, 2 * sizeof(int32_t), cudaMemcpyDeviceToHost,
                                     I->stream));
     JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    JINF_CHECK(device_error(I), "decode step");
     *token = I->pinned[1];
     return JINF_OK;
 }
@@ -1044,7 +1212,9 @@ extern "C" jinf_status jinf_engine_decode_resident(jinf_engine* e, int n_steps, 
             JINF_CUDA_CHECK(cudaMemcpyAsync(&out_tokens[i], &I->st->argmax_token, sizeof(int32_t),
                                             cudaMemcpyDeviceToHost, I->stream));
     }
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->pinned[2], &I->st->error, sizeof(int32_t), cudaMemcpyDeviceToHost, I->stream));
     JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    JINF_CHECK(device_error(I), "decode step");
     return JINF_OK;
 }
 
@@ -1062,6 +1232,10 @@ extern "C" jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uin
     JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
     e->n_past = n_pos;
     return JINF_OK;
+}
+
+extern "C" int jinf_engine_is_persistent(const jinf_engine* e) {
+    return e && e->impl && e->impl->persistent ? 1 : 0;
 }
 
 extern "C" uint64_t jinf_engine_weight_bytes_per_token(const jinf_engine* e) {

@@ -1,26 +1,17 @@
-// Host interface of the fused Q4T GEMV kernels (gemv_q4t.cu).
+// Host interface of the fused Q4M tensor-core GEMV kernels (gemv_q4m.cu).
 #pragma once
 
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "device_state.cuh"
 #include "q4m.cuh"
-#include "q4t.cuh"
 
 namespace jinf {
 
-#ifndef JINF_GEMV_THREADS
-#define JINF_GEMV_THREADS 256
-#endif
-#ifndef JINF_GEMV_NBUF
-#define JINF_GEMV_NBUF 3
-#endif
-constexpr int GEMV_THREADS = JINF_GEMV_THREADS;
-constexpr int GEMV_NBUF = JINF_GEMV_NBUF;  // shared-memory chunk slots per warp (GEMV_NBUF - 1 in flight)
-
-// Tensor-core GEMV over the Q4M layout (gemv_q4m.cu): one persistent CTA of 16 warps per
-// SM, each warp with a private ring of GEMV_M_NBUF chunk slots.
+// One CTA of 16 warps per SM (persistent), each warp with a private ring of GEMV_M_NBUF
+// chunk slots.
 #ifndef JINF_GEMV_M_NBUF
 #define JINF_GEMV_M_NBUF 5
 #endif
@@ -28,13 +19,11 @@ constexpr int GEMV_M_THREADS = 512;
 constexpr int GEMV_M_NBUF = JINF_GEMV_M_NBUF;
 
 enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3 };
-enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3 };
+enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3, EPI_RESID = 4 };
 
 struct GemvParams {
-    const uint8_t* w;  // Q4T or Q4M stream of the matrix
-    int rows, cols, lk, steps, tiles;
-    // Q4M only
-    int groups;             // cols / 128
+    const uint8_t* w;  // Q4M stream of the matrix
+    int rows, cols, tiles, groups;
     int kw;                 // K parts per tile (tasks per tile)
     float* part;            // kw > 1: [tiles * kw][16] partial row sums
     unsigned int* cnt;      // kw > 1: [tiles] arrival counters, zero before the first launch (self-resetting)
@@ -58,22 +47,6 @@ struct GemvParams {
     const uint8_t* pf_ptr;
     uint64_t pf_bytes;
 };
-
-inline void gemv_params_for(GemvParams& p, const void* w, const Q4TShape& sh) {
-    p.w = (const uint8_t*)w;
-    p.rows = sh.rows;
-    p.cols = sh.cols;
-    p.lk = sh.lk;
-    p.steps = sh.steps;
-    p.tiles = sh.tiles;
-}
-
-size_t gemv_smem_bytes(int cols, int lk);
-// Persistent grid size: min(tile groups, resident CTAs per SM * num_sms).
-int gemv_grid(const GemvParams& p, int xm, int epi, int num_sms);
-cudaError_t gemv_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
-// AoS Q4_0 [rows][cols] (device) -> Q4T (device, sh.bytes).
-cudaError_t q4t_repack(const void* aos, void* dst, const Q4TShape& sh, cudaStream_t s);
 
 inline void gemvm_params_for(GemvParams& p, const void* w, const Q4MShape& sh) {
     p.w = (const uint8_t*)w;

@@ -1,0 +1,77 @@
+// Host interface of the persistent decode-step kernel (step_kernel.cu).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "device_state.cuh"
+#include "gemv.h"
+
+namespace jinf {
+
+#ifndef JINF_STEP_NBUF
+#define JINF_STEP_NBUF 6
+#endif
+#ifndef JINF_STEP_PF_DIST
+#define JINF_STEP_PF_DIST 24
+#endif
+constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
+constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 chunks in flight)
+constexpr int STEP_PF_DIST = JINF_STEP_PF_DIST;  // L2 prefetch distance per warp, in chunks
+constexpr int ATTN_POS_PER_CTA = 512;  // attention positions per CTA: 16 warps x 32
+constexpr int ATTN_MAX_SPLIT = 64;     // CTAs per kv head (contexts up to 32768 positions)
+constexpr int ATTN_MAX_GROUP = 8;      // query heads per kv head
+
+enum PhaseKind { PH_GEMV = 0, PH_ATTN = 1 };
+
+// One phase of the decode step. A phase starts (on every CTA) once phase `dep` has
+// reported `dep_target` finished units: GEMV phases count finished 16-row tiles,
+// attention counts finished kv heads.
+struct StepPhase {
+    int kind;
+    int dep;                 // -1: no dependency
+    unsigned int dep_target;
+    // PH_GEMV
+    int xm, epi;
+    const uint8_t* w;        // Q4M matrix
+    int rows, cols, tiles, groups;
+    const float* x;          // X_PLAIN_F32: input (written earlier in the step)
+    const float* hsrc;       // X_RMSNORM: residual stream; X_EMBED_NORM: token_embd [V][cols]
+    float* hout;             // X_EMBED_NORM: residual stream (CTA 0 stores the embedding row)
+    const float* norm_w;     // RMSNorm gain
+    float* y;                // epilogue output; EPI_RESID: the residual stream (h += W x)
+    __half* kcache;          // EPI_QKV and PH_ATTN: this layer's cache [Hkv][max_ctx][hd]
+    __half* vcache;
+    // PH_ATTN
+    const float* q;          // [n_heads * hd], RoPE applied
+    float* out;              // [n_heads * hd]
+};
+
+struct StepParams {
+    const StepPhase* phases;  // device array
+    int n_phases;
+    unsigned int* done;       // [n_phases + 1] zero at launch; [n_phases] counts exiting CTAs
+    float* attn_part;         // [Hkv][ATTN_MAX_SPLIT][ATTN_MAX_GROUP][hd + 2] per-CTA attention partials
+    DeviceState* st;
+    int nq, nk, head_dim, max_ctx, n_heads, n_kv_heads;
+    float rope_base, eps;
+    int with_argmax;          // the last phase is the LM head: finish the argmax, feed it back
+    unsigned int xstage_bytes;  // shared bytes for the staged GEMV input / attention scratch
+    unsigned long long spin_limit;  // polls before a dependency wait gives up (DEV_ERR_TIMEOUT)
+};
+
+// CTA c of C owns tiles [step_cta_tile(c), step_cta_tile(c + 1)) of every GEMV phase.
+__host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)((long long)c * T / C); }
+
+// Shared bytes of the staged input for the widest GEMV phase, or of the attention scratch
+// (q of one kv head's query heads + per-warp partials), whichever is larger.
+unsigned int step_xstage_bytes(int max_cols, int group, int head_dim);
+size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases);
+// Launches the step on `grid` CTAs (one per SM) as a cooperative launch.
+cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s);
+// Resident CTAs per SM for this shared-memory size (must be >= 1).
+int step_occupancy(size_t smem);
+
+}  // namespace jinf

@@ -52,7 +52,7 @@ class EngineConfig(C.Structure):
 class B200Options(C.Structure):
     _fields_ = [("device", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int), ("nccl_id", C.c_void_p),
                 ("kv_type", C.c_int), ("use_graph", C.c_int), ("eos_token", C.c_int), ("sparse_mode", C.c_int),
-                ("sparse_keep", C.c_float), ("sparse_seed", C.c_uint64)]
+                ("sparse_keep", C.c_float), ("sparse_seed", C.c_uint64), ("persistent", C.c_int)]
 
 
 class PerfStats(C.Structure):
@@ -152,10 +152,6 @@ SIGNATURES = {
     # sparse_ops.h
     "jinf_cuda_sparse_ffn": (None, [vp, vp, vp, vp, i32, i32, i32, i32, vp, vp]),
     # b200.h
-    "jinf_b200_q4t_bytes": (u64, [i32, i32]),
-    "jinf_b200_q4t_pack": (i32, [vp, vp, i32, i32, vp]),
-    "jinf_b200_gemv_q4t": (i32, [vp, vp, i32, vp, i32, i32, vp]),
-    "jinf_b200_gemv_q4t_rmsnorm": (i32, [vp, vp, vp, f32, vp, i32, i32, vp]),
     "jinf_b200_q4m_bytes": (u64, [i32, i32]),
     "jinf_b200_q4m_pack": (i32, [vp, vp, i32, i32, vp]),
     "jinf_b200_gemv_q4m_workspace_bytes": (sz, [i32, i32]),
@@ -220,6 +216,7 @@ SIGNATURES = {
     "jinf_engine_decode_resident": (i32, [C.POINTER(Engine), i32, C.POINTER(C.c_int32)]),
     "jinf_engine_last_argmax": (i32, [C.POINTER(Engine), C.POINTER(C.c_int32)]),
     "jinf_engine_fill_kv_random": (i32, [C.POINTER(Engine), i32, u64]),
+    "jinf_engine_is_persistent": (i32, [vp]),
     "jinf_engine_weight_bytes_per_token": (u64, [C.POINTER(Engine)]),
     "jinf_engine_profile_kernels": (i32, [C.POINTER(Engine), i32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "jinf_nccl_get_unique_id": (i32, [vp]),

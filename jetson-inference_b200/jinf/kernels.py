@@ -75,25 +75,6 @@ def sparse_ffn(bundles, x, out, offsets, n_act: int, hidden: int, bundle_size: i
     _raise_last("jinf_cuda_sparse_ffn")
 
 
-def q4t_bytes(rows: int, cols: int) -> int:
-    return int(L.lib.jinf_b200_q4t_bytes(rows, cols))
-
-
-def q4t_pack(aos, q4t, rows: int, cols: int, stream=None) -> None:
-    L.check(L.lib.jinf_b200_q4t_pack(_p(aos), _p(q4t), rows, cols, _s(stream)), "jinf_b200_q4t_pack")
-
-
-def gemv_q4t(q4t, x, y, rows: int, cols: int, stream=None) -> None:
-    import torch
-    xt = L.F32 if x.dtype == torch.float32 else L.F16
-    L.check(L.lib.jinf_b200_gemv_q4t(_p(q4t), _p(x), xt, _p(y), rows, cols, _s(stream)), "jinf_b200_gemv_q4t")
-
-
-def gemv_q4t_rmsnorm(q4t, h, gain, eps: float, y, rows: int, cols: int, stream=None) -> None:
-    L.check(L.lib.jinf_b200_gemv_q4t_rmsnorm(_p(q4t), _p(h), _p(gain), eps, _p(y), rows, cols, _s(stream)),
-            "jinf_b200_gemv_q4t_rmsnorm")
-
-
 def q4m_bytes(rows: int, cols: int) -> int:
     return int(L.lib.jinf_b200_q4m_bytes(rows, cols))
 

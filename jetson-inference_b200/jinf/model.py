@@ -120,11 +120,12 @@ class SynthModel:
 
 
 def b200_options(device: int = 0, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
-                 use_graph: bool = True, eos_token: int = 2) -> L.B200Options:
+                 use_graph: bool = True, eos_token: int = 2, persistent: bool = True) -> L.B200Options:
     o = L.B200Options()
     o.device, o.tp_rank, o.tp_size = device, tp_rank, tp_size
     o.kv_type, o.use_graph, o.eos_token = L.F16, int(use_graph), eos_token
     o.sparse_mode, o.sparse_keep, o.sparse_seed = 0, 0.15, 0
+    o.persistent = int(persistent)
     o._nccl_buf = None
     if nccl_id is not None:
         buf = C.create_string_buffer(bytes(nccl_id), 128)
@@ -230,6 +231,11 @@ class Engine:
 
     def fill_kv_random(self, n_pos: int, seed: int = 0) -> None:
         L.check(L.lib.jinf_engine_fill_kv_random(self.h, n_pos, seed), "fill_kv_random")
+
+    @property
+    def persistent(self) -> bool:
+        """True when each decode token runs as one persistent kernel."""
+        return bool(L.lib.jinf_engine_is_persistent(self.h))
 
     def weight_bytes_per_token(self) -> int:
         return L.lib.jinf_engine_weight_bytes_per_token(self.h)
