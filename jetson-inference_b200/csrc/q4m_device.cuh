@@ -89,15 +89,19 @@ __device__ __forceinline__ void chunk_mma(uint32_t sl, const uint16_t* xb, const
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(sc) : "r"(sl + 1024 + lane * 4));
     const uint4 xv = *reinterpret_cast<const uint4*>(xb + (size_t)g * 256 + lane * 8);
     const float k = xk[g * 4 + (lane & 3)];
+    // four independent accumulator chains (steps i, i+4 share one) hide the MMA latency
     float da[4] = {k, 0.f, k, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+    float dc[4] = {0.f, 0.f, 0.f, 0.f}, dd[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
+    for (int i = 0; i < 8; i += 4) {
         mma_step(w[i], __byte_perm(xw[i >> 1], 0u, bs.s0e), __byte_perm(xw[i >> 1], 0u, bs.s1e), da);
         mma_step(w[i + 1], __byte_perm(xw[i >> 1], 0u, bs.s0o), __byte_perm(xw[i >> 1], 0u, bs.s1o), db);
+        mma_step(w[i + 2], __byte_perm(xw[(i >> 1) + 1], 0u, bs.s0e), __byte_perm(xw[(i >> 1) + 1], 0u, bs.s1e), dc);
+        mma_step(w[i + 3], __byte_perm(xw[(i >> 1) + 1], 0u, bs.s0o), __byte_perm(xw[(i >> 1) + 1], 0u, bs.s1o), dd);
     }
-    const float t0 = (da[0] + da[1]) + (db[0] + db[1]);
-    const float t1 = (da[2] + da[3]) + (db[2] + db[3]);
+    const float t0 = ((da[0] + da[1]) + (db[0] + db[1])) + ((dc[0] + dc[1]) + (dd[0] + dd[1]));
+    const float t1 = ((da[2] + da[3]) + (db[2] + db[3])) + ((dc[2] + dc[3]) + (dd[2] + dd[3]));
     acc0 = fmaf(jinf_h2f((uint16_t)(sc & 0xffffu)), t0, acc0);
     acc1 = fmaf(jinf_h2f((uint16_t)(sc >> 16)), t1, acc1);
 }

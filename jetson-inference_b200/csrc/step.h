@@ -14,12 +14,8 @@ namespace jinf {
 #ifndef JINF_STEP_NBUF
 #define JINF_STEP_NBUF 6
 #endif
-#ifndef JINF_STEP_PF_DIST
-#define JINF_STEP_PF_DIST 24
-#endif
 constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
 constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 chunks in flight)
-constexpr int STEP_PF_DIST = JINF_STEP_PF_DIST;  // L2 prefetch distance per warp, in chunks
 constexpr int ATTN_POS_PER_CTA = 512;  // attention positions per CTA: 16 warps x 32
 constexpr int ATTN_MAX_SPLIT = 64;     // CTAs per kv head (contexts up to 32768 positions)
 constexpr int ATTN_MAX_GROUP = 8;      // query heads per kv head
@@ -63,7 +59,8 @@ struct StepParams {
 };
 
 // CTA c of C owns tiles [step_cta_tile(c), step_cta_tile(c + 1)) of every GEMV phase.
-__host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)((long long)c * T / C); }
+// (c * T stays far below 2^31: at most a few hundred CTAs times tens of thousands of tiles.)
+__host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)((unsigned)(c * T) / (unsigned)C); }
 
 // Shared bytes of the staged input for the widest GEMV phase, or of the attention scratch
 // (q of one kv head's query heads + per-warp partials), whichever is larger.

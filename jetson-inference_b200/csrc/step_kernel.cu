@@ -68,38 +68,44 @@ struct PhaseInfo {
     int tiles, groups;
 };
 
-// Chunk range of warp `warp` of CTA `cta` (of C) in a tiles x groups matrix.
-__device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int G, long long& c0, long long& c1) {
-    const long long t0 = step_cta_tile(cta, C, T), t1 = step_cta_tile(cta + 1, C, T);
-    const long long n = (t1 - t0) * G;
-    c0 = t0 * G + warp * n / NW;
-    c1 = t0 * G + (warp + 1) * n / NW;
+// Chunk range [c0, c1) of warp `warp` of CTA `cta` (of C) in a tiles x groups matrix
+// (32-bit: a matrix has far fewer than 2^31 chunks).
+__device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int G, int& c0, int& c1) {
+    const int t0 = step_cta_tile(cta, C, T), t1 = step_cta_tile(cta + 1, C, T);
+    const int n = (t1 - t0) * G;
+    c0 = t0 * G + ((warp * n) >> 4);
+    c1 = t0 * G + (((warp + 1) * n) >> 4);
 }
+static_assert(NW == 16, "warp_range divides by the warp count with a shift");
 
-// Walks one warp's chunks over the GEMV phases in the order they are consumed.
-struct Cursor {
-    const PhaseInfo* pi;
-    int n, i, cta, C, warp;
-    long long c, c1;
+// Where a warp's weight stream continues: the first GEMV phase at or after `from` in which
+// it has chunks, and that range. Out of line: it runs once per phase, and keeping it out of
+// the copy loop keeps the loop's live state small.
+struct StreamPos {
     const uint8_t* w;
-    __device__ void seek(int from) {
-        for (i = from; i < n; ++i) {
-            const int G = pi[i].groups;
-            if (!G) continue;
-            warp_range(cta, C, warp, pi[i].tiles, G, c, c1);
-            if (c < c1) {
-                w = pi[i].w;
-                return;
-            }
+    int ph, c, c1;
+};
+__device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int from, int cta, int C, int warp) {
+    StreamPos r;
+    for (int i = from; i < n; ++i) {
+        const int G = pinfo[i].groups;
+        if (!G) continue;
+        int c0, c1;
+        warp_range(cta, C, warp, pinfo[i].tiles, G, c0, c1);
+        if (c0 < c1) {
+            r.w = pinfo[i].w;
+            r.ph = i;
+            r.c = c0;
+            r.c1 = c1;
+            return r;
         }
     }
-    __device__ const uint8_t* next() {
-        if (i >= n) return nullptr;
-        const uint8_t* a = w + c * Q4M_CHUNK;
-        if (++c == c1) seek(i + 1);
-        return a;
-    }
-};
+    r.w = nullptr;
+    r.ph = n;
+    r.c = 0;
+    r.c1 = 0;
+    return r;
+}
 
 __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&v);
@@ -284,26 +290,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     }
     __syncthreads();
 
-    // ---------------- weight stream: copy cursor (ring) and L2 prefetch cursor (further ahead)
-    Cursor cc;
-    cc.pi = pinfo;
-    cc.n = P.n_phases;
-    cc.cta = blockIdx.x;
-    cc.C = C;
-    cc.warp = warp;
-    cc.seek(0);
-    Cursor pc = cc;
-    for (int i = 0; i < STEP_NBUF - 1; ++i) pc.next();
-    for (int i = 0; i < STEP_PF_DIST; ++i) {
-        const uint8_t* b = pc.next();
-        if (b && lane == 0) prefetch_l2(b, Q4M_CHUNK);
-    }
+    // ---------------- weight stream: this warp's chunk ranges of all GEMV phases, copied in
+    // consumption order into the ring (STEP_NBUF - 1 chunks ahead of the arithmetic)
+    StreamPos sp = stream_seek(pinfo, P.n_phases, 0, blockIdx.x, C, warp);
     auto issue = [&](int slot) {
-        const uint8_t* a = cc.next();
-        if (a) copy_chunk_async(ring + slot * Q4M_CHUNK, a, lane);
+        if (sp.c < sp.c1) {
+            copy_chunk_async(ring + slot * Q4M_CHUNK, sp.w + (size_t)sp.c * Q4M_CHUNK, lane);
+            if (++sp.c == sp.c1) sp = stream_seek(pinfo, P.n_phases, sp.ph + 1, blockIdx.x, C, warp);
+        }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
-        const uint8_t* b = pc.next();
-        if (b && lane == 0) prefetch_l2(b, Q4M_CHUNK);
     };
 #pragma unroll
     for (int i = 0; i < STEP_NBUF - 1; ++i) issue(i);
@@ -422,20 +417,24 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         // the CTA that owns tile 0 stores the embedding row as the residual stream
         const float inv_alpha = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps,
                                                       d.cols, xbase, xk, misc, true);
-        EpiArgs ea;
-        ea.epi = d.epi;
-        ea.rows = d.rows;
-        ea.y = d.y;
-        ea.kcache = d.kcache;
-        ea.vcache = d.vcache;
-        ea.nq = P.nq;
-        ea.nk = P.nk;
-        ea.head_dim = P.head_dim;
-        ea.max_ctx = P.max_ctx;
-        ea.pos = pos;
-        ea.rope_base = P.rope_base;
-        ea.coherent = true;
-        long long c, c1;
+        // epilogue arguments are read from the shared descriptor when a tile finishes
+        auto epilogue = [&](int row, float v0, float v1) {
+            EpiArgs ea;
+            ea.epi = d.epi;
+            ea.rows = d.rows;
+            ea.y = d.y;
+            ea.kcache = d.kcache;
+            ea.vcache = d.vcache;
+            ea.nq = P.nq;
+            ea.nk = P.nk;
+            ea.head_dim = P.head_dim;
+            ea.max_ctx = P.max_ctx;
+            ea.pos = pos;
+            ea.rope_base = P.rope_base;
+            ea.coherent = true;
+            epilogue_pair(ea, row, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
+        };
+        int c, c1;
         warp_range(blockIdx.x, C, warp, d.tiles, G, c, c1);
         if (lane == 0) {
             ftile[warp] = -1;
@@ -443,10 +442,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         }
         bool first_piece = true;
         int own_tile = -1, own_slot = 0;  // the split tile this warp finishes (its piece starts the tile)
-        while (c < c1) {
-            const int tile = (int)(c / G);
-            const int gb = (int)(c - (long long)tile * G);
-            const int ge = (int)(c1 - c < (long long)(G - gb) ? gb + (c1 - c) : G);
+        int tile = c / G, gb = c - tile * G;  // walked incrementally: no division per piece
+        for (; c < c1; ++tile, gb = 0) {
+            const int ge = c1 - c < G - gb ? gb + (c1 - c) : G;
             float acc0 = 0.f, acc1 = 0.f;
             for (int g = gb; g < ge; ++g) {
                 issue(slot == 0 ? STEP_NBUF - 1 : slot - 1);
@@ -462,8 +460,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             if (gb == 0 && ge == G) {
                 float v0, v1;
                 tile_rows(acc0, acc1, lane, v0, v1);
-                if (lane < 8)
-                    epilogue_pair(ea, tile * Q4M_ROWS + 2 * lane, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
+                if (lane < 8) epilogue(tile * Q4M_ROWS + 2 * lane, v0, v1);
             } else {
                 // a piece of a tile shared with the neighbouring warps: partial rows to shared memory
                 acc0 += __shfl_xor_sync(JINF_FULL_MASK, acc0, 1);
@@ -494,7 +491,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                 v0 += part_s[(w2 * 2) * 16 + 2 * lane];
                 v1 += part_s[(w2 * 2) * 16 + 2 * lane + 1];
             }
-            epilogue_pair(ea, own_tile * Q4M_ROWS + 2 * lane, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
+            epilogue(own_tile * Q4M_ROWS + 2 * lane, v0, v1);
         }
         __syncthreads();  // every epilogue store of the CTA precedes the report
         if (tid == 0) {
