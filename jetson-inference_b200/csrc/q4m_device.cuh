@@ -200,34 +200,27 @@ __device__ __forceinline__ float stage_x(int xm, const void* x, const float* hsr
     const float alpha = pow2_prescale(amax * rnorm * 1.0001f);
     const int G = cols / Q4M_KG;
     for (int g = warp; g < G; g += NW) {
-        float v[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = xf[g * 128 + j * 32 + lane];
+        // lane l converts elements 4(l%8) .. 4(l%8)+3 of block j = l/8 of the group
+        const float4 v = reinterpret_cast<const float4*>(xf + g * 128)[lane];
         __syncwarp();  // the whole group is in registers before it is overwritten
-        float s[4];
+        const int j = lane >> 3, q = lane & 7;
+        const float scale = (norm ? rnorm : 1.0f) * alpha * (j < 2 ? 1.0f : 0.0625f);
+        const float vv[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
+        float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float xv = norm ? v[j] * rnorm : v[j];
-            const float sv = xv * alpha * (j < 2 ? 1.0f : 0.0625f);
-            const __half hi = __float2half_rn(sv);
-            const __half lo = __float2half_rn(sv - __half2float(hi));
-            // element e = lane of block j: lane record 4*(2j + h) + (e & 3), half e >> 2
-            uint16_t* rec = xb + (size_t)g * 256 + (8 * j + (lane & 3)) * 8 + (lane >> 2);
+        for (int t = 0; t < 4; ++t) {
+            const __half hi = __float2half_rn(vv[t]);
+            const __half lo = __float2half_rn(vv[t] - __half2float(hi));
+            // element e = 4q + t of block j: lane record 4*(2j + h) + t, half q
+            uint16_t* rec = xb + (size_t)g * 256 + (8 * j + t) * 8 + q;
             rec[0] = __half_as_ushort(hi);
             rec[32] = __half_as_ushort(lo);  // h = 1: four lane records further
-            s[j] = __half2float(hi) + __half2float(lo);
+            s += __half2float(hi) + __half2float(lo);
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) s[j] += __shfl_xor_sync(JINF_FULL_MASK, s[j], o);
-        if (lane < 4) {
-            float sj = s[0];
-#pragma unroll
-            for (int j = 1; j < 4; ++j)
-                if (lane == j) sj = s[j];
-            xk[g * 4 + lane] = -(lane < 2 ? 1032.0f : 1152.0f) * sj;
-        }
+        s += __shfl_xor_sync(JINF_FULL_MASK, s, 1);
+        s += __shfl_xor_sync(JINF_FULL_MASK, s, 2);
+        s += __shfl_xor_sync(JINF_FULL_MASK, s, 4);
+        if (q == 0) xk[g * 4 + j] = -(j < 2 ? 1032.0f : 1152.0f) * s;
     }
     __syncthreads();
     return 1.0f / alpha;  // exact: alpha is a power of two

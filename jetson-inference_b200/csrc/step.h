@@ -16,7 +16,9 @@ namespace jinf {
 #endif
 constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
 constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 chunks in flight)
+constexpr int ATTN_POS_PER_WARP = 32;  // attention positions per warp (one lane each)
 constexpr int ATTN_POS_PER_CTA = 512;  // attention positions per CTA: 16 warps x 32
+
 constexpr int ATTN_MAX_SPLIT = 64;     // CTAs per kv head (contexts up to 32768 positions)
 constexpr int ATTN_MAX_GROUP = 8;      // query heads per kv head
 

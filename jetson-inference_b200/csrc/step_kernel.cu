@@ -107,6 +107,43 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
     return r;
 }
 
+// The weight stream of one warp between calls: ring slot of the next chunk to consume and
+// the copy position.
+struct WarpStream {
+    StreamPos sp;
+    int slot;
+};
+
+struct PieceSum {
+    float acc0, acc1;
+};
+
+// Consume groups [gb, ge) of one tile from the ring (tensor-core decode, q4m_device.cuh),
+// refilling it as it goes. Out of line so that the hot loop gets a register allocation of
+// its own, independent of the rest of the step kernel.
+__device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, const PhaseInfo* pinfo, int n_phases,
+                                              int C, const uint16_t* xb, const float* xk, int gb, int ge) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const BSel bs(lane);
+    StreamPos sp = ws.sp;
+    int slot = ws.slot;
+    float acc0 = 0.f, acc1 = 0.f;
+    for (int g = gb; g < ge; ++g) {
+        const int is = slot == 0 ? STEP_NBUF - 1 : slot - 1;
+        if (sp.c < sp.c1) {
+            copy_chunk_async(ring + is * Q4M_CHUNK, sp.w + (size_t)sp.c * Q4M_CHUNK, lane);
+            if (++sp.c == sp.c1) sp = stream_seek(pinfo, n_phases, sp.ph + 1, blockIdx.x, C, warp);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
+        asm volatile("cp.async.wait_group %0;" ::"n"(STEP_NBUF - 1) : "memory");
+        chunk_mma(ring + slot * Q4M_CHUNK, xb, xk, g, lane, bs, acc0, acc1);
+        slot = slot + 1 == STEP_NBUF ? 0 : slot + 1;
+    }
+    ws.sp = sp;
+    ws.slot = slot;
+    return PieceSum{acc0, acc1};
+}
+
 __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&v);
 #pragma unroll
@@ -137,83 +174,96 @@ __device__ __forceinline__ void load_vrow(const __half* vrow, int lane, bool ok,
 
 // One warp's share of the decode attention (math of reference cuda/attention_kernel.cu:
 // 45-98: scores q.k / sqrt(hd), GQA head map h -> h / (H/Hkv), max-subtracted softmax,
-// P.V): positions [p0, p1), at most 32, for all GQ query heads of one kv head. Lanes own
-// positions for q.k and head dims for p.v; the (m, l, acc[hd]) of each query head goes to
-// `part` ([GQ][HD + 2]). qs holds the pre-scaled q of the GQ heads.
+// P.V): positions [p0, p1) in blocks of 32, for all GQ query heads of one kv head, with an
+// online softmax across the blocks. Lanes own positions for q.k and head dims for p.v; the
+// (m, l, acc[hd]) of each query head goes to `part` ([GQ][HD + 2]). qs holds the
+// pre-scaled q of the GQ heads.
 template <int HD, int GQ>
 __device__ __noinline__ void attn_warp(const float* qs, const __half* kb, const __half* vb, int p0, int p1, int lane,
                                        float* part) {
     constexpr int DPL = HD / 32;  // head dims per lane
-    const int pp = p0 + lane;
-    const bool valid = pp < p1;
-    const int nj = p1 - p0;
-    float sc[GQ];
-#pragma unroll
-    for (int g = 0; g < GQ; ++g) sc[g] = 0.f;
-    if (valid) {
-        // this lane's K row, eight 16-byte loads in flight at a time
-        const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)pp * HD);
-#pragma unroll
-        for (int hb = 0; hb < HD / 64; ++hb) {
-            uint4 kv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) kv[u] = __ldcg(kr + hb * 8 + u);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int c8 = hb * 8 + u;
-                float kf[8];
-                unpack8(kv[u], kf);
-#pragma unroll
-                for (int g = 0; g < GQ; ++g) {
-                    const float4 qa = reinterpret_cast<const float4*>(qs)[(g * HD) / 4 + 2 * c8];
-                    const float4 qb = reinterpret_cast<const float4*>(qs)[(g * HD) / 4 + 2 * c8 + 1];
-                    float a = sc[g];
-                    a = fmaf(qa.x, kf[0], a);
-                    a = fmaf(qa.y, kf[1], a);
-                    a = fmaf(qa.z, kf[2], a);
-                    a = fmaf(qa.w, kf[3], a);
-                    a = fmaf(qb.x, kf[4], a);
-                    a = fmaf(qb.y, kf[5], a);
-                    a = fmaf(qb.z, kf[6], a);
-                    a = fmaf(qb.w, kf[7], a);
-                    sc[g] = a;
-                }
-            }
-        }
-    }
-    // the first 16 V rows are requested before the softmax (they do not depend on it)
-    float v0[16][DPL];
-#pragma unroll
-    for (int u = 0; u < 16; ++u) load_vrow<DPL>(vb + (size_t)(p0 + u) * HD, lane, u < nj, v0[u]);
-    float m[GQ], l[GQ], pr[GQ], acc[GQ][DPL];
+    float m[GQ], l[GQ], acc[GQ][DPL];
 #pragma unroll
     for (int g = 0; g < GQ; ++g) {
-        const float sv = valid ? sc[g] : -INFINITY;
-        m[g] = warp_max(sv);
-        pr[g] = valid ? expf(sv - m[g]) : 0.f;
-        l[g] = warp_sum(pr[g]);
+        m[g] = -INFINITY;
+        l[g] = 0.f;
 #pragma unroll
         for (int k = 0; k < DPL; ++k) acc[g][k] = 0.f;
     }
+    for (int b0 = p0; b0 < p1; b0 += 32) {
+        const int pp = b0 + lane;
+        const bool valid = pp < p1;
+        const int nj = p1 - b0 < 32 ? p1 - b0 : 32;
+        float sc[GQ];
 #pragma unroll
-    for (int u = 0; u < 16; ++u)
+        for (int g = 0; g < GQ; ++g) sc[g] = 0.f;
+        if (valid) {
+            // this lane's K row, eight 16-byte loads in flight at a time
+            const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)pp * HD);
+#pragma unroll
+            for (int hb = 0; hb < HD / 64; ++hb) {
+                uint4 kv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) kv[u] = __ldcg(kr + hb * 8 + u);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int c8 = hb * 8 + u;
+                    float kf[8];
+                    unpack8(kv[u], kf);
+#pragma unroll
+                    for (int g = 0; g < GQ; ++g) {
+                        const float4 qa = reinterpret_cast<const float4*>(qs)[(g * HD) / 4 + 2 * c8];
+                        const float4 qb = reinterpret_cast<const float4*>(qs)[(g * HD) / 4 + 2 * c8 + 1];
+                        float a = sc[g];
+                        a = fmaf(qa.x, kf[0], a);
+                        a = fmaf(qa.y, kf[1], a);
+                        a = fmaf(qa.z, kf[2], a);
+                        a = fmaf(qa.w, kf[3], a);
+                        a = fmaf(qb.x, kf[4], a);
+                        a = fmaf(qb.y, kf[5], a);
+                        a = fmaf(qb.z, kf[6], a);
+                        a = fmaf(qb.w, kf[7], a);
+                        sc[g] = a;
+                    }
+                }
+            }
+        }
+        // the first 16 V rows are requested before the softmax (they do not depend on it)
+        float v0[16][DPL];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) load_vrow<DPL>(vb + (size_t)(b0 + u) * HD, lane, u < nj, v0[u]);
+        float pr[GQ];
 #pragma unroll
         for (int g = 0; g < GQ; ++g) {
-            const float pj = __shfl_sync(JINF_FULL_MASK, pr[g], u);
+            const float sv = valid ? sc[g] : -INFINITY;
+            const float mn = fmaxf(m[g], warp_max(sv));
+            const float corr = m[g] == -INFINITY ? 0.f : expf(m[g] - mn);
+            pr[g] = valid ? expf(sv - mn) : 0.f;
+            l[g] = l[g] * corr + warp_sum(pr[g]);
 #pragma unroll
-            for (int k = 0; k < DPL; ++k) acc[g][k] = fmaf(pj, v0[u][k], acc[g][k]);
+            for (int k = 0; k < DPL; ++k) acc[g][k] *= corr;
+            m[g] = mn;
         }
-    if (nj > 16) {
-#pragma unroll
-        for (int u = 0; u < 16; ++u) load_vrow<DPL>(vb + (size_t)(p0 + 16 + u) * HD, lane, 16 + u < nj, v0[u]);
 #pragma unroll
         for (int u = 0; u < 16; ++u)
 #pragma unroll
             for (int g = 0; g < GQ; ++g) {
-                const float pj = __shfl_sync(JINF_FULL_MASK, pr[g], 16 + u);
+                const float pj = __shfl_sync(JINF_FULL_MASK, pr[g], u);
 #pragma unroll
                 for (int k = 0; k < DPL; ++k) acc[g][k] = fmaf(pj, v0[u][k], acc[g][k]);
             }
+        if (nj > 16) {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) load_vrow<DPL>(vb + (size_t)(b0 + 16 + u) * HD, lane, 16 + u < nj, v0[u]);
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+#pragma unroll
+                for (int g = 0; g < GQ; ++g) {
+                    const float pj = __shfl_sync(JINF_FULL_MASK, pr[g], 16 + u);
+#pragma unroll
+                    for (int k = 0; k < DPL; ++k) acc[g][k] = fmaf(pj, v0[u][k], acc[g][k]);
+                }
+        }
     }
 #pragma unroll
     for (int g = 0; g < GQ; ++g) {
@@ -292,21 +342,19 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 
     // ---------------- weight stream: this warp's chunk ranges of all GEMV phases, copied in
     // consumption order into the ring (STEP_NBUF - 1 chunks ahead of the arithmetic)
-    StreamPos sp = stream_seek(pinfo, P.n_phases, 0, blockIdx.x, C, warp);
-    auto issue = [&](int slot) {
-        if (sp.c < sp.c1) {
-            copy_chunk_async(ring + slot * Q4M_CHUNK, sp.w + (size_t)sp.c * Q4M_CHUNK, lane);
-            if (++sp.c == sp.c1) sp = stream_seek(pinfo, P.n_phases, sp.ph + 1, blockIdx.x, C, warp);
+    WarpStream ws;
+    ws.sp = stream_seek(pinfo, P.n_phases, 0, blockIdx.x, C, warp);
+    ws.slot = 0;
+    for (int i = 0; i < STEP_NBUF - 1; ++i) {
+        if (ws.sp.c < ws.sp.c1) {
+            copy_chunk_async(ring + i * Q4M_CHUNK, ws.sp.w + (size_t)ws.sp.c * Q4M_CHUNK, lane);
+            if (++ws.sp.c == ws.sp.c1) ws.sp = stream_seek(pinfo, P.n_phases, ws.sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
-    };
-#pragma unroll
-    for (int i = 0; i < STEP_NBUF - 1; ++i) issue(i);
+    }
 
-    const BSel bs(lane);
     const int gr = lane >> 2, c4 = lane & 3;
     const uint16_t* xb = reinterpret_cast<const uint16_t*>(xbase);
-    int slot = 0;
     float lmax = -INFINITY;
     int lidx = 0;
     constexpr int DWORDS = (int)(sizeof(StepPhase) / 4);
@@ -346,7 +394,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             }
             __syncthreads();
             float* mypart = wp + (size_t)warp * gq * (hd + 2);
-            const int wp0 = p0 + warp * 32, wp1 = min(p1, wp0 + 32);
+            const int wp0 = p0 + warp * ATTN_POS_PER_WARP, wp1 = min(p1, wp0 + ATTN_POS_PER_WARP);
             const __half* kb = d.kcache + (size_t)kvh * P.max_ctx * hd;
             const __half* vb = d.vcache + (size_t)kvh * P.max_ctx * hd;
             if (wp0 < wp1) {
@@ -409,6 +457,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         }
 
         // ---------------- GEMV phase: this CTA's tiles [t0, t1)
+        if (d.epi == EPI_QKV && tid == 0 && pos > 0 && (int)blockIdx.x < 2 * P.n_kv_heads) {
+            // the attention after this phase reads this layer's K and V rows 0..pos-1 (one
+            // region per CTA): bring them into L2 now, while the QKV weights stream
+            const int kvh = blockIdx.x >> 1;
+            const __half* base = ((blockIdx.x & 1) ? d.vcache : d.kcache) + (size_t)kvh * P.max_ctx * P.head_dim;
+            const uint32_t bytes = (uint32_t)pos * (uint32_t)P.head_dim * 2u;
+            for (uint32_t off = 0; off < bytes; off += (1u << 20))
+                prefetch_l2(reinterpret_cast<const uint8_t*>(base) + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
+        }
         const int G = d.groups;
         const int t0 = step_cta_tile(blockIdx.x, C, d.tiles), t1 = step_cta_tile(blockIdx.x + 1, C, d.tiles);
         if (t0 >= t1) continue;
@@ -445,13 +502,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         int tile = c / G, gb = c - tile * G;  // walked incrementally: no division per piece
         for (; c < c1; ++tile, gb = 0) {
             const int ge = c1 - c < G - gb ? gb + (c1 - c) : G;
-            float acc0 = 0.f, acc1 = 0.f;
-            for (int g = gb; g < ge; ++g) {
-                issue(slot == 0 ? STEP_NBUF - 1 : slot - 1);
-                asm volatile("cp.async.wait_group %0;" ::"n"(STEP_NBUF - 1) : "memory");
-                chunk_mma(ring + slot * Q4M_CHUNK, xb, xk, g, lane, bs, acc0, acc1);
-                slot = slot + 1 == STEP_NBUF ? 0 : slot + 1;
-            }
+            const PieceSum ps = stream_piece(ws, ring, pinfo, P.n_phases, C, xb, xk, gb, ge);
+            float acc0 = ps.acc0, acc1 = ps.acc1;
             c += ge - gb;
             if (first_piece && lane == 0) {
                 ftile[warp] = tile;
