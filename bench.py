@@ -38,6 +38,20 @@ METRIC = "decode tok/s Llama-3-8B-shape Q4_0 @1/2/4/8 B200; GEMV HBM GB/s vs pea
 PROMPT = 512
 
 
+def traffic_ratio():
+    """DRAM bytes / algorithmic bytes of the step kernel from the committed ncu summary
+    (profiles/k_step_4layer_8bshape_full.md, captured on a 4-layer case of the same kernel
+    and scaled per launch by the bytes processed), or None."""
+    p = os.path.join(ROOT, "profiles", "k_step_4layer_8bshape_full.md")
+    try:
+        for ln in open(p):
+            if ln.startswith("traffic_ratio:"):
+                return float(ln.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -147,13 +161,13 @@ def cpu_decode_sample(shape, layers: int, target_s: float, min_reps: int = 2):
     from oracle import oracle
     import jinf
     syn = jinf.SynthModel(shape, seed=0)
-    om = oracle.OracleModel(syn, max_ctx=PROMPT + 64, kv_f16=True, layers=layers)
+    om = oracle.OracleModel(syn, max_ctx=PROMPT + 512, kv_f16=True, layers=layers)
     om.fill_kv_random(PROMPT, seed=1)
     tok = 1
     om.forward(tok, want_logits=False)  # warm caches / threads
     t_layers, t_full = [], []
     t0 = time.perf_counter()
-    while (len(t_layers) < min_reps or time.perf_counter() - t0 < target_s) and om.pos < PROMPT + 60:
+    while (len(t_layers) < min_reps or time.perf_counter() - t0 < target_s) and om.pos < PROMPT + 500:
         a = time.perf_counter()
         om.forward(tok, want_logits=False)
         b = time.perf_counter()
@@ -330,10 +344,14 @@ def run_ours(args, rank, world, local):
     kv_bytes = 2 * 2 * shape.n_layers * (shape.n_heads_kv // world) * shape.head_dim * (PROMPT + args.warmup + args.steps / 2)
     step_gbs = (wbytes + kv_bytes) / (dev_s / args.steps) / 1e9
     if persistent:
+        ratio = traffic_ratio()
         roof = {"bound": "hbm", "kernel": "k_step (persistent decode step, one launch per token)",
                 "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(step_gbs / peak, 4),
-                "peak_kind": peak_kind, "traffic": None, "bytes_per_launch": int(wbytes + kv_bytes),
-                "us_per_launch": round(1e6 * dev_s / args.steps, 2)}
+                "peak_kind": peak_kind,
+                "traffic": int((wbytes + kv_bytes) * ratio) if ratio else None,
+                "traffic_note": "ncu dram read+write bytes per launch, measured on a 4-layer case of the same "
+                                "kernel and scaled by bytes processed (profiles/k_step_4layer_8bshape_full.md)",
+                "bytes_per_launch": int(wbytes + kv_bytes), "us_per_launch": round(1e6 * dev_s / args.steps, 2)}
     else:
         top = max(("qkv", "o_proj", "gate_up", "down", "lm_head"),
                   key=lambda k: prof[k]["us"] * (shape.n_layers if k != "lm_head" else 1))
