@@ -40,6 +40,15 @@ jinf_status jinf_b200_gemv_q4m(const void* q4m, const void* x, int x_type, float
 jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* h, const float* gain, float eps, float* y,
                                        int rows, int cols, void* workspace, int kw, cudaStream_t stream);
 
+// Same as jinf_b200_gemv_q4m with kw = 0, but allocation-free: no counterpart in the
+// reference. The split-K workspace is a 4 MB static device array inside the library
+// (counters zero at load and left zero by every call), so the caller neither allocates nor
+// passes one; the first call on each device looks the array up and must not be inside a
+// stream capture. rows <= 262144; a shape whose partial sums exceed the array is rejected
+// with JINF_ERR_INVALID. Calls that overlap in time share the array and race: serialise them.
+jinf_status jinf_b200_gemv_q4m_noalloc(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
+                                       cudaStream_t stream);
+
 // Workspace bytes needed by jinf_b200_attention_f16 for this shape.
 size_t jinf_b200_attention_workspace_bytes(int n_kv_heads, int head_dim, int max_ctx);
 

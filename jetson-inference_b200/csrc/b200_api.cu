@@ -83,6 +83,72 @@ extern "C" jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* 
     return gemv_q4m_common(p, sh, X_RMSNORM, workspace, kw, stream);
 }
 
+// ---------------------------------------------------------------- allocation-free GEMV
+//
+// jinf_b200_gemv_q4m_noalloc: the same split-K tensor-core GEMV as jinf_b200_gemv_q4m, with
+// its workspace in this file-scope device array instead of caller memory, for callers that
+// cannot allocate device memory (or hand out a workspace) at call time. Layout: arrival
+// counters of up to kNoAllocMaxTiles tiles at a fixed offset (zero at module load; every
+// call leaves them zero again, so they are zero between calls), then the partial rows.
+// Calls that overlap in time (other streams, other host threads) share it and race.
+static constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;  // 4 MB
+static constexpr int kNoAllocMaxTiles = 16384;                   // rows <= 262144
+static constexpr size_t kNoAllocCntBytes = (size_t)kNoAllocMaxTiles * sizeof(unsigned int);
+static __device__ __align__(256) unsigned char g_gemv_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch on the current device, looked up once per device (the
+// first call on a device must not be inside a stream capture).
+static jinf_status noalloc_scratch(uint8_t** out) {
+    static uint8_t* addr[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return JINF_ERR_CUDA;
+    if (!addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            JINF_LOG("jinf_b200_gemv_q4m_noalloc: scratch address lookup failed: %s", cudaGetErrorString(e));
+            return JINF_ERR_CUDA;
+        }
+        addr[dev] = (uint8_t*)p;
+    }
+    *out = addr[dev];
+    return JINF_OK;
+}
+
+extern "C" jinf_status jinf_b200_gemv_q4m_noalloc(const void* q4m, const void* x, int x_type, float* y, int rows,
+                                                  int cols, cudaStream_t stream) {
+    Q4MShape sh;
+    if (!q4m || !x || !y || !q4m_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
+    if (sh.cols > gemvm_max_cols()) return JINF_ERR_INVALID;
+    if (sh.tiles > kNoAllocMaxTiles) {
+        JINF_LOG("jinf_b200_gemv_q4m_noalloc: %d rows exceed the static scratch limit of %d rows", rows,
+                 kNoAllocMaxTiles * Q4M_ROWS);
+        return JINF_ERR_INVALID;
+    }
+    const int xm = x_type == JINF_TYPE_F32 ? X_PLAIN_F32 : X_PLAIN_F16;
+    const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms());
+    const int kw = gemvm_pick_kw(sh.tiles, sh.groups, grid, kQ4mMaxKw);
+    const size_t part_bytes = (size_t)sh.tiles * kw * 16 * sizeof(float);
+    if (kw > 1 && part_bytes > kNoAllocScratchBytes - kNoAllocCntBytes) {
+        JINF_LOG("jinf_b200_gemv_q4m_noalloc: %d x %d needs %zu bytes of partial sums, the static scratch holds %zu",
+                 rows, cols, part_bytes, kNoAllocScratchBytes - kNoAllocCntBytes);
+        return JINF_ERR_INVALID;
+    }
+    uint8_t* scratch = nullptr;
+    JINF_CHECK(noalloc_scratch(&scratch), "noalloc scratch");
+    GemvParams p{};
+    gemvm_params_for(p, q4m, sh);
+    p.x = x;
+    p.y = y;
+    p.kw = kw;
+    if (kw > 1) {
+        p.cnt = (unsigned int*)scratch;
+        p.part = (float*)(scratch + kNoAllocCntBytes);
+    }
+    return gemvm_launch(p, xm, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
 extern "C" size_t jinf_b200_attention_workspace_bytes(int n_kv_heads, int head_dim, int max_ctx) {
     int n_split = (max_ctx + 63) / 64;
     if (n_split < 1) n_split = 1;
