@@ -18,7 +18,8 @@ typedef struct CUstream_st* cudaStream_t;
 extern "C" {
 #endif
 
-// Bytes of the Q4M image of a rows x cols Q4_0 matrix; 0 if cols is not a multiple of 128.
+// Bytes of the Q4M image of a rows x cols Q4_0 matrix; 0 if cols is not a multiple of 32
+// (whole blocks; the last 128-column group is zero-padded).
 // Q4M is the layout of the tensor-core GEMV: 16-row tiles x 128-column groups, 1152 bytes
 // per (tile, group), every nibble and scale of the AoS blocks moved, none re-quantised.
 uint64_t jinf_b200_q4m_bytes(int rows, int cols);

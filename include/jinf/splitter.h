@@ -67,6 +67,12 @@ void        jinf_split_plan_print(const jinf_split_plan* plan);
 
 // New: split role of a tensor by name.
 jinf_tp_role jinf_split_tp_role(const char* tensor_name);
+// New: the slice of a rows x cols tensor that tensor-parallel rank `rank` of `size` holds,
+// from its role: JINF_TP_COLUMN tensors are split by rows, JINF_TP_ROW tensors by columns
+// (whole 32-element blocks), others are whole. JINF_ERR_INVALID when the split dimension
+// does not divide evenly. The engine loads each rank's weights with it.
+jinf_status jinf_tp_shard(const char* name, int64_t rows, int64_t cols, int rank, int size, int64_t* row0,
+                          int64_t* n_rows, int64_t* col0, int64_t* n_cols);
 
 #ifdef __cplusplus
 }

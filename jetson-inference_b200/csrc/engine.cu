@@ -681,6 +681,24 @@ struct Loader {
         return JINF_OK;
     }
 
+    // Stage this rank's tensor-parallel slice of `name` (jinf_tp_shard), which must be
+    // want_rows x want_cols.
+    jinf_status stage_shard(const char* name, int64_t want_rows, int64_t want_cols, int64_t dst_row_bytes,
+                            int64_t dst_row0, int64_t dst_step) {
+        TensorMeta m;
+        if (!src->meta(name, &m)) {
+            JINF_LOG("tensor %s missing", name);
+            return JINF_ERR_PARSE;
+        }
+        int64_t r0, nr, c0, nc;
+        if (jinf_tp_shard(name, m.rows(), m.cols(), I->tp_rank, I->tp_size, &r0, &nr, &c0, &nc) != JINF_OK ||
+            nr != want_rows || nc != want_cols) {
+            JINF_LOG("tensor %s: shard of rank %d/%d does not match the model shape", name, I->tp_rank, I->tp_size);
+            return JINF_ERR_INVALID;
+        }
+        return stage(name, r0, nr, c0, nc, dst_row_bytes, dst_row0, dst_step);
+    }
+
     // Repack the staged AoS matrix into the arena.
     jinf_status pack(uint8_t* dst, const Q4MShape& sh) {
         JINF_CUDA_CHECK(q4m_repack(dstage, dst, sh, I->stream));
@@ -835,7 +853,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         auto& ly = I->layers[L];
         if (!place(ly.qkv_sh, qkv_rows, d, ly.qkv) || !place(ly.o_sh, d, I->Hl * hd, ly.o) ||
             !place(ly.gu_sh, 2 * I->ffl, d, ly.gu) || !place(ly.down_sh, d, I->ffl, ly.down)) {
-            JINF_LOG("matrix shapes not supported by the Q4M layout (columns must be multiples of 128)");
+            JINF_LOG("matrix shapes not supported by the Q4M layout (columns must be whole 32-element blocks)");
             return fail(JINF_ERR_INVALID);
         }
     }
@@ -910,42 +928,42 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             // QKV: this rank's q heads, then its k heads, then its v heads
             const int64_t nq = (int64_t)I->Hl * hd, nk = (int64_t)I->Hkvl * hd;
             snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", L);
-            s = ld.stage(nm, I->tp_rank * nq, nq, 0, d, rb_d, 0, 1);
+            s = ld.stage_shard(nm, nq, d, rb_d, 0, 1);
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", L);
-                s = ld.stage(nm, I->tp_rank * nk, nk, 0, d, rb_d, nq, 1);
+                s = ld.stage_shard(nm, nk, d, rb_d, nq, 1);
             }
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", L);
-                s = ld.stage(nm, I->tp_rank * nk, nk, 0, d, rb_d, nq + nk, 1);
+                s = ld.stage_shard(nm, nk, d, rb_d, nq + nk, 1);
             }
             if (s == JINF_OK) s = ld.pack(ly.qkv, ly.qkv_sh);
             // o: every output row, this rank's input columns (row split)
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", L);
-                s = ld.stage(nm, 0, d, I->tp_rank * nq, nq, (nq / 32) * 18, 0, 1);
+                s = ld.stage_shard(nm, d, nq, (nq / 32) * 18, 0, 1);
             }
             if (s == JINF_OK) s = ld.pack(ly.o, ly.o_sh);
             // gate|up interleaved by neuron: gate_n -> row 2n, up_n -> row 2n+1
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", L);
-                s = ld.stage(nm, (int64_t)I->tp_rank * I->ffl, I->ffl, 0, d, rb_d, 0, 2);
+                s = ld.stage_shard(nm, I->ffl, d, rb_d, 0, 2);
             }
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", L);
-                s = ld.stage(nm, (int64_t)I->tp_rank * I->ffl, I->ffl, 0, d, rb_d, 1, 2);
+                s = ld.stage_shard(nm, I->ffl, d, rb_d, 1, 2);
             }
             if (s == JINF_OK) s = ld.pack(ly.gu, ly.gu_sh);
             // down: every output row, this rank's neuron columns (row split)
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", L);
-                s = ld.stage(nm, 0, d, (int64_t)I->tp_rank * I->ffl, I->ffl, (int64_t)(I->ffl / 32) * 18, 0, 1);
+                s = ld.stage_shard(nm, d, I->ffl, (int64_t)(I->ffl / 32) * 18, 0, 1);
             }
             if (s == JINF_OK) s = ld.pack(ly.down, ly.down_sh);
         }
         I->out_norm = I->norms + (size_t)(2 * I->L) * d;
         if (s == JINF_OK) s = ld.read_f32("output_norm.weight", I->out_norm, d);
-        if (s == JINF_OK) s = ld.stage("output.weight", I->vocab_off, I->Vl, 0, d, rb_d, 0, 1);
+        if (s == JINF_OK) s = ld.stage_shard("output.weight", I->Vl, d, rb_d, 0, 1);
         if (s == JINF_OK) s = ld.pack(I->lm, I->lm_sh);
         if (s == JINF_OK) s = ld.read_f32("token_embd.weight", I->embed, (int64_t)I->V * d);
         if (s != JINF_OK) return fail(s);

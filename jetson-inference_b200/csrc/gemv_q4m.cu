@@ -47,10 +47,10 @@ __device__ __forceinline__ void l2_prefetch(const uint8_t* p, uint64_t bytes) {
 template <int XM, int EPI>
 __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
-    const int G = p.groups, nb = p.cols / 32;
+    const int G = p.groups;
     uint16_t* xb = reinterpret_cast<uint16_t*>(smem_raw);                   // [G][32 lanes][8] fp16 B values
-    float* xk = reinterpret_cast<float*>(smem_raw + (size_t)G * 512);      // [nb] accumulator offsets
-    float* misc = xk + nb;                                                  // 64 floats
+    float* xk = reinterpret_cast<float*>(smem_raw + (size_t)G * 512);      // [4G] accumulator offsets
+    float* misc = xk + 4 * G;                                               // 64 floats
     const uint32_t ring0 = smem_u32(misc + 64);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * Q4M_CHUNK);
@@ -182,19 +182,18 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
 // ---------------------------------------------------------------- repack
 
 // One thread per (tile, group, lane): its 8 nibble words and 2 scales, gathered from the
-// AoS blocks. Rows past `rows` read as zero.
+// AoS blocks ([rows][nb] blocks of 18 bytes). Rows past `rows` and blocks past nb read as zero.
 __global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
-                             int tiles) {
+                             int tiles, int nb) {
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)tiles * groups * 32) return;
     const int lane = (int)(gid & 31);
     const int64_t tg = gid >> 5;
     const int t = (int)(tg / groups), G = (int)(tg % groups);
     const int gr = lane >> 2, c = lane & 3;
-    const int nb = groups * 4;
     auto block = [&](int r, int j) -> const uint8_t* {
         const int row = t * Q4M_ROWS + r;
-        return row < rows ? aos + ((size_t)row * nb + (size_t)G * 4 + j) * 18 : nullptr;
+        return row < rows && G * 4 + j < nb ? aos + ((size_t)row * nb + (size_t)G * 4 + j) * 18 : nullptr;
     };
     uint8_t* chunk = dst + (size_t)tg * Q4M_CHUNK;
     for (int i = 0; i < 8; ++i) {
@@ -221,8 +220,8 @@ __global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restric
 // ---------------------------------------------------------------- host side
 
 size_t gemvm_smem_bytes(int cols) {
-    const int G = cols / Q4M_KG;
-    return (size_t)G * 512 + sizeof(float) * ((size_t)(cols / 32) + 64) + (size_t)NW * GEMV_M_NBUF * Q4M_CHUNK;
+    const int G = (cols + Q4M_KG - 1) / Q4M_KG;
+    return (size_t)G * 512 + sizeof(float) * ((size_t)G * 4 + 64) + (size_t)NW * GEMV_M_NBUF * Q4M_CHUNK;
 }
 
 int gemvm_max_cols() {
@@ -333,7 +332,7 @@ cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStr
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s) {
     const int64_t n = (int64_t)sh.tiles * sh.groups * 32;
     k_repack_q4m<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows, sh.groups,
-                                                             sh.tiles);
+                                                             sh.tiles, sh.cols / 32);
     return cudaGetLastError();
 }
 

@@ -10,7 +10,8 @@
 //   bytes  512 .. 1023   piece 1: [32 lanes][4 words]   words 4..7 (MMA steps 4..7)
 //   bytes 1024 .. 1151   [32 lanes][2 x fp16]           d(row gr, block c), d(row gr+8, block c)
 // for lane = 4*gr + c (gr = 0..7, c = 0..3), so every warp access is one contiguous 512-
-// or 128-byte segment and a matrix streams front to back. Rows past `rows` are zero.
+// or 128-byte segment and a matrix streams front to back. Rows past `rows` and blocks past
+// cols/32 are zero.
 //
 // MMA mapping. Step i (0..7) of a group multiplies a 16 x 16 A tile whose k index packs
 // element e = 4i + c' of all four blocks: k = 2c' + (j & 1) + 8*(j >> 1). The A fragment
@@ -39,16 +40,18 @@ constexpr int Q4M_CHUNK = 1152;  // bytes per (tile, group)
 struct Q4MShape {
     int rows, cols;
     int tiles;   // ceil(rows / 16)
-    int groups;  // cols / 128
+    int groups;  // ceil(cols / 128)
     uint64_t bytes;
 };
 
+// cols must be whole Q4_0 blocks (a multiple of 32); the last group is padded with zero
+// blocks (scale 0) when cols is not a multiple of 128, and the GEMV stages zeros for x there.
 inline bool q4m_shape(int rows, int cols, Q4MShape* s) {
-    if (rows <= 0 || cols <= 0 || cols % Q4M_KG) return false;
+    if (rows <= 0 || cols <= 0 || cols % 32) return false;
     s->rows = rows;
     s->cols = cols;
     s->tiles = (rows + Q4M_ROWS - 1) / Q4M_ROWS;
-    s->groups = cols / Q4M_KG;
+    s->groups = (cols + Q4M_KG - 1) / Q4M_KG;
     s->bytes = (uint64_t)s->tiles * s->groups * Q4M_CHUNK;
     return true;
 }

@@ -179,6 +179,9 @@ __device__ __forceinline__ float stage_x(int xm, const void* x, const float* hsr
         amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
         reinterpret_cast<float4*>(xf)[i] = v;
     }
+    // a padded last group (cols not a multiple of 128) stages zeros: its weights have scale 0
+    const int G = (cols + Q4M_KG - 1) / Q4M_KG;
+    for (int i = cols / 4 + tid; i < G * 32; i += NT) reinterpret_cast<float4*>(xf)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         ss += __shfl_xor_sync(JINF_FULL_MASK, ss, o);
@@ -198,7 +201,6 @@ __device__ __forceinline__ float stage_x(int xm, const void* x, const float* hsr
     }
     const float rnorm = norm ? rsqrtf(ss / (float)cols + eps) : 1.0f;
     const float alpha = pow2_prescale(amax * rnorm * 1.0001f);
-    const int G = cols / Q4M_KG;
     for (int g = warp; g < G; g += NW) {
         // lane l converts elements 4(l%8) .. 4(l%8)+3 of block j = l/8 of the group
         const float4 v = reinterpret_cast<const float4*>(xf + g * 128)[lane];

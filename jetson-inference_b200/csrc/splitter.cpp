@@ -45,6 +45,31 @@ extern "C" jinf_tp_role jinf_split_tp_role(const char* name) {
     }
 }
 
+extern "C" jinf_status jinf_tp_shard(const char* name, int64_t rows, int64_t cols, int rank, int size,
+                                     int64_t* row0, int64_t* n_rows, int64_t* col0, int64_t* n_cols) {
+    if (!name || !row0 || !n_rows || !col0 || !n_cols || rows <= 0 || cols <= 0 || size <= 0 || rank < 0 ||
+        rank >= size)
+        return JINF_ERR_INVALID;
+    *row0 = 0;
+    *n_rows = rows;
+    *col0 = 0;
+    *n_cols = cols;
+    switch (jinf_split_tp_role(name)) {
+        case JINF_TP_COLUMN:  // output rows split evenly: every rank a contiguous slice
+            if (rows % size) return JINF_ERR_INVALID;
+            *n_rows = rows / size;
+            *row0 = (int64_t)rank * *n_rows;
+            break;
+        case JINF_TP_ROW:  // input columns split evenly, on whole 32-element blocks
+            if (cols % ((int64_t)size * 32)) return JINF_ERR_INVALID;
+            *n_cols = cols / size;
+            *col0 = (int64_t)rank * *n_cols;
+            break;
+        default: break;
+    }
+    return JINF_OK;
+}
+
 extern "C" jinf_status jinf_split_analyze(const jinf_gguf_file* model, const jinf_split_config* cfg,
                                           jinf_split_plan** out) {
     if (!model || !cfg || !out) return JINF_ERR_INVALID;

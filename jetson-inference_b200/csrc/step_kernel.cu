@@ -589,7 +589,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 // ---------------------------------------------------------------- host side
 
 unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
-    const size_t gemv = (size_t)(max_cols / Q4M_KG) * 512 + (size_t)(max_cols / 32) * sizeof(float);
+    const size_t G = (size_t)(max_cols + Q4M_KG - 1) / Q4M_KG;
+    const size_t gemv = G * 512 + G * 4 * sizeof(float);
     const size_t attn = (size_t)group * head_dim * sizeof(float) + (size_t)NW * group * (head_dim + 2) * sizeof(float);
     const size_t b = gemv > attn ? gemv : attn;
     return (unsigned int)((b + 15) & ~(size_t)15);

@@ -203,6 +203,7 @@ SIGNATURES = {
     "jinf_split_plan_free": (None, [C.POINTER(SplitPlan)]),
     "jinf_split_plan_print": (None, [C.POINTER(SplitPlan)]),
     "jinf_split_tp_role": (i32, [C.c_char_p]),
+    "jinf_tp_shard": (i32, [C.c_char_p, C.c_int64, C.c_int64, i32, i32, vp, vp, vp, vp]),
     # engine.h
     "jinf_engine_create": (i32, [C.POINTER(C.POINTER(Engine)), C.POINTER(EngineConfig)]),
     "jinf_engine_destroy": (None, [C.POINTER(Engine)]),

@@ -18,13 +18,13 @@ def nibble_bit(r, j):
 def pack(aos: np.ndarray, rows: int, cols: int) -> np.ndarray:
     """AoS Q4_0 [rows][cols/32*18] uint8 -> Q4M bytes."""
     nb = cols // 32
-    groups = cols // KG
+    groups = (cols + KG - 1) // KG
     tiles = (rows + ROWS - 1) // ROWS
-    blk = np.zeros((tiles * ROWS, nb, 18), dtype=np.uint8)
-    blk[:rows] = aos.reshape(rows, nb, 18)
+    blk = np.zeros((tiles * ROWS, groups * 4, 18), dtype=np.uint8)   # padded blocks: scale 0, nibbles 0
+    blk[:rows, :nb] = aos.reshape(rows, nb, 18)
     qs = blk[:, :, 2:]
     # q[row, block, e]: element 2i = low nibble of byte i, 2i+1 = high nibble
-    q = np.empty((tiles * ROWS, nb, 32), dtype=np.uint32)
+    q = np.empty((tiles * ROWS, groups * 4, 32), dtype=np.uint32)
     q[:, :, 0::2] = qs & 15
     q[:, :, 1::2] = qs >> 4
     d = blk[:, :, 0].astype(np.uint32) | (blk[:, :, 1].astype(np.uint32) << 8)
@@ -67,7 +67,7 @@ def _f16(bits):
 
 
 def emulate_gemv(img: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
-    groups = cols // KG
+    groups = (cols + KG - 1) // KG
     tiles = (rows + ROWS - 1) // ROWS
     words, sc = unpack_words(img, tiles, groups)
     # decode: a0 = (w & 0x000F000F) | 0x64006400, a2 = (w & 0x00F000F0) | ..., a1/a3 from w >> 8
@@ -90,7 +90,9 @@ def emulate_gemv(img: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.nda
     ex = int((np.float32(amax).view(np.uint32) >> 23) & 0xFF)
     k = min(max(268 - ex, 1), 254)
     alpha = np.uint32(k << 23).view(np.float32)
-    xs = x.reshape(groups, 4, 32).astype(np.float32) * alpha
+    xp = np.zeros(groups * KG, dtype=np.float32)
+    xp[:cols] = x
+    xs = xp.reshape(groups, 4, 32).astype(np.float32) * alpha
     xs[:, 2:, :] *= np.float32(0.0625)
     hi = xs.astype(np.float16).astype(np.float32)
     lo = (xs - hi).astype(np.float16).astype(np.float32)

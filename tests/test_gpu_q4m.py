@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 REL = 1e-3
 
 SHAPES = [(4096, 4096), (1024, 4096), (6144, 4096), (28672, 4096), (4096, 14336), (4096, 512), (4096, 1792),
-          (768, 512), (2816, 512), (512, 1408), (1, 128), (37, 384), (130, 4096), (128256, 4096)]
+          (768, 512), (2816, 512), (512, 1408), (1, 128), (37, 384), (130, 4096), (128256, 4096),
+          (512, 704), (40, 96), (4096, 7168)]
 
 
 def packed(w, rows, cols, cuda):
@@ -29,7 +30,7 @@ def workspace(rows, cols, cuda):
     return torch.zeros(K.gemv_q4m_workspace_bytes(rows, cols), dtype=torch.uint8, device=cuda)
 
 
-@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (100, 1408), (4096, 4096)])
+@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (100, 1408), (4096, 4096), (24, 704), (16, 96)])
 def test_q4m_pack_matches_layout(cuda, rows, cols):
     w = q4_0_rows(rows, cols, seed=rows)
     got = packed(w, rows, cols, cuda).cpu().numpy()

@@ -29,9 +29,9 @@ def rel_err(got, want):
 
 def test_q4m_bytes_formula():
     import jinf
-    for rows, cols in [(1, 128), (37, 384), (4096, 4096), (128256, 4096)]:
-        assert jinf.lib.jinf_b200_q4m_bytes(rows, cols) == ((rows + 15) // 16) * (cols // 128) * 1152
-    assert jinf.lib.jinf_b200_q4m_bytes(16, 96) == 0
+    for rows, cols in [(1, 128), (37, 384), (4096, 4096), (128256, 4096), (16, 96), (4096, 704)]:
+        assert jinf.lib.jinf_b200_q4m_bytes(rows, cols) == ((rows + 15) // 16) * ((cols + 127) // 128) * 1152
+    assert jinf.lib.jinf_b200_q4m_bytes(16, 100) == 0
 
 
 def test_nibble_positions_are_a_permutation():
@@ -39,16 +39,16 @@ def test_nibble_positions_are_a_permutation():
     assert bits == list(range(0, 32, 4))
 
 
-@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (100, 1408)])
+@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (100, 1408), (24, 704), (16, 96)])
 def test_pack_is_lossless(rows, cols):
     w = q4_0_rows(rows, cols, seed=rows)
     img = q4m_ref.pack(w, rows, cols)
-    tiles, groups = (rows + 15) // 16, cols // 128
+    tiles, groups = (rows + 15) // 16, (cols + 127) // 128
     assert img.size == tiles * groups * 1152
     words, sc = q4m_ref.unpack_words(img, tiles, groups)
     # every nibble exactly once: rebuild the AoS qs bytes from the words
     blocks = w.reshape(rows, cols // 32, 18)
-    got = np.zeros((tiles * 16, cols // 32, 32), dtype=np.uint8)
+    got = np.zeros((tiles * 16, groups * 4, 32), dtype=np.uint8)
     for lane in range(32):
         gr, c = lane >> 2, lane & 3
         for i in range(8):
@@ -61,11 +61,11 @@ def test_pack_is_lossless(rows, cols):
     want = np.empty((rows, cols // 32, 32), dtype=np.uint8)
     want[:, :, 0::2] = blocks[:, :, 2:] & 15
     want[:, :, 1::2] = blocks[:, :, 2:] >> 4
-    assert np.array_equal(got[:rows], want)
-    assert not got[rows:].any()
+    assert np.array_equal(got[:rows, :cols // 32], want)
+    assert not got[rows:].any() and not got[:, cols // 32:].any()
 
 
-@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (64, 1024), (100, 1408)])
+@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (64, 1024), (100, 1408), (48, 704), (16, 96)])
 def test_emulated_gemv_matches_oracle(rows, cols):
     w = q4_0_rows(rows, cols, seed=rows + cols)
     x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
