@@ -40,19 +40,19 @@ static constexpr int kQ4mMaxKw = 32;
 extern "C" size_t jinf_b200_gemv_q4m_workspace_bytes(int rows, int cols) {
     Q4MShape sh;
     if (!q4m_shape(rows, cols, &sh)) return 0;
-    return (size_t)sh.tiles * kQ4mMaxKw * 16 * sizeof(float) + (size_t)sh.tiles * sizeof(unsigned int);
+    return (size_t)sh.pairs * kQ4mMaxKw * Q4M_PAIR_ROWS * sizeof(float) + (size_t)sh.pairs * sizeof(unsigned int);
 }
 
 static jinf_status gemv_q4m_common(GemvParams& p, const Q4MShape& sh, int xm, void* workspace, int kw,
                                    cudaStream_t stream) {
     if (sh.cols > gemvm_max_cols() || kw < 0 || kw > kQ4mMaxKw) return JINF_ERR_INVALID;
     const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms());
-    if (kw == 0) kw = gemvm_pick_kw(sh.tiles, sh.groups, grid, workspace ? kQ4mMaxKw : 1);
+    if (kw == 0) kw = gemvm_pick_kw(sh.pairs, sh.groups, grid, workspace ? kQ4mMaxKw : 1);
     if (kw > sh.groups || (kw > 1 && !workspace)) return JINF_ERR_INVALID;
     p.kw = kw;
     if (kw > 1) {
         p.part = (float*)workspace;
-        p.cnt = (unsigned int*)((uint8_t*)workspace + (size_t)sh.tiles * kQ4mMaxKw * 16 * sizeof(float));
+        p.cnt = (unsigned int*)((uint8_t*)workspace + (size_t)sh.pairs * kQ4mMaxKw * Q4M_PAIR_ROWS * sizeof(float));
     }
     return gemvm_launch(p, xm, EPI_STORE, grid, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
 }
@@ -88,12 +88,12 @@ extern "C" jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* 
 // jinf_b200_gemv_q4m_noalloc: the same split-K tensor-core GEMV as jinf_b200_gemv_q4m, with
 // its workspace in this file-scope device array instead of caller memory, for callers that
 // cannot allocate device memory (or hand out a workspace) at call time. Layout: arrival
-// counters of up to kNoAllocMaxTiles tiles at a fixed offset (zero at module load; every
+// counters of up to kNoAllocMaxPairs tile pairs at a fixed offset (zero at module load; every
 // call leaves them zero again, so they are zero between calls), then the partial rows.
 // Calls that overlap in time (other streams, other host threads) share it and race.
 static constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;  // 4 MB
-static constexpr int kNoAllocMaxTiles = 16384;                   // rows <= 262144
-static constexpr size_t kNoAllocCntBytes = (size_t)kNoAllocMaxTiles * sizeof(unsigned int);
+static constexpr int kNoAllocMaxPairs = 8192;                    // rows <= 262144
+static constexpr size_t kNoAllocCntBytes = (size_t)kNoAllocMaxPairs * sizeof(unsigned int);
 static __device__ __align__(256) unsigned char g_gemv_noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of the scratch on the current device, looked up once per device (the
@@ -121,15 +121,15 @@ extern "C" jinf_status jinf_b200_gemv_q4m_noalloc(const void* q4m, const void* x
     if (!q4m || !x || !y || !q4m_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
     if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
     if (sh.cols > gemvm_max_cols()) return JINF_ERR_INVALID;
-    if (sh.tiles > kNoAllocMaxTiles) {
+    if (sh.pairs > kNoAllocMaxPairs) {
         JINF_LOG("jinf_b200_gemv_q4m_noalloc: %d rows exceed the static scratch limit of %d rows", rows,
-                 kNoAllocMaxTiles * Q4M_ROWS);
+                 kNoAllocMaxPairs * Q4M_PAIR_ROWS);
         return JINF_ERR_INVALID;
     }
     const int xm = x_type == JINF_TYPE_F32 ? X_PLAIN_F32 : X_PLAIN_F16;
     const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms());
-    const int kw = gemvm_pick_kw(sh.tiles, sh.groups, grid, kQ4mMaxKw);
-    const size_t part_bytes = (size_t)sh.tiles * kw * 16 * sizeof(float);
+    const int kw = gemvm_pick_kw(sh.pairs, sh.groups, grid, kQ4mMaxKw);
+    const size_t part_bytes = (size_t)sh.pairs * kw * Q4M_PAIR_ROWS * sizeof(float);
     if (kw > 1 && part_bytes > kNoAllocScratchBytes - kNoAllocCntBytes) {
         JINF_LOG("jinf_b200_gemv_q4m_noalloc: %d x %d needs %zu bytes of partial sums, the static scratch holds %zu",
                  rows, cols, part_bytes, kNoAllocScratchBytes - kNoAllocCntBytes);

@@ -366,7 +366,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
     // grid and K split of a stand-alone GEMV
     auto finish = [&](Op& op) {
         op.grid = gemvm_grid(op.gp.cols, op.xm, op.epi, I->num_sms);
-        op.gp.kw = gemvm_pick_kw(op.gp.tiles, op.gp.groups, op.grid, kEngineMaxKw);
+        op.gp.kw = gemvm_pick_kw(op.gp.pairs, op.gp.groups, op.grid, kEngineMaxKw);
         op.gp.part = I->gemv_part;
         op.gp.cnt = I->gemv_cnt;
     };
@@ -525,7 +525,7 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         p.w = w;
         p.rows = sh.rows;
         p.cols = sh.cols;
-        p.tiles = sh.tiles;
+        p.pairs = sh.pairs;
         p.groups = sh.groups;
         ph.push_back(p);
         return ph.back();
@@ -567,7 +567,7 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
     }
     for (size_t i = 0; i < ph.size(); ++i) {
         ph[i].dep = (int)i - 1;
-        ph[i].dep_target = i == 0 ? 0u : ph[i - 1].kind == PH_GEMV ? (unsigned)ph[i - 1].tiles : (unsigned)I->Hkvl;
+        ph[i].dep_target = i == 0 ? 0u : ph[i - 1].kind == PH_GEMV ? (unsigned)ph[i - 1].pairs : (unsigned)I->Hkvl;
     }
 }
 
@@ -989,13 +989,13 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
 
     // ---- split-K workspace of the stand-alone GEMVs (counters zero, self-resetting)
     {
-        size_t tiles = I->lm_sh.tiles;
+        size_t pairs = I->lm_sh.pairs;
         for (const auto& ly : I->layers)
-            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) tiles = std::max(tiles, (size_t)sh->tiles);
-        if (cudaMalloc(&I->gemv_part, sizeof(float) * tiles * kEngineMaxKw * 16) != cudaSuccess ||
-            cudaMalloc(&I->gemv_cnt, sizeof(unsigned int) * tiles) != cudaSuccess)
+            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) pairs = std::max(pairs, (size_t)sh->pairs);
+        if (cudaMalloc(&I->gemv_part, sizeof(float) * pairs * kEngineMaxKw * Q4M_PAIR_ROWS) != cudaSuccess ||
+            cudaMalloc(&I->gemv_cnt, sizeof(unsigned int) * pairs) != cudaSuccess)
             return fail(JINF_ERR_OOM);
-        cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * tiles);
+        cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * pairs);
     }
     if (tp == 1 && opt.persistent) {
         const jinf_status s = setup_persistent(I);

@@ -11,9 +11,9 @@
 namespace jinf {
 
 // One CTA of 16 warps per SM (persistent), each warp with a private ring of GEMV_M_NBUF
-// chunk slots.
+// unit slots (2304-byte tile-pair units).
 #ifndef JINF_GEMV_M_NBUF
-#define JINF_GEMV_M_NBUF 5
+#define JINF_GEMV_M_NBUF 4
 #endif
 constexpr int GEMV_M_THREADS = 512;
 constexpr int GEMV_M_NBUF = JINF_GEMV_M_NBUF;
@@ -23,10 +23,10 @@ enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3, EPI_R
 
 struct GemvParams {
     const uint8_t* w;  // Q4M stream of the matrix
-    int rows, cols, tiles, groups;
-    int kw;                 // K parts per tile (tasks per tile)
-    float* part;            // kw > 1: [tiles * kw][16] partial row sums
-    unsigned int* cnt;      // kw > 1: [tiles] arrival counters, zero before the first launch (self-resetting)
+    int rows, cols, pairs, groups;
+    int kw;                 // K parts per tile pair (tasks per pair)
+    float* part;            // kw > 1: [pairs * kw][32] partial row sums
+    unsigned int* cnt;      // kw > 1: [pairs] arrival counters, zero before the first launch (self-resetting)
     // prologue
     const void* x;          // X_PLAIN_*: input vector
     const float* hin;       // X_RMSNORM: residual stream
@@ -52,7 +52,7 @@ inline void gemvm_params_for(GemvParams& p, const void* w, const Q4MShape& sh) {
     p.w = (const uint8_t*)w;
     p.rows = sh.rows;
     p.cols = sh.cols;
-    p.tiles = sh.tiles;
+    p.pairs = sh.pairs;
     p.groups = sh.groups;
     p.kw = 1;
 }
@@ -60,8 +60,8 @@ size_t gemvm_smem_bytes(int cols);
 int gemvm_max_cols();
 // Persistent grid: resident CTAs per SM * num_sms.
 int gemvm_grid(int cols, int xm, int epi, int num_sms);
-// K parts per tile for a grid of `grid` CTAs (1 <= kw <= min(groups, max_kw)).
-int gemvm_pick_kw(int tiles, int groups, int grid, int max_kw);
+// K parts per tile pair for a grid of `grid` CTAs (1 <= kw <= min(groups, max_kw)).
+int gemvm_pick_kw(int pairs, int groups, int grid, int max_kw);
 cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
 // AoS Q4_0 [rows][cols] (device) -> Q4M (device, sh.bytes).
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s);

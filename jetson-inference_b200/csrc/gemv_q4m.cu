@@ -10,12 +10,12 @@
 //             EPI_GATEUP     rows interleaved (gate_n, up_n): h[n] = silu(gate_n) * up_n
 //             EPI_LMHEAD     logits[row] and a packed (value, index) atomicMax argmax
 //
-// Scheduling. Tasks are (tile, K part) pairs: a tile's groups are split over `kw` tasks so
-// that every SM gets about the same work. Each warp streams its tasks' chunks through a
-// private cp.async ring (GEMV_M_NBUF - 1 chunks of 1152 bytes in flight) that runs ahead
-// across task boundaries; the first chunks are requested before the kernel waits on its
+// Scheduling. Tasks are (tile pair, K part): a pair's groups are split over `kw` tasks so
+// that every SM gets about the same work. Each warp streams its tasks' units through a
+// private cp.async ring (GEMV_M_NBUF - 1 units of 2304 bytes in flight) that runs ahead
+// across task boundaries; the first units are requested before the kernel waits on its
 // producer (programmatic dependent launch), because weights never depend on it. With kw > 1
-// each task writes its 16 partial sums to a workspace and the last task of a tile (arrival
+// each task writes its 32 partial sums to a workspace and the last task of a pair (arrival
 // counter, reset by that task) adds them in K order, so results are deterministic.
 #include "common.cuh"
 #include "gemv.h"
@@ -53,9 +53,9 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     float* misc = xk + 4 * G;                                               // 64 floats
     const uint32_t ring0 = smem_u32(misc + 64);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * Q4M_CHUNK);
+    const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * Q4M_UNIT);
     const int kw = p.kw;
-    const int T = p.tiles * kw;
+    const int T = p.pairs * kw;  // tasks: (tile pair, K part)
     const int W = gridDim.x * NW;
 
     // ---------------- weight stream: tasks gw, gw + W, ... (consecutive tasks on different SMs)
@@ -68,8 +68,8 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     }
     auto issue = [&](int slot) {
         if (ctask < T) {
-            const int tile = ctask / kw;
-            copy_chunk_async(ring + slot * Q4M_CHUNK, p.w + ((size_t)tile * G + cg) * Q4M_CHUNK, lane);
+            const int pair = ctask / kw;
+            copy_unit_async(ring + slot * Q4M_UNIT, p.w + ((size_t)pair * G + cg) * Q4M_UNIT, lane);
             if (++cg == cge) {
                 ctask += W;
                 if (ctask < T) {
@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
 
     // ---------------- main loop
     const BSel bs(lane);
-    const int gr = lane >> 2, c = lane & 3;
+    const int c = lane & 3;
     EpiArgs ea;
     ea.epi = EPI;
     ea.rows = p.rows;
@@ -117,46 +117,44 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     int lidx = 0;
     int slot = 0;
     for (int task = gw; task < T; task += W) {
-        const int tile = task / kw, kp = task % kw;
+        const int pair = task / kw, kp = task % kw;
         const int g0 = kp * G / kw, g1 = (kp + 1) * G / kw;
-        float acc0 = 0.f, acc1 = 0.f;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int g = g0; g < g1; ++g) {
             issue(slot == 0 ? GEMV_M_NBUF - 1 : slot - 1);
             asm volatile("cp.async.wait_group %0;" ::"n"(GEMV_M_NBUF - 1) : "memory");
-            chunk_mma(ring + slot * Q4M_CHUNK, xb, xk, g, lane, bs, acc0, acc1);
+            unit_mma(ring + slot * Q4M_UNIT, xb, xk, g, lane, bs, acc);
             slot = slot + 1 == GEMV_M_NBUF ? 0 : slot + 1;
         }
-        const int r0 = 2 * (lane & 7);
+        unit_reduce(acc);
+        // lane q < 16 finishes rows 2q, 2q+1 of the pair's 32
+        const int r0 = 2 * (lane & 15);
         float v0, v1;
         if (kw == 1) {
-            tile_rows(acc0, acc1, lane, v0, v1);
+            v0 = unit_row(acc, r0);
+            v1 = unit_row(acc, r0 + 1);
         } else {
-            acc0 += __shfl_xor_sync(JINF_FULL_MASK, acc0, 1);
-            acc1 += __shfl_xor_sync(JINF_FULL_MASK, acc1, 1);
-            acc0 += __shfl_xor_sync(JINF_FULL_MASK, acc0, 2);
-            acc1 += __shfl_xor_sync(JINF_FULL_MASK, acc1, 2);
-            float* pt = p.part + (size_t)task * 16;
-            if (c == 0) {
-                pt[gr] = acc0;
-                pt[gr + 8] = acc1;
-            }
+            float* pt = p.part + (size_t)task * Q4M_PAIR_ROWS;
+            if (c == 0)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) pt[unit_row_of(i, lane)] = acc[i];
             __threadfence();
             __syncwarp();
             unsigned old = 0;
-            if (lane == 0) old = atomicAdd(p.cnt + tile, 1u);
+            if (lane == 0) old = atomicAdd(p.cnt + pair, 1u);
             old = __shfl_sync(JINF_FULL_MASK, old, 0);
-            if (old != (unsigned)(kw - 1)) continue;  // another task of this tile finishes it
+            if (old != (unsigned)(kw - 1)) continue;  // another task of this pair finishes it
             __threadfence();
-            if (lane == 0) p.cnt[tile] = 0u;  // ready for the next launch
+            if (lane == 0) p.cnt[pair] = 0u;  // ready for the next launch
             v0 = 0.f;
             v1 = 0.f;
-            const float* pb = p.part + (size_t)tile * kw * 16;
+            const float* pb = p.part + (size_t)pair * kw * Q4M_PAIR_ROWS;
             for (int q = 0; q < kw; ++q) {
-                v0 += __ldcg(pb + q * 16 + r0);
-                v1 += __ldcg(pb + q * 16 + r0 + 1);
+                v0 += __ldcg(pb + q * Q4M_PAIR_ROWS + r0);
+                v1 += __ldcg(pb + q * Q4M_PAIR_ROWS + r0 + 1);
             }
         }
-        if (lane < 8) epilogue_pair(ea, tile * Q4M_ROWS + r0, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
+        if (lane < 16) epilogue_pair(ea, pair * Q4M_PAIR_ROWS + r0, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 
@@ -195,7 +193,7 @@ __global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restric
         const int row = t * Q4M_ROWS + r;
         return row < rows && G * 4 + j < nb ? aos + ((size_t)row * nb + (size_t)G * 4 + j) * 18 : nullptr;
     };
-    uint8_t* chunk = dst + (size_t)tg * Q4M_CHUNK;
+    uint8_t* chunk = dst + q4m_chunk_offset(t, G, groups);
     for (int i = 0; i < 8; ++i) {
         const int e = 4 * i + c;
         uint32_t word = 0;
@@ -221,7 +219,7 @@ __global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restric
 
 size_t gemvm_smem_bytes(int cols) {
     const int G = (cols + Q4M_KG - 1) / Q4M_KG;
-    return (size_t)G * 512 + sizeof(float) * ((size_t)G * 4 + 64) + (size_t)NW * GEMV_M_NBUF * Q4M_CHUNK;
+    return (size_t)G * 512 + sizeof(float) * ((size_t)G * 4 + 64) + (size_t)NW * GEMV_M_NBUF * Q4M_UNIT;
 }
 
 int gemvm_max_cols() {
@@ -303,14 +301,14 @@ int gemvm_grid(int cols, int xm, int epi, int num_sms) {
     return occ_fn() * num_sms;
 }
 
-// K split per tile: the smallest cost ceil(tasks / grid) * (groups per task + overhead),
+// K split per tile pair: the smallest cost ceil(tasks / grid) * (groups per task + overhead),
 // with at least 8 busy warps per CTA where the matrix allows it.
-int gemvm_pick_kw(int tiles, int groups, int grid, int max_kw) {
+int gemvm_pick_kw(int pairs, int groups, int grid, int max_kw) {
     int best = 1;
     double best_cost = 1e300;
     const int lim = groups < max_kw ? groups : max_kw;
     for (int kw = 1; kw <= lim; ++kw) {
-        const long long T = (long long)tiles * kw;
+        const long long T = (long long)pairs * kw;
         const bool busy = T >= (long long)grid * 8;
         const double per_cta = (double)((T + grid - 1) / grid);
         const double cost = per_cta * ((double)((groups + kw - 1) / kw) + (kw > 1 ? 0.6 : 0.1)) + (busy ? 0.0 : 1e9 / (double)T);

@@ -5,7 +5,9 @@
 //
 // Geometry. A matrix [rows][cols] is cut into tiles of 16 rows (the MMA's M) and groups
 // of 128 columns (4 Q4_0 blocks j = 0..3). The bytes of one (tile t, group G) form one
-// contiguous chunk of 1152 bytes at byte (t * groups + G) * 1152:
+// contiguous chunk of 1152 bytes; the chunks of the two tiles of a tile pair (t = 2P, 2P+1)
+// and one group are adjacent, forming a 2304-byte unit at byte (P * groups + G) * 2304, so
+// one copy brings 32 rows x 128 columns and both tiles share the same x fragments. A chunk:
 //   bytes    0 ..  511   piece 0: [32 lanes][4 words]   words 0..3 (MMA steps 0..3)
 //   bytes  512 .. 1023   piece 1: [32 lanes][4 words]   words 4..7 (MMA steps 4..7)
 //   bytes 1024 .. 1151   [32 lanes][2 x fp16]           d(row gr, block c), d(row gr+8, block c)
@@ -33,16 +35,24 @@
 
 namespace jinf {
 
-constexpr int Q4M_ROWS = 16;     // rows per tile
-constexpr int Q4M_KG = 128;      // columns per group
-constexpr int Q4M_CHUNK = 1152;  // bytes per (tile, group)
+constexpr int Q4M_ROWS = 16;             // rows per tile
+constexpr int Q4M_KG = 128;              // columns per group
+constexpr int Q4M_CHUNK = 1152;          // bytes per (tile, group)
+constexpr int Q4M_UNIT = 2 * Q4M_CHUNK;  // bytes per (tile pair, group)
+constexpr int Q4M_PAIR_ROWS = 2 * Q4M_ROWS;
 
 struct Q4MShape {
     int rows, cols;
-    int tiles;   // ceil(rows / 16)
+    int tiles;   // 2 * pairs (rows padded to a multiple of 32)
+    int pairs;   // ceil(rows / 32)
     int groups;  // ceil(cols / 128)
     uint64_t bytes;
 };
+
+// Byte offset of the chunk of tile t, group g.
+__host__ __device__ inline uint64_t q4m_chunk_offset(int t, int g, int groups) {
+    return ((uint64_t)(t >> 1) * groups + g) * Q4M_UNIT + (uint64_t)(t & 1) * Q4M_CHUNK;
+}
 
 // cols must be whole Q4_0 blocks (a multiple of 32); the last group is padded with zero
 // blocks (scale 0) when cols is not a multiple of 128, and the GEMV stages zeros for x there.
@@ -50,9 +60,10 @@ inline bool q4m_shape(int rows, int cols, Q4MShape* s) {
     if (rows <= 0 || cols <= 0 || cols % 32) return false;
     s->rows = rows;
     s->cols = cols;
-    s->tiles = (rows + Q4M_ROWS - 1) / Q4M_ROWS;
+    s->pairs = (rows + Q4M_PAIR_ROWS - 1) / Q4M_PAIR_ROWS;
+    s->tiles = 2 * s->pairs;
     s->groups = (cols + Q4M_KG - 1) / Q4M_KG;
-    s->bytes = (uint64_t)s->tiles * s->groups * Q4M_CHUNK;
+    s->bytes = (uint64_t)s->pairs * s->groups * Q4M_UNIT;
     return true;
 }
 

@@ -106,6 +106,71 @@ __device__ __forceinline__ void chunk_mma(uint32_t sl, const uint16_t* xb, const
     acc1 = fmaf(jinf_h2f((uint16_t)(sc >> 16)), t1, acc1);
 }
 
+// This lane's share of one 2304-byte unit (the chunks of a tile pair and one group).
+__device__ __forceinline__ void copy_unit_async(uint32_t slot, const uint8_t* unit, int lane) {
+    copy_chunk_async(slot, unit, lane);
+    copy_chunk_async(slot + Q4M_CHUNK, unit + Q4M_CHUNK, lane);
+}
+
+// One unit (32 rows x 128 columns) from ring slot `sl` against staged group g: both tiles
+// of the pair share the B fragments. acc[0], acc[1] += rows gr, gr+8 of the first tile,
+// acc[2], acc[3] += rows gr, gr+8 of the second (block c of the group, c = lane & 3).
+__device__ __forceinline__ void unit_mma(uint32_t sl, const uint16_t* xb, const float* xk, int g, int lane,
+                                         const BSel& bs, float (&acc)[4]) {
+    uint32_t w[8], v[8], sca, scb;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "r"(sl + lane * 16));
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7]) : "r"(sl + 512 + lane * 16));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(sca) : "r"(sl + 1024 + lane * 4));
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]) : "r"(sl + Q4M_CHUNK + lane * 16));
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]) : "r"(sl + Q4M_CHUNK + 512 + lane * 16));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(scb) : "r"(sl + Q4M_CHUNK + 1024 + lane * 4));
+    const uint4 xv = *reinterpret_cast<const uint4*>(xb + (size_t)g * 256 + lane * 8);
+    const float k = xk[g * 4 + (lane & 3)];
+    float da[4] = {k, 0.f, k, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+    float ea[4] = {k, 0.f, k, 0.f}, eb[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const uint32_t p0 = __byte_perm(xw[i >> 1], 0u, bs.s0e), p1 = __byte_perm(xw[i >> 1], 0u, bs.s1e);
+        const uint32_t q0 = __byte_perm(xw[i >> 1], 0u, bs.s0o), q1 = __byte_perm(xw[i >> 1], 0u, bs.s1o);
+        mma_step(w[i], p0, p1, da);
+        mma_step(v[i], p0, p1, ea);
+        mma_step(w[i + 1], q0, q1, db);
+        mma_step(v[i + 1], q0, q1, eb);
+    }
+    acc[0] = fmaf(jinf_h2f((uint16_t)(sca & 0xffffu)), (da[0] + da[1]) + (db[0] + db[1]), acc[0]);
+    acc[1] = fmaf(jinf_h2f((uint16_t)(sca >> 16)), (da[2] + da[3]) + (db[2] + db[3]), acc[1]);
+    acc[2] = fmaf(jinf_h2f((uint16_t)(scb & 0xffffu)), (ea[0] + ea[1]) + (eb[0] + eb[1]), acc[2]);
+    acc[3] = fmaf(jinf_h2f((uint16_t)(scb >> 16)), (ea[2] + ea[3]) + (eb[2] + eb[3]), acc[3]);
+}
+
+// Sum the four accumulators over the lanes of a row group (blocks c = 0..3): afterwards
+// lane (gr, c) holds rows gr, gr+8, 16+gr, 24+gr of the unit's 32 rows.
+__device__ __forceinline__ void unit_reduce(float (&acc)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc[i] += __shfl_xor_sync(JINF_FULL_MASK, acc[i], 1);
+        acc[i] += __shfl_xor_sync(JINF_FULL_MASK, acc[i], 2);
+    }
+}
+
+// Row r (0..31) of a reduced unit as seen from the calling lane (all lanes participate).
+__device__ __forceinline__ float unit_row(const float (&acc)[4], int r) {
+    const int rr = r & 15, src = 4 * (rr & 7), which = ((r >> 4) << 1) | (rr >> 3);
+    const float v0 = __shfl_sync(JINF_FULL_MASK, acc[0], src);
+    const float v1 = __shfl_sync(JINF_FULL_MASK, acc[1], src);
+    const float v2 = __shfl_sync(JINF_FULL_MASK, acc[2], src);
+    const float v3 = __shfl_sync(JINF_FULL_MASK, acc[3], src);
+    return which == 0 ? v0 : which == 1 ? v1 : which == 2 ? v2 : v3;
+}
+
+// Index of the reduced row held in acc[i] by lane (gr, c): gr, gr+8, 16+gr, 24+gr.
+__device__ __forceinline__ int unit_row_of(int i, int lane) { return (lane >> 2) + 8 * i; }
+
 __device__ __forceinline__ uint32_t ordered_bits(float v) {
     const uint32_t b = __float_as_uint(v);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);

@@ -12,10 +12,10 @@
 namespace jinf {
 
 #ifndef JINF_STEP_NBUF
-#define JINF_STEP_NBUF 6
+#define JINF_STEP_NBUF 4
 #endif
 constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
-constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 chunks in flight)
+constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 units in flight)
 constexpr int ATTN_POS_PER_WARP = 32;  // attention positions per warp (one lane each)
 constexpr int ATTN_POS_PER_CTA = 512;  // attention positions per CTA: 16 warps x 32
 
@@ -25,7 +25,7 @@ constexpr int ATTN_MAX_GROUP = 8;      // query heads per kv head
 enum PhaseKind { PH_GEMV = 0, PH_ATTN = 1 };
 
 // One phase of the decode step. A phase starts (on every CTA) once phase `dep` has
-// reported `dep_target` finished units: GEMV phases count finished 16-row tiles,
+// reported `dep_target` finished units: GEMV phases count finished 32-row tile pairs,
 // attention counts finished kv heads.
 struct StepPhase {
     int kind;
@@ -34,7 +34,7 @@ struct StepPhase {
     // PH_GEMV
     int xm, epi;
     const uint8_t* w;        // Q4M matrix
-    int rows, cols, tiles, groups;
+    int rows, cols, pairs, groups;
     const float* x;          // X_PLAIN_F32: input (written earlier in the step)
     const float* hsrc;       // X_RMSNORM: residual stream; X_EMBED_NORM: token_embd [V][cols]
     float* hout;             // X_EMBED_NORM: residual stream (CTA 0 stores the embedding row)
@@ -60,8 +60,8 @@ struct StepParams {
     unsigned long long spin_limit;  // polls before a dependency wait gives up (DEV_ERR_TIMEOUT)
 };
 
-// CTA c of C owns tiles [step_cta_tile(c), step_cta_tile(c + 1)) of every GEMV phase.
-// (c * T stays far below 2^31: at most a few hundred CTAs times tens of thousands of tiles.)
+// CTA c of C owns tile pairs [step_cta_tile(c), step_cta_tile(c + 1)) of every GEMV phase.
+// (c * T stays far below 2^32: at most a few hundred CTAs times tens of thousands of pairs.)
 __host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)((unsigned)(c * T) / (unsigned)C); }
 
 // Shared bytes of the staged input for the widest GEMV phase, or of the attention scratch

@@ -6,15 +6,15 @@
 // (about 5-8 us per kernel on B200), more than the 1-10 us its weights take to stream.
 // Here the weight stream does not stop at phase boundaries, and every dependency costs as
 // few global round trips as possible (one round trip under load is ~0.75-1 us):
-//   * CTA c owns a contiguous, balanced set of whole 16-row tiles of every matrix; its 16
-//     warps split the CTA's 1152-byte Q4M chunks (q4m.cuh) evenly, so a tile shared by
-//     several warps is merged through shared memory in warp order (deterministic, no
-//     global atomics), and the CTA reports its finished tiles with one counter add;
-//   * each warp walks its chunk ranges of all matrices in step order with a cp.async ring
-//     (STEP_NBUF - 1 chunks in flight) feeding the tensor-core decode (q4m_device.cuh) and
-//     an L2-prefetch cursor STEP_PF_DIST chunks further ahead, so while a CTA waits for
-//     the inputs of the next phase its weights are already on their way; the stream's
-//     geometry lives in shared memory;
+//   * CTA c owns a contiguous, balanced set of whole 32-row tile pairs of every matrix; its
+//     16 warps split the CTA's 2304-byte Q4M units (q4m.cuh: a tile pair x 128 columns)
+//     evenly, so a pair shared by several warps is merged through shared memory in warp
+//     order (deterministic, no global atomics), and the CTA reports its finished pairs
+//     with one counter add;
+//   * each warp walks its unit ranges of all matrices in step order with a cp.async ring
+//     (STEP_NBUF - 1 units in flight) feeding the tensor-core decode (q4m_device.cuh), so
+//     while a CTA waits for the inputs of the next phase its first weights are already on
+//     their way; the stream's geometry lives in shared memory;
 //   * phases wait on completion counters instead of kernel boundaries (bounded spins:
 //     DEV_ERR_TIMEOUT in the device state, never a hang).
 // Per layer the phases are the reference's decode order (src/engine.cpp:418-511):
@@ -65,11 +65,11 @@ __device__ bool wait_ge(const unsigned* c, unsigned target, DeviceState* st, uns
 // Stream geometry of one phase, kept in shared memory (groups == 0: no weights).
 struct PhaseInfo {
     const uint8_t* w;
-    int tiles, groups;
+    int pairs, groups;
 };
 
-// Chunk range [c0, c1) of warp `warp` of CTA `cta` (of C) in a tiles x groups matrix
-// (32-bit: a matrix has far fewer than 2^31 chunks).
+// Unit range [c0, c1) of warp `warp` of CTA `cta` (of C) in a pairs x groups matrix
+// (32-bit: a matrix has far fewer than 2^31 units).
 __device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int G, int& c0, int& c1) {
     const int t0 = step_cta_tile(cta, C, T), t1 = step_cta_tile(cta + 1, C, T);
     const int n = (t1 - t0) * G;
@@ -79,7 +79,7 @@ __device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int 
 static_assert(NW == 16, "warp_range divides by the warp count with a shift");
 
 // Where a warp's weight stream continues: the first GEMV phase at or after `from` in which
-// it has chunks, and that range. Out of line: it runs once per phase, and keeping it out of
+// it has units, and that range. Out of line: it runs once per phase, and keeping it out of
 // the copy loop keeps the loop's live state small.
 struct StreamPos {
     const uint8_t* w;
@@ -91,7 +91,7 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
         const int G = pinfo[i].groups;
         if (!G) continue;
         int c0, c1;
-        warp_range(cta, C, warp, pinfo[i].tiles, G, c0, c1);
+        warp_range(cta, C, warp, pinfo[i].pairs, G, c0, c1);
         if (c0 < c1) {
             r.w = pinfo[i].w;
             r.ph = i;
@@ -107,7 +107,7 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
     return r;
 }
 
-// The weight stream of one warp between calls: ring slot of the next chunk to consume and
+// The weight stream of one warp between calls: ring slot of the next unit to consume and
 // the copy position.
 struct WarpStream {
     StreamPos sp;
@@ -115,10 +115,10 @@ struct WarpStream {
 };
 
 struct PieceSum {
-    float acc0, acc1;
+    float acc[4];
 };
 
-// Consume groups [gb, ge) of one tile from the ring (tensor-core decode, q4m_device.cuh),
+// Consume groups [gb, ge) of one tile pair from the ring (tensor-core decode, q4m_device.cuh),
 // refilling it as it goes. Out of line so that the hot loop gets a register allocation of
 // its own, independent of the rest of the step kernel.
 __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, const PhaseInfo* pinfo, int n_phases,
@@ -127,21 +127,21 @@ __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, con
     const BSel bs(lane);
     StreamPos sp = ws.sp;
     int slot = ws.slot;
-    float acc0 = 0.f, acc1 = 0.f;
+    PieceSum r{{0.f, 0.f, 0.f, 0.f}};
     for (int g = gb; g < ge; ++g) {
         const int is = slot == 0 ? STEP_NBUF - 1 : slot - 1;
         if (sp.c < sp.c1) {
-            copy_chunk_async(ring + is * Q4M_CHUNK, sp.w + (size_t)sp.c * Q4M_CHUNK, lane);
+            copy_unit_async(ring + is * Q4M_UNIT, sp.w + (size_t)sp.c * Q4M_UNIT, lane);
             if (++sp.c == sp.c1) sp = stream_seek(pinfo, n_phases, sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
         asm volatile("cp.async.wait_group %0;" ::"n"(STEP_NBUF - 1) : "memory");
-        chunk_mma(ring + slot * Q4M_CHUNK, xb, xk, g, lane, bs, acc0, acc1);
+        unit_mma(ring + slot * Q4M_UNIT, xb, xk, g, lane, bs, r.acc);
         slot = slot + 1 == STEP_NBUF ? 0 : slot + 1;
     }
     ws.sp = sp;
     ws.slot = slot;
-    return PieceSum{acc0, acc1};
+    return r;
 }
 
 __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
@@ -312,7 +312,7 @@ __device__ __forceinline__ float merge_parts(const float* base, int n, size_t st
 
 __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     extern __shared__ __align__(16) uint8_t smem[];
-    // shared memory: [xstage | misc 256 B | flags, keys, piece table 512 B | partial rows 2 KB |
+    // shared memory: [xstage | misc 256 B | flags, keys, piece table 512 B | partial rows 4 KB |
     //                 phase descriptor 2 x 256 B | phase infos | rings]
     uint8_t* xbase = smem;
     float* misc = reinterpret_cast<float*>(smem + P.xstage_bytes);        // 64 floats of reductions
@@ -320,12 +320,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     u64* wkeys = reinterpret_cast<u64*>(smem + P.xstage_bytes + 256 + 64);  // [NW] argmax keys
     int* ftile = reinterpret_cast<int*>(smem + P.xstage_bytes + 256 + 192);  // [NW] tile of a warp's first piece
     int* fmid = ftile + NW;                                                  // [NW] first piece starts mid-tile
-    float* part_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768);   // [NW][2][16] partial rows
-    StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 2048);  // [2] descriptors
-    PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 2048 + 512);
+    float* part_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768);   // [NW][2][32] partial rows
+    StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 4096);  // [2] descriptors
+    PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 4096 + 512);
     const uint32_t ring_base = smem_u32(pinfo + ((P.n_phases + 1) & ~1));
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t ring = ring_base + (uint32_t)(warp * STEP_NBUF * Q4M_CHUNK);
+    const uint32_t ring = ring_base + (uint32_t)(warp * STEP_NBUF * Q4M_UNIT);
     const int C = gridDim.x;
     DeviceState* st = P.st;
     const int pos = *(volatile int*)&st->pos;
@@ -334,26 +334,26 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     for (int i = tid; i < P.n_phases; i += STEP_THREADS) {
         PhaseInfo pi;
         pi.w = P.phases[i].w;
-        pi.tiles = P.phases[i].tiles;
+        pi.pairs = P.phases[i].pairs;
         pi.groups = P.phases[i].kind == PH_GEMV ? P.phases[i].groups : 0;
         pinfo[i] = pi;
     }
     __syncthreads();
 
-    // ---------------- weight stream: this warp's chunk ranges of all GEMV phases, copied in
-    // consumption order into the ring (STEP_NBUF - 1 chunks ahead of the arithmetic)
+    // ---------------- weight stream: this warp's unit ranges of all GEMV phases, copied in
+    // consumption order into the ring (STEP_NBUF - 1 units ahead of the arithmetic)
     WarpStream ws;
     ws.sp = stream_seek(pinfo, P.n_phases, 0, blockIdx.x, C, warp);
     ws.slot = 0;
     for (int i = 0; i < STEP_NBUF - 1; ++i) {
         if (ws.sp.c < ws.sp.c1) {
-            copy_chunk_async(ring + i * Q4M_CHUNK, ws.sp.w + (size_t)ws.sp.c * Q4M_CHUNK, lane);
+            copy_unit_async(ring + i * Q4M_UNIT, ws.sp.w + (size_t)ws.sp.c * Q4M_UNIT, lane);
             if (++ws.sp.c == ws.sp.c1) ws.sp = stream_seek(pinfo, P.n_phases, ws.sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
     }
 
-    const int gr = lane >> 2, c4 = lane & 3;
+    const int c4 = lane & 3;
     const uint16_t* xb = reinterpret_cast<const uint16_t*>(xbase);
     float lmax = -INFINITY;
     int lidx = 0;
@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             continue;
         }
 
-        // ---------------- GEMV phase: this CTA's tiles [t0, t1)
+        // ---------------- GEMV phase: this CTA's tile pairs [t0, t1)
         if (d.epi == EPI_QKV && tid == 0 && pos > 0 && (int)blockIdx.x < 2 * P.n_kv_heads) {
             // the attention after this phase reads this layer's K and V rows 0..pos-1 (one
             // region per CTA): bring them into L2 now, while the QKV weights stream
@@ -467,11 +467,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                 prefetch_l2(reinterpret_cast<const uint8_t*>(base) + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
         }
         const int G = d.groups;
-        const int t0 = step_cta_tile(blockIdx.x, C, d.tiles), t1 = step_cta_tile(blockIdx.x + 1, C, d.tiles);
+        const int t0 = step_cta_tile(blockIdx.x, C, d.pairs), t1 = step_cta_tile(blockIdx.x + 1, C, d.pairs);
         if (t0 >= t1) continue;
         float* xk = reinterpret_cast<float*>(xbase + (size_t)G * 512);
         const float* hsrc = d.xm == X_EMBED_NORM ? d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols : d.hsrc;
-        // the CTA that owns tile 0 stores the embedding row as the residual stream
+        // the CTA that owns pair 0 stores the embedding row as the residual stream
         const float inv_alpha = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps,
                                                       d.cols, xbase, xk, misc, true);
         // epilogue arguments are read from the shared descriptor when a tile finishes
@@ -492,58 +492,54 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             epilogue_pair(ea, row, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
         };
         int c, c1;
-        warp_range(blockIdx.x, C, warp, d.tiles, G, c, c1);
+        warp_range(blockIdx.x, C, warp, d.pairs, G, c, c1);
         if (lane == 0) {
             ftile[warp] = -1;
             fmid[warp] = 0;
         }
         bool first_piece = true;
-        int own_tile = -1, own_slot = 0;  // the split tile this warp finishes (its piece starts the tile)
-        int tile = c / G, gb = c - tile * G;  // walked incrementally: no division per piece
-        for (; c < c1; ++tile, gb = 0) {
+        int own_pair = -1, own_slot = 0;  // the split pair this warp finishes (its piece starts the pair)
+        int pair = c / G, gb = c - pair * G;  // walked incrementally: no division per piece
+        for (; c < c1; ++pair, gb = 0) {
             const int ge = c1 - c < G - gb ? gb + (c1 - c) : G;
-            const PieceSum ps = stream_piece(ws, ring, pinfo, P.n_phases, C, xb, xk, gb, ge);
-            float acc0 = ps.acc0, acc1 = ps.acc1;
+            PieceSum ps = stream_piece(ws, ring, pinfo, P.n_phases, C, xb, xk, gb, ge);
             c += ge - gb;
             if (first_piece && lane == 0) {
-                ftile[warp] = tile;
+                ftile[warp] = pair;
                 fmid[warp] = gb > 0;
             }
+            unit_reduce(ps.acc);
             if (gb == 0 && ge == G) {
-                float v0, v1;
-                tile_rows(acc0, acc1, lane, v0, v1);
-                if (lane < 8) epilogue(tile * Q4M_ROWS + 2 * lane, v0, v1);
+                const int q = lane & 15;
+                const float v0 = unit_row(ps.acc, 2 * q), v1 = unit_row(ps.acc, 2 * q + 1);
+                if (lane < 16) epilogue(pair * Q4M_PAIR_ROWS + 2 * q, v0, v1);
             } else {
-                // a piece of a tile shared with the neighbouring warps: partial rows to shared memory
-                acc0 += __shfl_xor_sync(JINF_FULL_MASK, acc0, 1);
-                acc1 += __shfl_xor_sync(JINF_FULL_MASK, acc1, 1);
-                acc0 += __shfl_xor_sync(JINF_FULL_MASK, acc0, 2);
-                acc1 += __shfl_xor_sync(JINF_FULL_MASK, acc1, 2);
+                // a piece of a pair shared with the neighbouring warps: partial rows to shared memory
                 const int sl = first_piece ? 0 : 1;
                 if (c4 == 0) {
-                    part_s[(warp * 2 + sl) * 16 + gr] = acc0;
-                    part_s[(warp * 2 + sl) * 16 + gr + 8] = acc1;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) part_s[(warp * 2 + sl) * 32 + unit_row_of(i, lane)] = ps.acc[i];
                 }
                 if (gb == 0) {
-                    own_tile = tile;
+                    own_pair = pair;
                     own_slot = sl;
                 }
             }
             first_piece = false;
         }
         __syncthreads();
-        if (own_tile >= 0 && lane < 8) {
+        if (own_pair >= 0 && lane < 16) {
             // add the pieces of the following warps in warp order, then the epilogue
-            float v0 = part_s[(warp * 2 + own_slot) * 16 + 2 * lane];
-            float v1 = part_s[(warp * 2 + own_slot) * 16 + 2 * lane + 1];
+            float v0 = part_s[(warp * 2 + own_slot) * 32 + 2 * lane];
+            float v1 = part_s[(warp * 2 + own_slot) * 32 + 2 * lane + 1];
             for (int w2 = warp + 1; w2 < NW; ++w2) {
                 const int ft = ftile[w2];
-                if (ft < 0) continue;                       // a warp with no chunks in this phase
-                if (ft != own_tile || !fmid[w2]) break;     // the next tile starts
-                v0 += part_s[(w2 * 2) * 16 + 2 * lane];
-                v1 += part_s[(w2 * 2) * 16 + 2 * lane + 1];
+                if (ft < 0) continue;                       // a warp with no units in this phase
+                if (ft != own_pair || !fmid[w2]) break;     // the next pair starts
+                v0 += part_s[(w2 * 2) * 32 + 2 * lane];
+                v1 += part_s[(w2 * 2) * 32 + 2 * lane + 1];
             }
-            epilogue(own_tile * Q4M_ROWS + 2 * lane, v0, v1);
+            epilogue(own_pair * Q4M_PAIR_ROWS + 2 * lane, v0, v1);
         }
         __syncthreads();  // every epilogue store of the CTA precedes the report
         if (tid == 0) {
@@ -598,7 +594,7 @@ unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
 
 size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases) {
     const size_t infos = sizeof(PhaseInfo) * (size_t)((n_phases + 1) & ~1);
-    return (size_t)xstage_bytes + 768 + 2048 + 512 + infos + (size_t)NW * STEP_NBUF * Q4M_CHUNK;
+    return (size_t)xstage_bytes + 768 + 4096 + 512 + infos + (size_t)NW * STEP_NBUF * Q4M_UNIT;
 }
 
 static cudaError_t step_configure(size_t smem) {

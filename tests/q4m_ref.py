@@ -8,7 +8,7 @@ be checked against the oracle without a GPU.
 """
 import numpy as np
 
-ROWS, KG, CHUNK = 16, 128, 1152
+ROWS, KG, CHUNK = 16, 128, 1152   # chunks of tiles 2P and 2P+1 (one group) are adjacent
 
 
 def nibble_bit(r, j):
@@ -19,7 +19,7 @@ def pack(aos: np.ndarray, rows: int, cols: int) -> np.ndarray:
     """AoS Q4_0 [rows][cols/32*18] uint8 -> Q4M bytes."""
     nb = cols // 32
     groups = (cols + KG - 1) // KG
-    tiles = (rows + ROWS - 1) // ROWS
+    tiles = 2 * ((rows + 2 * ROWS - 1) // (2 * ROWS))
     blk = np.zeros((tiles * ROWS, groups * 4, 18), dtype=np.uint8)   # padded blocks: scale 0, nibbles 0
     blk[:rows, :nb] = aos.reshape(rows, nb, 18)
     qs = blk[:, :, 2:]
@@ -50,11 +50,12 @@ def pack(aos: np.ndarray, rows: int, cols: int) -> np.ndarray:
         gr, c = lane >> 2, lane & 3
         sc[:, :, lane] = d[:, gr, :, c] | (d[:, gr + 8, :, c] << 16)
     out[:, :, 1024:] = sc.astype('<u4').view(np.uint8).reshape(tiles, groups, 128)
-    return out.reshape(-1)
+    # memory order: (tile pair, group, tile in pair)
+    return out.reshape(tiles // 2, 2, groups, CHUNK).transpose(0, 2, 1, 3).reshape(-1)
 
 
 def unpack_words(img: np.ndarray, tiles: int, groups: int):
-    ch = img.reshape(tiles, groups, CHUNK)
+    ch = img.reshape(tiles // 2, groups, 2, CHUNK).transpose(0, 2, 1, 3).reshape(tiles, groups, CHUNK)
     w = np.concatenate([ch[:, :, 0:512].reshape(tiles, groups, 32, 16),
                         ch[:, :, 512:1024].reshape(tiles, groups, 32, 16)], axis=3)
     words = w.copy().view('<u4').reshape(tiles, groups, 32, 8)
@@ -68,7 +69,7 @@ def _f16(bits):
 
 def emulate_gemv(img: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
     groups = (cols + KG - 1) // KG
-    tiles = (rows + ROWS - 1) // ROWS
+    tiles = 2 * ((rows + 2 * ROWS - 1) // (2 * ROWS))
     words, sc = unpack_words(img, tiles, groups)
     # decode: a0 = (w & 0x000F000F) | 0x64006400, a2 = (w & 0x00F000F0) | ..., a1/a3 from w >> 8
     val = np.zeros((tiles, groups, ROWS, 4, 32), dtype=np.float32)  # decoded A value (1024 + s q)

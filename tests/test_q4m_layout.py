@@ -30,7 +30,7 @@ def rel_err(got, want):
 def test_q4m_bytes_formula():
     import jinf
     for rows, cols in [(1, 128), (37, 384), (4096, 4096), (128256, 4096), (16, 96), (4096, 704)]:
-        assert jinf.lib.jinf_b200_q4m_bytes(rows, cols) == ((rows + 15) // 16) * ((cols + 127) // 128) * 1152
+        assert jinf.lib.jinf_b200_q4m_bytes(rows, cols) == ((rows + 31) // 32) * ((cols + 127) // 128) * 2304
     assert jinf.lib.jinf_b200_q4m_bytes(16, 100) == 0
 
 
@@ -43,7 +43,7 @@ def test_nibble_positions_are_a_permutation():
 def test_pack_is_lossless(rows, cols):
     w = q4_0_rows(rows, cols, seed=rows)
     img = q4m_ref.pack(w, rows, cols)
-    tiles, groups = (rows + 15) // 16, (cols + 127) // 128
+    tiles, groups = 2 * ((rows + 31) // 32), (cols + 127) // 128
     assert img.size == tiles * groups * 1152
     words, sc = q4m_ref.unpack_words(img, tiles, groups)
     # every nibble exactly once: rebuild the AoS qs bytes from the words

@@ -77,6 +77,6 @@ def test_noalloc_rejects_oversize_and_bad_arguments(cuda):
     dummy = torch.zeros(64, dtype=torch.uint8, device=cuda)
     xf = torch.zeros(128, dtype=torch.float32, device=cuda)
     y = torch.zeros(16, dtype=torch.float32, device=cuda)
-    # 16385 tiles of 16 rows: beyond the static scratch (checked before any memory is touched)
-    assert noalloc(dummy, xf, y, 16385 * 16, 128) == JINF_ERR_INVALID
-    assert noalloc(dummy, xf, y, 16, 96) == JINF_ERR_INVALID    # cols not a multiple of 128
+    # 8193 tile pairs of 32 rows: beyond the static scratch (checked before any memory is touched)
+    assert noalloc(dummy, xf, y, 8193 * 32, 128) == JINF_ERR_INVALID
+    assert noalloc(dummy, xf, y, 16, 100) == JINF_ERR_INVALID   # cols not a multiple of 32
