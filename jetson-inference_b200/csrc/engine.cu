@@ -568,6 +568,25 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
     for (size_t i = 0; i < ph.size(); ++i) {
         ph[i].dep = (int)i - 1;
         ph[i].dep_target = i == 0 ? 0u : ph[i - 1].kind == PH_GEMV ? (unsigned)ph[i - 1].pairs : (unsigned)I->Hkvl;
+        ph[i].pf[0] = ph[i].pf[1] = -1;
+    }
+    // L2 prefetch schedule (phase order per layer: qkv, attention, o, gate|up, down). HBM
+    // would idle while attention runs and while CTAs stage inputs and merge rows; in those
+    // windows each CTA pulls the weights it owns in a later phase into L2, and the later
+    // ring copies hit L2. At most ~80 MB are outstanding at any time (L2: 126 MB).
+    const int n = (int)ph.size();
+    for (int i = 0; i < n; ++i) {
+        const bool gemv_next = i + 1 < n && ph[i + 1].kind == PH_GEMV;
+        if (ph[i].kind == PH_ATTN) {
+            if (JINF_STEP_PF_MODE >= 1 && i + 2 < n) {
+                ph[i].pf[0] = i + 1;  // o
+                ph[i].pf[1] = i + 2;  // gate|up
+            }
+        } else if (ph[i].epi == EPI_GATEUP) {
+            if (JINF_STEP_PF_MODE >= 2 && gemv_next) ph[i].pf[0] = i + 1;  // down
+        } else if (ph[i].epi == EPI_RESID && ph[i].xm == X_PLAIN_F32 && i > 0 && ph[i - 1].epi == EPI_GATEUP) {
+            if (JINF_STEP_PF_MODE >= 3 && gemv_next && ph[i + 1].epi == EPI_QKV) ph[i].pf[0] = i + 1;  // next qkv
+        }
     }
 }
 

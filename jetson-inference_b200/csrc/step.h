@@ -14,6 +14,11 @@ namespace jinf {
 #ifndef JINF_STEP_NBUF
 #define JINF_STEP_NBUF 4
 #endif
+// L2 prefetch schedule of the persistent step (engine.cu, build_step): 0 none; 1 o and
+// gate|up during attention; 2 also down during gate|up; 3 also the next layer's QKV during down.
+#ifndef JINF_STEP_PF_MODE
+#define JINF_STEP_PF_MODE 0
+#endif
 constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
 constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 units in flight)
 constexpr int ATTN_POS_PER_WARP = 32;  // attention positions per warp (one lane each)
@@ -31,6 +36,8 @@ struct StepPhase {
     int kind;
     int dep;                 // -1: no dependency
     unsigned int dep_target;
+    int pf[2];               // GEMV phases (-1: none) whose weights this CTA owns are prefetched
+                             // into L2 when the CTA reaches this phase (before its wait)
     // PH_GEMV
     int xm, epi;
     const uint8_t* w;        // Q4M matrix

@@ -107,6 +107,19 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
     return r;
 }
 
+// Bring the units that CTA `cta` owns in GEMV phase `pi` (one contiguous byte range: whole
+// tile pairs, all groups) into L2. Issued while the CTA would otherwise wait on a dependency,
+// so that HBM keeps streaming weights through attention, input staging and merges.
+__device__ __noinline__ void prefetch_cta_range(const PhaseInfo& pi, int cta, int C) {
+    if (!pi.groups) return;
+    const int t0 = step_cta_tile(cta, C, pi.pairs), t1 = step_cta_tile(cta + 1, C, pi.pairs);
+    if (t0 >= t1) return;
+    const uint8_t* b = pi.w + (size_t)t0 * pi.groups * Q4M_UNIT;
+    const uint32_t bytes = (uint32_t)(t1 - t0) * (uint32_t)pi.groups * (uint32_t)Q4M_UNIT;  // multiple of 16
+    for (uint32_t off = 0; off < bytes; off += (1u << 20))
+        prefetch_l2(b + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
+}
+
 // The weight stream of one warp between calls: ring slot of the next unit to consume and
 // the copy position.
 struct WarpStream {
@@ -366,6 +379,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             flags[ph & 1] = g.dep < 0 ? 1 : (wait_ge(P.done + g.dep, g.dep_target, st, P.spin_limit) ? 1 : 0);
         } else if (tid >= 32 && tid < 32 + DWORDS) {  // descriptor -> shared memory while warp 0 polls
             reinterpret_cast<uint32_t*>(&d)[tid - 32] = reinterpret_cast<const uint32_t*>(P.phases + ph)[tid - 32];
+        } else if (tid == 32 * 9) {  // L2 prefetch of later weights while warp 0 polls
+            for (int k = 0; k < 2; ++k) {
+                const int j = P.phases[ph].pf[k];
+                if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C);
+            }
         }
         __syncthreads();  // also: every warp is done with the previous phase's shared data
         if (!flags[ph & 1]) break;
