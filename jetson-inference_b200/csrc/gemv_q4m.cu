@@ -48,9 +48,8 @@ template <int XM, int EPI>
 __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int G = p.groups;
-    uint16_t* xb = reinterpret_cast<uint16_t*>(smem_raw);                   // [G][32 lanes][8] fp16 B values
-    float* xk = reinterpret_cast<float*>(smem_raw + (size_t)G * 512);      // [4G] accumulator offsets
-    float* misc = xk + 4 * G;                                               // 64 floats
+    uint8_t* rec = smem_raw;                                                     // input digit records
+    float* misc = reinterpret_cast<float*>(smem_raw + xrec_bytes(G));           // 64 floats
     const uint32_t ring0 = smem_u32(misc + 64);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * Q4M_UNIT);
@@ -92,13 +91,13 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     pdl_wait();
     pdl_trigger();
 
-    // ---------------- prologue: x -> block-diagonal fp16 hi/lo B values in shared memory
+    // ---------------- prologue: x -> int8 digit records in shared memory
     const float* hsrc = XM == X_EMBED_NORM ? p.embed + (size_t)p.st->token * p.cols : p.hin;
-    const float inv_alpha = stage_x<GEMV_M_THREADS>(XM, p.x, hsrc, p.yres, p.hout, blockIdx.x == 0, p.norm_w, p.eps,
-                                                     p.cols, smem_raw, xk, misc, false);
+    const float fac = stage_x<GEMV_M_THREADS>(XM, p.x, hsrc, p.yres, p.hout, blockIdx.x == 0, p.norm_w, p.eps, p.cols,
+                                              rec, misc, false);
+    const XRecS xr{smem_u32(rec), smem_u32(rec + (size_t)G * 256)};
 
     // ---------------- main loop
-    const BSel bs(lane);
     const int c = lane & 3;
     EpiArgs ea;
     ea.epi = EPI;
@@ -123,7 +122,7 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
         for (int g = g0; g < g1; ++g) {
             issue(slot == 0 ? GEMV_M_NBUF - 1 : slot - 1);
             asm volatile("cp.async.wait_group %0;" ::"n"(GEMV_M_NBUF - 1) : "memory");
-            unit_mma(ring + slot * Q4M_UNIT, xb, xk, g, lane, bs, acc);
+            unit_mma(ring + slot * Q4M_UNIT, xr, g, lane, acc);
             slot = slot + 1 == GEMV_M_NBUF ? 0 : slot + 1;
         }
         unit_reduce(acc);
@@ -154,7 +153,7 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
                 v1 += __ldcg(pb + q * Q4M_PAIR_ROWS + r0 + 1);
             }
         }
-        if (lane < 16) epilogue_pair(ea, pair * Q4M_PAIR_ROWS + r0, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
+        if (lane < 16) epilogue_pair(ea, pair * Q4M_PAIR_ROWS + r0, v0 * fac, v1 * fac, lmax, lidx);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 
@@ -179,47 +178,53 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
 
 // ---------------------------------------------------------------- repack
 
-// One thread per (tile, group, lane): its 8 nibble words and 2 scales, gathered from the
-// AoS blocks ([rows][nb] blocks of 18 bytes). Rows past `rows` and blocks past nb read as zero.
+// One thread per (pair, group, lane): its 16 nibble words and 2 scale words (q4m.cuh),
+// gathered from the AoS blocks ([rows][nb] blocks of 18 bytes). Rows past `rows` and
+// blocks past nb read as zero.
 __global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
-                             int tiles, int nb) {
+                             int pairs, int nb) {
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (int64_t)tiles * groups * 32) return;
+    if (gid >= (int64_t)pairs * groups * 32) return;
     const int lane = (int)(gid & 31);
-    const int64_t tg = gid >> 5;
-    const int t = (int)(tg / groups), G = (int)(tg % groups);
+    const int64_t pg = gid >> 5;
+    const int p = (int)(pg / groups), G = (int)(pg % groups);
     const int gr = lane >> 2, c = lane & 3;
-    auto block = [&](int r, int j) -> const uint8_t* {
-        const int row = t * Q4M_ROWS + r;
+    auto block = [&](int r, int j) -> const uint8_t* {  // pair row r, block j of the group
+        const int row = p * Q4M_PAIR_ROWS + r;
         return row < rows && G * 4 + j < nb ? aos + ((size_t)row * nb + (size_t)G * 4 + j) * 18 : nullptr;
     };
-    uint8_t* chunk = dst + q4m_chunk_offset(t, G, groups);
-    for (int i = 0; i < 8; ++i) {
-        const int e = 4 * i + c;
-        uint32_t word = 0;
-        for (int half = 0; half < 2; ++half)
-            for (int j = 0; j < 4; ++j) {
-                const int r = gr + 8 * half;
-                const uint8_t* blk = block(r, j);
-                if (!blk) continue;
-                const uint8_t byte = blk[2 + (e >> 1)];
-                const uint32_t q = (e & 1) ? (byte >> 4) : (byte & 15);
-                word |= q << q4m_nibble_bit(r, j);
+    auto nib = [](const uint8_t* blk, int k) -> uint32_t {  // element k: byte k/2, low nibble if k even
+        if (!blk) return 0u;
+        const uint8_t byte = blk[2 + (k >> 1)];
+        return (k & 1) ? (uint32_t)(byte >> 4) : (uint32_t)(byte & 15);
+    };
+    uint8_t* unit = dst + q4m_unit_offset(p, G, groups);
+    for (int j = 0; j < 4; ++j)
+        for (int i = 0; i < 4; ++i) {
+            const int rt = gr + 8 * (i & 1);
+            const uint8_t* a = block(rt, j);
+            const uint8_t* b = block(16 + rt, j);
+            uint32_t word = 0;
+            for (int t = 0; t < 4; ++t) {
+                const int k = 16 * (i >> 1) + 4 * c + t;
+                word |= (nib(a, k) | (nib(b, k) << 4)) << (8 * t);
             }
-        *reinterpret_cast<uint32_t*>(chunk + (i >> 2) * 512 + lane * 16 + (i & 3) * 4) = word;
+            *reinterpret_cast<uint32_t*>(unit + 512 * j + 16 * lane + 4 * i) = word;
+        }
+    for (int t = 0; t < 2; ++t) {
+        const uint8_t* b0 = block(16 * t + gr, c);
+        const uint8_t* b1 = block(16 * t + gr + 8, c);
+        const uint32_t d0 = b0 ? (uint32_t)b0[0] | ((uint32_t)b0[1] << 8) : 0u;
+        const uint32_t d1 = b1 ? (uint32_t)b1[0] | ((uint32_t)b1[1] << 8) : 0u;
+        *reinterpret_cast<uint32_t*>(unit + Q4M_SCALES + 128 * t + 4 * lane) = d0 | (d1 << 16);
     }
-    const uint8_t* b0 = block(gr, c);
-    const uint8_t* b1 = block(gr + 8, c);
-    const uint32_t d0 = b0 ? (uint32_t)b0[0] | ((uint32_t)b0[1] << 8) : 0u;
-    const uint32_t d1 = b1 ? (uint32_t)b1[0] | ((uint32_t)b1[1] << 8) : 0u;
-    *reinterpret_cast<uint32_t*>(chunk + 1024 + lane * 4) = d0 | (d1 << 16);
 }
 
 // ---------------------------------------------------------------- host side
 
 size_t gemvm_smem_bytes(int cols) {
     const int G = (cols + Q4M_KG - 1) / Q4M_KG;
-    return (size_t)G * 512 + sizeof(float) * ((size_t)G * 4 + 64) + (size_t)NW * GEMV_M_NBUF * Q4M_UNIT;
+    return xrec_bytes(G) + sizeof(float) * 64 + (size_t)NW * GEMV_M_NBUF * Q4M_UNIT;
 }
 
 int gemvm_max_cols() {
@@ -328,9 +333,9 @@ cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStr
 }
 
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s) {
-    const int64_t n = (int64_t)sh.tiles * sh.groups * 32;
+    const int64_t n = (int64_t)sh.pairs * sh.groups * 32;
     k_repack_q4m<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows, sh.groups,
-                                                             sh.tiles, sh.cols / 32);
+                                                             sh.pairs, sh.cols / 32);
     return cudaGetLastError();
 }
 

@@ -17,7 +17,7 @@ namespace jinf {
 // L2 prefetch schedule of the persistent step (engine.cu, build_step): 0 none; 1 o and
 // gate|up during attention; 2 also down during gate|up; 3 also the next layer's QKV during down.
 #ifndef JINF_STEP_PF_MODE
-#define JINF_STEP_PF_MODE 0
+#define JINF_STEP_PF_MODE 1
 #endif
 constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
 constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 units in flight)

@@ -135,9 +135,8 @@ struct PieceSum {
 // refilling it as it goes. Out of line so that the hot loop gets a register allocation of
 // its own, independent of the rest of the step kernel.
 __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, const PhaseInfo* pinfo, int n_phases,
-                                              int C, const uint16_t* xb, const float* xk, int gb, int ge) {
+                                              int C, const XRecS xr, int gb, int ge) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const BSel bs(lane);
     StreamPos sp = ws.sp;
     int slot = ws.slot;
     PieceSum r{{0.f, 0.f, 0.f, 0.f}};
@@ -149,7 +148,7 @@ __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, con
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
         asm volatile("cp.async.wait_group %0;" ::"n"(STEP_NBUF - 1) : "memory");
-        unit_mma(ring + slot * Q4M_UNIT, xb, xk, g, lane, bs, r.acc);
+        unit_mma(ring + slot * Q4M_UNIT, xr, g, lane, r.acc);
         slot = slot + 1 == STEP_NBUF ? 0 : slot + 1;
     }
     ws.sp = sp;
@@ -367,7 +366,6 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     }
 
     const int c4 = lane & 3;
-    const uint16_t* xb = reinterpret_cast<const uint16_t*>(xbase);
     float lmax = -INFINITY;
     int lidx = 0;
     constexpr int DWORDS = (int)(sizeof(StepPhase) / 4);
@@ -487,11 +485,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         const int G = d.groups;
         const int t0 = step_cta_tile(blockIdx.x, C, d.pairs), t1 = step_cta_tile(blockIdx.x + 1, C, d.pairs);
         if (t0 >= t1) continue;
-        float* xk = reinterpret_cast<float*>(xbase + (size_t)G * 512);
         const float* hsrc = d.xm == X_EMBED_NORM ? d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols : d.hsrc;
         // the CTA that owns pair 0 stores the embedding row as the residual stream
-        const float inv_alpha = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps,
-                                                      d.cols, xbase, xk, misc, true);
+        const float fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps, d.cols,
+                                                xbase, misc, true);
+        const XRecS xr{smem_u32(xbase), smem_u32(xbase + (size_t)G * 256)};
         // epilogue arguments are read from the shared descriptor when a tile finishes
         auto epilogue = [&](int row, float v0, float v1) {
             EpiArgs ea;
@@ -507,7 +505,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             ea.pos = pos;
             ea.rope_base = P.rope_base;
             ea.coherent = true;
-            epilogue_pair(ea, row, v0 * inv_alpha, v1 * inv_alpha, lmax, lidx);
+            epilogue_pair(ea, row, v0 * fac, v1 * fac, lmax, lidx);
         };
         int c, c1;
         warp_range(blockIdx.x, C, warp, d.pairs, G, c, c1);
@@ -520,7 +518,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         int pair = c / G, gb = c - pair * G;  // walked incrementally: no division per piece
         for (; c < c1; ++pair, gb = 0) {
             const int ge = c1 - c < G - gb ? gb + (c1 - c) : G;
-            PieceSum ps = stream_piece(ws, ring, pinfo, P.n_phases, C, xb, xk, gb, ge);
+            PieceSum ps = stream_piece(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
             c += ge - gb;
             if (first_piece && lane == 0) {
                 ftile[warp] = pair;
@@ -604,7 +602,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 
 unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
     const size_t G = (size_t)(max_cols + Q4M_KG - 1) / Q4M_KG;
-    const size_t gemv = G * 512 + G * 4 * sizeof(float);
+    const size_t gemv = xrec_bytes((int)G);
     const size_t attn = (size_t)group * head_dim * sizeof(float) + (size_t)NW * group * (head_dim + 2) * sizeof(float);
     const size_t b = gemv > attn ? gemv : attn;
     return (unsigned int)((b + 15) & ~(size_t)15);

@@ -1,6 +1,8 @@
 """The tensor-core Q4M GEMV (jinf_b200_q4m_* / jinf_b200_gemv_q4m*) on the GPU: the device
-repack against the numpy statement of the layout (bit-exact), and the GEMV against the CPU
-oracle (reference cuda/matmul_kernels.cu:8-43) within 1e-3 relative, for every K split."""
+repack against the numpy statement of the layout (bit-exact), the GEMV against the CPU
+oracle (reference cuda/matmul_kernels.cu:8-43) within 1e-3 relative, for every K split, and
+against the numpy statement of its own arithmetic (int8 digit records) within fp32
+summation-order noise."""
 import numpy as np
 import pytest
 import torch
@@ -35,6 +37,21 @@ def test_q4m_pack_matches_layout(cuda, rows, cols):
     w = q4_0_rows(rows, cols, seed=rows)
     got = packed(w, rows, cols, cuda).cpu().numpy()
     assert np.array_equal(got, q4m_ref.pack(w, rows, cols))
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 1024), (96, 704), (4096, 4096), (512, 14336)])
+def test_gemv_q4m_follows_documented_arithmetic(cuda, rows, cols):
+    from jinf import kernels as K
+    w = q4_0_rows(rows, cols, seed=rows + cols)
+    rng = np.random.default_rng(rows)
+    x = (rng.standard_normal(cols) * np.repeat(10.0 ** rng.integers(-3, 3, size=cols // 32), 32)).astype(np.float32)
+    x[:32] = 0.0                                   # an all-zero block: zero records
+    q = packed(w, rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    K.gemv_q4m(q, torch.from_numpy(x).to(cuda), y, rows, cols, workspace=workspace(rows, cols, cuda), kw=1)
+    torch.cuda.synchronize()
+    want = q4m_ref.emulate_gemv(q4m_ref.pack(w, rows, cols), x, rows, cols)
+    assert rel_err(y.cpu().numpy(), want) < 1e-5
 
 
 @pytest.mark.parametrize("rows,cols", SHAPES)

@@ -1,7 +1,8 @@
 """The Q4M layout and the tensor-core GEMV arithmetic, checked on the CPU: the numpy packer
-is lossless, and the kernel's derivation (exact fp16 decode 1024 + s*q, x as fp16 hi + lo
-with a power-of-two pre-scale, block-diagonal B, accumulator offset -(1024 + 8s) * sum(B))
-reproduces the oracle's matvec (reference cuda/matmul_kernels.cu:8-43) within 1e-3."""
+is lossless, and the kernel's derivation (u8 weights, x as two int8 digits per element with
+a per-block scale, exact integer block sums with the zero point removed through the
+accumulator's start value) reproduces the oracle's matvec (reference
+cuda/matmul_kernels.cu:8-43) within 1e-3."""
 import ctypes as C
 
 import numpy as np
@@ -35,34 +36,37 @@ def test_q4m_bytes_formula():
 
 
 def test_nibble_positions_are_a_permutation():
-    bits = sorted(q4m_ref.nibble_bit(r, j) for r in (0, 8) for j in range(4))
-    assert bits == list(range(0, 32, 4))
+    off = q4m_ref._layout()[:16].reshape(-1)   # tile A rows; tile B shares the bytes (high nibbles)
+    assert np.array_equal(np.sort(off), np.arange(2048))
 
 
-@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (100, 1408), (24, 704), (16, 96)])
+@pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (100, 1408), (24, 704), (16, 96), (64, 256)])
 def test_pack_is_lossless(rows, cols):
     w = q4_0_rows(rows, cols, seed=rows)
     img = q4m_ref.pack(w, rows, cols)
-    tiles, groups = 2 * ((rows + 31) // 32), (cols + 127) // 128
-    assert img.size == tiles * groups * 1152
-    words, sc = q4m_ref.unpack_words(img, tiles, groups)
-    # every nibble exactly once: rebuild the AoS qs bytes from the words
+    pairs, groups = (rows + 31) // 32, (cols + 127) // 128
+    assert img.size == pairs * groups * 2304
+    q, d = q4m_ref.unpack(img, rows, cols)
     blocks = w.reshape(rows, cols // 32, 18)
-    got = np.zeros((tiles * 16, groups * 4, 32), dtype=np.uint8)
-    for lane in range(32):
-        gr, c = lane >> 2, lane & 3
-        for i in range(8):
-            for half in range(2):
-                r = gr + 8 * half
-                for j in range(4):
-                    q = (words[:, :, lane, i] >> q4m_ref.nibble_bit(r, j)) & 15
-                    rows_idx = np.arange(tiles) * 16 + r
-                    got[rows_idx[:, None], np.arange(groups)[None, :] * 4 + j, 4 * i + c] = q
     want = np.empty((rows, cols // 32, 32), dtype=np.uint8)
     want[:, :, 0::2] = blocks[:, :, 2:] & 15
     want[:, :, 1::2] = blocks[:, :, 2:] >> 4
-    assert np.array_equal(got[:rows, :cols // 32], want)
-    assert not got[rows:].any() and not got[:, cols // 32:].any()
+    assert np.array_equal(q[:, :cols // 32], want)
+    assert np.array_equal(d[:, :cols // 32], blocks[:, :, 0].astype(np.uint16) | (blocks[:, :, 1].astype(np.uint16) << 8))
+    assert not q[:, cols // 32:].any() and not d[:, cols // 32:].any()
+    # rows past `rows` are zero in the image: repacking with them dropped changes nothing
+    full = q4m_ref.pack(np.concatenate([w, np.zeros((pairs * 32 - rows, w.shape[1]), np.uint8)]), pairs * 32, cols)
+    assert np.array_equal(full, img)
+
+
+def test_digit_records_round_trip():
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal(384) * np.repeat(10.0 ** rng.integers(-6, 6, size=12), 32)).astype(np.float32)
+    x[64:96] = 0.0                              # an all-zero block
+    hi, lo, inv_alpha = q4m_ref.x_records(x, 384)
+    back = ((256 * hi + lo) * inv_alpha[:, None]).reshape(-1)
+    amax = np.repeat(np.max(np.abs(x.reshape(-1, 32)), axis=1), 32)
+    assert np.all(np.abs(back - x) <= amax * 2.0 ** -15)
 
 
 @pytest.mark.parametrize("rows,cols", [(16, 128), (37, 384), (64, 1024), (100, 1408), (48, 704), (16, 96)])
@@ -83,5 +87,6 @@ def test_emulated_gemv_extreme_scales_and_inputs():
     w = w.reshape(rows, -1)
     for scale in (1e-6, 1.0, 1e5):
         x = (rng.standard_normal(cols) * scale).astype(np.float32)
+        x[128:160] = 0.0
         y = q4m_ref.emulate_gemv(q4m_ref.pack(w, rows, cols), x, rows, cols)
         assert rel_err(y, oracle.matvec(w, 2, x, rows, cols)) < REL
