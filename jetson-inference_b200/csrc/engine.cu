@@ -294,6 +294,10 @@ struct jinf_engine_impl {
     StepPhase* d_phases = nullptr;  // [n_full + n_body]
     unsigned int* step_done = nullptr;
     float* step_attn_part = nullptr;
+    // input records of the GEMV phases (inputs of o, gate|up, down, qkv / LM head), written by
+    // the producing phase, and the per-pair sums of h^2 behind the RMSNorm inputs
+    uint8_t* step_rec[4] = {nullptr, nullptr, nullptr, nullptr};
+    float* step_ss = nullptr;
     StepParams sp_full{}, sp_body{};
     // ops and graphs
     std::vector<Op> ops_full, ops_body;
@@ -527,6 +531,7 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         p.cols = sh.cols;
         p.pairs = sh.pairs;
         p.groups = sh.groups;
+        p.gran = 1;
         ph.push_back(p);
         return ph.back();
     };
@@ -534,6 +539,11 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         const auto& ly = I->layers[L];
         __half* kc = I->kc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
         __half* vc = I->vc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        // The attention output and the activation arrive as records from their producing
+        // phase (attention -> o: rec 0, gate|up -> down: rec 2). The RMSNorm inputs are staged
+        // by every CTA from h (records of h * gain would cost the o and down epilogues an
+        // extra dependent round trip each, more than they save; step_rec[1], [3] and
+        // step_ss stay available for that form).
         StepPhase& qkv = add_gemv(ly.qkv, ly.qkv_sh, L == 0 ? X_EMBED_NORM : X_RMSNORM, EPI_QKV);
         qkv.hsrc = L == 0 ? I->embed : I->hA;
         qkv.hout = L == 0 ? I->hA : nullptr;
@@ -547,16 +557,20 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         at.out = I->attn;
         at.kcache = kc;
         at.vcache = vc;
+        at.rec_out = I->step_rec[0];
+        at.groups_out = ly.o_sh.groups;
         ph.push_back(at);
-        StepPhase& o = add_gemv(ly.o, ly.o_sh, X_PLAIN_F32, EPI_RESID);
-        o.x = I->attn;
+        StepPhase& o = add_gemv(ly.o, ly.o_sh, X_RECORDS, EPI_RESID);
+        o.rec = I->step_rec[0];
         o.y = I->hA;
         StepPhase& gu = add_gemv(ly.gu, ly.gu_sh, X_RMSNORM, EPI_GATEUP);
         gu.hsrc = I->hA;
         gu.norm_w = ly.ffn_norm;
-        gu.y = I->act;
-        StepPhase& dn = add_gemv(ly.down, ly.down_sh, X_PLAIN_F32, EPI_RESID);
-        dn.x = I->act;
+        gu.gran = 2;
+        gu.rec_out = I->step_rec[2];
+        gu.groups_out = ly.down_sh.groups;
+        StepPhase& dn = add_gemv(ly.down, ly.down_sh, X_RECORDS, EPI_RESID);
+        dn.rec = I->step_rec[2];
         dn.y = I->hA;
     }
     if (with_head) {
@@ -584,7 +598,7 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
             }
         } else if (ph[i].epi == EPI_GATEUP) {
             if (JINF_STEP_PF_MODE >= 2 && gemv_next) ph[i].pf[0] = i + 1;  // down
-        } else if (ph[i].epi == EPI_RESID && ph[i].xm == X_PLAIN_F32 && i > 0 && ph[i - 1].epi == EPI_GATEUP) {
+        } else if (ph[i].epi == EPI_RESID && i > 0 && ph[i - 1].epi == EPI_GATEUP) {
             if (JINF_STEP_PF_MODE >= 3 && gemv_next && ph[i + 1].epi == EPI_QKV) ph[i].pf[0] = i + 1;  // next qkv
         }
     }
@@ -600,13 +614,30 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
         for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) max_cols = std::max(max_cols, sh->cols);
     const unsigned xs = step_xstage_bytes(max_cols, G, I->hd);
     const size_t smem = step_smem_bytes(xs, 5 * I->L + 1);
-    if (G > ATTN_MAX_GROUP || I->Hkvl > 64 || I->max_ctx > ATTN_POS_PER_CTA * ATTN_MAX_SPLIT || smem > 227 * 1024 ||
-        step_occupancy(smem) < 1) {
+    // input records: a tile pair of h is one 32-element block, a CTA's gate|up rows are whole
+    // activation blocks and fit the 1024-float conversion buffer, as do a kv head's outputs
+    const int gu_pairs = I->layers.empty() ? 0 : I->layers[0].gu_sh.pairs;
+    const int gu_per_cta = 2 * ((gu_pairs / 2 + I->num_sms - 1) / I->num_sms);
+    const bool records_ok = I->d % 32 == 0 && (I->Hl * I->hd) % 32 == 0 && gu_pairs % 2 == 0 &&
+                            gu_per_cta * 16 <= 1024 && G * I->hd <= 1024;
+    if (G > ATTN_MAX_GROUP || I->Hkvl > 64 || (I->hd != 64 && I->hd != 128) || smem > 227 * 1024 ||
+        step_occupancy(smem) < 1 || !records_ok) {
         JINF_LOG("persistent step unavailable for this shape (%zu bytes of shared memory); using one kernel per "
                  "operation", smem);
         return JINF_OK;
     }
     I->step_grid = I->num_sms;
+    {
+        const auto& ly = I->layers[0];
+        const int rec_groups[4] = {ly.o_sh.groups, ly.gu_sh.groups, ly.down_sh.groups,
+                                   std::max(ly.qkv_sh.groups, I->lm_sh.groups)};
+        for (int i = 0; i < 4; ++i) {
+            // zero once: padding blocks past the real columns are never written and stay zero
+            JINF_CUDA_CHECK(cudaMalloc(&I->step_rec[i], xrec_bytes(rec_groups[i])));
+            JINF_CUDA_CHECK(cudaMemset(I->step_rec[i], 0, xrec_bytes(rec_groups[i])));
+        }
+        JINF_CUDA_CHECK(cudaMalloc(&I->step_ss, sizeof(float) * (size_t)(I->d / 32)));
+    }
     std::vector<StepPhase> full, body;
     build_step(I, true, full);
     build_step(I, false, body);
@@ -630,6 +661,7 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     sp.n_kv_heads = I->Hkvl;
     sp.rope_base = I->rope_base;
     sp.eps = I->eps;
+    sp.attn_smax = std::max(1, std::min(ATTN_MAX_SPLIT, I->num_sms / I->Hkvl));
     sp.xstage_bytes = xs;
     sp.spin_limit = 4000000ull;  // about a second of polling: far beyond any phase, never a hang
     I->sp_full = sp;
@@ -781,7 +813,8 @@ void free_impl(jinf_engine_impl* I) {
     }
     void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
                     I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
-                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part};
+                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_rec[0], I->step_rec[1],
+                    I->step_rec[2], I->step_rec[3], I->step_ss};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);

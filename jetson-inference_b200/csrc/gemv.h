@@ -18,7 +18,9 @@ namespace jinf {
 constexpr int GEMV_M_THREADS = 512;
 constexpr int GEMV_M_NBUF = JINF_GEMV_M_NBUF;
 
-enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3 };
+// X_RECORDS (persistent step only): the input is already staged as digit records in global
+// memory by the phase that produced it (q4m_device.cuh, xrec_bytes).
+enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3, X_RECORDS = 4 };
 enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3, EPI_RESID = 4 };
 
 struct GemvParams {

@@ -44,6 +44,12 @@ struct Q4MShape {
     uint64_t bytes;
 };
 
+// Input records of one GEMV (the x operand, q4m_device.cuh): digits [G][32 lanes][2 words]
+// (256 bytes per group: lane 4 gr + c holds digit gr & 1 of block gr >> 1, word r = elements
+// 16 r + 4c .. +3), then params [G][4 blocks] {-8 sum(hi), -8 sum(lo) (int bits), 1/alpha,
+// 1/(16 alpha)}.
+__host__ __device__ inline size_t xrec_bytes(int groups) { return (size_t)groups * 320; }
+
 // Byte offset of the unit of pair p, group g.
 __host__ __device__ inline uint64_t q4m_unit_offset(int p, int g, int groups) {
     return ((uint64_t)p * groups + g) * Q4M_UNIT;

@@ -32,11 +32,6 @@ typedef unsigned long long u64;
 
 constexpr float XREC_DIGIT_MAX = 32639.0f;  // |x| alpha <= 32639 keeps hi = (v + 128) >> 8 in int8
 
-// Input records of one GEMV: digits [G][32 lanes][2 words] (256 bytes per group: lane
-// 4 gr + c holds digit gr & 1 of block gr >> 1, word r = elements 16 r + 4c .. +3), then
-// params [G][4 blocks] {-8 sum(hi), -8 sum(lo) (int bits), 1/alpha, 1/(16 alpha)}.
-__host__ __device__ inline size_t xrec_bytes(int groups) { return (size_t)groups * 320; }
-
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // This lane's share of a 2304-byte unit: its nibble words of the four blocks and its two
@@ -151,8 +146,10 @@ __device__ __forceinline__ float4 ld_f4(const float* p, int i, bool coherent) {
 // Digit records of one 32-element block held by an octet of lanes (lane q = lane & 7 of the
 // octet holds elements 4q .. 4q+3 in v): `dig` is the group's 64 record words and `prm` its
 // 4 block params (shared or global memory), j the block within the group. All 32 lanes of
-// the warp call it (the octet reductions shuffle); a block of zeros gives zero records.
-__device__ __forceinline__ void octet_to_records(float4 v, int lane, int j, uint32_t* dig, float4* prm) {
+// the warp call it (the octet reductions shuffle); only octets with `store` write. A block
+// of zeros gives zero records.
+__device__ __forceinline__ void octet_to_records(float4 v, int lane, int j, uint32_t* dig, float4* prm,
+                                                 bool store = true) {
     const int q = lane & 7;
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     amax = fmaxf(amax, __shfl_xor_sync(JINF_FULL_MASK, amax, 1));
@@ -178,6 +175,7 @@ __device__ __forceinline__ void octet_to_records(float4 v, int lane, int j, uint
     }
     // elements k = 4q .. 4q+3: word r = q >> 2 of record lanes 4 (2j + h) + (q & 3)
     const int r = q >> 2, c = q & 3;
+    if (!store) return;
     dig[(8 * j + c) * 2 + r] = H;
     dig[(8 * j + 4 + c) * 2 + r] = L;
     if (q == 0) {

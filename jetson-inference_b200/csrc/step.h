@@ -21,10 +21,10 @@ namespace jinf {
 #endif
 constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
 constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 units in flight)
-constexpr int ATTN_POS_PER_WARP = 32;  // attention positions per warp (one lane each)
-constexpr int ATTN_POS_PER_CTA = 512;  // attention positions per CTA: 16 warps x 32
+constexpr int ATTN_CHUNK = 32;         // attention cache rows staged in shared memory at a time
+constexpr int ATTN_MIN_POS = 16;       // positions per CTA below which fewer CTAs split a kv head
 
-constexpr int ATTN_MAX_SPLIT = 64;     // CTAs per kv head (contexts up to 32768 positions)
+constexpr int ATTN_MAX_SPLIT = 64;     // CTAs per kv head
 constexpr int ATTN_MAX_GROUP = 8;      // query heads per kv head
 
 enum PhaseKind { PH_GEMV = 0, PH_ATTN = 1 };
@@ -36,6 +36,8 @@ struct StepPhase {
     int kind;
     int dep;                 // -1: no dependency
     unsigned int dep_target;
+    int gran;                // a CTA owns whole runs of `gran` tile pairs (2: its gate|up rows
+                             // make whole 32-element blocks of the activation)
     int pf[2];               // GEMV phases (-1: none) whose weights this CTA owns are prefetched
                              // into L2 when the CTA reaches this phase (before its wait)
     // PH_GEMV
@@ -49,6 +51,18 @@ struct StepPhase {
     float* y;                // epilogue output; EPI_RESID: the residual stream (h += W x)
     __half* kcache;          // EPI_QKV and PH_ATTN: this layer's cache [Hkv][max_ctx][hd]
     __half* vcache;
+    // X_RECORDS input: the digit records written by the producing phase and, for an RMSNorm
+    // input, the producer's per-pair sums of h^2 (n_ss of them) that give the norm factor
+    const uint8_t* rec;
+    const float* ssp;
+    int n_ss;
+    // records this phase writes for the next GEMV phase (null: none), that phase's group
+    // count, and for EPI_RESID the per-pair sums of h^2 and the next RMSNorm gain (the
+    // records then hold h * gain)
+    int groups_out;
+    uint8_t* rec_out;
+    float* ss_out;
+    const float* gain_out;
     // PH_ATTN
     const float* q;          // [n_heads * hd], RoPE applied
     float* out;              // [n_heads * hd]
@@ -62,6 +76,7 @@ struct StepParams {
     DeviceState* st;
     int nq, nk, head_dim, max_ctx, n_heads, n_kv_heads;
     float rope_base, eps;
+    int attn_smax;            // CTAs per kv head at most (grid / kv heads, <= ATTN_MAX_SPLIT)
     int with_argmax;          // the last phase is the LM head: finish the argmax, feed it back
     unsigned int xstage_bytes;  // shared bytes for the staged GEMV input / attention scratch
     unsigned long long spin_limit;  // polls before a dependency wait gives up (DEV_ERR_TIMEOUT)

@@ -62,16 +62,68 @@ __device__ bool wait_ge(const unsigned* c, unsigned target, DeviceState* st, uns
     }
 }
 
+// ---------------------------------------------------------------- bulk copies
+//
+// Inputs staged once per phase (records, attention cache rows) come in by TMA bulk copy
+// (cp.async.bulk, global -> shared) completing on an mbarrier, so waiting for them never
+// waits on the weight rings' per-thread cp.async groups (which by then hold the next phase's
+// first units).
+__device__ __forceinline__ void mbar_init(uint32_t mbar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mbar) : "memory");
+}
+__device__ __forceinline__ void bulk_expect(uint32_t mbar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
+}
+// 16-byte aligned addresses, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(mbar)
+                 : "memory");
+}
+// Orders this thread's (and, after a barrier, its CTA's) generic-proxy accesses before its
+// following bulk copies: the copied data was written through the generic proxy, and the
+// shared destination was last read through it.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+// Wait for phase `parity` of the mbarrier; gives up after `limit` polls (DEV_ERR_TIMEOUT).
+__device__ __noinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, DeviceState* st, unsigned long long limit) {
+    for (unsigned long long it = 0;; ++it) {
+        uint32_t ok;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(ok)
+            : "r"(mbar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (it >= limit) {
+            atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(32);
+    }
+}
+
 // Stream geometry of one phase, kept in shared memory (groups == 0: no weights).
 struct PhaseInfo {
     const uint8_t* w;
-    int pairs, groups;
+    int pairs, groups, gran;
 };
+
+// Tile pairs [t0, t1) of CTA `cta` (of C): balanced runs of `gran` pairs (T % gran == 0).
+__device__ __forceinline__ void cta_range(int cta, int C, int T, int gran, int& t0, int& t1) {
+    if (gran == 2) {
+        t0 = 2 * step_cta_tile(cta, C, T >> 1);
+        t1 = 2 * step_cta_tile(cta + 1, C, T >> 1);
+    } else {
+        t0 = step_cta_tile(cta, C, T);
+        t1 = step_cta_tile(cta + 1, C, T);
+    }
+}
 
 // Unit range [c0, c1) of warp `warp` of CTA `cta` (of C) in a pairs x groups matrix
 // (32-bit: a matrix has far fewer than 2^31 units).
-__device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int G, int& c0, int& c1) {
-    const int t0 = step_cta_tile(cta, C, T), t1 = step_cta_tile(cta + 1, C, T);
+__device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int gran, int G, int& c0, int& c1) {
+    int t0, t1;
+    cta_range(cta, C, T, gran, t0, t1);
     const int n = (t1 - t0) * G;
     c0 = t0 * G + ((warp * n) >> 4);
     c1 = t0 * G + (((warp + 1) * n) >> 4);
@@ -91,7 +143,7 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
         const int G = pinfo[i].groups;
         if (!G) continue;
         int c0, c1;
-        warp_range(cta, C, warp, pinfo[i].pairs, G, c0, c1);
+        warp_range(cta, C, warp, pinfo[i].pairs, pinfo[i].gran, G, c0, c1);
         if (c0 < c1) {
             r.w = pinfo[i].w;
             r.ph = i;
@@ -112,7 +164,8 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
 // so that HBM keeps streaming weights through attention, input staging and merges.
 __device__ __noinline__ void prefetch_cta_range(const PhaseInfo& pi, int cta, int C) {
     if (!pi.groups) return;
-    const int t0 = step_cta_tile(cta, C, pi.pairs), t1 = step_cta_tile(cta + 1, C, pi.pairs);
+    int t0, t1;
+    cta_range(cta, C, pi.pairs, pi.gran, t0, t1);
     if (t0 >= t1) return;
     const uint8_t* b = pi.w + (size_t)t0 * pi.groups * Q4M_UNIT;
     const uint32_t bytes = (uint32_t)(t1 - t0) * (uint32_t)pi.groups * (uint32_t)Q4M_UNIT;  // multiple of 16
@@ -156,168 +209,239 @@ __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, con
     return r;
 }
 
-__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
-    const __half2* h = reinterpret_cast<const __half2*>(&v);
+// ---------------------------------------------------------------- input records
+//
+// A GEMV phase whose input was produced earlier in the step receives it as digit records
+// (q4m_device.cuh) written by the producing phase's epilogue, so its CTAs only copy them
+// (one L2 round trip) instead of each converting the whole input. For an RMSNorm input the
+// records hold h * gain and the producer also leaves the sum of h^2 of every tile pair;
+// every warp adds those up in the same fixed order (deterministic) for the norm factor.
+
+// Copy the records (xrec_bytes(G)) into shared memory with one bulk copy on `mbar` (phase
+// `parity`); returns the epilogue factor (1 / sqrt(mean(h^2) + eps) for a norm input, else
+// 1). Every thread returns once the records are in shared memory.
+__device__ __noinline__ float stage_records(const uint8_t* rec, const float* ssp, int n_ss, int cols, float eps,
+                                           int G, uint8_t* xbase, uint32_t mbar, uint32_t parity, DeviceState* st,
+                                           unsigned long long limit) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid == 0) {
+        fence_proxy_async();
+        bulk_expect(mbar, (uint32_t)xrec_bytes(G));
+        bulk_g2s(smem_u32(xbase), rec, (uint32_t)xrec_bytes(G), mbar);
+    }
+    float s = 0.f;
+    if (ssp)
+        for (int i = lane; i < n_ss; i += 32) s += __ldcg(ssp + i);
+    float fac = 1.0f;
+    if (ssp) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 t = __half22float2(h[i]);
-        f[2 * i] = t.x;
-        f[2 * i + 1] = t.y;
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(JINF_FULL_MASK, s, o);
+        fac = rsqrtf(s / (float)cols + eps);
+    }
+    mbar_wait(mbar, parity, st, limit);
+    return fac;
+}
+
+// EPI_RESID of one tile pair with records for the next phase, by a whole warp: lanes q < 16
+// hold rows 2q, 2q+1 (v0, v1, already scaled). h += W x is stored; the pair's sum of h^2 and
+// the records of h * gain (the pair is one 32-element block of the next input) are written.
+__device__ __noinline__ void resid_records(const StepPhase& d, int pr, float v0, float v1) {
+    const int lane = threadIdx.x & 31, q = lane & 15, row = pr * Q4M_PAIR_ROWS + 2 * q;
+    float h0 = 0.f, h1 = 0.f;
+    if (lane < 16 && row < d.rows) {
+        h0 = __ldcg(d.y + row) + v0;
+        d.y[row] = h0;
+        if (row + 1 < d.rows) {
+            h1 = __ldcg(d.y + row + 1) + v1;
+            d.y[row + 1] = h1;
+        }
+    }
+    float s = fmaf(h0, h0, h1 * h1);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) s += __shfl_xor_sync(JINF_FULL_MASK, s, o);
+    if (lane == 0) d.ss_out[pr] = s;
+    // octet layout: lane L < 8 takes elements 4L .. 4L+3 (rows of lanes 2L and 2L+1)
+    const int src = 2 * (lane & 7);
+    const float e0 = __shfl_sync(JINF_FULL_MASK, h0, src), e1 = __shfl_sync(JINF_FULL_MASK, h1, src);
+    const float e2 = __shfl_sync(JINF_FULL_MASK, h0, src + 1), e3 = __shfl_sync(JINF_FULL_MASK, h1, src + 1);
+    float4 gn = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lane < 8 && pr * Q4M_PAIR_ROWS + 4 * lane < d.rows)
+        gn = reinterpret_cast<const float4*>(d.gain_out + pr * Q4M_PAIR_ROWS)[lane];
+    uint32_t* dig = reinterpret_cast<uint32_t*>(d.rec_out);
+    float4* prm = reinterpret_cast<float4*>(d.rec_out + (size_t)d.groups_out * 256);
+    octet_to_records(make_float4(e0 * gn.x, e1 * gn.y, e2 * gn.z, e3 * gn.w), lane, pr & 3, dig + (pr >> 2) * 64,
+                     prm + (pr >> 2) * 4, lane < 8);
+}
+
+// Records of blocks [b0, b0 + nb) of the next input from fp32 values in shared memory
+// (vals[32 * i] = first element of block b0 + i), by the whole CTA (4 blocks per warp pass).
+__device__ __noinline__ void blocks_to_records(const float* vals, int b0, int nb, int groups_out, uint8_t* rec_out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t* dig = reinterpret_cast<uint32_t*>(rec_out);
+    float4* prm = reinterpret_cast<float4*>(rec_out + (size_t)groups_out * 256);
+    for (int i0 = warp * 4; i0 < nb; i0 += NW * 4) {
+        const int i = i0 + (lane >> 3);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < nb) v = reinterpret_cast<const float4*>(vals + 32 * i)[lane & 7];
+        const int blk = b0 + i;
+        octet_to_records(v, lane, blk & 3, dig + (blk >> 2) * 64, prm + (blk >> 2) * 4, i < nb);
     }
 }
 
-template <int DPL>
-__device__ __forceinline__ void load_vrow(const __half* vrow, int lane, bool ok, float (&v)[DPL]) {
-    if constexpr (DPL == 4) {
-        const uint2 raw = ok ? __ldcg(reinterpret_cast<const uint2*>(vrow) + lane) : make_uint2(0u, 0u);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-        v[0] = a.x;
-        v[1] = a.y;
-        v[2] = b.x;
-        v[3] = b.y;
-    } else {
-        const unsigned raw = ok ? __ldcg(reinterpret_cast<const unsigned*>(vrow) + lane) : 0u;
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw));
-        v[0] = a.x;
-        v[1] = a.y;
-    }
+// ---------------------------------------------------------------- attention
+//
+// Decode attention over the fp16 cache (math of reference cuda/attention_kernel.cu:45-98:
+// scores q.k / sqrt(hd), GQA head map h -> h / (H/Hkv), max-subtracted softmax, P.V). The
+// positions of a kv head are split over S CTAs (S grows with the context up to the CTAs
+// available per kv head), each walking its positions in chunks of ATTN_CHUNK rows staged in
+// shared memory, with an online softmax across chunks; the splits are merged in a fixed
+// order by the last CTA of the kv head to finish. The rows before `pos` of a CTA's first
+// chunk are requested before the CTA waits for the QKV phase (they were written by earlier
+// tokens), so after the wait only q and the new position's row are still in flight.
+
+struct AttnGeom {
+    int kvh, sp, S, p0, p1;
+};
+
+// Split of CTA `cta` for a context of pos + 1 positions (false: no attention work).
+__device__ __forceinline__ bool attn_geom(int pos, int n_kv_heads, int s_max, int cta, AttnGeom& a) {
+    const int n_pos = pos + 1;
+    int S = (n_pos + ATTN_MIN_POS - 1) / ATTN_MIN_POS;
+    S = S > s_max ? s_max : S;
+    if (cta >= n_kv_heads * S) return false;
+    const int per = (n_pos + S - 1) / S;
+    a.kvh = cta / S;
+    a.sp = cta % S;
+    a.S = S;
+    a.p0 = a.sp * per;
+    a.p1 = min(n_pos, a.p0 + per);
+    if (a.p0 > a.p1) a.p0 = a.p1;
+    return true;
 }
 
-// One warp's share of the decode attention (math of reference cuda/attention_kernel.cu:
-// 45-98: scores q.k / sqrt(hd), GQA head map h -> h / (H/Hkv), max-subtracted softmax,
-// P.V): positions [p0, p1) in blocks of 32, for all GQ query heads of one kv head, with an
-// online softmax across the blocks. Lanes own positions for q.k and head dims for p.v; the
-// (m, l, acc[hd]) of each query head goes to `part` ([GQ][HD + 2]). qs holds the
-// pre-scaled q of the GQ heads.
-template <int HD, int GQ>
-__device__ __noinline__ void attn_warp(const float* qs, const __half* kb, const __half* vb, int p0, int p1, int lane,
-                                       float* part) {
-    constexpr int DPL = HD / 32;  // head dims per lane
-    float m[GQ], l[GQ], acc[GQ][DPL];
-#pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-#pragma unroll
-        for (int k = 0; k < DPL; ++k) acc[g][k] = 0.f;
-    }
-    for (int b0 = p0; b0 < p1; b0 += 32) {
-        const int pp = b0 + lane;
-        const bool valid = pp < p1;
-        const int nj = p1 - b0 < 32 ? p1 - b0 : 32;
-        float sc[GQ];
-#pragma unroll
-        for (int g = 0; g < GQ; ++g) sc[g] = 0.f;
-        if (valid) {
-            // this lane's K row, eight 16-byte loads in flight at a time
-            const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)pp * HD);
-#pragma unroll
-            for (int hb = 0; hb < HD / 64; ++hb) {
-                uint4 kv[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) kv[u] = __ldcg(kr + hb * 8 + u);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const int c8 = hb * 8 + u;
-                    float kf[8];
-                    unpack8(kv[u], kf);
-#pragma unroll
-                    for (int g = 0; g < GQ; ++g) {
-                        const float4 qa = reinterpret_cast<const float4*>(qs)[(g * HD) / 4 + 2 * c8];
-                        const float4 qb = reinterpret_cast<const float4*>(qs)[(g * HD) / 4 + 2 * c8 + 1];
-                        float a = sc[g];
-                        a = fmaf(qa.x, kf[0], a);
-                        a = fmaf(qa.y, kf[1], a);
-                        a = fmaf(qa.z, kf[2], a);
-                        a = fmaf(qa.w, kf[3], a);
-                        a = fmaf(qb.x, kf[4], a);
-                        a = fmaf(qb.y, kf[5], a);
-                        a = fmaf(qb.z, kf[6], a);
-                        a = fmaf(qb.w, kf[7], a);
-                        sc[g] = a;
-                    }
-                }
-            }
-        }
-        // the first 16 V rows are requested before the softmax (they do not depend on it)
-        float v0[16][DPL];
-#pragma unroll
-        for (int u = 0; u < 16; ++u) load_vrow<DPL>(vb + (size_t)(b0 + u) * HD, lane, u < nj, v0[u]);
-        float pr[GQ];
-#pragma unroll
-        for (int g = 0; g < GQ; ++g) {
-            const float sv = valid ? sc[g] : -INFINITY;
-            const float mn = fmaxf(m[g], warp_max(sv));
-            const float corr = m[g] == -INFINITY ? 0.f : expf(m[g] - mn);
-            pr[g] = valid ? expf(sv - mn) : 0.f;
-            l[g] = l[g] * corr + warp_sum(pr[g]);
-#pragma unroll
-            for (int k = 0; k < DPL; ++k) acc[g][k] *= corr;
-            m[g] = mn;
-        }
-#pragma unroll
-        for (int u = 0; u < 16; ++u)
-#pragma unroll
-            for (int g = 0; g < GQ; ++g) {
-                const float pj = __shfl_sync(JINF_FULL_MASK, pr[g], u);
-#pragma unroll
-                for (int k = 0; k < DPL; ++k) acc[g][k] = fmaf(pj, v0[u][k], acc[g][k]);
-            }
-        if (nj > 16) {
-#pragma unroll
-            for (int u = 0; u < 16; ++u) load_vrow<DPL>(vb + (size_t)(b0 + 16 + u) * HD, lane, 16 + u < nj, v0[u]);
-#pragma unroll
-            for (int u = 0; u < 16; ++u)
-#pragma unroll
-                for (int g = 0; g < GQ; ++g) {
-                    const float pj = __shfl_sync(JINF_FULL_MASK, pr[g], 16 + u);
-#pragma unroll
-                    for (int k = 0; k < DPL; ++k) acc[g][k] = fmaf(pj, v0[u][k], acc[g][k]);
-                }
-        }
-    }
-#pragma unroll
-    for (int g = 0; g < GQ; ++g) {
-#pragma unroll
-        for (int k = 0; k < DPL; ++k) part[g * (HD + 2) + lane * DPL + k] = acc[g][k];
-        if (lane == 0) {
-            part[g * (HD + 2) + HD] = m[g];
-            part[g * (HD + 2) + HD + 1] = l[g];
-        }
-    }
-}
-
+// One CTA's split [p0, p1) of kv head attention, after the QKV phase has finished: q of the
+// gq heads of the kv head at `q`, cache rows at kb / vb. Leaves either the normalised output
+// in `outs` ([gq][HD], shared memory; `part` null) or the split's partial (acc, m, l) in
+// `part` ([gq][HD + 2], global). Cache rows come in by bulk copy on `mbar` (`par` is its
+// next phase); chunk 0's rows before `pos` were requested before the QKV wait (`pre`).
 template <int HD>
-__device__ void attn_warp_dispatch(int gq, const float* qs, const __half* kb, const __half* vb, int p0, int p1,
-                                   int lane, float* part) {
-    switch (gq) {
-        case 1: attn_warp<HD, 1>(qs, kb, vb, p0, p1, lane, part); break;
-        case 2: attn_warp<HD, 2>(qs, kb, vb, p0, p1, lane, part); break;
-        case 4: attn_warp<HD, 4>(qs, kb, vb, p0, p1, lane, part); break;
-        default: attn_warp<HD, 8>(qs, kb, vb, p0, p1, lane, part); break;
+__device__ __noinline__ void attn_split(const float* q, const __half* kb, const __half* vb, int p0, int p1, int pos,
+                                        int gq, uint8_t* xbase, float* part, float* outs, uint32_t mbar, uint32_t& par,
+                                        bool pre, DeviceState* st, unsigned long long limit) {
+    constexpr int DPL = HD / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t kv_s = smem_u32(xbase);
+    const __half* kvh_s = reinterpret_cast<const __half*>(xbase);         // [2][ATTN_CHUNK][HD]
+    float* w_s = reinterpret_cast<float*>(xbase + 2 * ATTN_CHUNK * HD * 2);  // [gq][ATTN_CHUNK]
+    float* ml_s = w_s + ATTN_MAX_GROUP * ATTN_CHUNK;                         // [gq][3]: m, l, correction
+    const float scale = rsqrtf((float)HD);
+    // this lane's head dims of every query head (pre-scaled)
+    float qr[ATTN_MAX_GROUP][DPL];
+#pragma unroll
+    for (int g = 0; g < ATTN_MAX_GROUP; ++g)
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) qr[g][k] = g < gq ? __ldcg(q + g * HD + lane * DPL + k) * scale : 0.f;
+    if (tid < gq) {
+        ml_s[tid * 3] = -INFINITY;
+        ml_s[tid * 3 + 1] = 0.f;
     }
-}
-
-// Merge `n` partials (stride `stride` floats, [g][HD + 2] each; m = -inf marks an empty
-// one) of query head g, dim dd: returns sum_i e^(m_i - M) acc_i and sets L (sum of weighted
-// l_i) and M. Fixed order: deterministic.
-__device__ __forceinline__ float merge_parts(const float* base, int n, size_t stride, int g, int dd, int hd,
-                                             bool coherent, float& M, float& L) {
-    auto ld = [&](const float* p) { return coherent ? __ldcg(p) : *p; };
-    M = -INFINITY;
-    for (int i = 0; i < n; ++i) M = fmaxf(M, ld(base + i * stride + g * (hd + 2) + hd));
-    float a = 0.f;
-    L = 0.f;
-    for (int i = 0; i < n; ++i) {
-        const float* r = base + i * stride + g * (hd + 2);
-        const float mi = ld(r + hd);
-        if (mi == -INFINITY) continue;
-        const float f = expf(mi - M);
-        L = fmaf(ld(r + hd + 1), f, L);
-        a = fmaf(ld(r + dd), f, a);
+    const int n_out = gq * HD;
+    float acc0 = 0.f, acc1 = 0.f;  // outputs tid and tid + STEP_THREADS
+    for (int cb = p0; cb < p1; cb += ATTN_CHUNK) {
+        const int n = min(ATTN_CHUNK, p1 - cb);
+        if (cb == p0) {
+            // chunk 0: the rows from pos on (at most the new one) by plain loads
+            const int lo = max(cb, min(pos, cb + n));
+            constexpr int PER_ROW = HD * 2 / 16;
+            for (int i = tid; i < 2 * (cb + n - lo) * PER_ROW; i += STEP_THREADS) {
+                const int v = i >= (cb + n - lo) * PER_ROW, k = v ? i - (cb + n - lo) * PER_ROW : i;
+                const int r = lo + k / PER_ROW, c = k % PER_ROW;
+                const uint4 x = __ldcg(reinterpret_cast<const uint4*>((v ? vb : kb) + (size_t)r * HD) + c);
+                *reinterpret_cast<uint4*>(xbase + ((v ? ATTN_CHUNK : 0) + (r - cb)) * HD * 2 + c * 16) = x;
+            }
+            if (pre) {
+                mbar_wait(mbar, par, st, limit);
+                par ^= 1u;
+            }
+        } else {
+            if (tid == 0) {
+                fence_proxy_async();
+                bulk_expect(mbar, (uint32_t)(2 * n * HD * 2));
+                bulk_g2s(kv_s, kb + (size_t)cb * HD, (uint32_t)(n * HD * 2), mbar);
+                bulk_g2s(kv_s + ATTN_CHUNK * HD * 2, vb + (size_t)cb * HD, (uint32_t)(n * HD * 2), mbar);
+            }
+            mbar_wait(mbar, par, st, limit);
+            par ^= 1u;
+        }
+        __syncthreads();
+        // q.k: warp w takes positions w, w + 16; lanes own head dims
+        for (int j = warp; j < n; j += NW) {
+            float kf[DPL];
+            const __half2* kr = reinterpret_cast<const __half2*>(kvh_s + j * HD + lane * DPL);
+#pragma unroll
+            for (int k = 0; k < DPL / 2; ++k) {
+                const float2 t = __half22float2(kr[k]);
+                kf[2 * k] = t.x;
+                kf[2 * k + 1] = t.y;
+            }
+#pragma unroll
+            for (int g = 0; g < ATTN_MAX_GROUP; ++g) {
+                if (g >= gq) break;
+                float a = 0.f;
+#pragma unroll
+                for (int k = 0; k < DPL; ++k) a = fmaf(qr[g][k], kf[k], a);
+                a = warp_sum(a);
+                if (lane == 0) w_s[g * ATTN_CHUNK + j] = a;
+            }
+        }
+        __syncthreads();
+        // online softmax of the chunk, one warp per query head
+        if (warp < gq) {
+            const float sv = lane < n ? w_s[warp * ATTN_CHUNK + lane] : -INFINITY;
+            const float mo = ml_s[warp * 3], mn = fmaxf(mo, warp_max(sv));
+            const float e = lane < n ? expf(sv - mn) : 0.f;
+            const float corr = mo == -INFINITY ? 0.f : expf(mo - mn);
+            const float ln = fmaf(ml_s[warp * 3 + 1], corr, warp_sum(e));
+            w_s[warp * ATTN_CHUNK + lane] = e;
+            __syncwarp();
+            if (lane == 0) {
+                ml_s[warp * 3] = mn;
+                ml_s[warp * 3 + 1] = ln;
+                ml_s[warp * 3 + 2] = corr;
+            }
+        }
+        __syncthreads();
+        // p.v: one output (query head g, dim dd) per thread (two when gq * HD > 512)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int o = tid + h * STEP_THREADS;
+            if (o >= n_out) break;
+            const int g = o / HD, dd = o % HD;
+            float a = (h ? acc1 : acc0) * ml_s[g * 3 + 2];
+            const float* wr = w_s + g * ATTN_CHUNK;
+            const __half* vr = kvh_s + ATTN_CHUNK * HD + dd;
+            for (int j = 0; j < n; ++j) a = fmaf(wr[j], __half2float(vr[j * HD]), a);
+            if (h) acc1 = a;
+            else acc0 = a;
+        }
+        __syncthreads();  // the next chunk overwrites the rows and the weights
     }
-    return a;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int o = tid + h * STEP_THREADS;
+        if (o >= n_out) break;
+        const int g = o / HD, dd = o % HD;
+        const float a = h ? acc1 : acc0;
+        if (part) {
+            part[g * (HD + 2) + dd] = a;
+            if (dd == 0) {
+                part[g * (HD + 2) + HD] = p1 > p0 ? ml_s[g * 3] : -INFINITY;  // an empty split
+                part[g * (HD + 2) + HD + 1] = ml_s[g * 3 + 1];
+            }
+        } else {
+            outs[o] = a / ml_s[g * 3 + 1];
+        }
+    }
 }
 
 }  // namespace
@@ -325,7 +449,7 @@ __device__ __forceinline__ float merge_parts(const float* base, int n, size_t st
 __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     extern __shared__ __align__(16) uint8_t smem[];
     // shared memory: [xstage | misc 256 B | flags, keys, piece table 512 B | partial rows 4 KB |
-    //                 phase descriptor 2 x 256 B | phase infos | rings]
+    //                 outputs to convert 4 KB | phase descriptor 2 x 256 B | phase infos | rings]
     uint8_t* xbase = smem;
     float* misc = reinterpret_cast<float*>(smem + P.xstage_bytes);        // 64 floats of reductions
     int* flags = reinterpret_cast<int*>(smem + P.xstage_bytes + 256);     // [0..1] go, [2] attention last
@@ -333,8 +457,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     int* ftile = reinterpret_cast<int*>(smem + P.xstage_bytes + 256 + 192);  // [NW] tile of a warp's first piece
     int* fmid = ftile + NW;                                                  // [NW] first piece starts mid-tile
     float* part_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768);   // [NW][2][32] partial rows
-    StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 4096);  // [2] descriptors
-    PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 4096 + 512);
+    float* outs_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768 + 4096);  // [1024] outputs to convert
+    const uint32_t mbar_rec = smem_u32(smem + P.xstage_bytes + 576);  // bulk copies of input records
+    const uint32_t mbar_kv = smem_u32(smem + P.xstage_bytes + 584);   // bulk copies of attention cache rows
+    StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 8192);  // [2] descriptors
+    PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 8192 + 512);
     const uint32_t ring_base = smem_u32(pinfo + ((P.n_phases + 1) & ~1));
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ring = ring_base + (uint32_t)(warp * STEP_NBUF * Q4M_UNIT);
@@ -347,9 +474,16 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         PhaseInfo pi;
         pi.w = P.phases[i].w;
         pi.pairs = P.phases[i].pairs;
+        pi.gran = P.phases[i].gran;
         pi.groups = P.phases[i].kind == PH_GEMV ? P.phases[i].groups : 0;
         pinfo[i] = pi;
     }
+    if (tid == 0) {
+        mbar_init(mbar_rec);
+        mbar_init(mbar_kv);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    uint32_t par_rec = 0, par_kv = 0;  // next phase of each mbarrier (the same in every thread)
     __syncthreads();
 
     // ---------------- weight stream: this warp's unit ranges of all GEMV phases, copied in
@@ -377,92 +511,106 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             flags[ph & 1] = g.dep < 0 ? 1 : (wait_ge(P.done + g.dep, g.dep_target, st, P.spin_limit) ? 1 : 0);
         } else if (tid >= 32 && tid < 32 + DWORDS) {  // descriptor -> shared memory while warp 0 polls
             reinterpret_cast<uint32_t*>(&d)[tid - 32] = reinterpret_cast<const uint32_t*>(P.phases + ph)[tid - 32];
-        } else if (tid == 32 * 9) {  // L2 prefetch of later weights while warp 0 polls
-            for (int k = 0; k < 2; ++k) {
-                const int j = P.phases[ph].pf[k];
-                if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C);
+        } else if (tid >= 96) {
+            if (tid == 32 * 9) {  // L2 prefetch of later weights while warp 0 polls
+                for (int k = 0; k < 2; ++k) {
+                    const int j = P.phases[ph].pf[k];
+                    if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C);
+                }
+            }
+            AttnGeom a;
+            if (tid == 96 && P.phases[ph].kind == PH_ATTN && attn_geom(pos, P.n_kv_heads, P.attn_smax, blockIdx.x, a)) {
+                // the first chunk's cache rows written by earlier tokens, while warp 0 polls
+                const int hi = min(min(a.p0 + ATTN_CHUNK, a.p1), pos);
+                if (hi > a.p0) {
+                    const StepPhase& g = P.phases[ph];
+                    const size_t off = ((size_t)a.kvh * P.max_ctx + a.p0) * P.head_dim;
+                    const uint32_t rb = (uint32_t)((hi - a.p0) * P.head_dim * 2);
+                    fence_proxy_async();
+                    bulk_expect(mbar_kv, 2 * rb);
+                    bulk_g2s(smem_u32(xbase), g.kcache + off, rb, mbar_kv);
+                    bulk_g2s(smem_u32(xbase) + ATTN_CHUNK * P.head_dim * 2, g.vcache + off, rb, mbar_kv);
+                }
             }
         }
         __syncthreads();  // also: every warp is done with the previous phase's shared data
         if (!flags[ph & 1]) break;
 
         if (d.kind == PH_ATTN) {
-            // ---------------- attention: CTA (kvh, split) covers up to ATTN_POS_PER_CTA positions
+            // ---------------- attention: CTA (kv head, split) of the context
+            AttnGeom a;
+            if (!attn_geom(pos, P.n_kv_heads, P.attn_smax, blockIdx.x, a)) continue;
             const int hd = P.head_dim, gq = P.n_heads / P.n_kv_heads;
-            const int n_pos = pos + 1;
-            int cpk = (n_pos + ATTN_POS_PER_CTA - 1) / ATTN_POS_PER_CTA;
-            cpk = cpk > ATTN_MAX_SPLIT ? ATTN_MAX_SPLIT : cpk;
-            const int per = (n_pos + cpk - 1) / cpk;
-            if ((int)blockIdx.x >= P.n_kv_heads * cpk) continue;
-            const int kvh = blockIdx.x / cpk, sp = blockIdx.x % cpk;
-            const int p0 = sp * per, p1 = min(n_pos, p0 + per);
-            float* qs = reinterpret_cast<float*>(xbase);                   // [gq][hd], pre-scaled
-            float* wp = qs + gq * hd;                                       // [NW][gq][hd + 2]
-            const float scale = rsqrtf((float)hd);
-            const float4* qsrc = reinterpret_cast<const float4*>(d.q + (size_t)kvh * gq * hd);
-            for (int i = tid; i < gq * hd / 4; i += STEP_THREADS) {
-                float4 v = __ldcg(qsrc + i);
-                v.x *= scale;
-                v.y *= scale;
-                v.z *= scale;
-                v.w *= scale;
-                reinterpret_cast<float4*>(qs)[i] = v;
-            }
-            __syncthreads();
-            float* mypart = wp + (size_t)warp * gq * (hd + 2);
-            const int wp0 = p0 + warp * ATTN_POS_PER_WARP, wp1 = min(p1, wp0 + ATTN_POS_PER_WARP);
-            const __half* kb = d.kcache + (size_t)kvh * P.max_ctx * hd;
-            const __half* vb = d.vcache + (size_t)kvh * P.max_ctx * hd;
-            if (wp0 < wp1) {
-                if (hd == 64) attn_warp_dispatch<64>(gq, qs, kb, vb, wp0, wp1, lane, mypart);
-                else attn_warp_dispatch<128>(gq, qs, kb, vb, wp0, wp1, lane, mypart);
-            } else if (lane < gq) {
-                mypart[lane * (hd + 2) + hd] = -INFINITY;  // empty
-            }
-            __syncthreads();
-            // merge the warps (fixed order)
-            float* gpart = P.attn_part + ((size_t)kvh * ATTN_MAX_SPLIT + sp) * ATTN_MAX_GROUP * (hd + 2);
-            for (int i = tid; i < gq * hd; i += STEP_THREADS) {
-                const int g = i / hd, dd = i % hd;
-                float M, L;
-                const float a = merge_parts(wp, NW, (size_t)gq * (hd + 2), g, dd, hd, false, M, L);
-                if (cpk == 1) {
-                    d.out[(size_t)(kvh * gq + g) * hd + dd] = a / L;
-                } else {
-                    gpart[g * (hd + 2) + dd] = a;
-                    if (dd == 0) {
-                        gpart[g * (hd + 2) + hd] = M;
-                        gpart[g * (hd + 2) + hd + 1] = L;
-                    }
-                }
-            }
-            bool wrote = cpk == 1;
-            if (cpk > 1) {
-                // last CTA of this kv head merges the CTAs' partials (split order)
+            const float* qh = d.q + (size_t)a.kvh * gq * hd;
+            const __half* kb = d.kcache + (size_t)a.kvh * P.max_ctx * hd;
+            const __half* vb = d.vcache + (size_t)a.kvh * P.max_ctx * hd;
+            float* gpart =
+                a.S > 1 ? P.attn_part + ((size_t)a.kvh * ATTN_MAX_SPLIT + a.sp) * ATTN_MAX_GROUP * (hd + 2) : nullptr;
+            const bool pre = min(min(a.p0 + ATTN_CHUNK, a.p1), pos) > a.p0;  // as requested above
+            if (hd == 64)
+                attn_split<64>(qh, kb, vb, a.p0, a.p1, pos, gq, xbase, gpart, outs_s, mbar_kv, par_kv, pre, st,
+                               P.spin_limit);
+            else
+                attn_split<128>(qh, kb, vb, a.p0, a.p1, pos, gq, xbase, gpart, outs_s, mbar_kv, par_kv, pre, st,
+                                P.spin_limit);
+            bool wrote = a.S == 1;
+            if (a.S > 1) {
+                // the last split of this kv head to finish merges all splits (split order)
                 __syncthreads();
                 if (tid == 0) {
                     __threadfence();
-                    const unsigned old = atomicAdd(&st->attn_count[kvh], 1u);
-                    flags[2] = old == (unsigned)(cpk - 1);
+                    const unsigned old = atomicAdd(&st->attn_count[a.kvh], 1u);
+                    flags[2] = old == (unsigned)(a.S - 1);
                     if (flags[2]) {
                         __threadfence();
-                        st->attn_count[kvh] = 0u;
+                        st->attn_count[a.kvh] = 0u;
                     }
                 }
                 __syncthreads();
                 wrote = flags[2] != 0;
                 if (wrote) {
-                    const float* base = P.attn_part + (size_t)kvh * ATTN_MAX_SPLIT * ATTN_MAX_GROUP * (hd + 2);
+                    // (m, l) of every split -> weights e^(m_s - M) / L per query head, then one pass
+                    // over the splits' accumulators (split order: deterministic)
+                    const size_t stride = (size_t)ATTN_MAX_GROUP * (hd + 2);
+                    const float* base = P.attn_part + (size_t)a.kvh * ATTN_MAX_SPLIT * stride;
+                    float* wts = reinterpret_cast<float*>(xbase);  // [S][gq][2]
+                    for (int i = tid; i < a.S * gq; i += STEP_THREADS) {
+                        const float* r = base + (i / gq) * stride + (i % gq) * (hd + 2);
+                        wts[2 * i] = __ldcg(r + hd);
+                        wts[2 * i + 1] = __ldcg(r + hd + 1);
+                    }
+                    __syncthreads();
+                    if (tid < gq) {
+                        float M = -INFINITY, L = 0.f;
+                        for (int s2 = 0; s2 < a.S; ++s2) M = fmaxf(M, wts[2 * (s2 * gq + tid)]);
+                        for (int s2 = 0; s2 < a.S; ++s2) {
+                            const float m = wts[2 * (s2 * gq + tid)];
+                            if (m != -INFINITY) L = fmaf(wts[2 * (s2 * gq + tid) + 1], expf(m - M), L);
+                        }
+                        for (int s2 = 0; s2 < a.S; ++s2) {
+                            const float m = wts[2 * (s2 * gq + tid)];
+                            wts[2 * (s2 * gq + tid)] = m == -INFINITY ? 0.f : expf(m - M) / L;
+                        }
+                    }
+                    __syncthreads();
                     for (int i = tid; i < gq * hd; i += STEP_THREADS) {
                         const int g = i / hd, dd = i % hd;
-                        float M, L;
-                        const float a =
-                            merge_parts(base, cpk, (size_t)ATTN_MAX_GROUP * (hd + 2), g, dd, hd, true, M, L);
-                        d.out[(size_t)(kvh * gq + g) * hd + dd] = a / L;
+                        const float* r = base + g * (hd + 2) + dd;
+                        float v = 0.f;
+#pragma unroll 8
+                        for (int s2 = 0; s2 < a.S; ++s2) v = fmaf(wts[2 * (s2 * gq + g)], __ldcg(r + s2 * stride), v);
+                        outs_s[i] = v;
                     }
                 }
             }
             if (wrote) {
+                __syncthreads();
+                if (d.rec_out) {
+                    // this kv head's outputs are whole blocks of the o projection's input
+                    blocks_to_records(outs_s, a.kvh * gq * hd / 32, gq * hd / 32, d.groups_out, d.rec_out);
+                } else {
+                    for (int i = tid; i < gq * hd; i += STEP_THREADS) d.out[(size_t)a.kvh * gq * hd + i] = outs_s[i];
+                }
                 __syncthreads();
                 if (tid == 0) {
                     __threadfence();
@@ -483,12 +631,20 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                 prefetch_l2(reinterpret_cast<const uint8_t*>(base) + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
         }
         const int G = d.groups;
-        const int t0 = step_cta_tile(blockIdx.x, C, d.pairs), t1 = step_cta_tile(blockIdx.x + 1, C, d.pairs);
+        int t0, t1;
+        cta_range(blockIdx.x, C, d.pairs, d.gran, t0, t1);
         if (t0 >= t1) continue;
-        const float* hsrc = d.xm == X_EMBED_NORM ? d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols : d.hsrc;
-        // the CTA that owns pair 0 stores the embedding row as the residual stream
-        const float fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps, d.cols,
-                                                xbase, misc, true);
+        float fac;
+        if (d.xm == X_RECORDS) {
+            fac = stage_records(d.rec, d.ssp, d.n_ss, d.cols, P.eps, G, xbase, mbar_rec, par_rec, st, P.spin_limit);
+            par_rec ^= 1u;
+        } else {
+            const float* hsrc =
+                d.xm == X_EMBED_NORM ? d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols : d.hsrc;
+            // the CTA that owns pair 0 stores the embedding row as the residual stream
+            fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps, d.cols, xbase,
+                                        misc, true);
+        }
         const XRecS xr{smem_u32(xbase), smem_u32(xbase + (size_t)G * 256)};
         // epilogue arguments are read from the shared descriptor when a tile finishes
         auto epilogue = [&](int row, float v0, float v1) {
@@ -507,8 +663,23 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             ea.coherent = true;
             epilogue_pair(ea, row, v0 * fac, v1 * fac, lmax, lidx);
         };
+        // a finished pair, by the whole warp (lanes q < 16 hold rows 2q, 2q+1)
+        auto finish_pair = [&](int pr, float v0, float v1) {
+            const int q = lane & 15, row = pr * Q4M_PAIR_ROWS + 2 * q;
+            if (d.rec_out && d.epi == EPI_RESID) {
+                resid_records(d, pr, v0 * fac, v1 * fac);
+            } else if (d.rec_out && d.epi == EPI_GATEUP) {
+                // the activation goes to shared memory; whole blocks become records below
+                if (lane < 16) {
+                    const float g = v0 * fac, u = v1 * fac;
+                    outs_s[(pr - t0) * 16 + q] = row < d.rows ? g / (1.0f + expf(-g)) * u : 0.f;
+                }
+            } else if (lane < 16) {
+                epilogue(row, v0, v1);
+            }
+        };
         int c, c1;
-        warp_range(blockIdx.x, C, warp, d.pairs, G, c, c1);
+        warp_range(blockIdx.x, C, warp, d.pairs, d.gran, G, c, c1);
         if (lane == 0) {
             ftile[warp] = -1;
             fmid[warp] = 0;
@@ -528,7 +699,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             if (gb == 0 && ge == G) {
                 const int q = lane & 15;
                 const float v0 = unit_row(ps.acc, 2 * q), v1 = unit_row(ps.acc, 2 * q + 1);
-                if (lane < 16) epilogue(pair * Q4M_PAIR_ROWS + 2 * q, v0, v1);
+                finish_pair(pair, v0, v1);
             } else {
                 // a piece of a pair shared with the neighbouring warps: partial rows to shared memory
                 const int sl = first_piece ? 0 : 1;
@@ -544,20 +715,26 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             first_piece = false;
         }
         __syncthreads();
-        if (own_pair >= 0 && lane < 16) {
+        if (own_pair >= 0) {
             // add the pieces of the following warps in warp order, then the epilogue
-            float v0 = part_s[(warp * 2 + own_slot) * 32 + 2 * lane];
-            float v1 = part_s[(warp * 2 + own_slot) * 32 + 2 * lane + 1];
+            const int q = lane & 15;
+            float v0 = part_s[(warp * 2 + own_slot) * 32 + 2 * q];
+            float v1 = part_s[(warp * 2 + own_slot) * 32 + 2 * q + 1];
             for (int w2 = warp + 1; w2 < NW; ++w2) {
                 const int ft = ftile[w2];
                 if (ft < 0) continue;                       // a warp with no units in this phase
                 if (ft != own_pair || !fmid[w2]) break;     // the next pair starts
-                v0 += part_s[(w2 * 2) * 32 + 2 * lane];
-                v1 += part_s[(w2 * 2) * 32 + 2 * lane + 1];
+                v0 += part_s[(w2 * 2) * 32 + 2 * q];
+                v1 += part_s[(w2 * 2) * 32 + 2 * q + 1];
             }
-            epilogue(own_pair * Q4M_PAIR_ROWS + 2 * lane, v0, v1);
+            finish_pair(own_pair, v0, v1);
         }
         __syncthreads();  // every epilogue store of the CTA precedes the report
+        if (d.rec_out && d.epi == EPI_GATEUP) {
+            // pairs [t0, t1) hold activation blocks [t0 / 2, t1 / 2) (gran 2)
+            blocks_to_records(outs_s, t0 >> 1, (t1 - t0) >> 1, d.groups_out, d.rec_out);
+            __syncthreads();
+        }
         if (tid == 0) {
             __threadfence();
             atomicAdd(P.done + ph, (unsigned)(t1 - t0));
@@ -603,14 +780,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
     const size_t G = (size_t)(max_cols + Q4M_KG - 1) / Q4M_KG;
     const size_t gemv = xrec_bytes((int)G);
-    const size_t attn = (size_t)group * head_dim * sizeof(float) + (size_t)NW * group * (head_dim + 2) * sizeof(float);
+    const size_t attn = (size_t)2 * ATTN_CHUNK * head_dim * 2 + (size_t)ATTN_MAX_GROUP * (ATTN_CHUNK + 3) * sizeof(float);
     const size_t b = gemv > attn ? gemv : attn;
     return (unsigned int)((b + 15) & ~(size_t)15);
 }
 
 size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases) {
     const size_t infos = sizeof(PhaseInfo) * (size_t)((n_phases + 1) & ~1);
-    return (size_t)xstage_bytes + 768 + 4096 + 512 + infos + (size_t)NW * STEP_NBUF * Q4M_UNIT;
+    return (size_t)xstage_bytes + 768 + 8192 + 512 + infos + (size_t)NW * STEP_NBUF * Q4M_UNIT;
 }
 
 static cudaError_t step_configure(size_t smem) {
