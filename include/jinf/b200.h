@@ -20,9 +20,18 @@ extern "C" {
 
 // Bytes of the Q4M image of a rows x cols Q4_0 matrix; 0 if cols is not a multiple of 32
 // (whole blocks; the last 128-column group is zero-padded).
-// Q4M is the layout of the tensor-core GEMV: 16-row tiles x 128-column groups, 1152 bytes
-// per (tile, group), every nibble and scale of the AoS blocks moved, none re-quantised.
+// Q4M is the layout of the tensor-core GEMV: 32-row tile pairs x 128-column groups, 2304
+// bytes per (pair, group), every nibble and scale of the AoS blocks moved, none re-quantised.
 uint64_t jinf_b200_q4m_bytes(int rows, int cols);
+
+// The same for either weight type: qtype JINF_TYPE_Q4_0 or JINF_TYPE_Q4_K (2432 bytes per
+// (pair, group); cols a multiple of 256). 0 for other types or shapes. No counterpart in
+// the reference, whose Q4_K matvec reads the AoS super-blocks (reference
+// cuda/matmul_kernels.cu:47-100).
+uint64_t jinf_b200_q4m_bytes_qt(int rows, int cols, int qtype);
+jinf_status jinf_b200_q4m_pack_qt(const void* aos, int qtype, void* q4m, int rows, int cols, cudaStream_t stream);
+jinf_status jinf_b200_gemv_q4m_qt(const void* q4m, int qtype, const void* x, int x_type, float* y, int rows,
+                                  int cols, void* workspace, int kw, cudaStream_t stream);
 
 // Repack reference AoS Q4_0 blocks [rows][cols/32] (device) into Q4M (device, q4m_bytes).
 jinf_status jinf_b200_q4m_pack(const void* aos, void* q4m, int rows, int cols, cudaStream_t stream);

@@ -35,6 +35,24 @@ extern "C" jinf_status jinf_b200_q4m_pack(const void* aos, void* q4m, int rows, 
     return q4m_repack(aos, q4m, sh, stream) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
 }
 
+static int q4m_fmt_of(int qtype) {
+    return qtype == JINF_TYPE_Q4_0 ? Q4M_Q4_0 : qtype == JINF_TYPE_Q4_K ? Q4M_Q4_K : -1;
+}
+
+extern "C" uint64_t jinf_b200_q4m_bytes_qt(int rows, int cols, int qtype) {
+    Q4MShape sh;
+    const int fmt = q4m_fmt_of(qtype);
+    return fmt >= 0 && q4m_shape(rows, cols, &sh, fmt) ? sh.bytes : 0;
+}
+
+extern "C" jinf_status jinf_b200_q4m_pack_qt(const void* aos, int qtype, void* q4m, int rows, int cols,
+                                             cudaStream_t stream) {
+    Q4MShape sh;
+    const int fmt = q4m_fmt_of(qtype);
+    if (!aos || !q4m || fmt < 0 || !q4m_shape(rows, cols, &sh, fmt)) return JINF_ERR_INVALID;
+    return q4m_repack(aos, q4m, sh, stream) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+}
+
 static constexpr int kQ4mMaxKw = 32;
 
 extern "C" size_t jinf_b200_gemv_q4m_workspace_bytes(int rows, int cols) {
@@ -45,8 +63,8 @@ extern "C" size_t jinf_b200_gemv_q4m_workspace_bytes(int rows, int cols) {
 
 static jinf_status gemv_q4m_common(GemvParams& p, const Q4MShape& sh, int xm, void* workspace, int kw,
                                    cudaStream_t stream) {
-    if (sh.cols > gemvm_max_cols() || kw < 0 || kw > kQ4mMaxKw) return JINF_ERR_INVALID;
-    const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms());
+    if (sh.cols > gemvm_max_cols(sh.fmt) || kw < 0 || kw > kQ4mMaxKw) return JINF_ERR_INVALID;
+    const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms(), sh.fmt);
     if (kw == 0) kw = gemvm_pick_kw(sh.pairs, sh.groups, grid, workspace ? kQ4mMaxKw : 1);
     if (kw > sh.groups || (kw > 1 && !workspace)) return JINF_ERR_INVALID;
     p.kw = kw;
@@ -61,6 +79,19 @@ extern "C" jinf_status jinf_b200_gemv_q4m(const void* q4m, const void* x, int x_
                                           void* workspace, int kw, cudaStream_t stream) {
     Q4MShape sh;
     if (!q4m || !x || !y || !q4m_shape(rows, cols, &sh)) return JINF_ERR_INVALID;
+    if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
+    GemvParams p{};
+    gemvm_params_for(p, q4m, sh);
+    p.x = x;
+    p.y = y;
+    return gemv_q4m_common(p, sh, x_type == JINF_TYPE_F32 ? X_PLAIN_F32 : X_PLAIN_F16, workspace, kw, stream);
+}
+
+extern "C" jinf_status jinf_b200_gemv_q4m_qt(const void* q4m, int qtype, const void* x, int x_type, float* y,
+                                             int rows, int cols, void* workspace, int kw, cudaStream_t stream) {
+    Q4MShape sh;
+    const int fmt = q4m_fmt_of(qtype);
+    if (!q4m || !x || !y || fmt < 0 || !q4m_shape(rows, cols, &sh, fmt)) return JINF_ERR_INVALID;
     if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
     GemvParams p{};
     gemvm_params_for(p, q4m, sh);

@@ -68,11 +68,11 @@ struct ModelSource {
     virtual ~ModelSource() {}
     virtual bool meta(const char* name, TensorMeta* m) const = 0;
     virtual jinf_status read_rows(const char* name, int64_t row0, int64_t n, void* dst) const = 0;
-    // Optional device-side generation (synthetic models): Q4_0 rows [r0, r0+nr) x columns
-    // [c0, c0+nc) into device rows dst_row0 + i*dst_step of pitch dst_row_bytes, or the
-    // whole f32 tensor. Return false when the source has no device path.
-    virtual bool device_q4_0(const char*, int64_t, int64_t, int64_t, int64_t, uint8_t*, int64_t, int64_t, int64_t,
-                             cudaStream_t, jinf_status*) const { return false; }
+    // Optional device-side generation (synthetic models): Q4_0 or Q4_K rows [r0, r0+nr) x
+    // columns [c0, c0+nc) into device rows dst_row0 + i*dst_step of pitch dst_row_bytes, or
+    // the whole f32 tensor. Return false when the source has no device path.
+    virtual bool device_quant(const char*, int64_t, int64_t, int64_t, int64_t, uint8_t*, int64_t, int64_t, int64_t,
+                              cudaStream_t, jinf_status*) const { return false; }
     virtual bool device_f32(const char*, float*, cudaStream_t, jinf_status*) const { return false; }
     jinf_model_hparams hp{};
     int primary_type = JINF_TYPE_Q4_0;
@@ -91,17 +91,21 @@ struct SynthSource : ModelSource {
     jinf_status read_rows(const char* name, int64_t row0, int64_t n, void* dst) const override {
         return jinf_synth_read_rows(m, name, row0, n, dst);
     }
-    bool device_q4_0(const char* name, int64_t r0, int64_t nr, int64_t c0, int64_t nc, uint8_t* dst,
-                     int64_t dst_row_bytes, int64_t dst_row0, int64_t dst_step, cudaStream_t s,
-                     jinf_status* st) const override {
+    bool device_quant(const char* name, int64_t r0, int64_t nr, int64_t c0, int64_t nc, uint8_t* dst,
+                      int64_t dst_row_bytes, int64_t dst_row0, int64_t dst_step, cudaStream_t s,
+                      jinf_status* st) const override {
         uint64_t key;
         float stdv;
         int role;
         TensorMeta t;
-        if (!synth_tensor_params(m, name, &key, &stdv, &role) || !meta(name, &t) || t.type != JINF_TYPE_Q4_0)
+        if (!synth_tensor_params(m, name, &key, &stdv, &role) || !meta(name, &t) ||
+            (t.type != JINF_TYPE_Q4_0 && t.type != JINF_TYPE_Q4_K))
             return false;
-        *st = synth_fill_q4_0(key, stdv, t.cols(), r0, nr, c0, nc, dst, dst_row_bytes, dst_row0, dst_step, s) ==
-                      cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+        const cudaError_t e =
+            t.type == JINF_TYPE_Q4_K
+                ? synth_fill_q4_k(key, stdv, t.cols(), r0, nr, c0, nc, dst, dst_row_bytes, dst_row0, dst_step, s)
+                : synth_fill_q4_0(key, stdv, t.cols(), r0, nr, c0, nc, dst, dst_row_bytes, dst_row0, dst_step, s);
+        *st = e == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
         return true;
     }
     bool device_f32(const char* name, float* dst, cudaStream_t s, jinf_status* st) const override {
@@ -240,6 +244,8 @@ struct jinf_engine_impl {
     int device = 0;
     int tp_rank = 0, tp_size = 1;
     int num_sms = 148;
+    int wfmt = Q4M_Q4_0;       // Q4MFormat of every weight matrix (the model's quantisation)
+    int wtype = JINF_TYPE_Q4_0;
     cudaStream_t stream = nullptr;
     bool use_graph = true;
     int eos = 2;
@@ -298,6 +304,7 @@ struct jinf_engine_impl {
     // the producing phase, and the per-pair sums of h^2 behind the RMSNorm inputs
     uint8_t* step_rec[4] = {nullptr, nullptr, nullptr, nullptr};
     float* step_ss = nullptr;
+    unsigned int* step_attn_cnt = nullptr;  // [layers][Hkv] attention split arrival counters
     StepParams sp_full{}, sp_body{};
     // ops and graphs
     std::vector<Op> ops_full, ops_body;
@@ -369,7 +376,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
     };
     // grid and K split of a stand-alone GEMV
     auto finish = [&](Op& op) {
-        op.grid = gemvm_grid(op.gp.cols, op.xm, op.epi, I->num_sms);
+        op.grid = gemvm_grid(op.gp.cols, op.xm, op.epi, I->num_sms, op.gp.fmt);
         op.gp.kw = gemvm_pick_kw(op.gp.pairs, op.gp.groups, op.grid, kEngineMaxKw);
         op.gp.part = I->gemv_part;
         op.gp.cnt = I->gemv_cnt;
@@ -557,6 +564,7 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         at.out = I->attn;
         at.kcache = kc;
         at.vcache = vc;
+        at.layer = L;
         at.rec_out = I->step_rec[0];
         at.groups_out = ly.o_sh.groups;
         ph.push_back(at);
@@ -581,7 +589,10 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
     }
     for (size_t i = 0; i < ph.size(); ++i) {
         ph[i].dep = (int)i - 1;
-        ph[i].dep_target = i == 0 ? 0u : ph[i - 1].kind == PH_GEMV ? (unsigned)ph[i - 1].pairs : (unsigned)I->Hkvl;
+        // GEMV phases report tile pairs, attention its 32-element output blocks
+        ph[i].dep_target = i == 0                      ? 0u
+                           : ph[i - 1].kind == PH_GEMV ? (unsigned)ph[i - 1].pairs
+                                                       : (unsigned)(I->Hl * I->hd / 32);
         ph[i].pf[0] = ph[i].pf[1] = -1;
     }
     // L2 prefetch schedule (phase order per layer: qkv, attention, o, gate|up, down). HBM
@@ -613,15 +624,15 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     for (const auto& ly : I->layers)
         for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) max_cols = std::max(max_cols, sh->cols);
     const unsigned xs = step_xstage_bytes(max_cols, G, I->hd);
-    const size_t smem = step_smem_bytes(xs, 5 * I->L + 1);
+    const size_t smem = step_smem_bytes(xs, 5 * I->L + 1, I->wfmt);
     // input records: a tile pair of h is one 32-element block, a CTA's gate|up rows are whole
     // activation blocks and fit the 1024-float conversion buffer, as do a kv head's outputs
     const int gu_pairs = I->layers.empty() ? 0 : I->layers[0].gu_sh.pairs;
     const int gu_per_cta = 2 * ((gu_pairs / 2 + I->num_sms - 1) / I->num_sms);
     const bool records_ok = I->d % 32 == 0 && (I->Hl * I->hd) % 32 == 0 && gu_pairs % 2 == 0 &&
                             gu_per_cta * 16 <= 1024 && G * I->hd <= 1024;
-    if (G > ATTN_MAX_GROUP || I->Hkvl > 64 || (I->hd != 64 && I->hd != 128) || smem > 227 * 1024 ||
-        step_occupancy(smem) < 1 || !records_ok) {
+    if (G > ATTN_MAX_GROUP || (G & (G - 1)) || I->Hkvl > 64 || (I->hd != 64 && I->hd != 128) || smem > 227 * 1024 ||
+        step_occupancy(smem, I->wfmt) < 1 || !records_ok) {
         JINF_LOG("persistent step unavailable for this shape (%zu bytes of shared memory); using one kernel per "
                  "operation", smem);
         return JINF_OK;
@@ -637,6 +648,8 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
             JINF_CUDA_CHECK(cudaMemset(I->step_rec[i], 0, xrec_bytes(rec_groups[i])));
         }
         JINF_CUDA_CHECK(cudaMalloc(&I->step_ss, sizeof(float) * (size_t)(I->d / 32)));
+        JINF_CUDA_CHECK(cudaMalloc(&I->step_attn_cnt, sizeof(unsigned int) * (size_t)I->L * I->Hkvl));
+        JINF_CUDA_CHECK(cudaMemset(I->step_attn_cnt, 0, sizeof(unsigned int) * (size_t)I->L * I->Hkvl));
     }
     std::vector<StepPhase> full, body;
     build_step(I, true, full);
@@ -652,6 +665,8 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     StepParams sp{};
     sp.done = I->step_done;
     sp.attn_part = I->step_attn_part;
+    sp.attn_cnt = I->step_attn_cnt;
+    sp.n_attn_cnt = I->L * I->Hkvl;
     sp.st = I->st;
     sp.nq = I->Hl * I->hd;
     sp.nk = I->Hkvl * I->hd;
@@ -662,6 +677,7 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     sp.rope_base = I->rope_base;
     sp.eps = I->eps;
     sp.attn_smax = std::max(1, std::min(ATTN_MAX_SPLIT, I->num_sms / I->Hkvl));
+    sp.fmt = I->wfmt;
     sp.xstage_bytes = xs;
     sp.spin_limit = 4000000ull;  // about a second of polling: far beyond any phase, never a hang
     I->sp_full = sp;
@@ -709,24 +725,25 @@ struct Loader {
             JINF_LOG("tensor %s missing", name);
             return JINF_ERR_PARSE;
         }
-        if (m.type != JINF_TYPE_Q4_0) {
-            JINF_LOG("tensor %s: type %s not supported by the B200 engine (Q4_0 required)", name,
-                     jinf_qtype_name((jinf_qtype)m.type));
+        if (m.type != I->wtype) {
+            JINF_LOG("tensor %s: type %s, but the model's projections are %s (one type for all of them)", name,
+                     jinf_qtype_name((jinf_qtype)m.type), jinf_qtype_name((jinf_qtype)I->wtype));
             return JINF_ERR_INVALID;
         }
-        if (r0 < 0 || c0 < 0 || r0 + nr > m.rows() || c0 + nc > m.cols() || c0 % 32 || nc % 32) {
+        const int bs = I->wtype == JINF_TYPE_Q4_K ? 256 : 32, bb = I->wtype == JINF_TYPE_Q4_K ? 144 : 18;
+        if (r0 < 0 || c0 < 0 || r0 + nr > m.rows() || c0 + nc > m.cols() || c0 % bs || nc % bs) {
             JINF_LOG("tensor %s: slice [%lld+%lld, %lld+%lld) out of range", name, (long long)r0, (long long)nr,
                      (long long)c0, (long long)nc);
             return JINF_ERR_INVALID;
         }
         jinf_status st = JINF_OK;
-        if (src->device_q4_0(name, r0, nr, c0, nc, dstage, dst_row_bytes, dst_row0, dst_step, I->stream, &st))
+        if (src->device_quant(name, r0, nr, c0, nc, dstage, dst_row_bytes, dst_row0, dst_step, I->stream, &st))
             return st;
         const uint64_t rb = m.row_bytes();
         host.resize((size_t)(nr * rb));
         JINF_CHECK(src->read_rows(name, r0, nr, host.data()), name);
         JINF_CUDA_CHECK(cudaMemcpy2DAsync(dstage + dst_row0 * dst_row_bytes, (size_t)(dst_step * dst_row_bytes),
-                                          host.data() + (c0 / 32) * 18, (size_t)rb, (size_t)(nc / 32) * 18,
+                                          host.data() + (c0 / bs) * bb, (size_t)rb, (size_t)(nc / bs) * bb,
                                           (size_t)nr, cudaMemcpyHostToDevice, I->stream));
         JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));  // `host` is reused by the next call
         return JINF_OK;
@@ -814,7 +831,7 @@ void free_impl(jinf_engine_impl* I) {
     void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
                     I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
                     I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_rec[0], I->step_rec[1],
-                    I->step_rec[2], I->step_rec[3], I->step_ss};
+                    I->step_rec[2], I->step_rec[3], I->step_ss, I->step_attn_cnt};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);
@@ -876,6 +893,17 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         JINF_LOG("head_dim %d not supported (64 or 128)", I->hd);
         return fail(JINF_ERR_INVALID);
     }
+    {
+        // the projections' quantisation: Q4_0 or Q4_K, the same for every matrix
+        TensorMeta m;
+        if (src.meta("blk.0.attn_q.weight", &m)) I->wtype = m.type;
+        if (I->wtype != JINF_TYPE_Q4_0 && I->wtype != JINF_TYPE_Q4_K) {
+            JINF_LOG("weights of type %s are not supported by the B200 engine (Q4_0 or Q4_K)",
+                     jinf_qtype_name((jinf_qtype)I->wtype));
+            return fail(JINF_ERR_INVALID);
+        }
+        I->wfmt = I->wtype == JINF_TYPE_Q4_K ? Q4M_Q4_K : Q4M_Q4_0;
+    }
     if (I->H / I->Hkv > 8) {
         JINF_LOG("more than 8 query heads per kv head are not supported");
         return fail(JINF_ERR_INVALID);
@@ -895,7 +923,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     I->layers.resize(I->L);
     uint64_t off = 0;
     auto place = [&](Q4MShape& sh, int rows, int cols, uint8_t*& ptr) -> bool {
-        if (!q4m_shape(rows, cols, &sh) || cols > gemvm_max_cols()) return false;
+        if (!q4m_shape(rows, cols, &sh, I->wfmt) || cols > gemvm_max_cols(I->wfmt)) return false;
         ptr = (uint8_t*)(uintptr_t)off;  // offset for now
         off += (sh.bytes + 255) & ~255ull;
         I->weight_bytes_token += (uint64_t)rows * (cols / 32) * 18;
@@ -905,7 +933,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         auto& ly = I->layers[L];
         if (!place(ly.qkv_sh, qkv_rows, d, ly.qkv) || !place(ly.o_sh, d, I->Hl * hd, ly.o) ||
             !place(ly.gu_sh, 2 * I->ffl, d, ly.gu) || !place(ly.down_sh, d, I->ffl, ly.down)) {
-            JINF_LOG("matrix shapes not supported by the Q4M layout (columns must be whole 32-element blocks)");
+            JINF_LOG("matrix shapes not supported by the Q4M layout (columns must be whole %d-element blocks)",
+                     I->wfmt == Q4M_Q4_K ? 256 : 32);
             return fail(JINF_ERR_INVALID);
         }
     }
@@ -964,7 +993,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
                 max_stage = std::max(max_stage, (size_t)sh->rows * (sh->cols / 32) * 18);
         max_stage = std::max(max_stage, (size_t)I->lm_sh.rows * (I->lm_sh.cols / 32) * 18);
         if (ld.ensure_dstage(max_stage) != JINF_OK) return fail(JINF_ERR_OOM);
-        const int64_t rb_d = (int64_t)(d / 32) * 18;  // AoS row bytes of a d-column matrix
+        // AoS row bytes of a d-column matrix (Q4_0 and Q4_K both take 9/16 byte per weight)
+        const int64_t rb_d = (int64_t)(d / 32) * 18;
         char nm[128];
         jinf_status s = JINF_OK;
         for (int L = 0; L < I->L && s == JINF_OK; ++L) {

@@ -26,6 +26,7 @@ enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3, EPI_R
 struct GemvParams {
     const uint8_t* w;  // Q4M stream of the matrix
     int rows, cols, pairs, groups;
+    int fmt;                // Q4MFormat of w
     int kw;                 // K parts per tile pair (tasks per pair)
     float* part;            // kw > 1: [pairs * kw][32] partial row sums
     unsigned int* cnt;      // kw > 1: [pairs] arrival counters, zero before the first launch (self-resetting)
@@ -56,16 +57,17 @@ inline void gemvm_params_for(GemvParams& p, const void* w, const Q4MShape& sh) {
     p.cols = sh.cols;
     p.pairs = sh.pairs;
     p.groups = sh.groups;
+    p.fmt = sh.fmt;
     p.kw = 1;
 }
-size_t gemvm_smem_bytes(int cols);
-int gemvm_max_cols();
+size_t gemvm_smem_bytes(int cols, int fmt = Q4M_Q4_0);
+int gemvm_max_cols(int fmt = Q4M_Q4_0);
 // Persistent grid: resident CTAs per SM * num_sms.
-int gemvm_grid(int cols, int xm, int epi, int num_sms);
+int gemvm_grid(int cols, int xm, int epi, int num_sms, int fmt = Q4M_Q4_0);
 // K parts per tile pair for a grid of `grid` CTAs (1 <= kw <= min(groups, max_kw)).
 int gemvm_pick_kw(int pairs, int groups, int grid, int max_kw);
 cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
-// AoS Q4_0 [rows][cols] (device) -> Q4M (device, sh.bytes).
+// AoS Q4_0 or Q4_K (sh.fmt) [rows][cols] (device) -> Q4M (device, sh.bytes).
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s);
 
 }  // namespace jinf

@@ -44,15 +44,16 @@ __device__ __forceinline__ void l2_prefetch(const uint8_t* p, uint64_t bytes) {
 
 }  // namespace
 
-template <int XM, int EPI>
+template <int XM, int EPI, int FMT>
 __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p) {
+    constexpr int UB = FMT == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT;  // unit bytes
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int G = p.groups;
     uint8_t* rec = smem_raw;                                                     // input digit records
     float* misc = reinterpret_cast<float*>(smem_raw + xrec_bytes(G));           // 64 floats
     const uint32_t ring0 = smem_u32(misc + 64);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * Q4M_UNIT);
+    const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * UB);
     const int kw = p.kw;
     const int T = p.pairs * kw;  // tasks: (tile pair, K part)
     const int W = gridDim.x * NW;
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     auto issue = [&](int slot) {
         if (ctask < T) {
             const int pair = ctask / kw;
-            copy_unit_async(ring + slot * Q4M_UNIT, p.w + ((size_t)pair * G + cg) * Q4M_UNIT, lane);
+            copy_unit_fmt<FMT>(ring + slot * UB, p.w + ((size_t)pair * G + cg) * UB, lane);
             if (++cg == cge) {
                 ctask += W;
                 if (ctask < T) {
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
         for (int g = g0; g < g1; ++g) {
             issue(slot == 0 ? GEMV_M_NBUF - 1 : slot - 1);
             asm volatile("cp.async.wait_group %0;" ::"n"(GEMV_M_NBUF - 1) : "memory");
-            unit_mma(ring + slot * Q4M_UNIT, xr, g, lane, acc);
+            unit_mma_fmt<FMT>(ring + slot * UB, xr, g, lane, acc);
             slot = slot + 1 == GEMV_M_NBUF ? 0 : slot + 1;
         }
         unit_reduce(acc);
@@ -220,37 +221,96 @@ __global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restric
     }
 }
 
-// ---------------------------------------------------------------- host side
-
-size_t gemvm_smem_bytes(int cols) {
-    const int G = (cols + Q4M_KG - 1) / Q4M_KG;
-    return xrec_bytes(G) + sizeof(float) * 64 + (size_t)NW * GEMV_M_NBUF * Q4M_UNIT;
+// One thread per (pair, group, lane) of a Q4_K matrix (AoS super-blocks of 144 bytes,
+// [rows][nsb]): the unit's nibble words (group G = sub-blocks 4 (G % 2) + j of super-block
+// G / 2), the lane's sc | m words, and lanes 0..15 / 16..31 the d, dmin of tile A / B row
+// lane % 16 (q4m.cuh). The 6-bit sc and m unpacking follows reference src/quant.cpp:71-77.
+__global__ void k_repack_q4mk(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
+                              int pairs, int nsb) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)pairs * groups * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t pg = gid >> 5;
+    const int p = (int)(pg / groups), G = (int)(pg % groups);
+    const int gr = lane >> 2, c = lane & 3, sbk = G >> 1, half = G & 1;
+    auto block = [&](int r) -> const uint8_t* {  // super-block sbk of pair row r
+        const int row = p * Q4M_PAIR_ROWS + r;
+        return row < rows && sbk < nsb ? aos + ((size_t)row * nsb + sbk) * 144 : nullptr;
+    };
+    auto nib = [&](const uint8_t* blk, int sb, int k) -> uint32_t {
+        if (!blk) return 0u;
+        const uint8_t byte = blk[16 + sb * 16 + (k >> 1)];
+        return (k & 1) ? (uint32_t)(byte >> 4) : (uint32_t)(byte & 15);
+    };
+    auto scm = [&](const uint8_t* blk, int sb) -> uint32_t {  // sc | m << 8 of sub-block sb
+        if (!blk) return 0u;
+        const uint8_t* s = blk + 4;
+        uint32_t sc, m;
+        if (sb < 4) {
+            sc = s[sb] & 0x3F;
+            m = s[sb + 4] & 0x3F;
+        } else {
+            sc = (uint32_t)((s[sb + 4] & 0x0F) << 2) | (uint32_t)(s[sb - 4] >> 6);
+            m = (uint32_t)((s[sb + 4] >> 4) << 2) | (uint32_t)(s[sb] >> 6);
+        }
+        return sc | (m << 8);
+    };
+    uint8_t* unit = dst + q4m_unit_offset(p, G, groups, Q4M_Q4_K);
+    for (int j = 0; j < 4; ++j)
+        for (int i = 0; i < 4; ++i) {
+            const int rt = gr + 8 * (i & 1);
+            const uint8_t* a = block(rt);
+            const uint8_t* b = block(16 + rt);
+            const int sb = 4 * half + j;
+            uint32_t word = 0;
+            for (int t = 0; t < 4; ++t) {
+                const int k = 16 * (i >> 1) + 4 * c + t;
+                word |= (nib(a, sb, k) | (nib(b, sb, k) << 4)) << (8 * t);
+            }
+            *reinterpret_cast<uint32_t*>(unit + 512 * j + 16 * lane + 4 * i) = word;
+        }
+    for (int t = 0; t < 2; ++t)
+        *reinterpret_cast<uint32_t*>(unit + Q4M_SCALES + 128 * t + 4 * lane) =
+            scm(block(16 * t + gr), 4 * half + c) | (scm(block(16 * t + gr + 8), 4 * half + c) << 16);
+    const uint8_t* own = block(lane);  // tile A rows 0..15, tile B rows 16..31
+    const uint32_t dd = own ? (uint32_t)own[0] | ((uint32_t)own[1] << 8) | ((uint32_t)own[2] << 16) |
+                                  ((uint32_t)own[3] << 24)
+                            : 0u;
+    *reinterpret_cast<uint32_t*>(unit + Q4M_DMIN_K + 4 * lane) = dd;
 }
 
-int gemvm_max_cols() {
+// ---------------------------------------------------------------- host side
+
+size_t gemvm_smem_bytes(int cols, int fmt) {
+    const int G = (cols + Q4M_KG - 1) / Q4M_KG;
+    return xrec_bytes(G) + sizeof(float) * 64 + (size_t)NW * GEMV_M_NBUF * q4m_unit_bytes(fmt);
+}
+
+int gemvm_max_cols(int fmt) {
     // largest multiple of 128 whose staging fits next to the ring in the 227 KB per CTA
     int c = 128;
-    while (gemvm_smem_bytes(c + 128) <= 226 * 1024) c += 128;  // static shared memory rides along
+    while (gemvm_smem_bytes(c + 128, fmt) <= 226 * 1024) c += 128;  // static shared memory rides along
     return c;
 }
 
-template <int XM, int EPI>
+template <int XM, int EPI, int FMT>
 struct GemvMKernelInfo {
     static cudaError_t ensure_smem(size_t smem) {
         static size_t configured = 0;
         if (smem <= configured) return cudaSuccess;
-        const size_t want = gemvm_smem_bytes(gemvm_max_cols());
-        cudaError_t e = cudaFuncSetAttribute(k_gemv_q4m<XM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+        const size_t want = gemvm_smem_bytes(gemvm_max_cols(FMT), FMT);
+        cudaError_t e =
+            cudaFuncSetAttribute(k_gemv_q4m<XM, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
         if (e == cudaSuccess) configured = want;
         return e;
     }
     static int occupancy(int cols) {
         static int cached_cols = -1, cached_occ = 1;
         if (cached_cols != cols) {
-            const size_t smem = gemvm_smem_bytes(cols);
+            const size_t smem = gemvm_smem_bytes(cols, FMT);
             ensure_smem(smem);
             int n = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv_q4m<XM, EPI>, GEMV_M_THREADS, smem) !=
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv_q4m<XM, EPI, FMT>, GEMV_M_THREADS, smem) !=
                     cudaSuccess ||
                 n < 1)
                 n = 1;
@@ -260,7 +320,7 @@ struct GemvMKernelInfo {
         return cached_occ;
     }
     static cudaError_t launch(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-        const size_t smem = gemvm_smem_bytes(p.cols);
+        const size_t smem = gemvm_smem_bytes(p.cols, FMT);
         cudaError_t e = ensure_smem(smem);
         if (e != cudaSuccess) return e;
         cudaLaunchConfig_t cfg = {};
@@ -273,34 +333,40 @@ struct GemvMKernelInfo {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = pdl ? 1 : 0;
-        return cudaLaunchKernelEx(&cfg, k_gemv_q4m<XM, EPI>, p);
+        return cudaLaunchKernelEx(&cfg, k_gemv_q4m<XM, EPI, FMT>, p);
     }
 };
 
-template <int XM, int EPI>
-static int occ_m(int cols) { return GemvMKernelInfo<XM, EPI>::occupancy(cols); }
-template <int XM, int EPI>
+template <int XM, int EPI, int FMT>
+static int occ_m(int cols) { return GemvMKernelInfo<XM, EPI, FMT>::occupancy(cols); }
+template <int XM, int EPI, int FMT>
 static cudaError_t launch_m(const GemvParams& p, int grid, cudaStream_t s, bool pdl) {
-    return GemvMKernelInfo<XM, EPI>::launch(p, grid, s, pdl);
+    return GemvMKernelInfo<XM, EPI, FMT>::launch(p, grid, s, pdl);
 }
 
-#define JINF_GEMVM_DISPATCH(FN, ...)                                                    \
-    switch (xm * 16 + epi) {                                                            \
-        case X_PLAIN_F32 * 16 + EPI_STORE:   return FN<X_PLAIN_F32, EPI_STORE>(__VA_ARGS__);   \
-        case X_PLAIN_F16 * 16 + EPI_STORE:   return FN<X_PLAIN_F16, EPI_STORE>(__VA_ARGS__);   \
-        case X_RMSNORM * 16 + EPI_STORE:     return FN<X_RMSNORM, EPI_STORE>(__VA_ARGS__);     \
-        case X_RMSNORM * 16 + EPI_QKV:       return FN<X_RMSNORM, EPI_QKV>(__VA_ARGS__);       \
-        case X_EMBED_NORM * 16 + EPI_QKV:    return FN<X_EMBED_NORM, EPI_QKV>(__VA_ARGS__);    \
-        case X_RMSNORM * 16 + EPI_GATEUP:    return FN<X_RMSNORM, EPI_GATEUP>(__VA_ARGS__);    \
-        case X_PLAIN_F32 * 16 + EPI_GATEUP:  return FN<X_PLAIN_F32, EPI_GATEUP>(__VA_ARGS__);  \
-        case X_RMSNORM * 16 + EPI_LMHEAD:    return FN<X_RMSNORM, EPI_LMHEAD>(__VA_ARGS__);    \
-        case X_PLAIN_F32 * 16 + EPI_LMHEAD:  return FN<X_PLAIN_F32, EPI_LMHEAD>(__VA_ARGS__);  \
-        default: break;                                                                 \
+#define JINF_GEMVM_CASES(FN, F, ...)                                                                   \
+    switch (xm * 16 + epi) {                                                                           \
+        case X_PLAIN_F32 * 16 + EPI_STORE:   return FN<X_PLAIN_F32, EPI_STORE, F>(__VA_ARGS__);   \
+        case X_PLAIN_F16 * 16 + EPI_STORE:   return FN<X_PLAIN_F16, EPI_STORE, F>(__VA_ARGS__);   \
+        case X_RMSNORM * 16 + EPI_STORE:     return FN<X_RMSNORM, EPI_STORE, F>(__VA_ARGS__);     \
+        case X_RMSNORM * 16 + EPI_QKV:       return FN<X_RMSNORM, EPI_QKV, F>(__VA_ARGS__);       \
+        case X_EMBED_NORM * 16 + EPI_QKV:    return FN<X_EMBED_NORM, EPI_QKV, F>(__VA_ARGS__);    \
+        case X_RMSNORM * 16 + EPI_GATEUP:    return FN<X_RMSNORM, EPI_GATEUP, F>(__VA_ARGS__);    \
+        case X_PLAIN_F32 * 16 + EPI_GATEUP:  return FN<X_PLAIN_F32, EPI_GATEUP, F>(__VA_ARGS__);  \
+        case X_RMSNORM * 16 + EPI_LMHEAD:    return FN<X_RMSNORM, EPI_LMHEAD, F>(__VA_ARGS__);    \
+        case X_PLAIN_F32 * 16 + EPI_LMHEAD:  return FN<X_PLAIN_F32, EPI_LMHEAD, F>(__VA_ARGS__);  \
+        default: break;                                                                                \
+    }
+#define JINF_GEMVM_DISPATCH(FMTV, FN, ...)                  \
+    if ((FMTV) == Q4M_Q4_K) {                               \
+        JINF_GEMVM_CASES(FN, Q4M_Q4_K, __VA_ARGS__)         \
+    } else {                                                \
+        JINF_GEMVM_CASES(FN, Q4M_Q4_0, __VA_ARGS__)         \
     }
 
-int gemvm_grid(int cols, int xm, int epi, int num_sms) {
+int gemvm_grid(int cols, int xm, int epi, int num_sms, int fmt) {
     auto occ_fn = [&]() -> int {
-        JINF_GEMVM_DISPATCH(occ_m, cols)
+        JINF_GEMVM_DISPATCH(fmt, occ_m, cols)
         return 1;
     };
     return occ_fn() * num_sms;
@@ -327,15 +393,19 @@ int gemvm_pick_kw(int pairs, int groups, int grid, int max_kw) {
 
 cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl) {
     if (p.kw < 1 || p.kw > p.groups || (p.kw > 1 && (!p.part || !p.cnt))) return cudaErrorInvalidValue;
-    if (p.cols > gemvm_max_cols()) return cudaErrorInvalidValue;
-    JINF_GEMVM_DISPATCH(launch_m, p, grid, s, pdl)
+    if (p.cols > gemvm_max_cols(p.fmt)) return cudaErrorInvalidValue;
+    JINF_GEMVM_DISPATCH(p.fmt, launch_m, p, grid, s, pdl)
     return cudaErrorInvalidValue;
 }
 
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s) {
     const int64_t n = (int64_t)sh.pairs * sh.groups * 32;
-    k_repack_q4m<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows, sh.groups,
-                                                             sh.pairs, sh.cols / 32);
+    if (sh.fmt == Q4M_Q4_K)
+        k_repack_q4mk<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows,
+                                                                  sh.groups, sh.pairs, sh.cols / 256);
+    else
+        k_repack_q4m<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows,
+                                                                 sh.groups, sh.pairs, sh.cols / 32);
     return cudaGetLastError();
 }
 

@@ -25,6 +25,17 @@
 //
 // Block element e = 2i of the reference block is the low nibble of qs byte i, e = 2i+1 the
 // high nibble (reference src/quant.cpp:49-60, cuda/matmul_kernels.cu:27-34).
+//
+// Q4_K matrices (reference include/jinf/quant.h:38-46: 256-element super-blocks, d and dmin
+// in fp16, a 6-bit scale sc and min m per 32-element sub-block, w = d sc q - dmin m) use
+// the same unit with a larger scale area (Q4M_UNIT_K = 2432 bytes): the four blocks of
+// group G are sub-blocks 4 (G % 2) + j of super-block G / 2, their nibbles laid out as above,
+// then
+//   bytes 2048 .. 2175   [32 lanes][2 x u16]   tile A: sc | m << 8 of (row gr, block c), (row gr+8, block c)
+//   bytes 2176 .. 2303   [32 lanes][2 x u16]   tile B: the same for rows 16+gr, 24+gr
+//   bytes 2304 .. 2367   [16 rows][fp16 d, fp16 dmin]   tile A rows 0..15
+//   bytes 2368 .. 2431   [16 rows][fp16 d, fp16 dmin]   tile B rows 16..31
+// (d, dmin repeat in both units of a super-block). Q4_K columns are whole super-blocks.
 #pragma once
 
 #include <stdint.h>
@@ -36,11 +47,18 @@ constexpr int Q4M_KG = 128;              // columns per group
 constexpr int Q4M_UNIT = 2304;           // bytes per (tile pair, group)
 constexpr int Q4M_SCALES = 2048;         // byte offset of the scales in a unit
 constexpr int Q4M_PAIR_ROWS = 2 * Q4M_ROWS;
+constexpr int Q4M_UNIT_K = 2432;         // bytes per (tile pair, group) of a Q4_K matrix
+constexpr int Q4M_DMIN_K = 2304;         // byte offset of the per-row d, dmin in a Q4_K unit
+
+// Weight formats of a Q4M matrix
+enum Q4MFormat { Q4M_Q4_0 = 0, Q4M_Q4_K = 1 };
+__host__ __device__ constexpr inline int q4m_unit_bytes(int fmt) { return fmt == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT; }
 
 struct Q4MShape {
     int rows, cols;
     int pairs;   // ceil(rows / 32)
     int groups;  // ceil(cols / 128)
+    int fmt;     // Q4MFormat
     uint64_t bytes;
 };
 
@@ -51,20 +69,21 @@ struct Q4MShape {
 __host__ __device__ inline size_t xrec_bytes(int groups) { return (size_t)groups * 320; }
 
 // Byte offset of the unit of pair p, group g.
-__host__ __device__ inline uint64_t q4m_unit_offset(int p, int g, int groups) {
-    return ((uint64_t)p * groups + g) * Q4M_UNIT;
+__host__ __device__ inline uint64_t q4m_unit_offset(int p, int g, int groups, int fmt = Q4M_Q4_0) {
+    return ((uint64_t)p * groups + g) * q4m_unit_bytes(fmt);
 }
 
 // cols must be whole Q4_0 blocks (a multiple of 32); the last group is padded with zero
 // blocks (scale 0) when cols is not a multiple of 128, and the GEMV stages zero digits for
 // x there.
-inline bool q4m_shape(int rows, int cols, Q4MShape* s) {
-    if (rows <= 0 || cols <= 0 || cols % 32) return false;
+inline bool q4m_shape(int rows, int cols, Q4MShape* s, int fmt = Q4M_Q4_0) {
+    if (rows <= 0 || cols <= 0 || cols % (fmt == Q4M_Q4_K ? 256 : 32)) return false;
     s->rows = rows;
     s->cols = cols;
     s->pairs = (rows + Q4M_PAIR_ROWS - 1) / Q4M_PAIR_ROWS;
     s->groups = (cols + Q4M_KG - 1) / Q4M_KG;
-    s->bytes = (uint64_t)s->pairs * s->groups * Q4M_UNIT;
+    s->fmt = fmt;
+    s->bytes = (uint64_t)s->pairs * s->groups * q4m_unit_bytes(fmt);
     return true;
 }
 

@@ -51,6 +51,28 @@ __device__ __forceinline__ void copy_unit_async(uint32_t slot, const uint8_t* un
                  : "memory");
 }
 
+// This lane's share of a 2432-byte Q4_K unit: its nibble words (as Q4_0), and lanes 0..23
+// one 16-byte piece of the 384-byte scale area each. The scale area is read across lanes,
+// so the consumer synchronises the warp after waiting for the copies (unit_mma_k).
+__device__ __forceinline__ void copy_unit_k_async(uint32_t slot, const uint8_t* unit, int lane) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + 512 * j + lane * 16),
+                     "l"(unit + 512 * j + lane * 16)
+                     : "memory");
+    if (lane < 24)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + Q4M_SCALES + lane * 16),
+                     "l"(unit + Q4M_SCALES + lane * 16)
+                     : "memory");
+}
+
+// The copy routine of a unit of format `fmt` (q4m.cuh).
+template <int FMT>
+__device__ __forceinline__ void copy_unit_fmt(uint32_t slot, const uint8_t* unit, int lane) {
+    if (FMT == Q4M_Q4_K) copy_unit_k_async(slot, unit, lane);
+    else copy_unit_async(slot, unit, lane);
+}
+
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -104,6 +126,62 @@ __device__ __forceinline__ void unit_mma(uint32_t sl, const XRecS& xr, int g, in
     acc[1] = fmaf(jinf_h2f((uint16_t)(sca >> 16)) * ia, (float)(da[2] * 256 + da[3]), acc[1]);
     acc[2] = fmaf(jinf_h2f((uint16_t)(scb & 0xffffu)) * ib, (float)(db[0] * 256 + db[1]), acc[2]);
     acc[3] = fmaf(jinf_h2f((uint16_t)(scb >> 16)) * ib, (float)(db[2] * 256 + db[3]), acc[3]);
+}
+
+// unit_mma for a Q4_K unit (q4m.cuh): the accumulators start at zero (the weights are
+// d sc q - dmin m, no zero point), and block c of row r contributes
+// (d sc (256 D_hi + D_lo) - dmin m (256 S_hi + S_lo)) / alpha, S the block's digit sums
+// (recovered exactly from the record's zero-point params, -8 S). The warp synchronises
+// before (its lanes read scale words other lanes copied) and after (before a lane copies
+// the next unit into the slot).
+__device__ __forceinline__ void unit_mma_k(uint32_t sl, const XRecS& xr, int g, int lane, float (&acc)[4]) {
+    __syncwarp();
+    uint32_t w[16], sca, scb, b0, b1, dA0, dA1, dB0, dB1;
+    int kh, kl;
+    float ia, ib;
+    const int gr = lane >> 2;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[4 * j]), "=r"(w[4 * j + 1]), "=r"(w[4 * j + 2]), "=r"(w[4 * j + 3])
+                     : "r"(sl + 512 * j + lane * 16));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(sca) : "r"(sl + Q4M_SCALES + lane * 4));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(scb) : "r"(sl + Q4M_SCALES + 128 + lane * 4));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dA0) : "r"(sl + Q4M_DMIN_K + gr * 4));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dA1) : "r"(sl + Q4M_DMIN_K + (gr + 8) * 4));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dB0) : "r"(sl + Q4M_DMIN_K + 64 + gr * 4));
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dB1) : "r"(sl + Q4M_DMIN_K + 64 + (gr + 8) * 4));
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xr.dig + g * 256 + lane * 8));
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(kh), "=r"(kl), "=f"(ia), "=f"(ib)
+                 : "r"(xr.prm + (g * 4 + (lane & 3)) * 16));
+    const int myblk = lane >> 3;
+    int da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t x0 = myblk == j ? b0 : 0u, x1 = myblk == j ? b1 : 0u;
+        mma_u8s8(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), x0, x1, da);
+        mma_u8s8(nib_hi(w[4 * j]), nib_hi(w[4 * j + 1]), nib_hi(w[4 * j + 2]), nib_hi(w[4 * j + 3]), x0, x1, db);
+    }
+    const float S = (float)(-((kh << 8) + kl) >> 3);  // 256 S_hi + S_lo of block c (exact)
+    // tile B's block sums carry the 16 of its high-nibble operand: its min term is taken
+    // x16 too and the whole row scaled by 1/(16 alpha) (powers of two: exact)
+    auto row = [&](uint32_t scm, uint32_t dd, float dsum, float s) {
+        const float sub_d = jinf_h2f((uint16_t)(dd & 0xffffu)) * (float)(scm & 63u);
+        const float sub_m = jinf_h2f((uint16_t)(dd >> 16)) * (float)((scm >> 8) & 63u);
+        return fmaf(sub_d, dsum, -sub_m * s);
+    };
+    acc[0] = fmaf(row(sca & 0xffffu, dA0, (float)(da[0] * 256 + da[1]), S), ia, acc[0]);
+    acc[1] = fmaf(row(sca >> 16, dA1, (float)(da[2] * 256 + da[3]), S), ia, acc[1]);
+    acc[2] = fmaf(row(scb & 0xffffu, dB0, (float)(db[0] * 256 + db[1]), 16.0f * S), ib, acc[2]);
+    acc[3] = fmaf(row(scb >> 16, dB1, (float)(db[2] * 256 + db[3]), 16.0f * S), ib, acc[3]);
+    __syncwarp();  // every lane's reads of the slot precede the next copy into it
+}
+
+template <int FMT>
+__device__ __forceinline__ void unit_mma_fmt(uint32_t sl, const XRecS& xr, int g, int lane, float (&acc)[4]) {
+    if (FMT == Q4M_Q4_K) unit_mma_k(sl, xr, g, lane, acc);
+    else unit_mma(sl, xr, g, lane, acc);
 }
 
 // Sum the four accumulators over the lanes of a row group (blocks c = 0..3): afterwards

@@ -38,6 +38,7 @@ struct StepPhase {
     unsigned int dep_target;
     int gran;                // a CTA owns whole runs of `gran` tile pairs (2: its gate|up rows
                              // make whole 32-element blocks of the activation)
+    int layer;               // PH_ATTN: layer index (selects its split arrival counters)
     int pf[2];               // GEMV phases (-1: none) whose weights this CTA owns are prefetched
                              // into L2 when the CTA reaches this phase (before its wait)
     // PH_GEMV
@@ -73,11 +74,14 @@ struct StepParams {
     int n_phases;
     unsigned int* done;       // [n_phases + 1] zero at launch; [n_phases] counts exiting CTAs
     float* attn_part;         // [Hkv][ATTN_MAX_SPLIT][ATTN_MAX_GROUP][hd + 2] per-CTA attention partials
+    unsigned int* attn_cnt;   // [layers][Hkv] split arrival counters, zero at launch (cleared at the end)
+    int n_attn_cnt;
     DeviceState* st;
     int nq, nk, head_dim, max_ctx, n_heads, n_kv_heads;
     float rope_base, eps;
     int attn_smax;            // CTAs per kv head at most (grid / kv heads, <= ATTN_MAX_SPLIT)
     int with_argmax;          // the last phase is the LM head: finish the argmax, feed it back
+    int fmt;                  // Q4MFormat of every weight matrix of the step
     unsigned int xstage_bytes;  // shared bytes for the staged GEMV input / attention scratch
     unsigned long long spin_limit;  // polls before a dependency wait gives up (DEV_ERR_TIMEOUT)
 };
@@ -89,10 +93,10 @@ __host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)
 // Shared bytes of the staged input for the widest GEMV phase, or of the attention scratch
 // (q of one kv head's query heads + per-warp partials), whichever is larger.
 unsigned int step_xstage_bytes(int max_cols, int group, int head_dim);
-size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases);
+size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt);
 // Launches the step on `grid` CTAs (one per SM) as a cooperative launch.
 cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s);
 // Resident CTAs per SM for this shared-memory size (must be >= 1).
-int step_occupancy(size_t smem);
+int step_occupancy(size_t smem, int fmt);
 
 }  // namespace jinf

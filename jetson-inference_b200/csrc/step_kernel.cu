@@ -162,13 +162,13 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
 // Bring the units that CTA `cta` owns in GEMV phase `pi` (one contiguous byte range: whole
 // tile pairs, all groups) into L2. Issued while the CTA would otherwise wait on a dependency,
 // so that HBM keeps streaming weights through attention, input staging and merges.
-__device__ __noinline__ void prefetch_cta_range(const PhaseInfo& pi, int cta, int C) {
+__device__ __noinline__ void prefetch_cta_range(const PhaseInfo& pi, int cta, int C, int ub) {
     if (!pi.groups) return;
     int t0, t1;
     cta_range(cta, C, pi.pairs, pi.gran, t0, t1);
     if (t0 >= t1) return;
-    const uint8_t* b = pi.w + (size_t)t0 * pi.groups * Q4M_UNIT;
-    const uint32_t bytes = (uint32_t)(t1 - t0) * (uint32_t)pi.groups * (uint32_t)Q4M_UNIT;  // multiple of 16
+    const uint8_t* b = pi.w + (size_t)t0 * pi.groups * ub;
+    const uint32_t bytes = (uint32_t)(t1 - t0) * (uint32_t)pi.groups * (uint32_t)ub;  // multiple of 16
     for (uint32_t off = 0; off < bytes; off += (1u << 20))
         prefetch_l2(b + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
 }
@@ -187,6 +187,7 @@ struct PieceSum {
 // Consume groups [gb, ge) of one tile pair from the ring (tensor-core decode, q4m_device.cuh),
 // refilling it as it goes. Out of line so that the hot loop gets a register allocation of
 // its own, independent of the rest of the step kernel.
+template <int FMT>
 __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, const PhaseInfo* pinfo, int n_phases,
                                               int C, const XRecS xr, int gb, int ge) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -196,12 +197,12 @@ __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, con
     for (int g = gb; g < ge; ++g) {
         const int is = slot == 0 ? STEP_NBUF - 1 : slot - 1;
         if (sp.c < sp.c1) {
-            copy_unit_async(ring + is * Q4M_UNIT, sp.w + (size_t)sp.c * Q4M_UNIT, lane);
+            copy_unit_fmt<FMT>(ring + is * q4m_unit_bytes(FMT), sp.w + (size_t)sp.c * q4m_unit_bytes(FMT), lane);
             if (++sp.c == sp.c1) sp = stream_seek(pinfo, n_phases, sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
         asm volatile("cp.async.wait_group %0;" ::"n"(STEP_NBUF - 1) : "memory");
-        unit_mma(ring + slot * Q4M_UNIT, xr, g, lane, r.acc);
+        unit_mma_fmt<FMT>(ring + slot * q4m_unit_bytes(FMT), xr, g, lane, r.acc);
         slot = slot + 1 == STEP_NBUF ? 0 : slot + 1;
     }
     ws.sp = sp;
@@ -324,23 +325,29 @@ __device__ __forceinline__ bool attn_geom(int pos, int n_kv_heads, int s_max, in
 // in `outs` ([gq][HD], shared memory; `part` null) or the split's partial (acc, m, l) in
 // `part` ([gq][HD + 2], global). Cache rows come in by bulk copy on `mbar` (`par` is its
 // next phase); chunk 0's rows before `pos` were requested before the QKV wait (`pre`).
-template <int HD>
+template <int HD, int GQ>
 __device__ __noinline__ void attn_split(const float* q, const __half* kb, const __half* vb, int p0, int p1, int pos,
-                                        int gq, uint8_t* xbase, float* part, float* outs, uint32_t mbar, uint32_t& par,
-                                        bool pre, DeviceState* st, unsigned long long limit) {
-    constexpr int DPL = HD / 32;
+                                        uint8_t* xbase, float* part, float* outs, uint32_t mbar, uint32_t& par, bool pre,
+                                        DeviceState* st, unsigned long long limit) {
+    constexpr int gq = GQ;
+    constexpr int DG = 32 / GQ;  // lanes per query head in q.k
+    constexpr int D = HD / DG;   // head dims per lane in q.k
+    static_assert(D % 8 == 0 || D == 4 || D == 2, "q.k dims per lane");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int qg = lane / DG, dgi = lane % DG;
     const uint32_t kv_s = smem_u32(xbase);
     const __half* kvh_s = reinterpret_cast<const __half*>(xbase);         // [2][ATTN_CHUNK][HD]
     float* w_s = reinterpret_cast<float*>(xbase + 2 * ATTN_CHUNK * HD * 2);  // [gq][ATTN_CHUNK]
     float* ml_s = w_s + ATTN_MAX_GROUP * ATTN_CHUNK;                         // [gq][3]: m, l, correction
     const float scale = rsqrtf((float)HD);
-    // this lane's head dims of every query head (pre-scaled)
-    float qr[ATTN_MAX_GROUP][DPL];
+    // this lane's dims [dgi D, dgi D + D) of query head qg (pre-scaled)
+    float qr[D];
 #pragma unroll
-    for (int g = 0; g < ATTN_MAX_GROUP; ++g)
-#pragma unroll
-        for (int k = 0; k < DPL; ++k) qr[g][k] = g < gq ? __ldcg(q + g * HD + lane * DPL + k) * scale : 0.f;
+    for (int k = 0; k < D; k += 2) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(q + qg * HD + dgi * D + k));
+        qr[k] = v.x * scale;
+        qr[k + 1] = v.y * scale;
+    }
     if (tid < gq) {
         ml_s[tid * 3] = -INFINITY;
         ml_s[tid * 3 + 1] = 0.f;
@@ -374,25 +381,34 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
             par ^= 1u;
         }
         __syncthreads();
-        // q.k: warp w takes positions w, w + 16; lanes own head dims
+        // q.k: warp w takes positions w, w + 16; lane (qg, dgi) sums D dims of query head qg,
+        // then the DG lanes of the head reduce
         for (int j = warp; j < n; j += NW) {
-            float kf[DPL];
-            const __half2* kr = reinterpret_cast<const __half2*>(kvh_s + j * HD + lane * DPL);
+            const __half* krow = kvh_s + j * HD + dgi * D;
+            float a = 0.f;
+            if constexpr (D % 8 == 0) {
 #pragma unroll
-            for (int k = 0; k < DPL / 2; ++k) {
-                const float2 t = __half22float2(kr[k]);
-                kf[2 * k] = t.x;
-                kf[2 * k + 1] = t.y;
+                for (int k = 0; k < D / 8; ++k) {
+                    const uint4 raw = reinterpret_cast<const uint4*>(krow)[k];
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float2 f = __half22float2(h2[t]);
+                        a = fmaf(qr[8 * k + 2 * t], f.x, a);
+                        a = fmaf(qr[8 * k + 2 * t + 1], f.y, a);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < D / 2; ++t) {
+                    const float2 f = __half22float2(reinterpret_cast<const __half2*>(krow)[t]);
+                    a = fmaf(qr[2 * t], f.x, a);
+                    a = fmaf(qr[2 * t + 1], f.y, a);
+                }
             }
 #pragma unroll
-            for (int g = 0; g < ATTN_MAX_GROUP; ++g) {
-                if (g >= gq) break;
-                float a = 0.f;
-#pragma unroll
-                for (int k = 0; k < DPL; ++k) a = fmaf(qr[g][k], kf[k], a);
-                a = warp_sum(a);
-                if (lane == 0) w_s[g * ATTN_CHUNK + j] = a;
-            }
+            for (int o = DG / 2; o > 0; o >>= 1) a += __shfl_xor_sync(JINF_FULL_MASK, a, o);
+            if (dgi == 0) w_s[qg * ATTN_CHUNK + j] = a;
         }
         __syncthreads();
         // online softmax of the chunk, one warp per query head
@@ -446,7 +462,9 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
 
 }  // namespace
 
+template <int FMT>
 __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
+    constexpr int UB = FMT == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT;  // weight unit bytes
     extern __shared__ __align__(16) uint8_t smem[];
     // shared memory: [xstage | misc 256 B | flags, keys, piece table 512 B | partial rows 4 KB |
     //                 outputs to convert 4 KB | phase descriptor 2 x 256 B | phase infos | rings]
@@ -464,7 +482,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 8192 + 512);
     const uint32_t ring_base = smem_u32(pinfo + ((P.n_phases + 1) & ~1));
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t ring = ring_base + (uint32_t)(warp * STEP_NBUF * Q4M_UNIT);
+    const uint32_t ring = ring_base + (uint32_t)(warp * STEP_NBUF * UB);
     const int C = gridDim.x;
     DeviceState* st = P.st;
     const int pos = *(volatile int*)&st->pos;
@@ -493,7 +511,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     ws.slot = 0;
     for (int i = 0; i < STEP_NBUF - 1; ++i) {
         if (ws.sp.c < ws.sp.c1) {
-            copy_unit_async(ring + i * Q4M_UNIT, ws.sp.w + (size_t)ws.sp.c * Q4M_UNIT, lane);
+            copy_unit_fmt<FMT>(ring + i * UB, ws.sp.w + (size_t)ws.sp.c * UB, lane);
             if (++ws.sp.c == ws.sp.c1) ws.sp = stream_seek(pinfo, P.n_phases, ws.sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
@@ -515,7 +533,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             if (tid == 32 * 9) {  // L2 prefetch of later weights while warp 0 polls
                 for (int k = 0; k < 2; ++k) {
                     const int j = P.phases[ph].pf[k];
-                    if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C);
+                    if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C, UB);
                 }
             }
             AttnGeom a;
@@ -547,75 +565,92 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             float* gpart =
                 a.S > 1 ? P.attn_part + ((size_t)a.kvh * ATTN_MAX_SPLIT + a.sp) * ATTN_MAX_GROUP * (hd + 2) : nullptr;
             const bool pre = min(min(a.p0 + ATTN_CHUNK, a.p1), pos) > a.p0;  // as requested above
-            if (hd == 64)
-                attn_split<64>(qh, kb, vb, a.p0, a.p1, pos, gq, xbase, gpart, outs_s, mbar_kv, par_kv, pre, st,
-                               P.spin_limit);
-            else
-                attn_split<128>(qh, kb, vb, a.p0, a.p1, pos, gq, xbase, gpart, outs_s, mbar_kv, par_kv, pre, st,
-                                P.spin_limit);
-            bool wrote = a.S == 1;
-            if (a.S > 1) {
-                // the last split of this kv head to finish merges all splits (split order)
-                __syncthreads();
-                if (tid == 0) {
-                    __threadfence();
-                    const unsigned old = atomicAdd(&st->attn_count[a.kvh], 1u);
-                    flags[2] = old == (unsigned)(a.S - 1);
-                    if (flags[2]) {
-                        __threadfence();
-                        st->attn_count[a.kvh] = 0u;
-                    }
-                }
-                __syncthreads();
-                wrote = flags[2] != 0;
-                if (wrote) {
-                    // (m, l) of every split -> weights e^(m_s - M) / L per query head, then one pass
-                    // over the splits' accumulators (split order: deterministic)
-                    const size_t stride = (size_t)ATTN_MAX_GROUP * (hd + 2);
-                    const float* base = P.attn_part + (size_t)a.kvh * ATTN_MAX_SPLIT * stride;
-                    float* wts = reinterpret_cast<float*>(xbase);  // [S][gq][2]
-                    for (int i = tid; i < a.S * gq; i += STEP_THREADS) {
-                        const float* r = base + (i / gq) * stride + (i % gq) * (hd + 2);
-                        wts[2 * i] = __ldcg(r + hd);
-                        wts[2 * i + 1] = __ldcg(r + hd + 1);
-                    }
-                    __syncthreads();
-                    if (tid < gq) {
-                        float M = -INFINITY, L = 0.f;
-                        for (int s2 = 0; s2 < a.S; ++s2) M = fmaxf(M, wts[2 * (s2 * gq + tid)]);
-                        for (int s2 = 0; s2 < a.S; ++s2) {
-                            const float m = wts[2 * (s2 * gq + tid)];
-                            if (m != -INFINITY) L = fmaf(wts[2 * (s2 * gq + tid) + 1], expf(m - M), L);
-                        }
-                        for (int s2 = 0; s2 < a.S; ++s2) {
-                            const float m = wts[2 * (s2 * gq + tid)];
-                            wts[2 * (s2 * gq + tid)] = m == -INFINITY ? 0.f : expf(m - M) / L;
-                        }
-                    }
-                    __syncthreads();
-                    for (int i = tid; i < gq * hd; i += STEP_THREADS) {
-                        const int g = i / hd, dd = i % hd;
-                        const float* r = base + g * (hd + 2) + dd;
-                        float v = 0.f;
-#pragma unroll 8
-                        for (int s2 = 0; s2 < a.S; ++s2) v = fmaf(wts[2 * (s2 * gq + g)], __ldcg(r + s2 * stride), v);
-                        outs_s[i] = v;
-                    }
-                }
+#define JINF_ATTN_SPLIT(HD_, GQ_)                                                                            \
+    attn_split<HD_, GQ_>(qh, kb, vb, a.p0, a.p1, pos, xbase, gpart, outs_s, mbar_kv, par_kv, pre, st, \
+                         P.spin_limit)
+            if (hd == 64) {
+                if (gq == 8) JINF_ATTN_SPLIT(64, 8);
+                else if (gq == 4) JINF_ATTN_SPLIT(64, 4);
+                else if (gq == 2) JINF_ATTN_SPLIT(64, 2);
+                else JINF_ATTN_SPLIT(64, 1);
+            } else {
+                if (gq == 8) JINF_ATTN_SPLIT(128, 8);
+                else if (gq == 4) JINF_ATTN_SPLIT(128, 4);
+                else if (gq == 2) JINF_ATTN_SPLIT(128, 2);
+                else JINF_ATTN_SPLIT(128, 1);
             }
-            if (wrote) {
+#undef JINF_ATTN_SPLIT
+            const int nblk = gq * hd / 32;  // 32-element output blocks of this kv head
+            if (a.S == 1) {
                 __syncthreads();
                 if (d.rec_out) {
-                    // this kv head's outputs are whole blocks of the o projection's input
-                    blocks_to_records(outs_s, a.kvh * gq * hd / 32, gq * hd / 32, d.groups_out, d.rec_out);
+                    blocks_to_records(outs_s, a.kvh * nblk, nblk, d.groups_out, d.rec_out);
                 } else {
                     for (int i = tid; i < gq * hd; i += STEP_THREADS) d.out[(size_t)a.kvh * gq * hd + i] = outs_s[i];
                 }
                 __syncthreads();
                 if (tid == 0) {
                     __threadfence();
-                    atomicAdd(P.done + ph, 1u);
+                    atomicAdd(P.done + ph, (unsigned)nblk);
                 }
+                continue;
+            }
+            // publish this split's partial; the splits that own output blocks (split sp owns
+            // blocks sp, sp + S, ...) wait for all S partials of the kv head, then each merges its
+            // blocks in split order (deterministic) and writes them as records
+            __syncthreads();
+            unsigned* cnt = P.attn_cnt + d.layer * P.n_kv_heads + a.kvh;
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(cnt, 1u);
+            }
+            if (a.sp >= nblk) continue;
+            if (tid == 0) flags[2] = wait_ge(cnt, (unsigned)a.S, st, P.spin_limit) ? 1 : 0;
+            __syncthreads();  // (a timeout is recorded in the device state; the step is then discarded)
+            const size_t stride = (size_t)ATTN_MAX_GROUP * (hd + 2);
+            const float* base = P.attn_part + (size_t)a.kvh * ATTN_MAX_SPLIT * stride;
+            float* ml = reinterpret_cast<float*>(xbase);  // [S][2] (m, l) of the block's query head
+            float* av = ml + 2 * ATTN_MAX_SPLIT;           // [S][32] accumulators of the block
+            unsigned mine = 0;
+            for (int b = a.sp; b < nblk; b += a.S, ++mine) {
+                const int g = b * 32 / hd, dd0 = b * 32 % hd;
+                for (int t = tid; t < a.S * 32; t += STEP_THREADS)
+                    av[t] = __ldcg(base + (t >> 5) * stride + g * (hd + 2) + dd0 + (t & 31));
+                for (int t = tid; t < a.S; t += STEP_THREADS) {
+                    ml[2 * t] = __ldcg(base + t * stride + g * (hd + 2) + hd);
+                    ml[2 * t + 1] = __ldcg(base + t * stride + g * (hd + 2) + hd + 1);
+                }
+                __syncthreads();
+                if (warp == 0) {
+                    float M = -INFINITY;
+                    for (int s2 = 0; s2 < a.S; ++s2) M = fmaxf(M, ml[2 * s2]);
+                    float L = 0.f, v = 0.f;
+                    for (int s2 = 0; s2 < a.S; ++s2) {
+                        const float m = ml[2 * s2];
+                        if (m == -INFINITY) continue;  // an empty split
+                        const float e = expf(m - M);
+                        L = fmaf(ml[2 * s2 + 1], e, L);
+                        v = fmaf(e, av[s2 * 32 + lane], v);
+                    }
+                    v /= L;
+                    const int blk = a.kvh * nblk + b;  // block of the o projection's input
+                    if (d.rec_out) {
+                        // octet layout: lane q < 8 takes elements 4q .. 4q+3
+                        const int src = 4 * (lane & 7);
+                        const float4 x = make_float4(__shfl_sync(JINF_FULL_MASK, v, src), __shfl_sync(JINF_FULL_MASK, v, src + 1),
+                                                     __shfl_sync(JINF_FULL_MASK, v, src + 2), __shfl_sync(JINF_FULL_MASK, v, src + 3));
+                        uint32_t* dig = reinterpret_cast<uint32_t*>(d.rec_out);
+                        float4* prm = reinterpret_cast<float4*>(d.rec_out + (size_t)d.groups_out * 256);
+                        octet_to_records(x, lane, blk & 3, dig + (blk >> 2) * 64, prm + (blk >> 2) * 4, lane < 8);
+                    } else {
+                        d.out[(size_t)blk * 32 + lane] = v;
+                    }
+                }
+                __syncthreads();  // the scratch is reused by the next block
+            }
+            if (tid == 0) {
+                __threadfence();
+                atomicAdd(P.done + ph, mine);
             }
             continue;
         }
@@ -689,7 +724,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         int pair = c / G, gb = c - pair * G;  // walked incrementally: no division per piece
         for (; c < c1; ++pair, gb = 0) {
             const int ge = c1 - c < G - gb ? gb + (c1 - c) : G;
-            PieceSum ps = stream_piece(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
+            PieceSum ps = stream_piece<FMT>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
             c += ge - gb;
             if (first_piece && lane == 0) {
                 ftile[warp] = pair;
@@ -771,6 +806,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             }
             st->pos = pos + 1;
             for (int i = 0; i <= P.n_phases; ++i) P.done[i] = 0u;
+            for (int i = 0; i < P.n_attn_cnt; ++i) P.attn_cnt[i] = 0u;
         }
     }
 }
@@ -785,32 +821,39 @@ unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
     return (unsigned int)((b + 15) & ~(size_t)15);
 }
 
-size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases) {
+size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt) {
     const size_t infos = sizeof(PhaseInfo) * (size_t)((n_phases + 1) & ~1);
-    return (size_t)xstage_bytes + 768 + 8192 + 512 + infos + (size_t)NW * STEP_NBUF * Q4M_UNIT;
+    return (size_t)xstage_bytes + 768 + 8192 + 512 + infos + (size_t)NW * STEP_NBUF * q4m_unit_bytes(fmt);
 }
 
-static cudaError_t step_configure(size_t smem) {
+template <int FMT>
+static cudaError_t step_configure_t(size_t smem) {
     static size_t configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (smem <= configured[dev]) return cudaSuccess;
-    const cudaError_t e = cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const cudaError_t e = cudaFuncSetAttribute(k_step<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess) configured[dev] = smem;
     return e;
 }
 
-int step_occupancy(size_t smem) {
-    if (step_configure(smem) != cudaSuccess) return 0;
+static cudaError_t step_configure(size_t smem, int fmt) {
+    return fmt == Q4M_Q4_K ? step_configure_t<Q4M_Q4_K>(smem) : step_configure_t<Q4M_Q4_0>(smem);
+}
+
+int step_occupancy(size_t smem, int fmt) {
+    if (step_configure(smem, fmt) != cudaSuccess) return 0;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_step, STEP_THREADS, smem) != cudaSuccess) return 0;
-    return n;
+    const cudaError_t e =
+        fmt == Q4M_Q4_K ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_step<Q4M_Q4_K>, STEP_THREADS, smem)
+                        : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_step<Q4M_Q4_0>, STEP_THREADS, smem);
+    return e == cudaSuccess ? n : 0;
 }
 
 cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
-    const size_t smem = step_smem_bytes(p.xstage_bytes, p.n_phases);
-    cudaError_t e = step_configure(smem);
+    const size_t smem = step_smem_bytes(p.xstage_bytes, p.n_phases, p.fmt);
+    cudaError_t e = step_configure(smem, p.fmt);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -822,7 +865,7 @@ cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k_step, p);
+    return p.fmt == Q4M_Q4_K ? cudaLaunchKernelEx(&cfg, k_step<Q4M_Q4_K>, p) : cudaLaunchKernelEx(&cfg, k_step<Q4M_Q4_0>, p);
 }
 
 }  // namespace jinf

@@ -18,6 +18,10 @@ bool synth_tensor_params(const jinf_synth_model* m, const char* name, uint64_t* 
 cudaError_t synth_fill_q4_0(uint64_t key, float stdv, int64_t cols, int64_t r0, int64_t nr, int64_t c0, int64_t nc,
                             uint8_t* dst, int64_t dst_row_bytes, int64_t dst_row0, int64_t dst_row_step,
                             cudaStream_t s);
+// The same for Q4_K (columns whole 256-element super-blocks).
+cudaError_t synth_fill_q4_k(uint64_t key, float stdv, int64_t cols, int64_t r0, int64_t nr, int64_t c0, int64_t nc,
+                            uint8_t* dst, int64_t dst_row_bytes, int64_t dst_row0, int64_t dst_row_step,
+                            cudaStream_t s);
 // f32 rows [r0, r0+nr) (full rows) into dst.
 cudaError_t synth_fill_f32(uint64_t key, float stdv, int64_t cols, int64_t r0, int64_t nr, float* dst,
                            cudaStream_t s);

@@ -158,6 +158,86 @@ JINF_HD uint16_t fp32_to_fp16(float f) {
 
 JINF_HD float fabs_(float v) { return u2f(f2u(v) & 0x7fffffffu); }
 
+// fp16 bits -> fp32 (exact: normal, subnormal, zero, inf, NaN).
+JINF_HD float fp16_to_fp32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    const uint32_t exp = (h >> 10) & 0x1f;
+    uint32_t man = h & 0x3ff;
+    if (exp == 0x1f) return u2f(sign | 0x7f800000u | (man << 13));
+    if (exp != 0) return u2f(sign | ((exp + 112) << 23) | (man << 13));
+    if (man == 0) return u2f(sign);
+    int e = -1;
+    do {
+        man <<= 1;
+        ++e;
+    } while ((man & 0x400) == 0);
+    return u2f(sign | ((uint32_t)(112 - e) << 23) | ((man & 0x3ff) << 13));
+}
+
+// round to nearest, ties to even (lrintf in the default rounding mode)
+JINF_HD int rint_i(float x) {
+#ifdef __CUDA_ARCH__
+    return __float2int_rn(x);
+#else
+    return (int)lrintf(x);
+#endif
+}
+
+JINF_HD float fmin_(float a, float b) { return b < a ? b : a; }
+JINF_HD float fmax_(float a, float b) { return b > a ? b : a; }
+
+// Q4_K super-block from 256 floats, step for step the engine's host quantiser
+// (jinf_quantize_q4_K, csrc/quant.cpp): per sub-block min m = -min(0, lo) and step
+// s = (hi + m) / 15; d = max s / 63 and dmin = max m / 63 as fp16; 6-bit sc, m = rint(s / d),
+// rint(m / dmin); q = clamp(rint((x + dmin m) / (d sc)), 0, 15). out: 144 bytes.
+JINF_HD void quantize_q4_k_block(const float* v, uint8_t* out) {
+    float s[8], m[8], smax = 0.f, mmax = 0.f;
+    for (int j = 0; j < 8; ++j) {
+        float lo = v[32 * j], hi = v[32 * j];
+        for (int i = 1; i < 32; ++i) {
+            lo = fmin_(lo, v[32 * j + i]);
+            hi = fmax_(hi, v[32 * j + i]);
+        }
+        m[j] = lo < 0.f ? -lo : 0.f;
+        s[j] = (hi + m[j]) / 15.f;
+        smax = fmax_(smax, s[j]);
+        mmax = fmax_(mmax, m[j]);
+    }
+    const uint16_t dh = fp32_to_fp16(smax / 63.f);
+    const uint16_t mh = fp32_to_fp16(mmax / 63.f);
+    const float d = fp16_to_fp32(dh), dmin = fp16_to_fp32(mh);
+    int ls[8], lm[8];
+    for (int j = 0; j < 8; ++j) {
+        const int a = d > 0.f ? rint_i(s[j] / d) : 0;
+        const int c = dmin > 0.f ? rint_i(m[j] / dmin) : 0;
+        ls[j] = a < 0 ? 0 : (a > 63 ? 63 : a);
+        lm[j] = c < 0 ? 0 : (c > 63 ? 63 : c);
+    }
+    out[0] = (uint8_t)(dh & 0xff);
+    out[1] = (uint8_t)(dh >> 8);
+    out[2] = (uint8_t)(mh & 0xff);
+    out[3] = (uint8_t)(mh >> 8);
+    uint8_t* sc = out + 4;
+    for (int i = 0; i < 4; ++i) {
+        sc[i] = (uint8_t)((ls[i] & 63) | ((ls[i + 4] & 3) << 6));
+        sc[i + 4] = (uint8_t)((lm[i] & 63) | ((lm[i + 4] & 3) << 6));
+        sc[i + 8] = (uint8_t)(((ls[i + 4] >> 2) & 15) | (((lm[i + 4] >> 2) & 15) << 4));
+    }
+    for (int j = 0; j < 8; ++j) {
+        const float step = d * (float)ls[j];
+        const float off = dmin * (float)lm[j];
+        for (int i = 0; i < 16; ++i) {
+            int q[2];
+            for (int t = 0; t < 2; ++t) {
+                const float val = v[32 * j + 2 * i + t];
+                const int qq = step > 0.f ? rint_i((val + off) / step) : 0;
+                q[t] = qq < 0 ? 0 : (qq > 15 ? 15 : qq);
+            }
+            out[16 + 16 * j + i] = (uint8_t)(q[0] | (q[1] << 4));
+        }
+    }
+}
+
 // Q4_0 block from 32 floats: d = (value of largest magnitude)/-8, q = clamp(int(x/d+8.5)),
 // reference nibble pairing (byte i = elements 2i | 2i+1 << 4). out: 18 bytes.
 JINF_HD void quantize_q4_0_block(const float* v, uint8_t* out) {

@@ -83,6 +83,23 @@ def q4m_pack(aos, q4m, rows: int, cols: int, stream=None) -> None:
     L.check(L.lib.jinf_b200_q4m_pack(_p(aos), _p(q4m), rows, cols, _s(stream)), "jinf_b200_q4m_pack")
 
 
+def q4m_bytes_qt(rows: int, cols: int, qtype: int) -> int:
+    """Q4M image bytes for qtype Q4_0 (2) or Q4_K (12); 0 for an unsupported type or shape."""
+    return int(L.lib.jinf_b200_q4m_bytes_qt(rows, cols, qtype))
+
+
+def q4m_pack_qt(aos, qtype: int, q4m, rows: int, cols: int, stream=None) -> None:
+    L.check(L.lib.jinf_b200_q4m_pack_qt(_p(aos), qtype, _p(q4m), rows, cols, _s(stream)), "jinf_b200_q4m_pack_qt")
+
+
+def gemv_q4m_qt(q4m, qtype: int, x, y, rows: int, cols: int, workspace=None, kw: int = 0, stream=None) -> None:
+    import torch
+    xt = L.F32 if x.dtype == torch.float32 else L.F16
+    ws = _p(workspace) if workspace is not None else None
+    L.check(L.lib.jinf_b200_gemv_q4m_qt(_p(q4m), qtype, _p(x), xt, _p(y), rows, cols, ws, kw, _s(stream)),
+            "jinf_b200_gemv_q4m_qt")
+
+
 def gemv_q4m_workspace_bytes(rows: int, cols: int) -> int:
     return int(L.lib.jinf_b200_gemv_q4m_workspace_bytes(rows, cols))
 

@@ -110,3 +110,87 @@ def emulate_gemv(img: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.nda
     blk = (256 * dhi + dlo).astype(np.float32)
     s = (_f16(d) * inv_alpha[None, :]).astype(np.float32)
     return (s * blk).astype(np.float64).sum(axis=1).astype(np.float32)
+
+
+# ---------------------------------------------------------------- Q4_K (jetson-inference_b200/csrc/q4m.cuh)
+
+UNIT_K = 2432
+
+
+def _q4k_fields(aos: np.ndarray, rows: int, cols: int):
+    """AoS Q4_K [rows][cols/256*144] -> q [rows][cols/32][32], sc, m [rows][cols/32], d, dmin bits [rows][cols/256]."""
+    nsb = cols // 256
+    b = aos.reshape(rows, nsb, 144)
+    d = b[:, :, 0].astype(np.uint16) | (b[:, :, 1].astype(np.uint16) << 8)
+    dmin = b[:, :, 2].astype(np.uint16) | (b[:, :, 3].astype(np.uint16) << 8)
+    s = b[:, :, 4:16].astype(np.uint8)
+    sc = np.empty((rows, nsb, 8), np.uint8)
+    mn = np.empty((rows, nsb, 8), np.uint8)
+    sc[:, :, 0:4] = s[:, :, 0:4] & 0x3F
+    mn[:, :, 0:4] = s[:, :, 4:8] & 0x3F
+    sc[:, :, 4:8] = ((s[:, :, 8:12] & 0x0F) << 2) | (s[:, :, 0:4] >> 6)
+    mn[:, :, 4:8] = ((s[:, :, 8:12] >> 4) << 2) | (s[:, :, 4:8] >> 6)
+    qs = b[:, :, 16:].reshape(rows, nsb, 8, 16)
+    q = np.empty((rows, nsb, 8, 32), np.uint8)
+    q[..., 0::2] = qs & 15
+    q[..., 1::2] = qs >> 4
+    return q.reshape(rows, nsb * 8, 32), sc.reshape(rows, nsb * 8), mn.reshape(rows, nsb * 8), d, dmin
+
+
+def pack_q4k(aos: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """AoS Q4_K blocks -> Q4M (Q4_K form) bytes."""
+    q, sc, mn, d, dmin = _q4k_fields(aos, rows, cols)
+    groups, pairs = cols // KG, (rows + PAIR - 1) // PAIR
+    R = pairs * PAIR
+    qp = np.zeros((R, groups * 4, 32), np.uint8); qp[:rows] = q
+    scm = np.zeros((R, groups * 4), np.uint32); scm[:rows] = sc.astype(np.uint32) | (mn.astype(np.uint32) << 8)
+    dd = np.zeros((R, cols // 256), np.uint32); dd[:rows] = d.astype(np.uint32) | (dmin.astype(np.uint32) << 16)
+    qp = qp.reshape(pairs, PAIR, groups, 4, 32).transpose(0, 2, 1, 3, 4)
+    scm = scm.reshape(pairs, PAIR, groups, 4).transpose(0, 2, 1, 3)
+    dd = np.repeat(dd, 2, axis=1).reshape(pairs, PAIR, groups).transpose(0, 2, 1)   # both units of a super-block
+    out = np.zeros((pairs, groups, UNIT_K), np.uint8)
+    off = _layout()
+    out[:, :, off[:16].reshape(-1)] = (qp[:, :, :16] | (qp[:, :, 16:] << 4)).reshape(pairs, groups, -1)
+    sw = np.zeros((pairs, groups, 2, 32), np.uint32)
+    for lane in range(32):
+        gr, c = lane >> 2, lane & 3
+        for t in range(2):
+            sw[:, :, t, lane] = scm[:, :, 16 * t + gr, c] | (scm[:, :, 16 * t + gr + 8, c] << 16)
+    out[:, :, 2048:2304] = sw.astype('<u4').view(np.uint8).reshape(pairs, groups, 256)
+    out[:, :, 2304:] = np.ascontiguousarray(dd.astype('<u4')).view(np.uint8).reshape(pairs, groups, 128)
+    return out.reshape(-1)
+
+
+def unpack_q4k(img: np.ndarray, rows: int, cols: int):
+    """Q4M (Q4_K form) -> (q [rows][cols/32][32], sc, m [rows][cols/32], d, dmin bits [rows][cols/32])."""
+    groups, pairs = cols // KG, (rows + PAIR - 1) // PAIR
+    u = img.reshape(pairs, groups, UNIT_K)
+    off = _layout()
+    byt = u[:, :, off[:16].reshape(-1)].reshape(pairs, groups, 16, 4, 32)
+    q = np.concatenate([byt & 15, byt >> 4], axis=2).transpose(0, 2, 1, 3, 4).reshape(pairs * PAIR, groups * 4, 32)
+    sw = u[:, :, 2048:2304].copy().view('<u4').reshape(pairs, groups, 2, 32)
+    scm = np.zeros((pairs, groups, PAIR, 4), np.uint32)
+    for lane in range(32):
+        gr, c = lane >> 2, lane & 3
+        for t in range(2):
+            scm[:, :, 16 * t + gr, c] = sw[:, :, t, lane] & 0xFFFF
+            scm[:, :, 16 * t + gr + 8, c] = sw[:, :, t, lane] >> 16
+    scm = scm.transpose(0, 2, 1, 3).reshape(pairs * PAIR, groups * 4)
+    dd = u[:, :, 2304:].copy().view('<u4').reshape(pairs, groups, PAIR).transpose(0, 2, 1).reshape(pairs * PAIR, groups)
+    dd = np.repeat(dd, 4, axis=1)
+    return (q[:rows], (scm[:rows] & 0x3F).astype(np.uint8), ((scm[:rows] >> 8) & 0x3F).astype(np.uint8),
+            (dd[:rows] & 0xFFFF).astype(np.uint16), (dd[:rows] >> 16).astype(np.uint16))
+
+
+def emulate_gemv_q4k(img: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """The kernel's arithmetic: per block d sc * sum q v - dmin m * sum v (v = digits, exact
+    integers), scaled by 1/alpha in fp32."""
+    q, sc, mn, d, dmin = unpack_q4k(img, rows, cols)
+    hi, lo, inv_alpha = x_records(x, cols)
+    qi = q.astype(np.int64)
+    dq = 256 * np.einsum('rbk,bk->rb', qi, hi.astype(np.int64)) + np.einsum('rbk,bk->rb', qi, lo.astype(np.int64))
+    s = (256 * hi.astype(np.int64).sum(axis=1) + lo.astype(np.int64).sum(axis=1))
+    sub_d = (_f16(d) * sc.astype(np.float32)).astype(np.float32)
+    sub_m = (_f16(dmin) * mn.astype(np.float32)).astype(np.float32)
+    v = (sub_d * dq.astype(np.float32) - sub_m * s[None, :].astype(np.float32)).astype(np.float32)
+    return (v * inv_alpha[None, :]).astype(np.float64).sum(axis=1).astype(np.float32)

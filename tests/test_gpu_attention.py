@@ -49,3 +49,17 @@ def test_device_generator_bit_identical_to_host(cuda, name, row0, n):
     syn.read_rows_device(name, out, row0, n)
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy(), host.reshape(-1).view(np.uint8))
+
+
+@pytest.mark.parametrize("name,row0,n", [("blk.0.attn_q.weight", 0, 512), ("blk.3.ffn_down.weight", 100, 300),
+                                         ("output.weight", 7, 1)])
+def test_device_q4k_generator_bit_identical_to_host(cuda, name, row0, n):
+    """Q4_K models: the GPU generator's quantiser reproduces the host quantiser's bytes."""
+    import jinf
+    from jinf import _lib as L
+    syn = jinf.SynthModel(jinf.LlamaShape(4, 512, 8, 2, 1536, 4096, 10000.0, 1e-5), seed=0, weight_type=L.Q4_K)
+    host = syn.read_rows(name, row0, n)
+    out = torch.empty(host.nbytes, dtype=torch.uint8, device=cuda)
+    syn.read_rows_device(name, out, row0, n)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), host.reshape(-1).view(np.uint8))

@@ -146,3 +146,48 @@ def test_gemv_q4m_rmsnorm_prologue(cuda, rows, cols):
                        workspace=workspace(rows, cols, cuda))
     want = oracle.matvec(w, 2, oracle.rmsnorm(h, g, 1e-5), rows, cols)
     assert rel_err(y.cpu().numpy(), want) < REL
+
+
+# ---------------------------------------------------------------- Q4_K weights
+
+def packed_k(w, rows, cols, cuda):
+    from jinf import kernels as K
+    q = torch.empty(K.q4m_bytes_qt(rows, cols, 12), dtype=torch.uint8, device=cuda)
+    K.q4m_pack_qt(torch.from_numpy(np.ascontiguousarray(w)).to(cuda), 12, q, rows, cols)
+    return q
+
+
+@pytest.mark.parametrize("rows,cols", [(16, 256), (37, 512), (100, 1024), (4096, 4096)])
+def test_q4k_pack_matches_layout(cuda, rows, cols):
+    from test_q4m_layout import q4_k_rows
+    w = q4_k_rows(rows, cols, seed=rows)
+    assert np.array_equal(packed_k(w, rows, cols, cuda).cpu().numpy(), q4m_ref.pack_q4k(w, rows, cols))
+
+
+@pytest.mark.parametrize("rows,cols", [(4096, 4096), (1024, 8192), (8192, 1024), (3584, 8192), (8192, 3584),
+                                       (16032, 8192), (37, 512), (128, 14336)])
+def test_gemv_q4k(cuda, rows, cols):
+    from jinf import kernels as K
+    from test_q4m_layout import q4_k_rows
+    w = q4_k_rows(rows, cols, seed=rows + cols)
+    x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
+    q = packed_k(w, rows, cols, cuda)
+    ws = workspace(rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    y2 = torch.empty(rows, dtype=torch.float32, device=cuda)
+    xd = torch.from_numpy(x).to(cuda)
+    K.gemv_q4m_qt(q, 12, xd, y, rows, cols, workspace=ws)
+    K.gemv_q4m_qt(q, 12, xd, y2, rows, cols, workspace=ws)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.matvec(w, 12, x, rows, cols)) < REL
+    assert torch.equal(y, y2)
+    if rows * cols <= 4096 * 4096:
+        want = q4m_ref.emulate_gemv_q4k(q4m_ref.pack_q4k(w, rows, cols), x, rows, cols)
+        assert rel_err(y.cpu().numpy(), want) < 1e-5
+
+
+def test_q4k_rejects_partial_superblocks(cuda):
+    from jinf import kernels as K
+    assert K.q4m_bytes_qt(16, 384, 12) == 0       # not whole 256-element super-blocks
+    assert K.q4m_bytes_qt(16, 384, 2) > 0
+    assert K.q4m_bytes_qt(16, 256, 8) == 0        # Q8_0: no Q4M form

@@ -90,3 +90,30 @@ def test_emulated_gemv_extreme_scales_and_inputs():
         x[128:160] = 0.0
         y = q4m_ref.emulate_gemv(q4m_ref.pack(w, rows, cols), x, rows, cols)
         assert rel_err(y, oracle.matvec(w, 2, x, rows, cols)) < REL
+
+
+def q4_k_rows(rows, cols, seed, std=0.02):
+    import jinf
+    x = (np.random.default_rng(seed).standard_normal(rows * cols) * std).astype(np.float32)
+    out = np.empty(rows * cols // 256 * 144, dtype=np.uint8)
+    jinf.lib.jinf_quantize_q4_K(x.ctypes.data_as(C.c_void_p), out.ctypes.data_as(C.c_void_p), rows * cols)
+    return out.reshape(rows, -1)
+
+
+@pytest.mark.parametrize("rows,cols", [(16, 256), (37, 512), (100, 1024), (64, 768)])
+def test_pack_q4k_is_lossless(rows, cols):
+    w = q4_k_rows(rows, cols, seed=rows)
+    img = q4m_ref.pack_q4k(w, rows, cols)
+    assert img.size == ((rows + 31) // 32) * (cols // 128) * 2432
+    q, sc, mn, d, dmin = q4m_ref.unpack_q4k(img, rows, cols)
+    wq, wsc, wmn, wd, wdmin = q4m_ref._q4k_fields(w, rows, cols)
+    assert np.array_equal(q, wq) and np.array_equal(sc, wsc) and np.array_equal(mn, wmn)
+    assert np.array_equal(d, np.repeat(wd, 8, axis=1)) and np.array_equal(dmin, np.repeat(wdmin, 8, axis=1))
+
+
+@pytest.mark.parametrize("rows,cols", [(16, 256), (37, 512), (64, 1024), (100, 2048)])
+def test_emulated_gemv_q4k_matches_oracle(rows, cols):
+    w = q4_k_rows(rows, cols, seed=rows + cols)
+    x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
+    y = q4m_ref.emulate_gemv_q4k(q4m_ref.pack_q4k(w, rows, cols), x, rows, cols)
+    assert rel_err(y, oracle.matvec(w, 12, x, rows, cols)) < REL
