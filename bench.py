@@ -1,6 +1,6 @@
 """Decode benchmark: Llama-3-8B-shape Q4_0 greedy decode on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 8b|tiny]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 8b|tiny|70b]
 
 A step is one greedy decode token at batch 1 (the reference's per-token decode loop,
 reference src/engine.cpp:684-804), after a 512-token prompt: positions 512+W .. 512+W+K-1.
@@ -145,7 +145,17 @@ def all_max(dist, v: float) -> float:
 
 def shape_for(name):
     import jinf
-    return {"8b": jinf.LLAMA3_8B, "tiny": jinf.TINY}[name]
+    return {"8b": jinf.LLAMA3_8B, "tiny": jinf.TINY, "70b": jinf.LLAMA3_70B}[name]
+
+
+def wtype_for(name):
+    """Weight quantisation of a config: Q4_K for the 70B shape, else Q4_0."""
+    from jinf import _lib as L
+    return L.Q4_K if name == "70b" else L.Q4_0
+
+
+def wname_for(name):
+    return "q4_k" if name == "70b" else "q4_0"
 
 
 def prompt_ids(n_vocab, n=PROMPT):
@@ -155,12 +165,12 @@ def prompt_ids(n_vocab, n=PROMPT):
 
 # ------------------------------------------------------------------------- CPU oracle
 
-def cpu_decode_sample(shape, layers: int, target_s: float, min_reps: int = 2):
+def cpu_decode_sample(shape, layers: int, target_s: float, min_reps: int = 2, wtype=None):
     """Time the CPU oracle on `layers` layers (+ LM head) of a decode token at position PROMPT,
     extrapolate the per-token time to all layers. Returns (tok/s, threads, description)."""
     from oracle import oracle
     import jinf
-    syn = jinf.SynthModel(shape, seed=0)
+    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype) if wtype is not None else jinf.SynthModel(shape, seed=0)
     om = oracle.OracleModel(syn, max_ctx=PROMPT + 512, kv_f16=True, layers=layers)
     om.fill_kv_random(PROMPT, seed=1)
     tok = 1
@@ -196,7 +206,7 @@ def run_reference(args, rank, world):
     from oracle import oracle
     import jinf
     layers = 1
-    syn = jinf.SynthModel(shape, seed=0)
+    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config))
     om = oracle.OracleModel(syn, max_ctx=PROMPT + args.warmup + args.steps + 8, kv_f16=True, layers=layers)
     om.fill_kv_random(PROMPT, seed=1)
     for _ in range(args.warmup):
@@ -217,8 +227,9 @@ def run_reference(args, rank, world):
               f"tok/s = 1/({shape.n_layers}*mean step + LM head)")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * per_tok,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "q4_0 weights, f32",
-            "data": "synthetic (seeded N(0,0.02) Q4_0 weights)",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": f"{wname_for(args.config)} weights, f32",
+            "data": f"synthetic (seeded N(0,0.02) {wname_for(args.config).upper()} weights)",
             "config": {"workload": f"{args.config} decode batch 1, prompt {PROMPT}", "model": args.config,
                        "global_batch": 1, "seq_len": PROMPT + args.steps, "parallelism": "cpu"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
@@ -297,9 +308,10 @@ def run_ours(args, rank, world, local):
         dist.broadcast_object_list(buf, src=0)
         nccl_id = buf[0]
     t_load = time.perf_counter()
-    syn = jinf.SynthModel(shape, seed=0)
+    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config))
     max_ctx = PROMPT + args.warmup + args.steps + 8
-    opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1)
+    opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
+                             sparse_mode=args.sparse)
     eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=opts)
     t_load = time.perf_counter() - t_load
     stream = torch.cuda.ExternalStream(eng.h.contents.compute_stream, device=dev)
@@ -353,10 +365,11 @@ def run_ours(args, rank, world, local):
                                 "kernel and scaled by bytes processed (profiles/k_step_4layer_8bshape_full.md)",
                 "bytes_per_launch": int(wbytes + kv_bytes), "us_per_launch": round(1e6 * dev_s / args.steps, 2)}
     else:
-        top = max(("qkv", "o_proj", "gate_up", "down", "lm_head"),
+        top = max(("qkv", "o_proj", "gate_up", "down", "lm_head", "sparse_ffn"),
                   key=lambda k: prof[k]["us"] * (shape.n_layers if k != "lm_head" else 1))
         achieved = prof[top]["bytes"] / (prof[top]["us"] * 1e-6) / 1e9
-        roof = {"bound": "hbm", "kernel": f"k_gemv_q4m ({top})", "achieved": round(achieved, 1), "peak": peak,
+        kname = "sparse FFN (predictor + bundles)" if top == "sparse_ffn" else f"k_gemv_q4m ({top})"
+        roof = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": None,
                 "bytes_per_launch": prof[top]["bytes"], "us_per_launch": round(prof[top]["us"], 2)}
 
@@ -366,18 +379,21 @@ def run_ours(args, rank, world, local):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            cv, cores, desc, _ = cpu_decode_sample(shape, layers=2 if args.config == "8b" else shape.n_layers,
-                                                   target_s=args.cpu_seconds)
+            cv, cores, desc, _ = cpu_decode_sample(
+                shape, layers={"8b": 2, "70b": 1}.get(args.config, shape.n_layers), target_s=args.cpu_seconds,
+                wtype=wtype_for(args.config))
             cpu = {"value": cv, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * dev_s / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "q4_0 weights, f32 activations, f16 KV",
-            "data": "synthetic (seeded N(0,0.02) Q4_0 weights, uniform prompt ids)",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": f"{wname_for(args.config)} weights, f32 activations, f16 KV",
+            "data": f"synthetic (seeded N(0,0.02) {wname_for(args.config).upper()} weights, uniform prompt ids)",
             "config": {"workload": f"{args.config} greedy decode batch 1, prompt {PROMPT}, positions "
                                    f"{PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
                        "model": f"llama3-{args.config}-shape", "global_batch": 1, "seq_len": PROMPT + args.steps,
                        "parallelism": f"tp{world}",
+                       "ffn": ["dense", "sparse: device predictor top-k 15%", "sparse: fixed mask 15% (runs of 8)"][args.sparse],
                        "l2": f"{wbytes / 1e9:.2f} GB of weights streamed per step >> 126 MB L2 (no flush needed)"},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
             "gpu_launches": launches_per_step * args.steps,
@@ -406,10 +422,12 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "tiny"])
+    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "70b"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the C2 GEMV shape sweep")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--sparse", type=int, default=0, choices=[0, 1, 2],
+                    help="FFN: 0 dense, 1 device predictor top-k, 2 fixed mask (BASELINE config C4)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -59,6 +59,22 @@ jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* h, const fl
 jinf_status jinf_b200_gemv_q4m_noalloc(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
                                        cudaStream_t stream);
 
+// ---- sparse FFN (engine sparse modes; reference src/engine.cpp:339-415, src/activation_predictor.cpp)
+//
+// Fixed neuron mask of a layer: runs of 8 consecutive neurons, each kept with probability
+// `keep` (seeded). Writes the kept ids ascending when `ids` is not NULL; returns the count.
+int jinf_sparse_fixed_mask(uint64_t seed, int layer, int n_ff, float keep, int32_t* ids);
+// Predictor matrix `which` (1: W1 [r][d], 2: W2 [n_ff][r]) of a layer as fp16 bits ~ N(0, 0.02)
+// (host; the engine generates the same values on the device).
+void jinf_sparse_predictor_weights(uint64_t seed, int layer, int which, int64_t n, uint16_t* out);
+// Predictor on the device: z = ReLU(W1 x), s = W2 z (W1, W2 fp16, fp32 sums), then the k
+// largest scores (ties: lower index first) as ids ascending and bundle byte offsets
+// id * bundle_size. d and r multiples of 8; scratch: r + n_ff floats (device). No
+// counterpart in the reference, whose predictor ran on the host.
+jinf_status jinf_b200_sparse_predict(const void* w1, const void* w2, const float* x, int d, int r, int n_ff, int k,
+                                     int bundle_size, int32_t* ids, int32_t* offsets, float* scratch,
+                                     cudaStream_t stream);
+
 // Workspace bytes needed by jinf_b200_attention_f16 for this shape.
 size_t jinf_b200_attention_workspace_bytes(int n_kv_heads, int head_dim, int max_ctx);
 

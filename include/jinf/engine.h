@@ -162,11 +162,16 @@ jinf_status jinf_engine_last_argmax(jinf_engine* e, int32_t* token);
 jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uint64_t seed);
 // 1 when each decode token runs as one persistent kernel, 0 for one kernel per operation.
 int         jinf_engine_is_persistent(const jinf_engine* e);
+// Sparse FFN modes: the active neurons of `layer` used by the last forward (ids ascending,
+// at most `max` written to the host array `ids`); *n their count. JINF_ERR_INVALID in
+// dense mode.
+jinf_status jinf_engine_sparse_ids(jinf_engine* e, int layer, int32_t* ids, int max, int* n);
 // Bytes of quantized weights this rank streams per token (algorithmic weight traffic).
 uint64_t    jinf_engine_weight_bytes_per_token(const jinf_engine* e);
 // Time one launch of each fused kernel kind on its own (CUDA events, `reps` repetitions
-// rotated over the layers). times_us receives 6 values: qkv, attention, o_proj, gate_up,
-// down, lm_head. bytes receives the algorithmic bytes of one launch of each.
+// rotated over the layers). times_us receives 7 values: qkv, attention, o_proj, gate_up,
+// down, lm_head, sparse_ffn (sparse modes: the whole FFN of a layer; 0 in dense mode, where
+// gate_up and down are the FFN). bytes receives the algorithmic bytes of one launch of each.
 jinf_status jinf_engine_profile_kernels(jinf_engine* e, int reps, double* times_us, double* bytes);
 
 // nccl unique id (128 bytes) for tensor-parallel set-up; rank 0 creates it and the

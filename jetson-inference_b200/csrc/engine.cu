@@ -23,9 +23,11 @@
 // HBM arena laid out in consumption order; in the kernel-per-operation form each GEMV
 // prefetches the next matrix into L2 (cp.async.bulk.prefetch.L2) before it waits on its
 // inputs, so HBM keeps streaming across kernel boundaries.
+#include "jinf/b200.h"
 #include "jinf/engine.h"
 #include "jinf/kernels.h"
 #include "jinf/quant.h"
+#include "jinf/sparse_ops.h"
 #include "jinf/splitter.h"
 
 #include "attn_f16.h"
@@ -34,6 +36,7 @@
 #include "gemv.h"
 #include "nccl_shim.h"
 #include "q4m.cuh"
+#include "sparse_engine.h"
 #include "step.h"
 #include "synth_internal.h"
 
@@ -222,7 +225,8 @@ __global__ void k_even_rows(const float* in, float* out, int n) {
 }
 
 
-enum OpKind { OP_GEMV = 0, OP_ATTN = 1, OP_ALLREDUCE_F32 = 2, OP_ALLREDUCE_MAXU64 = 3, OP_FINALIZE = 4 };
+enum OpKind { OP_GEMV = 0, OP_ATTN = 1, OP_ALLREDUCE_F32 = 2, OP_ALLREDUCE_MAXU64 = 3, OP_FINALIZE = 4,
+              OP_SPARSE_FFN = 5 };
 enum GemvRole { ROLE_QKV = 0, ROLE_O = 1, ROLE_GATEUP = 2, ROLE_DOWN = 3, ROLE_LM = 4, ROLE_NONE = 5 };
 
 struct Op {
@@ -284,6 +288,20 @@ struct jinf_engine_impl {
     float* attn = nullptr;
     float* act = nullptr;
     float* gate_raw = nullptr;  // FFN hook buffer
+    // sparse FFN mode (0 dense, 1 predictor top-k, 2 fixed mask; tp_size 1, kernel per operation)
+    int sparse_mode = 0;
+    int sparse_k = 0;                // neurons kept per layer (mode 1)
+    int pred_r = 0;                  // predictor rank (mode 1)
+    int bundle_size = 0;
+    uint8_t* bundles = nullptr;      // [L][ff][bundle_size]
+    __half* pred_w1 = nullptr;       // [L][r][d] fp16
+    __half* pred_w2 = nullptr;       // [L][ff][r] fp16
+    int32_t* sparse_ids = nullptr;   // [L][ff] active neuron ids (ascending)
+    int32_t* sparse_offs = nullptr;  // [L][ff] their bundle byte offsets
+    std::vector<int> sparse_n;       // active neurons per layer
+    float* sparse_x = nullptr;       // [d] normalised FFN input
+    float* sparse_scratch = nullptr; // [r + ff] predictor scores
+    float* gate_up_tmp = nullptr;    // [ff]
     float* logits = nullptr;    // local shard [Vl]
     float* logits_full = nullptr;  // [V] (== logits when tp_size == 1)
     float* attn_partial = nullptr;
@@ -322,6 +340,25 @@ jinf_status run_op(jinf_engine_impl* I, const Op& op, cudaStream_t s) {
         case OP_GEMV: e = gemvm_launch(op.gp, op.xm, op.epi, op.grid, s, true); break;
         case OP_ATTN: e = attn_launch(op.ap, s, true); break;
         case OP_FINALIZE: k_finalize<<<1, 1, 0, s>>>(I->st, op.with_argmax); e = cudaGetLastError(); break;
+        case OP_SPARSE_FFN: {
+            // h = h + y_o; x = RMSNorm(h) * ffn_norm; [predictor]; y_down = FFN over the active
+            // neurons (the next layer's QKV prologue adds y_down to h)
+            const int L = op.layer;
+            const size_t ff = (size_t)I->ffl;
+            int32_t* ids = I->sparse_ids + (size_t)L * ff;
+            int32_t* offs = I->sparse_offs + (size_t)L * ff;
+            e = sparse_ffn_prologue(I->hA, I->y_o, I->hB, I->layers[L].ffn_norm, I->eps, I->d, I->sparse_x, s);
+            if (e == cudaSuccess && I->sparse_mode == 1)
+                e = sparse_predict(I->pred_w1 + (size_t)L * I->pred_r * I->d, I->pred_w2 + (size_t)L * ff * I->pred_r,
+                                   I->sparse_x, I->d, I->pred_r, I->ffl, I->sparse_k, I->bundle_size, ids, offs,
+                                   I->sparse_scratch, s);
+            if (e == cudaSuccess) {
+                jinf_cuda_sparse_ffn(I->bundles + (size_t)L * ff * I->bundle_size, I->sparse_x, I->y_down, offs,
+                                     I->sparse_n[L], I->d, I->bundle_size, I->wtype, I->gate_up_tmp, s);
+                e = cudaGetLastError();
+            }
+            break;
+        }
         case OP_ALLREDUCE_F32:
         case OP_ALLREDUCE_MAXU64: {
             const NcclApi* n = nccl_api();
@@ -445,6 +482,14 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
             ar.buf = I->y_o;
             ar.count = (size_t)I->d;
             ops.push_back(ar);
+        }
+
+        if (I->sparse_mode) {
+            Op sp{OP_SPARSE_FFN};
+            sp.layer = L;
+            sp.bytes = (uint64_t)I->sparse_n[L] * I->bundle_size;
+            ops.push_back(sp);
+            continue;
         }
 
         Op gu{OP_GEMV};
@@ -831,7 +876,8 @@ void free_impl(jinf_engine_impl* I) {
     void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
                     I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
                     I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_rec[0], I->step_rec[1],
-                    I->step_rec[2], I->step_rec[3], I->step_ss, I->step_attn_cnt};
+                    I->step_rec[2], I->step_rec[3], I->step_ss, I->step_attn_cnt, I->bundles, I->pred_w1,
+                    I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);
@@ -906,6 +952,14 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     }
     if (I->H / I->Hkv > 8) {
         JINF_LOG("more than 8 query heads per kv head are not supported");
+        return fail(JINF_ERR_INVALID);
+    }
+    I->sparse_mode = opt.sparse_mode;
+    if (I->sparse_mode < 0 || I->sparse_mode > 2 || (I->sparse_mode && (tp > 1 || !(opt.sparse_keep > 0.f) ||
+                                                                       opt.sparse_keep > 1.f || I->d % 32 ||
+                                                                       I->d > 8192))) {
+        JINF_LOG("sparse_mode %d (keep %.3f) not supported: modes 0-2, keep in (0, 1], one GPU, d <= 8192",
+                 opt.sparse_mode, opt.sparse_keep);
         return fail(JINF_ERR_INVALID);
     }
     if (cudaSetDevice(I->device) != cudaSuccess) {
@@ -984,6 +1038,50 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     cudaMemset(I->y_o, 0, sizeof(float) * d);
     cudaMemset(I->y_down, 0, sizeof(float) * d);
 
+    // ---- sparse FFN mode: neuron bundles (filled while loading), predictor or fixed masks
+    if (I->sparse_mode) {
+        const size_t ff = (size_t)I->ffl;
+        I->bundle_size = sparse_bundle_bytes(d, I->wtype);
+        I->sparse_n.assign(I->L, 0);
+        std::vector<int32_t> ids(ff * I->L, 0), offs(ff * I->L, 0);
+        if (I->sparse_mode == 1) {
+            I->pred_r = d / 4;
+            I->sparse_k = (int)std::floor((double)opt.sparse_keep * (double)I->ffl);
+            if (I->sparse_k < 1) I->sparse_k = 1;
+            for (int L = 0; L < I->L; ++L) I->sparse_n[L] = I->sparse_k;
+        } else {
+            for (int L = 0; L < I->L; ++L) {
+                I->sparse_n[L] = jinf_sparse_fixed_mask(opt.sparse_seed, L, I->ffl, opt.sparse_keep, ids.data() + L * ff);
+                for (int i = 0; i < I->sparse_n[L]; ++i)
+                    offs[L * ff + i] = ids[L * ff + i] * I->bundle_size;
+            }
+        }
+        bool sok = cudaMalloc(&I->bundles, (size_t)I->L * ff * I->bundle_size) == cudaSuccess &&
+                   cudaMalloc(&I->sparse_ids, sizeof(int32_t) * ff * I->L) == cudaSuccess &&
+                   cudaMalloc(&I->sparse_offs, sizeof(int32_t) * ff * I->L) == cudaSuccess &&
+                   cudaMalloc(&I->sparse_x, sizeof(float) * (size_t)d) == cudaSuccess &&
+                   cudaMalloc(&I->gate_up_tmp, sizeof(float) * ff) == cudaSuccess;
+        if (sok && I->sparse_mode == 1)
+            sok = cudaMalloc(&I->pred_w1, sizeof(__half) * (size_t)I->L * I->pred_r * d) == cudaSuccess &&
+                  cudaMalloc(&I->pred_w2, sizeof(__half) * (size_t)I->L * ff * I->pred_r) == cudaSuccess &&
+                  cudaMalloc(&I->sparse_scratch, sizeof(float) * ((size_t)I->pred_r + ff)) == cudaSuccess;
+        if (!sok) {
+            JINF_LOG("cannot allocate the sparse-FFN buffers (%.1f MB of bundles)",
+                     (double)I->L * ff * I->bundle_size / 1048576.0);
+            return fail(JINF_ERR_OOM);
+        }
+        cudaMemset(I->bundles, 0, (size_t)I->L * ff * I->bundle_size);
+        JINF_CUDA_CHECK(cudaMemcpy(I->sparse_ids, ids.data(), sizeof(int32_t) * ids.size(), cudaMemcpyHostToDevice));
+        JINF_CUDA_CHECK(cudaMemcpy(I->sparse_offs, offs.data(), sizeof(int32_t) * offs.size(), cudaMemcpyHostToDevice));
+        if (I->sparse_mode == 1)
+            for (int L = 0; L < I->L; ++L) {
+                JINF_CUDA_CHECK(sparse_fill_predictor(opt.sparse_seed, L, 1, (int64_t)I->pred_r * d,
+                                                      I->pred_w1 + (size_t)L * I->pred_r * d, I->stream));
+                JINF_CUDA_CHECK(sparse_fill_predictor(opt.sparse_seed, L, 2, (int64_t)ff * I->pred_r,
+                                                      I->pred_w2 + (size_t)L * ff * I->pred_r, I->stream));
+            }
+    }
+
     // ---- load weights (per matrix: stage AoS rows in HBM, then repack into the arena)
     {
         Loader ld{I, &src};
@@ -1035,12 +1133,19 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
                 snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", L);
                 s = ld.stage_shard(nm, I->ffl, d, rb_d, 1, 2);
             }
+            uint8_t* bl = I->bundles ? I->bundles + (size_t)L * I->ffl * I->bundle_size : nullptr;
+            if (s == JINF_OK && bl && sparse_bundle_gate_up(ld.dstage, I->ffl, (int)rb_d, bl, I->bundle_size,
+                                                            I->stream) != cudaSuccess)
+                s = JINF_ERR_CUDA;
             if (s == JINF_OK) s = ld.pack(ly.gu, ly.gu_sh);
             // down: every output row, this rank's neuron columns (row split)
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", L);
                 s = ld.stage_shard(nm, d, I->ffl, (int64_t)(I->ffl / 32) * 18, 0, 1);
             }
+            if (s == JINF_OK && bl && sparse_bundle_down(ld.dstage, d, I->ffl, I->wtype, bl, I->bundle_size,
+                                                         (int)(2 * rb_d), I->stream) != cudaSuccess)
+                s = JINF_ERR_CUDA;
             if (s == JINF_OK) s = ld.pack(ly.down, ly.down_sh);
         }
         I->out_norm = I->norms + (size_t)(2 * I->L) * d;
@@ -1079,7 +1184,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             return fail(JINF_ERR_OOM);
         cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * pairs);
     }
-    if (tp == 1 && opt.persistent) {
+    if (tp == 1 && opt.persistent && !I->sparse_mode) {
         const jinf_status s = setup_persistent(I);
         if (s != JINF_OK) return fail(s);
     }
@@ -1338,6 +1443,19 @@ extern "C" int jinf_engine_is_persistent(const jinf_engine* e) {
     return e && e->impl && e->impl->persistent ? 1 : 0;
 }
 
+extern "C" jinf_status jinf_engine_sparse_ids(jinf_engine* e, int layer, int32_t* ids, int max, int* n) {
+    if (!e || !e->impl || !n || !e->impl->sparse_mode || layer < 0 || layer >= e->impl->L) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    if (I->device >= 0) cudaSetDevice(I->device);
+    *n = I->sparse_n[layer];
+    if (ids && max > 0) {
+        JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+        JINF_CUDA_CHECK(cudaMemcpy(ids, I->sparse_ids + (size_t)layer * I->ffl,
+                                   sizeof(int32_t) * (size_t)std::min(max, *n), cudaMemcpyDeviceToHost));
+    }
+    return JINF_OK;
+}
+
 extern "C" uint64_t jinf_engine_weight_bytes_per_token(const jinf_engine* e) {
     return e && e->impl ? e->impl->weight_bytes_token : 0;
 }
@@ -1346,14 +1464,16 @@ extern "C" jinf_status jinf_engine_profile_kernels(jinf_engine* e, int reps, dou
     if (!e || !e->impl || reps <= 0 || !times_us || !bytes) return JINF_ERR_INVALID;
     jinf_engine_impl* I = e->impl;
     JINF_CUDA_CHECK(cudaSetDevice(I->device));
-    const int roles[6] = {ROLE_QKV, -1 /* attention */, ROLE_O, ROLE_GATEUP, ROLE_DOWN, ROLE_LM};
+    const int roles[7] = {ROLE_QKV, -1 /* attention */, ROLE_O, ROLE_GATEUP, ROLE_DOWN, ROLE_LM, -2 /* sparse FFN */};
     cudaEvent_t a, b;
     cudaEventCreate(&a);
     cudaEventCreate(&b);
-    for (int k = 0; k < 6; ++k) {
+    for (int k = 0; k < 7; ++k) {
         std::vector<const Op*> sel;
         for (const Op& op : I->ops_full) {
-            if (k == 1 ? op.kind == OP_ATTN : (op.kind == OP_GEMV && op.role == roles[k])) sel.push_back(&op);
+            if (k == 1 ? op.kind == OP_ATTN
+                       : k == 6 ? op.kind == OP_SPARSE_FFN : (op.kind == OP_GEMV && op.role == roles[k]))
+                sel.push_back(&op);
         }
         times_us[k] = 0;
         bytes[k] = 0;

@@ -277,3 +277,29 @@ bool jinf::synth_tensor_params(const jinf_synth_model* m, const char* name, uint
     *role = t->role;
     return true;
 }
+
+// ---------------------------------------------------------------- sparse-FFN synthetic data
+
+// Fixed neuron mask of a layer: runs of 8 consecutive neurons, each kept with probability
+// `keep` (seeded). Writes the kept ids ascending (when `ids` is not NULL); returns the count.
+extern "C" int jinf_sparse_fixed_mask(uint64_t seed, int layer, int n_ff, float keep, int32_t* ids) {
+    if (n_ff <= 0 || layer < 0) return 0;
+    int n = 0;
+    const uint64_t base = jinf_synth::mask_key(seed, layer);
+    for (int run = 0; run < (n_ff + 7) / 8; ++run) {
+        const double u = jinf_synth::to_unit(jinf_synth::splitmix64(base + (uint64_t)run));
+        if (u > (double)keep) continue;  // u in (0, 1]: kept with probability `keep`
+        for (int i = 8 * run; i < 8 * run + 8 && i < n_ff; ++i) {
+            if (ids) ids[n] = i;
+            ++n;
+        }
+    }
+    return n;
+}
+
+// Predictor weights of a layer (which 1: W1 [r][d], 2: W2 [n_ff][r]) as fp16 bits ~ N(0, 0.02):
+// the same values the engine generates on the device.
+extern "C" void jinf_sparse_predictor_weights(uint64_t seed, int layer, int which, int64_t n, uint16_t* out) {
+    const uint64_t key = jinf_synth::predictor_key(seed, layer, which);
+    for (int64_t i = 0; i < n; ++i) out[i] = jinf_synth::fp32_to_fp16(jinf_synth::normal_at(key, (uint64_t)i, 0.02f));
+}

@@ -158,6 +158,16 @@ JINF_HD uint16_t fp32_to_fp16(float f) {
 
 JINF_HD float fabs_(float v) { return u2f(f2u(v) & 0x7fffffffu); }
 
+// Streams of the sparse-FFN synthetic data: predictor matrix `which` (1: W1, 2: W2) of a
+// layer, and a layer's fixed neuron mask.
+JINF_HD uint64_t predictor_key(uint64_t seed, int layer, int which) {
+    return splitmix64(seed ^ (0x5052454449435452ull + (uint64_t)layer * 0x9E3779B97F4A7C15ull +
+                              (uint64_t)which * 0xD1B54A32D192ED03ull));
+}
+JINF_HD uint64_t mask_key(uint64_t seed, int layer) {
+    return splitmix64(seed ^ (0x4D41534Bull + (uint64_t)layer * 0x9E3779B97F4A7C15ull));
+}
+
 // fp16 bits -> fp32 (exact: normal, subnormal, zero, inf, NaN).
 JINF_HD float fp16_to_fp32(uint16_t h) {
     const uint32_t sign = (uint32_t)(h >> 15) << 31;

@@ -222,6 +222,10 @@ SIGNATURES = {
     "jinf_engine_last_argmax": (i32, [C.POINTER(Engine), C.POINTER(C.c_int32)]),
     "jinf_engine_fill_kv_random": (i32, [C.POINTER(Engine), i32, u64]),
     "jinf_engine_is_persistent": (i32, [vp]),
+    "jinf_engine_sparse_ids": (i32, [vp, i32, vp, i32, vp]),
+    "jinf_sparse_fixed_mask": (i32, [C.c_uint64, i32, i32, C.c_float, vp]),
+    "jinf_sparse_predictor_weights": (None, [C.c_uint64, i32, i32, i64, vp]),
+    "jinf_b200_sparse_predict": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp]),
     "jinf_engine_weight_bytes_per_token": (u64, [C.POINTER(Engine)]),
     "jinf_engine_profile_kernels": (i32, [C.POINTER(Engine), i32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "jinf_nccl_get_unique_id": (i32, [vp]),

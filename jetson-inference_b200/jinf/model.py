@@ -120,11 +120,13 @@ class SynthModel:
 
 
 def b200_options(device: int = 0, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
-                 use_graph: bool = True, eos_token: int = 2, persistent: bool = True) -> L.B200Options:
+                 use_graph: bool = True, eos_token: int = 2, persistent: bool = True, sparse_mode: int = 0,
+                 sparse_keep: float = 0.15, sparse_seed: int = 0) -> L.B200Options:
+    """sparse_mode: 0 dense FFN, 1 device predictor top-k, 2 fixed mask (runs of 8)."""
     o = L.B200Options()
     o.device, o.tp_rank, o.tp_size = device, tp_rank, tp_size
     o.kv_type, o.use_graph, o.eos_token = L.F16, int(use_graph), eos_token
-    o.sparse_mode, o.sparse_keep, o.sparse_seed = 0, 0.15, 0
+    o.sparse_mode, o.sparse_keep, o.sparse_seed = sparse_mode, sparse_keep, sparse_seed
     o.persistent = int(persistent)
     o._nccl_buf = None
     if nccl_id is not None:
@@ -237,14 +239,23 @@ class Engine:
         """True when each decode token runs as one persistent kernel."""
         return bool(L.lib.jinf_engine_is_persistent(self.h))
 
+    def sparse_ids(self, layer: int) -> np.ndarray:
+        """Sparse modes: the active neurons of `layer` used by the last forward."""
+        n = C.c_int()
+        L.check(L.lib.jinf_engine_sparse_ids(self.h, layer, None, 0, C.byref(n)), "jinf_engine_sparse_ids")
+        out = np.empty(n.value, dtype=np.int32)
+        L.check(L.lib.jinf_engine_sparse_ids(self.h, layer, out.ctypes.data_as(C.c_void_p), n.value, C.byref(n)),
+                "jinf_engine_sparse_ids")
+        return out
+
     def weight_bytes_per_token(self) -> int:
         return L.lib.jinf_engine_weight_bytes_per_token(self.h)
 
     def profile_kernels(self, reps: int = 32) -> dict:
-        t = (C.c_double * 6)()
-        b = (C.c_double * 6)()
+        t = (C.c_double * 7)()
+        b = (C.c_double * 7)()
         L.check(L.lib.jinf_engine_profile_kernels(self.h, reps, t, b), "profile_kernels")
-        names = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head"]
+        names = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "sparse_ffn"]
         return {n: {"us": t[i], "bytes": b[i]} for i, n in enumerate(names)}
 
     def stats(self) -> L.PerfStats:

@@ -278,6 +278,8 @@ struct orc_model {
     int pos = 0;
     std::unordered_map<std::string, OrcTensor> t;
     std::vector<float> kc, vc;  // [L][ctx][nkv*hd]
+    std::vector<std::vector<int>> ffn_mask;  // per layer: active neurons (empty vector: dense)
+    std::vector<char> has_mask;
 };
 
 orc_model* orc_model_create(int n_layers, int d, int nh, int nkv, int ff, int vocab, float eps, float base,
@@ -309,6 +311,25 @@ int orc_model_bind(orc_model* m, const char* name, int qt, const void* data) {
 }
 
 int orc_model_pos(const orc_model* m) { return m->pos; }
+
+// Restrict the FFN of `layer` to the neurons ids[0..n) (n < 0: dense again): the other
+// neurons' SiLU(gate)*up is 0, the semantics of the reference's sparse FFN
+// (src/engine.cpp:339-415, cuda/sparse_matmul.cu:104-110, :211-218).
+int orc_model_set_ffn_mask(orc_model* m, int layer, const int* ids, int n) {
+    if (!m || layer < 0 || layer >= m->L) return -1;
+    if ((int)m->ffn_mask.size() < m->L) {
+        m->ffn_mask.resize(m->L);
+        m->has_mask.assign(m->L, 0);
+    }
+    if (n < 0) {
+        m->has_mask[layer] = 0;
+        m->ffn_mask[layer].clear();
+        return 0;
+    }
+    m->has_mask[layer] = 1;
+    m->ffn_mask[layer].assign(ids, ids + n);
+    return 0;
+}
 
 static const OrcTensor* need(orc_model* m, const std::string& n) {
     auto it = m->t.find(n);
@@ -367,6 +388,12 @@ int orc_forward(orc_model* m, int token, float* logits) {
         matvec_t(wg, xn.data(), g.data(), m->ff, d);
         matvec_t(wu, xn.data(), u.data(), m->ff, d);
         orc_silu_mul(g.data(), g.data(), u.data(), m->ff);
+        if ((int)m->has_mask.size() > L && m->has_mask[L]) {
+            std::vector<float> keep((size_t)m->ff, 0.f);
+            for (int id : m->ffn_mask[L])
+                if (id >= 0 && id < m->ff) keep[id] = g[id];
+            g.swap(keep);
+        }
         matvec_t(wd, g.data(), o.data(), d, m->ff);
         for (int i = 0; i < d; ++i) h[i] += o[i];
     }

@@ -51,6 +51,7 @@ def lib() -> C.CDLL:
             "orc_model_destroy": (None, [vp]),
             "orc_model_bind": (i32, [vp, C.c_char_p, i32, vp]),
             "orc_model_pos": (i32, [vp]),
+            "orc_model_set_ffn_mask": (i32, [vp, i32, vp, i32]),
             "orc_forward": (i32, [vp, i32, vp]),
             "orc_argmax": (i32, [vp, i32]),
             "orc_fill_kv_random": (i32, [vp, i32, C.c_uint64]),
@@ -205,6 +206,16 @@ class OracleModel:
         if rc != 0:
             raise RuntimeError(f"orc_forward failed ({rc})")
         return logits
+
+    def set_ffn_mask(self, layer: int, ids) -> None:
+        """Restrict layer `layer`'s FFN to the neurons `ids` (None: dense)."""
+        if ids is None:
+            rc = lib().orc_model_set_ffn_mask(self.h, layer, None, -1)
+        else:
+            a = np.ascontiguousarray(ids, dtype=np.int32)
+            rc = lib().orc_model_set_ffn_mask(self.h, layer, _vp(a), int(a.size))
+        if rc != 0:
+            raise RuntimeError("orc_model_set_ffn_mask failed")
 
     def fill_kv_random(self, n_pos: int, seed: int = 0) -> None:
         if lib().orc_fill_kv_random(self.h, n_pos, seed) != 0:
