@@ -240,7 +240,7 @@ def run_reference(args, rank, world):
 # ------------------------------------------------------------------------- our arm
 
 def gemv_microbench(dev, peak):
-    """C2: Q4_0 GEMV on the 8B projection shapes, batch 1, fp16 x, rotating weight copies
+    """C2: Q4_0 GEMV on the 8B projection shapes, batch 1 / 4 / 8, fp16 x, rotating weight copies
     so every launch streams from HBM (>= 4x L2 of weights per shape); the launches are
     captured in a CUDA graph so the host launch rate does not cap small shapes."""
     import numpy as np
@@ -262,30 +262,42 @@ def gemv_microbench(dev, peak):
             K.q4m_pack(aos, q, rows, cols)
             qs.append(q)
         del aos
-        ws = torch.zeros(K.gemv_q4m_workspace_bytes(rows, cols), dtype=torch.uint8, device=dev)
-        x = torch.from_numpy(np.random.default_rng(0).standard_normal(cols).astype(np.float16)).to(dev)
-        y = torch.empty(rows, dtype=torch.float32, device=dev)
-        for i in range(3):
-            K.gemv_q4m(qs[i % copies], x, y, rows, cols, workspace=ws)
-        torch.cuda.synchronize()
-        n = copies * max(1, 60 // copies)
-        s = torch.cuda.Stream()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(g, stream=s):
-                for i in range(n):
-                    K.gemv_q4m(qs[i % copies], x, y, rows, cols, workspace=ws)
-        g.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        g.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        del g
-        us = e0.elapsed_time(e1) * 1000.0 / n
-        gbs = (wbytes + 2 * cols + 4 * rows) / (us * 1e-6) / 1e9
-        out[f"{rows}x{cols}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3)}
+        out[f"{rows}x{cols}"] = {}
+        for batch in (1, 4, 8):
+            if batch == 1:
+                ws = torch.zeros(K.gemv_q4m_workspace_bytes(rows, cols), dtype=torch.uint8, device=dev)
+            else:
+                ws = torch.zeros(K.gemv_q4m_batch_workspace_bytes(rows, cols, batch), dtype=torch.uint8, device=dev)
+            x = torch.from_numpy(np.random.default_rng(0).standard_normal((batch, cols)).astype(np.float16)).to(dev)
+            y = torch.empty((batch, rows), dtype=torch.float32, device=dev)
+
+            def launch(q):
+                if batch == 1:
+                    K.gemv_q4m(q, x, y, rows, cols, workspace=ws)
+                else:
+                    K.gemv_q4m_batch(q, x, y, rows, cols, batch, workspace=ws)
+
+            for i in range(3):
+                launch(qs[i % copies])
+            torch.cuda.synchronize()
+            n = copies * max(1, 60 // copies)
+            s = torch.cuda.Stream()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    for i in range(n):
+                        launch(qs[i % copies])
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del g
+            us = e0.elapsed_time(e1) * 1000.0 / n
+            gbs = (wbytes + batch * (2 * cols + 4 * rows)) / (us * 1e-6) / 1e9
+            out[f"{rows}x{cols}"][f"b{batch}"] = {"us": round(us, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3)}
         del qs
         torch.cuda.empty_cache()
     return out

@@ -46,6 +46,14 @@ size_t jinf_b200_gemv_q4m_workspace_bytes(int rows, int cols);
 jinf_status jinf_b200_gemv_q4m(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
                                void* workspace, int kw, cudaStream_t stream);
 
+// Batched: Y[b][rows] = W . X[b] for b < batch (1..8), X [batch][cols] fp32 or fp16, one pass
+// over the Q4_0 Q4M matrix (tensor cores: the MMA's columns carry 4 vectors' digits). Needs
+// `workspace` (gemv_q4m_batch_workspace_bytes, zeroed once, reusable on the same stream)
+// for shapes that split K. No counterpart in the reference (batch-1 GEMVs only).
+size_t jinf_b200_gemv_q4m_batch_workspace_bytes(int rows, int cols, int batch);
+jinf_status jinf_b200_gemv_q4m_batch(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
+                                     int batch, void* workspace, cudaStream_t stream);
+
 // y[rows] = W . (rmsnorm(h) * gain) over a Q4M matrix; workspace and kw as above.
 jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* h, const float* gain, float eps, float* y,
                                        int rows, int cols, void* workspace, int kw, cudaStream_t stream);

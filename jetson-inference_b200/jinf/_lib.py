@@ -155,6 +155,8 @@ SIGNATURES = {
     "jinf_b200_q4m_bytes": (u64, [i32, i32]),
     "jinf_b200_q4m_pack": (i32, [vp, vp, i32, i32, vp]),
     "jinf_b200_q4m_bytes_qt": (u64, [i32, i32, i32]),
+    "jinf_b200_gemv_q4m_batch_workspace_bytes": (sz, [i32, i32, i32]),
+    "jinf_b200_gemv_q4m_batch": (i32, [vp, vp, i32, vp, i32, i32, i32, vp, vp]),
     "jinf_b200_q4m_pack_qt": (i32, [vp, i32, vp, i32, i32, vp]),
     "jinf_b200_gemv_q4m_qt": (i32, [vp, i32, vp, i32, vp, i32, i32, vp, i32, vp]),
     "jinf_b200_gemv_q4m_workspace_bytes": (sz, [i32, i32]),

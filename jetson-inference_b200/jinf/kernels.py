@@ -83,6 +83,19 @@ def q4m_pack(aos, q4m, rows: int, cols: int, stream=None) -> None:
     L.check(L.lib.jinf_b200_q4m_pack(_p(aos), _p(q4m), rows, cols, _s(stream)), "jinf_b200_q4m_pack")
 
 
+def gemv_q4m_batch_workspace_bytes(rows: int, cols: int, batch: int) -> int:
+    return int(L.lib.jinf_b200_gemv_q4m_batch_workspace_bytes(rows, cols, batch))
+
+
+def gemv_q4m_batch(q4m, x, y, rows: int, cols: int, batch: int, workspace=None, stream=None) -> None:
+    """Y[b] = W . X[b] for the `batch` rows of X ([batch][cols], fp32 or fp16) -> y [batch][rows]."""
+    import torch
+    xt = L.F32 if x.dtype == torch.float32 else L.F16
+    ws = _p(workspace) if workspace is not None else None
+    L.check(L.lib.jinf_b200_gemv_q4m_batch(_p(q4m), _p(x), xt, _p(y), rows, cols, batch, ws, _s(stream)),
+            "jinf_b200_gemv_q4m_batch")
+
+
 def q4m_bytes_qt(rows: int, cols: int, qtype: int) -> int:
     """Q4M image bytes for qtype Q4_0 (2) or Q4_K (12); 0 for an unsupported type or shape."""
     return int(L.lib.jinf_b200_q4m_bytes_qt(rows, cols, qtype))

@@ -191,3 +191,30 @@ def test_q4k_rejects_partial_superblocks(cuda):
     assert K.q4m_bytes_qt(16, 384, 12) == 0       # not whole 256-element super-blocks
     assert K.q4m_bytes_qt(16, 384, 2) > 0
     assert K.q4m_bytes_qt(16, 256, 8) == 0        # Q8_0: no Q4M form
+
+
+# ---------------------------------------------------------------- batched GEMV (C2 at batch 4 / 8)
+
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 4), (4096, 4096, 8), (1024, 4096, 8), (14336, 4096, 4),
+                                             (4096, 14336, 8), (37, 384, 3), (128256, 4096, 8), (512, 704, 5),
+                                             (4096, 4096, 1)])
+def test_gemv_q4m_batch(cuda, rows, cols, batch):
+    from jinf import kernels as K
+    w = q4_0_rows(rows, cols, seed=rows + cols + batch)
+    x = np.random.default_rng(batch).standard_normal((batch, cols)).astype(np.float16)
+    q = packed(w, rows, cols, cuda)
+    ws = torch.zeros(K.gemv_q4m_batch_workspace_bytes(rows, cols, batch), dtype=torch.uint8, device=cuda)
+    xd = torch.from_numpy(x).to(cuda)
+    y = torch.empty((batch, rows), dtype=torch.float32, device=cuda)
+    y2 = torch.empty_like(y)
+    K.gemv_q4m_batch(q, xd, y, rows, cols, batch, workspace=ws)
+    K.gemv_q4m_batch(q, xd, y2, rows, cols, batch, workspace=ws)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    for b in range(batch):
+        assert rel_err(got[b], oracle.matvec(w, 2, x[b].astype(np.float32), rows, cols)) < REL, f"vector {b}"
+    assert torch.equal(y, y2)
+    if rows * cols <= 4096 * 4096:
+        for b in range(min(batch, 2)):
+            want = q4m_ref.emulate_gemv(q4m_ref.pack(w, rows, cols), x[b].astype(np.float32), rows, cols)
+            assert rel_err(got[b], want) < 1e-5
