@@ -669,7 +669,13 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     for (const auto& ly : I->layers)
         for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) max_cols = std::max(max_cols, sh->cols);
     const unsigned xs = step_xstage_bytes(max_cols, G, I->hd);
-    const size_t smem = step_smem_bytes(xs, 5 * I->L + 1, I->wfmt);
+    // ring depth: STEP_NBUF slots per warp when they fit next to the staged inputs, else 3
+    int nbuf = STEP_NBUF;
+    size_t smem = step_smem_bytes(xs, 5 * I->L + 1, I->wfmt, nbuf);
+    if (smem > 227 * 1024) {
+        nbuf = 3;
+        smem = step_smem_bytes(xs, 5 * I->L + 1, I->wfmt, nbuf);
+    }
     // input records: a tile pair of h is one 32-element block, a CTA's gate|up rows are whole
     // activation blocks and fit the 1024-float conversion buffer, as do a kv head's outputs
     const int gu_pairs = I->layers.empty() ? 0 : I->layers[0].gu_sh.pairs;
@@ -677,7 +683,7 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     const bool records_ok = I->d % 32 == 0 && (I->Hl * I->hd) % 32 == 0 && gu_pairs % 2 == 0 &&
                             gu_per_cta * 16 <= 1024 && G * I->hd <= 1024;
     if (G > ATTN_MAX_GROUP || (G & (G - 1)) || I->Hkvl > 64 || (I->hd != 64 && I->hd != 128) || smem > 227 * 1024 ||
-        step_occupancy(smem, I->wfmt) < 1 || !records_ok) {
+        step_occupancy(smem, I->wfmt, nbuf) < 1 || !records_ok) {
         JINF_LOG("persistent step unavailable for this shape (%zu bytes of shared memory); using one kernel per "
                  "operation", smem);
         return JINF_OK;
@@ -723,6 +729,7 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     sp.eps = I->eps;
     sp.attn_smax = std::max(1, std::min(ATTN_MAX_SPLIT, I->num_sms / I->Hkvl));
     sp.fmt = I->wfmt;
+    sp.nbuf = nbuf;
     sp.xstage_bytes = xs;
     sp.spin_limit = 4000000ull;  // about a second of polling: far beyond any phase, never a hang
     I->sp_full = sp;

@@ -82,6 +82,7 @@ struct StepParams {
     int attn_smax;            // CTAs per kv head at most (grid / kv heads, <= ATTN_MAX_SPLIT)
     int with_argmax;          // the last phase is the LM head: finish the argmax, feed it back
     int fmt;                  // Q4MFormat of every weight matrix of the step
+    int nbuf;                 // weight ring slots per warp: STEP_NBUF, or 3 for wide models
     unsigned int xstage_bytes;  // shared bytes for the staged GEMV input / attention scratch
     unsigned long long spin_limit;  // polls before a dependency wait gives up (DEV_ERR_TIMEOUT)
 };
@@ -93,10 +94,10 @@ __host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)
 // Shared bytes of the staged input for the widest GEMV phase, or of the attention scratch
 // (q of one kv head's query heads + per-warp partials), whichever is larger.
 unsigned int step_xstage_bytes(int max_cols, int group, int head_dim);
-size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt);
+size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt, int nbuf);
 // Launches the step on `grid` CTAs (one per SM) as a cooperative launch.
 cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s);
 // Resident CTAs per SM for this shared-memory size (must be >= 1).
-int step_occupancy(size_t smem, int fmt);
+int step_occupancy(size_t smem, int fmt, int nbuf);
 
 }  // namespace jinf

@@ -12,7 +12,7 @@
 //     order (deterministic, no global atomics), and the CTA reports its finished pairs
 //     with one counter add;
 //   * each warp walks its unit ranges of all matrices in step order with a cp.async ring
-//     (STEP_NBUF - 1 units in flight) feeding the tensor-core decode (q4m_device.cuh), so
+//     (NBUF - 1 units in flight) feeding the tensor-core decode (q4m_device.cuh), so
 //     while a CTA waits for the inputs of the next phase its first weights are already on
 //     their way; the stream's geometry lives in shared memory;
 //   * phases wait on completion counters instead of kernel boundaries (bounded spins:
@@ -187,7 +187,7 @@ struct PieceSum {
 // Consume groups [gb, ge) of one tile pair from the ring (tensor-core decode, q4m_device.cuh),
 // refilling it as it goes. Out of line so that the hot loop gets a register allocation of
 // its own, independent of the rest of the step kernel.
-template <int FMT>
+template <int FMT, int NBUF>
 __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, const PhaseInfo* pinfo, int n_phases,
                                               int C, const XRecS xr, int gb, int ge) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -195,15 +195,15 @@ __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, con
     int slot = ws.slot;
     PieceSum r{{0.f, 0.f, 0.f, 0.f}};
     for (int g = gb; g < ge; ++g) {
-        const int is = slot == 0 ? STEP_NBUF - 1 : slot - 1;
+        const int is = slot == 0 ? NBUF - 1 : slot - 1;
         if (sp.c < sp.c1) {
             copy_unit_fmt<FMT>(ring + is * q4m_unit_bytes(FMT), sp.w + (size_t)sp.c * q4m_unit_bytes(FMT), lane);
             if (++sp.c == sp.c1) sp = stream_seek(pinfo, n_phases, sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
-        asm volatile("cp.async.wait_group %0;" ::"n"(STEP_NBUF - 1) : "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(NBUF - 1) : "memory");
         unit_mma_fmt<FMT>(ring + slot * q4m_unit_bytes(FMT), xr, g, lane, r.acc);
-        slot = slot + 1 == STEP_NBUF ? 0 : slot + 1;
+        slot = slot + 1 == NBUF ? 0 : slot + 1;
     }
     ws.sp = sp;
     ws.slot = slot;
@@ -462,7 +462,7 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
 
 }  // namespace
 
-template <int FMT>
+template <int FMT, int NBUF>
 __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     constexpr int UB = FMT == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT;  // weight unit bytes
     extern __shared__ __align__(16) uint8_t smem[];
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 8192 + 512);
     const uint32_t ring_base = smem_u32(pinfo + ((P.n_phases + 1) & ~1));
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t ring = ring_base + (uint32_t)(warp * STEP_NBUF * UB);
+    const uint32_t ring = ring_base + (uint32_t)(warp * NBUF * UB);
     const int C = gridDim.x;
     DeviceState* st = P.st;
     const int pos = *(volatile int*)&st->pos;
@@ -505,11 +505,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     __syncthreads();
 
     // ---------------- weight stream: this warp's unit ranges of all GEMV phases, copied in
-    // consumption order into the ring (STEP_NBUF - 1 units ahead of the arithmetic)
+    // consumption order into the ring (NBUF - 1 units ahead of the arithmetic)
     WarpStream ws;
     ws.sp = stream_seek(pinfo, P.n_phases, 0, blockIdx.x, C, warp);
     ws.slot = 0;
-    for (int i = 0; i < STEP_NBUF - 1; ++i) {
+    for (int i = 0; i < NBUF - 1; ++i) {
         if (ws.sp.c < ws.sp.c1) {
             copy_unit_fmt<FMT>(ring + i * UB, ws.sp.w + (size_t)ws.sp.c * UB, lane);
             if (++ws.sp.c == ws.sp.c1) ws.sp = stream_seek(pinfo, P.n_phases, ws.sp.ph + 1, blockIdx.x, C, warp);
@@ -724,7 +724,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         int pair = c / G, gb = c - pair * G;  // walked incrementally: no division per piece
         for (; c < c1; ++pair, gb = 0) {
             const int ge = c1 - c < G - gb ? gb + (c1 - c) : G;
-            PieceSum ps = stream_piece<FMT>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
+            PieceSum ps = stream_piece<FMT, NBUF>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
             c += ge - gb;
             if (first_piece && lane == 0) {
                 ftile[warp] = pair;
@@ -821,39 +821,44 @@ unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
     return (unsigned int)((b + 15) & ~(size_t)15);
 }
 
-size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt) {
+size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt, int nbuf) {
     const size_t infos = sizeof(PhaseInfo) * (size_t)((n_phases + 1) & ~1);
-    return (size_t)xstage_bytes + 768 + 8192 + 512 + infos + (size_t)NW * STEP_NBUF * q4m_unit_bytes(fmt);
+    return (size_t)xstage_bytes + 768 + 8192 + 512 + infos + (size_t)NW * nbuf * q4m_unit_bytes(fmt);
 }
 
-template <int FMT>
-static cudaError_t step_configure_t(size_t smem) {
-    static size_t configured[64] = {0};
+// The kernel instances: weight format x ring depth (STEP_NBUF, or 3 when a model's staged
+// inputs leave no room for STEP_NBUF slots).
+typedef void (*StepKernel)(const StepParams);
+static StepKernel step_kernel_for(int fmt, int nbuf) {
+    if (fmt == Q4M_Q4_K) return nbuf == 3 ? k_step<Q4M_Q4_K, 3> : k_step<Q4M_Q4_K, STEP_NBUF>;
+    return nbuf == 3 ? k_step<Q4M_Q4_0, 3> : k_step<Q4M_Q4_0, STEP_NBUF>;
+}
+
+static cudaError_t step_configure(size_t smem, int fmt, int nbuf) {
+    static size_t configured[64][4] = {{0}};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    if (smem <= configured[dev]) return cudaSuccess;
-    const cudaError_t e = cudaFuncSetAttribute(k_step<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess) configured[dev] = smem;
+    const int slot = (fmt == Q4M_Q4_K ? 2 : 0) + (nbuf == 3 ? 1 : 0);
+    if (smem <= configured[dev][slot]) return cudaSuccess;
+    const cudaError_t e =
+        cudaFuncSetAttribute(step_kernel_for(fmt, nbuf), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) configured[dev][slot] = smem;
     return e;
 }
 
-static cudaError_t step_configure(size_t smem, int fmt) {
-    return fmt == Q4M_Q4_K ? step_configure_t<Q4M_Q4_K>(smem) : step_configure_t<Q4M_Q4_0>(smem);
-}
-
-int step_occupancy(size_t smem, int fmt) {
-    if (step_configure(smem, fmt) != cudaSuccess) return 0;
+int step_occupancy(size_t smem, int fmt, int nbuf) {
+    if (step_configure(smem, fmt, nbuf) != cudaSuccess) return 0;
     int n = 0;
-    const cudaError_t e =
-        fmt == Q4M_Q4_K ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_step<Q4M_Q4_K>, STEP_THREADS, smem)
-                        : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_step<Q4M_Q4_0>, STEP_THREADS, smem);
-    return e == cudaSuccess ? n : 0;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, step_kernel_for(fmt, nbuf), STEP_THREADS, smem) ==
+                   cudaSuccess
+               ? n
+               : 0;
 }
 
 cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
-    const size_t smem = step_smem_bytes(p.xstage_bytes, p.n_phases, p.fmt);
-    cudaError_t e = step_configure(smem, p.fmt);
+    const size_t smem = step_smem_bytes(p.xstage_bytes, p.n_phases, p.fmt, p.nbuf);
+    cudaError_t e = step_configure(smem, p.fmt, p.nbuf);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -865,7 +870,7 @@ cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return p.fmt == Q4M_Q4_K ? cudaLaunchKernelEx(&cfg, k_step<Q4M_Q4_K>, p) : cudaLaunchKernelEx(&cfg, k_step<Q4M_Q4_0>, p);
+    return cudaLaunchKernelEx(&cfg, step_kernel_for(p.fmt, p.nbuf), p);
 }
 
 }  // namespace jinf
