@@ -77,8 +77,10 @@ int jinf_sparse_fixed_mask(uint64_t seed, int layer, int n_ff, float keep, int32
 void jinf_sparse_predictor_weights(uint64_t seed, int layer, int which, int64_t n, uint16_t* out);
 // Predictor on the device: z = ReLU(W1 x), s = W2 z (W1, W2 fp16, fp32 sums), then the k
 // largest scores (ties: lower index first) as ids ascending and bundle byte offsets
-// id * bundle_size. d and r multiples of 8; scratch: r + n_ff floats (device). No
-// counterpart in the reference, whose predictor ran on the host.
+// id * bundle_size. d and r multiples of 8 and at most 8192, n_ff <= JINF_TOPK_MAX_N (the scores are selected
+// in one CTA's shared memory); scratch: r + n_ff floats (device). No counterpart in the
+// reference, whose predictor ran on the host.
+#define JINF_TOPK_MAX_N 49152
 jinf_status jinf_b200_sparse_predict(const void* w1, const void* w2, const float* x, int d, int r, int n_ff, int k,
                                      int bundle_size, int32_t* ids, int32_t* offsets, float* scratch,
                                      cudaStream_t stream);

@@ -347,13 +347,22 @@ jinf_status run_op(jinf_engine_impl* I, const Op& op, cudaStream_t s) {
             const size_t ff = (size_t)I->ffl;
             int32_t* ids = I->sparse_ids + (size_t)L * ff;
             int32_t* offs = I->sparse_offs + (size_t)L * ff;
-            e = sparse_ffn_prologue(I->hA, I->y_o, I->hB, I->layers[L].ffn_norm, I->eps, I->d, I->sparse_x, s);
-            if (e == cudaSuccess && I->sparse_mode == 1)
-                e = sparse_predict(I->pred_w1 + (size_t)L * I->pred_r * I->d, I->pred_w2 + (size_t)L * ff * I->pred_r,
-                                   I->sparse_x, I->d, I->pred_r, I->ffl, I->sparse_k, I->bundle_size, ids, offs,
-                                   I->sparse_scratch, s);
+            const uint8_t* bund = I->bundles + (size_t)L * ff * I->bundle_size;
+            if (I->sparse_mode == 2 && sparse_ffn_fused_ok(I->d, I->wtype) && I->sparse_n[L] > 0) {
+                // fixed mask: the prologue runs inside the gate/up kernel
+                e = sparse_ffn_fused(bund, I->hA, I->y_o, I->hB, I->layers[L].ffn_norm, I->eps, I->y_down, offs,
+                                     I->sparse_n[L], I->d, I->bundle_size, I->gate_up_tmp, s);
+                break;
+            }
+            if (I->sparse_mode == 1)  // predictor: the prologue runs inside its first GEMV
+                e = sparse_predict_norm(I->pred_w1 + (size_t)L * I->pred_r * I->d,
+                                        I->pred_w2 + (size_t)L * ff * I->pred_r, I->hA, I->y_o, I->hB,
+                                        I->layers[L].ffn_norm, I->eps, I->sparse_x, I->d, I->pred_r, I->ffl,
+                                        I->sparse_k, I->bundle_size, ids, offs, I->sparse_scratch, s);
+            else
+                e = sparse_ffn_prologue(I->hA, I->y_o, I->hB, I->layers[L].ffn_norm, I->eps, I->d, I->sparse_x, s);
             if (e == cudaSuccess) {
-                jinf_cuda_sparse_ffn(I->bundles + (size_t)L * ff * I->bundle_size, I->sparse_x, I->y_down, offs,
+                jinf_cuda_sparse_ffn(bund, I->sparse_x, I->y_down, offs,
                                      I->sparse_n[L], I->d, I->bundle_size, I->wtype, I->gate_up_tmp, s);
                 e = cudaGetLastError();
             }
@@ -472,8 +481,9 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         o.gp.x = I->attn;
         o.gp.y = I->y_o;
         o.gp.st = I->st;
-        o.gp.pf_ptr = ly.gu;
-        o.gp.pf_bytes = ly.gu_sh.bytes;
+        // the dense gate|up matrix is next, unless the FFN runs over sparse bundles
+        o.gp.pf_ptr = I->sparse_mode ? nullptr : ly.gu;
+        o.gp.pf_bytes = I->sparse_mode ? 0 : ly.gu_sh.bytes;
         finish(o);
         o.bytes = gemv_bytes(ly.o_sh, ly.o_sh.cols, ly.o_sh.rows);
         ops.push_back(o);
@@ -488,6 +498,8 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
             Op sp{OP_SPARSE_FFN};
             sp.layer = L;
             sp.bytes = (uint64_t)I->sparse_n[L] * I->bundle_size;
+            if (I->sparse_mode == 1)  // fp16 predictor W1 [r][d] and W2 [ff][r]
+                sp.bytes += 2ull * I->pred_r * ((uint64_t)I->d + I->ffl);
             ops.push_back(sp);
             continue;
         }
@@ -964,9 +976,12 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     I->sparse_mode = opt.sparse_mode;
     if (I->sparse_mode < 0 || I->sparse_mode > 2 || (I->sparse_mode && (tp > 1 || !(opt.sparse_keep > 0.f) ||
                                                                        opt.sparse_keep > 1.f || I->d % 32 ||
-                                                                       I->d > 8192))) {
-        JINF_LOG("sparse_mode %d (keep %.3f) not supported: modes 0-2, keep in (0, 1], one GPU, d <= 8192",
-                 opt.sparse_mode, opt.sparse_keep);
+                                                                       I->d > 8192 ||
+                                                                       (I->sparse_mode == 1 &&
+                                                                        I->ff > JINF_TOPK_MAX_N)))) {
+        JINF_LOG("sparse_mode %d (keep %.3f) not supported: modes 0-2, keep in (0, 1], one GPU, d <= 8192, "
+                 "predictor n_ff <= %d",
+                 opt.sparse_mode, opt.sparse_keep, JINF_TOPK_MAX_N);
         return fail(JINF_ERR_INVALID);
     }
     if (cudaSetDevice(I->device) != cudaSuccess) {

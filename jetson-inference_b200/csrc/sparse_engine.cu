@@ -21,6 +21,8 @@
 
 #include <math.h>
 
+#include <algorithm>
+
 namespace jinf {
 
 namespace {
@@ -32,57 +34,166 @@ __device__ __forceinline__ uint32_t order_key(float v) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// h = h_in + y_res (stored to h_out), x = h * rsqrt(mean(h^2) + eps) * gain. One CTA.
+// h = h_in + y_res (stored to h_out), x = h * rsqrt(mean(h^2) + eps) * gain. One CTA of 1024
+// threads, d a multiple of 4 and at most 8192: each thread loads its (at most two) 16-byte
+// pieces at once.
 __global__ void __launch_bounds__(1024) k_ffn_prologue(const float* h_in, const float* y_res, float* h_out,
                                                        const float* gain, float eps, int d, float* x) {
     __shared__ float red[32];
+    float4 h[2];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        const float h = h_in[i] + y_res[i];
-        h_out[i] = h;
-        ss = fmaf(h, h, ss);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int i = 4 * (threadIdx.x + 1024 * u);
+        if (i < d) {
+            const float4 a = *reinterpret_cast<const float4*>(h_in + i), c = *reinterpret_cast<const float4*>(y_res + i);
+            h[u] = make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w);
+            *reinterpret_cast<float4*>(h_out + i) = h[u];
+            ss = fmaf(h[u].x, h[u].x, ss);
+            ss = fmaf(h[u].y, h[u].y, ss);
+            ss = fmaf(h[u].z, h[u].z, ss);
+            ss = fmaf(h[u].w, h[u].w, ss);
+        }
     }
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) red[0] = v;
+    const float r = rsqrtf(block_sum(ss, red) / (float)d + eps);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+        const int i = 4 * (threadIdx.x + 1024 * u);
+        if (i < d) {
+            const float4 g = *reinterpret_cast<const float4*>(gain + i);
+            *reinterpret_cast<float4*>(x + i) =
+                make_float4(h[u].x * r * g.x, h[u].y * r * g.y, h[u].z * r * g.z, h[u].w * r * g.w);
+        }
     }
-    __syncthreads();
-    const float r = rsqrtf(red[0] / (float)d + eps);
-    for (int i = threadIdx.x; i < d; i += blockDim.x) x[i] = h_out[i] * r * gain[i];
 }
 
-// y[row] = W[row] . x (fp16 W [rows][cols], cols a multiple of 256), optionally ReLU. A warp
-// per row, eight halves per 16-byte load, fp32 sums in a fixed order.
-__global__ void k_gemv_f16(const __half* __restrict__ w, const float* __restrict__ x, float* __restrict__ y, int rows,
-                           int cols, int relu) {
-    const int lane = threadIdx.x & 31;
-    const int warps = (gridDim.x * blockDim.x) >> 5;
-    for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
-        const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)row * cols);
-        float acc = 0.f;
-        for (int c = lane; c < cols / 8; c += 32) {
-            const uint4 raw = __ldg(wr + c);
-            const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-            const float4 xa = __ldg(reinterpret_cast<const float4*>(x) + 2 * c);
-            const float4 xb = __ldg(reinterpret_cast<const float4*>(x) + 2 * c + 1);
-            const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
-            const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
-            acc = fmaf(f0.x, xa.x, acc);
-            acc = fmaf(f0.y, xa.y, acc);
-            acc = fmaf(f1.x, xa.z, acc);
-            acc = fmaf(f1.y, xa.w, acc);
-            acc = fmaf(f2.x, xb.x, acc);
-            acc = fmaf(f2.y, xb.y, acc);
-            acc = fmaf(f3.x, xb.z, acc);
-            acc = fmaf(f3.y, xb.w, acc);
+// y[row] = W[row] . x (fp16 W [rows][cols], cols a multiple of 8, at most 8192), optionally
+// ReLU. x is staged in shared memory once per CTA: read as is, or (NORM) computed in every
+// CTA as RMSNorm(h_in + y_res) * gain, CTA 0 also storing h_out and x_out. A warp owns
+// 16 / PL rows at a time, PL = 16-byte loads per lane per row (cols <= 256 * PL; PL = 32 walks
+// a row in two passes), and issues all 16 loads before it uses any. fp32 sums in a fixed order.
+struct NormArgs {
+    const float* h_in;
+    const float* y_res;
+    float* h_out;
+    const float* gain;
+    float eps;
+    float* x_out;
+};
+
+template <int PL, bool NORM>
+__global__ void __launch_bounds__(256) k_gemv_f16(const __half* __restrict__ w, const float* __restrict__ x,
+                                                  float* __restrict__ y, int rows, int cols, int relu, NormArgs na) {
+    extern __shared__ float4 xs4[];
+    __shared__ float red[32];
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int n4 = cols >> 2;
+    if (NORM) {
+        float4 h[8];
+        float ss = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = tid + 256 * u;
+            h[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < n4) {
+                const float4 a = __ldg(reinterpret_cast<const float4*>(na.h_in) + i);
+                const float4 c = __ldg(reinterpret_cast<const float4*>(na.y_res) + i);
+                h[u] = make_float4(a.x + c.x, a.y + c.y, a.z + c.z, a.w + c.w);
+                ss = fmaf(h[u].x, h[u].x, ss);
+                ss = fmaf(h[u].y, h[u].y, ss);
+                ss = fmaf(h[u].z, h[u].z, ss);
+                ss = fmaf(h[u].w, h[u].w, ss);
+            }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) y[row] = relu && acc < 0.f ? 0.f : acc;
+        const float r = rsqrtf(block_sum(ss, red) / (float)cols + na.eps);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = tid + 256 * u;
+            if (i < n4) {
+                const float4 g = __ldg(reinterpret_cast<const float4*>(na.gain) + i);
+                const float4 v = make_float4(h[u].x * r * g.x, h[u].y * r * g.y, h[u].z * r * g.z, h[u].w * r * g.w);
+                xs4[i] = v;
+                if (blockIdx.x == 0) {
+                    reinterpret_cast<float4*>(na.h_out)[i] = h[u];
+                    reinterpret_cast<float4*>(na.x_out)[i] = v;
+                }
+            }
+        }
+    } else {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = tid + 256 * u;
+            v[u] = i < n4 ? __ldg(reinterpret_cast<const float4*>(x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (tid + 256 * u < n4) xs4[tid + 256 * u] = v[u];
     }
+    __syncthreads();
+    constexpr int PLC = PL < 16 ? PL : 16;  // loads per row per pass
+    constexpr int R = 16 / PLC;             // rows per warp
+    const int n8 = cols >> 3;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int r0 = ((blockIdx.x * blockDim.x + tid) >> 5) * R; r0 < rows; r0 += nwarps * R) {
+        float acc[R];
+#pragma unroll
+        for (int j = 0; j < R; ++j) acc[j] = 0.f;
+        for (int cb = 0; cb < n8; cb += 32 * PLC) {
+            uint4 raw[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int row = r0 + u / PLC, c = cb + (u % PLC) * 32 + lane;
+                raw[u] = row < rows && c < n8 ? ldg_stream_u4(w + (size_t)row * cols + 8 * (size_t)c)
+                                              : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int c = cb + (u % PLC) * 32 + lane;
+                if (c < n8) {
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw[u]);
+                    const float4 xa = xs4[2 * c], xb = xs4[2 * c + 1];
+                    const float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+                    const float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+                    float a = acc[u / PLC];
+                    a = fmaf(f0.x, xa.x, a);
+                    a = fmaf(f0.y, xa.y, a);
+                    a = fmaf(f1.x, xa.z, a);
+                    a = fmaf(f1.y, xa.w, a);
+                    a = fmaf(f2.x, xb.x, a);
+                    a = fmaf(f2.y, xb.y, a);
+                    a = fmaf(f3.x, xb.z, a);
+                    a = fmaf(f3.y, xb.w, a);
+                    acc[u / PLC] = a;
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            const float t = warp_sum(acc[j]);
+            if (lane == 0 && r0 + j < rows) y[r0 + j] = relu && t < 0.f ? 0.f : t;
+        }
+    }
+}
+
+template <bool NORM>
+cudaError_t launch_gemv_f16(const void* w, const float* x, float* y, int rows, int cols, int relu, const NormArgs& na,
+                            cudaStream_t s) {
+    const int pl = (cols / 8 + 31) / 32;
+    const size_t smem = sizeof(float) * (size_t)cols;
+    const int rpw = pl >= 16 ? 1 : 16 / (pl <= 1 ? 1 : pl <= 2 ? 2 : pl <= 4 ? 4 : pl <= 8 ? 8 : 16);
+    const int64_t warps = (rows + rpw - 1) / rpw;
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, 65535));
+    const __half* wh = (const __half*)w;
+#define JINF_GF16(P) k_gemv_f16<P, NORM><<<grid, 256, smem, s>>>(wh, x, y, rows, cols, relu, na)
+    if (pl <= 1) JINF_GF16(1);
+    else if (pl <= 2) JINF_GF16(2);
+    else if (pl <= 4) JINF_GF16(4);
+    else if (pl <= 8) JINF_GF16(8);
+    else if (pl <= 16) JINF_GF16(16);
+    else JINF_GF16(32);
+#undef JINF_GF16
+    return cudaGetLastError();
 }
 
 // Block-wide exclusive prefix sum of one value per thread (TOPK_THREADS threads).
@@ -115,14 +226,34 @@ __device__ int block_exclusive_scan(int v, int* tmp, int& total) {
 }
 
 // The k largest of s[0..n) (ties: lower index first), ids ascending, and their bundle byte
-// offsets. One CTA: a 4-pass radix select on the ordered keys finds the k-th largest key T,
-// then one ordered compaction keeps every key > T and the first (k - #greater) keys == T.
+// offsets. One CTA with the ordered keys in shared memory: a 4-pass radix select finds the
+// k-th largest key T, then one ordered compaction keeps every key > T and the first
+// (k - #greater) keys == T. Each pass counts a 256-bin histogram in 32 lane-private copies
+// (lane l adds to copy l, so the adds of one warp never meet on an address even when the
+// scores crowd a few bins), sums the copies per bin, and one warp locates the bin that holds
+// the k-th key with a suffix scan.
+constexpr int TOPK_HIST_BYTES = 256 * 32 * 4;
+
 __global__ void __launch_bounds__(TOPK_THREADS) k_topk(const float* __restrict__ s, int n, int k, int bundle_size,
                                                        int32_t* ids, int32_t* offsets) {
+    extern __shared__ uint32_t dyn[];
+    int* hist32 = reinterpret_cast<int*>(dyn);                 // [256 bins][32 lanes]
+    uint32_t* keys = dyn + TOPK_HIST_BYTES / 4;                 // [n]
     __shared__ int hist[256];
     __shared__ int tmp[33];
     __shared__ uint32_t sel[2];  // prefix, remaining
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i0 = tid; i0 < n; i0 += 8 * TOPK_THREADS) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u * TOPK_THREADS;
+            v[u] = i < n ? __ldg(s + i) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (i0 + u * TOPK_THREADS < n) keys[i0 + u * TOPK_THREADS] = order_key(v[u]);
+    }
     if (tid == 0) {
         sel[0] = 0u;
         sel[1] = (uint32_t)k;
@@ -130,23 +261,46 @@ __global__ void __launch_bounds__(TOPK_THREADS) k_topk(const float* __restrict__
     uint32_t mask = 0u;
     for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
-        if (tid < 256) hist[tid] = 0;
+        for (int j = tid; j < 256 * 32; j += TOPK_THREADS) hist32[j] = 0;
         __syncthreads();
         const uint32_t prefix = sel[0];
         for (int i = tid; i < n; i += TOPK_THREADS) {
-            const uint32_t key = order_key(s[i]);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+            const uint32_t key = keys[i];
+            if ((key & mask) == prefix) atomicAdd(&hist32[((key >> shift) & 255) * 32 + lane], 1);
         }
         __syncthreads();
-        if (tid == 0) {
-            uint32_t rem = sel[1];
-            int b = 255;
-            for (; b > 0; --b) {
-                if ((uint32_t)hist[b] >= rem) break;
-                rem -= (uint32_t)hist[b];
+        // warp w sums bins 8w..8w+7 over the 32 copies
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int b = 8 * warp + j;
+            int c = hist32[b * 32 + lane];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(JINF_FULL_MASK, c, o);
+            if (lane == 0) hist[b] = c;
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane l owns bins 8l..8l+7; above = number of keys in the bins of higher lanes
+            int own = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) own += hist[8 * lane + j];
+            int incl = own;  // inclusive suffix sum over lanes l..31
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_down_sync(JINF_FULL_MASK, incl, o);
+                if (lane + o < 32) incl += t;
             }
-            sel[0] = prefix | ((uint32_t)b << shift);
-            sel[1] = rem;  // how many keys equal to the final prefix still to take (after the last pass)
+            const uint32_t rem = sel[1];
+            uint32_t above = (uint32_t)(incl - own);
+            if (above < rem && (uint32_t)incl >= rem) {
+                int b = 8 * lane + 7;
+                for (; b > 8 * lane; --b) {
+                    if (above + (uint32_t)hist[b] >= rem) break;
+                    above += (uint32_t)hist[b];
+                }
+                sel[0] = prefix | ((uint32_t)b << shift);
+                sel[1] = rem - above;  // keys equal to the final prefix still to take (after the last pass)
+            }
         }
         mask |= 255u << shift;
         __syncthreads();
@@ -154,16 +308,16 @@ __global__ void __launch_bounds__(TOPK_THREADS) k_topk(const float* __restrict__
     const uint32_t T = sel[0], need_eq = sel[1];
     // contiguous chunk of indices per thread: ordered compaction
     const int per = (n + TOPK_THREADS - 1) / TOPK_THREADS;
-    const int i0 = tid * per, i1 = min(n, i0 + per);
+    const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
     int n_eq = 0;
-    for (int i = i0; i < i1; ++i) n_eq += order_key(s[i]) == T;
+    for (int i = i0; i < i1; ++i) n_eq += keys[i] == T;
     int tot;
     int eq_base = block_exclusive_scan(n_eq, tmp, tot);
     int n_sel = 0;
     {
         int e = eq_base;
         for (int i = i0; i < i1; ++i) {
-            const uint32_t key = order_key(s[i]);
+            const uint32_t key = keys[i];
             if (key > T) ++n_sel;
             else if (key == T && (uint32_t)(e++) < need_eq) ++n_sel;
         }
@@ -171,7 +325,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) k_topk(const float* __restrict__
     int out = block_exclusive_scan(n_sel, tmp, tot);
     int e = eq_base;
     for (int i = i0; i < i1; ++i) {
-        const uint32_t key = order_key(s[i]);
+        const uint32_t key = keys[i];
         const bool take = key > T || (key == T && (uint32_t)(e++) < need_eq);
         if (take) {
             ids[out] = i;
@@ -241,14 +395,39 @@ cudaError_t sparse_ffn_prologue(const float* h_in, const float* y_res, float* h_
     return cudaGetLastError();
 }
 
+static cudaError_t launch_topk(const float* sc, int n_ff, int k, int bundle_size, int32_t* ids, int32_t* offsets,
+                               cudaStream_t s) {
+    const size_t smem = TOPK_HIST_BYTES + sizeof(uint32_t) * (size_t)n_ff;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(k_topk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k_topk<<<1, TOPK_THREADS, smem, s>>>(sc, n_ff, k, bundle_size, ids, offsets);
+    return cudaGetLastError();
+}
+
 cudaError_t sparse_predict(const void* w1, const void* w2, const float* x, int d, int r, int n_ff, int k,
                            int bundle_size, int32_t* ids, int32_t* offsets, float* scratch, cudaStream_t s) {
     float* z = scratch;
     float* sc = scratch + r;
-    k_gemv_f16<<<grid_for((int64_t)r * 32, 256), 256, 0, s>>>((const __half*)w1, x, z, r, d, 1);
-    k_gemv_f16<<<grid_for((int64_t)n_ff * 32, 256), 256, 0, s>>>((const __half*)w2, z, sc, n_ff, r, 0);
-    k_topk<<<1, TOPK_THREADS, 0, s>>>(sc, n_ff, k, bundle_size, ids, offsets);
-    return cudaGetLastError();
+    const NormArgs none{};
+    cudaError_t e = launch_gemv_f16<false>(w1, x, z, r, d, 1, none, s);
+    if (e == cudaSuccess) e = launch_gemv_f16<false>(w2, z, sc, n_ff, r, 0, none, s);
+    if (e == cudaSuccess) e = launch_topk(sc, n_ff, k, bundle_size, ids, offsets, s);
+    return e;
+}
+
+cudaError_t sparse_predict_norm(const void* w1, const void* w2, const float* h_in, const float* y_res, float* h_out,
+                                const float* gain, float eps, float* x, int d, int r, int n_ff, int k, int bundle_size,
+                                int32_t* ids, int32_t* offsets, float* scratch, cudaStream_t s) {
+    float* z = scratch;
+    float* sc = scratch + r;
+    const NormArgs na{h_in, y_res, h_out, gain, eps, x};
+    const NormArgs none{};
+    cudaError_t e = launch_gemv_f16<true>(w1, nullptr, z, r, d, 1, na, s);
+    if (e == cudaSuccess) e = launch_gemv_f16<false>(w2, z, sc, n_ff, r, 0, none, s);
+    if (e == cudaSuccess) e = launch_topk(sc, n_ff, k, bundle_size, ids, offsets, s);
+    return e;
 }
 
 cudaError_t sparse_bundle_gate_up(const uint8_t* gu_aos, int n_ff, int row_bytes, uint8_t* bundles, int bundle_size,
@@ -285,7 +464,7 @@ extern "C" jinf_status jinf_b200_sparse_predict(const void* w1, const void* w2, 
                                                 int k, int bundle_size, int32_t* ids, int32_t* offsets,
                                                 float* scratch, cudaStream_t stream) {
     if (!w1 || !w2 || !x || !ids || !offsets || !scratch || d <= 0 || d % 8 || r <= 0 || r % 8 ||
-        n_ff <= 0 || k <= 0 || k > n_ff)
+        d > 8192 || r > 8192 || n_ff <= 0 || n_ff > JINF_TOPK_MAX_N || k <= 0 || k > n_ff)
         return JINF_ERR_INVALID;
     return sparse_predict(w1, w2, x, d, r, n_ff, k, bundle_size, ids, offsets, scratch, stream) == cudaSuccess
                ? JINF_OK

@@ -215,15 +215,16 @@ def test_attention_long_context_no_smem_limit(cuda):
     assert rel_err(out.cpu().numpy(), oracle.attention(q, kc, vc, hd, nh, nkv, n)) < REL
 
 
-def make_bundles(hidden, n_ff, qt, seed):
-    """Reference bundle layout: [gate row][up row][down column f32], padded to 4 KB."""
+def make_bundles(hidden, n_ff, qt, seed, extra=None):
+    """Reference bundle layout: [gate row][up row][down column f32], padded to 4 KB (or, with
+    `extra`, to the raw size plus `extra` bytes, which misaligns every other bundle)."""
     rng = np.random.default_rng(seed)
     gate = quant_rows(n_ff, hidden, qt, seed)
     up = quant_rows(n_ff, hidden, qt, seed + 1)
     down = (rng.standard_normal((n_ff, hidden)) * 0.02).astype(np.float32)  # column i of down = row i here
     rb = gate.shape[1]
     raw = 2 * rb + 4 * hidden
-    bsz = (raw + 4095) // 4096 * 4096
+    bsz = (raw + 4095) // 4096 * 4096 if extra is None else raw + extra
     buf = np.zeros((n_ff, bsz), dtype=np.uint8)
     buf[:, :rb] = gate
     buf[:, rb:2 * rb] = up
@@ -251,3 +252,29 @@ def test_sparse_ffn(cuda, qt, n_act):
     else:
         assert rel_err(gu.cpu().numpy()[:n_act], want_gu) < REL
         assert rel_err(out.cpu().numpy(), want) < REL
+
+
+@pytest.mark.parametrize("hidden,n_act,extra,alias", [
+    (4096, 2150, None, False),   # the 8B shape at 15% of 14336 (fewer bundles here)
+    (4096, 333, 4, True),        # every other gate row 4 bytes off 8-byte alignment; out aliases x
+    (8192, 300, 0, False),       # two 128-block rounds per lane
+    (480, 57, 4, True),          # hidden not a multiple of 128: the per-block path
+])
+def test_sparse_ffn_shapes(cuda, hidden, n_act, extra, alias):
+    """Vectorised Q4_0 gate/up and down paths, their alignment fall-backs and an output that
+    aliases the input (the reference engine passes the same buffer, src/engine.cpp:404-408)."""
+    from jinf import kernels as K
+    n_ff = max(n_act + 7, 400)
+    buf, bsz = make_bundles(hidden, n_ff, 2, seed=hidden + n_act, extra=extra)
+    rng = np.random.default_rng(n_act)
+    act = np.sort(rng.choice(n_ff, size=n_act, replace=False)).astype(np.int32)
+    offs = (act.astype(np.int64) * bsz).astype(np.int32)
+    x = rng.standard_normal(hidden).astype(np.float32)
+    want, want_gu = oracle.sparse_ffn(buf, x, offs, n_act, hidden, 2)
+    xd = dev(x, cuda)
+    out = xd if alias else torch.full((hidden,), 5.0, dtype=torch.float32, device=cuda)
+    gu = torch.empty(n_act, dtype=torch.float32, device=cuda)
+    K.sparse_ffn(dev(buf, cuda), xd, out, dev(offs, cuda), n_act, hidden, bsz, 2, gu)
+    torch.cuda.synchronize()
+    assert rel_err(gu.cpu().numpy(), want_gu) < REL
+    assert rel_err(out.cpu().numpy(), want) < REL
