@@ -312,8 +312,13 @@ struct jinf_engine_impl {
     // split-K workspace of the stand-alone GEMV kernels
     float* gemv_part = nullptr;
     unsigned int* gemv_cnt = nullptr;
-    // persistent step (tp_size == 1): phase tables on the device, counters, partials
+    // persistent step: phase tables on the device, counters, partials
     bool persistent = false;
+    // tensor-parallel persistent step: this rank's exchange area and every rank's, mapped
+    // (xpeer[tp_rank] == xchg; the others are IPC mappings of the peers' areas)
+    uint8_t* xchg = nullptr;
+    uint8_t* xpeer[STEP_MAX_TP] = {};
+    XchgLayout xl{};
     int step_grid = 0;
     StepPhase* d_phases = nullptr;  // [n_full + n_body]
     unsigned int* step_done = nullptr;
@@ -596,8 +601,21 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         p.pairs = sh.pairs;
         p.groups = sh.groups;
         p.gran = 1;
+        p.xin = p.xout = -1;
         ph.push_back(p);
         return ph.back();
+    };
+    // tensor parallel: o and down store partials into exchange points 2L and 2L + 1 of every
+    // rank; the next RMSNorm input adds them up (h ping-pongs between hA and hB, so that no
+    // CTA overwrites the h another CTA is still reading)
+    const bool tp = I->tp_size > 1;
+    float* hcur = I->hA;
+    auto tp_input = [&](StepPhase& p, int point) {
+        p.xm = X_RMSNORM_TP;
+        p.xin = point;
+        p.hsrc = hcur;
+        p.hout = hcur == I->hA ? I->hB : I->hA;
+        hcur = p.hout;
     };
     for (int L = 0; L < I->L; ++L) {
         const auto& ly = I->layers[L];
@@ -611,12 +629,14 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         StepPhase& qkv = add_gemv(ly.qkv, ly.qkv_sh, L == 0 ? X_EMBED_NORM : X_RMSNORM, EPI_QKV);
         qkv.hsrc = L == 0 ? I->embed : I->hA;
         qkv.hout = L == 0 ? I->hA : nullptr;
+        if (tp && L > 0) tp_input(qkv, 2 * (L - 1) + 1);
         qkv.norm_w = ly.attn_norm;
         qkv.y = I->q;
         qkv.kcache = kc;
         qkv.vcache = vc;
         StepPhase at{};
         at.kind = PH_ATTN;
+        at.xin = at.xout = -1;
         at.q = I->q;
         at.out = I->attn;
         at.kcache = kc;
@@ -625,22 +645,29 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         at.rec_out = I->step_rec[0];
         at.groups_out = ly.o_sh.groups;
         ph.push_back(at);
-        StepPhase& o = add_gemv(ly.o, ly.o_sh, X_RECORDS, EPI_RESID);
+        StepPhase& o = add_gemv(ly.o, ly.o_sh, X_RECORDS, tp ? EPI_PARTIAL : EPI_RESID);
         o.rec = I->step_rec[0];
         o.y = I->hA;
+        if (tp) o.xout = 2 * L;
         StepPhase& gu = add_gemv(ly.gu, ly.gu_sh, X_RMSNORM, EPI_GATEUP);
         gu.hsrc = I->hA;
+        if (tp) tp_input(gu, 2 * L);
         gu.norm_w = ly.ffn_norm;
         gu.gran = 2;
         gu.rec_out = I->step_rec[2];
         gu.groups_out = ly.down_sh.groups;
-        StepPhase& dn = add_gemv(ly.down, ly.down_sh, X_RECORDS, EPI_RESID);
+        StepPhase& dn = add_gemv(ly.down, ly.down_sh, X_RECORDS, tp ? EPI_PARTIAL : EPI_RESID);
         dn.rec = I->step_rec[2];
         dn.y = I->hA;
+        if (tp) dn.xout = 2 * L + 1;
     }
     if (with_head) {
         StepPhase& lm = add_gemv(I->lm, I->lm_sh, X_RMSNORM, EPI_LMHEAD);
         lm.hsrc = I->hA;
+        if (tp) {
+            tp_input(lm, 2 * (I->L - 1) + 1);
+            lm.hout = nullptr;  // the step's last h is not needed
+        }
         lm.norm_w = I->out_norm;
         lm.y = I->logits;
     }
@@ -670,6 +697,68 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
             if (JINF_STEP_PF_MODE >= 3 && gemv_next && ph[i + 1].epi == EPI_QKV) ph[i].pf[0] = i + 1;  // next qkv
         }
     }
+}
+
+// Tensor-parallel persistent step: allocate this rank's exchange area (zeroed), share its
+// IPC handle with every rank over NCCL and map the peers' areas. Returns false (and logs)
+// when peer mappings are not available; the engine then runs one kernel per operation.
+bool setup_exchange(jinf_engine_impl* I) {
+    const int tp = I->tp_size, rank = I->tp_rank;
+    const NcclApi* n = nccl_api();
+    if (tp > STEP_MAX_TP || !n || !I->comm) return false;
+    I->xl = step_xchg_layout(2 * I->L, tp, I->d);
+    if (cudaMalloc(&I->xchg, I->xl.total) != cudaSuccess) return false;
+    cudaMemset(I->xchg, 0, I->xl.total);
+    cudaDeviceSynchronize();  // zero before any peer can have the handle
+    cudaIpcMemHandle_t mine;
+    if (cudaIpcGetMemHandle(&mine, I->xchg) != cudaSuccess) {
+        JINF_LOG("tensor-parallel persistent step: no IPC handle for the exchange area");
+        cudaGetLastError();
+        return false;
+    }
+    std::vector<cudaIpcMemHandle_t> all(tp);
+    uint8_t* dev = nullptr;
+    if (cudaMalloc(&dev, sizeof(cudaIpcMemHandle_t) * tp) != cudaSuccess) return false;
+    cudaMemcpy(dev + sizeof(cudaIpcMemHandle_t) * rank, &mine, sizeof mine, cudaMemcpyHostToDevice);
+    const bool ok = n->AllGather(dev + sizeof(cudaIpcMemHandle_t) * rank, dev, sizeof(cudaIpcMemHandle_t), ncclUint8,
+                                 I->comm, I->stream) == ncclSuccess &&
+                    cudaStreamSynchronize(I->stream) == cudaSuccess &&
+                    cudaMemcpy(all.data(), dev, sizeof(cudaIpcMemHandle_t) * tp, cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(dev);
+    if (!ok) return false;
+    bool mapped = true;
+    for (int r = 0; r < tp; ++r) {
+        if (r == rank) {
+            I->xpeer[r] = I->xchg;
+            continue;
+        }
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            JINF_LOG("tensor-parallel persistent step: rank %d's exchange area cannot be mapped", r);
+            cudaGetLastError();
+            mapped = false;
+            break;
+        }
+        I->xpeer[r] = (uint8_t*)p;
+    }
+    // every rank must agree: all ranks take the persistent form or none does
+    int* flag = nullptr;
+    int v = mapped ? 1 : 0;
+    if (cudaMalloc(&flag, sizeof(int)) != cudaSuccess) return false;
+    cudaMemcpy(flag, &v, sizeof v, cudaMemcpyHostToDevice);
+    const bool agreed = n->AllReduce(flag, flag, 1, ncclInt32, ncclMin, I->comm, I->stream) == ncclSuccess &&
+                        cudaStreamSynchronize(I->stream) == cudaSuccess &&
+                        cudaMemcpy(&v, flag, sizeof v, cudaMemcpyDeviceToHost) == cudaSuccess && v == 1;
+    cudaFree(flag);
+    return agreed;
+}
+
+void free_exchange(jinf_engine_impl* I) {
+    for (int r = 0; r < STEP_MAX_TP; ++r)
+        if (I->xpeer[r] && I->xpeer[r] != I->xchg) cudaIpcCloseMemHandle(I->xpeer[r]);
+    for (int r = 0; r < STEP_MAX_TP; ++r) I->xpeer[r] = nullptr;
+    if (I->xchg) cudaFree(I->xchg);
+    I->xchg = nullptr;
 }
 
 // Set up the persistent step: phase tables on the device, counters and partial buffers.
@@ -744,6 +833,18 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     sp.nbuf = nbuf;
     sp.xstage_bytes = xs;
     sp.spin_limit = 4000000ull;  // about a second of polling: far beyond any phase, never a hang
+    sp.tp_rank = I->tp_rank;
+    sp.tp_size = I->tp_size;
+    sp.vocab_off = I->vocab_off;
+    if (I->tp_size > 1) {
+        for (int r = 0; r < I->tp_size; ++r) sp.xpeer[r] = I->xpeer[r];
+        sp.x_cnt = I->xl.cnt;
+        sp.x_keycnt = I->xl.keycnt;
+        sp.x_keys = I->xl.keys;
+        sp.x_data = I->xl.data;
+        sp.x_point = I->xl.point;
+        sp.x_slot = I->xl.slot;
+    }
     I->sp_full = sp;
     I->sp_full.phases = I->d_phases;
     I->sp_full.n_phases = (int)full.size();
@@ -888,6 +989,8 @@ void free_impl(jinf_engine_impl* I) {
     if (I->device >= 0) cudaSetDevice(I->device);
     if (I->exec_full) cudaGraphExecDestroy(I->exec_full);
     if (I->exec_body) cudaGraphExecDestroy(I->exec_body);
+    if (I->stream) cudaStreamSynchronize(I->stream);
+    free_exchange(I);  // every write of a peer into this area landed before our last step ended
     if (I->comm) {
         const NcclApi* n = nccl_api();
         if (n) n->CommDestroy(I->comm);
@@ -1206,9 +1309,16 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             return fail(JINF_ERR_OOM);
         cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * pairs);
     }
-    if (tp == 1 && opt.persistent && !I->sparse_mode) {
-        const jinf_status s = setup_persistent(I);
-        if (s != JINF_OK) return fail(s);
+    if (opt.persistent && !I->sparse_mode) {
+        // tensor parallel: the exchange areas first (every rank decides the same way)
+        bool ok = tp == 1 || setup_exchange(I);
+        if (!ok) {
+            JINF_LOG("tensor-parallel persistent step unavailable; using one kernel per operation");
+            free_exchange(I);
+        } else {
+            const jinf_status s = setup_persistent(I);
+            if (s != JINF_OK) return fail(s);
+        }
     }
 
     // ---- step programs

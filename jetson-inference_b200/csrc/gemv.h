@@ -20,8 +20,12 @@ constexpr int GEMV_M_NBUF = JINF_GEMV_M_NBUF;
 
 // X_RECORDS (persistent step only): the input is already staged as digit records in global
 // memory by the phase that produced it (q4m_device.cuh, xrec_bytes).
-enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3, X_RECORDS = 4 };
-enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3, EPI_RESID = 4 };
+// X_RMSNORM_TP (persistent step, tensor parallel): x = RMSNorm(h + the sum of the ranks'
+// partial outputs of the previous row-split GEMV, added in rank order).
+enum XMode { X_PLAIN_F32 = 0, X_PLAIN_F16 = 1, X_RMSNORM = 2, X_EMBED_NORM = 3, X_RECORDS = 4, X_RMSNORM_TP = 5 };
+// EPI_PARTIAL (persistent step, tensor parallel): the rank's partial W x is stored to every
+// rank's exchange slot for it.
+enum EpiMode { EPI_STORE = 0, EPI_QKV = 1, EPI_GATEUP = 2, EPI_LMHEAD = 3, EPI_RESID = 4, EPI_PARTIAL = 5 };
 
 struct GemvParams {
     const uint8_t* w;  // Q4M stream of the matrix

@@ -26,6 +26,7 @@ constexpr int ATTN_MIN_POS = 16;       // positions per CTA below which fewer CT
 
 constexpr int ATTN_MAX_SPLIT = 64;     // CTAs per kv head
 constexpr int ATTN_MAX_GROUP = 8;      // query heads per kv head
+constexpr int STEP_MAX_TP = 8;         // ranks of the tensor-parallel persistent step
 
 enum PhaseKind { PH_GEMV = 0, PH_ATTN = 1 };
 
@@ -41,6 +42,9 @@ struct StepPhase {
     int layer;               // PH_ATTN: layer index (selects its split arrival counters)
     int pf[2];               // GEMV phases (-1: none) whose weights this CTA owns are prefetched
                              // into L2 when the CTA reaches this phase (before its wait)
+    int xin;                 // tensor parallel: exchange point this phase reads (X_RMSNORM_TP; its
+                             // arrival counter replaces `dep`, target per step dep_target * ranks)
+    int xout;                // exchange point this phase writes (EPI_PARTIAL), -1: none
     // PH_GEMV
     int xm, epi;
     const uint8_t* w;        // Q4M matrix
@@ -85,7 +89,27 @@ struct StepParams {
     int nbuf;                 // weight ring slots per warp: STEP_NBUF, or 3 for wide models
     unsigned int xstage_bytes;  // shared bytes for the staged GEMV input / attention scratch
     unsigned long long spin_limit;  // polls before a dependency wait gives up (DEV_ERR_TIMEOUT)
+    // tensor parallel (tp_size > 1): the exchange area of every rank, mapped into this
+    // process (xpeer[tp_rank] is this rank's own), laid out as step_xchg_layout says
+    int tp_rank, tp_size;
+    int vocab_off;           // global id of this rank's first LM-head row
+    uint8_t* xpeer[STEP_MAX_TP];
+    unsigned long long x_cnt, x_keycnt, x_keys, x_data, x_point, x_slot;
 };
+
+// Exchange area of one rank for the tensor-parallel persistent step (same layout on every
+// rank; all offsets 256-byte aligned):
+//   [0, 8)     epoch: steps this rank's persistent kernel has finished (its parity selects
+//              the data and key halves of a step, so a step never overwrites the previous)
+//   cnt        [n_points] u64 arrival counters, monotonic: each rank adds the tile pairs it
+//              stored into an exchange point, so a step's target is (epoch + 1) * ranks * pairs
+//   keycnt     u64 arrival counter of the LM-head argmax keys (target (epoch + 1) * ranks)
+//   keys       [2 parities][STEP_MAX_TP] packed argmax keys
+//   data       [n_points][2 parities][ranks][slot] the ranks' partial outputs (slot = d floats)
+struct XchgLayout {
+    unsigned long long cnt, keycnt, keys, data, point, slot, total;
+};
+XchgLayout step_xchg_layout(int n_points, int tp_size, int d);
 
 // CTA c of C owns tile pairs [step_cta_tile(c), step_cta_tile(c + 1)) of every GEMV phase.
 // (c * T stays far below 2^32: at most a few hundred CTAs times tens of thousands of pairs.)

@@ -62,6 +62,34 @@ __device__ bool wait_ge(const unsigned* c, unsigned target, DeviceState* st, uns
     }
 }
 
+// Tensor-parallel exchange (other ranks' kernels write this rank's exchange area over
+// NVLink): system-scope acquire polls of a monotonic 64-bit counter, bounded like wait_ge.
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ bool wait_ge_sys(const unsigned long long* c, unsigned long long target, DeviceState* st,
+                            unsigned long long limit) {
+    for (unsigned long long it = 0;; ++it) {
+        if (ld_acquire_sys(c) >= target) return true;
+        if (*(volatile int*)&st->error != DEV_OK) return false;
+        if (it >= limit) {
+            atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(32);
+    }
+}
+__device__ __forceinline__ unsigned long long* xchg_cnt(const StepParams& P, int rank, int point) {
+    return reinterpret_cast<unsigned long long*>(P.xpeer[rank] + P.x_cnt) + point;
+}
+// This step's data of exchange point `point` in rank `rank`'s area, slot of rank `src`.
+__device__ __forceinline__ float* xchg_data(const StepParams& P, int rank, int point, unsigned par, int src) {
+    return reinterpret_cast<float*>(P.xpeer[rank] + P.x_data + ((size_t)point * 2 + par) * P.x_point +
+                                    (size_t)src * P.x_slot);
+}
+
 // ---------------------------------------------------------------- bulk copies
 //
 // Inputs staged once per phase (records, attention cache rows) come in by TMA bulk copy
@@ -486,6 +514,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     const int C = gridDim.x;
     DeviceState* st = P.st;
     const int pos = *(volatile int*)&st->pos;
+    // tensor parallel: this step's epoch (steps finished so far, the same on every rank)
+    const bool tp = P.tp_size > 1;
+    const unsigned long long ep = tp ? *(volatile unsigned long long*)P.xpeer[P.tp_rank] : 0ull;
+    const unsigned par = (unsigned)(ep & 1ull);
 
     // stream geometry of every phase -> shared memory
     for (int i = tid; i < P.n_phases; i += STEP_THREADS) {
@@ -526,7 +558,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         StepPhase& d = dsm[ph & 1];
         if (tid == 0) {
             const StepPhase& g = P.phases[ph];
-            flags[ph & 1] = g.dep < 0 ? 1 : (wait_ge(P.done + g.dep, g.dep_target, st, P.spin_limit) ? 1 : 0);
+            if (g.xin >= 0)  // every rank's partials of the previous row-split GEMV
+                flags[ph & 1] = wait_ge_sys(xchg_cnt(P, P.tp_rank, g.xin),
+                                            (ep + 1ull) * (unsigned long long)P.tp_size * g.dep_target, st,
+                                            P.spin_limit)
+                                    ? 1
+                                    : 0;
+            else
+                flags[ph & 1] = g.dep < 0 ? 1 : (wait_ge(P.done + g.dep, g.dep_target, st, P.spin_limit) ? 1 : 0);
         } else if (tid >= 32 && tid < 32 + DWORDS) {  // descriptor -> shared memory while warp 0 polls
             reinterpret_cast<uint32_t*>(&d)[tid - 32] = reinterpret_cast<const uint32_t*>(P.phases + ph)[tid - 32];
         } else if (tid >= 96) {
@@ -677,8 +716,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             const float* hsrc =
                 d.xm == X_EMBED_NORM ? d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols : d.hsrc;
             // the CTA that owns pair 0 stores the embedding row as the residual stream
-            fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps, d.cols, xbase,
-                                        misc, true);
+            const float* parts = d.xm == X_RMSNORM_TP ? xchg_data(P, P.tp_rank, d.xin, par, 0) : nullptr;
+            fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, parts, d.hout, t0 == 0, d.norm_w, P.eps, d.cols, xbase,
+                                        misc, true, P.tp_size, (int)(P.x_slot / 16));
         }
         const XRecS xr{smem_u32(xbase), smem_u32(xbase + (size_t)G * 256)};
         // epilogue arguments are read from the shared descriptor when a tile finishes
@@ -701,7 +741,17 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         // a finished pair, by the whole warp (lanes q < 16 hold rows 2q, 2q+1)
         auto finish_pair = [&](int pr, float v0, float v1) {
             const int q = lane & 15, row = pr * Q4M_PAIR_ROWS + 2 * q;
-            if (d.rec_out && d.epi == EPI_RESID) {
+            if (d.epi == EPI_PARTIAL) {
+                // this rank's partial rows into its slot of every rank's exchange area
+                if (lane < 16 && row < d.rows) {
+                    const float a0 = v0 * fac, a1 = v1 * fac;
+                    for (int r = 0; r < P.tp_size; ++r) {
+                        float* dst = xchg_data(P, r, d.xout, par, P.tp_rank) + row;
+                        if (row + 1 < d.rows) *reinterpret_cast<float2*>(dst) = make_float2(a0, a1);
+                        else dst[0] = a0;
+                    }
+                }
+            } else if (d.rec_out && d.epi == EPI_RESID) {
                 resid_records(d, pr, v0 * fac, v1 * fac);
             } else if (d.rec_out && d.epi == EPI_GATEUP) {
                 // the activation goes to shared memory; whole blocks become records below
@@ -771,7 +821,13 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             __syncthreads();
         }
         if (tid == 0) {
-            __threadfence();
+            if (d.epi == EPI_PARTIAL) {
+                // the CTA's partial rows are in every rank's area before any rank counts them
+                __threadfence_system();
+                for (int r = 0; r < P.tp_size; ++r) atomicAdd_system(xchg_cnt(P, r, d.xout), (unsigned long long)(t1 - t0));
+            } else {
+                __threadfence();
+            }
             atomicAdd(P.done + ph, (unsigned)(t1 - t0));
         }
     }
@@ -779,7 +835,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 
     // ---------------- leave: LM head argmax, then the last CTA finishes the step
     if (P.with_argmax) {
-        u64 key = lmax == -INFINITY ? 0ull : argmax_key(lmax, lidx);
+        u64 key = lmax == -INFINITY ? 0ull : argmax_key(lmax, lidx + P.vocab_off);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const u64 other = __shfl_xor_sync(JINF_FULL_MASK, key, o);
@@ -798,8 +854,26 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         const unsigned old = atomicAdd(P.done + P.n_phases, 1u);
         if (old == gridDim.x - 1) {
             __threadfence();
+            u64 b = P.with_argmax ? atomicAdd(&st->best, 0ull) : 0ull;
+            if (tp) {
+                // every rank's argmax key to every rank, then the largest (the key order puts the
+                // lower global index first on ties). Steps without an LM head exchange a zero key,
+                // so that every rank's step ends only after all writes into its area have landed.
+                u64* keys = reinterpret_cast<u64*>(P.xpeer[P.tp_rank] + P.x_keys) + par * STEP_MAX_TP;
+                for (int r = 0; r < P.tp_size; ++r)
+                    reinterpret_cast<volatile u64*>(P.xpeer[r] + P.x_keys)[par * STEP_MAX_TP + P.tp_rank] = b;
+                __threadfence_system();
+                for (int r = 0; r < P.tp_size; ++r)
+                    atomicAdd_system(reinterpret_cast<unsigned long long*>(P.xpeer[r] + P.x_keycnt), 1ull);
+                if (wait_ge_sys(reinterpret_cast<const unsigned long long*>(P.xpeer[P.tp_rank] + P.x_keycnt),
+                                (ep + 1ull) * (unsigned long long)P.tp_size, st, P.spin_limit)) {
+                    for (int r = 0; r < P.tp_size; ++r) {
+                        const u64 k = __ldcg(keys + r);
+                        b = k > b ? k : b;
+                    }
+                }
+            }
             if (P.with_argmax) {
-                const u64 b = atomicAdd(&st->best, 0ull);
                 st->argmax_token = b ? (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull)) : 0;
                 st->token = st->argmax_token;
                 st->best = 0ull;
@@ -807,6 +881,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             st->pos = pos + 1;
             for (int i = 0; i <= P.n_phases; ++i) P.done[i] = 0u;
             for (int i = 0; i < P.n_attn_cnt; ++i) P.attn_cnt[i] = 0u;
+            if (tp) *reinterpret_cast<volatile unsigned long long*>(P.xpeer[P.tp_rank]) = ep + 1ull;
         }
     }
 }
@@ -819,6 +894,19 @@ unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
     const size_t attn = (size_t)2 * ATTN_CHUNK * head_dim * 2 + (size_t)ATTN_MAX_GROUP * (ATTN_CHUNK + 3) * sizeof(float);
     const size_t b = gemv > attn ? gemv : attn;
     return (unsigned int)((b + 15) & ~(size_t)15);
+}
+
+XchgLayout step_xchg_layout(int n_points, int tp_size, int d) {
+    auto up = [](unsigned long long v) { return (v + 255ull) & ~255ull; };
+    XchgLayout l;
+    l.cnt = 256;
+    l.keycnt = up(l.cnt + 8ull * (unsigned long long)n_points);
+    l.keys = l.keycnt + 256;
+    l.data = up(l.keys + 2ull * STEP_MAX_TP * 8ull);
+    l.slot = up(4ull * (unsigned long long)d);
+    l.point = l.slot * (unsigned long long)tp_size;  // one parity of one point: every rank's slot
+    l.total = l.data + (unsigned long long)n_points * 2ull * l.point;
+    return l;
 }
 
 size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt, int nbuf) {

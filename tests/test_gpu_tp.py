@@ -1,7 +1,8 @@
-"""Tensor-parallel decode (SURVEY 8e shape: q/k/v, gate/up and the vocabulary split by
-rows, o and down by columns, NCCL allreduce after each row-split GEMV) on 2 GPUs, one
-process per GPU: the gathered logits and the greedy tokens match the CPU oracle and the
-single-GPU engine. Skipped with fewer than 2 GPUs."""
+"""Tensor-parallel decode (q/k/v, gate/up and the vocabulary split by rows, o and down by
+columns, a sum over the ranks after each row-split GEMV) on 2 GPUs, one process per GPU, in
+both forms: the persistent step (one kernel per token per rank; the partial outputs cross
+NVLink into every rank's exchange area) and one kernel per operation (NCCL allreduce). The
+gathered logits and the greedy tokens match the CPU oracle. Skipped with fewer than 2 GPUs."""
 import os
 import queue
 
@@ -24,7 +25,7 @@ def rel_err(got, want):
     return float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-30))
 
 
-def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, out_q):
+def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, persistent, out_q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "jetson-inference_b200"))
@@ -33,7 +34,8 @@ def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, out_q):
         torch.cuda.set_device(rank)
         shape = jinf.LlamaShape(*shape_args)
         syn = jinf.SynthModel(shape, seed=0)
-        opts = jinf.b200_options(device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1)
+        opts = jinf.b200_options(device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
+                                 persistent=persistent)
         eng = jinf.Engine.from_synth(syn, max_context=64, options=opts)
         logits = [eng.logits_host(prompt)]
         toks = [eng.last_argmax()]
@@ -50,14 +52,15 @@ def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, out_q):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
 @pytest.mark.parametrize("shape_args", [(4, 512, 8, 2, 1408, 4096, 1e4), (2, 4096, 32, 8, 14336, 32000, 5e5)],
                          ids=["tiny", "8b_layers"])
-def test_tp2_matches_oracle_and_single_gpu(shape_args):
+@pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "per_op"])
+def test_tp2_matches_oracle(shape_args, persistent):
     import jinf
     prompt = [int(t) for t in np.random.default_rng(0).integers(0, shape_args[5], size=8)]
     n_greedy = 4
     nccl_id = jinf.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, nccl_id, shape_args, prompt, n_greedy, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, nccl_id, shape_args, prompt, n_greedy, persistent, q))
              for r in range(WORLD)]
     for p in procs:
         p.start()
@@ -74,7 +77,7 @@ def test_tp2_matches_oracle_and_single_gpu(shape_args):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
-    assert not results[0][2] and not results[1][2], "tensor parallel runs use the kernel-per-operation form"
+    assert results[0][2] == persistent and results[1][2] == persistent, "the requested form runs on both ranks"
     # both ranks see the same gathered logits and argmax tokens
     for a, b in zip(results[0][0], results[1][0]):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
