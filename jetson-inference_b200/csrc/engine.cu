@@ -838,7 +838,6 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     sp.vocab_off = I->vocab_off;
     if (I->tp_size > 1) {
         for (int r = 0; r < I->tp_size; ++r) sp.xpeer[r] = I->xpeer[r];
-        sp.x_cnt = I->xl.cnt;
         sp.x_keycnt = I->xl.keycnt;
         sp.x_keys = I->xl.keys;
         sp.x_data = I->xl.data;

@@ -264,10 +264,9 @@ __device__ __forceinline__ void octet_to_records(float4 v, int lane, int j, uint
 
 // Load one group's input of the calling lane (elements 4 (g*32 + lane) .. +3) for stage_x;
 // zero past cols.
-// X_RMSNORM_TP: `yres` holds `nres` partial vectors, `rstride4` 16-byte pieces apart.
 __device__ __forceinline__ void stage_load(int xm, const void* x, const float* hsrc, const float* yres,
                                            const float* norm_w, int g, int G, int n4, int lane, bool coherent,
-                                           float4& h, float4& gn, int nres = 0, int rstride4 = 0) {
+                                           float4& h, float4& gn) {
     const int i = g * 32 + lane;
     h = make_float4(0.f, 0.f, 0.f, 0.f);
     gn = h;
@@ -287,20 +286,6 @@ __device__ __forceinline__ void stage_load(int xm, const void* x, const float* h
             h.y += r.y;
             h.z += r.z;
             h.w += r.w;
-        } else if (xm == X_RMSNORM_TP) {
-            float4 r[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-                r[k] = k < nres ? ld_f4(yres + (size_t)k * rstride4 * 4, i, true) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                if (k < nres) {
-                    h.x += r[k].x;
-                    h.y += r[k].y;
-                    h.z += r[k].z;
-                    h.w += r[k].w;
-                }
-            }
         }
         gn = reinterpret_cast<const float4*>(norm_w)[i];
     }
@@ -311,12 +296,10 @@ __device__ __forceinline__ void stage_load(int xm, const void* x, const float* h
 template <int NW, int BG, bool NORM>
 __device__ __forceinline__ void stage_batch(int xm, const void* x, const float* hsrc, const float* yres, float* hout,
                                             bool store_h, const float* norm_w, int g0, int G, int n4, int lane,
-                                            bool coherent, uint32_t* dig, float4* prm, float& ss, int nres = 0,
-                                            int rstride4 = 0) {
+                                            bool coherent, uint32_t* dig, float4* prm, float& ss) {
     float4 h[BG], gn[BG];
 #pragma unroll
-    for (int b = 0; b < BG; ++b)
-        stage_load(xm, x, hsrc, yres, norm_w, g0 + b * NW, G, n4, lane, coherent, h[b], gn[b], nres, rstride4);
+    for (int b = 0; b < BG; ++b) stage_load(xm, x, hsrc, yres, norm_w, g0 + b * NW, G, n4, lane, coherent, h[b], gn[b]);
 #pragma unroll
     for (int b = 0; b < BG; ++b) {
         const int g = g0 + b * NW;
@@ -346,20 +329,16 @@ __device__ __forceinline__ void stage_batch(int xm, const void* x, const float* 
 template <int NT>
 __device__ __forceinline__ float stage_x(int xm, const void* x, const float* hsrc, const float* yres, float* hout,
                                          bool store_h_cta, const float* norm_w, float eps, int cols, uint8_t* rec,
-                                         float* misc, bool coherent, int nres = 0, int rstride4 = 0) {
+                                         float* misc, bool coherent) {
     constexpr int NW = NT / 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool norm = xm == X_RMSNORM || xm == X_EMBED_NORM || xm == X_RMSNORM_TP;
+    const bool norm = xm == X_RMSNORM || xm == X_EMBED_NORM;
     const bool store_h = norm && store_h_cta && hout;
     const int G = (cols + Q4M_KG - 1) / Q4M_KG, n4 = cols / 4;
     uint32_t* dig = reinterpret_cast<uint32_t*>(rec);
     float4* prm = reinterpret_cast<float4*>(rec + (size_t)G * 256);
     float ss = 0.f;
-    if (xm == X_RMSNORM_TP) {  // up to 8 partial vectors per group: smaller batches
-        for (int g0 = warp; g0 < G; g0 += NW * 2)
-            stage_batch<NW, 2, true>(xm, x, hsrc, yres, hout, store_h, norm_w, g0, G, n4, lane, coherent, dig, prm, ss,
-                                     nres, rstride4);
-    } else if (norm) {
+    if (norm) {
         for (int g0 = warp; g0 < G; g0 += NW * 4)
             stage_batch<NW, 4, true>(xm, x, hsrc, yres, hout, store_h, norm_w, g0, G, n4, lane, coherent, dig, prm, ss);
     } else {

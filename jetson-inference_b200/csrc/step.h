@@ -43,7 +43,7 @@ struct StepPhase {
     int pf[2];               // GEMV phases (-1: none) whose weights this CTA owns are prefetched
                              // into L2 when the CTA reaches this phase (before its wait)
     int xin;                 // tensor parallel: exchange point this phase reads (X_RMSNORM_TP; its
-                             // arrival counter replaces `dep`, target per step dep_target * ranks)
+                             // staging waits for the flagged words, in place of `dep`), -1: none
     int xout;                // exchange point this phase writes (EPI_PARTIAL), -1: none
     // PH_GEMV
     int xm, epi;
@@ -94,20 +94,20 @@ struct StepParams {
     int tp_rank, tp_size;
     int vocab_off;           // global id of this rank's first LM-head row
     uint8_t* xpeer[STEP_MAX_TP];
-    unsigned long long x_cnt, x_keycnt, x_keys, x_data, x_point, x_slot;
+    unsigned long long x_keycnt, x_keys, x_data, x_point, x_slot;
 };
 
 // Exchange area of one rank for the tensor-parallel persistent step (same layout on every
 // rank; all offsets 256-byte aligned):
 //   [0, 8)     epoch: steps this rank's persistent kernel has finished (its parity selects
 //              the data and key halves of a step, so a step never overwrites the previous)
-//   cnt        [n_points] u64 arrival counters, monotonic: each rank adds the tile pairs it
-//              stored into an exchange point, so a step's target is (epoch + 1) * ranks * pairs
-//   keycnt     u64 arrival counter of the LM-head argmax keys (target (epoch + 1) * ranks)
+//   keycnt     u64 arrival counter of the LM-head argmax keys, monotonic (a step's target is
+//              (epoch + 1) * ranks)
 //   keys       [2 parities][STEP_MAX_TP] packed argmax keys
-//   data       [n_points][2 parities][ranks][slot] the ranks' partial outputs (slot = d floats)
+//   data       [n_points][2 parities][ranks][slot] the ranks' partial outputs: per row one
+//              8-byte word {value bits, epoch + 1} (slot = 8 d bytes)
 struct XchgLayout {
-    unsigned long long cnt, keycnt, keys, data, point, slot, total;
+    unsigned long long keycnt, keys, data, point, slot, total;
 };
 XchgLayout step_xchg_layout(int n_points, int tp_size, int d);
 

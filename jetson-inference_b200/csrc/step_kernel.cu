@@ -32,6 +32,8 @@
 #include "q4m_device.cuh"
 #include "step.h"
 
+#include <algorithm>
+
 #include <math.h>
 
 namespace jinf {
@@ -81,13 +83,28 @@ __device__ bool wait_ge_sys(const unsigned long long* c, unsigned long long targ
         __nanosleep(32);
     }
 }
-__device__ __forceinline__ unsigned long long* xchg_cnt(const StepParams& P, int rank, int point) {
-    return reinterpret_cast<unsigned long long*>(P.xpeer[rank] + P.x_cnt) + point;
+// This step's slot of rank `src` at exchange point `point` in rank `rank`'s area: one 8-byte
+// word per row, {value bits, flag} with flag = this step's epoch + 1 in the high half. An
+// aligned 8-byte word is written and read whole, so a word whose flag matches carries this
+// step's value: the consumer's load is also its wait, with no fence or counter on the way.
+__device__ __forceinline__ unsigned long long* xchg_data(const StepParams& P, int rank, int point, unsigned par,
+                                                         int src) {
+    return reinterpret_cast<unsigned long long*>(P.xpeer[rank] + P.x_data + ((size_t)point * 2 + par) * P.x_point +
+                                                 (size_t)src * P.x_slot);
 }
-// This step's data of exchange point `point` in rank `rank`'s area, slot of rank `src`.
-__device__ __forceinline__ float* xchg_data(const StepParams& P, int rank, int point, unsigned par, int src) {
-    return reinterpret_cast<float*>(P.xpeer[rank] + P.x_data + ((size_t)point * 2 + par) * P.x_point +
-                                    (size_t)src * P.x_slot);
+__device__ __forceinline__ unsigned long long ll_word(float v, uint32_t flag) {
+    return ((unsigned long long)flag << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void st_ll2(unsigned long long* p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ ulonglong2 ld_ll2(const unsigned long long* p) {
+    ulonglong2 v;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ bool ll_ok(const ulonglong2& w, uint32_t flag) {
+    return (uint32_t)(w.x >> 32) == flag && (uint32_t)(w.y >> 32) == flag;
 }
 
 // ---------------------------------------------------------------- bulk copies
@@ -236,6 +253,79 @@ __device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, con
     ws.sp = sp;
     ws.slot = slot;
     return r;
+}
+
+// ---------------------------------------------------------------- tensor-parallel input
+//
+// RMSNorm input after a row-split GEMV on several ranks: h = hsrc + the ranks' partial rows
+// of exchange point `point`, added in rank order (every rank adds the same words in the same
+// order, so every rank holds the same h). Each warp converts whole groups as stage_x does;
+// a lane loads its 4 elements of up to 4 ranks at a time and reloads the words whose flag is
+// not yet this step's, at most `limit` times (then DEV_ERR_TIMEOUT; the step is discarded).
+// h goes to `hout` from the CTA that owns pair 0; the records hold h * gain and the return
+// value is 1 / sqrt(mean(h^2) + eps). Ends with the CTA synchronised.
+// `base`: rank 0's slot of the point in this rank's area; `rs`: words from one slot to the next.
+__device__ __noinline__ float stage_x_tp(const unsigned long long* base, size_t rs, int nranks, float eps,
+                                         unsigned long long limit, const float* hsrc, float* hout, bool store_h,
+                                         const float* norm_w, int cols, uint32_t flag, uint8_t* rec, float* misc,
+                                         DeviceState* st) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = (cols + Q4M_KG - 1) / Q4M_KG, n4 = cols / 4;
+    uint32_t* dig = reinterpret_cast<uint32_t*>(rec);
+    float4* prm = reinterpret_cast<float4*>(rec + (size_t)G * 256);
+    float ss = 0.f;
+    for (int g = warp; g < G; g += NW) {
+        const int i = g * 32 + lane;  // 16-byte piece of h: elements 4i .. 4i + 3
+        float4 h = make_float4(0.f, 0.f, 0.f, 0.f), gn = h;
+        if (i < n4) {
+            h = __ldcg(reinterpret_cast<const float4*>(hsrc) + i);
+            gn = reinterpret_cast<const float4*>(norm_w)[i];
+            for (int r0 = 0; r0 < nranks; r0 += 4) {
+                ulonglong2 w[4][2];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (r0 + k < nranks) {
+                        const unsigned long long* p = base + (size_t)(r0 + k) * rs + 4 * (size_t)i;
+                        w[k][0] = ld_ll2(p);
+                        w[k][1] = ld_ll2(p + 2);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (r0 + k >= nranks) break;
+                    const unsigned long long* p = base + (size_t)(r0 + k) * rs + 4 * (size_t)i;
+                    for (unsigned long long it = 0; !(ll_ok(w[k][0], flag) && ll_ok(w[k][1], flag)); ++it) {
+                        if (it >= limit || *(volatile int*)&st->error != DEV_OK) {
+                            atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
+                            break;
+                        }
+                        __nanosleep(32);
+                        w[k][0] = ld_ll2(p);
+                        w[k][1] = ld_ll2(p + 2);
+                    }
+                    h.x += __uint_as_float((uint32_t)w[k][0].x);
+                    h.y += __uint_as_float((uint32_t)w[k][0].y);
+                    h.z += __uint_as_float((uint32_t)w[k][1].x);
+                    h.w += __uint_as_float((uint32_t)w[k][1].y);
+                }
+            }
+            if (store_h) reinterpret_cast<float4*>(hout)[i] = h;
+            ss = fmaf(h.x, h.x, ss);
+            ss = fmaf(h.y, h.y, ss);
+            ss = fmaf(h.z, h.z, ss);
+            ss = fmaf(h.w, h.w, ss);
+        }
+        const float4 v = make_float4(h.x * gn.x, h.y * gn.y, h.z * gn.z, h.w * gn.w);
+        octet_to_records(v, lane, lane >> 3, dig + g * 64, prm + g * 4);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(JINF_FULL_MASK, ss, o);
+    if (lane == 0) misc[warp] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) ss += misc[w];
+    return rsqrtf(ss / (float)cols + eps);
 }
 
 // ---------------------------------------------------------------- input records
@@ -490,7 +580,7 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
 
 }  // namespace
 
-template <int FMT, int NBUF>
+template <int FMT, int NBUF, bool TP>
 __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     constexpr int UB = FMT == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT;  // weight unit bytes
     extern __shared__ __align__(16) uint8_t smem[];
@@ -514,10 +604,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     const int C = gridDim.x;
     DeviceState* st = P.st;
     const int pos = *(volatile int*)&st->pos;
-    // tensor parallel: this step's epoch (steps finished so far, the same on every rank)
-    const bool tp = P.tp_size > 1;
-    const unsigned long long ep = tp ? *(volatile unsigned long long*)P.xpeer[P.tp_rank] : 0ull;
-    const unsigned par = (unsigned)(ep & 1ull);
+    // tensor parallel: this step's epoch (steps finished so far, the same on every rank; only
+    // the finalizer advances it, after every CTA's last use). Re-read where needed rather
+    // than kept live through the kernel.
+    auto epoch = [&]() -> unsigned long long { return *(volatile unsigned long long*)P.xpeer[P.tp_rank]; };
 
     // stream geometry of every phase -> shared memory
     for (int i = tid; i < P.n_phases; i += STEP_THREADS) {
@@ -558,14 +648,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         StepPhase& d = dsm[ph & 1];
         if (tid == 0) {
             const StepPhase& g = P.phases[ph];
-            if (g.xin >= 0)  // every rank's partials of the previous row-split GEMV
-                flags[ph & 1] = wait_ge_sys(xchg_cnt(P, P.tp_rank, g.xin),
-                                            (ep + 1ull) * (unsigned long long)P.tp_size * g.dep_target, st,
-                                            P.spin_limit)
-                                    ? 1
-                                    : 0;
-            else
-                flags[ph & 1] = g.dep < 0 ? 1 : (wait_ge(P.done + g.dep, g.dep_target, st, P.spin_limit) ? 1 : 0);
+            // (a tensor-parallel input waits in its staging: the flagged words are the signal)
+            flags[ph & 1] = g.dep < 0 || (TP && g.xin >= 0)
+                                ? 1
+                                : (wait_ge(P.done + g.dep, g.dep_target, st, P.spin_limit) ? 1 : 0);
         } else if (tid >= 32 && tid < 32 + DWORDS) {  // descriptor -> shared memory while warp 0 polls
             reinterpret_cast<uint32_t*>(&d)[tid - 32] = reinterpret_cast<const uint32_t*>(P.phases + ph)[tid - 32];
         } else if (tid >= 96) {
@@ -716,9 +802,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             const float* hsrc =
                 d.xm == X_EMBED_NORM ? d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols : d.hsrc;
             // the CTA that owns pair 0 stores the embedding row as the residual stream
-            const float* parts = d.xm == X_RMSNORM_TP ? xchg_data(P, P.tp_rank, d.xin, par, 0) : nullptr;
-            fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, parts, d.hout, t0 == 0, d.norm_w, P.eps, d.cols, xbase,
-                                        misc, true, P.tp_size, (int)(P.x_slot / 16));
+            if (TP && d.xm == X_RMSNORM_TP) {
+                const unsigned long long ep = epoch();
+                fac = stage_x_tp(xchg_data(P, P.tp_rank, d.xin, (unsigned)(ep & 1ull), 0), (size_t)(P.x_slot / 8),
+                                 P.tp_size, P.eps, P.spin_limit, hsrc, d.hout, t0 == 0 && d.hout, d.norm_w, d.cols,
+                                 (uint32_t)(ep + 1ull), xbase, misc, st);
+            } else
+                fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps, d.cols,
+                                            xbase, misc, true);
         }
         const XRecS xr{smem_u32(xbase), smem_u32(xbase + (size_t)G * 256)};
         // epilogue arguments are read from the shared descriptor when a tile finishes
@@ -741,15 +832,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         // a finished pair, by the whole warp (lanes q < 16 hold rows 2q, 2q+1)
         auto finish_pair = [&](int pr, float v0, float v1) {
             const int q = lane & 15, row = pr * Q4M_PAIR_ROWS + 2 * q;
-            if (d.epi == EPI_PARTIAL) {
+            if (TP && d.epi == EPI_PARTIAL) {
                 // this rank's partial rows into its slot of every rank's exchange area
-                if (lane < 16 && row < d.rows) {
-                    const float a0 = v0 * fac, a1 = v1 * fac;
-                    for (int r = 0; r < P.tp_size; ++r) {
-                        float* dst = xchg_data(P, r, d.xout, par, P.tp_rank) + row;
-                        if (row + 1 < d.rows) *reinterpret_cast<float2*>(dst) = make_float2(a0, a1);
-                        else dst[0] = a0;
-                    }
+                if (lane < 16 && row < d.rows) {  // (rows: a multiple of 32)
+                    const unsigned long long ep = epoch();
+                    const uint32_t flag = (uint32_t)(ep + 1ull);
+                    const unsigned long long w0 = ll_word(v0 * fac, flag), w1 = ll_word(v1 * fac, flag);
+                    for (int r = 0; r < P.tp_size; ++r)
+                        st_ll2(xchg_data(P, r, d.xout, (unsigned)(ep & 1ull), P.tp_rank) + row, w0, w1);
                 }
             } else if (d.rec_out && d.epi == EPI_RESID) {
                 resid_records(d, pr, v0 * fac, v1 * fac);
@@ -821,13 +911,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             __syncthreads();
         }
         if (tid == 0) {
-            if (d.epi == EPI_PARTIAL) {
-                // the CTA's partial rows are in every rank's area before any rank counts them
-                __threadfence_system();
-                for (int r = 0; r < P.tp_size; ++r) atomicAdd_system(xchg_cnt(P, r, d.xout), (unsigned long long)(t1 - t0));
-            } else {
-                __threadfence();
-            }
+            __threadfence();
             atomicAdd(P.done + ph, (unsigned)(t1 - t0));
         }
     }
@@ -855,6 +939,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         if (old == gridDim.x - 1) {
             __threadfence();
             u64 b = P.with_argmax ? atomicAdd(&st->best, 0ull) : 0ull;
+            const bool tp = TP && P.tp_size > 1;
+            const unsigned long long ep = tp ? epoch() : 0ull;
+            const unsigned par = (unsigned)(ep & 1ull);
             if (tp) {
                 // every rank's argmax key to every rank, then the largest (the key order puts the
                 // lower global index first on ties). Steps without an LM head exchange a zero key,
@@ -899,11 +986,10 @@ unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
 XchgLayout step_xchg_layout(int n_points, int tp_size, int d) {
     auto up = [](unsigned long long v) { return (v + 255ull) & ~255ull; };
     XchgLayout l;
-    l.cnt = 256;
-    l.keycnt = up(l.cnt + 8ull * (unsigned long long)n_points);
+    l.keycnt = 256;
     l.keys = l.keycnt + 256;
     l.data = up(l.keys + 2ull * STEP_MAX_TP * 8ull);
-    l.slot = up(4ull * (unsigned long long)d);
+    l.slot = up(8ull * (unsigned long long)d);
     l.point = l.slot * (unsigned long long)tp_size;  // one parity of one point: every rank's slot
     l.total = l.data + (unsigned long long)n_points * 2ull * l.point;
     return l;
@@ -915,38 +1001,48 @@ size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt, int nbu
 }
 
 // The kernel instances: weight format x ring depth (STEP_NBUF, or 3 when a model's staged
-// inputs leave no room for STEP_NBUF slots).
+// inputs leave no room for STEP_NBUF slots) x tensor parallel (the single-GPU instance
+// carries none of the exchange code).
 typedef void (*StepKernel)(const StepParams);
-static StepKernel step_kernel_for(int fmt, int nbuf) {
-    if (fmt == Q4M_Q4_K) return nbuf == 3 ? k_step<Q4M_Q4_K, 3> : k_step<Q4M_Q4_K, STEP_NBUF>;
-    return nbuf == 3 ? k_step<Q4M_Q4_0, 3> : k_step<Q4M_Q4_0, STEP_NBUF>;
+static StepKernel step_kernel_for(int fmt, int nbuf, bool tp) {
+    if (tp) {
+        if (fmt == Q4M_Q4_K) return nbuf == 3 ? k_step<Q4M_Q4_K, 3, true> : k_step<Q4M_Q4_K, STEP_NBUF, true>;
+        return nbuf == 3 ? k_step<Q4M_Q4_0, 3, true> : k_step<Q4M_Q4_0, STEP_NBUF, true>;
+    }
+    if (fmt == Q4M_Q4_K) return nbuf == 3 ? k_step<Q4M_Q4_K, 3, false> : k_step<Q4M_Q4_K, STEP_NBUF, false>;
+    return nbuf == 3 ? k_step<Q4M_Q4_0, 3, false> : k_step<Q4M_Q4_0, STEP_NBUF, false>;
 }
 
-static cudaError_t step_configure(size_t smem, int fmt, int nbuf) {
-    static size_t configured[64][4] = {{0}};
+static cudaError_t step_configure(size_t smem, int fmt, int nbuf, bool tp) {
+    static size_t configured[64][8] = {{0}};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    const int slot = (fmt == Q4M_Q4_K ? 2 : 0) + (nbuf == 3 ? 1 : 0);
+    const int slot = (fmt == Q4M_Q4_K ? 2 : 0) + (nbuf == 3 ? 1 : 0) + (tp ? 4 : 0);
     if (smem <= configured[dev][slot]) return cudaSuccess;
     const cudaError_t e =
-        cudaFuncSetAttribute(step_kernel_for(fmt, nbuf), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(step_kernel_for(fmt, nbuf, tp), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e == cudaSuccess) configured[dev][slot] = smem;
     return e;
 }
 
 int step_occupancy(size_t smem, int fmt, int nbuf) {
-    if (step_configure(smem, fmt, nbuf) != cudaSuccess) return 0;
-    int n = 0;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, step_kernel_for(fmt, nbuf), STEP_THREADS, smem) ==
-                   cudaSuccess
-               ? n
-               : 0;
+    int lo = 0;
+    for (const bool tp : {false, true}) {
+        if (step_configure(smem, fmt, nbuf, tp) != cudaSuccess) return 0;
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, step_kernel_for(fmt, nbuf, tp), STEP_THREADS, smem) !=
+            cudaSuccess)
+            return 0;
+        lo = tp ? std::min(lo, n) : n;
+    }
+    return lo;
 }
 
 cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
     const size_t smem = step_smem_bytes(p.xstage_bytes, p.n_phases, p.fmt, p.nbuf);
-    cudaError_t e = step_configure(smem, p.fmt, p.nbuf);
+    const bool tp = p.tp_size > 1;
+    cudaError_t e = step_configure(smem, p.fmt, p.nbuf, tp);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -958,7 +1054,7 @@ cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, step_kernel_for(p.fmt, p.nbuf), p);
+    return cudaLaunchKernelEx(&cfg, step_kernel_for(p.fmt, p.nbuf, tp), p);
 }
 
 }  // namespace jinf
