@@ -371,7 +371,22 @@ struct EpiArgs {
     int nq, nk, head_dim, max_ctx, pos;
     float rope_base;
     bool coherent;  // EPI_RESID reads h through L2
+    // Optional values prepared before the GEMV finished (shared memory, indexed by
+    // row - pre_row0): EPI_RESID the current h of the row, EPI_QKV at the even row of a
+    // q or k pair the RoPE cosine and at the odd row the sine (rope_pair). Null: computed here.
+    const float* pre = nullptr;
+    int pre_row0 = 0;
 };
+
+// RoPE rotation of the adjacent pair (row, row + 1) of a q or k head at position `pos`:
+// theta = base^(-2i / hd), i = the pair's index in its head (reference cuda/rope_kernel.cu).
+__device__ __forceinline__ void rope_pair(int rr, int pos, float base, int head_dim, float& cs, float& sn) {
+    const int i = (rr % head_dim) >> 1;
+    const float theta = powf(base, -2.0f * (float)i / (float)head_dim);
+    const float ang = (float)pos * theta;
+    cs = cosf(ang);
+    sn = sinf(ang);
+}
 
 __device__ __forceinline__ void epilogue_pair(const EpiArgs& a, int row, float v0, float v1, float& lmax, int& lidx) {
     if (row >= a.rows) return;
@@ -384,10 +399,10 @@ __device__ __forceinline__ void epilogue_pair(const EpiArgs& a, int row, float v
         }
     } else if (a.epi == EPI_RESID) {
         // h += W x, the reference's residual add (src/engine.cpp:470-472, 505-507)
-        const float h0 = a.coherent ? __ldcg(a.y + row) : a.y[row];
+        const float h0 = a.pre ? a.pre[row - a.pre_row0] : a.coherent ? __ldcg(a.y + row) : a.y[row];
         a.y[row] = h0 + v0;
         if (row + 1 < a.rows) {
-            const float h1 = a.coherent ? __ldcg(a.y + row + 1) : a.y[row + 1];
+            const float h1 = a.pre ? a.pre[row + 1 - a.pre_row0] : a.coherent ? __ldcg(a.y + row + 1) : a.y[row + 1];
             a.y[row + 1] = h1 + v1;
         }
     } else if (a.epi == EPI_GATEUP) {
@@ -396,10 +411,13 @@ __device__ __forceinline__ void epilogue_pair(const EpiArgs& a, int row, float v
         const int pos = a.pos;
         if (row < a.nq + a.nk) {
             const int rr = row < a.nq ? row : row - a.nq;
-            const int i = (rr % a.head_dim) >> 1;
-            const float theta = powf(a.rope_base, -2.0f * (float)i / (float)a.head_dim);
-            const float ang = (float)pos * theta;
-            const float cs = cosf(ang), sn = sinf(ang);
+            float cs, sn;
+            if (a.pre) {
+                cs = a.pre[row - a.pre_row0];
+                sn = a.pre[row + 1 - a.pre_row0];
+            } else {
+                rope_pair(rr, pos, a.rope_base, a.head_dim, cs, sn);
+            }
             const float o0 = v0 * cs - v1 * sn, o1 = v0 * sn + v1 * cs;
             if (row < a.nq) {
                 a.y[row] = o0;

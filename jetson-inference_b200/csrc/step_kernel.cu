@@ -794,6 +794,25 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         int t0, t1;
         cta_range(blockIdx.x, C, d.pairs, d.gran, t0, t1);
         if (t0 >= t1) continue;
+        // Epilogue inputs that do not depend on this GEMV, prepared now by warps 1.. while
+        // warp 0 starts the input staging (outs_s is free in these phases): the residual rows
+        // of an EPI_RESID phase, the RoPE factors of an EPI_QKV phase. The staging ends with
+        // the CTA synchronised, before any epilogue reads them.
+        const int prow0 = t0 * Q4M_PAIR_ROWS, nprow = (t1 - t0) * Q4M_PAIR_ROWS;
+        const bool pre = ((d.epi == EPI_RESID && !d.rec_out) || d.epi == EPI_QKV) && nprow <= 1024;
+        if (pre && tid >= 32) {
+            for (int i = tid - 32; i < nprow; i += STEP_THREADS - 32) {
+                const int row = prow0 + i;
+                if (d.epi == EPI_RESID) {
+                    outs_s[i] = row < d.rows ? __ldcg(d.y + row) : 0.f;
+                } else if ((i & 1) == 0 && row < P.nq + P.nk) {
+                    float cs, sn;
+                    rope_pair(row < P.nq ? row : row - P.nq, pos, P.rope_base, P.head_dim, cs, sn);
+                    outs_s[i] = cs;
+                    outs_s[i + 1] = sn;
+                }
+            }
+        }
         float fac;
         if (d.xm == X_RECORDS) {
             fac = stage_records(d.rec, d.ssp, d.n_ss, d.cols, P.eps, G, xbase, mbar_rec, par_rec, st, P.spin_limit);
@@ -827,6 +846,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             ea.pos = pos;
             ea.rope_base = P.rope_base;
             ea.coherent = true;
+            ea.pre = pre ? outs_s : nullptr;
+            ea.pre_row0 = prow0;
             epilogue_pair(ea, row, v0 * fac, v1 * fac, lmax, lidx);
         };
         // a finished pair, by the whole warp (lanes q < 16 hold rows 2q, 2q+1)
@@ -891,16 +912,30 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         }
         __syncthreads();
         if (own_pair >= 0) {
-            // add the pieces of the following warps in warp order, then the epilogue
+            // add the pieces of the following warps in warp order, then the epilogue. The
+            // contributing warps are the ones after this warp, up to the first warp with units
+            // that does not continue this pair (warps without units skipped): found with two
+            // ballots over the per-warp tile words, so the piece loads issue back to back.
             const int q = lane & 15;
+            const int ftl = ftile[q], fml = fmid[q];
+            const unsigned bad = __ballot_sync(JINF_FULL_MASK, lane < NW && lane > warp && ftl >= 0 &&
+                                                                   (ftl != own_pair || !fml));
+            const int stop = bad ? __ffs(bad) - 1 : NW;
+            const unsigned good = __ballot_sync(JINF_FULL_MASK, lane < NW && lane > warp && lane < stop && ftl >= 0);
             float v0 = part_s[(warp * 2 + own_slot) * 32 + 2 * q];
             float v1 = part_s[(warp * 2 + own_slot) * 32 + 2 * q + 1];
-            for (int w2 = warp + 1; w2 < NW; ++w2) {
-                const int ft = ftile[w2];
-                if (ft < 0) continue;                       // a warp with no units in this phase
-                if (ft != own_pair || !fmid[w2]) break;     // the next pair starts
-                v0 += part_s[(w2 * 2) * 32 + 2 * q];
-                v1 += part_s[(w2 * 2) * 32 + 2 * q + 1];
+            float p0[NW], p1[NW];
+#pragma unroll
+            for (int w2 = 0; w2 < NW; ++w2) {
+                p0[w2] = (good >> w2) & 1u ? part_s[(w2 * 2) * 32 + 2 * q] : 0.f;
+                p1[w2] = (good >> w2) & 1u ? part_s[(w2 * 2) * 32 + 2 * q + 1] : 0.f;
+            }
+#pragma unroll
+            for (int w2 = 0; w2 < NW; ++w2) {
+                if ((good >> w2) & 1u) {
+                    v0 += p0[w2];
+                    v1 += p1[w2];
+                }
             }
             finish_pair(own_pair, v0, v1);
         }
