@@ -21,8 +21,11 @@ namespace jinf {
 #endif
 constexpr int STEP_THREADS = 512;              // 16 warps, one CTA per SM
 constexpr int STEP_NBUF = JINF_STEP_NBUF;      // ring slots per warp (STEP_NBUF - 1 units in flight)
-constexpr int ATTN_CHUNK = 32;         // attention cache rows staged in shared memory at a time
-constexpr int ATTN_MIN_POS = 16;       // positions per CTA below which fewer CTAs split a kv head
+constexpr int ATTN_PW = 4;             // attention positions per warp in one block (16 warps: 64)
+#ifndef JINF_ATTN_SPLIT_POS
+#define JINF_ATTN_SPLIT_POS 16
+#endif
+constexpr int ATTN_SPLIT_POS = JINF_ATTN_SPLIT_POS;  // positions per CTA below which fewer CTAs split a kv head
 
 constexpr int ATTN_MAX_SPLIT = 64;     // CTAs per kv head
 constexpr int ATTN_MAX_GROUP = 8;      // query heads per kv head

@@ -411,12 +411,12 @@ __device__ __noinline__ void blocks_to_records(const float* vals, int b0, int nb
 //
 // Decode attention over the fp16 cache (math of reference cuda/attention_kernel.cu:45-98:
 // scores q.k / sqrt(hd), GQA head map h -> h / (H/Hkv), max-subtracted softmax, P.V). The
-// positions of a kv head are split over S CTAs (S grows with the context up to the CTAs
-// available per kv head), each walking its positions in chunks of ATTN_CHUNK rows staged in
-// shared memory, with an online softmax across chunks; the splits are merged in a fixed
-// order by the last CTA of the kv head to finish. The rows before `pos` of a CTA's first
-// chunk are requested before the CTA waits for the QKV phase (they were written by earlier
-// tokens), so after the wait only q and the new position's row are still in flight.
+// positions of a kv head are split over S CTAs (S grows with the context, ATTN_SPLIT_POS
+// positions per CTA, up to the CTAs available per kv head); the splits are merged in a
+// fixed order by the CTAs that own the output blocks. Within a CTA the positions go in
+// blocks of 16 warps x ATTN_PW: lanes own head dims, so a warp's load of a cache row is one
+// contiguous 256-byte read (the rows were pulled into L2 during the QKV phase), every load
+// of a block is issued before any arithmetic, and an online softmax joins the blocks.
 
 struct AttnGeom {
     int kvh, sp, S, p0, p1;
@@ -425,7 +425,7 @@ struct AttnGeom {
 // Split of CTA `cta` for a context of pos + 1 positions (false: no attention work).
 __device__ __forceinline__ bool attn_geom(int pos, int n_kv_heads, int s_max, int cta, AttnGeom& a) {
     const int n_pos = pos + 1;
-    int S = (n_pos + ATTN_MIN_POS - 1) / ATTN_MIN_POS;
+    int S = (n_pos + ATTN_SPLIT_POS - 1) / ATTN_SPLIT_POS;
     S = S > s_max ? s_max : S;
     if (cta >= n_kv_heads * S) return false;
     const int per = (n_pos + S - 1) / S;
@@ -438,142 +438,156 @@ __device__ __forceinline__ bool attn_geom(int pos, int n_kv_heads, int s_max, in
     return true;
 }
 
+template <int VD>
+struct HalfVec;  // VD halves of one cache row, as loaded by one lane
+template <>
+struct HalfVec<4> {
+    uint2 r;
+    __device__ __forceinline__ void load(const __half* p) { r = __ldcg(reinterpret_cast<const uint2*>(p)); }
+    __device__ __forceinline__ void zero() { r = make_uint2(0u, 0u); }
+    __device__ __forceinline__ float get(int d) const {
+        const __half2 h = *reinterpret_cast<const __half2*>(d < 2 ? &r.x : &r.y);
+        return (d & 1) ? __high2float(h) : __low2float(h);
+    }
+};
+template <>
+struct HalfVec<2> {
+    uint32_t r;
+    __device__ __forceinline__ void load(const __half* p) { r = __ldcg(reinterpret_cast<const unsigned int*>(p)); }
+    __device__ __forceinline__ void zero() { r = 0u; }
+    __device__ __forceinline__ float get(int d) const {
+        const __half2 h = *reinterpret_cast<const __half2*>(&r);
+        return d ? __high2float(h) : __low2float(h);
+    }
+};
+
 // One CTA's split [p0, p1) of kv head attention, after the QKV phase has finished: q of the
-// gq heads of the kv head at `q`, cache rows at kb / vb. Leaves either the normalised output
-// in `outs` ([gq][HD], shared memory; `part` null) or the split's partial (acc, m, l) in
-// `part` ([gq][HD + 2], global). Cache rows come in by bulk copy on `mbar` (`par` is its
-// next phase); chunk 0's rows before `pos` were requested before the QKV wait (`pre`).
+// GQ heads of the kv head at `q`, cache rows at kb / vb. Leaves either the normalised output
+// in `outs` ([GQ][HD], shared memory; `part` null) or the split's partial (acc, m, l) in
+// `part` ([GQ][HD + 2], global). Shared scratch at `xbase`: step_xstage_bytes covers it.
 template <int HD, int GQ>
-__device__ __noinline__ void attn_split(const float* q, const __half* kb, const __half* vb, int p0, int p1, int pos,
-                                        uint8_t* xbase, float* part, float* outs, uint32_t mbar, uint32_t& par, bool pre,
-                                        DeviceState* st, unsigned long long limit) {
-    constexpr int gq = GQ;
-    constexpr int DG = 32 / GQ;  // lanes per query head in q.k
-    constexpr int D = HD / DG;   // head dims per lane in q.k
-    static_assert(D % 8 == 0 || D == 4 || D == 2, "q.k dims per lane");
+__device__ __noinline__ void attn_split(const float* q, const __half* kb, const __half* vb, int p0, int p1,
+                                        uint8_t* xbase, float* part, float* outs) {
+    constexpr int VD = HD / 32;                               // head dims per lane
+    constexpr int PW = GQ * VD >= 32 ? ATTN_PW / 2 : ATTN_PW;  // positions per warp and block (registers)
+    constexpr int BLK = NW * PW;                              // positions per block
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int qg = lane / DG, dgi = lane % DG;
-    const uint32_t kv_s = smem_u32(xbase);
-    const __half* kvh_s = reinterpret_cast<const __half*>(xbase);         // [2][ATTN_CHUNK][HD]
-    float* w_s = reinterpret_cast<float*>(xbase + 2 * ATTN_CHUNK * HD * 2);  // [gq][ATTN_CHUNK]
-    float* ml_s = w_s + ATTN_MAX_GROUP * ATTN_CHUNK;                         // [gq][3]: m, l, correction
+    float* w_s = reinterpret_cast<float*>(xbase);  // [GQ][BLK] scores, then softmax weights
+    float* ml_s = w_s + GQ * BLK;                   // [GQ][4]: m, l, correction
+    float* red_s = ml_s + 4 * ATTN_MAX_GROUP;       // [NW][GQ][HD] per-warp p.v sums
     const float scale = rsqrtf((float)HD);
-    // this lane's dims [dgi D, dgi D + D) of query head qg (pre-scaled)
-    float qr[D];
+    float qr[GQ][VD];
 #pragma unroll
-    for (int k = 0; k < D; k += 2) {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(q + qg * HD + dgi * D + k));
-        qr[k] = v.x * scale;
-        qr[k + 1] = v.y * scale;
-    }
-    if (tid < gq) {
-        ml_s[tid * 3] = -INFINITY;
-        ml_s[tid * 3 + 1] = 0.f;
-    }
-    const int n_out = gq * HD;
-    float acc0 = 0.f, acc1 = 0.f;  // outputs tid and tid + STEP_THREADS
-    for (int cb = p0; cb < p1; cb += ATTN_CHUNK) {
-        const int n = min(ATTN_CHUNK, p1 - cb);
-        if (cb == p0) {
-            // chunk 0: the rows from pos on (at most the new one) by plain loads
-            const int lo = max(cb, min(pos, cb + n));
-            constexpr int PER_ROW = HD * 2 / 16;
-            for (int i = tid; i < 2 * (cb + n - lo) * PER_ROW; i += STEP_THREADS) {
-                const int v = i >= (cb + n - lo) * PER_ROW, k = v ? i - (cb + n - lo) * PER_ROW : i;
-                const int r = lo + k / PER_ROW, c = k % PER_ROW;
-                const uint4 x = __ldcg(reinterpret_cast<const uint4*>((v ? vb : kb) + (size_t)r * HD) + c);
-                *reinterpret_cast<uint4*>(xbase + ((v ? ATTN_CHUNK : 0) + (r - cb)) * HD * 2 + c * 16) = x;
-            }
-            if (pre) {
-                mbar_wait(mbar, par, st, limit);
-                par ^= 1u;
-            }
+    for (int g = 0; g < GQ; ++g) {
+        if constexpr (VD == 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(q + g * HD) + lane);
+            qr[g][0] = v.x * scale; qr[g][1] = v.y * scale; qr[g][2] = v.z * scale; qr[g][3] = v.w * scale;
         } else {
-            if (tid == 0) {
-                fence_proxy_async();
-                bulk_expect(mbar, (uint32_t)(2 * n * HD * 2));
-                bulk_g2s(kv_s, kb + (size_t)cb * HD, (uint32_t)(n * HD * 2), mbar);
-                bulk_g2s(kv_s + ATTN_CHUNK * HD * 2, vb + (size_t)cb * HD, (uint32_t)(n * HD * 2), mbar);
-            }
-            mbar_wait(mbar, par, st, limit);
-            par ^= 1u;
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(q + g * HD) + lane);
+            qr[g][0] = v.x * scale; qr[g][1] = v.y * scale;
         }
-        __syncthreads();
-        // q.k: warp w takes positions w, w + 16; lane (qg, dgi) sums D dims of query head qg,
-        // then the DG lanes of the head reduce
-        for (int j = warp; j < n; j += NW) {
-            const __half* krow = kvh_s + j * HD + dgi * D;
-            float a = 0.f;
-            if constexpr (D % 8 == 0) {
+    }
+    if (tid < GQ) {
+        ml_s[tid * 4] = -INFINITY;
+        ml_s[tid * 4 + 1] = 0.f;
+    }
+    float acc[GQ][VD];
 #pragma unroll
-                for (int k = 0; k < D / 8; ++k) {
-                    const uint4 raw = reinterpret_cast<const uint4*>(krow)[k];
-                    const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+    for (int g = 0; g < GQ; ++g)
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        const float2 f = __half22float2(h2[t]);
-                        a = fmaf(qr[8 * k + 2 * t], f.x, a);
-                        a = fmaf(qr[8 * k + 2 * t + 1], f.y, a);
-                    }
-                }
+        for (int d = 0; d < VD; ++d) acc[g][d] = 0.f;
+    for (int b0 = p0; b0 < p1; b0 += BLK) {
+        const int n = min(BLK, p1 - b0);
+        // every K and V row piece of this warp's positions warp, warp + 16, ... at once
+        HalfVec<VD> kr[PW], vr[PW];
+#pragma unroll
+        for (int k = 0; k < PW; ++k) {
+            const int j = warp + NW * k;
+            if (j < n) {
+                kr[k].load(kb + (size_t)(b0 + j) * HD + lane * VD);
+                vr[k].load(vb + (size_t)(b0 + j) * HD + lane * VD);
             } else {
-#pragma unroll
-                for (int t = 0; t < D / 2; ++t) {
-                    const float2 f = __half22float2(reinterpret_cast<const __half2*>(krow)[t]);
-                    a = fmaf(qr[2 * t], f.x, a);
-                    a = fmaf(qr[2 * t + 1], f.y, a);
-                }
+                kr[k].zero();
+                vr[k].zero();
             }
+        }
+        // scores: each lane's dims, summed over the warp
 #pragma unroll
-            for (int o = DG / 2; o > 0; o >>= 1) a += __shfl_xor_sync(JINF_FULL_MASK, a, o);
-            if (dgi == 0) w_s[qg * ATTN_CHUNK + j] = a;
+        for (int k = 0; k < PW; ++k) {
+            const int j = warp + NW * k;
+#pragma unroll
+            for (int g = 0; g < GQ; ++g) {
+                float a = 0.f;
+#pragma unroll
+                for (int d = 0; d < VD; ++d) a = fmaf(qr[g][d], kr[k].get(d), a);
+                a = warp_sum(a);
+                if (lane == 0 && j < n) w_s[g * BLK + j] = a;
+            }
         }
         __syncthreads();
-        // online softmax of the chunk, one warp per query head
-        if (warp < gq) {
-            const float sv = lane < n ? w_s[warp * ATTN_CHUNK + lane] : -INFINITY;
-            const float mo = ml_s[warp * 3], mn = fmaxf(mo, warp_max(sv));
-            const float e = lane < n ? expf(sv - mn) : 0.f;
+        // online softmax of the block, one warp per query head
+        if (warp < GQ) {
+            float sv[BLK / 32];
+            float mb = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < BLK / 32; ++t) {
+                const int j = lane + 32 * t;
+                sv[t] = j < n ? w_s[warp * BLK + j] : -INFINITY;
+                mb = fmaxf(mb, sv[t]);
+            }
+            const float mo = ml_s[warp * 4], mn = fmaxf(mo, warp_max(mb));
+            float es = 0.f;
+#pragma unroll
+            for (int t = 0; t < BLK / 32; ++t) {
+                const int j = lane + 32 * t;
+                const float e = j < n ? expf(sv[t] - mn) : 0.f;
+                if (j < BLK) w_s[warp * BLK + j] = e;
+                es += e;
+            }
             const float corr = mo == -INFINITY ? 0.f : expf(mo - mn);
-            const float ln = fmaf(ml_s[warp * 3 + 1], corr, warp_sum(e));
-            w_s[warp * ATTN_CHUNK + lane] = e;
+            const float ln = fmaf(ml_s[warp * 4 + 1], corr, warp_sum(es));
             __syncwarp();
             if (lane == 0) {
-                ml_s[warp * 3] = mn;
-                ml_s[warp * 3 + 1] = ln;
-                ml_s[warp * 3 + 2] = corr;
+                ml_s[warp * 4] = mn;
+                ml_s[warp * 4 + 1] = ln;
+                ml_s[warp * 4 + 2] = corr;
             }
         }
         __syncthreads();
-        // p.v: one output (query head g, dim dd) per thread (two when gq * HD > 512)
+        // p.v over this warp's positions, lanes own dims
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int o = tid + h * STEP_THREADS;
-            if (o >= n_out) break;
-            const int g = o / HD, dd = o % HD;
-            float a = (h ? acc1 : acc0) * ml_s[g * 3 + 2];
-            const float* wr = w_s + g * ATTN_CHUNK;
-            const __half* vr = kvh_s + ATTN_CHUNK * HD + dd;
-            for (int j = 0; j < n; ++j) a = fmaf(wr[j], __half2float(vr[j * HD]), a);
-            if (h) acc1 = a;
-            else acc0 = a;
+        for (int g = 0; g < GQ; ++g) {
+            const float c = ml_s[g * 4 + 2];
+#pragma unroll
+            for (int d = 0; d < VD; ++d) acc[g][d] *= c;
+#pragma unroll
+            for (int k = 0; k < PW; ++k) {
+                const float e = w_s[g * BLK + warp + NW * k];  // 0 past the block's positions
+#pragma unroll
+                for (int d = 0; d < VD; ++d) acc[g][d] = fmaf(e, vr[k].get(d), acc[g][d]);
+            }
         }
-        __syncthreads();  // the next chunk overwrites the rows and the weights
+        __syncthreads();  // the next block overwrites the weights
     }
+    // sum the warps' p.v in warp order
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int o = tid + h * STEP_THREADS;
-        if (o >= n_out) break;
+    for (int g = 0; g < GQ; ++g)
+#pragma unroll
+        for (int d = 0; d < VD; ++d) red_s[(warp * GQ + g) * HD + lane * VD + d] = acc[g][d];
+    __syncthreads();
+    for (int o = tid; o < GQ * HD; o += STEP_THREADS) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) a += red_s[w * GQ * HD + o];
         const int g = o / HD, dd = o % HD;
-        const float a = h ? acc1 : acc0;
         if (part) {
             part[g * (HD + 2) + dd] = a;
             if (dd == 0) {
-                part[g * (HD + 2) + HD] = p1 > p0 ? ml_s[g * 3] : -INFINITY;  // an empty split
-                part[g * (HD + 2) + HD + 1] = ml_s[g * 3 + 1];
+                part[g * (HD + 2) + HD] = p1 > p0 ? ml_s[g * 4] : -INFINITY;  // an empty split
+                part[g * (HD + 2) + HD + 1] = ml_s[g * 4 + 1];
             }
         } else {
-            outs[o] = a / ml_s[g * 3 + 1];
+            outs[o] = a / ml_s[g * 4 + 1];
         }
     }
 }
@@ -595,7 +609,6 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     float* part_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768);   // [NW][2][32] partial rows
     float* outs_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768 + 4096);  // [1024] outputs to convert
     const uint32_t mbar_rec = smem_u32(smem + P.xstage_bytes + 576);  // bulk copies of input records
-    const uint32_t mbar_kv = smem_u32(smem + P.xstage_bytes + 584);   // bulk copies of attention cache rows
     StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 8192);  // [2] descriptors
     PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 8192 + 512);
     const uint32_t ring_base = smem_u32(pinfo + ((P.n_phases + 1) & ~1));
@@ -620,10 +633,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     }
     if (tid == 0) {
         mbar_init(mbar_rec);
-        mbar_init(mbar_kv);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    uint32_t par_rec = 0, par_kv = 0;  // next phase of each mbarrier (the same in every thread)
+    uint32_t par_rec = 0;  // next phase of the records mbarrier (the same in every thread)
     __syncthreads();
 
     // ---------------- weight stream: this warp's unit ranges of all GEMV phases, copied in
@@ -661,20 +673,6 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                     if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C, UB);
                 }
             }
-            AttnGeom a;
-            if (tid == 96 && P.phases[ph].kind == PH_ATTN && attn_geom(pos, P.n_kv_heads, P.attn_smax, blockIdx.x, a)) {
-                // the first chunk's cache rows written by earlier tokens, while warp 0 polls
-                const int hi = min(min(a.p0 + ATTN_CHUNK, a.p1), pos);
-                if (hi > a.p0) {
-                    const StepPhase& g = P.phases[ph];
-                    const size_t off = ((size_t)a.kvh * P.max_ctx + a.p0) * P.head_dim;
-                    const uint32_t rb = (uint32_t)((hi - a.p0) * P.head_dim * 2);
-                    fence_proxy_async();
-                    bulk_expect(mbar_kv, 2 * rb);
-                    bulk_g2s(smem_u32(xbase), g.kcache + off, rb, mbar_kv);
-                    bulk_g2s(smem_u32(xbase) + ATTN_CHUNK * P.head_dim * 2, g.vcache + off, rb, mbar_kv);
-                }
-            }
         }
         __syncthreads();  // also: every warp is done with the previous phase's shared data
         if (!flags[ph & 1]) break;
@@ -689,10 +687,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             const __half* vb = d.vcache + (size_t)a.kvh * P.max_ctx * hd;
             float* gpart =
                 a.S > 1 ? P.attn_part + ((size_t)a.kvh * ATTN_MAX_SPLIT + a.sp) * ATTN_MAX_GROUP * (hd + 2) : nullptr;
-            const bool pre = min(min(a.p0 + ATTN_CHUNK, a.p1), pos) > a.p0;  // as requested above
-#define JINF_ATTN_SPLIT(HD_, GQ_)                                                                            \
-    attn_split<HD_, GQ_>(qh, kb, vb, a.p0, a.p1, pos, xbase, gpart, outs_s, mbar_kv, par_kv, pre, st, \
-                         P.spin_limit)
+#define JINF_ATTN_SPLIT(HD_, GQ_) attn_split<HD_, GQ_>(qh, kb, vb, a.p0, a.p1, xbase, gpart, outs_s)
             if (hd == 64) {
                 if (gq == 8) JINF_ATTN_SPLIT(64, 8);
                 else if (gq == 4) JINF_ATTN_SPLIT(64, 4);
@@ -1013,7 +1008,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
     const size_t G = (size_t)(max_cols + Q4M_KG - 1) / Q4M_KG;
     const size_t gemv = xrec_bytes((int)G);
-    const size_t attn = (size_t)2 * ATTN_CHUNK * head_dim * 2 + (size_t)ATTN_MAX_GROUP * (ATTN_CHUNK + 3) * sizeof(float);
+    // attention: scores [group][NW * ATTN_PW], (m, l, correction) [ATTN_MAX_GROUP][4], p.v sums
+    // [NW][group][head_dim]
+    const size_t attn = sizeof(float) * ((size_t)group * NW * ATTN_PW + 4 * ATTN_MAX_GROUP + (size_t)NW * group * head_dim);
     const size_t b = gemv > attn ? gemv : attn;
     return (unsigned int)((b + 15) & ~(size_t)15);
 }
