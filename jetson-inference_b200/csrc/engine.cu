@@ -224,6 +224,29 @@ __global__ void k_even_rows(const float* in, float* out, int n) {
     if (i < n) out[i] = in[2 * i];
 }
 
+// Sparse FFN in the persistent step (fixed masks): dst row i = src row idx[i] of an AoS
+// matrix (row_bytes each); idx[i] < 0 gives a zero row (scale 0: the row contributes 0).
+__global__ void k_gather_rows(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, const int* __restrict__ idx,
+                              int n, int row_bytes) {
+    const int64_t total = (int64_t)n * row_bytes;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int i = (int)(t / row_bytes), b = (int)(t % row_bytes);
+        const int r = idx[i];
+        dst[t] = r < 0 ? 0 : src[(int64_t)r * row_bytes + b];
+    }
+}
+
+// dst[r][j] = src[r][blk[j]]: the listed column blocks (bb bytes each) of every row.
+__global__ void k_gather_blocks(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, const int* __restrict__ blk,
+                                int rows, int nb_src, int nb, int bb) {
+    const int64_t total = (int64_t)rows * nb * bb;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = t / ((int64_t)nb * bb);
+        const int j = (int)((t / bb) % nb), b = (int)(t % bb);
+        dst[t] = src[(r * nb_src + blk[j]) * bb + b];
+    }
+}
+
 
 enum OpKind { OP_GEMV = 0, OP_ATTN = 1, OP_ALLREDUCE_F32 = 2, OP_ALLREDUCE_MAXU64 = 3, OP_FINALIZE = 4,
               OP_SPARSE_FFN = 5 };
@@ -299,6 +322,11 @@ struct jinf_engine_impl {
     int32_t* sparse_ids = nullptr;   // [L][ff] active neuron ids (ascending)
     int32_t* sparse_offs = nullptr;  // [L][ff] their bundle byte offsets
     std::vector<int> sparse_n;       // active neurons per layer
+    // fixed masks in the persistent step: per layer the 32-neuron blocks that hold an active
+    // neuron (ascending) and the active flags; gate|up and down are stored compacted to them
+    bool sparse_persistent = false;
+    std::vector<std::vector<int>> sparse_blocks;
+    std::vector<std::vector<uint8_t>> sparse_active;
     float* sparse_x = nullptr;       // [d] normalised FFN input
     float* sparse_scratch = nullptr; // [r + ff] predictor scores
     float* gate_up_tmp = nullptr;    // [ff]
@@ -878,6 +906,37 @@ struct Loader {
         return JINF_OK;
     }
 
+    // Replace the staged matrix by a gather of it (via a scratch buffer of the same size).
+    jinf_status gather_rows(const std::vector<int>& idx, int row_bytes) {
+        uint8_t* tmp = nullptr;
+        int* didx = nullptr;
+        JINF_CUDA_CHECK(cudaMalloc(&tmp, (size_t)idx.size() * row_bytes));
+        JINF_CUDA_CHECK(cudaMalloc(&didx, sizeof(int) * idx.size()));
+        JINF_CUDA_CHECK(cudaMemcpy(didx, idx.data(), sizeof(int) * idx.size(), cudaMemcpyHostToDevice));
+        k_gather_rows<<<1184, 256, 0, I->stream>>>(dstage, tmp, didx, (int)idx.size(), row_bytes);
+        JINF_CUDA_CHECK(cudaGetLastError());
+        JINF_CUDA_CHECK(cudaMemcpyAsync(dstage, tmp, (size_t)idx.size() * row_bytes, cudaMemcpyDeviceToDevice, I->stream));
+        JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+        cudaFree(tmp);
+        cudaFree(didx);
+        return JINF_OK;
+    }
+    jinf_status gather_blocks(const std::vector<int>& blk, int rows, int nb_src, int bb) {
+        uint8_t* tmp = nullptr;
+        int* dblk = nullptr;
+        const size_t bytes = (size_t)rows * blk.size() * bb;
+        JINF_CUDA_CHECK(cudaMalloc(&tmp, bytes));
+        JINF_CUDA_CHECK(cudaMalloc(&dblk, sizeof(int) * blk.size()));
+        JINF_CUDA_CHECK(cudaMemcpy(dblk, blk.data(), sizeof(int) * blk.size(), cudaMemcpyHostToDevice));
+        k_gather_blocks<<<1184, 256, 0, I->stream>>>(dstage, tmp, dblk, rows, nb_src, (int)blk.size(), bb);
+        JINF_CUDA_CHECK(cudaGetLastError());
+        JINF_CUDA_CHECK(cudaMemcpyAsync(dstage, tmp, bytes, cudaMemcpyDeviceToDevice, I->stream));
+        JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+        cudaFree(tmp);
+        cudaFree(dblk);
+        return JINF_OK;
+    }
+
     // Stage rows [r0, r0+nr) x columns [c0, c0+nc) of Q4_0 tensor `name` as AoS blocks into
     // the device staging buffer, row i at staging row dst_row0 + i*dst_step (pitch
     // dst_row_bytes). Synthetic models are generated in place on the device; files are
@@ -1095,6 +1154,25 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     cudaEventCreate(&I->ev0);
     cudaEventCreate(&I->ev1);
 
+    // ---- fixed masks in the persistent step: gate|up and down compacted to the 32-neuron
+    // blocks that hold an active neuron (Q4_0 only: its blocks are 32 columns wide)
+    I->sparse_persistent = I->sparse_mode == 2 && opt.persistent && tp == 1 && I->wtype == JINF_TYPE_Q4_0 &&
+                           I->ffl % 32 == 0;
+    if (I->sparse_persistent) {
+        std::vector<int32_t> ids(I->ffl);
+        I->sparse_blocks.assign(I->L, {});
+        I->sparse_active.assign(I->L, std::vector<uint8_t>(I->ffl, 0));
+        for (int L = 0; L < I->L; ++L) {
+            const int n = jinf_sparse_fixed_mask(opt.sparse_seed, L, I->ffl, opt.sparse_keep, ids.data());
+            for (int i = 0; i < n; ++i) {
+                I->sparse_active[L][ids[i]] = 1;
+                const int b = ids[i] / 32;
+                if (I->sparse_blocks[L].empty() || I->sparse_blocks[L].back() != b) I->sparse_blocks[L].push_back(b);
+            }
+            if (I->sparse_blocks[L].empty()) I->sparse_blocks[L].push_back(0);  // keep a non-empty (all-zero) FFN
+        }
+    }
+
     // ---- shapes and arena layout (consumption order)
     const int d = I->d, hd = I->hd;
     const int qkv_rows = (I->Hl + 2 * I->Hkvl) * hd;
@@ -1109,8 +1187,9 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     };
     for (int L = 0; L < I->L; ++L) {
         auto& ly = I->layers[L];
+        const int ffc = I->sparse_persistent ? 32 * (int)I->sparse_blocks[L].size() : I->ffl;  // FFN width stored
         if (!place(ly.qkv_sh, qkv_rows, d, ly.qkv) || !place(ly.o_sh, d, I->Hl * hd, ly.o) ||
-            !place(ly.gu_sh, 2 * I->ffl, d, ly.gu) || !place(ly.down_sh, d, I->ffl, ly.down)) {
+            !place(ly.gu_sh, 2 * ffc, d, ly.gu) || !place(ly.down_sh, d, ffc, ly.down)) {
             JINF_LOG("matrix shapes not supported by the Q4M layout (columns must be whole %d-element blocks)",
                      I->wfmt == Q4M_Q4_K ? 256 : 32);
             return fail(JINF_ERR_INVALID);
@@ -1261,6 +1340,17 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             if (s == JINF_OK && bl && sparse_bundle_gate_up(ld.dstage, I->ffl, (int)rb_d, bl, I->bundle_size,
                                                             I->stream) != cudaSuccess)
                 s = JINF_ERR_CUDA;
+            if (s == JINF_OK && I->sparse_persistent) {
+                // the gate and up rows of every neuron of the kept blocks; inactive ones zeroed
+                std::vector<int> idx;
+                for (const int b : I->sparse_blocks[L])
+                    for (int k = 0; k < 32; ++k) {
+                        const int n = 32 * b + k;
+                        idx.push_back(I->sparse_active[L][n] ? 2 * n : -1);
+                        idx.push_back(I->sparse_active[L][n] ? 2 * n + 1 : -1);
+                    }
+                s = ld.gather_rows(idx, (int)rb_d);
+            }
             if (s == JINF_OK) s = ld.pack(ly.gu, ly.gu_sh);
             // down: every output row, this rank's neuron columns (row split)
             if (s == JINF_OK) {
@@ -1270,6 +1360,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             if (s == JINF_OK && bl && sparse_bundle_down(ld.dstage, d, I->ffl, I->wtype, bl, I->bundle_size,
                                                          (int)(2 * rb_d), I->stream) != cudaSuccess)
                 s = JINF_ERR_CUDA;
+            if (s == JINF_OK && I->sparse_persistent)  // the kept blocks' columns (whole Q4_0 blocks)
+                s = ld.gather_blocks(I->sparse_blocks[L], d, I->ffl / 32, 18);
             if (s == JINF_OK) s = ld.pack(ly.down, ly.down_sh);
         }
         I->out_norm = I->norms + (size_t)(2 * I->L) * d;
@@ -1308,7 +1400,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             return fail(JINF_ERR_OOM);
         cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * pairs);
     }
-    if (opt.persistent && !I->sparse_mode) {
+    if (opt.persistent && (!I->sparse_mode || I->sparse_persistent)) {
         // tensor parallel: the exchange areas first (every rank decides the same way)
         bool ok = tp == 1 || setup_exchange(I);
         if (!ok) {

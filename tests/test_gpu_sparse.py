@@ -66,13 +66,17 @@ def prompt():
     return [int(t) for t in np.random.default_rng(1).integers(0, 4096, size=12)]
 
 
-def test_sparse_fixed_mask_decode_matches_masked_oracle(cuda, tiny, prompt):
+@pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "per_op"])
+def test_sparse_fixed_mask_decode_matches_masked_oracle(cuda, tiny, prompt, persistent):
+    """Fixed masks in both forms: the persistent step over gate|up and down compacted to the
+    32-neuron blocks that hold an active neuron (inactive rows zeroed), and the kernel per
+    operation over the reference's neuron bundles."""
     import jinf
     keep, seed = 0.15, 3
     eng = jinf.Engine.from_synth(tiny, max_context=96,
                                  options=jinf.b200_options(eos_token=-1, sparse_mode=2, sparse_keep=keep,
-                                                           sparse_seed=seed))
-    assert not eng.persistent
+                                                           sparse_seed=seed, persistent=persistent))
+    assert eng.persistent == persistent
     orc = oracle.OracleModel(tiny, max_ctx=96, kv_f16=True)
     for L in range(tiny.shape.n_layers):
         ids = fixed_mask(seed, L, tiny.shape.n_ff, keep)
