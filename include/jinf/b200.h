@@ -85,6 +85,18 @@ jinf_status jinf_b200_sparse_predict(const void* w1, const void* w2, const float
                                      int bundle_size, int32_t* ids, int32_t* offsets, float* scratch,
                                      cudaStream_t stream);
 
+// ---- activation profiles (the reference's static-predictor file format, see
+// jinf_engine_config.predictor_path): int32 n_layers, n_ff, total_tokens, then n_layers x n_ff
+// float32 frequencies. Writer of reference tools/profile_activations.cpp:143-162: frequency =
+// counts[l][n] / total_tokens. Reader of reference src/activation_predictor.cpp:226-300: the
+// active neurons of layer l are those with frequency > threshold, written ascending to
+// ids[l * n_ff ...] with their count in n_active[l]. JINF_ERR_INVALID when the file is of
+// another shape, JINF_ERR_PARSE when it is truncated.
+jinf_status jinf_activation_profile_write(const char* path, int n_layers, int n_ff, int total_tokens,
+                                          const int32_t* counts);
+jinf_status jinf_activation_profile_read(const char* path, float threshold, int n_layers, int n_ff, int32_t* ids,
+                                         int32_t* n_active);
+
 // Workspace bytes needed by jinf_b200_attention_f16 for this shape.
 size_t jinf_b200_attention_workspace_bytes(int n_kv_heads, int head_dim, int max_ctx);
 

@@ -166,6 +166,13 @@ int         jinf_engine_is_persistent(const jinf_engine* e);
 // at most `max` written to the host array `ids`); *n their count. JINF_ERR_INVALID in
 // dense mode.
 jinf_status jinf_engine_sparse_ids(jinf_engine* e, int layer, int32_t* ids, int max, int* n);
+// Calibration (reference tools/profile_activations.cpp): forward `n_tokens` tokens from the
+// current position and add to counts[l * n_ff + n] (host) one for every token on which
+// |SiLU(gate_n)| of layer l exceeds `threshold`. Counted on the device, no host copy per
+// layer. Dense FFN, one GPU. jinf_activation_profile_write turns the counts into the
+// profile that jinf_engine_config.predictor_path reads.
+jinf_status jinf_engine_count_activations(jinf_engine* e, const int32_t* tokens, int n_tokens, float threshold,
+                                          int32_t* counts);
 // Bytes of quantized weights this rank streams per token (algorithmic weight traffic).
 uint64_t    jinf_engine_weight_bytes_per_token(const jinf_engine* e);
 // Time one launch of each fused kernel kind on its own (CUDA events, `reps` repetitions

@@ -224,6 +224,15 @@ __global__ void k_even_rows(const float* in, float* out, int n) {
     if (i < n) out[i] = in[2 * i];
 }
 
+// Calibration: counts[n] += 1 where |SiLU(gate[n])| > thr (reference
+// tools/profile_activations.cpp:56-68, counted on the device instead of after a host copy).
+__global__ void k_count_active(const float* __restrict__ gate, int n, float thr, int32_t* __restrict__ counts) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float g = gate[i];
+    if (fabsf(g / (1.0f + expf(-g))) > thr) counts[i] += 1;
+}
+
 // Sparse FFN in the persistent step (fixed masks): dst row i = src row idx[i] of an AoS
 // matrix (row_bytes each); idx[i] < 0 gives a zero row (scale 0: the row contributes 0).
 __global__ void k_gather_rows(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, const int* __restrict__ idx,
@@ -325,6 +334,10 @@ struct jinf_engine_impl {
     // fixed masks in the persistent step: per layer the 32-neuron blocks that hold an active
     // neuron (ascending) and the active flags; gate|up and down are stored compacted to them
     bool sparse_persistent = false;
+    std::vector<std::vector<int32_t>> static_ids;  // mode 2: the active neurons of each layer
+    // calibration (jinf_engine_count_activations): device counters [L][ffl] while counting
+    int32_t* count_dev = nullptr;
+    float count_thr = 0.f;
     std::vector<std::vector<int>> sparse_blocks;
     std::vector<std::vector<uint8_t>> sparse_active;
     float* sparse_x = nullptr;       // [d] normalised FFN input
@@ -1156,14 +1169,39 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
 
     // ---- fixed masks in the persistent step: gate|up and down compacted to the 32-neuron
     // blocks that hold an active neuron (Q4_0 only: its blocks are 32 columns wide)
+    // the static active sets of mode 2: the reference's activation profile when the config
+    // names one (reference src/engine.cpp:228-252: a profile that cannot be read leaves the
+    // FFN dense), else the seeded fixed masks
+    if (cfg->predictor_path && tp == 1 && I->d <= 8192) {
+        std::vector<int32_t> ids((size_t)I->L * I->ffl), cnt(I->L);
+        const jinf_status ps = jinf_activation_profile_read(cfg->predictor_path, cfg->sparsity_threshold, I->L, I->ffl,
+                                                            ids.data(), cnt.data());
+        if (ps == JINF_OK) {
+            I->sparse_mode = 2;
+            I->static_ids.assign(I->L, {});
+            for (int L = 0; L < I->L; ++L)
+                I->static_ids[L].assign(ids.begin() + (size_t)L * I->ffl, ids.begin() + (size_t)L * I->ffl + cnt[L]);
+            JINF_LOG("static predictor %s (threshold %.2f): sparse FFN", cfg->predictor_path, cfg->sparsity_threshold);
+        } else {
+            JINF_LOG("Warning: cannot use the activation profile %s (%s); dense FFN", cfg->predictor_path,
+                     jinf_status_str(ps));
+        }
+    } else if (I->sparse_mode == 2) {
+        std::vector<int32_t> ids(I->ffl);
+        I->static_ids.assign(I->L, {});
+        for (int L = 0; L < I->L; ++L) {
+            const int n = jinf_sparse_fixed_mask(opt.sparse_seed, L, I->ffl, opt.sparse_keep, ids.data());
+            I->static_ids[L].assign(ids.begin(), ids.begin() + n);
+        }
+    }
     I->sparse_persistent = I->sparse_mode == 2 && opt.persistent && tp == 1 && I->wtype == JINF_TYPE_Q4_0 &&
                            I->ffl % 32 == 0;
     if (I->sparse_persistent) {
-        std::vector<int32_t> ids(I->ffl);
         I->sparse_blocks.assign(I->L, {});
         I->sparse_active.assign(I->L, std::vector<uint8_t>(I->ffl, 0));
         for (int L = 0; L < I->L; ++L) {
-            const int n = jinf_sparse_fixed_mask(opt.sparse_seed, L, I->ffl, opt.sparse_keep, ids.data());
+            const std::vector<int32_t>& ids = I->static_ids[L];
+            const int n = (int)ids.size();
             for (int i = 0; i < n; ++i) {
                 I->sparse_active[L][ids[i]] = 1;
                 const int b = ids[i] / 32;
@@ -1254,9 +1292,11 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             for (int L = 0; L < I->L; ++L) I->sparse_n[L] = I->sparse_k;
         } else {
             for (int L = 0; L < I->L; ++L) {
-                I->sparse_n[L] = jinf_sparse_fixed_mask(opt.sparse_seed, L, I->ffl, opt.sparse_keep, ids.data() + L * ff);
-                for (int i = 0; i < I->sparse_n[L]; ++i)
+                I->sparse_n[L] = (int)I->static_ids[L].size();
+                for (int i = 0; i < I->sparse_n[L]; ++i) {
+                    ids[L * ff + i] = I->static_ids[L][i];
                     offs[L * ff + i] = ids[L * ff + i] * I->bundle_size;
+                }
             }
         }
         bool sok = cudaMalloc(&I->bundles, (size_t)I->L * ff * I->bundle_size) == cudaSuccess &&
@@ -1451,7 +1491,7 @@ jinf_status step(jinf_engine* e, bool with_head) {
         JINF_LOG("context full (%d positions)", I->max_ctx);
         return JINF_ERR_INVALID;
     }
-    if (e->ffn_hook) {
+    if (e->ffn_hook || I->count_dev) {
         // Layer-by-layer path that exposes the raw gate pre-activation of each layer.
         const std::vector<Op>& ops = with_head ? I->ops_full : I->ops_body;
         for (const Op& op : ops) {
@@ -1471,8 +1511,14 @@ jinf_status step(jinf_engine* e, bool with_head) {
                 JINF_CUDA_CHECK(gemvm_launch(gp, X_RMSNORM, EPI_STORE, op.grid, I->stream, false));
                 k_even_rows<<<(I->ffl + 255) / 256, 256, 0, I->stream>>>(I->gate_raw + I->ffl, I->gate_raw, I->ffl);
                 JINF_CUDA_CHECK(cudaGetLastError());
-                JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
-                e->ffn_hook(e->ffn_hook_data, op.layer, I->gate_raw, I->ffl);
+                if (I->count_dev) {
+                    k_count_active<<<(I->ffl + 255) / 256, 256, 0, I->stream>>>(
+                        I->gate_raw, I->ffl, I->count_thr, I->count_dev + (size_t)op.layer * I->ffl);
+                    JINF_CUDA_CHECK(cudaGetLastError());
+                } else {
+                    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+                    e->ffn_hook(e->ffn_hook_data, op.layer, I->gate_raw, I->ffl);
+                }
             }
         }
     } else if (I->persistent) {
@@ -1664,6 +1710,31 @@ extern "C" jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uin
 
 extern "C" int jinf_engine_is_persistent(const jinf_engine* e) {
     return e && e->impl && e->impl->persistent ? 1 : 0;
+}
+
+extern "C" jinf_status jinf_engine_count_activations(jinf_engine* e, const int32_t* tokens, int n_tokens,
+                                                    float threshold, int32_t* counts) {
+    if (!e || !e->impl || !tokens || n_tokens <= 0 || !counts) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    if (I->tp_size != 1 || I->sparse_mode) {
+        JINF_LOG("activation counting needs the dense FFN on one GPU");
+        return JINF_ERR_INVALID;
+    }
+    cudaSetDevice(I->device);
+    const size_t n = (size_t)I->L * I->ffl;
+    JINF_CUDA_CHECK(cudaMalloc(&I->count_dev, sizeof(int32_t) * n));
+    JINF_CUDA_CHECK(cudaMemset(I->count_dev, 0, sizeof(int32_t) * n));
+    I->count_thr = threshold;
+    float* logits = nullptr;
+    const jinf_status s = jinf_engine_forward(e, tokens, n_tokens, &logits);
+    std::vector<int32_t> add(n);
+    const bool copied = cudaMemcpy(add.data(), I->count_dev, sizeof(int32_t) * n, cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(I->count_dev);
+    I->count_dev = nullptr;
+    if (s != JINF_OK) return s;
+    if (!copied) return JINF_ERR_CUDA;
+    for (size_t i = 0; i < n; ++i) counts[i] += add[i];
+    return JINF_OK;
 }
 
 extern "C" jinf_status jinf_engine_sparse_ids(jinf_engine* e, int layer, int32_t* ids, int max, int* n) {

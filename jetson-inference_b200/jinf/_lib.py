@@ -225,6 +225,9 @@ SIGNATURES = {
     "jinf_engine_fill_kv_random": (i32, [C.POINTER(Engine), i32, u64]),
     "jinf_engine_is_persistent": (i32, [vp]),
     "jinf_engine_sparse_ids": (i32, [vp, i32, vp, i32, vp]),
+    "jinf_engine_count_activations": (i32, [vp, vp, i32, C.c_float, vp]),
+    "jinf_activation_profile_write": (i32, [C.c_char_p, i32, i32, i32, vp]),
+    "jinf_activation_profile_read": (i32, [C.c_char_p, C.c_float, i32, i32, vp, vp]),
     "jinf_sparse_fixed_mask": (i32, [C.c_uint64, i32, i32, C.c_float, vp]),
     "jinf_sparse_predictor_weights": (None, [C.c_uint64, i32, i32, i64, vp]),
     "jinf_b200_sparse_predict": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp]),

@@ -163,9 +163,14 @@ class Engine:
 
     @classmethod
     def from_synth(cls, model: SynthModel, max_context: int = 512,
-                   options: L.B200Options | None = None) -> "Engine":
+                   options: L.B200Options | None = None, predictor_path: str | None = None,
+                   sparsity_threshold: float = 0.5) -> "Engine":
+        """`predictor_path`: an activation profile in the reference's format (static predictor:
+        the neurons with frequency > sparsity_threshold run, the FFN in sparse mode)."""
         cfg = L.EngineConfig()
-        cfg.max_context, cfg.io_queue_depth, cfg.sparsity_threshold = max_context, 64, 0.5
+        cfg.max_context, cfg.io_queue_depth, cfg.sparsity_threshold = max_context, 64, sparsity_threshold
+        if predictor_path:
+            cfg.predictor_path = predictor_path.encode()
         opts = options if options is not None else b200_options()
         e = C.POINTER(L.Engine)()
         L.check(L.lib.jinf_engine_create_synthetic(C.byref(e), C.byref(cfg), model.handle, C.byref(opts)),
@@ -247,6 +252,14 @@ class Engine:
         L.check(L.lib.jinf_engine_sparse_ids(self.h, layer, out.ctypes.data_as(C.c_void_p), n.value, C.byref(n)),
                 "jinf_engine_sparse_ids")
         return out
+
+    def count_activations(self, tokens, threshold: float, counts: np.ndarray) -> None:
+        """Calibration: forward `tokens`, adding to counts [n_layers, n_ff] (int32) the tokens
+        on which |SiLU(gate)| > threshold (reference tools/profile_activations.cpp)."""
+        assert counts.dtype == np.int32 and counts.flags.c_contiguous
+        arr = np.ascontiguousarray(tokens, dtype=np.int32)
+        L.check(L.lib.jinf_engine_count_activations(self.h, arr.ctypes.data_as(C.c_void_p), len(arr), threshold,
+                                                    counts.ctypes.data_as(C.c_void_p)), "jinf_engine_count_activations")
 
     def weight_bytes_per_token(self) -> int:
         return L.lib.jinf_engine_weight_bytes_per_token(self.h)

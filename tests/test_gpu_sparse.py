@@ -132,3 +132,90 @@ def test_sparse_mode_rejects_bad_options(cuda, tiny):
     for opts in (dict(sparse_mode=3), dict(sparse_mode=1, sparse_keep=0.0), dict(sparse_mode=2, sparse_keep=1.5)):
         with pytest.raises(jinf.JinfError):
             jinf.Engine.from_synth(tiny, max_context=32, options=jinf.b200_options(**opts))
+
+
+def _cudart():
+    for name in ("libcudart.so", "libcudart.so.12"):
+        try:
+            lib = C.CDLL(name)
+            lib.cudaMemcpy.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int]
+            return lib
+        except OSError:
+            continue
+    pytest.skip("no CUDA runtime library to copy the hook's gate")
+
+
+def test_count_activations_matches_host_hook_counting(cuda, tiny, prompt):
+    """Device-side calibration counts equal the reference tool's method: the FFN hook's gate
+    copied to the host, |SiLU(g)| > threshold counted there (tools/profile_activations.cpp)."""
+    import jinf
+    from jinf import _lib as L
+    thr = 0.05
+    eng = jinf.Engine.from_synth(tiny, max_context=96, options=jinf.b200_options(eos_token=-1))
+    n_layers, n_ff = tiny.shape.n_layers, tiny.shape.n_ff
+    got = np.zeros((n_layers, n_ff), np.int32)
+    eng.count_activations(prompt, thr, got)
+    eng.reset()
+    want = np.zeros((n_layers, n_ff), np.int64)
+    rt = _cudart()
+    buf = np.empty(n_ff, np.float32)
+
+    def hook(_data, layer, gate, n):
+        assert rt.cudaMemcpy(buf.ctypes.data, gate, 4 * n, 2) == 0
+        g = buf[:n]
+        silu = g / (np.float32(1.0) + np.exp(-g))
+        want[layer, :n] += np.abs(silu) > np.float32(thr)
+
+    cb = L.FFN_HOOK(hook)
+    eng.h.contents.ffn_hook = cb
+    eng.logits_host(prompt)
+    eng.h.contents.ffn_hook = L.FFN_HOOK()
+    eng.close()
+    assert got.sum() > 0
+    # expf on the device and exp on the host may round a value at the threshold differently
+    assert np.sum(got != want) <= 2, np.argwhere(got != want)[:8]
+
+
+def test_predictor_path_static_profile_matches_oracle(cuda, tiny, prompt, tmp_path):
+    """jinf_engine_config.predictor_path: the reference's static predictor (neurons whose
+    profiled frequency exceeds sparsity_threshold), in the persistent step."""
+    import jinf
+    from jinf.calibrate import write_profile
+    n_layers, n_ff = tiny.shape.n_layers, tiny.shape.n_ff
+    rng = np.random.default_rng(9)
+    counts = rng.integers(0, 1000, size=(n_layers, n_ff)).astype(np.int32)
+    path = str(tmp_path / "act.bin")
+    write_profile(path, counts, 1000)
+    thr = 0.8
+    eng = jinf.Engine.from_synth(tiny, max_context=96, options=jinf.b200_options(eos_token=-1),
+                                 predictor_path=path, sparsity_threshold=thr)
+    assert eng.persistent
+    orc = oracle.OracleModel(tiny, max_ctx=96, kv_f16=True)
+    for L in range(n_layers):
+        ids = np.nonzero(counts[L].astype(np.float32) / np.float32(1000) > np.float32(thr))[0]
+        assert np.array_equal(eng.sparse_ids(L), ids)
+        orc.set_ffn_mask(L, ids.astype(np.int32))
+    want = None
+    for t in prompt:
+        want = orc.forward(t)
+    got = eng.logits_host(prompt)
+    assert rel_err(got, want) < LOGIT_REL
+    for step in range(8):
+        tok = oracle.argmax(want)
+        assert eng.last_argmax() == tok, f"step {step}"
+        want = orc.forward(tok)
+        got = eng.logits_host([tok])
+        assert rel_err(got, want) < LOGIT_REL, f"step {step}"
+
+
+def test_predictor_path_that_cannot_be_read_leaves_the_ffn_dense(cuda, tiny, prompt, tmp_path):
+    import jinf
+    eng = jinf.Engine.from_synth(tiny, max_context=96, options=jinf.b200_options(eos_token=-1),
+                                 predictor_path=str(tmp_path / "missing.bin"))
+    with pytest.raises(Exception):
+        eng.sparse_ids(0)
+    orc = oracle.OracleModel(tiny, max_ctx=96, kv_f16=True)
+    want = None
+    for t in prompt:
+        want = orc.forward(t)
+    assert rel_err(eng.logits_host(prompt), want) < LOGIT_REL
