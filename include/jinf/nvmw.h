@@ -106,6 +106,12 @@ jinf_status jinf_nvmw_writer_add_tensor_entry(jinf_nvmw_writer* w, const jinf_nv
 jinf_status jinf_nvmw_writer_write_hot(jinf_nvmw_writer* w, const void* data, size_t size);
 jinf_status jinf_nvmw_writer_write_cold_layer(jinf_nvmw_writer* w, int layer, const void* data, size_t size);
 jinf_status jinf_nvmw_writer_finalize(jinf_nvmw_writer* w);
+
+// GGUF -> NVMW conversion as the reference's tools/prepare_model writes it (the same file,
+// byte for byte): the split plan for `gpu_budget_mb`, hot and per-layer cold tensors 4 KB
+// padded, and with `bundled` the neuron bundles (gate row, up row, fp32 down column) and
+// their index (version 2). New: the reference has it only as a command-line tool.
+jinf_status jinf_prepare_model(const char* gguf_path, const char* nvmw_path, size_t gpu_budget_mb, int bundled);
 jinf_status jinf_nvmw_writer_write_bundle_section(jinf_nvmw_writer* w,
                                                   const jinf_nvmw_bundle_header* bh,
                                                   const jinf_nvmw_bundle_layer_desc* layer_descs,
