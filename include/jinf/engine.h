@@ -173,6 +173,11 @@ jinf_status jinf_engine_sparse_ids(jinf_engine* e, int layer, int32_t* ids, int 
 // profile that jinf_engine_config.predictor_path reads.
 jinf_status jinf_engine_count_activations(jinf_engine* e, const int32_t* tokens, int n_tokens, float threshold,
                                           int32_t* counts);
+// Failure-path check of the persistent step (one GPU): runs one step whose attention phase
+// waits for a count that nothing reaches, with `spin_limit` polls per wait. Every CTA gives
+// up, the step returns JINF_ERR_TIMEOUT and the context stays usable; the engine's state is
+// then undefined until jinf_engine_reset.
+jinf_status jinf_engine_debug_step_timeout(jinf_engine* e, unsigned long long spin_limit);
 // Bytes of quantized weights this rank streams per token (algorithmic weight traffic).
 uint64_t    jinf_engine_weight_bytes_per_token(const jinf_engine* e);
 // Time one launch of each fused kernel kind on its own (CUDA events, `reps` repetitions

@@ -1712,6 +1712,37 @@ extern "C" int jinf_engine_is_persistent(const jinf_engine* e) {
     return e && e->impl && e->impl->persistent ? 1 : 0;
 }
 
+extern "C" jinf_status jinf_engine_debug_step_timeout(jinf_engine* e, unsigned long long spin_limit) {
+    if (!e || !e->impl || spin_limit == 0) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    if (!I->persistent || I->tp_size != 1) return JINF_ERR_INVALID;
+    cudaSetDevice(I->device);
+    // a copy of the phase table whose attention phase waits for more finished QKV tile
+    // pairs than exist: nothing ever sets what it waits for
+    StepParams sp = I->sp_full;
+    std::vector<StepPhase> ph((size_t)sp.n_phases);
+    JINF_CUDA_CHECK(cudaMemcpy(ph.data(), sp.phases, sizeof(StepPhase) * ph.size(), cudaMemcpyDeviceToHost));
+    for (auto& p : ph)
+        if (p.kind == PH_ATTN) {
+            p.dep_target = 0xFFFFFFFFu;
+            break;
+        }
+    StepPhase* dph = nullptr;
+    JINF_CUDA_CHECK(cudaMalloc(&dph, sizeof(StepPhase) * ph.size()));
+    JINF_CUDA_CHECK(cudaMemcpy(dph, ph.data(), sizeof(StepPhase) * ph.size(), cudaMemcpyHostToDevice));
+    sp.phases = dph;
+    sp.spin_limit = spin_limit;
+    const cudaError_t le = step_launch(sp, I->step_grid, I->stream);
+    int32_t err = DEV_OK;
+    const cudaError_t ce = cudaStreamSynchronize(I->stream);
+    cudaMemcpy(&err, &I->st->error, sizeof err, cudaMemcpyDeviceToHost);
+    cudaFree(dph);
+    if (le != cudaSuccess || ce != cudaSuccess) return JINF_ERR_CUDA;
+    // the step is discarded: clear the recorded error; the caller resets the engine
+    cudaMemset(&I->st->error, 0, sizeof(int32_t));
+    return err == DEV_ERR_TIMEOUT ? JINF_ERR_TIMEOUT : err == DEV_OK ? JINF_OK : JINF_ERR_CUDA;
+}
+
 extern "C" jinf_status jinf_engine_count_activations(jinf_engine* e, const int32_t* tokens, int n_tokens,
                                                     float threshold, int32_t* counts) {
     if (!e || !e->impl || !tokens || n_tokens <= 0 || !counts) return JINF_ERR_INVALID;

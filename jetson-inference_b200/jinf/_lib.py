@@ -227,6 +227,7 @@ SIGNATURES = {
     "jinf_engine_is_persistent": (i32, [vp]),
     "jinf_engine_sparse_ids": (i32, [vp, i32, vp, i32, vp]),
     "jinf_engine_count_activations": (i32, [vp, vp, i32, C.c_float, vp]),
+    "jinf_engine_debug_step_timeout": (i32, [vp, C.c_ulonglong]),
     "jinf_activation_profile_write": (i32, [C.c_char_p, i32, i32, i32, vp]),
     "jinf_activation_profile_read": (i32, [C.c_char_p, C.c_float, i32, i32, vp, vp]),
     "jinf_sparse_fixed_mask": (i32, [C.c_uint64, i32, i32, C.c_float, vp]),
