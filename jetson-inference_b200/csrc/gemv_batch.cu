@@ -43,7 +43,14 @@ struct BatchParams {
     unsigned* cnt;  // [pairs]
 };
 
-__host__ __device__ inline size_t batch_rec_bytes(int batch, int gk) { return (size_t)batch * gk * 320; }
+// Staged records: digits [batch][gk][256 B] then params [batch][gk][4][16 B], each vector's
+// run padded (digits +64 B, params +16 B) so that the lanes of one load that read different
+// vectors fall in different shared-memory banks.
+__host__ __device__ inline int batch_dig_stride(int gk) { return gk * 256 + 64; }  // bytes per vector
+__host__ __device__ inline int batch_prm_stride(int gk) { return gk * 64 + 16; }
+__host__ __device__ inline size_t batch_rec_bytes(int batch, int gk) {
+    return (size_t)batch * (batch_dig_stride(gk) + batch_prm_stride(gk));
+}
 
 // One unit against the staged groups `gl` (local index) of vectors 4 vb .. 4 vb + 3:
 // lane (gr, c) adds vector 4 vb + c's block sums of rows gr, gr+8 (tile A) and 16+gr, 24+gr
@@ -60,13 +67,13 @@ __device__ __forceinline__ void unit_batch(const uint32_t (&w)[16], const uint32
         if (v < batch)
             asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
                          : "=r"(b0), "=r"(b1)
-                         : "r"(dig + (uint32_t)((v * gk + gl) * 256 + ((2 * j + h) * 4 + c) * 8)));
+                         : "r"(dig + (uint32_t)(v * batch_dig_stride(gk) + gl * 256 + ((2 * j + h) * 4 + c) * 8)));
         int kh = 0, kl = 0;
         float ia = 0.f, ib = 0.f;
         if (vo < batch)
             asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
                          : "=r"(kh), "=r"(kl), "=f"(ia), "=f"(ib)
-                         : "r"(prm + (uint32_t)(((vo * gk + gl) * 4 + j) * 16)));
+                         : "r"(prm + (uint32_t)(vo * batch_prm_stride(gk) + (gl * 4 + j) * 16)));
         int da[4] = {kh, kl, kh, kl};
         int db[4] = {kh * 16, kl * 16, kh * 16, kl * 16};
         mma_u8s8(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), b0, b1, da);
@@ -85,9 +92,9 @@ __global__ void __launch_bounds__(BT, 1) k_gemv_q4m_batch(const BatchParams p) {
     const int G = p.groups, kw = p.kw, gk = p.gk;
     const int kp = blockIdx.x % kw, cgrid = gridDim.x / kw, cidx = blockIdx.x / kw;
     const int g0 = kp * G / kw, g1 = (kp + 1) * G / kw, ng = g1 - g0;
-    uint8_t* rec = smem_b;  // digits [batch][gk][256], then params [batch][gk][4][16]
+    uint8_t* rec = smem_b;  // digits, then params (batch_rec_bytes)
     uint32_t* dig = reinterpret_cast<uint32_t*>(rec);
-    float4* prm = reinterpret_cast<float4*>(rec + (size_t)p.batch * gk * 256);
+    float4* prm = reinterpret_cast<float4*>(rec + (size_t)p.batch * batch_dig_stride(gk));
     const uint32_t ring = smem_u32(rec + batch_rec_bytes(p.batch, gk)) + (uint32_t)(warp * BNBUF * Q4M_UNIT);
 
     // tasks of this warp: tile pairs q = cidx + (warp + BNW i) cgrid, all ng groups of K part kp
@@ -121,7 +128,8 @@ __global__ void __launch_bounds__(BT, 1) k_gemv_q4m_batch(const BatchParams p) {
                 v = reinterpret_cast<const float4*>(p.x)[(size_t)b * n4 + i4];
             }
         }
-        octet_to_records(v, lane, lane >> 3, dig + (b * gk + gl) * 64, prm + (b * gk + gl) * 4);
+        octet_to_records(v, lane, lane >> 3, dig + (b * batch_dig_stride(gk) + gl * 256) / 4,
+                         prm + (b * batch_prm_stride(gk) + gl * 64) / 16);
     }
     __syncthreads();
     const uint32_t dig_s = smem_u32(dig), prm_s = smem_u32(prm);
