@@ -64,7 +64,12 @@ extern "C" size_t jinf_b200_gemv_q4m_workspace_bytes(int rows, int cols) {
 static jinf_status gemv_q4m_common(GemvParams& p, const Q4MShape& sh, int xm, void* workspace, int kw,
                                    cudaStream_t stream) {
     if (sh.cols > gemvm_max_cols(sh.fmt) || kw < 0 || kw > kQ4mMaxKw) return JINF_ERR_INVALID;
-    const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms(), sh.fmt);
+    int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms(), sh.fmt);
+    if (kw == 0 && gemvm_use_local(sh.pairs, grid)) {  // one pair per CTA, K split by its warps
+        p.kw = 1;
+        p.local_k = 1;
+        return gemvm_launch(p, xm, EPI_STORE, sh.pairs, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+    }
     if (kw == 0) kw = gemvm_pick_kw(sh.pairs, sh.groups, grid, workspace ? kQ4mMaxKw : 1);
     if (kw > sh.groups || (kw > 1 && !workspace)) return JINF_ERR_INVALID;
     p.kw = kw;

@@ -472,6 +472,11 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         op.gp.kw = gemvm_pick_kw(op.gp.pairs, op.gp.groups, op.grid, kEngineMaxKw);
         op.gp.part = I->gemv_part;
         op.gp.cnt = I->gemv_cnt;
+        if (gemvm_use_local(op.gp.pairs, op.grid)) {
+            op.gp.kw = 1;
+            op.gp.local_k = 1;
+            op.grid = op.gp.pairs;
+        }
     };
     for (int L = 0; L < I->L; ++L) {
         const auto& ly = I->layers[L];

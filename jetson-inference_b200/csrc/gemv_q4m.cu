@@ -51,7 +51,8 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     const int G = p.groups;
     uint8_t* rec = smem_raw;                                                     // input digit records
     float* misc = reinterpret_cast<float*>(smem_raw + xrec_bytes(G));           // 64 floats
-    const uint32_t ring0 = smem_u32(misc + 64);
+    float* part_s = misc + 64;                                                   // [NW][32] (local_k)
+    const uint32_t ring0 = smem_u32(part_s + NW * Q4M_PAIR_ROWS);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * UB);
     const int kw = p.kw;
@@ -66,8 +67,21 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
         cg = kp * G / kw;
         cge = (kp + 1) * G / kw;
     }
+    // CTA-local K split (p.local_k): CTA c takes tile pairs c, c + grid, ...; warp w takes
+    // groups [w G / NW, (w + 1) G / NW) of each; the warps' partial rows meet in shared memory
+    const bool local = p.local_k != 0;
+    const int lg0 = warp * G / NW, lg1 = (warp + 1) * G / NW;
+    int lpair = blockIdx.x, lcg = lg0;  // copy cursor (local_k)
     auto issue = [&](int slot) {
-        if (ctask < T) {
+        if (local) {
+            if (lg0 < lg1 && lpair < p.pairs) {
+                copy_unit_fmt<FMT>(ring + slot * UB, p.w + ((size_t)lpair * G + lcg) * UB, lane);
+                if (++lcg == lg1) {
+                    lcg = lg0;
+                    lpair += gridDim.x;
+                }
+            }
+        } else if (ctask < T) {
             const int pair = ctask / kw;
             copy_unit_fmt<FMT>(ring + slot * UB, p.w + ((size_t)pair * G + cg) * UB, lane);
             if (++cg == cge) {
@@ -116,7 +130,35 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     float lmax = -INFINITY;
     int lidx = 0;
     int slot = 0;
-    for (int task = gw; task < T; task += W) {
+    if (local) {
+        for (int pair = blockIdx.x; pair < p.pairs; pair += gridDim.x) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int g = lg0; g < lg1; ++g) {
+                issue(slot == 0 ? GEMV_M_NBUF - 1 : slot - 1);
+                asm volatile("cp.async.wait_group %0;" ::"n"(GEMV_M_NBUF - 1) : "memory");
+                unit_mma_fmt<FMT>(ring + slot * UB, xr, g, lane, acc);
+                slot = slot + 1 == GEMV_M_NBUF ? 0 : slot + 1;
+            }
+            unit_reduce(acc);
+            if (c == 0) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) part_s[warp * Q4M_PAIR_ROWS + unit_row_of(i, lane)] = acc[i];
+            }
+            __syncthreads();
+            if (warp == 0) {  // rows 2q, 2q+1: the warps' pieces added in warp order
+                const int r0 = 2 * (lane & 15);
+                float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+                for (int w = 0; w < NW; ++w) {
+                    v0 += part_s[w * Q4M_PAIR_ROWS + r0];
+                    v1 += part_s[w * Q4M_PAIR_ROWS + r0 + 1];
+                }
+                if (lane < 16) epilogue_pair(ea, pair * Q4M_PAIR_ROWS + r0, v0 * fac, v1 * fac, lmax, lidx);
+            }
+            __syncthreads();  // part_s is rewritten by the next pair
+        }
+    }
+    for (int task = local ? T : gw; task < T; task += W) {
         const int pair = task / kw, kp = task % kw;
         const int g0 = kp * G / kw, g1 = (kp + 1) * G / kw;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -283,8 +325,10 @@ __global__ void k_repack_q4mk(const uint8_t* __restrict__ aos, uint8_t* __restri
 
 size_t gemvm_smem_bytes(int cols, int fmt) {
     const int G = (cols + Q4M_KG - 1) / Q4M_KG;
-    return xrec_bytes(G) + sizeof(float) * 64 + (size_t)NW * GEMV_M_NBUF * q4m_unit_bytes(fmt);
+    return xrec_bytes(G) + sizeof(float) * (64 + NW * Q4M_PAIR_ROWS) + (size_t)NW * GEMV_M_NBUF * q4m_unit_bytes(fmt);
 }
+
+bool gemvm_use_local(int pairs, int grid) { return pairs <= grid; }
 
 int gemvm_max_cols(int fmt) {
     // largest multiple of 128 whose staging fits next to the ring in the 227 KB per CTA
