@@ -65,10 +65,12 @@ static jinf_status gemv_q4m_common(GemvParams& p, const Q4MShape& sh, int xm, vo
                                    cudaStream_t stream) {
     if (sh.cols > gemvm_max_cols(sh.fmt) || kw < 0 || kw > kQ4mMaxKw) return JINF_ERR_INVALID;
     int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms(), sh.fmt);
-    if (kw == 0 && gemvm_use_local(sh.pairs, grid)) {  // one pair per CTA, K split by its warps
+    if (kw == 0 && gemvm_use_local(sh.pairs, grid)) {  // pairs spread evenly over CTAs, K split by their warps
         p.kw = 1;
         p.local_k = 1;
-        return gemvm_launch(p, xm, EPI_STORE, sh.pairs, stream, false) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
+        return gemvm_launch(p, xm, EPI_STORE, gemvm_local_grid(sh.pairs, grid), stream, false) == cudaSuccess
+                   ? JINF_OK
+                   : JINF_ERR_CUDA;
     }
     if (kw == 0) kw = gemvm_pick_kw(sh.pairs, sh.groups, grid, workspace ? kQ4mMaxKw : 1);
     if (kw > sh.groups || (kw > 1 && !workspace)) return JINF_ERR_INVALID;

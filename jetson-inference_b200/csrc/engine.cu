@@ -475,7 +475,7 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         if (gemvm_use_local(op.gp.pairs, op.grid)) {
             op.gp.kw = 1;
             op.gp.local_k = 1;
-            op.grid = op.gp.pairs;
+            op.grid = gemvm_local_grid(op.gp.pairs, op.grid);
         }
     };
     for (int L = 0; L < I->L; ++L) {

@@ -73,9 +73,11 @@ int gemvm_max_cols(int fmt = Q4M_Q4_0);
 int gemvm_grid(int cols, int xm, int epi, int num_sms, int fmt = Q4M_Q4_0);
 // K parts per tile pair for a grid of `grid` CTAs (1 <= kw <= min(groups, max_kw)).
 int gemvm_pick_kw(int pairs, int groups, int grid, int max_kw);
-// The CTA-local K split serves matrices of at most `grid` tile pairs (one pair per CTA):
-// no global partial sums, no arrival counters.
+// The CTA-local K split serves matrices of at most 4 `grid` tile pairs: no global partial
+// sums, no arrival counters. It runs on gemvm_local_grid CTAs, each taking the same number of
+// pairs.
 bool gemvm_use_local(int pairs, int grid);
+int gemvm_local_grid(int pairs, int grid);
 cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
 // AoS Q4_0 or Q4_K (sh.fmt) [rows][cols] (device) -> Q4M (device, sh.bytes).
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s);

@@ -328,7 +328,12 @@ size_t gemvm_smem_bytes(int cols, int fmt) {
     return xrec_bytes(G) + sizeof(float) * (64 + NW * Q4M_PAIR_ROWS) + (size_t)NW * GEMV_M_NBUF * q4m_unit_bytes(fmt);
 }
 
-bool gemvm_use_local(int pairs, int grid) { return pairs <= grid; }
+bool gemvm_use_local(int pairs, int grid) { return pairs <= 4 * grid; }
+
+int gemvm_local_grid(int pairs, int grid) {
+    const int rounds = (pairs + grid - 1) / grid;  // pairs per CTA, the same for every CTA
+    return (pairs + rounds - 1) / rounds;
+}
 
 int gemvm_max_cols(int fmt) {
     // largest multiple of 128 whose staging fits next to the ring in the 227 KB per CTA
