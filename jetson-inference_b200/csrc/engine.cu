@@ -1758,8 +1758,13 @@ extern "C" jinf_status jinf_engine_count_activations(jinf_engine* e, const int32
     }
     cudaSetDevice(I->device);
     const size_t n = (size_t)I->L * I->ffl;
-    JINF_CUDA_CHECK(cudaMalloc(&I->count_dev, sizeof(int32_t) * n));
-    JINF_CUDA_CHECK(cudaMemset(I->count_dev, 0, sizeof(int32_t) * n));
+    int32_t* dev = nullptr;
+    JINF_CUDA_CHECK(cudaMalloc(&dev, sizeof(int32_t) * n));
+    if (cudaMemset(dev, 0, sizeof(int32_t) * n) != cudaSuccess) {
+        cudaFree(dev);
+        return JINF_ERR_CUDA;
+    }
+    I->count_dev = dev;  // counting on for this forward only
     I->count_thr = threshold;
     float* logits = nullptr;
     const jinf_status s = jinf_engine_forward(e, tokens, n_tokens, &logits);
