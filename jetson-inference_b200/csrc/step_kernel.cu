@@ -20,14 +20,19 @@
 // Per layer the phases are the reference's decode order (src/engine.cpp:418-511):
 //   QKV GEMV     x = RMSNorm(h) * attn_norm (layer 0: the embedding row); epilogue RoPE,
 //                q -> fp32, k/v -> fp16 KV cache at pos
-//   attention    one CTA per kv head and up to 512 positions, warps of 32 positions,
-//                merged in shared memory (and across CTAs for long contexts)
+//   attention    each kv head's positions split over several CTAs (lanes on head dims,
+//                cache rows read from L2 into registers), the splits merged by the CTAs
+//                that own the output blocks, which write the o phase's input records
 //   o GEMV       h += W_o attn            (residual fused into the epilogue)
-//   gate|up      x = RMSNorm(h) * ffn_norm; epilogue silu(gate) * up
+//   gate|up      x = RMSNorm(h) * ffn_norm; epilogue silu(gate) * up -> down's input records
 //   down GEMV    h += W_down act
 // then the LM head (x = RMSNorm(h) * output_norm; logits + argmax). The last CTA to leave
 // turns the argmax into the next input token, advances the position and clears the
 // counters for the next launch.
+// Tensor parallel (k_step<.., TP = true>, one rank per GPU): o and down write this rank's
+// partial rows into every rank's exchange area over NVLink as flagged 8-byte words, and
+// the next RMSNorm input adds all ranks' rows in rank order (stage_x_tp); the last CTA
+// exchanges the argmax keys.
 #include "common.cuh"
 #include "q4m_device.cuh"
 #include "step.h"
