@@ -736,27 +736,42 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             const float* base = P.attn_part + (size_t)a.kvh * ATTN_MAX_SPLIT * stride;
             float* ml = reinterpret_cast<float*>(xbase);  // [S][2] (m, l) of the block's query head
             float* av = ml + 2 * ATTN_MAX_SPLIT;           // [S][32] accumulators of the block
+            float* ew = av + 32 * ATTN_MAX_SPLIT;          // [S] split weights e^(m_s - M)
             unsigned mine = 0;
             for (int b = a.sp; b < nblk; b += a.S, ++mine) {
                 const int g = b * 32 / hd, dd0 = b * 32 % hd;
-                for (int t = tid; t < a.S * 32; t += STEP_THREADS)
-                    av[t] = __ldcg(base + (t >> 5) * stride + g * (hd + 2) + dd0 + (t & 31));
-                for (int t = tid; t < a.S; t += STEP_THREADS) {
-                    ml[2 * t] = __ldcg(base + t * stride + g * (hd + 2) + hd);
-                    ml[2 * t + 1] = __ldcg(base + t * stride + g * (hd + 2) + hd + 1);
+                {  // every partial load of the thread before any store (S <= 64: at most 4)
+                    float t4[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int t = tid + k * STEP_THREADS;
+                        t4[k] = t < a.S * 32 ? __ldcg(base + (t >> 5) * stride + g * (hd + 2) + dd0 + (t & 31)) : 0.f;
+                    }
+                    const float m0 = tid < a.S ? __ldcg(base + tid * stride + g * (hd + 2) + hd) : 0.f;
+                    const float l0 = tid < a.S ? __ldcg(base + tid * stride + g * (hd + 2) + hd + 1) : 0.f;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (tid + k * STEP_THREADS < a.S * 32) av[tid + k * STEP_THREADS] = t4[k];
+                    if (tid < a.S) {
+                        ml[2 * tid] = m0;
+                        ml[2 * tid + 1] = l0;
+                    }
                 }
                 __syncthreads();
                 if (warp == 0) {
-                    float M = -INFINITY;
-                    for (int s2 = 0; s2 < a.S; ++s2) M = fmaxf(M, ml[2 * s2]);
-                    float L = 0.f, v = 0.f;
-                    for (int s2 = 0; s2 < a.S; ++s2) {
-                        const float m = ml[2 * s2];
-                        if (m == -INFINITY) continue;  // an empty split
-                        const float e = expf(m - M);
-                        L = fmaf(ml[2 * s2 + 1], e, L);
-                        v = fmaf(e, av[s2 * 32 + lane], v);
-                    }
+                    // lanes own splits lane, lane + 32: the max, the weights and their sum in parallel
+                    const float ma = lane < a.S ? ml[2 * lane] : -INFINITY;
+                    const float mb = lane + 32 < a.S ? ml[2 * (lane + 32)] : -INFINITY;
+                    const float M = warp_max(fmaxf(ma, mb));
+                    const float ea = ma == -INFINITY ? 0.f : expf(ma - M);  // 0: an empty split
+                    const float eb = mb == -INFINITY ? 0.f : expf(mb - M);
+                    const float L = warp_sum((lane < a.S ? ml[2 * lane + 1] * ea : 0.f) +
+                                             (lane + 32 < a.S ? ml[2 * (lane + 32) + 1] * eb : 0.f));
+                    if (lane < a.S) ew[lane] = ea;
+                    if (lane + 32 < a.S) ew[lane + 32] = eb;
+                    __syncwarp();
+                    float v = 0.f;
+                    for (int s2 = 0; s2 < a.S; ++s2) v = fmaf(ew[s2], av[s2 * 32 + lane], v);
                     v /= L;
                     const int blk = a.kvh * nblk + b;  // block of the o projection's input
                     if (d.rec_out) {
@@ -1016,7 +1031,9 @@ unsigned int step_xstage_bytes(int max_cols, int group, int head_dim) {
     // attention: scores [group][NW * ATTN_PW], (m, l, correction) [ATTN_MAX_GROUP][4], p.v sums
     // [NW][group][head_dim]
     const size_t attn = sizeof(float) * ((size_t)group * NW * ATTN_PW + 4 * ATTN_MAX_GROUP + (size_t)NW * group * head_dim);
-    const size_t b = gemv > attn ? gemv : attn;
+    const size_t merge = sizeof(float) * (size_t)(2 + 32 + 1) * ATTN_MAX_SPLIT;  // split merge scratch
+    size_t b = gemv > attn ? gemv : attn;
+    b = b > merge ? b : merge;
     return (unsigned int)((b + 15) & ~(size_t)15);
 }
 
