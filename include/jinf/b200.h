@@ -24,10 +24,11 @@ extern "C" {
 // bytes per (pair, group), every nibble and scale of the AoS blocks moved, none re-quantised.
 uint64_t jinf_b200_q4m_bytes(int rows, int cols);
 
-// The same for either weight type: qtype JINF_TYPE_Q4_0 or JINF_TYPE_Q4_K (2432 bytes per
-// (pair, group); cols a multiple of 256). 0 for other types or shapes. No counterpart in
-// the reference, whose Q4_K matvec reads the AoS super-blocks (reference
-// cuda/matmul_kernels.cu:47-100).
+// The same for any weight type the engine streams: qtype JINF_TYPE_Q4_0, JINF_TYPE_Q4_K
+// (2432 bytes per (pair, group); cols a multiple of 256), JINF_TYPE_Q6_K (3392 bytes; cols a
+// multiple of 256) or JINF_TYPE_Q8_0 (4352 bytes; cols a multiple of 32). 0 for other types
+// or shapes. No counterpart in the reference, whose matvecs read the AoS blocks (reference
+// cuda/matmul_kernels.cu:47-185).
 uint64_t jinf_b200_q4m_bytes_qt(int rows, int cols, int qtype);
 jinf_status jinf_b200_q4m_pack_qt(const void* aos, int qtype, void* q4m, int rows, int cols, cudaStream_t stream);
 jinf_status jinf_b200_gemv_q4m_qt(const void* q4m, int qtype, const void* x, int x_type, float* y, int rows,

@@ -124,9 +124,11 @@ static inline jinf_b200_options jinf_b200_options_default(void) {
 typedef struct jinf_synth_config {
     jinf_model_hparams hp;  // arch "llama"; n_ctx_train is informative only
     uint64_t seed;
-    int      weight_type;   // JINF_TYPE_Q4_0 or JINF_TYPE_Q4_K for the 7 projections + output
+    int      weight_type;   // JINF_TYPE_Q4_0, Q4_K, Q6_K or Q8_0 for the 7 projections + output
     float    weight_std;    // 0.02
     float    embed_std;     // 0.02 (token_embd is f32)
+    int      mix_type;      // 0, or a second type for attn_v and ffn_down of the even layers and
+                            // for output (the pattern of a Q4_K_M file: mix_type Q6_K)
 } jinf_synth_config;
 
 typedef struct jinf_synth_model jinf_synth_model;

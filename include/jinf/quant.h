@@ -159,6 +159,11 @@ uint16_t jinf_fp32_to_fp16(float f);  // round-to-nearest-even
 void jinf_quantize_q4_0(const float* x, jinf_block_q4_0* out, int64_t n);
 // Quantize n (multiple of 256) floats to Q4_K blocks in the reference scale packing.
 void jinf_quantize_q4_K(const float* x, jinf_block_q4_K* out, int64_t n);
+// Quantize n (multiple of 32) floats to Q8_0 blocks: d = max|x| / 127, q = round(x / d).
+void jinf_quantize_q8_0(const float* x, jinf_block_q8_0* out, int64_t n);
+// Quantize n (multiple of 256) floats to Q6_K blocks in the reference GPU kernel's bit layout
+// (ql[e/2] nibble, qh[e/4] bits 2 (e%4), int8 scale per 16, fp16 d last).
+void jinf_quantize_q6_K(const float* x, jinf_block_q6_K* out, int64_t n);
 
 #ifdef __cplusplus
 }

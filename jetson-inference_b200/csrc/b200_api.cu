@@ -35,9 +35,7 @@ extern "C" jinf_status jinf_b200_q4m_pack(const void* aos, void* q4m, int rows, 
     return q4m_repack(aos, q4m, sh, stream) == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
 }
 
-static int q4m_fmt_of(int qtype) {
-    return qtype == JINF_TYPE_Q4_0 ? Q4M_Q4_0 : qtype == JINF_TYPE_Q4_K ? Q4M_Q4_K : -1;
-}
+static int q4m_fmt_of(int qtype) { return q4m_fmt_of_qtype(qtype); }
 
 extern "C" uint64_t jinf_b200_q4m_bytes_qt(int rows, int cols, int qtype) {
     Q4MShape sh;

@@ -47,6 +47,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <array>
 #include <memory>
 #include <string>
 #include <vector>
@@ -280,7 +281,8 @@ struct jinf_engine_impl {
     int device = 0;
     int tp_rank = 0, tp_size = 1;
     int num_sms = 148;
-    int wfmt = Q4M_Q4_0;       // Q4MFormat of every weight matrix (the model's quantisation)
+    int wfmt = Q4M_Q4_0;       // Q4MFormat of the weight matrices when they share one (uniform)
+    bool uniform = true;       // every projection and the output head of one type, Q4_0 or Q4_K
     int wtype = JINF_TYPE_Q4_0;
     cudaStream_t stream = nullptr;
     bool use_graph = true;
@@ -295,7 +297,8 @@ struct jinf_engine_impl {
     uint64_t arena_bytes = 0;
     uint64_t weight_bytes_token = 0;  // algorithmic quantized bytes per token (this rank)
     struct Layer {
-        uint8_t* qkv; Q4MShape qkv_sh;
+        uint8_t* qkv; Q4MShape qkv_sh;  // [q | k | v] rows, or [q | k] when v has its own type
+        uint8_t* v = nullptr; Q4MShape v_sh{};  // v rows of another weight type (Q4_K_M files)
         uint8_t* o; Q4MShape o_sh;
         uint8_t* gu; Q4MShape gu_sh;
         uint8_t* down; Q4MShape down_sh;
@@ -464,7 +467,7 @@ constexpr int kEngineMaxKw = 16;  // K parts per tile of the stand-alone GEMVs
 void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
     ops.clear();
     auto gemv_bytes = [](const Q4MShape& sh, int in_elems, int out_elems) -> uint64_t {
-        return (uint64_t)sh.rows * (sh.cols / 32) * 18 + 4ull * in_elems + 4ull * out_elems;
+        return (uint64_t)sh.rows * aos_row_bytes(sh.fmt, sh.cols) + 4ull * in_elems + 4ull * out_elems;
     };
     // grid and K split of a stand-alone GEMV
     auto finish = [&](Op& op) {
@@ -502,11 +505,25 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
         qkv.gp.max_ctx = I->max_ctx;
         qkv.gp.rope_base = I->rope_base;
         qkv.gp.st = I->st;
-        qkv.gp.pf_ptr = ly.o;
-        qkv.gp.pf_bytes = ly.o_sh.bytes;
+        qkv.gp.pf_ptr = ly.v ? ly.v : ly.o;
+        qkv.gp.pf_bytes = ly.v ? ly.v_sh.bytes : ly.o_sh.bytes;
         finish(qkv);
         qkv.bytes = gemv_bytes(ly.qkv_sh, I->d, ly.qkv_sh.rows);
         ops.push_back(qkv);
+        if (ly.v) {
+            // v of another weight type: a GEMV of its own over the same input, every row a v
+            // row (nq = nk = 0); both GEMVs store the same h
+            Op v = qkv;
+            gemvm_params_for(v.gp, ly.v, ly.v_sh);
+            v.gp.local_k = 0;
+            v.gp.nq = 0;
+            v.gp.nk = 0;
+            v.gp.pf_ptr = ly.o;
+            v.gp.pf_bytes = ly.o_sh.bytes;
+            finish(v);
+            v.bytes = gemv_bytes(ly.v_sh, I->d, ly.v_sh.rows);
+            ops.push_back(v);
+        }
 
         Op at{OP_ATTN};
         at.layer = L;
@@ -966,12 +983,11 @@ struct Loader {
             JINF_LOG("tensor %s missing", name);
             return JINF_ERR_PARSE;
         }
-        if (m.type != I->wtype) {
-            JINF_LOG("tensor %s: type %s, but the model's projections are %s (one type for all of them)", name,
-                     jinf_qtype_name((jinf_qtype)m.type), jinf_qtype_name((jinf_qtype)I->wtype));
+        if (q4m_fmt_of_qtype(m.type) < 0) {
+            JINF_LOG("tensor %s: type %s has no Q4M form", name, jinf_qtype_name((jinf_qtype)m.type));
             return JINF_ERR_INVALID;
         }
-        const int bs = I->wtype == JINF_TYPE_Q4_K ? 256 : 32, bb = I->wtype == JINF_TYPE_Q4_K ? 144 : 18;
+        const int bs = jinf_qtype_block_size((jinf_qtype)m.type), bb = (int)jinf_qtype_type_size((jinf_qtype)m.type);
         if (r0 < 0 || c0 < 0 || r0 + nr > m.rows() || c0 + nc > m.cols() || c0 % bs || nc % bs) {
             JINF_LOG("tensor %s: slice [%lld+%lld, %lld+%lld) out of range", name, (long long)r0, (long long)nr,
                      (long long)c0, (long long)nc);
@@ -1137,16 +1153,53 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         JINF_LOG("head_dim %d not supported (64 or 128)", I->hd);
         return fail(JINF_ERR_INVALID);
     }
+    // the projections' quantisation, per matrix: Q4_0, Q4_K, Q6_K or Q8_0 (Q4_K_M files
+    // keep attn_v, ffn_down of some layers and the output head in Q6_K); q and k, and gate
+    // and up, must share a type (they are fused). The persistent step serves models whose
+    // matrices are all Q4_0 or all Q4_K; others run one kernel per operation.
+    std::vector<std::array<int, 5>> lfmt((size_t)I->L);  // per layer: q|k, v, o, gate|up, down
+    int lm_fmt = -1;
     {
-        // the projections' quantisation: Q4_0 or Q4_K, the same for every matrix
         TensorMeta m;
         if (src.meta("blk.0.attn_q.weight", &m)) I->wtype = m.type;
-        if (I->wtype != JINF_TYPE_Q4_0 && I->wtype != JINF_TYPE_Q4_K) {
-            JINF_LOG("weights of type %s are not supported by the B200 engine (Q4_0 or Q4_K)",
-                     jinf_qtype_name((jinf_qtype)I->wtype));
+        auto fmt_of = [&](const char* nm, int* fmt) -> bool {
+            TensorMeta t;
+            if (!src.meta(nm, &t)) {
+                JINF_LOG("tensor %s missing", nm);
+                return false;
+            }
+            *fmt = q4m_fmt_of_qtype(t.type);
+            if (*fmt < 0) {
+                JINF_LOG("tensor %s: weights of type %s are not supported by the B200 engine (Q4_0, Q4_K, Q6_K or "
+                         "Q8_0)", nm, jinf_qtype_name((jinf_qtype)t.type));
+                return false;
+            }
+            return true;
+        };
+        char nm[128];
+        for (int L = 0; L < I->L; ++L) {
+            int f[7];
+            const char* parts[7] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"};
+            for (int i = 0; i < 7; ++i) {
+                snprintf(nm, sizeof nm, "blk.%d.%s.weight", L, parts[i]);
+                if (!fmt_of(nm, &f[i])) return fail(JINF_ERR_INVALID);
+            }
+            if (f[0] != f[1] || f[4] != f[5]) {
+                JINF_LOG("layer %d: attn_q and attn_k, and ffn_gate and ffn_up, must share a weight type", L);
+                return fail(JINF_ERR_INVALID);
+            }
+            lfmt[L] = {f[0], f[2], f[3], f[4], f[6]};
+        }
+        if (!fmt_of("output.weight", &lm_fmt)) return fail(JINF_ERR_INVALID);
+        I->wfmt = lm_fmt;
+        for (const auto& lf : lfmt)
+            for (const int f : lf) I->uniform = I->uniform && f == lm_fmt;
+        I->uniform = I->uniform && (lm_fmt == Q4M_Q4_0 || lm_fmt == Q4M_Q4_K);
+        if (I->uniform) I->wtype = lm_fmt == Q4M_Q4_K ? JINF_TYPE_Q4_K : JINF_TYPE_Q4_0;
+        if (!I->uniform && opt.sparse_mode) {
+            JINF_LOG("sparse FFN modes need every projection in one type, Q4_0 or Q4_K");
             return fail(JINF_ERR_INVALID);
         }
-        I->wfmt = I->wtype == JINF_TYPE_Q4_K ? Q4M_Q4_K : Q4M_Q4_0;
     }
     if (I->H / I->Hkv > 8) {
         JINF_LOG("more than 8 query heads per kv head are not supported");
@@ -1221,24 +1274,29 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     const int qkv_rows = (I->Hl + 2 * I->Hkvl) * hd;
     I->layers.resize(I->L);
     uint64_t off = 0;
-    auto place = [&](Q4MShape& sh, int rows, int cols, uint8_t*& ptr) -> bool {
-        if (!q4m_shape(rows, cols, &sh, I->wfmt) || cols > gemvm_max_cols(I->wfmt)) return false;
+    auto place = [&](Q4MShape& sh, int rows, int cols, uint8_t*& ptr, int fmt) -> bool {
+        if (!q4m_shape(rows, cols, &sh, fmt) || cols > gemvm_max_cols(fmt)) {
+            JINF_LOG("a %d x %d matrix is not supported by the Q4M layout of its type (columns must be whole "
+                     "%d-element blocks, at most %d)", rows, cols, q4m_col_align(fmt), gemvm_max_cols(fmt));
+            return false;
+        }
         ptr = (uint8_t*)(uintptr_t)off;  // offset for now
         off += (sh.bytes + 255) & ~255ull;
-        I->weight_bytes_token += (uint64_t)rows * (cols / 32) * 18;
+        I->weight_bytes_token += (uint64_t)rows * aos_row_bytes(fmt, cols);
         return true;
     };
     for (int L = 0; L < I->L; ++L) {
         auto& ly = I->layers[L];
+        const auto& lf = lfmt[L];
         const int ffc = I->sparse_persistent ? 32 * (int)I->sparse_blocks[L].size() : I->ffl;  // FFN width stored
-        if (!place(ly.qkv_sh, qkv_rows, d, ly.qkv) || !place(ly.o_sh, d, I->Hl * hd, ly.o) ||
-            !place(ly.gu_sh, 2 * ffc, d, ly.gu) || !place(ly.down_sh, d, ffc, ly.down)) {
-            JINF_LOG("matrix shapes not supported by the Q4M layout (columns must be whole %d-element blocks)",
-                     I->wfmt == Q4M_Q4_K ? 256 : 32);
+        const int qk_rows = (I->Hl + I->Hkvl) * hd;
+        const bool split_v = lf[1] != lf[0];
+        if (!place(ly.qkv_sh, split_v ? qk_rows : qkv_rows, d, ly.qkv, lf[0]) ||
+            (split_v && !place(ly.v_sh, I->Hkvl * hd, d, ly.v, lf[1])) || !place(ly.o_sh, d, I->Hl * hd, ly.o, lf[2]) ||
+            !place(ly.gu_sh, 2 * ffc, d, ly.gu, lf[3]) || !place(ly.down_sh, d, ffc, ly.down, lf[4]))
             return fail(JINF_ERR_INVALID);
-        }
     }
-    if (!place(I->lm_sh, I->Vl, d, I->lm)) return fail(JINF_ERR_INVALID);
+    if (!place(I->lm_sh, I->Vl, d, I->lm, lm_fmt)) return fail(JINF_ERR_INVALID);
     I->arena_bytes = off;
     if (cudaMalloc(&I->arena, I->arena_bytes) != cudaSuccess) {
         JINF_LOG("cannot allocate %.1f MB of weights", I->arena_bytes / 1048576.0);
@@ -1246,6 +1304,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     }
     for (auto& ly : I->layers) {
         ly.qkv = I->arena + (uintptr_t)ly.qkv;
+        if (ly.v) ly.v = I->arena + (uintptr_t)ly.v;
         ly.o = I->arena + (uintptr_t)ly.o;
         ly.gu = I->arena + (uintptr_t)ly.gu;
         ly.down = I->arena + (uintptr_t)ly.down;
@@ -1335,11 +1394,12 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         Loader ld{I, &src};
         size_t max_stage = 0;
         for (const auto& ly : I->layers)
-            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh})
-                max_stage = std::max(max_stage, (size_t)sh->rows * (sh->cols / 32) * 18);
-        max_stage = std::max(max_stage, (size_t)I->lm_sh.rows * (I->lm_sh.cols / 32) * 18);
+            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.v_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh})
+                if (sh->rows > 0) max_stage = std::max(max_stage, (size_t)sh->rows * aos_row_bytes(sh->fmt, sh->cols));
+        max_stage = std::max(max_stage, (size_t)I->lm_sh.rows * aos_row_bytes(I->lm_sh.fmt, I->lm_sh.cols));
         if (ld.ensure_dstage(max_stage) != JINF_OK) return fail(JINF_ERR_OOM);
-        // AoS row bytes of a d-column matrix (Q4_0 and Q4_K both take 9/16 byte per weight)
+        // AoS row bytes of a d-column Q4_0 / Q4_K matrix (both take 9/16 byte per weight): the
+        // sparse FFN bundles, built from uniform Q4 models only
         const int64_t rb_d = (int64_t)(d / 32) * 18;
         char nm[128];
         jinf_status s = JINF_OK;
@@ -1355,31 +1415,38 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             if (s != JINF_OK) break;
             // QKV: this rank's q heads, then its k heads, then its v heads
             const int64_t nq = (int64_t)I->Hl * hd, nk = (int64_t)I->Hkvl * hd;
+            const int64_t rb_qk = (int64_t)aos_row_bytes(ly.qkv_sh.fmt, d);
             snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", L);
-            s = ld.stage_shard(nm, nq, d, rb_d, 0, 1);
+            s = ld.stage_shard(nm, nq, d, rb_qk, 0, 1);
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", L);
-                s = ld.stage_shard(nm, nk, d, rb_d, nq, 1);
+                s = ld.stage_shard(nm, nk, d, rb_qk, nq, 1);
             }
-            if (s == JINF_OK) {
+            if (s == JINF_OK && !ly.v) {
                 snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", L);
-                s = ld.stage_shard(nm, nk, d, rb_d, nq + nk, 1);
+                s = ld.stage_shard(nm, nk, d, rb_qk, nq + nk, 1);
             }
             if (s == JINF_OK) s = ld.pack(ly.qkv, ly.qkv_sh);
+            if (s == JINF_OK && ly.v) {  // v of its own type: a matrix of its own
+                snprintf(nm, sizeof nm, "blk.%d.attn_v.weight", L);
+                s = ld.stage_shard(nm, nk, d, (int64_t)aos_row_bytes(ly.v_sh.fmt, d), 0, 1);
+                if (s == JINF_OK) s = ld.pack(ly.v, ly.v_sh);
+            }
             // o: every output row, this rank's input columns (row split)
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.attn_output.weight", L);
-                s = ld.stage_shard(nm, d, nq, (nq / 32) * 18, 0, 1);
+                s = ld.stage_shard(nm, d, nq, (int64_t)aos_row_bytes(ly.o_sh.fmt, nq), 0, 1);
             }
             if (s == JINF_OK) s = ld.pack(ly.o, ly.o_sh);
             // gate|up interleaved by neuron: gate_n -> row 2n, up_n -> row 2n+1
+            const int64_t rb_gu = (int64_t)aos_row_bytes(ly.gu_sh.fmt, d);
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.ffn_gate.weight", L);
-                s = ld.stage_shard(nm, I->ffl, d, rb_d, 0, 2);
+                s = ld.stage_shard(nm, I->ffl, d, rb_gu, 0, 2);
             }
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.ffn_up.weight", L);
-                s = ld.stage_shard(nm, I->ffl, d, rb_d, 1, 2);
+                s = ld.stage_shard(nm, I->ffl, d, rb_gu, 1, 2);
             }
             uint8_t* bl = I->bundles ? I->bundles + (size_t)L * I->ffl * I->bundle_size : nullptr;
             if (s == JINF_OK && bl && sparse_bundle_gate_up(ld.dstage, I->ffl, (int)rb_d, bl, I->bundle_size,
@@ -1400,7 +1467,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             // down: every output row, this rank's neuron columns (row split)
             if (s == JINF_OK) {
                 snprintf(nm, sizeof nm, "blk.%d.ffn_down.weight", L);
-                s = ld.stage_shard(nm, d, I->ffl, (int64_t)(I->ffl / 32) * 18, 0, 1);
+                s = ld.stage_shard(nm, d, I->ffl, (int64_t)aos_row_bytes(ly.down_sh.fmt, I->ffl), 0, 1);
             }
             if (s == JINF_OK && bl && sparse_bundle_down(ld.dstage, d, I->ffl, I->wtype, bl, I->bundle_size,
                                                          (int)(2 * rb_d), I->stream) != cudaSuccess)
@@ -1411,7 +1478,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         }
         I->out_norm = I->norms + (size_t)(2 * I->L) * d;
         if (s == JINF_OK) s = ld.read_f32("output_norm.weight", I->out_norm, d);
-        if (s == JINF_OK) s = ld.stage_shard("output.weight", I->Vl, d, rb_d, 0, 1);
+        if (s == JINF_OK)
+            s = ld.stage_shard("output.weight", I->Vl, d, (int64_t)aos_row_bytes(I->lm_sh.fmt, d), 0, 1);
         if (s == JINF_OK) s = ld.pack(I->lm, I->lm_sh);
         if (s == JINF_OK) s = ld.read_f32("token_embd.weight", I->embed, (int64_t)I->V * d);
         if (s != JINF_OK) return fail(s);
@@ -1439,13 +1507,16 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     {
         size_t pairs = I->lm_sh.pairs;
         for (const auto& ly : I->layers)
-            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) pairs = std::max(pairs, (size_t)sh->pairs);
+            for (const Q4MShape* sh : {&ly.qkv_sh, &ly.v_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh})
+                pairs = std::max(pairs, (size_t)sh->pairs);
         if (cudaMalloc(&I->gemv_part, sizeof(float) * pairs * kEngineMaxKw * Q4M_PAIR_ROWS) != cudaSuccess ||
             cudaMalloc(&I->gemv_cnt, sizeof(unsigned int) * pairs) != cudaSuccess)
             return fail(JINF_ERR_OOM);
         cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * pairs);
     }
-    if (opt.persistent && (!I->sparse_mode || I->sparse_persistent)) {
+    if (opt.persistent && !I->uniform)
+        JINF_LOG("weight types differ between matrices (or are not Q4_0 / Q4_K): one kernel per operation");
+    if (opt.persistent && I->uniform && (!I->sparse_mode || I->sparse_persistent)) {
         // tensor parallel: the exchange areas first (every rank decides the same way)
         bool ok = tp == 1 || setup_exchange(I);
         if (!ok) {

@@ -17,6 +17,14 @@ namespace jinf {
 #endif
 constexpr int GEMV_M_THREADS = 512;
 constexpr int GEMV_M_NBUF = JINF_GEMV_M_NBUF;
+// Ring slots per warp for a weight format: the larger Q6_K and Q8_0 units take 2, so that
+// the ring still leaves room for the input records of 28672 columns (a 70B down projection).
+#ifndef JINF_GEMV_M_NBUF_WIDE
+#define JINF_GEMV_M_NBUF_WIDE 2
+#endif
+__host__ __device__ constexpr inline int gemvm_nbuf(int fmt) {
+    return fmt == Q4M_Q6_K || fmt == Q4M_Q8_0 ? JINF_GEMV_M_NBUF_WIDE : GEMV_M_NBUF;
+}
 
 // X_RECORDS (persistent step only): the input is already staged as digit records in global
 // memory by the phase that produced it (q4m_device.cuh, xrec_bytes).
@@ -79,7 +87,12 @@ int gemvm_pick_kw(int pairs, int groups, int grid, int max_kw);
 bool gemvm_use_local(int pairs, int grid);
 int gemvm_local_grid(int pairs, int grid);
 cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
-// AoS Q4_0 or Q4_K (sh.fmt) [rows][cols] (device) -> Q4M (device, sh.bytes).
+// Q4M format of a reference block type (jinf_qtype: Q4_0 = 2, Q8_0 = 8, Q4_K = 12,
+// Q6_K = 14); -1 for types the Q4M GEMV does not stream.
+inline int q4m_fmt_of_qtype(int qtype) {
+    return qtype == 2 ? Q4M_Q4_0 : qtype == 12 ? Q4M_Q4_K : qtype == 14 ? Q4M_Q6_K : qtype == 8 ? Q4M_Q8_0 : -1;
+}
+// AoS Q4_0, Q4_K, Q6_K or Q8_0 (sh.fmt) [rows][cols] (device) -> Q4M (device, sh.bytes).
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s);
 
 }  // namespace jinf

@@ -12,7 +12,7 @@
 //
 // Scheduling. Tasks are (tile pair, K part): a pair's groups are split over `kw` tasks so
 // that every SM gets about the same work. Each warp streams its tasks' units through a
-// private cp.async ring (GEMV_M_NBUF - 1 units of 2304 bytes in flight) that runs ahead
+// private cp.async ring (gemvm_nbuf(fmt) - 1 units in flight) that runs ahead
 // across task boundaries; the first units are requested before the kernel waits on its
 // producer (programmatic dependent launch), because weights never depend on it. With kw > 1
 // each task writes its 32 partial sums to a workspace and the last task of a pair (arrival
@@ -46,7 +46,7 @@ __device__ __forceinline__ void l2_prefetch(const uint8_t* p, uint64_t bytes) {
 
 template <int XM, int EPI, int FMT>
 __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p) {
-    constexpr int UB = FMT == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT;  // unit bytes
+    constexpr int UB = q4m_unit_bytes(FMT);  // unit bytes
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int G = p.groups;
     uint8_t* rec = smem_raw;                                                     // input digit records
@@ -54,7 +54,8 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
     float* part_s = misc + 64;                                                   // [NW][32] (local_k)
     const uint32_t ring0 = smem_u32(part_s + NW * Q4M_PAIR_ROWS);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t ring = ring0 + (uint32_t)(warp * GEMV_M_NBUF * UB);
+    constexpr int NB = gemvm_nbuf(FMT);       // ring slots per warp
+    const uint32_t ring = ring0 + (uint32_t)(warp * NB * UB);
     const int kw = p.kw;
     const int T = p.pairs * kw;  // tasks: (tile pair, K part)
     const int W = gridDim.x * NW;
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
     };
 #pragma unroll
-    for (int i = 0; i < GEMV_M_NBUF - 1; ++i) issue(i);
+    for (int i = 0; i < NB - 1; ++i) issue(i);
 
     if (tid == 0 && p.pf_bytes) {
         const uint64_t share = ((p.pf_bytes + gridDim.x - 1) / gridDim.x + 15) & ~15ull;
@@ -134,10 +135,10 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
         for (int pair = blockIdx.x; pair < p.pairs; pair += gridDim.x) {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
             for (int g = lg0; g < lg1; ++g) {
-                issue(slot == 0 ? GEMV_M_NBUF - 1 : slot - 1);
-                asm volatile("cp.async.wait_group %0;" ::"n"(GEMV_M_NBUF - 1) : "memory");
+                issue(slot == 0 ? NB - 1 : slot - 1);
+                asm volatile("cp.async.wait_group %0;" ::"n"(NB - 1) : "memory");
                 unit_mma_fmt<FMT>(ring + slot * UB, xr, g, lane, acc);
-                slot = slot + 1 == GEMV_M_NBUF ? 0 : slot + 1;
+                slot = slot + 1 == NB ? 0 : slot + 1;
             }
             unit_reduce(acc);
             if (c == 0) {
@@ -163,10 +164,10 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
         const int g0 = kp * G / kw, g1 = (kp + 1) * G / kw;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int g = g0; g < g1; ++g) {
-            issue(slot == 0 ? GEMV_M_NBUF - 1 : slot - 1);
-            asm volatile("cp.async.wait_group %0;" ::"n"(GEMV_M_NBUF - 1) : "memory");
+            issue(slot == 0 ? NB - 1 : slot - 1);
+            asm volatile("cp.async.wait_group %0;" ::"n"(NB - 1) : "memory");
             unit_mma_fmt<FMT>(ring + slot * UB, xr, g, lane, acc);
-            slot = slot + 1 == GEMV_M_NBUF ? 0 : slot + 1;
+            slot = slot + 1 == NB ? 0 : slot + 1;
         }
         unit_reduce(acc);
         // lane q < 16 finishes rows 2q, 2q+1 of the pair's 32
@@ -321,11 +322,126 @@ __global__ void k_repack_q4mk(const uint8_t* __restrict__ aos, uint8_t* __restri
     *reinterpret_cast<uint32_t*>(unit + Q4M_DMIN_K + 4 * lane) = dd;
 }
 
+// One thread per (pair, group, lane) of a Q6_K matrix (AoS super-blocks of 210 bytes,
+// [rows][nsb]): the lane's nibble words and crumb words, its two scale words, and lanes with
+// c = 0 the d record of row group gr (q4m.cuh). Element e of a super-block is
+// low4 | high2 << 4 with low4 from ql[e / 2] (low nibble for even e) and high2 from bits
+// 2 (e % 4) of qh[e / 4] (reference cuda/dequant_kernels.cu:82-110). Rows past `rows` pack
+// as q = 32 with d = 0 (weight 0).
+__global__ void k_repack_q6k(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
+                             int pairs, int nsb) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)pairs * groups * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t pg = gid >> 5;
+    const int p = (int)(pg / groups), G = (int)(pg % groups);
+    const int gr = lane >> 2, c = lane & 3, sbk = G >> 1, half = G & 1;
+    auto block = [&](int r) -> const uint8_t* {  // super-block sbk of pair row r
+        const int row = p * Q4M_PAIR_ROWS + r;
+        return row < rows && sbk < nsb ? aos + ((size_t)row * nsb + sbk) * 210 : nullptr;
+    };
+    // low nibble and flipped crumb of element k of block j (of this group) of a super-block
+    auto low4 = [&](const uint8_t* blk, int j, int k) -> uint32_t {
+        if (!blk) return 0u;
+        const int e = 128 * half + 32 * j + k;
+        const uint8_t byte = blk[e >> 1];
+        return (e & 1) ? (uint32_t)(byte >> 4) : (uint32_t)(byte & 15);
+    };
+    auto crumb = [&](const uint8_t* blk, int j, int k) -> uint32_t {
+        if (!blk) return 0u;
+        const int e = 128 * half + 32 * j + k;
+        return (((uint32_t)blk[128 + (e >> 2)] >> (2 * (e & 3))) & 3u) ^ 2u;
+    };
+    uint8_t* unit = dst + q4m_unit_offset(p, G, groups, Q4M_Q6_K);
+    for (int j = 0; j < 4; ++j) {
+        for (int i = 0; i < 4; ++i) {
+            const int rt = gr + 8 * (i & 1);
+            const uint8_t* a = block(rt);
+            const uint8_t* b = block(16 + rt);
+            uint32_t word = 0;
+            for (int t = 0; t < 4; ++t) {
+                const int k = 16 * (i >> 1) + 4 * c + t;
+                word |= (low4(a, j, k) | (low4(b, j, k) << 4)) << (8 * t);
+            }
+            *reinterpret_cast<uint32_t*>(unit + 512 * j + 16 * lane + 4 * i) = word;
+        }
+        for (int h = 0; h < 2; ++h) {
+            uint32_t word = 0;
+            for (int t = 0; t < 4; ++t) {
+                uint32_t byte = 0;
+                for (int u = 0; u < 2; ++u) {  // words i = 2h + u: rows gr + 8u of tiles A and B
+                    const int k = 16 * h + 4 * c + t;
+                    byte |= (crumb(block(gr + 8 * u), j, k) | (crumb(block(16 + gr + 8 * u), j, k) << 2)) << (4 * u);
+                }
+                word |= byte << (8 * t);
+            }
+            *reinterpret_cast<uint32_t*>(unit + Q4M_CRUMB_6 + 512 * (j >> 1) + 16 * lane + 4 * (2 * (j & 1) + h)) =
+                word;
+        }
+    }
+    for (int t = 0; t < 2; ++t) {
+        uint32_t word = 0;
+        for (int u = 0; u < 2; ++u) {
+            const uint8_t* blk = block(16 * t + gr + 8 * u);
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t sc = blk ? (uint32_t)blk[192 + 8 * half + 2 * c + h] : 0u;
+                word |= sc << (8 * (2 * u + h));
+            }
+        }
+        *reinterpret_cast<uint32_t*>(unit + Q4M_SC_6 + 8 * lane + 4 * t) = word;
+    }
+    if (c == 0) {
+        uint16_t d4[4];
+        for (int q = 0; q < 4; ++q) {
+            const uint8_t* blk = block(gr + 8 * q);  // rows gr, gr + 8, 16 + gr, 24 + gr
+            d4[q] = blk ? (uint16_t)(blk[208] | (blk[209] << 8)) : (uint16_t)0;
+        }
+        uint32_t* o = reinterpret_cast<uint32_t*>(unit + Q4M_D_6 + 8 * gr);
+        o[0] = d4[0] | ((uint32_t)d4[1] << 16);
+        o[1] = d4[2] | ((uint32_t)d4[3] << 16);
+    }
+}
+
+// One thread per (pair, group, lane) of a Q8_0 matrix (AoS blocks of 34 bytes: fp16 d, 32
+// int8 q; [rows][nb], reference include/jinf/quant.h:50-56): the lane's eight weight words
+// and its scale record. Rows past `rows` and blocks past nb pack as zeros.
+__global__ void k_repack_q80(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
+                             int pairs, int nb) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)pairs * groups * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t pg = gid >> 5;
+    const int p = (int)(pg / groups), G = (int)(pg % groups);
+    const int gr = lane >> 2, c = lane & 3;
+    auto block = [&](int r, int j) -> const uint8_t* {
+        const int row = p * Q4M_PAIR_ROWS + r;
+        return row < rows && G * 4 + j < nb ? aos + ((size_t)row * nb + (size_t)G * 4 + j) * 34 : nullptr;
+    };
+    uint8_t* unit = dst + q4m_unit_offset(p, G, groups, Q4M_Q8_0);
+    for (int j = 0; j < 4; ++j)
+        for (int t = 0; t < 2; ++t)
+            for (int i = 0; i < 4; ++i) {
+                const uint8_t* blk = block(16 * t + gr + 8 * (i & 1), j);
+                uint32_t word = 0;
+                if (blk)
+                    for (int b = 0; b < 4; ++b) word |= (uint32_t)blk[2 + 16 * (i >> 1) + 4 * c + b] << (8 * b);
+                *reinterpret_cast<uint32_t*>(unit + 1024 * j + 512 * t + 16 * lane + 4 * i) = word;
+            }
+    uint16_t d4[4];
+    for (int q = 0; q < 4; ++q) {
+        const uint8_t* blk = block(gr + 8 * q, c);  // rows gr, gr + 8, 16 + gr, 24 + gr
+        d4[q] = blk ? (uint16_t)(blk[0] | (blk[1] << 8)) : (uint16_t)0;
+    }
+    uint32_t* o = reinterpret_cast<uint32_t*>(unit + Q4M_D_8 + 8 * lane);
+    o[0] = d4[0] | ((uint32_t)d4[1] << 16);
+    o[1] = d4[2] | ((uint32_t)d4[3] << 16);
+}
+
 // ---------------------------------------------------------------- host side
 
 size_t gemvm_smem_bytes(int cols, int fmt) {
     const int G = (cols + Q4M_KG - 1) / Q4M_KG;
-    return xrec_bytes(G) + sizeof(float) * (64 + NW * Q4M_PAIR_ROWS) + (size_t)NW * GEMV_M_NBUF * q4m_unit_bytes(fmt);
+    return xrec_bytes(G) + sizeof(float) * (64 + NW * Q4M_PAIR_ROWS) + (size_t)NW * gemvm_nbuf(fmt) * q4m_unit_bytes(fmt);
 }
 
 bool gemvm_use_local(int pairs, int grid) { return pairs <= 4 * grid; }
@@ -409,6 +525,10 @@ static cudaError_t launch_m(const GemvParams& p, int grid, cudaStream_t s, bool 
 #define JINF_GEMVM_DISPATCH(FMTV, FN, ...)                  \
     if ((FMTV) == Q4M_Q4_K) {                               \
         JINF_GEMVM_CASES(FN, Q4M_Q4_K, __VA_ARGS__)         \
+    } else if ((FMTV) == Q4M_Q6_K) {                        \
+        JINF_GEMVM_CASES(FN, Q4M_Q6_K, __VA_ARGS__)         \
+    } else if ((FMTV) == Q4M_Q8_0) {                        \
+        JINF_GEMVM_CASES(FN, Q4M_Q8_0, __VA_ARGS__)         \
     } else {                                                \
         JINF_GEMVM_CASES(FN, Q4M_Q4_0, __VA_ARGS__)         \
     }
@@ -449,7 +569,13 @@ cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStr
 
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s) {
     const int64_t n = (int64_t)sh.pairs * sh.groups * 32;
-    if (sh.fmt == Q4M_Q4_K)
+    if (sh.fmt == Q4M_Q6_K)
+        k_repack_q6k<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows,
+                                                                 sh.groups, sh.pairs, sh.cols / 256);
+    else if (sh.fmt == Q4M_Q8_0)
+        k_repack_q80<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows,
+                                                                 sh.groups, sh.pairs, sh.cols / 32);
+    else if (sh.fmt == Q4M_Q4_K)
         k_repack_q4mk<<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const uint8_t*)aos, (uint8_t*)dst, sh.rows,
                                                                   sh.groups, sh.pairs, sh.cols / 256);
     else

@@ -36,6 +36,32 @@
 //   bytes 2304 .. 2367   [16 rows][fp16 d, fp16 dmin]   tile A rows 0..15
 //   bytes 2368 .. 2431   [16 rows][fp16 d, fp16 dmin]   tile B rows 16..31
 // (d, dmin repeat in both units of a super-block). Q4_K columns are whole super-blocks.
+//
+// Q6_K matrices (reference include/jinf/quant.h:59-69: 256-element super-blocks, fp16 d, an
+// int8 scale per 16-element sub-block, w = d sc (q - 32) with q = low4 | high2 << 4, low4 the
+// low nibble of ql[e / 2] for even e, high2 bits 2 (e % 4) of qh[e / 4]) use 3392-byte units
+// (Q4M_UNIT_6) of the same geometry (group G = elements 128 (G % 2) .. +127 of super-block
+// G / 2, block j = 32 of them, k the element in the block):
+//   bytes    0 .. 2047   the low nibbles of q, laid out exactly as the Q4_0 nibbles above
+//   bytes 2048 .. 3071   [2 block pairs jj][32 lanes][4 words]: word 2 (j % 2) + h of lane L
+//                         holds the high two bits of q for the words i = 2h, 2h + 1 of block
+//                         j = 2 jj + (j % 2): byte b has, from bit 0, the crumbs of tile A
+//                         word 2h, tile B word 2h, tile A word 2h + 1, tile B word 2h + 1,
+//                         each with its top bit flipped (crumb ^ 2)
+//   bytes 3072 .. 3327   [32 lanes][2 words]: tile A, tile B int8 sub-block scales of lane
+//                         (gr, c): sc(row gr, block c, half 0), (gr, c, 1), (gr + 8, c, 0),
+//                         (gr + 8, c, 1) (half = elements 0..15 / 16..31 of the block)
+//   bytes 3328 .. 3391   [8 gr][4 x fp16]: d of rows gr, gr + 8, 16 + gr, 24 + gr
+// With the flipped crumb, (low4 << 2) | (crumb ^ 2) << 6 is the byte of the int8 value
+// 4 (q - 32), the s8 tensor-core operand (q4m_device.cuh).
+//
+// Q8_0 matrices (reference include/jinf/quant.h:50-56: 32-element blocks, fp16 d, int8 q,
+// w = d q) use 4352-byte units (Q4M_UNIT_8):
+//   bytes    0 .. 4095   [4 blocks j][2 tiles t][32 lanes][4 words i]: byte b of word i is q
+//                         of row 16 t + gr + 8 (i & 1), element k = 16 (i >> 1) + 4 c + b
+//   bytes 4096 .. 4351   [32 lanes][4 x fp16]: d of (row gr, block c), (gr + 8, c),
+//                         (16 + gr, c), (24 + gr, c)
+// Q6_K columns are whole super-blocks, Q8_0 columns whole blocks.
 #pragma once
 
 #include <stdint.h>
@@ -49,10 +75,32 @@ constexpr int Q4M_SCALES = 2048;         // byte offset of the scales in a unit
 constexpr int Q4M_PAIR_ROWS = 2 * Q4M_ROWS;
 constexpr int Q4M_UNIT_K = 2432;         // bytes per (tile pair, group) of a Q4_K matrix
 constexpr int Q4M_DMIN_K = 2304;         // byte offset of the per-row d, dmin in a Q4_K unit
+constexpr int Q4M_UNIT_6 = 3392;         // bytes per (tile pair, group) of a Q6_K matrix
+constexpr int Q4M_CRUMB_6 = 2048;        // byte offsets in a Q6_K unit: high-bit crumbs,
+constexpr int Q4M_SC_6 = 3072;           //   sub-block scales,
+constexpr int Q4M_D_6 = 3328;            //   per-row d
+constexpr int Q4M_UNIT_8 = 4352;         // bytes per (tile pair, group) of a Q8_0 matrix
+constexpr int Q4M_D_8 = 4096;            // byte offset of the scales in a Q8_0 unit
 
 // Weight formats of a Q4M matrix
-enum Q4MFormat { Q4M_Q4_0 = 0, Q4M_Q4_K = 1 };
-__host__ __device__ constexpr inline int q4m_unit_bytes(int fmt) { return fmt == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT; }
+enum Q4MFormat { Q4M_Q4_0 = 0, Q4M_Q4_K = 1, Q4M_Q6_K = 2, Q4M_Q8_0 = 3 };
+constexpr int Q4M_NFMT = 4;
+__host__ __device__ constexpr inline int q4m_unit_bytes(int fmt) {
+    return fmt == Q4M_Q4_K ? Q4M_UNIT_K : fmt == Q4M_Q6_K ? Q4M_UNIT_6 : fmt == Q4M_Q8_0 ? Q4M_UNIT_8 : Q4M_UNIT;
+}
+// Columns of a matrix of format fmt come in whole blocks (32) or super-blocks (256).
+__host__ __device__ constexpr inline int q4m_col_align(int fmt) {
+    return fmt == Q4M_Q4_K || fmt == Q4M_Q6_K ? 256 : 32;
+}
+
+// Bytes of one row of `cols` weights in the reference's AoS blocks of format fmt (Q4_0: 18
+// per 32, Q4_K: 144 per 256, Q6_K: 210 per 256, Q8_0: 34 per 32).
+__host__ __device__ inline uint64_t aos_row_bytes(int fmt, int64_t cols) {
+    return fmt == Q4M_Q4_K ? (uint64_t)cols / 256 * 144
+         : fmt == Q4M_Q6_K ? (uint64_t)cols / 256 * 210
+         : fmt == Q4M_Q8_0 ? (uint64_t)cols / 32 * 34
+                           : (uint64_t)cols / 32 * 18;
+}
 
 struct Q4MShape {
     int rows, cols;
@@ -77,7 +125,7 @@ __host__ __device__ inline uint64_t q4m_unit_offset(int p, int g, int groups, in
 // blocks (scale 0) when cols is not a multiple of 128, and the GEMV stages zero digits for
 // x there.
 inline bool q4m_shape(int rows, int cols, Q4MShape* s, int fmt = Q4M_Q4_0) {
-    if (rows <= 0 || cols <= 0 || cols % (fmt == Q4M_Q4_K ? 256 : 32)) return false;
+    if (rows <= 0 || cols <= 0 || fmt < 0 || fmt >= Q4M_NFMT || cols % q4m_col_align(fmt)) return false;
     s->rows = rows;
     s->cols = cols;
     s->pairs = (rows + Q4M_PAIR_ROWS - 1) / Q4M_PAIR_ROWS;

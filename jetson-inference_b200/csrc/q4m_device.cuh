@@ -66,10 +66,48 @@ __device__ __forceinline__ void copy_unit_k_async(uint32_t slot, const uint8_t* 
                      : "memory");
 }
 
+// This lane's share of a 3392-byte Q6_K unit: its nibble words, its two 16-byte crumb
+// pieces and its scale words; lanes 0..3 one 16-byte piece of the per-row d each (read by
+// other lanes: the consumer synchronises the warp, unit_mma_q6).
+__device__ __forceinline__ void copy_unit_6_async(uint32_t slot, const uint8_t* unit, int lane) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + 512 * j + lane * 16),
+                     "l"(unit + 512 * j + lane * 16)
+                     : "memory");
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + Q4M_CRUMB_6 + 512 * jj + lane * 16),
+                     "l"(unit + Q4M_CRUMB_6 + 512 * jj + lane * 16)
+                     : "memory");
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(slot + Q4M_SC_6 + lane * 8),
+                 "l"(unit + Q4M_SC_6 + lane * 8)
+                 : "memory");
+    if (lane < 4)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + Q4M_D_6 + lane * 16),
+                     "l"(unit + Q4M_D_6 + lane * 16)
+                     : "memory");
+}
+
+// This lane's share of a 4352-byte Q8_0 unit: its eight weight words of 16 bytes and its
+// 8-byte scale record. Each lane reads back only what it copied.
+__device__ __forceinline__ void copy_unit_8_async(uint32_t slot, const uint8_t* unit, int lane) {
+#pragma unroll
+    for (int jt = 0; jt < 8; ++jt)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(slot + 512 * jt + lane * 16),
+                     "l"(unit + 512 * jt + lane * 16)
+                     : "memory");
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(slot + Q4M_D_8 + lane * 8),
+                 "l"(unit + Q4M_D_8 + lane * 8)
+                 : "memory");
+}
+
 // The copy routine of a unit of format `fmt` (q4m.cuh).
 template <int FMT>
 __device__ __forceinline__ void copy_unit_fmt(uint32_t slot, const uint8_t* unit, int lane) {
     if (FMT == Q4M_Q4_K) copy_unit_k_async(slot, unit, lane);
+    else if (FMT == Q4M_Q6_K) copy_unit_6_async(slot, unit, lane);
+    else if (FMT == Q4M_Q8_0) copy_unit_8_async(slot, unit, lane);
     else copy_unit_async(slot, unit, lane);
 }
 
@@ -84,6 +122,23 @@ __device__ __forceinline__ void mma_u8s8(uint32_t a0, uint32_t a1, uint32_t a2, 
         "{%0, %1, %2, %3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_s8s8(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1, int (&d)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// m16n8k16: the first (or second) half of a 32-element block on its own
+__device__ __forceinline__ void mma_s8s8_k16(uint32_t a0, uint32_t a1, uint32_t b0, int (&d)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
 }
 
 // The u8 operands of a nibble word: tile A (low nibbles) and tile B (high nibbles, 16 q).
@@ -178,9 +233,99 @@ __device__ __forceinline__ void unit_mma_k(uint32_t sl, const XRecS& xr, int g, 
     __syncwarp();  // every lane's reads of the slot precede the next copy into it
 }
 
+// unit_mma for a Q6_K unit (q4m.cuh). Each weight byte is rebuilt as the int8 value
+// 4 (q - 32) from its nibble (bits 2..5) and flipped crumb (bits 6..7), so the products need
+// no zero point. A Q6_K scale covers 16 elements, so every block is two m16n8k16 steps, one
+// per half, each into its own accumulators; block c of row r then contributes
+// d sc_0 (256 D0_hi + D0_lo) + d sc_1 (256 D1_hi + D1_lo), times 1 / (4 alpha). The warp
+// synchronises before (lanes read the d words lanes 0..3 copied) and after (before a lane
+// copies the next unit into the slot).
+__device__ __forceinline__ void unit_mma_q6(uint32_t sl, const XRecS& xr, int g, int lane, float (&acc)[4]) {
+    __syncwarp();
+    uint32_t w[16], cr[8], sca, scb, dlo, dhi, b0, b1;
+    float ia;
+    const int gr = lane >> 2;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[4 * j]), "=r"(w[4 * j + 1]), "=r"(w[4 * j + 2]), "=r"(w[4 * j + 3])
+                     : "r"(sl + 512 * j + lane * 16));
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj)
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(cr[4 * jj]), "=r"(cr[4 * jj + 1]), "=r"(cr[4 * jj + 2]), "=r"(cr[4 * jj + 3])
+                     : "r"(sl + Q4M_CRUMB_6 + 512 * jj + lane * 16));
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(sca), "=r"(scb) : "r"(sl + Q4M_SC_6 + lane * 8));
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(dlo), "=r"(dhi) : "r"(sl + Q4M_D_6 + gr * 8));
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xr.dig + g * 256 + lane * 8));
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(ia) : "r"(xr.prm + (g * 4 + (lane & 3)) * 16 + 8));
+    const int myblk = lane >> 3;
+    int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0}, c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+    constexpr uint32_t NM = 0x3C3C3C3Cu, CM = 0xC0C0C0C0u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t x0 = myblk == j ? b0 : 0u, x1 = myblk == j ? b1 : 0u;
+        const uint32_t* n = w + 4 * j;
+        const uint32_t h0 = cr[2 * j], h1 = cr[2 * j + 1];  // crumbs of words 0, 1 / 2, 3
+        // tile A (low nibbles) and tile B (high nibbles) operands of words i = 0..3
+        const uint32_t A0 = ((n[0] << 2) & NM) | ((h0 << 6) & CM), B0 = ((n[0] >> 2) & NM) | ((h0 << 4) & CM);
+        const uint32_t A1 = ((n[1] << 2) & NM) | ((h0 << 2) & CM), B1 = ((n[1] >> 2) & NM) | (h0 & CM);
+        const uint32_t A2 = ((n[2] << 2) & NM) | ((h1 << 6) & CM), B2 = ((n[2] >> 2) & NM) | ((h1 << 4) & CM);
+        const uint32_t A3 = ((n[3] << 2) & NM) | ((h1 << 2) & CM), B3 = ((n[3] >> 2) & NM) | (h1 & CM);
+        mma_s8s8_k16(A0, A1, x0, a0);
+        mma_s8s8_k16(A2, A3, x1, a1);
+        mma_s8s8_k16(B0, B1, x0, c0);
+        mma_s8s8_k16(B2, B3, x1, c1);
+    }
+    const float s = 0.25f * ia;
+    auto sc = [](uint32_t v, int b) { return (float)(int8_t)(uint8_t)(v >> (8 * b)); };
+    auto row = [&](float d, uint32_t scw, int b, const int (&h0)[4], const int (&h1)[4], int r) {
+        const float s0 = (float)(h0[2 * r] * 256 + h0[2 * r + 1]);
+        const float s1 = (float)(h1[2 * r] * 256 + h1[2 * r + 1]);
+        return d * fmaf(sc(scw, b), s0, sc(scw, b + 1) * s1);
+    };
+    acc[0] = fmaf(row(jinf_h2f((uint16_t)(dlo & 0xffffu)), sca, 0, a0, a1, 0), s, acc[0]);
+    acc[1] = fmaf(row(jinf_h2f((uint16_t)(dlo >> 16)), sca, 2, a0, a1, 1), s, acc[1]);
+    acc[2] = fmaf(row(jinf_h2f((uint16_t)(dhi & 0xffffu)), scb, 0, c0, c1, 0), s, acc[2]);
+    acc[3] = fmaf(row(jinf_h2f((uint16_t)(dhi >> 16)), scb, 2, c0, c1, 1), s, acc[3]);
+    __syncwarp();  // every lane's reads of the slot precede the next copy into it
+}
+
+// unit_mma for a Q8_0 unit (q4m.cuh): the weight words are the int8 q themselves, one
+// m16n8k32 step per block and tile, no zero point; block c of row r contributes
+// d (256 D_hi + D_lo) / alpha.
+__device__ __forceinline__ void unit_mma_q8(uint32_t sl, const XRecS& xr, int g, int lane, float (&acc)[4]) {
+    uint32_t b0, b1, d01, d23;
+    float ia;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(d01), "=r"(d23) : "r"(sl + Q4M_D_8 + lane * 8));
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xr.dig + g * 256 + lane * 8));
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(ia) : "r"(xr.prm + (g * 4 + (lane & 3)) * 16 + 8));
+    const int myblk = lane >> 3;
+    int da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t wa[4], wb[4];
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(wa[0]), "=r"(wa[1]), "=r"(wa[2]), "=r"(wa[3])
+                     : "r"(sl + 1024 * j + lane * 16));
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(wb[0]), "=r"(wb[1]), "=r"(wb[2]), "=r"(wb[3])
+                     : "r"(sl + 1024 * j + 512 + lane * 16));
+        const uint32_t x0 = myblk == j ? b0 : 0u, x1 = myblk == j ? b1 : 0u;
+        mma_s8s8(wa[0], wa[1], wa[2], wa[3], x0, x1, da);
+        mma_s8s8(wb[0], wb[1], wb[2], wb[3], x0, x1, db);
+    }
+    acc[0] = fmaf(jinf_h2f((uint16_t)(d01 & 0xffffu)) * ia, (float)(da[0] * 256 + da[1]), acc[0]);
+    acc[1] = fmaf(jinf_h2f((uint16_t)(d01 >> 16)) * ia, (float)(da[2] * 256 + da[3]), acc[1]);
+    acc[2] = fmaf(jinf_h2f((uint16_t)(d23 & 0xffffu)) * ia, (float)(db[0] * 256 + db[1]), acc[2]);
+    acc[3] = fmaf(jinf_h2f((uint16_t)(d23 >> 16)) * ia, (float)(db[2] * 256 + db[3]), acc[3]);
+}
+
 template <int FMT>
 __device__ __forceinline__ void unit_mma_fmt(uint32_t sl, const XRecS& xr, int g, int lane, float (&acc)[4]) {
     if (FMT == Q4M_Q4_K) unit_mma_k(sl, xr, g, lane, acc);
+    else if (FMT == Q4M_Q6_K) unit_mma_q6(sl, xr, g, lane, acc);
+    else if (FMT == Q4M_Q8_0) unit_mma_q8(sl, xr, g, lane, acc);
     else unit_mma(sl, xr, g, lane, acc);
 }
 

@@ -153,6 +153,57 @@ extern "C" void jinf_quantize_q4_0(const float* x, jinf_block_q4_0* out, int64_t
     for (int64_t b = 0; b < n / 32; ++b) jinf_synth::quantize_q4_0_block(x + 32 * b, (uint8_t*)(out + b));
 }
 
+// Q8_0: d = max|x| / 127 (stored fp16), q = round-half-away(x / d) clamped to [-127, 127]
+// against the stored d.
+extern "C" void jinf_quantize_q8_0(const float* x, jinf_block_q8_0* out, int64_t n) {
+    for (int64_t b = 0; b < n / 32; ++b) {
+        const float* v = x + 32 * b;
+        float amax = 0.f;
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        const uint16_t dh = jinf_fp32_to_fp16(amax / 127.f);
+        const float d = jinf_fp16_to_fp32(dh);
+        out[b].d = dh;
+        for (int i = 0; i < 32; ++i) {
+            int q = d > 0.f ? (int)lroundf(v[i] / d) : 0;
+            out[b].qs[i] = (int8_t)(q < -127 ? -127 : (q > 127 ? 127 : q));
+        }
+    }
+}
+
+// Q6_K: per 16-element sub-block a symmetric step s = max|x| / 31, the 16 steps quantised
+// to int8 scales against the fp16 super-scale d = max(s) / 127, then q = round(x / (d sc)) + 32
+// clamped to 0..63 against the stored parameters, packed in the reference GPU layout.
+extern "C" void jinf_quantize_q6_K(const float* x, jinf_block_q6_K* out, int64_t n) {
+    for (int64_t b = 0; b < n / 256; ++b) {
+        const float* v = x + 256 * b;
+        float st[16], smax = 0.f;
+        for (int j = 0; j < 16; ++j) {
+            float amax = 0.f;
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[16 * j + i]));
+            st[j] = amax / 31.f;
+            smax = fmaxf(smax, st[j]);
+        }
+        const uint16_t dh = jinf_fp32_to_fp16(smax / 127.f);
+        const float d = jinf_fp16_to_fp32(dh);
+        jinf_block_q6_K& o = out[b];
+        memset(&o, 0, sizeof o);
+        o.d = dh;
+        for (int j = 0; j < 16; ++j) {
+            int sc = d > 0.f ? (int)lrintf(st[j] / d) : 0;
+            sc = sc > 127 ? 127 : sc;
+            o.scales[j] = (int8_t)sc;
+            const float step = d * (float)sc;
+            for (int i = 0; i < 16; ++i) {
+                const int e = 16 * j + i;
+                int q = step > 0.f ? (int)lrintf(v[e] / step) + 32 : 32;
+                q = q < 0 ? 0 : (q > 63 ? 63 : q);
+                o.ql[e >> 1] |= (uint8_t)((q & 15) << (4 * (e & 1)));
+                o.qh[e >> 2] |= (uint8_t)((q >> 4) << (2 * (e & 3)));
+            }
+        }
+    }
+}
+
 // Q4_K: per 32-element sub-block an affine fit x ~ s*q - m (q in 0..15, m >= 0), the
 // 8 scales and mins quantised to 6 bits against fp16 super-scales d = max(s)/63 and
 // dmin = max(m)/63, then q re-derived from the stored (rounded) parameters. Packed in

@@ -83,10 +83,15 @@ extern "C" jinf_status jinf_synth_create(jinf_synth_model** out, const jinf_synt
         return JINF_ERR_INVALID;
     const uint32_t hkv = hp.n_heads_kv ? hp.n_heads_kv : hp.n_heads;
     if (hp.n_embd % hp.n_heads || hp.n_heads % hkv) return JINF_ERR_INVALID;
-    const int wt = cfg->weight_type;
-    const int bs = jinf_qtype_block_size((jinf_qtype)wt);
-    if (wt != JINF_TYPE_Q4_0 && wt != JINF_TYPE_Q4_K) return JINF_ERR_INVALID;
-    if (hp.n_embd % bs || hp.n_ff % bs) return JINF_ERR_INVALID;
+    const int wt = cfg->weight_type, mt = cfg->mix_type ? cfg->mix_type : cfg->weight_type;
+    auto quant_ok = [](int t) {
+        return t == JINF_TYPE_Q4_0 || t == JINF_TYPE_Q4_K || t == JINF_TYPE_Q6_K || t == JINF_TYPE_Q8_0;
+    };
+    if (!quant_ok(wt) || !quant_ok(mt)) return JINF_ERR_INVALID;
+    for (const int t : {wt, mt}) {
+        const int bs = jinf_qtype_block_size((jinf_qtype)t);
+        if (hp.n_embd % bs || hp.n_ff % bs) return JINF_ERR_INVALID;
+    }
 
     jinf_synth_model* m = new jinf_synth_model();
     m->cfg = *cfg;
@@ -106,15 +111,16 @@ extern "C" jinf_status jinf_synth_create(jinf_synth_model** out, const jinf_synt
         snprintf(buf, sizeof buf, "blk.%u.attn_norm.weight", L);   add(buf, JINF_TYPE_F32, 1, d, 1, 1);
         snprintf(buf, sizeof buf, "blk.%u.attn_q.weight", L);      add(buf, wt, 2, d, d, 0);
         snprintf(buf, sizeof buf, "blk.%u.attn_k.weight", L);      add(buf, wt, 2, d, kv, 0);
-        snprintf(buf, sizeof buf, "blk.%u.attn_v.weight", L);      add(buf, wt, 2, d, kv, 0);
+        const int lt = L % 2 == 0 ? mt : wt;  // attn_v and ffn_down of the even layers
+        snprintf(buf, sizeof buf, "blk.%u.attn_v.weight", L);      add(buf, lt, 2, d, kv, 0);
         snprintf(buf, sizeof buf, "blk.%u.attn_output.weight", L); add(buf, wt, 2, d, d, 0);
         snprintf(buf, sizeof buf, "blk.%u.ffn_norm.weight", L);    add(buf, JINF_TYPE_F32, 1, d, 1, 1);
         snprintf(buf, sizeof buf, "blk.%u.ffn_gate.weight", L);    add(buf, wt, 2, d, ff, 0);
         snprintf(buf, sizeof buf, "blk.%u.ffn_up.weight", L);      add(buf, wt, 2, d, ff, 0);
-        snprintf(buf, sizeof buf, "blk.%u.ffn_down.weight", L);    add(buf, wt, 2, ff, d, 0);
+        snprintf(buf, sizeof buf, "blk.%u.ffn_down.weight", L);    add(buf, lt, 2, ff, d, 0);
     }
     add("output_norm.weight", JINF_TYPE_F32, 1, d, 1, 1);
-    add("output.weight", wt, 2, d, V, 0);
+    add("output.weight", mt, 2, d, V, 0);
     *out = m;
     return JINF_OK;
 }
@@ -171,8 +177,12 @@ extern "C" jinf_status jinf_synth_read_rows(const jinf_synth_model* m, const cha
                 gen_normals(key, idx0, cols, stdv, row.data());
                 if (t->type == JINF_TYPE_Q4_0)
                     jinf_quantize_q4_0(row.data(), (jinf_block_q4_0*)o, cols);
-                else
+                else if (t->type == JINF_TYPE_Q4_K)
                     jinf_quantize_q4_K(row.data(), (jinf_block_q4_K*)o, cols);
+                else if (t->type == JINF_TYPE_Q6_K)
+                    jinf_quantize_q6_K(row.data(), (jinf_block_q6_K*)o, cols);
+                else
+                    jinf_quantize_q8_0(row.data(), (jinf_block_q8_0*)o, cols);
             }
         }
     }

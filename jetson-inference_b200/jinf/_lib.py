@@ -40,7 +40,7 @@ class HParams(C.Structure):
 
 class SynthConfig(C.Structure):
     _fields_ = [("hp", HParams), ("seed", C.c_uint64), ("weight_type", C.c_int),
-                ("weight_std", C.c_float), ("embed_std", C.c_float)]
+                ("weight_std", C.c_float), ("embed_std", C.c_float), ("mix_type", C.c_int)]
 
 
 class EngineConfig(C.Structure):
@@ -136,6 +136,8 @@ SIGNATURES = {
     "jinf_fp32_to_fp16": (C.c_uint16, [f32]),
     "jinf_quantize_q4_0": (None, [vp, vp, i64]),
     "jinf_quantize_q4_K": (None, [vp, vp, i64]),
+    "jinf_quantize_q8_0": (None, [vp, vp, i64]),
+    "jinf_quantize_q6_K": (None, [vp, vp, i64]),
     # kernels.h
     "jinf_cuda_dequant_matvec": (None, [vp, vp, vp, i32, i32, i32, vp]),
     "jinf_cuda_residual_add": (None, [vp, vp, i32, vp]),

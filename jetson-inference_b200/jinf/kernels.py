@@ -97,7 +97,8 @@ def gemv_q4m_batch(q4m, x, y, rows: int, cols: int, batch: int, workspace=None, 
 
 
 def q4m_bytes_qt(rows: int, cols: int, qtype: int) -> int:
-    """Q4M image bytes for qtype Q4_0 (2) or Q4_K (12); 0 for an unsupported type or shape."""
+    """Q4M image bytes for qtype Q4_0 (2), Q8_0 (8), Q4_K (12) or Q6_K (14); 0 for an
+    unsupported type or shape."""
     return int(L.lib.jinf_b200_q4m_bytes_qt(rows, cols, qtype))
 
 

@@ -50,16 +50,20 @@ class SynthModel:
     """Seeded synthetic model: every value is a pure function of (seed, tensor, index)."""
 
     def __init__(self, shape: LlamaShape, seed: int = 0, weight_type: int = L.Q4_0,
-                 weight_std: float = 0.02, embed_std: float = 0.02):
+                 weight_std: float = 0.02, embed_std: float = 0.02, mix_type: int = 0):
+        """mix_type (e.g. Q6_K with weight_type Q4_K, a Q4_K_M-like file) is the type of attn_v
+        and ffn_down in the even layers and of the output head; 0 keeps one type throughout."""
         cfg = L.SynthConfig()
         cfg.hp = shape.hparams()
         cfg.seed, cfg.weight_type, cfg.weight_std, cfg.embed_std = seed, weight_type, weight_std, embed_std
+        cfg.mix_type = mix_type
         h = C.c_void_p()
         L.check(L.lib.jinf_synth_create(C.byref(h), C.byref(cfg)), "jinf_synth_create")
         self.handle = h
         self.shape = shape
         self.seed = seed
         self.weight_type = weight_type
+        self.mix_type = mix_type
 
     def close(self) -> None:
         if self.handle:

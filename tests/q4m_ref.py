@@ -194,3 +194,185 @@ def emulate_gemv_q4k(img: np.ndarray, x: np.ndarray, rows: int, cols: int) -> np
     sub_m = (_f16(dmin) * mn.astype(np.float32)).astype(np.float32)
     v = (sub_d * dq.astype(np.float32) - sub_m * s[None, :].astype(np.float32)).astype(np.float32)
     return (v * inv_alpha[None, :]).astype(np.float64).sum(axis=1).astype(np.float32)
+
+
+# ---------------------------------------------------------------- Q6_K and Q8_0 (jetson-inference_b200/csrc/q4m.cuh)
+
+UNIT_6, UNIT_8 = 3392, 4352
+
+
+def random_q6k_rows(rows, cols, seed):
+    """Random AoS Q6_K blocks [rows][cols/256*210]: any ql, qh, int8 scales, small positive d."""
+    rng = np.random.default_rng(seed)
+    nsb = cols // 256
+    b = rng.integers(0, 256, size=(rows, nsb, 210), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal((rows, nsb))) * 2e-4 + 1e-5).astype(np.float16).view(np.uint16)
+    b[:, :, 208] = d & 0xFF
+    b[:, :, 209] = d >> 8
+    return b.reshape(rows, -1)
+
+
+def random_q80_rows(rows, cols, seed):
+    """Random AoS Q8_0 blocks [rows][cols/32*34]: any int8 q, small positive d."""
+    rng = np.random.default_rng(seed)
+    nb = cols // 32
+    b = rng.integers(0, 256, size=(rows, nb, 34), dtype=np.uint8)
+    d = (np.abs(rng.standard_normal((rows, nb))) * 2e-4 + 1e-5).astype(np.float16).view(np.uint16)
+    b[:, :, 0] = d & 0xFF
+    b[:, :, 1] = d >> 8
+    return b.reshape(rows, -1)
+
+
+def _q6k_fields(aos, rows, cols):
+    """AoS Q6_K -> q [rows][cols/32][32] (0..63), sc [rows][cols/16] int8, d bits [rows][cols/256]."""
+    nsb = cols // 256
+    b = aos.reshape(rows, nsb, 210)
+    e = np.arange(256)
+    lo = (b[:, :, e >> 1] >> ((e & 1) * 4).astype(np.uint8)) & 15
+    hi = (b[:, :, 128 + (e >> 2)] >> (2 * (e & 3)).astype(np.uint8)) & 3
+    q = (lo | (hi << 4)).astype(np.uint8).reshape(rows, nsb * 8, 32)
+    sc = b[:, :, 192:208].view(np.int8).reshape(rows, nsb * 16)
+    d = b[:, :, 208].astype(np.uint16) | (b[:, :, 209].astype(np.uint16) << 8)
+    return q, sc, d
+
+
+def pack_q6k(aos, rows, cols):
+    """AoS Q6_K blocks -> Q4M (Q6_K form) bytes, following the layout comment of q4m.cuh."""
+    q, sc, d = _q6k_fields(aos, rows, cols)
+    groups, pairs = cols // KG, (rows + PAIR - 1) // PAIR
+    R = pairs * PAIR
+    qp = np.full((R, groups * 4, 32), 32, np.uint8); qp[:rows] = q            # missing rows: q = 32
+    scp = np.zeros((R, groups * 8), np.int8); scp[:rows] = sc
+    dp = np.zeros((R, cols // 256), np.uint16); dp[:rows] = d
+    qp = qp.reshape(pairs, PAIR, groups, 4, 32).transpose(0, 2, 1, 3, 4)       # p, G, r, j, k
+    scp = scp.reshape(pairs, PAIR, groups, 4, 2).transpose(0, 2, 1, 3, 4)      # p, G, r, j, half
+    dp = np.repeat(dp, 2, axis=1).reshape(pairs, PAIR, groups).transpose(0, 2, 1)  # p, G, r
+    out = np.zeros((pairs, groups, UNIT_6), np.uint8)
+    off = _layout()
+    low = qp & 15
+    out[:, :, off[:16].reshape(-1)] = (low[:, :, :16] | (low[:, :, 16:] << 4)).reshape(pairs, groups, -1)
+    crumb = (qp >> 4) ^ 2
+    for lane in range(32):
+        gr, c = lane >> 2, lane & 3
+        for j in range(4):
+            for h in range(2):
+                word = np.zeros((pairs, groups), np.uint32)
+                for t in range(4):
+                    k = 16 * h + 4 * c + t
+                    byte = np.zeros((pairs, groups), np.uint32)
+                    for u in range(2):
+                        r = gr + 8 * u
+                        byte |= (crumb[:, :, r, j, k].astype(np.uint32)
+                                 | (crumb[:, :, 16 + r, j, k].astype(np.uint32) << 2)) << (4 * u)
+                    word |= byte << (8 * t)
+                o = 2048 + 512 * (j >> 1) + 16 * lane + 4 * (2 * (j & 1) + h)
+                out[:, :, o:o + 4] = word.astype('<u4')[..., None].view(np.uint8)
+        for t in range(2):
+            for u in range(2):
+                for h in range(2):
+                    out[:, :, 3072 + 8 * lane + 4 * t + 2 * u + h] = scp[:, :, 16 * t + gr + 8 * u, c, h].view(np.uint8)
+    for gr in range(8):
+        for qq in range(4):
+            out[:, :, 3328 + 8 * gr + 2 * qq:3328 + 8 * gr + 2 * qq + 2] = \
+                dp[:, :, gr + 8 * qq].astype('<u2')[..., None].view(np.uint8)
+    return out.reshape(-1)
+
+
+def emulate_gemv_q6k(img, x, rows, cols):
+    """unit_mma_q6 at element level: the s8 operand bytes are rebuilt from the unit's words
+    with the kernel's shifts and masks, summed exactly per 16-element half against the digits,
+    then scaled by d sc / (4 alpha) in fp32."""
+    groups, pairs = cols // KG, (rows + PAIR - 1) // PAIR
+    u = img.reshape(pairs, groups, UNIT_6)
+    w8 = np.zeros((pairs, groups, PAIR, 4, 32), np.int8)     # p, G, r, j, k: 4 (q - 32)
+    NM, CM = np.uint32(0x3C3C3C3C), np.uint32(0xC0C0C0C0)
+    words = u[:, :, :2048].copy().view('<u4').reshape(pairs, groups, 4, 32, 4)      # j, lane, i
+    crw = u[:, :, 2048:3072].copy().view('<u4').reshape(pairs, groups, 2, 32, 4)   # jj, lane, 2 (j&1) + h
+    for lane in range(32):
+        gr, c = lane >> 2, lane & 3
+        for j in range(4):
+            for i in range(4):
+                n = words[:, :, j, lane, i]
+                h = crw[:, :, j >> 1, lane, 2 * (j & 1) + (i >> 1)]
+                sa = 6 if i % 2 == 0 else 2      # tile A crumb of word i sits at bits 4 (i & 1)
+                sb = 4 if i % 2 == 0 else 0      # tile B crumb at bits 4 (i & 1) + 2
+                A = ((n << np.uint32(2)) & NM) | ((h << np.uint32(sa)) & CM)
+                B = ((n >> np.uint32(2)) & NM) | ((h << np.uint32(sb)) & CM)
+                r = gr + 8 * (i & 1)
+                for t in range(4):
+                    k = 16 * (i >> 1) + 4 * c + t
+                    w8[:, :, r, j, k] = ((A >> np.uint32(8 * t)) & np.uint32(255)).astype(np.uint8).view(np.int8)
+                    w8[:, :, 16 + r, j, k] = ((B >> np.uint32(8 * t)) & np.uint32(255)).astype(np.uint8).view(np.int8)
+    sw = u[:, :, 3072:3328].copy().view(np.int8).reshape(pairs, groups, 32, 2, 2, 2)   # lane, t, u, h
+    sc = np.zeros((pairs, groups, PAIR, 4, 2), np.float32)
+    for lane in range(32):
+        gr, c = lane >> 2, lane & 3
+        for t in range(2):
+            for uu in range(2):
+                sc[:, :, 16 * t + gr + 8 * uu, c, :] = sw[:, :, lane, t, uu, :]
+    db = u[:, :, 3328:].copy().view('<u2').reshape(pairs, groups, 8, 4)
+    d = np.zeros((pairs, groups, PAIR), np.uint16)
+    for gr in range(8):
+        for qq in range(4):
+            d[:, :, gr + 8 * qq] = db[:, :, gr, qq]
+    hi, lo, inv_alpha = x_records(x, cols)
+    hi = hi.reshape(groups, 4, 2, 16).astype(np.int64)
+    lo = lo.reshape(groups, 4, 2, 16).astype(np.int64)
+    wv = w8.astype(np.int64).reshape(pairs, groups, PAIR, 4, 2, 16)
+    S = 256 * np.einsum('pgrjhk,gjhk->pgrjh', wv, hi) + np.einsum('pgrjhk,gjhk->pgrjh', wv, lo)
+    v = (sc[:, :, :, :, 0] * S[..., 0].astype(np.float32) + sc[:, :, :, :, 1] * S[..., 1].astype(np.float32))
+    v = _f16(d)[..., None] * v * (0.25 * inv_alpha.reshape(groups, 4))[None, :, None, :]
+    y = v.astype(np.float64).sum(axis=(1, 3)).reshape(pairs * PAIR)
+    return y[:rows].astype(np.float32)
+
+
+def pack_q80(aos, rows, cols):
+    """AoS Q8_0 blocks -> Q4M (Q8_0 form) bytes, following the layout comment of q4m.cuh."""
+    nb = cols // 32
+    groups, pairs = (cols + KG - 1) // KG, (rows + PAIR - 1) // PAIR
+    b = np.zeros((pairs * PAIR, groups * 4, 34), np.uint8)
+    b[:rows, :nb] = aos.reshape(rows, nb, 34)
+    b = b.reshape(pairs, PAIR, groups, 4, 34).transpose(0, 2, 3, 1, 4)    # p, G, j, r, 34
+    out = np.zeros((pairs, groups, UNIT_8), np.uint8)
+    for lane in range(32):
+        gr, c = lane >> 2, lane & 3
+        for j in range(4):
+            for t in range(2):
+                for i in range(4):
+                    r = 16 * t + gr + 8 * (i & 1)
+                    k0 = 16 * (i >> 1) + 4 * c
+                    o = 1024 * j + 512 * t + 16 * lane + 4 * i
+                    out[:, :, o:o + 4] = b[:, :, j, r, 2 + k0:2 + k0 + 4]
+        for qq in range(4):
+            o = 4096 + 8 * lane + 2 * qq
+            out[:, :, o:o + 2] = b[:, :, c, gr + 8 * qq, 0:2]
+    return out.reshape(-1)
+
+
+def emulate_gemv_q80(img, x, rows, cols):
+    """unit_mma_q8 at element level: int8 q times the digits, summed exactly per block, scaled
+    by d / alpha in fp32."""
+    groups, pairs = (cols + KG - 1) // KG, (rows + PAIR - 1) // PAIR
+    u = img.reshape(pairs, groups, UNIT_8)
+    q = np.zeros((pairs, groups, 4, PAIR, 32), np.int8)
+    d = np.zeros((pairs, groups, 4, PAIR), np.uint16)
+    for lane in range(32):
+        gr, c = lane >> 2, lane & 3
+        for j in range(4):
+            for t in range(2):
+                for i in range(4):
+                    r = 16 * t + gr + 8 * (i & 1)
+                    k0 = 16 * (i >> 1) + 4 * c
+                    o = 1024 * j + 512 * t + 16 * lane + 4 * i
+                    q[:, :, j, r, k0:k0 + 4] = u[:, :, o:o + 4].view(np.int8)
+        for qq in range(4):
+            o = 4096 + 8 * lane + 2 * qq
+            d[:, :, c, gr + 8 * qq] = u[:, :, o:o + 2].copy().view('<u2')[..., 0]
+    hi, lo, inv_alpha = x_records(x, cols)
+    hi = hi.reshape(groups, 4, 32).astype(np.int64)
+    lo = lo.reshape(groups, 4, 32).astype(np.int64)
+    qv = q.astype(np.int64)
+    S = 256 * np.einsum('pgjrk,gjk->pgjr', qv, hi) + np.einsum('pgjrk,gjk->pgjr', qv, lo)
+    v = _f16(d) * S.astype(np.float32) * inv_alpha.reshape(groups, 4)[None, :, :, None]
+    y = v.astype(np.float64).sum(axis=(1, 2)).reshape(pairs * PAIR)
+    return y[:rows].astype(np.float32)

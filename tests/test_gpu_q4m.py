@@ -190,7 +190,68 @@ def test_q4k_rejects_partial_superblocks(cuda):
     from jinf import kernels as K
     assert K.q4m_bytes_qt(16, 384, 12) == 0       # not whole 256-element super-blocks
     assert K.q4m_bytes_qt(16, 384, 2) > 0
-    assert K.q4m_bytes_qt(16, 256, 8) == 0        # Q8_0: no Q4M form
+    assert K.q4m_bytes_qt(16, 384, 14) == 0       # Q6_K: whole super-blocks too
+    assert K.q4m_bytes_qt(16, 96, 8) > 0           # Q8_0: whole 32-element blocks
+    assert K.q4m_bytes_qt(16, 256, 1) == 0         # F16: no Q4M form
+
+
+# ---------------------------------------------------------------- Q6_K and Q8_0 weights
+
+QT_HELPERS = {14: (q4m_ref.random_q6k_rows, q4m_ref.pack_q6k, q4m_ref.emulate_gemv_q6k),
+              8: (q4m_ref.random_q80_rows, q4m_ref.pack_q80, q4m_ref.emulate_gemv_q80)}
+
+
+def packed_qt(w, qt, rows, cols, cuda):
+    from jinf import kernels as K
+    q = torch.empty(K.q4m_bytes_qt(rows, cols, qt), dtype=torch.uint8, device=cuda)
+    K.q4m_pack_qt(torch.from_numpy(np.ascontiguousarray(w)).to(cuda), qt, q, rows, cols)
+    return q
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(14, 16, 256), (14, 37, 512), (14, 100, 1024), (14, 1024, 4096),
+                                          (8, 16, 32), (8, 37, 160), (8, 100, 736), (8, 1024, 4096)])
+def test_q6k_q80_pack_matches_layout(cuda, qt, rows, cols):
+    gen, pack, _ = QT_HELPERS[qt]
+    w = gen(rows, cols, seed=rows + qt)
+    assert np.array_equal(packed_qt(w, qt, rows, cols, cuda).cpu().numpy(), pack(w, rows, cols))
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(14, 4096, 4096), (14, 1024, 4096), (14, 4096, 14336), (14, 128256, 4096),
+                                          (14, 37, 512), (14, 8192, 1024), (14, 8192, 28672),
+                                          (8, 4096, 4096), (8, 1024, 4096), (8, 4096, 14336), (8, 128256, 4096),
+                                          (8, 37, 160), (8, 40, 96), (8, 8192, 28672)])
+def test_gemv_q6k_q80(cuda, qt, rows, cols):
+    from jinf import kernels as K
+    gen, pack, emulate = QT_HELPERS[qt]
+    w = gen(rows, cols, seed=rows + cols + qt)
+    x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
+    q = packed_qt(w, qt, rows, cols, cuda)
+    ws = workspace(rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    y2 = torch.empty(rows, dtype=torch.float32, device=cuda)
+    xd = torch.from_numpy(x).to(cuda)
+    K.gemv_q4m_qt(q, qt, xd, y, rows, cols, workspace=ws)
+    K.gemv_q4m_qt(q, qt, xd, y2, rows, cols, workspace=ws)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.matvec(w, qt, x, rows, cols)) < REL
+    assert torch.equal(y, y2)
+    if rows * cols <= 1024 * 4096:
+        assert rel_err(y.cpu().numpy(), emulate(pack(w, rows, cols), x, rows, cols)) < 1e-5
+
+
+@pytest.mark.parametrize("qt", [14, 8])
+@pytest.mark.parametrize("kw", [1, 2, 3, 7, 32])
+def test_gemv_q6k_q80_every_k_split(cuda, qt, kw):
+    from jinf import kernels as K
+    rows, cols = 2048, 4096
+    gen = QT_HELPERS[qt][0]
+    w = gen(rows, cols, seed=kw + qt)
+    x = np.random.default_rng(kw).standard_normal(cols).astype(np.float32)
+    q = packed_qt(w, qt, rows, cols, cuda)
+    y = torch.empty(rows, dtype=torch.float32, device=cuda)
+    K.gemv_q4m_qt(q, qt, torch.from_numpy(x).to(cuda), y, rows, cols, workspace=workspace(rows, cols, cuda), kw=kw)
+    torch.cuda.synchronize()
+    assert rel_err(y.cpu().numpy(), oracle.matvec(w, qt, x, rows, cols)) < REL
 
 
 # ---------------------------------------------------------------- batched GEMV (C2 at batch 4 / 8)

@@ -117,3 +117,58 @@ def test_emulated_gemv_q4k_matches_oracle(rows, cols):
     x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
     y = q4m_ref.emulate_gemv_q4k(q4m_ref.pack_q4k(w, rows, cols), x, rows, cols)
     assert rel_err(y, oracle.matvec(w, 12, x, rows, cols)) < REL
+
+
+# ---------------------------------------------------------------- Q6_K and Q8_0 units
+
+@pytest.mark.parametrize("rows,cols", [(16, 256), (37, 512), (64, 1024), (100, 768)])
+def test_emulated_gemv_q6k_matches_oracle(rows, cols):
+    w = q4m_ref.random_q6k_rows(rows, cols, seed=rows + cols)
+    x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
+    img = q4m_ref.pack_q6k(w, rows, cols)
+    assert img.size == ((rows + 31) // 32) * (cols // 128) * 3392
+    y = q4m_ref.emulate_gemv_q6k(img, x, rows, cols)
+    assert rel_err(y, oracle.matvec(w, 14, x, rows, cols)) < REL
+
+
+@pytest.mark.parametrize("rows,cols", [(16, 32), (37, 160), (64, 1024), (100, 736)])
+def test_emulated_gemv_q80_matches_oracle(rows, cols):
+    w = q4m_ref.random_q80_rows(rows, cols, seed=rows + cols)
+    x = np.random.default_rng(cols).standard_normal(cols).astype(np.float32)
+    img = q4m_ref.pack_q80(w, rows, cols)
+    assert img.size == ((rows + 31) // 32) * ((cols + 127) // 128) * 4352
+    y = q4m_ref.emulate_gemv_q80(img, x, rows, cols)
+    assert rel_err(y, oracle.matvec(w, 8, x, rows, cols)) < REL
+
+
+@pytest.mark.parametrize("qt,fn,bb,bs", [(8, "jinf_quantize_q8_0", 34, 32), (14, "jinf_quantize_q6_K", 210, 256)])
+def test_host_quantizers_round_trip(qt, fn, bb, bs):
+    """The synthetic-model quantizers for Q8_0 and Q6_K: dequantized (oracle) values lie within
+    half a quantisation step (plus fp16 rounding of the scales) of the input."""
+    import jinf
+    n = 4096
+    x = (np.random.default_rng(qt).standard_normal(n) * 0.02).astype(np.float32)
+    out = np.zeros(n // bs * bb, dtype=np.uint8)
+    getattr(jinf.lib, fn)(x.ctypes.data_as(C.c_void_p), out.ctypes.data_as(C.c_void_p), n)
+    y = oracle.dequant(out, qt)
+    err = np.abs(y - x).reshape(-1, 16 if qt == 14 else 32).max(axis=1)
+    amax = np.abs(x).reshape(-1, 16 if qt == 14 else 32).max(axis=1)
+    steps = 31.0 if qt == 14 else 127.0
+    assert np.all(err <= amax / steps * 0.55 + 1e-6), float(np.max(err / (amax / steps)))
+
+
+def test_synth_mixed_types():
+    """mix_type puts attn_v and ffn_down of the even layers and the output head in the second
+    type, the Q4_K_M pattern; everything else keeps weight_type."""
+    import jinf
+    from jinf import _lib as L
+    syn = jinf.SynthModel(jinf.LlamaShape(4, 512, 8, 2, 1536, 4096, 10000.0, 1e-5), seed=0,
+                          weight_type=L.Q4_K, mix_type=L.Q6_K)
+    for name in syn.tensor_names():
+        t = syn.tensor_info(name)[0]
+        if name.endswith("norm.weight") or name == "token_embd.weight":
+            assert t == L.F32
+        elif name == "output.weight" or (name.split(".")[-2] in ("attn_v", "ffn_down") and int(name.split(".")[1]) % 2 == 0):
+            assert t == L.Q6_K, name
+        else:
+            assert t == L.Q4_K, name
