@@ -1,6 +1,6 @@
 """Decode benchmark: Llama-3-8B-shape Q4_0 greedy decode on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 8b|tiny|70b]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 8b|8b-q4km|tiny|70b]
 
 A step is one greedy decode token at batch 1 (the reference's per-token decode loop,
 reference src/engine.cpp:684-804), after a 512-token prompt: positions 512+W .. 512+W+K-1.
@@ -145,17 +145,25 @@ def all_max(dist, v: float) -> float:
 
 def shape_for(name):
     import jinf
-    return {"8b": jinf.LLAMA3_8B, "tiny": jinf.TINY, "70b": jinf.LLAMA3_70B}[name]
+    return {"8b": jinf.LLAMA3_8B, "8b-q4km": jinf.LLAMA3_8B, "tiny": jinf.TINY, "70b": jinf.LLAMA3_70B}[name]
 
 
 def wtype_for(name):
-    """Weight quantisation of a config: Q4_K for the 70B shape, else Q4_0."""
+    """Weight quantisation of a config: Q4_K for the 70B shape and for the
+    Q4_K_M-like 8B file, else Q4_0."""
     from jinf import _lib as L
-    return L.Q4_K if name == "70b" else L.Q4_0
+    return L.Q4_K if name in ("70b", "8b-q4km") else L.Q4_0
+
+
+def mix_for(name):
+    """Second weight type of a config: Q6_K for attn_v and ffn_down of the even layers and for
+    the output head in the Q4_K_M-like 8B file (8b-q4km), else none."""
+    from jinf import _lib as L
+    return L.Q6_K if name == "8b-q4km" else 0
 
 
 def wname_for(name):
-    return "q4_k" if name == "70b" else "q4_0"
+    return {"70b": "q4_k", "8b-q4km": "q4_k+q6_k"}.get(name, "q4_0")
 
 
 def prompt_ids(n_vocab, n=PROMPT):
@@ -165,12 +173,13 @@ def prompt_ids(n_vocab, n=PROMPT):
 
 # ------------------------------------------------------------------------- CPU oracle
 
-def cpu_decode_sample(shape, layers: int, target_s: float, min_reps: int = 2, wtype=None):
+def cpu_decode_sample(shape, layers: int, target_s: float, min_reps: int = 2, wtype=None, mix=0):
     """Time the CPU oracle on `layers` layers (+ LM head) of a decode token at position PROMPT,
     extrapolate the per-token time to all layers. Returns (tok/s, threads, description)."""
     from oracle import oracle
     import jinf
-    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype) if wtype is not None else jinf.SynthModel(shape, seed=0)
+    syn = (jinf.SynthModel(shape, seed=0, weight_type=wtype, mix_type=mix) if wtype is not None
+           else jinf.SynthModel(shape, seed=0))
     om = oracle.OracleModel(syn, max_ctx=PROMPT + 512, kv_f16=True, layers=layers)
     om.fill_kv_random(PROMPT, seed=1)
     tok = 1
@@ -206,7 +215,7 @@ def run_reference(args, rank, world):
     from oracle import oracle
     import jinf
     layers = 1
-    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config))
+    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config), mix_type=mix_for(args.config))
     om = oracle.OracleModel(syn, max_ctx=PROMPT + args.warmup + args.steps + 8, kv_f16=True, layers=layers)
     om.fill_kv_random(PROMPT, seed=1)
     for _ in range(args.warmup):
@@ -320,7 +329,7 @@ def run_ours(args, rank, world, local):
         dist.broadcast_object_list(buf, src=0)
         nccl_id = buf[0]
     t_load = time.perf_counter()
-    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config))
+    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config), mix_type=mix_for(args.config))
     max_ctx = PROMPT + args.warmup + args.steps + 8
     opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
                              sparse_mode=args.sparse)
@@ -392,8 +401,8 @@ def run_ours(args, rank, world, local):
         cpu = None
         if world == 1 and not args.no_cpu:
             cv, cores, desc, _ = cpu_decode_sample(
-                shape, layers={"8b": 2, "70b": 1}.get(args.config, shape.n_layers), target_s=args.cpu_seconds,
-                wtype=wtype_for(args.config))
+                shape, layers={"8b": 2, "8b-q4km": 2, "70b": 1}.get(args.config, shape.n_layers), target_s=args.cpu_seconds,
+                wtype=wtype_for(args.config), mix=mix_for(args.config))
             cpu = {"value": cv, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -434,7 +443,7 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="8b", choices=["8b", "tiny", "70b"])
+    ap.add_argument("--config", default="8b", choices=["8b", "8b-q4km", "tiny", "70b"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the C2 GEMV shape sweep")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
