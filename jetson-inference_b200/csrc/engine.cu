@@ -281,8 +281,10 @@ struct jinf_engine_impl {
     int device = 0;
     int tp_rank = 0, tp_size = 1;
     int num_sms = 148;
-    int wfmt = Q4M_Q4_0;       // Q4MFormat of the weight matrices when they share one (uniform)
+    int wfmt = Q4M_Q4_0;       // Q4MFormat of the weight matrices when they share one (uniform),
+                               // else Q4M_MIX (the persistent step's mixed instance)
     bool uniform = true;       // every projection and the output head of one type, Q4_0 or Q4_K
+    bool step_formats = true;  // every matrix Q4_0, Q4_K or Q6_K: the persistent step can stream it
     int wtype = JINF_TYPE_Q4_0;
     cudaStream_t stream = nullptr;
     bool use_graph = true;
@@ -663,6 +665,7 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         p.cols = sh.cols;
         p.pairs = sh.pairs;
         p.groups = sh.groups;
+        p.fmts = sh.fmt | (sh.fmt << 4) | (sh.pairs << 8);
         p.gran = 1;
         p.xin = p.xout = -1;
         ph.push_back(p);
@@ -690,6 +693,11 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         // extra dependent round trip each, more than they save; step_rec[1], [3] and
         // step_ss stay available for that form).
         StepPhase& qkv = add_gemv(ly.qkv, ly.qkv_sh, L == 0 ? X_EMBED_NORM : X_RMSNORM, EPI_QKV);
+        if (ly.v) {  // [q | k] rows, then the v rows of their own type right after them
+            qkv.rows = ly.qkv_sh.rows + ly.v_sh.rows;
+            qkv.pairs = ly.qkv_sh.pairs + ly.v_sh.pairs;
+            qkv.fmts = ly.qkv_sh.fmt | (ly.v_sh.fmt << 4) | (ly.qkv_sh.pairs << 8);
+        }
         qkv.hsrc = L == 0 ? I->embed : I->hA;
         qkv.hout = L == 0 ? I->hA : nullptr;
         if (tp && L > 0) tp_input(qkv, 2 * (L - 1) + 1);
@@ -834,7 +842,7 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
         for (const Q4MShape* sh : {&ly.qkv_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) max_cols = std::max(max_cols, sh->cols);
     const unsigned xs = step_xstage_bytes(max_cols, G, I->hd);
     // ring depth: STEP_NBUF slots per warp when they fit next to the staged inputs, else 3
-    int nbuf = STEP_NBUF;
+    int nbuf = I->wfmt == Q4M_MIX ? 3 : STEP_NBUF;
     size_t smem = step_smem_bytes(xs, 5 * I->L + 1, I->wfmt, nbuf);
     if (smem > 227 * 1024) {
         nbuf = 3;
@@ -1191,10 +1199,14 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             lfmt[L] = {f[0], f[2], f[3], f[4], f[6]};
         }
         if (!fmt_of("output.weight", &lm_fmt)) return fail(JINF_ERR_INVALID);
-        I->wfmt = lm_fmt;
+        I->step_formats = lm_fmt != Q4M_Q8_0;
         for (const auto& lf : lfmt)
-            for (const int f : lf) I->uniform = I->uniform && f == lm_fmt;
+            for (const int f : lf) {
+                I->uniform = I->uniform && f == lm_fmt;
+                I->step_formats = I->step_formats && f != Q4M_Q8_0;
+            }
         I->uniform = I->uniform && (lm_fmt == Q4M_Q4_0 || lm_fmt == Q4M_Q4_K);
+        I->wfmt = I->uniform ? lm_fmt : Q4M_MIX;
         if (I->uniform) I->wtype = lm_fmt == Q4M_Q4_K ? JINF_TYPE_Q4_K : JINF_TYPE_Q4_0;
         if (!I->uniform && opt.sparse_mode) {
             JINF_LOG("sparse FFN modes need every projection in one type, Q4_0 or Q4_K");
@@ -1514,9 +1526,14 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             return fail(JINF_ERR_OOM);
         cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * pairs);
     }
-    if (opt.persistent && !I->uniform)
-        JINF_LOG("weight types differ between matrices (or are not Q4_0 / Q4_K): one kernel per operation");
-    if (opt.persistent && I->uniform && (!I->sparse_mode || I->sparse_persistent)) {
+    // mixed models in the persistent step: a v of its own type must follow its [q | k] rows
+    // directly (one phase streams both) and start on a tile pair
+    bool step_ok = I->uniform || I->step_formats;
+    for (const auto& ly : I->layers)
+        if (ly.v && (ly.v != ly.qkv + ly.qkv_sh.bytes || ly.qkv_sh.rows % Q4M_PAIR_ROWS)) step_ok = false;
+    if (opt.persistent && !step_ok)
+        JINF_LOG("weight types not streamed by the persistent step (Q8_0 in a mixed model): one kernel per operation");
+    if (opt.persistent && step_ok && (!I->sparse_mode || I->sparse_persistent)) {
         // tensor parallel: the exchange areas first (every rank decides the same way)
         bool ok = tp == 1 || setup_exchange(I);
         if (!ok) {

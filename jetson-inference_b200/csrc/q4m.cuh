@@ -85,8 +85,14 @@ constexpr int Q4M_D_8 = 4096;            // byte offset of the scales in a Q8_0 
 // Weight formats of a Q4M matrix
 enum Q4MFormat { Q4M_Q4_0 = 0, Q4M_Q4_K = 1, Q4M_Q6_K = 2, Q4M_Q8_0 = 3 };
 constexpr int Q4M_NFMT = 4;
+// Not a matrix format: the persistent step's instance for models whose matrices mix Q4_0,
+// Q4_K and Q6_K, each phase with its own formats (its ring slots fit the largest unit).
+constexpr int Q4M_MIX = 4;
 __host__ __device__ constexpr inline int q4m_unit_bytes(int fmt) {
-    return fmt == Q4M_Q4_K ? Q4M_UNIT_K : fmt == Q4M_Q6_K ? Q4M_UNIT_6 : fmt == Q4M_Q8_0 ? Q4M_UNIT_8 : Q4M_UNIT;
+    return fmt == Q4M_Q4_K ? Q4M_UNIT_K
+         : fmt == Q4M_Q6_K || fmt == Q4M_MIX ? Q4M_UNIT_6
+         : fmt == Q4M_Q8_0 ? Q4M_UNIT_8
+                           : Q4M_UNIT;
 }
 // Columns of a matrix of format fmt come in whole blocks (32) or super-blocks (256).
 __host__ __device__ constexpr inline int q4m_col_align(int fmt) {

@@ -50,6 +50,8 @@ struct StepPhase {
     int xout;                // exchange point this phase writes (EPI_PARTIAL), -1: none
     // PH_GEMV
     int xm, epi;
+    int fmts;                // weight formats: pairs below fmts >> 8 are format fmts & 15, the
+                             // rest (fmts >> 4) & 15 (a QKV of [q|k] in one type, v in another)
     const uint8_t* w;        // Q4M matrix
     int rows, cols, pairs, groups;
     const float* x;          // X_PLAIN_F32: input (written earlier in the step)

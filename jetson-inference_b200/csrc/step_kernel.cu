@@ -37,6 +37,8 @@
 #include "q4m_device.cuh"
 #include "step.h"
 
+#include <type_traits>
+
 #include <algorithm>
 
 #include <math.h>
@@ -156,7 +158,16 @@ __device__ __noinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, DeviceSta
 struct PhaseInfo {
     const uint8_t* w;
     int pairs, groups, gran;
+    int fmts;  // StepPhase::fmts
 };
+
+// Byte offset of tile pair t in a phase's matrix (pairs below fmts >> 8 in format fmts & 15,
+// the rest in (fmts >> 4) & 15).
+__device__ __forceinline__ size_t pair_offset(int fmts, int groups, int t) {
+    const int ps = fmts >> 8;
+    const size_t ua = (size_t)groups * q4m_unit_bytes(fmts & 15);
+    return t <= ps ? (size_t)t * ua : (size_t)ps * ua + (size_t)(t - ps) * groups * q4m_unit_bytes((fmts >> 4) & 15);
+}
 
 // Tile pairs [t0, t1) of CTA `cta` (of C): balanced runs of `gran` pairs (T % gran == 0).
 __device__ __forceinline__ void cta_range(int cta, int C, int T, int gran, int& t0, int& t1) {
@@ -187,8 +198,19 @@ struct StreamPos {
     const uint8_t* w;
     int ph, c, c1;
 };
-__device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int from, int cta, int C, int warp) {
-    StreamPos r;
+// The mixed-format instance's position (Q4M_MIX): units below cs are format fa from w, the
+// rest fb from w2. Uniform instances keep the smaller StreamPos.
+struct StreamPosMix : StreamPos {
+    const uint8_t* w2;
+    int cs, fa, fb;
+};
+template <bool M>
+using StreamPosOf = typename std::conditional<M, StreamPosMix, StreamPos>::type;
+
+template <bool M>
+__device__ __noinline__ StreamPosOf<M> stream_seek(const PhaseInfo* pinfo, int n, int from, int cta, int C,
+                                                   int warp) {
+    StreamPosOf<M> r;
     for (int i = from; i < n; ++i) {
         const int G = pinfo[i].groups;
         if (!G) continue;
@@ -199,6 +221,13 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
             r.ph = i;
             r.c = c0;
             r.c1 = c1;
+            if constexpr (M) {
+                const int fm = pinfo[i].fmts;
+                r.cs = (fm >> 8) * G;
+                r.fa = fm & 15;
+                r.fb = (fm >> 4) & 15;
+                r.w2 = r.w + (size_t)r.cs * q4m_unit_bytes(r.fa);
+            }
             return r;
         }
     }
@@ -206,27 +235,34 @@ __device__ __noinline__ StreamPos stream_seek(const PhaseInfo* pinfo, int n, int
     r.ph = n;
     r.c = 0;
     r.c1 = 0;
+    if constexpr (M) {
+        r.w2 = nullptr;
+        r.cs = r.fa = r.fb = 0;
+    }
     return r;
 }
 
 // Bring the units that CTA `cta` owns in GEMV phase `pi` (one contiguous byte range: whole
 // tile pairs, all groups) into L2. Issued while the CTA would otherwise wait on a dependency,
 // so that HBM keeps streaming weights through attention, input staging and merges.
-__device__ __noinline__ void prefetch_cta_range(const PhaseInfo& pi, int cta, int C, int ub) {
+__device__ __noinline__ void prefetch_cta_range(const PhaseInfo& pi, int cta, int C, int ub, bool mixed) {
     if (!pi.groups) return;
     int t0, t1;
     cta_range(cta, C, pi.pairs, pi.gran, t0, t1);
     if (t0 >= t1) return;
-    const uint8_t* b = pi.w + (size_t)t0 * pi.groups * ub;
-    const uint32_t bytes = (uint32_t)(t1 - t0) * (uint32_t)pi.groups * (uint32_t)ub;  // multiple of 16
+    const size_t o0 = mixed ? pair_offset(pi.fmts, pi.groups, t0) : (size_t)t0 * pi.groups * ub;
+    const size_t o1 = mixed ? pair_offset(pi.fmts, pi.groups, t1) : (size_t)t1 * pi.groups * ub;
+    const uint8_t* b = pi.w + o0;
+    const uint32_t bytes = (uint32_t)(o1 - o0);  // multiple of 16
     for (uint32_t off = 0; off < bytes; off += (1u << 20))
         prefetch_l2(b + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
 }
 
 // The weight stream of one warp between calls: ring slot of the next unit to consume and
 // the copy position.
+template <bool M>
 struct WarpStream {
-    StreamPos sp;
+    StreamPosOf<M> sp;
     int slot;
 };
 
@@ -234,25 +270,52 @@ struct PieceSum {
     float acc[4];
 };
 
+// Copy the unit at the stream position into ring slot `slot` (slots of SB bytes). In the
+// mixed instance the unit's format and address follow the phase's split (StreamPos).
+template <int FMT>
+__device__ __forceinline__ void copy_stream_unit(uint32_t slot, const StreamPosOf<FMT == Q4M_MIX>& sp, int lane) {
+    if constexpr (FMT == Q4M_MIX) {
+        if (sp.c < sp.cs) {
+            const uint8_t* u = sp.w + (size_t)sp.c * q4m_unit_bytes(sp.fa);
+            if (sp.fa == Q4M_Q6_K) copy_unit_6_async(slot, u, lane);
+            else if (sp.fa == Q4M_Q4_K) copy_unit_k_async(slot, u, lane);
+            else copy_unit_async(slot, u, lane);
+        } else {
+            const uint8_t* u = sp.w2 + (size_t)(sp.c - sp.cs) * q4m_unit_bytes(sp.fb);
+            if (sp.fb == Q4M_Q6_K) copy_unit_6_async(slot, u, lane);
+            else if (sp.fb == Q4M_Q4_K) copy_unit_k_async(slot, u, lane);
+            else copy_unit_async(slot, u, lane);
+        }
+    } else {
+        copy_unit_fmt<FMT>(slot, sp.w + (size_t)sp.c * q4m_unit_bytes(FMT), lane);
+    }
+}
+
 // Consume groups [gb, ge) of one tile pair from the ring (tensor-core decode, q4m_device.cuh),
 // refilling it as it goes. Out of line so that the hot loop gets a register allocation of
-// its own, independent of the rest of the step kernel.
-template <int FMT, int NBUF>
-__device__ __noinline__ PieceSum stream_piece(WarpStream& ws, uint32_t ring, const PhaseInfo* pinfo, int n_phases,
+// its own, independent of the rest of the step kernel. CF is the pair's weight format (FMT
+// itself unless FMT is Q4M_MIX, whose ring may hold units of several formats: there the warp
+// synchronises after each unit, so that no lane's copy into a slot overtakes another lane's
+// reads of the unit it held).
+template <int FMT, int NBUF, int CF>
+__device__ __noinline__ PieceSum stream_piece(WarpStream<FMT == Q4M_MIX>& ws, uint32_t ring, const PhaseInfo* pinfo,
+                                              int n_phases,
                                               int C, const XRecS xr, int gb, int ge) {
+    constexpr int SB = q4m_unit_bytes(FMT);  // ring slot bytes
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    StreamPos sp = ws.sp;
+    StreamPosOf<FMT == Q4M_MIX> sp = ws.sp;
     int slot = ws.slot;
     PieceSum r{{0.f, 0.f, 0.f, 0.f}};
     for (int g = gb; g < ge; ++g) {
         const int is = slot == 0 ? NBUF - 1 : slot - 1;
         if (sp.c < sp.c1) {
-            copy_unit_fmt<FMT>(ring + is * q4m_unit_bytes(FMT), sp.w + (size_t)sp.c * q4m_unit_bytes(FMT), lane);
-            if (++sp.c == sp.c1) sp = stream_seek(pinfo, n_phases, sp.ph + 1, blockIdx.x, C, warp);
+            copy_stream_unit<FMT>(ring + is * SB, sp, lane);
+            if (++sp.c == sp.c1) sp = stream_seek<FMT == Q4M_MIX>(pinfo, n_phases, sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
         asm volatile("cp.async.wait_group %0;" ::"n"(NBUF - 1) : "memory");
-        unit_mma_fmt<FMT>(ring + slot * q4m_unit_bytes(FMT), xr, g, lane, r.acc);
+        unit_mma_fmt<CF>(ring + slot * SB, xr, g, lane, r.acc);
+        if constexpr (FMT == Q4M_MIX) __syncwarp();
         slot = slot + 1 == NBUF ? 0 : slot + 1;
     }
     ws.sp = sp;
@@ -601,7 +664,8 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
 
 template <int FMT, int NBUF, bool TP>
 __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
-    constexpr int UB = FMT == Q4M_Q4_K ? Q4M_UNIT_K : Q4M_UNIT;  // weight unit bytes
+    constexpr int UB = q4m_unit_bytes(FMT);  // ring slot bytes (the largest unit of a mixed model)
+    constexpr bool MIXED = FMT == Q4M_MIX;
     extern __shared__ __align__(16) uint8_t smem[];
     // shared memory: [xstage | misc 256 B | flags, keys, piece table 512 B | partial rows 4 KB |
     //                 outputs to convert 4 KB | phase descriptor 2 x 256 B | phase infos | rings]
@@ -634,6 +698,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         pi.pairs = P.phases[i].pairs;
         pi.gran = P.phases[i].gran;
         pi.groups = P.phases[i].kind == PH_GEMV ? P.phases[i].groups : 0;
+        pi.fmts = P.phases[i].fmts;
         pinfo[i] = pi;
     }
     if (tid == 0) {
@@ -645,13 +710,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 
     // ---------------- weight stream: this warp's unit ranges of all GEMV phases, copied in
     // consumption order into the ring (NBUF - 1 units ahead of the arithmetic)
-    WarpStream ws;
-    ws.sp = stream_seek(pinfo, P.n_phases, 0, blockIdx.x, C, warp);
+    WarpStream<MIXED> ws;
+    ws.sp = stream_seek<MIXED>(pinfo, P.n_phases, 0, blockIdx.x, C, warp);
     ws.slot = 0;
     for (int i = 0; i < NBUF - 1; ++i) {
         if (ws.sp.c < ws.sp.c1) {
-            copy_unit_fmt<FMT>(ring + i * UB, ws.sp.w + (size_t)ws.sp.c * UB, lane);
-            if (++ws.sp.c == ws.sp.c1) ws.sp = stream_seek(pinfo, P.n_phases, ws.sp.ph + 1, blockIdx.x, C, warp);
+            copy_stream_unit<FMT>(ring + i * UB, ws.sp, lane);
+            if (++ws.sp.c == ws.sp.c1)
+                ws.sp = stream_seek<MIXED>(pinfo, P.n_phases, ws.sp.ph + 1, blockIdx.x, C, warp);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");  // possibly empty: uniform group counts
     }
@@ -675,7 +741,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             if (tid == 32 * 9) {  // L2 prefetch of later weights while warp 0 polls
                 for (int k = 0; k < 2; ++k) {
                     const int j = P.phases[ph].pf[k];
-                    if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C, UB);
+                    if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C, UB, MIXED);
                 }
             }
         }
@@ -900,7 +966,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         int pair = c / G, gb = c - pair * G;  // walked incrementally: no division per piece
         for (; c < c1; ++pair, gb = 0) {
             const int ge = c1 - c < G - gb ? gb + (c1 - c) : G;
-            PieceSum ps = stream_piece<FMT, NBUF>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
+            PieceSum ps;
+            if constexpr (MIXED) {
+                const int f = pair < (d.fmts >> 8) ? (d.fmts & 15) : ((d.fmts >> 4) & 15);
+                ps = f == Q4M_Q6_K   ? stream_piece<FMT, NBUF, Q4M_Q6_K>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge)
+                     : f == Q4M_Q4_K ? stream_piece<FMT, NBUF, Q4M_Q4_K>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge)
+                                     : stream_piece<FMT, NBUF, Q4M_Q4_0>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
+            } else {
+                ps = stream_piece<FMT, NBUF, FMT>(ws, ring, pinfo, P.n_phases, C, xr, gb, ge);
+            }
             c += ge - gb;
             if (first_piece && lane == 0) {
                 ftile[warp] = pair;
@@ -1056,9 +1130,11 @@ size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt, int nbu
 
 // The kernel instances: weight format x ring depth (STEP_NBUF, or 3 when a model's staged
 // inputs leave no room for STEP_NBUF slots) x tensor parallel (the single-GPU instance
-// carries none of the exchange code).
+// carries none of the exchange code). Mixed-format models (Q4M_MIX) take 3 slots of the
+// largest unit.
 typedef void (*StepKernel)(const StepParams);
 static StepKernel step_kernel_for(int fmt, int nbuf, bool tp) {
+    if (fmt == Q4M_MIX) return tp ? k_step<Q4M_MIX, 3, true> : k_step<Q4M_MIX, 3, false>;
     if (tp) {
         if (fmt == Q4M_Q4_K) return nbuf == 3 ? k_step<Q4M_Q4_K, 3, true> : k_step<Q4M_Q4_K, STEP_NBUF, true>;
         return nbuf == 3 ? k_step<Q4M_Q4_0, 3, true> : k_step<Q4M_Q4_0, STEP_NBUF, true>;
@@ -1068,11 +1144,12 @@ static StepKernel step_kernel_for(int fmt, int nbuf, bool tp) {
 }
 
 static cudaError_t step_configure(size_t smem, int fmt, int nbuf, bool tp) {
-    static size_t configured[64][8] = {{0}};
+    static size_t configured[64][12] = {{0}};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
-    const int slot = (fmt == Q4M_Q4_K ? 2 : 0) + (nbuf == 3 ? 1 : 0) + (tp ? 4 : 0);
+    const int slot = (fmt == Q4M_MIX ? 8 : fmt == Q4M_Q4_K ? 2 : 0) + (nbuf == 3 ? 1 : 0) + (tp ? 4 : 0) -
+                     (fmt == Q4M_MIX && tp ? 2 : 0);  // mixed: 8 + nbuf3 (+ 2 for tp)
     if (smem <= configured[dev][slot]) return cudaSuccess;
     const cudaError_t e =
         cudaFuncSetAttribute(step_kernel_for(fmt, nbuf, tp), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
