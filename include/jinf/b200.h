@@ -31,6 +31,9 @@ uint64_t jinf_b200_q4m_bytes(int rows, int cols);
 // cuda/matmul_kernels.cu:47-185).
 uint64_t jinf_b200_q4m_bytes_qt(int rows, int cols, int qtype);
 jinf_status jinf_b200_q4m_pack_qt(const void* aos, int qtype, void* q4m, int rows, int cols, cudaStream_t stream);
+// The same repack on the host (host buffers, no GPU needed), bit-identical to the device's:
+// what a conversion tool uses to write pre-packed matrices (jinf_prepare_model_b200).
+jinf_status jinf_b200_q4m_pack_host(const void* aos, int qtype, void* q4m, int rows, int cols);
 jinf_status jinf_b200_gemv_q4m_qt(const void* q4m, int qtype, const void* x, int x_type, float* y, int rows,
                                   int cols, void* workspace, int kw, cudaStream_t stream);
 

@@ -14,6 +14,15 @@
 #define JINF_NVMW_MAGIC           0x574D564Eu  // "NVMW"
 #define JINF_NVMW_VERSION         1
 #define JINF_NVMW_VERSION_BUNDLED 2
+// New (no counterpart in the reference): the B200 layout, projections pre-packed into the
+// engine's Q4M images (jinf_prepare_model_b200); such a tensor's type is
+// JINF_NVMW_TYPE_Q4M + its Q4M format (0 Q4_0, 1 Q4_K, 2 Q6_K, 3 Q8_0).
+#define JINF_NVMW_VERSION_B200    3
+#define JINF_NVMW_TYPE_Q4M        0x40
+static inline int q4m_format_of_qtype(int qtype) {
+    return qtype == 2 ? 0 : qtype == 12 ? 1 : qtype == 14 ? 2 : qtype == 8 ? 3 : -1;
+}
+static inline int qtype_of_q4m_format(int fmt) { return fmt == 0 ? 2 : fmt == 1 ? 12 : fmt == 2 ? 14 : fmt == 3 ? 8 : -1; }
 
 // Tensor entry: natural (unpacked) alignment, 200 bytes.
 typedef struct jinf_nvmw_tensor_entry {
@@ -112,6 +121,11 @@ jinf_status jinf_nvmw_writer_finalize(jinf_nvmw_writer* w);
 // padded, and with `bundled` the neuron bundles (gate row, up row, fp32 down column) and
 // their index (version 2). New: the reference has it only as a command-line tool.
 jinf_status jinf_prepare_model(const char* gguf_path, const char* nvmw_path, size_t gpu_budget_mb, int bundled);
+// GGUF -> B200-layout NVMW (version 3) for one GPU and the dense FFN: every projection stored
+// as the engine's fused Q4M image (qkv, o, gate|up interleaved, down, output head), so the
+// engine copies it into HBM without repacking; the embedding and norms as in the GGUF. New:
+// no counterpart in the reference.
+jinf_status jinf_prepare_model_b200(const char* gguf_path, const char* nvmw_path);
 jinf_status jinf_nvmw_writer_write_bundle_section(jinf_nvmw_writer* w,
                                                   const jinf_nvmw_bundle_header* bh,
                                                   const jinf_nvmw_bundle_layer_desc* layer_descs,

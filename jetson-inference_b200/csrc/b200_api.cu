@@ -37,6 +37,14 @@ extern "C" jinf_status jinf_b200_q4m_pack(const void* aos, void* q4m, int rows, 
 
 static int q4m_fmt_of(int qtype) { return q4m_fmt_of_qtype(qtype); }
 
+extern "C" jinf_status jinf_b200_q4m_pack_host(const void* aos, int qtype, void* q4m, int rows, int cols) {
+    Q4MShape sh;
+    const int fmt = q4m_fmt_of(qtype);
+    if (!aos || !q4m || fmt < 0 || !q4m_shape(rows, cols, &sh, fmt)) return JINF_ERR_INVALID;
+    q4m_repack_host(aos, q4m, sh);
+    return JINF_OK;
+}
+
 extern "C" uint64_t jinf_b200_q4m_bytes_qt(int rows, int cols, int qtype) {
     Q4MShape sh;
     const int fmt = q4m_fmt_of(qtype);

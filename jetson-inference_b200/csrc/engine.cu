@@ -78,6 +78,10 @@ struct ModelSource {
     virtual bool device_quant(const char*, int64_t, int64_t, int64_t, int64_t, uint8_t*, int64_t, int64_t, int64_t,
                               cudaStream_t, jinf_status*) const { return false; }
     virtual bool device_f32(const char*, float*, cudaStream_t, jinf_status*) const { return false; }
+    // B200-layout files (NVMW version 3): the projections are stored as the engine's Q4M
+    // images; read_packed copies one into device memory (exactly `bytes` long).
+    virtual bool prepacked() const { return false; }
+    virtual jinf_status read_packed(const char*, uint8_t*, uint64_t) const { return JINF_ERR_INVALID; }
     jinf_model_hparams hp{};
     int primary_type = JINF_TYPE_Q4_0;
 };
@@ -133,13 +137,64 @@ struct NvmwSource : ModelSource {
         if (fd >= 0) close(fd);
         if (r) jinf_nvmw_close(r);
     }
+    bool b200 = false;  // version 3: pre-packed projections
+    bool prepacked() const override { return b200; }
+    // In a B200-layout file a projection's type is that of the Q4M image that holds it.
+    const jinf_nvmw_tensor_entry* packed_entry_for(const char* name) const {
+        int l = -1;
+        char part[64] = {0};
+        std::string img;
+        if (sscanf(name, "blk.%d.%63[a-z_].weight", &l, part) == 2) {
+            const std::string p(part);
+            const std::string pre = "blk." + std::to_string(l) + ".";
+            if (p == "attn_q" || p == "attn_k") img = pre + "qkv.q4m";
+            else if (p == "attn_v") img = jinf_nvmw_find_tensor(r, (pre + "v.q4m").c_str()) ? pre + "v.q4m" : pre + "qkv.q4m";
+            else if (p == "attn_output") img = pre + "o.q4m";
+            else if (p == "ffn_gate" || p == "ffn_up") img = pre + "gu.q4m";
+            else if (p == "ffn_down") img = pre + "down.q4m";
+        } else if (!strcmp(name, "output.weight")) {
+            img = "output.q4m";
+        }
+        return img.empty() ? nullptr : jinf_nvmw_find_tensor(r, img.c_str());
+    }
     bool meta(const char* name, TensorMeta* t) const override {
         const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, name);
+        if (!te && b200) {
+            const jinf_nvmw_tensor_entry* pe = packed_entry_for(name);
+            if (!pe || (int)pe->type < JINF_NVMW_TYPE_Q4M) return false;
+            t->type = qtype_of_q4m_format((int)pe->type - JINF_NVMW_TYPE_Q4M);
+            t->n_dims = 2;
+            t->shape[0] = pe->shape[0];
+            t->shape[1] = pe->shape[1];
+            t->shape[2] = t->shape[3] = 1;
+            return true;
+        }
         if (!te) return false;
         t->type = te->type;
         t->n_dims = (int)te->n_dims;
         for (int i = 0; i < 4; ++i) t->shape[i] = i < (int)te->n_dims ? te->shape[i] : 1;
         return true;
+    }
+    jinf_status read_packed(const char* name, uint8_t* dst_dev, uint64_t bytes) const override {
+        const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, name);
+        if (!te || (int)te->type < JINF_NVMW_TYPE_Q4M || te->n_bytes != bytes) {
+            JINF_LOG("tensor %s: no pre-packed image of %llu bytes in this file", name, (unsigned long long)bytes);
+            return JINF_ERR_INVALID;
+        }
+        std::vector<uint8_t> buf((size_t)std::min<uint64_t>(bytes, 64ull << 20));
+        uint64_t off = jinf_nvmw_tensor_file_offset(r, te), done = 0;
+        while (done < bytes) {
+            const size_t n = (size_t)std::min<uint64_t>(bytes - done, buf.size());
+            size_t got = 0;
+            while (got < n) {
+                const ssize_t k = pread(fd, buf.data() + got, n - got, (off_t)(off + done + got));
+                if (k <= 0) return JINF_ERR_IO;
+                got += (size_t)k;
+            }
+            JINF_CUDA_CHECK(cudaMemcpy(dst_dev + done, buf.data(), n, cudaMemcpyHostToDevice));
+            done += n;
+        }
+        return JINF_OK;
     }
     jinf_status read_rows(const char* name, int64_t row0, int64_t n, void* dst) const override {
         const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, name);
@@ -180,6 +235,7 @@ jinf_status open_nvmw_source(const char* path, std::unique_ptr<ModelSource>* out
     s->hp.rope_freq_base = h->rope_freq_base;
     s->hp.rms_norm_eps = h->rms_norm_eps;
     s->primary_type = h->primary_type;
+    s->b200 = h->version == JINF_NVMW_VERSION_B200;
     *out = std::move(s);
     return JINF_OK;
 }
@@ -1208,6 +1264,10 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         I->uniform = I->uniform && (lm_fmt == Q4M_Q4_0 || lm_fmt == Q4M_Q4_K);
         I->wfmt = I->uniform ? lm_fmt : Q4M_MIX;
         if (I->uniform) I->wtype = lm_fmt == Q4M_Q4_K ? JINF_TYPE_Q4_K : JINF_TYPE_Q4_0;
+        if (src.prepacked() && (tp > 1 || opt.sparse_mode)) {
+            JINF_LOG("a B200-layout model file is prepared for one GPU and the dense FFN");
+            return fail(JINF_ERR_INVALID);
+        }
         if (!I->uniform && opt.sparse_mode) {
             JINF_LOG("sparse FFN modes need every projection in one type, Q4_0 or Q4_K");
             return fail(JINF_ERR_INVALID);
@@ -1425,6 +1485,17 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             snprintf(nm, sizeof nm, "blk.%d.ffn_norm.weight", L);
             s = ld.read_f32(nm, ly.ffn_norm, d);
             if (s != JINF_OK) break;
+            if (src.prepacked()) {  // the file holds this layer's matrices as Q4M images
+                const std::pair<const char*, std::pair<uint8_t*, uint64_t>> imgs[5] = {
+                    {"qkv", {ly.qkv, ly.qkv_sh.bytes}}, {"v", {ly.v, ly.v ? ly.v_sh.bytes : 0}},
+                    {"o", {ly.o, ly.o_sh.bytes}}, {"gu", {ly.gu, ly.gu_sh.bytes}}, {"down", {ly.down, ly.down_sh.bytes}}};
+                for (const auto& im : imgs) {
+                    if (!im.second.first || s != JINF_OK) continue;
+                    snprintf(nm, sizeof nm, "blk.%d.%s.q4m", L, im.first);
+                    s = src.read_packed(nm, im.second.first, im.second.second);
+                }
+                continue;
+            }
             // QKV: this rank's q heads, then its k heads, then its v heads
             const int64_t nq = (int64_t)I->Hl * hd, nk = (int64_t)I->Hkvl * hd;
             const int64_t rb_qk = (int64_t)aos_row_bytes(ly.qkv_sh.fmt, d);
@@ -1490,9 +1561,13 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         }
         I->out_norm = I->norms + (size_t)(2 * I->L) * d;
         if (s == JINF_OK) s = ld.read_f32("output_norm.weight", I->out_norm, d);
-        if (s == JINF_OK)
-            s = ld.stage_shard("output.weight", I->Vl, d, (int64_t)aos_row_bytes(I->lm_sh.fmt, d), 0, 1);
-        if (s == JINF_OK) s = ld.pack(I->lm, I->lm_sh);
+        if (s == JINF_OK && src.prepacked()) {
+            s = src.read_packed("output.q4m", I->lm, I->lm_sh.bytes);
+        } else {
+            if (s == JINF_OK)
+                s = ld.stage_shard("output.weight", I->Vl, d, (int64_t)aos_row_bytes(I->lm_sh.fmt, d), 0, 1);
+            if (s == JINF_OK) s = ld.pack(I->lm, I->lm_sh);
+        }
         if (s == JINF_OK) s = ld.read_f32("token_embd.weight", I->embed, (int64_t)I->V * d);
         if (s != JINF_OK) return fail(s);
     }

@@ -94,5 +94,7 @@ inline int q4m_fmt_of_qtype(int qtype) {
 }
 // AoS Q4_0, Q4_K, Q6_K or Q8_0 (sh.fmt) [rows][cols] (device) -> Q4M (device, sh.bytes).
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s);
+// The same on the host (host pointers; every byte of the image is written).
+void q4m_repack_host(const void* aos, void* dst, const Q4MShape& sh);
 
 }  // namespace jinf

@@ -225,13 +225,8 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
 // One thread per (pair, group, lane): its 16 nibble words and 2 scale words (q4m.cuh),
 // gathered from the AoS blocks ([rows][nb] blocks of 18 bytes). Rows past `rows` and
 // blocks past nb read as zero.
-__global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
-                             int pairs, int nb) {
-    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (int64_t)pairs * groups * 32) return;
-    const int lane = (int)(gid & 31);
-    const int64_t pg = gid >> 5;
-    const int p = (int)(pg / groups), G = (int)(pg % groups);
+__host__ __device__ inline void pack_lane_q40(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows,
+                                      int groups, int nb, int p, int G, int lane) {
     const int gr = lane >> 2, c = lane & 3;
     auto block = [&](int r, int j) -> const uint8_t* {  // pair row r, block j of the group
         const int row = p * Q4M_PAIR_ROWS + r;
@@ -263,18 +258,22 @@ __global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restric
         *reinterpret_cast<uint32_t*>(unit + Q4M_SCALES + 128 * t + 4 * lane) = d0 | (d1 << 16);
     }
 }
-
-// One thread per (pair, group, lane) of a Q4_K matrix (AoS super-blocks of 144 bytes,
-// [rows][nsb]): the unit's nibble words (group G = sub-blocks 4 (G % 2) + j of super-block
-// G / 2), the lane's sc | m words, and lanes 0..15 / 16..31 the d, dmin of tile A / B row
-// lane % 16 (q4m.cuh). The 6-bit sc and m unpacking follows reference src/quant.cpp:71-77.
-__global__ void k_repack_q4mk(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
-                              int pairs, int nsb) {
+__global__ void k_repack_q4m(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
+                             int pairs, int nb) {
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)pairs * groups * 32) return;
     const int lane = (int)(gid & 31);
     const int64_t pg = gid >> 5;
     const int p = (int)(pg / groups), G = (int)(pg % groups);
+    pack_lane_q40(aos, dst, rows, groups, nb, p, G, lane);
+}
+
+// One thread per (pair, group, lane) of a Q4_K matrix (AoS super-blocks of 144 bytes,
+// [rows][nsb]): the unit's nibble words (group G = sub-blocks 4 (G % 2) + j of super-block
+// G / 2), the lane's sc | m words, and lanes 0..15 / 16..31 the d, dmin of tile A / B row
+// lane % 16 (q4m.cuh). The 6-bit sc and m unpacking follows reference src/quant.cpp:71-77.
+__host__ __device__ inline void pack_lane_q4k(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows,
+                                      int groups, int nsb, int p, int G, int lane) {
     const int gr = lane >> 2, c = lane & 3, sbk = G >> 1, half = G & 1;
     auto block = [&](int r) -> const uint8_t* {  // super-block sbk of pair row r
         const int row = p * Q4M_PAIR_ROWS + r;
@@ -321,6 +320,15 @@ __global__ void k_repack_q4mk(const uint8_t* __restrict__ aos, uint8_t* __restri
                             : 0u;
     *reinterpret_cast<uint32_t*>(unit + Q4M_DMIN_K + 4 * lane) = dd;
 }
+__global__ void k_repack_q4mk(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
+                              int pairs, int nsb) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)pairs * groups * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t pg = gid >> 5;
+    const int p = (int)(pg / groups), G = (int)(pg % groups);
+    pack_lane_q4k(aos, dst, rows, groups, nsb, p, G, lane);
+}
 
 // One thread per (pair, group, lane) of a Q6_K matrix (AoS super-blocks of 210 bytes,
 // [rows][nsb]): the lane's nibble words and crumb words, its two scale words, and lanes with
@@ -328,13 +336,8 @@ __global__ void k_repack_q4mk(const uint8_t* __restrict__ aos, uint8_t* __restri
 // low4 | high2 << 4 with low4 from ql[e / 2] (low nibble for even e) and high2 from bits
 // 2 (e % 4) of qh[e / 4] (reference cuda/dequant_kernels.cu:82-110). Rows past `rows` pack
 // as q = 32 with d = 0 (weight 0).
-__global__ void k_repack_q6k(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
-                             int pairs, int nsb) {
-    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (int64_t)pairs * groups * 32) return;
-    const int lane = (int)(gid & 31);
-    const int64_t pg = gid >> 5;
-    const int p = (int)(pg / groups), G = (int)(pg % groups);
+__host__ __device__ inline void pack_lane_q6k(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows,
+                                      int groups, int nsb, int p, int G, int lane) {
     const int gr = lane >> 2, c = lane & 3, sbk = G >> 1, half = G & 1;
     auto block = [&](int r) -> const uint8_t* {  // super-block sbk of pair row r
         const int row = p * Q4M_PAIR_ROWS + r;
@@ -401,17 +404,21 @@ __global__ void k_repack_q6k(const uint8_t* __restrict__ aos, uint8_t* __restric
         o[1] = d4[2] | ((uint32_t)d4[3] << 16);
     }
 }
-
-// One thread per (pair, group, lane) of a Q8_0 matrix (AoS blocks of 34 bytes: fp16 d, 32
-// int8 q; [rows][nb], reference include/jinf/quant.h:50-56): the lane's eight weight words
-// and its scale record. Rows past `rows` and blocks past nb pack as zeros.
-__global__ void k_repack_q80(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
-                             int pairs, int nb) {
+__global__ void k_repack_q6k(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
+                             int pairs, int nsb) {
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)pairs * groups * 32) return;
     const int lane = (int)(gid & 31);
     const int64_t pg = gid >> 5;
     const int p = (int)(pg / groups), G = (int)(pg % groups);
+    pack_lane_q6k(aos, dst, rows, groups, nsb, p, G, lane);
+}
+
+// One thread per (pair, group, lane) of a Q8_0 matrix (AoS blocks of 34 bytes: fp16 d, 32
+// int8 q; [rows][nb], reference include/jinf/quant.h:50-56): the lane's eight weight words
+// and its scale record. Rows past `rows` and blocks past nb pack as zeros.
+__host__ __device__ inline void pack_lane_q80(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows,
+                                      int groups, int nb, int p, int G, int lane) {
     const int gr = lane >> 2, c = lane & 3;
     auto block = [&](int r, int j) -> const uint8_t* {
         const int row = p * Q4M_PAIR_ROWS + r;
@@ -435,6 +442,15 @@ __global__ void k_repack_q80(const uint8_t* __restrict__ aos, uint8_t* __restric
     uint32_t* o = reinterpret_cast<uint32_t*>(unit + Q4M_D_8 + 8 * lane);
     o[0] = d4[0] | ((uint32_t)d4[1] << 16);
     o[1] = d4[2] | ((uint32_t)d4[3] << 16);
+}
+__global__ void k_repack_q80(const uint8_t* __restrict__ aos, uint8_t* __restrict__ dst, int rows, int groups,
+                             int pairs, int nb) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)pairs * groups * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t pg = gid >> 5;
+    const int p = (int)(pg / groups), G = (int)(pg % groups);
+    pack_lane_q80(aos, dst, rows, groups, nb, p, G, lane);
 }
 
 // ---------------------------------------------------------------- host side
@@ -565,6 +581,24 @@ cudaError_t gemvm_launch(const GemvParams& p, int xm, int epi, int grid, cudaStr
     if (p.cols > gemvm_max_cols(p.fmt)) return cudaErrorInvalidValue;
     JINF_GEMVM_DISPATCH(p.fmt, launch_m, p, grid, s, pdl)
     return cudaErrorInvalidValue;
+}
+
+// The same repack on the host (the lane functions the kernels run), for tools that write
+// pre-packed matrices without a GPU.
+void q4m_repack_host(const void* aos, void* dst, const Q4MShape& sh) {
+    const int64_t n = (int64_t)sh.pairs * sh.groups;
+    const uint8_t* a = (const uint8_t*)aos;
+    uint8_t* d = (uint8_t*)dst;
+#pragma omp parallel for schedule(static)
+    for (int64_t pg = 0; pg < n; ++pg) {
+        const int p = (int)(pg / sh.groups), G = (int)(pg % sh.groups);
+        for (int lane = 0; lane < 32; ++lane) {
+            if (sh.fmt == Q4M_Q6_K) pack_lane_q6k(a, d, sh.rows, sh.groups, sh.cols / 256, p, G, lane);
+            else if (sh.fmt == Q4M_Q8_0) pack_lane_q80(a, d, sh.rows, sh.groups, sh.cols / 32, p, G, lane);
+            else if (sh.fmt == Q4M_Q4_K) pack_lane_q4k(a, d, sh.rows, sh.groups, sh.cols / 256, p, G, lane);
+            else pack_lane_q40(a, d, sh.rows, sh.groups, sh.cols / 32, p, G, lane);
+        }
+    }
 }
 
 cudaError_t q4m_repack(const void* aos, void* dst, const Q4MShape& sh, cudaStream_t s) {

@@ -137,6 +137,7 @@ SIGNATURES = {
     "jinf_quantize_q4_0": (None, [vp, vp, i64]),
     "jinf_quantize_q4_K": (None, [vp, vp, i64]),
     "jinf_quantize_q8_0": (None, [vp, vp, i64]),
+    "jinf_b200_q4m_pack_host": (i32, [vp, i32, vp, i32, i32]),
     "jinf_quantize_q6_K": (None, [vp, vp, i64]),
     # kernels.h
     "jinf_cuda_dequant_matvec": (None, [vp, vp, vp, i32, i32, i32, vp]),
@@ -192,6 +193,7 @@ SIGNATURES = {
     "jinf_nvmw_writer_finalize": (i32, [vp]),
     "jinf_nvmw_writer_write_bundle_section": (i32, [vp, vp, vp, i32]),
     "jinf_prepare_model": (i32, [C.c_char_p, C.c_char_p, sz, i32]),
+    "jinf_prepare_model_b200": (i32, [C.c_char_p, C.c_char_p]),
     "jinf_nvmw_open": (i32, [C.POINTER(vp), C.c_char_p]),
     "jinf_nvmw_close": (None, [vp]),
     "jinf_nvmw_get_header": (C.POINTER(NvmwHeader), [vp]),

@@ -77,3 +77,52 @@ def test_prepared_file_reads_back(tiny_gguf, tmp_path):
                 assert f.read(len(want)) == want
     finally:
         lib.jinf_nvmw_close(r)
+
+
+def test_prepare_b200_layout_holds_engine_images(tmp_path):
+    """jinf_prepare_model_b200 (new, no reference counterpart): a version-3 file whose
+    projections are the engine's fused Q4M images. Checked against the numpy restatement of
+    the layout: gate|up interleaved by neuron, and a v of its own type (Q6_K in the even
+    layers of a Q4_K_M-like model) kept apart from [q | k]."""
+    import numpy as np
+    import jinf
+    import q4m_ref
+    from jinf import _lib as L
+    shape = jinf.LlamaShape(2, 512, 8, 2, 1536, 1024, 10000.0, 1e-5)
+    syn = jinf.SynthModel(shape, seed=5, weight_type=L.Q4_K, mix_type=L.Q6_K)
+    gguf = str(tmp_path / "m.gguf")
+    out = str(tmp_path / "m.nvmw")
+    syn.write_gguf(gguf)
+    assert L.lib.jinf_prepare_model_b200(gguf.encode(), out.encode()) == 0
+    r = C.c_void_p()
+    assert L.lib.jinf_nvmw_open(C.byref(r), out.encode()) == 0
+    try:
+        h = L.lib.jinf_nvmw_get_header(r).contents
+        assert h.version == 3
+        raw = np.fromfile(out, dtype=np.uint8)
+
+        def image(name):
+            e = L.lib.jinf_nvmw_find_tensor(r, name.encode())
+            assert e, name
+            e = e.contents
+            o = h.hot_offset + e.offset
+            return e.type, (e.shape[1], e.shape[0]), raw[o:o + e.n_bytes]
+
+        names = {L.lib.jinf_nvmw_get_tensor_entries(r, C.byref(C.c_int()))[i].name.decode()
+                 for i in range(h.n_tensors)}
+        assert "blk.0.v.q4m" in names and "blk.1.v.q4m" not in names   # v in Q6_K only in even layers
+        t, (rows, cols), img = image("blk.0.v.q4m")
+        assert t == 0x40 + 2 and (rows, cols) == (128, 512)
+        assert np.array_equal(img, q4m_ref.pack_q6k(syn.read_rows("blk.0.attn_v.weight"), rows, cols))
+        t, (rows, cols), img = image("blk.1.gu.q4m")
+        assert t == 0x40 + 1 and (rows, cols) == (2 * 1536, 512)
+        g, u = syn.read_rows("blk.1.ffn_gate.weight"), syn.read_rows("blk.1.ffn_up.weight")
+        inter = np.empty((2 * g.shape[0], g.shape[1]), dtype=np.uint8)
+        inter[0::2], inter[1::2] = g, u
+        assert np.array_equal(img, q4m_ref.pack_q4k(inter, rows, cols))
+        t, (rows, cols), img = image("output.q4m")
+        assert t == 0x40 + 2 and (rows, cols) == (1024, 512)
+        t, _, _ = image("blk.1.qkv.q4m")
+        assert t == 0x40 + 1
+    finally:
+        L.lib.jinf_nvmw_close(r)

@@ -172,3 +172,24 @@ def test_synth_mixed_types():
             assert t == L.Q6_K, name
         else:
             assert t == L.Q4_K, name
+
+
+@pytest.mark.parametrize("qt,rows,cols", [(2, 37, 384), (2, 100, 1408), (12, 37, 512), (14, 100, 768), (8, 40, 96),
+                                          (8, 64, 1024)])
+def test_host_pack_matches_layout(qt, rows, cols):
+    """jinf_b200_q4m_pack_host (the device repack's lane functions run on the host) writes the
+    documented layout, byte for byte."""
+    import jinf
+    if qt == 2:
+        w, ref = q4_0_rows(rows, cols, seed=rows), q4m_ref.pack
+    elif qt == 12:
+        w, ref = q4_k_rows(rows, cols, seed=rows), q4m_ref.pack_q4k
+    elif qt == 14:
+        w, ref = q4m_ref.random_q6k_rows(rows, cols, seed=rows), q4m_ref.pack_q6k
+    else:
+        w, ref = q4m_ref.random_q80_rows(rows, cols, seed=rows), q4m_ref.pack_q80
+    w = np.ascontiguousarray(w)
+    out = np.full(jinf.lib.jinf_b200_q4m_bytes_qt(rows, cols, qt), 0xAB, dtype=np.uint8)
+    assert jinf.lib.jinf_b200_q4m_pack_host(w.ctypes.data_as(C.c_void_p), qt, out.ctypes.data_as(C.c_void_p),
+                                            rows, cols) == 0
+    assert np.array_equal(out, ref(w, rows, cols))
