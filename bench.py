@@ -15,7 +15,10 @@ reference src/engine.cpp:684-804), after a 512-token prompt: positions 512+W .. 
          KV rows read per token, timed by the same CUDA events as `value`); under tensor
          parallelism the costliest per-operation GEMV timed alone.
   cpu_baseline  the CPU oracle (restated reference math, reference dequant conventions)
-         on the host cores, a bounded sample of the same decode, rank 0 at N=1 only.
+         on the host cores timing whole decode tokens (every layer and the LM head), a
+         bounded sample of the same decode, rank 0 at N=1 only; --impl reference runs the
+         same function over --steps tokens. Its weights come from the oracle's own copy of
+         the seeded generator, so that arm loads no B200 code.
 Under torchrun (N > 1) the model is tensor parallel over the ranks (NCCL allreduce inside
 the captured step). --impl reference times the CPU implementation of the path.
 Weights are synthetic N(0, 0.02) Q4_0 from seed 0 (no checkpoints): data "synthetic".
@@ -36,20 +39,6 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s Llama-3-8B-shape Q4_0 @1/2/4/8 B200; GEMV HBM GB/s vs peak"
 PROMPT = 512
-
-
-def traffic_ratio():
-    """DRAM bytes / algorithmic bytes of the step kernel from the committed ncu summary
-    (profiles/k_step_4layer_8bshape_full.md, captured on a 4-layer case of the same kernel
-    and scaled per launch by the bytes processed), or None."""
-    p = os.path.join(ROOT, "profiles", "k_step_4layer_8bshape_full.md")
-    try:
-        for ln in open(p):
-            if ln.startswith("traffic_ratio:"):
-                return float(ln.split(":", 1)[1])
-    except OSError:
-        pass
-    return None
 
 
 def peaks():
@@ -143,23 +132,41 @@ def all_max(dist, v: float) -> float:
     return float(t.item())
 
 
+class Shape:
+    """A Llama-architecture shape (the BASELINE configurations; the same fields as the
+    package's LlamaShape, kept here so the CPU arm never loads the B200 library)."""
+
+    def __init__(self, n_layers, n_embd, n_heads, n_heads_kv, n_ff, n_vocab, rope_freq_base, rms_norm_eps=1e-5):
+        self.n_layers, self.n_embd, self.n_heads, self.n_heads_kv = n_layers, n_embd, n_heads, n_heads_kv
+        self.n_ff, self.n_vocab, self.rope_freq_base, self.rms_norm_eps = n_ff, n_vocab, rope_freq_base, rms_norm_eps
+        self.n_ctx_train = 8192
+        self.head_dim = n_embd // n_heads
+
+    def llama(self):
+        import jinf
+        return jinf.LlamaShape(self.n_layers, self.n_embd, self.n_heads, self.n_heads_kv, self.n_ff, self.n_vocab,
+                               self.rope_freq_base, self.rms_norm_eps)
+
+
+SHAPES = {"8b": Shape(32, 4096, 32, 8, 14336, 128256, 500000.0), "8b-q4km": Shape(32, 4096, 32, 8, 14336, 128256, 500000.0),
+          "tiny": Shape(4, 512, 8, 2, 1408, 4096, 10000.0), "70b": Shape(80, 8192, 64, 8, 28672, 128256, 500000.0)}
+Q4_0, Q4_K, Q6_K = 2, 12, 14  # the reference's jinf_qtype values
+
+
 def shape_for(name):
-    import jinf
-    return {"8b": jinf.LLAMA3_8B, "8b-q4km": jinf.LLAMA3_8B, "tiny": jinf.TINY, "70b": jinf.LLAMA3_70B}[name]
+    return SHAPES[name]
 
 
 def wtype_for(name):
-    """Weight quantisation of a config: Q4_K for the 70B shape and for the
+    """Weight quantisation of a config: Q4_K for the 70B shape (config C5) and for the
     Q4_K_M-like 8B file, else Q4_0."""
-    from jinf import _lib as L
-    return L.Q4_K if name in ("70b", "8b-q4km") else L.Q4_0
+    return Q4_K if name in ("70b", "8b-q4km") else Q4_0
 
 
 def mix_for(name):
     """Second weight type of a config: Q6_K for attn_v and ffn_down of the even layers and for
     the output head in the Q4_K_M-like 8B file (8b-q4km), else none."""
-    from jinf import _lib as L
-    return L.Q6_K if name == "8b-q4km" else 0
+    return Q6_K if name == "8b-q4km" else 0
 
 
 def wname_for(name):
@@ -171,76 +178,82 @@ def prompt_ids(n_vocab, n=PROMPT):
     return [int(t) for t in np.random.default_rng(0).integers(0, n_vocab, size=n)]
 
 
-# ------------------------------------------------------------------------- CPU oracle
+# ------------------------------------------------------------------------- CPU decode
 
-def cpu_decode_sample(shape, layers: int, target_s: float, min_reps: int = 2, wtype=None, mix=0):
-    """Time the CPU oracle on `layers` layers (+ LM head) of a decode token at position PROMPT,
-    extrapolate the per-token time to all layers. Returns (tok/s, threads, description)."""
+def bench_config(args, world):
+    """The workload description both arms print (the same dict on both)."""
+    shape = shape_for(args.config)
+    wbytes = weight_bytes(shape, args.config)
+    return {"workload": f"{args.config} greedy decode batch 1, prompt {PROMPT}, positions "
+                        f"{PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
+            "model": f"llama3-{args.config}-shape", "global_batch": 1, "seq_len": PROMPT + args.steps,
+            "parallelism": f"tp{world}",
+            "ffn": ["dense", "sparse: device predictor top-k 15%", "sparse: fixed mask 15% (runs of 8)"][args.sparse],
+            "l2": f"{wbytes / 1e9:.2f} GB of weights streamed per step >> 126 MB L2 (no flush needed)"}
+
+
+def weight_bytes(shape, config):
+    """Quantized weight bytes of one decode token (all projections and the LM head), in the
+    reference's block sizes."""
     from oracle import oracle
-    import jinf
-    syn = (jinf.SynthModel(shape, seed=0, weight_type=wtype, mix_type=mix) if wtype is not None
-           else jinf.SynthModel(shape, seed=0))
-    om = oracle.OracleModel(syn, max_ctx=PROMPT + 512, kv_f16=True, layers=layers)
+    src = oracle.SynthSource(shape, seed=0, weight_type=wtype_for(config), mix_type=mix_for(config))
+    tot = 0
+    for n in src.tensor_names():
+        t, _, nb = src.tensor_info(n)
+        if t != 0 and n != "token_embd.weight":
+            tot += nb
+    src.close()
+    return tot
+
+
+def cpu_decode(shape, config, warmup: int, steps: int, max_seconds: float | None = None):
+    """The CPU implementation of the decode path (the oracle: the reference's dequant
+    conventions and its kernels' math restated on the host, OpenMP over rows) timing WHOLE
+    decode tokens: every layer and the LM head, positions PROMPT + warmup onwards over a KV
+    cache filled with seeded values for the prompt. Weights come from the oracle's own copy of
+    the seeded generator (oracle/libsynth.so), so nothing of the B200 library is loaded.
+    With max_seconds, stops early once that much timed work is done (at least 2 tokens).
+    Returns (tok/s, threads, tokens timed, seconds timed)."""
+    from oracle import oracle
+    src = oracle.SynthSource(shape, seed=0, weight_type=wtype_for(config), mix_type=mix_for(config))
+    om = oracle.OracleModel(src, max_ctx=PROMPT + warmup + steps + 8, kv_f16=True)
     om.fill_kv_random(PROMPT, seed=1)
     tok = 1
-    om.forward(tok, want_logits=False)  # warm caches / threads
-    t_layers, t_full = [], []
-    t0 = time.perf_counter()
-    while (len(t_layers) < min_reps or time.perf_counter() - t0 < target_s) and om.pos < PROMPT + 500:
+    for _ in range(warmup):
+        tok = oracle.argmax(om.forward(tok))
+    n, t = 0, 0.0
+    while n < steps:
         a = time.perf_counter()
-        om.forward(tok, want_logits=False)
-        b = time.perf_counter()
-        om.forward(tok, want_logits=True)
-        c = time.perf_counter()
-        t_layers.append(b - a)
-        t_full.append(c - b)
-    t_l = sorted(t_layers)[len(t_layers) // 2] / layers
-    t_head = max(0.0, sorted(t_full)[len(t_full) // 2] - t_l * layers)
-    per_tok = t_l * shape.n_layers + t_head
-    desc = (f"{len(t_layers)}x2 decode tokens at position {PROMPT}..{om.pos} over {layers}/{shape.n_layers} "
-            f"layers + LM head, per-token time = {shape.n_layers}*layer + head (extrapolated); "
-            f"{time.perf_counter() - t0:.1f} s of CPU work")
+        logits = om.forward(tok)
+        t += time.perf_counter() - a
+        tok = oracle.argmax(logits)
+        n += 1
+        if max_seconds is not None and n >= 2 and t >= max_seconds:
+            break
     om.close()
-    return 1.0 / per_tok, oracle.num_threads(), desc, per_tok
+    src.close()
+    return n / t, oracle.num_threads(), n, t
 
 
 # ------------------------------------------------------------------------- reference arm
 
 def run_reference(args, rank, world):
-    """CPU implementation of the decode path on the host cores (the reference has no CPU
-    forward pass: the oracle restatement of its math, with its dequant conventions)."""
+    """The reference's decode path on the host cores. The reference has no CPU forward pass
+    (its math exists only as CUDA kernels), so this is the oracle restatement of it
+    (cpu_decode), timing --steps whole tokens after --warmup untimed ones."""
     if rank != 0:
         return
     shape = shape_for(args.config)
-    from oracle import oracle
-    import jinf
-    layers = 1
-    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config), mix_type=mix_for(args.config))
-    om = oracle.OracleModel(syn, max_ctx=PROMPT + args.warmup + args.steps + 8, kv_f16=True, layers=layers)
-    om.fill_kv_random(PROMPT, seed=1)
-    for _ in range(args.warmup):
-        om.forward(1, want_logits=False)
-    times = []
-    for _ in range(args.steps):
-        a = time.perf_counter()
-        om.forward(1, want_logits=False)
-        times.append(time.perf_counter() - a)
-    a = time.perf_counter()
-    om.forward(1, want_logits=True)
-    t_head = max(0.0, time.perf_counter() - a - sorted(times)[len(times) // 2])
-    t_layer = sum(times) / len(times) / layers
-    per_tok = t_layer * shape.n_layers + t_head
-    value = 1.0 / per_tok
-    cores = oracle.num_threads()
-    sample = (f"each step = 1 of {shape.n_layers} layers of one decode token (positions {PROMPT}+), "
-              f"tok/s = 1/({shape.n_layers}*mean step + LM head)")
+    value, cores, n, secs = cpu_decode(shape, args.config, args.warmup, args.steps)
+    sample = (f"{n} whole decode tokens (all {shape.n_layers} layers + LM head, greedy argmax) at positions "
+              f"{PROMPT + args.warmup}..{PROMPT + args.warmup + n - 1} after {args.warmup} untimed, "
+              f"{secs:.1f} s timed")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * per_tok,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * secs / n,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": f"{wname_for(args.config)} weights, f32",
-            "data": f"synthetic (seeded N(0,0.02) {wname_for(args.config).upper()} weights)",
-            "config": {"workload": f"{args.config} decode batch 1, prompt {PROMPT}", "model": args.config,
-                       "global_batch": 1, "seq_len": PROMPT + args.steps, "parallelism": "cpu"},
+            "dtype": f"{wname_for(args.config)} weights, f32 activations, f16 KV",
+            "data": f"synthetic (seeded N(0,0.02) {wname_for(args.config).upper()} weights, uniform prompt ids)",
+            "config": bench_config(args, world),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -312,6 +325,29 @@ def gemv_microbench(dev, peak):
     return out
 
 
+def cpu_gemv_c2(reps: int = 5):
+    """C2 on the host cores: the oracle's dequant-matvec (reference Q4_0 conventions, OpenMP
+    over rows) on the same shapes at batch 1, GB/s of weight + x + y bytes, median of reps."""
+    import numpy as np
+    from oracle import oracle
+    out = {}
+    for rows, cols in [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]:
+        src = oracle.SynthSource(Shape(1, cols, 32, 8, 4096, rows, 10000.0), seed=rows)
+        w = np.ascontiguousarray(src.read_rows("output.weight"))
+        x = np.random.default_rng(0).standard_normal(cols).astype(np.float16).astype(np.float32)
+        oracle.matvec(w, Q4_0, x, rows, cols)
+        ts = []
+        for _ in range(reps):
+            a = time.perf_counter()
+            oracle.matvec(w, Q4_0, x, rows, cols)
+            ts.append(time.perf_counter() - a)
+        t = sorted(ts)[len(ts) // 2]
+        out[f"{rows}x{cols}"] = {"us": round(1e6 * t, 1), "GB/s": round((w.nbytes + 4 * cols + 4 * rows) / t / 1e9, 2)}
+        src.close()
+    out["cores"] = oracle.num_threads()
+    return out
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -329,7 +365,7 @@ def run_ours(args, rank, world, local):
         dist.broadcast_object_list(buf, src=0)
         nccl_id = buf[0]
     t_load = time.perf_counter()
-    syn = jinf.SynthModel(shape, seed=0, weight_type=wtype_for(args.config), mix_type=mix_for(args.config))
+    syn = jinf.SynthModel(shape.llama(), seed=0, weight_type=wtype_for(args.config), mix_type=mix_for(args.config))
     max_ctx = PROMPT + args.warmup + args.steps + 8
     opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
                              sparse_mode=args.sparse)
@@ -377,13 +413,11 @@ def run_ours(args, rank, world, local):
     kv_bytes = 2 * 2 * shape.n_layers * (shape.n_heads_kv // world) * shape.head_dim * (PROMPT + args.warmup + args.steps / 2)
     step_gbs = (wbytes + kv_bytes) / (dev_s / args.steps) / 1e9
     if persistent:
-        ratio = traffic_ratio()
         roof = {"bound": "hbm", "kernel": "k_step (persistent decode step, one launch per token)",
                 "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s", "frac": round(step_gbs / peak, 4),
-                "peak_kind": peak_kind,
-                "traffic": int((wbytes + kv_bytes) * ratio) if ratio else None,
-                "traffic_note": "ncu dram read+write bytes per launch, measured on a 4-layer case of the same "
-                                "kernel and scaled by bytes processed (profiles/k_step_4layer_8bshape_full.md)",
+                "peak_kind": peak_kind, "traffic": None,
+                "traffic_note": "not measured by this run (no profiler in the timed process); DRAM bytes of the "
+                                "same kernel come from separate ncu captures",
                 "bytes_per_launch": int(wbytes + kv_bytes), "us_per_launch": round(1e6 * dev_s / args.steps, 2)}
     else:
         top = max(("qkv", "o_proj", "gate_up", "down", "lm_head", "sparse_ffn"),
@@ -398,24 +432,22 @@ def run_ours(args, rank, world, local):
     launches_per_step = 1 if persistent else shape.n_layers * 5 + 2
     line = None
     if rank == 0:
-        cpu = None
+        cpu, cpu_gemv = None, None
         if world == 1 and not args.no_cpu:
-            cv, cores, desc, _ = cpu_decode_sample(
-                shape, layers={"8b": 2, "8b-q4km": 2, "70b": 1}.get(args.config, shape.n_layers), target_s=args.cpu_seconds,
-                wtype=wtype_for(args.config), mix=mix_for(args.config))
+            cv, cores, n, secs = cpu_decode(shape, args.config, 1, 1 << 30, max_seconds=args.cpu_seconds)
+            desc = (f"{n} whole decode tokens (all {shape.n_layers} layers + LM head, greedy argmax) at positions "
+                    f"{PROMPT + 1}..{PROMPT + n} after 1 untimed, {secs:.1f} s timed; the same method as "
+                    f"--impl reference")
             cpu = {"value": cv, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
+            if gemv:
+                cpu_gemv = cpu_gemv_c2()
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * dev_s / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": f"{wname_for(args.config)} weights, f32 activations, f16 KV",
             "data": f"synthetic (seeded N(0,0.02) {wname_for(args.config).upper()} weights, uniform prompt ids)",
-            "config": {"workload": f"{args.config} greedy decode batch 1, prompt {PROMPT}, positions "
-                                   f"{PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
-                       "model": f"llama3-{args.config}-shape", "global_batch": 1, "seq_len": PROMPT + args.steps,
-                       "parallelism": f"tp{world}",
-                       "ffn": ["dense", "sparse: device predictor top-k 15%", "sparse: fixed mask 15% (runs of 8)"][args.sparse],
-                       "l2": f"{wbytes / 1e9:.2f} GB of weights streamed per step >> 126 MB L2 (no flush needed)"},
+            "config": bench_config(args, world),
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": roof,
@@ -430,11 +462,31 @@ def run_ours(args, rank, world, local):
             line["cpu_baseline"] = cpu
         if gemv:
             line["gemv_c2"] = gemv
+        if cpu_gemv:
+            line["gemv_c2_cpu"] = cpu_gemv
         print(json.dumps(line), flush=True)
     eng.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def profile_case(steps: int) -> None:
+    """The small case of the persistent step for ncu captures: ~0.6 GB of weights plus a
+    0.5 GB embedding table; with a 3-token prompt the captured launch `-s 3 -c 1` is the
+    first decode step at position 513."""
+    import torch
+    import jinf
+    shape = jinf.LlamaShape(4, 4096, 32, 8, 14336, 32000, 5e5)
+    eng = jinf.Engine.from_synth(jinf.SynthModel(shape, seed=0), max_context=600,
+                                 options=jinf.b200_options(eos_token=-1))
+    eng.forward([1, 2, 3])
+    eng.fill_kv_random(512, seed=1)
+    eng.forward([5])
+    eng.decode_resident(steps)
+    torch.cuda.synchronize()
+    eng.close()
+    print("profile case ok")
 
 
 def main():
@@ -449,7 +501,14 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--sparse", type=int, default=0, choices=[0, 1, 2],
                     help="FFN: 0 dense, 1 device predictor top-k, 2 fixed mask (BASELINE config C4)")
+    ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",
+                    help="run only the small case used for ncu captures of the step kernel and exit: a 4-layer "
+                         "8B-shaped model (vocabulary 32000), KV filled to position 512, one forwarded token, "
+                         "then STEPS resident decode steps")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local = dist_env()

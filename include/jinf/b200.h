@@ -66,8 +66,9 @@ jinf_status jinf_b200_gemv_q4m_rmsnorm(const void* q4m, const float* h, const fl
 // reference. The split-K workspace is a 4 MB static device array inside the library
 // (counters zero at load and left zero by every call), so the caller neither allocates nor
 // passes one; the first call on each device looks the array up and must not be inside a
-// stream capture. rows <= 262144; a shape whose partial sums exceed the array is rejected
-// with JINF_ERR_INVALID. Calls that overlap in time share the array and race: serialise them.
+// stream capture. rows <= 262144 (else JINF_ERR_INVALID); where the K split that kw = 0
+// would pick needs more partial sums than the array holds, a smaller split is used. Calls
+// that overlap in time share the array and race: serialise them.
 jinf_status jinf_b200_gemv_q4m_noalloc(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
                                        cudaStream_t stream);
 

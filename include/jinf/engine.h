@@ -162,6 +162,11 @@ jinf_status jinf_engine_last_argmax(jinf_engine* e, int32_t* token);
 // Fill the KV cache positions [0, n_pos) of every layer with seeded N(0,1) fp16 values
 // and set n_past = n_pos (timing-only shortcut for long contexts).
 jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uint64_t seed);
+// Copy positions [0, n_pos) of this rank's fp16 KV cache to host memory, as
+// [layer][kv_head of this rank][n_pos][head_dim] fp16 for K and for V (each
+// n_layers * n_heads_kv_of_rank * n_pos * head_dim values). Lets a checker start from the
+// engine's cache (e.g. after jinf_engine_fill_kv_random). Synchronous.
+jinf_status jinf_engine_kv_read(jinf_engine* e, int n_pos, uint16_t* k_host, uint16_t* v_host);
 // 1 when each decode token runs as one persistent kernel, 0 for one kernel per operation.
 int         jinf_engine_is_persistent(const jinf_engine* e);
 // Sparse FFN modes: the active neurons of `layer` used by the last forward (ids ascending,

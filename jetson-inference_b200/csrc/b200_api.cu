@@ -8,20 +8,24 @@
 #include "device_state.cuh"
 #include "q4m.cuh"
 
+#include <algorithm>
+#include <atomic>
+
 using namespace jinf;
 
 static int device_sms() {
-    // per-device cache (up to 64 devices)
-    static int sms[64] = {0};
+    // per-device cache (up to 64 devices); every writer stores the same value
+    static std::atomic<int> sms[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
-    if (!sms[dev]) {
-        int n = 148;
+    int n = sms[dev].load(std::memory_order_relaxed);
+    if (!n) {
+        n = 148;
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        sms[dev] = n;
+        sms[dev].store(n, std::memory_order_relaxed);
     }
-    return sms[dev];
+    return n;
 }
 
 extern "C" uint64_t jinf_b200_q4m_bytes(int rows, int cols) {
@@ -143,19 +147,21 @@ static __device__ __align__(256) unsigned char g_gemv_noalloc_scratch[kNoAllocSc
 // Device address of the scratch on the current device, looked up once per device (the
 // first call on a device must not be inside a stream capture).
 static jinf_status noalloc_scratch(uint8_t** out) {
-    static uint8_t* addr[64] = {nullptr};
+    static std::atomic<uint8_t*> addr[64];  // every writer stores the same address
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return JINF_ERR_CUDA;
-    if (!addr[dev]) {
+    uint8_t* a = addr[dev].load(std::memory_order_acquire);
+    if (!a) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_noalloc_scratch);
         if (e != cudaSuccess || !p) {
             JINF_LOG("jinf_b200_gemv_q4m_noalloc: scratch address lookup failed: %s", cudaGetErrorString(e));
             return JINF_ERR_CUDA;
         }
-        addr[dev] = (uint8_t*)p;
+        a = (uint8_t*)p;
+        addr[dev].store(a, std::memory_order_release);
     }
-    *out = addr[dev];
+    *out = a;
     return JINF_OK;
 }
 
@@ -172,19 +178,24 @@ extern "C" jinf_status jinf_b200_gemv_q4m_noalloc(const void* q4m, const void* x
     }
     const int xm = x_type == JINF_TYPE_F32 ? X_PLAIN_F32 : X_PLAIN_F16;
     const int grid = gemvm_grid(sh.cols, xm, EPI_STORE, device_sms());
-    const int kw = gemvm_pick_kw(sh.pairs, sh.groups, grid, kQ4mMaxKw);
-    const size_t part_bytes = (size_t)sh.pairs * kw * Q4M_PAIR_ROWS * sizeof(float);
-    if (kw > 1 && part_bytes > kNoAllocScratchBytes - kNoAllocCntBytes) {
-        JINF_LOG("jinf_b200_gemv_q4m_noalloc: %d x %d needs %zu bytes of partial sums, the static scratch holds %zu",
-                 rows, cols, part_bytes, kNoAllocScratchBytes - kNoAllocCntBytes);
-        return JINF_ERR_INVALID;
-    }
-    uint8_t* scratch = nullptr;
-    JINF_CHECK(noalloc_scratch(&scratch), "noalloc scratch");
     GemvParams p{};
     gemvm_params_for(p, q4m, sh);
     p.x = x;
     p.y = y;
+    if (gemvm_use_local(sh.pairs, grid)) {  // as jinf_b200_gemv_q4m with kw = 0: K split inside each CTA
+        p.kw = 1;
+        p.local_k = 1;
+        return gemvm_launch(p, xm, EPI_STORE, gemvm_local_grid(sh.pairs, grid), stream, false) == cudaSuccess
+                   ? JINF_OK
+                   : JINF_ERR_CUDA;
+    }
+    // the K split that kw = 0 would pick, limited to what the array's partial rows hold
+    const size_t part_cap = kNoAllocScratchBytes - kNoAllocCntBytes;
+    const size_t per_kw = (size_t)sh.pairs * Q4M_PAIR_ROWS * sizeof(float);
+    const int kw_fit = (int)std::min<size_t>((size_t)kQ4mMaxKw, part_cap / per_kw);
+    const int kw = kw_fit <= 1 ? 1 : gemvm_pick_kw(sh.pairs, sh.groups, grid, kw_fit);
+    uint8_t* scratch = nullptr;
+    JINF_CHECK(noalloc_scratch(&scratch), "noalloc scratch");
     p.kw = kw;
     if (kw > 1) {
         p.cnt = (unsigned int*)scratch;

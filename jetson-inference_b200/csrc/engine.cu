@@ -1302,7 +1302,11 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     // the static active sets of mode 2: the reference's activation profile when the config
     // names one (reference src/engine.cpp:228-252: a profile that cannot be read leaves the
     // FFN dense), else the seeded fixed masks
-    if (cfg->predictor_path && tp == 1 && I->d <= 8192) {
+    if (cfg->predictor_path && src.prepacked()) {
+        // a B200-layout file holds the dense gate|up and down images only (as the reference
+        // runs a dense FFN for a model without neuron bundles, src/engine.cpp:253-255)
+        JINF_LOG("Warning: predictor path set but the B200-layout model holds no sparse FFN form; dense FFN");
+    } else if (cfg->predictor_path && tp == 1 && I->d <= 8192) {
         std::vector<int32_t> ids((size_t)I->L * I->ffl), cnt(I->L);
         const jinf_status ps = jinf_activation_profile_read(cfg->predictor_path, cfg->sparsity_threshold, I->L, I->ffl,
                                                             ids.data(), cnt.data());
@@ -1873,6 +1877,19 @@ extern "C" jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uin
     JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->pos, &n_pos, sizeof(int), cudaMemcpyHostToDevice, I->stream));
     JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
     e->n_past = n_pos;
+    return JINF_OK;
+}
+
+extern "C" jinf_status jinf_engine_kv_read(jinf_engine* e, int n_pos, uint16_t* k_host, uint16_t* v_host) {
+    if (!e || !e->impl || !k_host || !v_host || n_pos <= 0 || n_pos > e->impl->max_ctx) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    // the cache is [layer][kv head][max_ctx][hd]: one strided copy per cache, rows of n_pos * hd
+    const size_t w = (size_t)n_pos * I->hd * sizeof(__half), pitch = (size_t)I->max_ctx * I->hd * sizeof(__half);
+    const size_t h = (size_t)I->L * I->Hkvl;
+    JINF_CUDA_CHECK(cudaMemcpy2DAsync(k_host, w, I->kc, pitch, w, h, cudaMemcpyDeviceToHost, I->stream));
+    JINF_CUDA_CHECK(cudaMemcpy2DAsync(v_host, w, I->vc, pitch, w, h, cudaMemcpyDeviceToHost, I->stream));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
     return JINF_OK;
 }
 

@@ -228,6 +228,7 @@ SIGNATURES = {
     "jinf_engine_decode_resident": (i32, [C.POINTER(Engine), i32, C.POINTER(C.c_int32)]),
     "jinf_engine_last_argmax": (i32, [C.POINTER(Engine), C.POINTER(C.c_int32)]),
     "jinf_engine_fill_kv_random": (i32, [C.POINTER(Engine), i32, u64]),
+    "jinf_engine_kv_read": (i32, [C.POINTER(Engine), i32, vp, vp]),
     "jinf_engine_is_persistent": (i32, [vp]),
     "jinf_engine_sparse_ids": (i32, [vp, i32, vp, i32, vp]),
     "jinf_engine_count_activations": (i32, [vp, vp, i32, C.c_float, vp]),

@@ -153,11 +153,14 @@ class Engine:
         self.h = handle
 
     @classmethod
-    def from_nvmw(cls, path: str, max_context: int = 512, options: L.B200Options | None = None) -> "Engine":
+    def from_nvmw(cls, path: str, max_context: int = 512, options: L.B200Options | None = None,
+                  predictor_path: str | None = None, sparsity_threshold: float = 0.5) -> "Engine":
         cfg = L.EngineConfig()
         cfg.model_path = path.encode()
         cfg.gpu_memory_budget, cfg.buffer_capacity = 4500 << 20, 128 << 20
-        cfg.max_context, cfg.io_queue_depth, cfg.sparsity_threshold = max_context, 64, 0.5
+        cfg.max_context, cfg.io_queue_depth, cfg.sparsity_threshold = max_context, 64, sparsity_threshold
+        if predictor_path:
+            cfg.predictor_path = predictor_path.encode()
         e = C.POINTER(L.Engine)()
         if options is None:
             L.check(L.lib.jinf_engine_create(C.byref(e), C.byref(cfg)), "jinf_engine_create")
@@ -242,6 +245,17 @@ class Engine:
 
     def fill_kv_random(self, n_pos: int, seed: int = 0) -> None:
         L.check(L.lib.jinf_engine_fill_kv_random(self.h, n_pos, seed), "fill_kv_random")
+
+    def kv_read(self, n_pos: int, tp_size: int = 1):
+        """(K, V) of positions [0, n_pos) of this rank's cache as fp16 arrays
+        [n_layers][kv heads of this rank][n_pos][head_dim] (tp_size: the engine's ranks)."""
+        e = self.h.contents
+        hkv = e.n_heads_kv // max(1, tp_size)
+        shp = (e.n_layers, hkv, n_pos, e.n_embd // e.n_heads)
+        k, v = np.empty(shp, dtype=np.float16), np.empty(shp, dtype=np.float16)
+        L.check(L.lib.jinf_engine_kv_read(self.h, n_pos, k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p)),
+                "kv_read")
+        return k, v
 
     @property
     def persistent(self) -> bool:

@@ -434,6 +434,25 @@ int orc_fill_kv_random(orc_model* m, int n_pos, uint64_t seed) {
     return 0;
 }
 
+// Load positions [0, n_pos) of every layer's cache from fp16 values laid out
+// [layer][kv head][n_pos][hd] (the B200 engine's cache order, e.g. read back after its
+// seeded fill), and set the position to n_pos. The values are exact in both caches.
+int orc_model_load_kv_f16(orc_model* m, int n_pos, const uint16_t* k, const uint16_t* v) {
+    if (!m || !k || !v || n_pos < 0 || n_pos > m->max_ctx) return -1;
+    const size_t kvd = (size_t)m->nkv * m->hd;
+    for (int L = 0; L < m->L; ++L)
+        for (int h = 0; h < m->nkv; ++h)
+            for (int p = 0; p < n_pos; ++p)
+                for (int d = 0; d < m->hd; ++d) {
+                    const size_t src = (((size_t)L * m->nkv + h) * n_pos + p) * m->hd + d;
+                    const size_t dst = ((size_t)L * m->max_ctx + p) * kvd + (size_t)h * m->hd + d;
+                    m->kc[dst] = orc_fp16_to_fp32(k[src]);
+                    m->vc[dst] = orc_fp16_to_fp32(v[src]);
+                }
+    m->pos = n_pos;
+    return 0;
+}
+
 int orc_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

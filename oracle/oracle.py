@@ -15,15 +15,27 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
+SYNTH_SO = os.path.join(HERE, "libsynth.so")
 REF_SO = os.path.join(HERE, "_ref", "libjinf_ref.so")
 
 _orc = None
 _ref = None
+_syn = None
+
+
+def reference_dir() -> str | None:
+    """The reference source tree, if this machine has it: $JINF_REFERENCE_DIR, else a
+    checkout named `reference` beside this repository. None on machines without it (the
+    prebuilt _ref/ files are used there)."""
+    cand = os.environ.get("JINF_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isfile(os.path.join(cand, "src", "quant.cpp")) else None
 
 
 def build() -> None:
-    """Build liboracle.so (and _ref/ when the reference tree is present)."""
-    subprocess.run(["make", "-C", HERE], check=True, stdout=subprocess.DEVNULL)
+    """Build liboracle.so and libsynth.so (and _ref/ when the reference tree is present)."""
+    ref = reference_dir()
+    cmd = ["make", "-C", HERE] + ([f"REF={ref}"] if ref else [])
+    subprocess.run(cmd, check=True, stdout=subprocess.DEVNULL)
 
 
 def lib() -> C.CDLL:
@@ -55,6 +67,7 @@ def lib() -> C.CDLL:
             "orc_forward": (i32, [vp, i32, vp]),
             "orc_argmax": (i32, [vp, i32]),
             "orc_fill_kv_random": (i32, [vp, i32, C.c_uint64]),
+            "orc_model_load_kv_f16": (i32, [vp, i32, vp, vp]),
             "orc_num_threads": (i32, []),
         }
         for n, (r, a) in sig.items():
@@ -69,7 +82,7 @@ def ref_lib() -> C.CDLL | None:
     global _ref
     if _ref is None:
         if not os.path.exists(REF_SO):
-            if os.path.exists("/root/reference/src/quant.cpp"):
+            if reference_dir():
                 build()
             if not os.path.exists(REF_SO):
                 return None
@@ -166,6 +179,104 @@ def sparse_ffn(bundles, x, offsets, n_act, hidden, qtype) -> tuple[np.ndarray, n
     return out, gu[:n_act]
 
 
+class _HParams(C.Structure):
+    _fields_ = [("arch", C.c_char * 64), ("n_layers", C.c_uint32), ("n_embd", C.c_uint32),
+                ("n_heads", C.c_uint32), ("n_heads_kv", C.c_uint32), ("n_ff", C.c_uint32),
+                ("n_vocab", C.c_uint32), ("n_ctx_train", C.c_uint32), ("rope_freq_base", C.c_float),
+                ("rms_norm_eps", C.c_float)]
+
+
+class _SynthConfig(C.Structure):
+    _fields_ = [("hp", _HParams), ("seed", C.c_uint64), ("weight_type", C.c_int),
+                ("weight_std", C.c_float), ("embed_std", C.c_float), ("mix_type", C.c_int)]
+
+
+def synth_lib() -> C.CDLL:
+    """libsynth.so: the seeded synthetic-model generator built from the package's generator
+    sources, so that CPU baselines and fixture scripts run without the product library."""
+    global _syn
+    if _syn is None:
+        if not os.path.exists(SYNTH_SO):
+            build()
+        s = C.CDLL(SYNTH_SO)
+        vp, i32, i64 = C.c_void_p, C.c_int, C.c_int64
+        sig = {
+            "jinf_synth_create": (i32, [C.POINTER(vp), C.POINTER(_SynthConfig)]),
+            "jinf_synth_destroy": (None, [vp]),
+            "jinf_synth_n_tensors": (i32, [vp]),
+            "jinf_synth_tensor_name": (C.c_char_p, [vp, i32]),
+            "jinf_synth_tensor_info": (i32, [vp, C.c_char_p, C.POINTER(i32), C.POINTER(i64), C.POINTER(i32),
+                                             C.POINTER(C.c_uint64)]),
+            "jinf_synth_read_rows": (i32, [vp, C.c_char_p, i64, i64, vp]),
+            "jinf_synth_write_gguf": (i32, [vp, C.c_char_p]),
+        }
+        for n, (r, a) in sig.items():
+            fn = getattr(s, n)
+            fn.restype, fn.argtypes = r, a
+        _syn = s
+    return _syn
+
+
+class SynthSource:
+    """The seeded synthetic model (same bytes as the package's SynthModel: one generator
+    source), read through libsynth.so. `shape` is any object with the LlamaShape fields."""
+
+    def __init__(self, shape, seed: int = 0, weight_type: int = 2, mix_type: int = 0,
+                 weight_std: float = 0.02, embed_std: float = 0.02):
+        cfg = _SynthConfig()
+        cfg.hp.arch = b"llama"
+        cfg.hp.n_layers, cfg.hp.n_embd, cfg.hp.n_heads = shape.n_layers, shape.n_embd, shape.n_heads
+        cfg.hp.n_heads_kv, cfg.hp.n_ff, cfg.hp.n_vocab = shape.n_heads_kv, shape.n_ff, shape.n_vocab
+        cfg.hp.n_ctx_train = getattr(shape, "n_ctx_train", 8192)
+        cfg.hp.rope_freq_base, cfg.hp.rms_norm_eps = shape.rope_freq_base, shape.rms_norm_eps
+        cfg.seed, cfg.weight_type, cfg.weight_std, cfg.embed_std = seed, weight_type, weight_std, embed_std
+        cfg.mix_type = mix_type
+        h = C.c_void_p()
+        if synth_lib().jinf_synth_create(C.byref(h), C.byref(cfg)) != 0:
+            raise RuntimeError("jinf_synth_create failed")
+        self.handle, self.shape = h, shape
+
+    def close(self) -> None:
+        if self.handle:
+            synth_lib().jinf_synth_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def tensor_names(self) -> list[str]:
+        n = synth_lib().jinf_synth_n_tensors(self.handle)
+        return [synth_lib().jinf_synth_tensor_name(self.handle, i).decode() for i in range(n)]
+
+    def tensor_info(self, name: str):
+        t, nd, nb = C.c_int(), C.c_int(), C.c_uint64()
+        shape = (C.c_int64 * 4)()
+        if synth_lib().jinf_synth_tensor_info(self.handle, name.encode(), C.byref(t), shape, C.byref(nd),
+                                              C.byref(nb)) != 0:
+            raise KeyError(name)
+        return t.value, tuple(shape[i] for i in range(nd.value)), nb.value
+
+    def read_rows(self, name: str, row0: int = 0, n_rows: int | None = None) -> np.ndarray:
+        t, shape, nbytes = self.tensor_info(name)
+        rows = shape[1] if len(shape) > 1 else 1
+        if n_rows is None:
+            n_rows = rows - row0
+        row_bytes = nbytes // rows
+        buf = np.empty(n_rows * row_bytes, dtype=np.uint8)
+        if synth_lib().jinf_synth_read_rows(self.handle, name.encode(), row0, n_rows, _vp(buf)) != 0:
+            raise RuntimeError(f"read_rows({name})")
+        if t == 0:
+            return buf.view(np.float32).reshape(n_rows, -1)
+        return buf.reshape(n_rows, row_bytes)
+
+    def write_gguf(self, path: str) -> None:
+        if synth_lib().jinf_synth_write_gguf(self.handle, path.encode()) != 0:
+            raise RuntimeError("write_gguf failed")
+
+
 class OracleModel:
     """The whole decode step on the CPU, over tensors of a jinf SynthModel (borrowed arrays)."""
 
@@ -220,6 +331,16 @@ class OracleModel:
     def fill_kv_random(self, n_pos: int, seed: int = 0) -> None:
         if lib().orc_fill_kv_random(self.h, n_pos, seed) != 0:
             raise RuntimeError("orc_fill_kv_random failed")
+
+    def load_kv_f16(self, k: np.ndarray, v: np.ndarray) -> None:
+        """Cache positions [0, n) from fp16 arrays [layers][kv heads][n][head_dim] (the B200
+        engine's order, e.g. Engine.kv_read), and set the position to n."""
+        k = np.ascontiguousarray(k, dtype=np.float16)
+        v = np.ascontiguousarray(v, dtype=np.float16)
+        if k.shape != v.shape or k.ndim != 4:
+            raise ValueError("k and v must be [layers][kv heads][n][head_dim]")
+        if lib().orc_model_load_kv_f16(self.h, k.shape[2], _vp(k), _vp(v)) != 0:
+            raise RuntimeError("orc_model_load_kv_f16 failed")
 
 
 def argmax(v: np.ndarray) -> int:

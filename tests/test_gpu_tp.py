@@ -25,7 +25,7 @@ def rel_err(got, want):
     return float(np.max(np.abs(got - want)) / max(np.max(np.abs(want)), 1e-30))
 
 
-def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, persistent, out_q):
+def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, persistent, kv_pos, out_q):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "jetson-inference_b200"))
@@ -36,7 +36,11 @@ def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, persistent, o
         syn = jinf.SynthModel(shape, seed=0)
         opts = jinf.b200_options(device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
                                  persistent=persistent)
-        eng = jinf.Engine.from_synth(syn, max_context=64, options=opts)
+        eng = jinf.Engine.from_synth(syn, max_context=kv_pos + 64, options=opts)
+        kv = None
+        if kv_pos:  # the same seeded cache on every rank; the parent gathers the ranks' heads
+            eng.fill_kv_random(kv_pos, seed=1)
+            kv = eng.kv_read(kv_pos, tp_size=world)
         logits = [eng.logits_host(prompt)]
         toks = [eng.last_argmax()]
         for _ in range(n_greedy):
@@ -44,32 +48,36 @@ def _rank_main(rank, world, nccl_id, shape_args, prompt, n_greedy, persistent, o
             toks.append(eng.last_argmax())
         persistent = eng.persistent
         eng.close()
-        out_q.put((rank, "ok", [l.copy() for l in logits], toks, persistent))
+        out_q.put((rank, "ok", [l.copy() for l in logits], toks, (persistent, kv)))
     except Exception as e:  # reported to the parent, which fails the test
         out_q.put((rank, "error", repr(e), None, None))
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-@pytest.mark.parametrize("shape_args", [(4, 512, 8, 2, 1408, 4096, 1e4), (2, 4096, 32, 8, 14336, 32000, 5e5)],
-                         ids=["tiny", "8b_layers"])
+@pytest.mark.parametrize("shape_args,kv_pos", [((4, 512, 8, 2, 1408, 4096, 1e4), 0),
+                                                ((2, 4096, 32, 8, 14336, 32000, 5e5), 0),
+                                                ((2, 4096, 32, 8, 14336, 32000, 5e5), 512)],
+                         ids=["tiny", "8b_layers", "8b_layers_pos512"])
 @pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "per_op"])
-def test_tp2_matches_oracle(shape_args, persistent):
+def test_tp2_matches_oracle(shape_args, kv_pos, persistent):
+    """kv_pos 512: both sides start from the same 512-position cache (each rank's seeded
+    fill, gathered for the oracle), so attention runs at the benchmark's positions."""
     import jinf
     prompt = [int(t) for t in np.random.default_rng(0).integers(0, shape_args[5], size=8)]
     n_greedy = 4
     nccl_id = jinf.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, nccl_id, shape_args, prompt, n_greedy, persistent, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, nccl_id, shape_args, prompt, n_greedy, persistent, kv_pos, q))
              for r in range(WORLD)]
     for p in procs:
         p.start()
     results = {}
     try:
         for _ in range(WORLD):
-            rank, status, logits, toks, persistent = q.get(timeout=300)
+            rank, status, logits, toks, extra = q.get(timeout=300)
             assert status == "ok", f"rank {rank}: {logits}"
-            results[rank] = (logits, toks, persistent)
+            results[rank] = (logits, toks, extra[0], extra[1])
     except queue.Empty:
         pytest.fail("a tensor-parallel rank did not report within 300 s")
     finally:
@@ -84,11 +92,14 @@ def test_tp2_matches_oracle(shape_args, persistent):
     assert results[0][1] == results[1][1]
     # against the oracle, token by token
     syn = jinf.SynthModel(jinf.LlamaShape(*shape_args), seed=0)
-    orc = oracle.OracleModel(syn, max_ctx=64, kv_f16=True)
+    orc = oracle.OracleModel(syn, max_ctx=kv_pos + 64, kv_f16=True)
+    if kv_pos:
+        orc.load_kv_f16(np.concatenate([results[r][3][0] for r in range(WORLD)], axis=1),
+                        np.concatenate([results[r][3][1] for r in range(WORLD)], axis=1))
     want = None
     for t in prompt:
         want = orc.forward(t)
-    logits, toks, _ = results[0]
+    logits, toks = results[0][0], results[0][1]
     for step in range(n_greedy + 1):
         assert rel_err(logits[step], want) < LOGIT_REL, f"step {step}"
         assert toks[step] == oracle.argmax(want), f"step {step}"
