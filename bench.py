@@ -434,7 +434,7 @@ def run_ours(args, rank, world, local):
     if rank == 0:
         cpu, cpu_gemv = None, None
         if world == 1 and not args.no_cpu:
-            cv, cores, n, secs = cpu_decode(shape, args.config, 1, 1 << 30, max_seconds=args.cpu_seconds)
+            cv, cores, n, secs = cpu_decode(shape, args.config, 1, 64, max_seconds=args.cpu_seconds)
             desc = (f"{n} whole decode tokens (all {shape.n_layers} layers + LM head, greedy argmax) at positions "
                     f"{PROMPT + 1}..{PROMPT + n} after 1 untimed, {secs:.1f} s timed; the same method as "
                     f"--impl reference")

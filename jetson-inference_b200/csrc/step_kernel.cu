@@ -51,6 +51,24 @@ namespace {
 
 constexpr int NW = STEP_THREADS / 32;
 
+// Development timing (off unless built with -DJINF_STEP_TRACE): thread 0 of every CTA stamps
+// %globaltimer at fixed points of every phase into g_step_trace[phase][cta][point]; the last
+// launch's stamps are read with jinf_step_trace_read.
+#ifdef JINF_STEP_TRACE
+constexpr int TRACE_PTS = 6, TRACE_MAX_PH = 512, TRACE_MAX_CTA = 160;
+__device__ unsigned long long g_step_trace[TRACE_MAX_PH * TRACE_MAX_CTA * TRACE_PTS];
+__device__ __forceinline__ void trace_at(int ph, int pt) {
+    if (threadIdx.x == 0 && ph < TRACE_MAX_PH && blockIdx.x < TRACE_MAX_CTA) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g_step_trace[((size_t)ph * TRACE_MAX_CTA + blockIdx.x) * TRACE_PTS + pt] = t;
+    }
+}
+#define JINF_TRACE(ph, pt) trace_at(ph, pt)
+#else
+#define JINF_TRACE(ph, pt) ((void)0)
+#endif
+
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -729,6 +747,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     static_assert(sizeof(StepPhase) <= 256 && sizeof(StepPhase) % 4 == 0, "descriptor slot");
     for (int ph = 0; ph < P.n_phases; ++ph) {
         StepPhase& d = dsm[ph & 1];
+        JINF_TRACE(ph, 0);
         if (tid == 0) {
             const StepPhase& g = P.phases[ph];
             // (a tensor-parallel input waits in its staging: the flagged words are the signal)
@@ -747,6 +766,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         }
         __syncthreads();  // also: every warp is done with the previous phase's shared data
         if (!flags[ph & 1]) break;
+        JINF_TRACE(ph, 1);
 
         if (d.kind == PH_ATTN) {
             // ---------------- attention: CTA (kv head, split) of the context
@@ -771,6 +791,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                 else JINF_ATTN_SPLIT(128, 1);
             }
 #undef JINF_ATTN_SPLIT
+            JINF_TRACE(ph, 2);
             const int nblk = gq * hd / 32;  // 32-element output blocks of this kv head
             if (a.S == 1) {
                 __syncthreads();
@@ -784,6 +805,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                     __threadfence();
                     atomicAdd(P.done + ph, (unsigned)nblk);
                 }
+                JINF_TRACE(ph, 5);
                 continue;
             }
             // publish this split's partial; the splits that own output blocks (split sp owns
@@ -795,9 +817,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                 __threadfence();
                 atomicAdd(cnt, 1u);
             }
+            JINF_TRACE(ph, 3);
             if (a.sp >= nblk) continue;
             if (tid == 0) flags[2] = wait_ge(cnt, (unsigned)a.S, st, P.spin_limit) ? 1 : 0;
             __syncthreads();  // (a timeout is recorded in the device state; the step is then discarded)
+            JINF_TRACE(ph, 4);
             const size_t stride = (size_t)ATTN_MAX_GROUP * (hd + 2);
             const float* base = P.attn_part + (size_t)a.kvh * ATTN_MAX_SPLIT * stride;
             float* ml = reinterpret_cast<float*>(xbase);  // [S][2] (m, l) of the block's query head
@@ -858,6 +882,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                 __threadfence();
                 atomicAdd(P.done + ph, mine);
             }
+            JINF_TRACE(ph, 5);
             continue;
         }
 
@@ -911,6 +936,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                 fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps, d.cols,
                                             xbase, misc, true);
         }
+        JINF_TRACE(ph, 2);
         const XRecS xr{smem_u32(xbase), smem_u32(xbase + (size_t)G * 256)};
         // epilogue arguments are read from the shared descriptor when a tile finishes
         auto epilogue = [&](int row, float v0, float v1) {
@@ -999,7 +1025,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             }
             first_piece = false;
         }
+        JINF_TRACE(ph, 3);
         __syncthreads();
+        JINF_TRACE(ph, 4);
         if (own_pair >= 0) {
             // add the pieces of the following warps in warp order, then the epilogue. The
             // contributing warps are the ones after this warp, up to the first warp with units
@@ -1038,6 +1066,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             __threadfence();
             atomicAdd(P.done + ph, (unsigned)(t1 - t0));
         }
+        JINF_TRACE(ph, 5);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 
@@ -1169,6 +1198,14 @@ int step_occupancy(size_t smem, int fmt, int nbuf) {
     }
     return lo;
 }
+
+#ifdef JINF_STEP_TRACE
+extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
+    const size_t cap = (size_t)TRACE_MAX_PH * TRACE_MAX_CTA * TRACE_PTS;
+    if (n > cap) n = cap;
+    return cudaMemcpyFromSymbol(host, g_step_trace, n * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
     const size_t smem = step_smem_bytes(p.xstage_bytes, p.n_phases, p.fmt, p.nbuf);
