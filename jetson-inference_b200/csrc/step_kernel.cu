@@ -69,24 +69,65 @@ __device__ __forceinline__ void trace_at(int ph, int pt) {
 #define JINF_TRACE(ph, pt) ((void)0)
 #endif
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+// Development timing (off unless built with -DJINF_STEP_TRACE): thread 0 of every CTA stamps
+// %globaltimer at fixed points of every phase into g_step_trace[phase][cta][point]; the last
+// launch's stamps are read with jinf_step_trace_read.
+#ifdef JINF_STEP_TRACE
+constexpr int TRACE_PTS = 6, TRACE_MAX_PH = 512, TRACE_MAX_CTA = 160;
+__device__ unsigned long long g_step_trace[TRACE_MAX_PH * TRACE_MAX_CTA * TRACE_PTS];
+__device__ __forceinline__ void trace_at(int ph, int pt) {
+    if (threadIdx.x == 0 && ph < TRACE_MAX_PH && blockIdx.x < TRACE_MAX_CTA) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g_step_trace[((size_t)ph * TRACE_MAX_CTA + blockIdx.x) * TRACE_PTS + pt] = t;
+    }
+}
+#define JINF_TRACE(ph, pt) trace_at(ph, pt)
+#else
+#define JINF_TRACE(ph, pt) ((void)0)
+#endif
+
+// ---------------------------------------------------------------- flagged words
+//
+// Every tensor one phase hands to another travels as 8-byte words {value bits, flag}
+// (step.h: step_flag). The producer stores them with plain stores and no fence; the
+// consumer loads them and reloads the words whose flag is not yet the expected one, at
+// most `limit` times (then DEV_ERR_TIMEOUT is recorded and the step is discarded). It also
+// gives up as soon as another CTA has recorded an error, so a failed step ends quickly.
+typedef unsigned long long u64w;
+
+__device__ __forceinline__ u64w fword(float v, uint32_t flag) { return ((u64w)flag << 32) | __float_as_uint(v); }
+__device__ __forceinline__ u64w fword_u(uint32_t v, uint32_t flag) { return ((u64w)flag << 32) | v; }
+__device__ __forceinline__ void st_w(u64w* p, u64w w) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ u64w ld_w(const u64w* p) {
+    u64w v;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ float fval(u64w w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ bool fw_ok(u64w w, uint32_t flag) { return (uint32_t)(w >> 32) == flag; }
 
-// Wait until *c >= target. Gives up after `limit` polls, or as soon as another CTA has
-// recorded an error; a timeout records DEV_ERR_TIMEOUT.
-__device__ bool wait_ge(const unsigned* c, unsigned target, DeviceState* st, unsigned long long limit) {
-    for (unsigned long long it = 0;; ++it) {
-        if (ld_acquire(c) >= target) return true;
-        if (*(volatile int*)&st->error != DEV_OK) return false;
-        if (it >= limit) {
-            atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
-            return false;
+__device__ __noinline__ void note_timeout(DeviceState* st) { atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT); }
+
+// Reload the word at p (whose last load gave w) until it carries `flag`. The check is inline;
+// the reload loop is out of line, so that a word that is already there costs no call.
+__device__ __noinline__ u64w wait_word_slow(const u64w* p, u64w w, uint32_t flag, DeviceState* st,
+                                            unsigned long long limit) {
+    for (unsigned long long it = 0; !fw_ok(w, flag); ++it) {
+        if (it >= limit || *(volatile int*)&st->error != DEV_OK) {
+            note_timeout(st);
+            break;
         }
         __nanosleep(32);
+        w = ld_w(p);
     }
+    return w;
+}
+__device__ __forceinline__ u64w wait_word(const u64w* p, u64w w, uint32_t flag, DeviceState* st,
+                                          unsigned long long limit) {
+    return fw_ok(w, flag) ? w : wait_word_slow(p, w, flag, st, limit);
 }
 
 // Tensor-parallel exchange (other ranks' kernels write this rank's exchange area over
@@ -131,45 +172,23 @@ __device__ __forceinline__ ulonglong2 ld_ll2(const unsigned long long* p) {
 __device__ __forceinline__ bool ll_ok(const ulonglong2& w, uint32_t flag) {
     return (uint32_t)(w.x >> 32) == flag && (uint32_t)(w.y >> 32) == flag;
 }
-
-// ---------------------------------------------------------------- bulk copies
-//
-// Inputs staged once per phase (records, attention cache rows) come in by TMA bulk copy
-// (cp.async.bulk, global -> shared) completing on an mbarrier, so waiting for them never
-// waits on the weight rings' per-thread cp.async groups (which by then hold the next phase's
-// first units).
-__device__ __forceinline__ void mbar_init(uint32_t mbar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mbar) : "memory");
-}
-__device__ __forceinline__ void bulk_expect(uint32_t mbar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(mbar), "r"(bytes) : "memory");
-}
-// 16-byte aligned addresses, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t mbar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(mbar)
-                 : "memory");
-}
-// Orders this thread's (and, after a barrier, its CTA's) generic-proxy accesses before its
-// following bulk copies: the copied data was written through the generic proxy, and the
-// shared destination was last read through it.
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
-// Wait for phase `parity` of the mbarrier; gives up after `limit` polls (DEV_ERR_TIMEOUT).
-__device__ __noinline__ bool mbar_wait(uint32_t mbar, uint32_t parity, DeviceState* st, unsigned long long limit) {
-    for (unsigned long long it = 0;; ++it) {
-        uint32_t ok;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-            : "=r"(ok)
-            : "r"(mbar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if (it >= limit) {
-            atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
-            return false;
+// Reload the 16-byte aligned pair of words at p (last loaded as w) until both carry `flag`
+// (inline check, out-of-line reload loop).
+__device__ __noinline__ ulonglong2 wait_pair_slow(const u64w* p, ulonglong2 w, uint32_t flag, DeviceState* st,
+                                                  unsigned long long limit) {
+    for (unsigned long long it = 0; !ll_ok(w, flag); ++it) {
+        if (it >= limit || *(volatile int*)&st->error != DEV_OK) {
+            note_timeout(st);
+            break;
         }
         __nanosleep(32);
+        w = ld_ll2(p);
     }
+    return w;
+}
+__device__ __forceinline__ ulonglong2 wait_pair(const u64w* p, ulonglong2 w, uint32_t flag, DeviceState* st,
+                                                unsigned long long limit) {
+    return ll_ok(w, flag) ? w : wait_pair_slow(p, w, flag, st, limit);
 }
 
 // Stream geometry of one phase, kept in shared memory (groups == 0: no weights).
@@ -341,20 +360,74 @@ __device__ __noinline__ PieceSum stream_piece(WarpStream<FMT == Q4M_MIX>& ws, ui
     return r;
 }
 
-// ---------------------------------------------------------------- tensor-parallel input
+// ---------------------------------------------------------------- RMSNorm inputs
 //
-// RMSNorm input after a row-split GEMV on several ranks: h = hsrc + the ranks' partial rows
+// A GEMV input that is RMSNorm(h) * gain is staged by every CTA from the flagged words of h:
+// the records hold h * gain and the returned factor is 1 / sqrt(mean(h^2) + eps), which the
+// epilogue applies (W (h g r) = r W (h g)). Each warp converts whole groups of 128 columns
+// (lane: elements 4 (g * 32 + lane) .. +3); a warp issues the loads of all its groups before
+// its first wait, so it pays one round trip, not one per group. Ends with the CTA synchronised.
+constexpr int STAGE_BG = 4;  // groups per warp in one batch of loads
+
+// h from the flagged words fh (flag `flag`).
+__device__ __noinline__ float stage_x_flag(const u64w* fh, uint32_t flag, const float* norm_w, float eps, int cols,
+                                           uint8_t* rec, float* misc, DeviceState* st, unsigned long long limit) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = (cols + Q4M_KG - 1) / Q4M_KG, n4 = cols / 4;
+    uint32_t* dig = reinterpret_cast<uint32_t*>(rec);
+    float4* prm = reinterpret_cast<float4*>(rec + (size_t)G * 256);
+    float ss = 0.f;
+    for (int g0 = warp; g0 < G; g0 += NW * STAGE_BG) {
+        ulonglong2 wa[STAGE_BG], wb[STAGE_BG];
+        float4 gn[STAGE_BG];
+#pragma unroll
+        for (int k = 0; k < STAGE_BG; ++k) {
+            const int i = (g0 + k * NW) * 32 + lane;
+            if (g0 + k * NW < G && i < n4) {
+                wa[k] = ld_ll2(fh + 4 * (size_t)i);
+                wb[k] = ld_ll2(fh + 4 * (size_t)i + 2);
+                gn[k] = reinterpret_cast<const float4*>(norm_w)[i];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < STAGE_BG; ++k) {
+            const int g = g0 + k * NW;
+            if (g >= G) break;
+            const int i = g * 32 + lane;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < n4) {
+                wa[k] = wait_pair(fh + 4 * (size_t)i, wa[k], flag, st, limit);
+                wb[k] = wait_pair(fh + 4 * (size_t)i + 2, wb[k], flag, st, limit);
+                const float4 h = make_float4(fval(wa[k].x), fval(wa[k].y), fval(wb[k].x), fval(wb[k].y));
+                ss = fmaf(h.x, h.x, ss);
+                ss = fmaf(h.y, h.y, ss);
+                ss = fmaf(h.z, h.z, ss);
+                ss = fmaf(h.w, h.w, ss);
+                v = make_float4(h.x * gn[k].x, h.y * gn[k].y, h.z * gn[k].z, h.w * gn[k].w);
+            }
+            octet_to_records(v, lane, lane >> 3, dig + g * 64, prm + g * 4);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(JINF_FULL_MASK, ss, o);
+    if (lane == 0) misc[warp] = ss;
+    __syncthreads();
+    ss = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) ss += misc[w];
+    return rsqrtf(ss / (float)cols + eps);
+}
+
+// Tensor parallel: h = (the flagged h words fres, flag `flag_res`) + the ranks' partial rows
 // of exchange point `point`, added in rank order (every rank adds the same words in the same
-// order, so every rank holds the same h). Each warp converts whole groups as stage_x does;
-// a lane loads its 4 elements of up to 4 ranks at a time and reloads the words whose flag is
-// not yet this step's, at most `limit` times (then DEV_ERR_TIMEOUT; the step is discarded).
-// h goes to `hout` from the CTA that owns pair 0; the records hold h * gain and the return
-// value is 1 / sqrt(mean(h^2) + eps). Ends with the CTA synchronised.
-// `base`: rank 0's slot of the point in this rank's area; `rs`: words from one slot to the next.
+// order, so every rank holds the same h). A lane loads its 4 elements of up to 4 ranks at a
+// time and reloads the words whose flag is not yet this step's exchange flag `xflag`.
+// `base`: rank 0's slot of the point in this rank's area; `rs`: words from one slot to the
+// next. `fhout` (may be null): where this CTA stores h (flag `flag_out`).
 __device__ __noinline__ float stage_x_tp(const unsigned long long* base, size_t rs, int nranks, float eps,
-                                         unsigned long long limit, const float* hsrc, float* hout, bool store_h,
-                                         const float* norm_w, int cols, uint32_t flag, uint8_t* rec, float* misc,
-                                         DeviceState* st) {
+                                         unsigned long long limit, const u64w* fres, uint32_t flag_res,
+                                         u64w* fhout, uint32_t flag_out, const float* norm_w, int cols, uint32_t xflag,
+                                         uint8_t* rec, float* misc, DeviceState* st) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = (cols + Q4M_KG - 1) / Q4M_KG, n4 = cols / 4;
     uint32_t* dig = reinterpret_cast<uint32_t*>(rec);
@@ -364,8 +437,9 @@ __device__ __noinline__ float stage_x_tp(const unsigned long long* base, size_t 
         const int i = g * 32 + lane;  // 16-byte piece of h: elements 4i .. 4i + 3
         float4 h = make_float4(0.f, 0.f, 0.f, 0.f), gn = h;
         if (i < n4) {
-            h = __ldcg(reinterpret_cast<const float4*>(hsrc) + i);
+            ulonglong2 ha = ld_ll2(fres + 4 * (size_t)i), hb = ld_ll2(fres + 4 * (size_t)i + 2);
             gn = reinterpret_cast<const float4*>(norm_w)[i];
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int r0 = 0; r0 < nranks; r0 += 4) {
                 ulonglong2 w[4][2];
 #pragma unroll
@@ -380,22 +454,21 @@ __device__ __noinline__ float stage_x_tp(const unsigned long long* base, size_t 
                 for (int k = 0; k < 4; ++k) {
                     if (r0 + k >= nranks) break;
                     const unsigned long long* p = base + (size_t)(r0 + k) * rs + 4 * (size_t)i;
-                    for (unsigned long long it = 0; !(ll_ok(w[k][0], flag) && ll_ok(w[k][1], flag)); ++it) {
-                        if (it >= limit || *(volatile int*)&st->error != DEV_OK) {
-                            atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
-                            break;
-                        }
-                        __nanosleep(32);
-                        w[k][0] = ld_ll2(p);
-                        w[k][1] = ld_ll2(p + 2);
-                    }
-                    h.x += __uint_as_float((uint32_t)w[k][0].x);
-                    h.y += __uint_as_float((uint32_t)w[k][0].y);
-                    h.z += __uint_as_float((uint32_t)w[k][1].x);
-                    h.w += __uint_as_float((uint32_t)w[k][1].y);
+                    w[k][0] = wait_pair(p, w[k][0], xflag, st, limit);
+                    w[k][1] = wait_pair(p + 2, w[k][1], xflag, st, limit);
+                    acc.x += fval(w[k][0].x);
+                    acc.y += fval(w[k][0].y);
+                    acc.z += fval(w[k][1].x);
+                    acc.w += fval(w[k][1].y);
                 }
             }
-            if (store_h) reinterpret_cast<float4*>(hout)[i] = h;
+            ha = wait_pair(fres + 4 * (size_t)i, ha, flag_res, st, limit);
+            hb = wait_pair(fres + 4 * (size_t)i + 2, hb, flag_res, st, limit);
+            h = make_float4(fval(ha.x) + acc.x, fval(ha.y) + acc.y, fval(hb.x) + acc.z, fval(hb.y) + acc.w);
+            if (fhout) {
+                st_ll2(fhout + 4 * (size_t)i, fword(h.x, flag_out), fword(h.y, flag_out));
+                st_ll2(fhout + 4 * (size_t)i + 2, fword(h.z, flag_out), fword(h.w, flag_out));
+            }
             ss = fmaf(h.x, h.x, ss);
             ss = fmaf(h.y, h.y, ss);
             ss = fmaf(h.z, h.z, ss);
@@ -416,80 +489,85 @@ __device__ __noinline__ float stage_x_tp(const unsigned long long* base, size_t 
 
 // ---------------------------------------------------------------- input records
 //
-// A GEMV phase whose input was produced earlier in the step receives it as digit records
-// (q4m_device.cuh) written by the producing phase's epilogue, so its CTAs only copy them
-// (one L2 round trip) instead of each converting the whole input. For an RMSNorm input the
-// records hold h * gain and the producer also leaves the sum of h^2 of every tile pair;
-// every warp adds those up in the same fixed order (deterministic) for the norm factor.
+// A GEMV phase whose input was produced earlier in the step (the attention output, the FFN
+// activation) receives it as digit records (q4m_device.cuh) written by the producing phase,
+// as flagged words in the record layout (xrec_bytes(G) / 4 of them): its CTAs only copy them
+// into shared memory instead of each converting the whole input.
 
-// Copy the records (xrec_bytes(G)) into shared memory with one bulk copy on `mbar` (phase
-// `parity`); returns the epilogue factor (1 / sqrt(mean(h^2) + eps) for a norm input, else
-// 1). Every thread returns once the records are in shared memory.
-__device__ __noinline__ float stage_records(const uint8_t* rec, const float* ssp, int n_ss, int cols, float eps,
-                                           int G, uint8_t* xbase, uint32_t mbar, uint32_t parity, DeviceState* st,
-                                           unsigned long long limit) {
-    const int tid = threadIdx.x, lane = tid & 31;
-    if (tid == 0) {
-        fence_proxy_async();
-        bulk_expect(mbar, (uint32_t)xrec_bytes(G));
-        bulk_g2s(smem_u32(xbase), rec, (uint32_t)xrec_bytes(G), mbar);
-    }
-    float s = 0.f;
-    if (ssp)
-        for (int i = lane; i < n_ss; i += 32) s += __ldcg(ssp + i);
-    float fac = 1.0f;
-    if (ssp) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(JINF_FULL_MASK, s, o);
-        fac = rsqrtf(s / (float)cols + eps);
-    }
-    mbar_wait(mbar, parity, st, limit);
-    return fac;
+// Block of word pair k of a G-group record buffer: pair k holds digit words 2k, 2k + 1
+// (block 4 (2k / 64) + (2k % 64) / 16) while 2k < 64 G, then param words (block
+// 4 (i / 16) + (i % 16) / 4, i = 2k - 64 G).
+__device__ __forceinline__ int rec_pair_block(int k, int G) {
+    const int w = 2 * k;
+    if (w < 64 * G) return 4 * (w >> 6) + ((w & 63) >> 4);
+    const int i = w - 64 * G;
+    return 4 * (i >> 4) + ((i & 15) >> 2);
 }
 
-// EPI_RESID of one tile pair with records for the next phase, by a whole warp: lanes q < 16
-// hold rows 2q, 2q+1 (v0, v1, already scaled). h += W x is stored; the pair's sum of h^2 and
-// the records of h * gain (the pair is one 32-element block of the next input) are written.
-__device__ __noinline__ void resid_records(const StepPhase& d, int pr, float v0, float v1) {
-    const int lane = threadIdx.x & 31, q = lane & 15, row = pr * Q4M_PAIR_ROWS + 2 * q;
-    float h0 = 0.f, h1 = 0.f;
-    if (lane < 16 && row < d.rows) {
-        h0 = __ldcg(d.y + row) + v0;
-        d.y[row] = h0;
-        if (row + 1 < d.rows) {
-            h1 = __ldcg(d.y + row + 1) + v1;
-            d.y[row + 1] = h1;
+// Copy the records of G groups (nb real 32-element blocks; the padding blocks of the last
+// group are never written and get zero records) from the flagged words fr into shared
+// memory; every thread issues up to 8 pair loads before its first wait. Ends with the CTA
+// synchronised.
+__device__ __noinline__ void stage_records_flag(const u64w* fr, uint32_t flag, int G, int nb, uint8_t* xbase,
+                                                DeviceState* st, unsigned long long limit) {
+    constexpr int B = 8;
+    const int n2 = G * 40;  // 16-byte pairs of words
+    uint2* dst = reinterpret_cast<uint2*>(xbase);
+    for (int k0 = threadIdx.x; k0 < n2; k0 += STEP_THREADS * B) {
+        ulonglong2 w[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const int k = k0 + b * STEP_THREADS;
+            if (k < n2 && rec_pair_block(k, G) < nb) w[b] = ld_ll2(fr + 2 * (size_t)k);
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const int k = k0 + b * STEP_THREADS;
+            if (k < n2) {
+                if (rec_pair_block(k, G) < nb) {
+                    w[b] = wait_pair(fr + 2 * (size_t)k, w[b], flag, st, limit);
+                    dst[k] = make_uint2((uint32_t)w[b].x, (uint32_t)w[b].y);
+                } else {
+                    dst[k] = make_uint2(0u, 0u);
+                }
+            }
         }
     }
-    float s = fmaf(h0, h0, h1 * h1);
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) s += __shfl_xor_sync(JINF_FULL_MASK, s, o);
-    if (lane == 0) d.ss_out[pr] = s;
-    // octet layout: lane L < 8 takes elements 4L .. 4L+3 (rows of lanes 2L and 2L+1)
-    const int src = 2 * (lane & 7);
-    const float e0 = __shfl_sync(JINF_FULL_MASK, h0, src), e1 = __shfl_sync(JINF_FULL_MASK, h1, src);
-    const float e2 = __shfl_sync(JINF_FULL_MASK, h0, src + 1), e3 = __shfl_sync(JINF_FULL_MASK, h1, src + 1);
-    float4 gn = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (lane < 8 && pr * Q4M_PAIR_ROWS + 4 * lane < d.rows)
-        gn = reinterpret_cast<const float4*>(d.gain_out + pr * Q4M_PAIR_ROWS)[lane];
-    uint32_t* dig = reinterpret_cast<uint32_t*>(d.rec_out);
-    float4* prm = reinterpret_cast<float4*>(d.rec_out + (size_t)d.groups_out * 256);
-    octet_to_records(make_float4(e0 * gn.x, e1 * gn.y, e2 * gn.z, e3 * gn.w), lane, pr & 3, dig + (pr >> 2) * 64,
-                     prm + (pr >> 2) * 4, lane < 8);
+    __syncthreads();
 }
 
-// Records of blocks [b0, b0 + nb) of the next input from fp32 values in shared memory
+// Records of one 32-element block held by an octet of lanes (octet_digits), as flagged words:
+// `fdig` is the group's 64 digit words and `fprm` its 16 param words in a record buffer of
+// flagged words, j the block within the group. All 32 lanes call it; octets with `store` write.
+__device__ __forceinline__ void octet_to_records_flag(float4 v, int lane, int j, u64w* fdig, u64w* fprm, uint32_t flag,
+                                                      bool store) {
+    const int q = lane & 7;
+    const OctetDigits o = octet_digits(v);
+    if (!store) return;
+    st_w(fdig + rec_word_hi(j, q), fword_u(o.H, flag));
+    st_w(fdig + rec_word_lo(j, q), fword_u(o.L, flag));
+    if (q == 0) {
+        const float ia = o.amax / XREC_DIGIT_MAX;
+        st_ll2(fprm + 4 * j, fword_u((uint32_t)(-8 * o.sh), flag), fword_u((uint32_t)(-8 * o.sl), flag));
+        st_ll2(fprm + 4 * j + 2, fword(ia, flag), fword(ia * 0.0625f, flag));
+    }
+}
+
+// Flagged records of blocks [b0, b0 + nb) of the next input from fp32 values in shared memory
 // (vals[32 * i] = first element of block b0 + i), by the whole CTA (4 blocks per warp pass).
-__device__ __noinline__ void blocks_to_records(const float* vals, int b0, int nb, int groups_out, uint8_t* rec_out) {
+// `fout`: the record buffer of a `groups_out`-group input.
+__device__ __noinline__ void blocks_to_records_flag(const float* vals, int b0, int nb, int groups_out, u64w* fout,
+                                                    uint32_t flag) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint32_t* dig = reinterpret_cast<uint32_t*>(rec_out);
-    float4* prm = reinterpret_cast<float4*>(rec_out + (size_t)groups_out * 256);
+    u64w* fdig = fout;
+    u64w* fprm = fout + (size_t)groups_out * 64;
     for (int i0 = warp * 4; i0 < nb; i0 += NW * 4) {
         const int i = i0 + (lane >> 3);
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < nb) v = reinterpret_cast<const float4*>(vals + 32 * i)[lane & 7];
         const int blk = b0 + i;
-        octet_to_records(v, lane, blk & 3, dig + (blk >> 2) * 64, prm + (blk >> 2) * 4, i < nb);
+        octet_to_records_flag(v, lane, blk & 3, fdig + (size_t)(blk >> 2) * 64, fprm + (size_t)(blk >> 2) * 16, flag,
+                              i < nb);
     }
 }
 
@@ -502,7 +580,9 @@ __device__ __noinline__ void blocks_to_records(const float* vals, int b0, int nb
 // fixed order by the CTAs that own the output blocks. Within a CTA the positions go in
 // blocks of 16 warps x ATTN_PW: lanes own head dims, so a warp's load of a cache row is one
 // contiguous 256-byte read (the rows were pulled into L2 during the QKV phase), every load
-// of a block is issued before any arithmetic, and an online softmax joins the blocks.
+// of a block is issued before any arithmetic, and an online softmax joins the blocks. The
+// rows of earlier positions are in the cache since earlier steps; the row of the step's own
+// position comes from the QKV phase's flagged words, and so does q.
 
 struct AttnGeom {
     int kvh, sp, S, p0, p1;
@@ -530,6 +610,11 @@ template <>
 struct HalfVec<4> {
     uint2 r;
     __device__ __forceinline__ void load(const __half* p) { r = __ldcg(reinterpret_cast<const uint2*>(p)); }
+    // the lane's dims of the step's own row: flagged words fw (two halves per word)
+    __device__ __forceinline__ void load_flag(const u64w* fw, uint32_t flag, DeviceState* st, unsigned long long lim) {
+        const ulonglong2 w = wait_pair(fw, ld_ll2(fw), flag, st, lim);
+        r = make_uint2((uint32_t)w.x, (uint32_t)w.y);
+    }
     __device__ __forceinline__ void zero() { r = make_uint2(0u, 0u); }
     __device__ __forceinline__ float get(int d) const {
         const __half2 h = *reinterpret_cast<const __half2*>(d < 2 ? &r.x : &r.y);
@@ -540,6 +625,9 @@ template <>
 struct HalfVec<2> {
     uint32_t r;
     __device__ __forceinline__ void load(const __half* p) { r = __ldcg(reinterpret_cast<const unsigned int*>(p)); }
+    __device__ __forceinline__ void load_flag(const u64w* fw, uint32_t flag, DeviceState* st, unsigned long long lim) {
+        r = (uint32_t)wait_word(fw, ld_w(fw), flag, st, lim);
+    }
     __device__ __forceinline__ void zero() { r = 0u; }
     __device__ __forceinline__ float get(int d) const {
         const __half2 h = *reinterpret_cast<const __half2*>(&r);
@@ -547,13 +635,25 @@ struct HalfVec<2> {
     }
 };
 
-// One CTA's split [p0, p1) of kv head attention, after the QKV phase has finished: q of the
-// GQ heads of the kv head at `q`, cache rows at kb / vb. Leaves either the normalised output
-// in `outs` ([GQ][HD], shared memory; `part` null) or the split's partial (acc, m, l) in
-// `part` ([GQ][HD + 2], global). Shared scratch at `xbase`: step_xstage_bytes covers it.
+// The flagged inputs of one kv head's attention: q of its GQ heads and the K and V rows of the
+// step's own position `pos` (the flag of the QKV phase).
+struct AttnIn {
+    const u64w* fq;  // [GQ][HD] q words of the kv head
+    const u64w* fk;  // [HD / 2] K words of position pos
+    const u64w* fv;  // [HD / 2] V words
+    uint32_t flag;
+    int pos;
+    DeviceState* st;
+    unsigned long long limit;
+};
+
+// One CTA's split [p0, p1) of kv head attention: cache rows at kb / vb (earlier positions)
+// and the flagged inputs `in`. Leaves either the normalised output in `outs` ([GQ][HD],
+// shared memory; `part` null) or the split's partial (acc, m, l) as flagged words (flag
+// `pflag`) in `part` ([GQ][HD + 2]). Shared scratch at `xbase`: step_xstage_bytes covers it.
 template <int HD, int GQ>
-__device__ __noinline__ void attn_split(const float* q, const __half* kb, const __half* vb, int p0, int p1,
-                                        uint8_t* xbase, float* part, float* outs) {
+__device__ __noinline__ void attn_split(const AttnIn in, const __half* kb, const __half* vb, int p0, int p1,
+                                        uint8_t* xbase, u64w* part, uint32_t pflag, float* outs) {
     constexpr int VD = HD / 32;                               // head dims per lane
     constexpr int PW = GQ * VD >= 32 ? ATTN_PW / 2 : ATTN_PW;  // positions per warp and block (registers)
     constexpr int BLK = NW * PW;                              // positions per block
@@ -562,15 +662,41 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
     float* ml_s = w_s + GQ * BLK;                   // [GQ][4]: m, l, correction
     float* red_s = ml_s + 4 * ATTN_MAX_GROUP;       // [NW][GQ][HD] per-warp p.v sums
     const float scale = rsqrtf((float)HD);
+    // the first block's cache rows are requested before q is awaited
+    HalfVec<VD> kr[PW], vr[PW];
+    auto load_rows = [&](int b0, int n) {
+#pragma unroll
+        for (int k = 0; k < PW; ++k) {
+            const int j = warp + NW * k;
+            if (j < n && b0 + j != in.pos) {
+                kr[k].load(kb + (size_t)(b0 + j) * HD + lane * VD);
+                vr[k].load(vb + (size_t)(b0 + j) * HD + lane * VD);
+            } else {
+                kr[k].zero();
+                vr[k].zero();
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < PW; ++k) {
+            const int j = warp + NW * k;
+            if (j < n && b0 + j == in.pos) {
+                kr[k].load_flag(in.fk + lane * VD / 2, in.flag, in.st, in.limit);
+                vr[k].load_flag(in.fv + lane * VD / 2, in.flag, in.st, in.limit);
+            }
+        }
+    };
+    if (p0 < p1) load_rows(p0, min(BLK, p1 - p0));
     float qr[GQ][VD];
 #pragma unroll
     for (int g = 0; g < GQ; ++g) {
+        const u64w* fq = in.fq + (size_t)g * HD + lane * VD;
         if constexpr (VD == 4) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(q + g * HD) + lane);
-            qr[g][0] = v.x * scale; qr[g][1] = v.y * scale; qr[g][2] = v.z * scale; qr[g][3] = v.w * scale;
+            const ulonglong2 a = wait_pair(fq, ld_ll2(fq), in.flag, in.st, in.limit);
+            const ulonglong2 b = wait_pair(fq + 2, ld_ll2(fq + 2), in.flag, in.st, in.limit);
+            qr[g][0] = fval(a.x) * scale; qr[g][1] = fval(a.y) * scale; qr[g][2] = fval(b.x) * scale; qr[g][3] = fval(b.y) * scale;
         } else {
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(q + g * HD) + lane);
-            qr[g][0] = v.x * scale; qr[g][1] = v.y * scale;
+            const ulonglong2 a = wait_pair(fq, ld_ll2(fq), in.flag, in.st, in.limit);
+            qr[g][0] = fval(a.x) * scale; qr[g][1] = fval(a.y) * scale;
         }
     }
     if (tid < GQ) {
@@ -584,19 +710,7 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
         for (int d = 0; d < VD; ++d) acc[g][d] = 0.f;
     for (int b0 = p0; b0 < p1; b0 += BLK) {
         const int n = min(BLK, p1 - b0);
-        // every K and V row piece of this warp's positions warp, warp + 16, ... at once
-        HalfVec<VD> kr[PW], vr[PW];
-#pragma unroll
-        for (int k = 0; k < PW; ++k) {
-            const int j = warp + NW * k;
-            if (j < n) {
-                kr[k].load(kb + (size_t)(b0 + j) * HD + lane * VD);
-                vr[k].load(vb + (size_t)(b0 + j) * HD + lane * VD);
-            } else {
-                kr[k].zero();
-                vr[k].zero();
-            }
-        }
+        if (b0 != p0) load_rows(b0, n);
         // scores: each lane's dims, summed over the warp
 #pragma unroll
         for (int k = 0; k < PW; ++k) {
@@ -667,21 +781,304 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
         for (int w = 0; w < NW; ++w) a += red_s[w * GQ * HD + o];
         const int g = o / HD, dd = o % HD;
         if (part) {
-            part[g * (HD + 2) + dd] = a;
-            if (dd == 0) {
-                part[g * (HD + 2) + HD] = p1 > p0 ? ml_s[g * 4] : -INFINITY;  // an empty split
-                part[g * (HD + 2) + HD + 1] = ml_s[g * 4 + 1];
-            }
+            st_w(part + g * (HD + 2) + dd, fword(a, pflag));
+            if (dd == 0)
+                st_ll2(part + g * (HD + 2) + HD, fword(p1 > p0 ? ml_s[g * 4] : -INFINITY, pflag),  // an empty split
+                       fword(ml_s[g * 4 + 1], pflag));
         } else {
             outs[o] = a / ml_s[g * 4 + 1];
         }
     }
 }
 
+// ---------------------------------------------------------------- phase pieces (out of line:
+// each gets a register allocation of its own, and the kernel's loop keeps a small live state)
+
+// Attention phase of one CTA: its split (kv head, positions) of the context, then, for the
+// splits that own output blocks (split sp owns blocks sp, sp + S, ...), the merge of each of
+// their blocks from all S partials of the kv head, in split order (deterministic), written as
+// records of the o phase's input.
+__device__ __noinline__ void attn_phase(const StepParams& P, const StepPhase& d, int pos, uint32_t fl_in,
+                                        uint32_t fl_out, uint8_t* xbase, float* outs_s) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    DeviceState* st = P.st;
+    AttnGeom a;
+    if (!attn_geom(pos, P.n_kv_heads, P.attn_smax, blockIdx.x, a)) return;
+    const int hd = P.head_dim, gq = P.n_heads / P.n_kv_heads;
+    AttnIn in;
+    in.fq = d.fin + (size_t)a.kvh * gq * hd;
+    in.fk = d.fkv + (size_t)a.kvh * (hd / 2);
+    in.fv = d.fkv + (size_t)P.nk / 2 + (size_t)a.kvh * (hd / 2);
+    in.flag = fl_in;
+    in.pos = pos;
+    in.st = st;
+    in.limit = P.spin_limit;
+    const __half* kb = d.kcache + (size_t)a.kvh * P.max_ctx * hd;
+    const __half* vb = d.vcache + (size_t)a.kvh * P.max_ctx * hd;
+    const size_t stride = (size_t)ATTN_MAX_GROUP * (hd + 2);  // words per split
+    u64w* gpart = a.S > 1 ? P.attn_part + ((size_t)a.kvh * ATTN_MAX_SPLIT + a.sp) * stride : nullptr;
+#define JINF_ATTN_SPLIT(HD_, GQ_) attn_split<HD_, GQ_>(in, kb, vb, a.p0, a.p1, xbase, gpart, fl_out, outs_s)
+    if (hd == 64) {
+        if (gq == 8) JINF_ATTN_SPLIT(64, 8);
+        else if (gq == 4) JINF_ATTN_SPLIT(64, 4);
+        else if (gq == 2) JINF_ATTN_SPLIT(64, 2);
+        else JINF_ATTN_SPLIT(64, 1);
+    } else {
+        if (gq == 8) JINF_ATTN_SPLIT(128, 8);
+        else if (gq == 4) JINF_ATTN_SPLIT(128, 4);
+        else if (gq == 2) JINF_ATTN_SPLIT(128, 2);
+        else JINF_ATTN_SPLIT(128, 1);
+    }
+#undef JINF_ATTN_SPLIT
+    const int nblk = gq * hd / 32;  // 32-element output blocks of this kv head
+    if (a.S == 1) {
+        __syncthreads();
+        blocks_to_records_flag(outs_s, a.kvh * nblk, nblk, d.groups_out, d.fout, fl_out);
+        return;
+    }
+    if (a.sp >= nblk) return;
+    __syncthreads();  // every thread is done with the split's scratch
+    const u64w* base = P.attn_part + (size_t)a.kvh * ATTN_MAX_SPLIT * stride;
+    float* ml = reinterpret_cast<float*>(xbase);  // [S][2] (m, l) of the block's query head
+    float* av = ml + 2 * ATTN_MAX_SPLIT;           // [S][32] accumulators of the block
+    float* ew = av + 32 * ATTN_MAX_SPLIT;          // [S] split weights e^(m_s - M)
+    for (int b = a.sp; b < nblk; b += a.S) {
+        const int g = b * 32 / hd, dd0 = b * 32 % hd;
+        {  // every partial load of the thread before any wait (S <= 64: at most 4 + 2)
+            u64w t4[4], mw = 0, lw = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int t = tid + k * STEP_THREADS;
+                t4[k] = t < a.S * 32 ? ld_w(base + (t >> 5) * stride + g * (hd + 2) + dd0 + (t & 31)) : 0ull;
+            }
+            if (tid < a.S) {
+                mw = ld_w(base + tid * stride + g * (hd + 2) + hd);
+                lw = ld_w(base + tid * stride + g * (hd + 2) + hd + 1);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int t = tid + k * STEP_THREADS;
+                if (t < a.S * 32) {
+                    const u64w* pw = base + (t >> 5) * stride + g * (hd + 2) + dd0 + (t & 31);
+                    av[t] = fval(wait_word(pw, t4[k], fl_out, st, P.spin_limit));
+                }
+            }
+            if (tid < a.S) {
+                ml[2 * tid] = fval(wait_word(base + tid * stride + g * (hd + 2) + hd, mw, fl_out, st, P.spin_limit));
+                ml[2 * tid + 1] = fval(wait_word(base + tid * stride + g * (hd + 2) + hd + 1, lw, fl_out, st, P.spin_limit));
+            }
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // lanes own splits lane, lane + 32: the max, the weights and their sum in parallel
+            const float ma = lane < a.S ? ml[2 * lane] : -INFINITY;
+            const float mb = lane + 32 < a.S ? ml[2 * (lane + 32)] : -INFINITY;
+            const float M = warp_max(fmaxf(ma, mb));
+            const float ea = ma == -INFINITY ? 0.f : expf(ma - M);  // 0: an empty split
+            const float eb = mb == -INFINITY ? 0.f : expf(mb - M);
+            const float L = warp_sum((lane < a.S ? ml[2 * lane + 1] * ea : 0.f) +
+                                     (lane + 32 < a.S ? ml[2 * (lane + 32) + 1] * eb : 0.f));
+            if (lane < a.S) ew[lane] = ea;
+            if (lane + 32 < a.S) ew[lane + 32] = eb;
+            __syncwarp();
+            float v = 0.f;
+            for (int s2 = 0; s2 < a.S; ++s2) v = fmaf(ew[s2], av[s2 * 32 + lane], v);
+            v /= L;
+            const int blk = a.kvh * nblk + b;  // block of the o projection's input
+            // octet layout: lane q < 8 takes elements 4q .. 4q+3
+            const int src = 4 * (lane & 7);
+            const float4 x = make_float4(__shfl_sync(JINF_FULL_MASK, v, src), __shfl_sync(JINF_FULL_MASK, v, src + 1),
+                                         __shfl_sync(JINF_FULL_MASK, v, src + 2), __shfl_sync(JINF_FULL_MASK, v, src + 3));
+            octet_to_records_flag(x, lane, blk & 3, d.fout + (size_t)(blk >> 2) * 64,
+                                  d.fout + (size_t)d.groups_out * 64 + (size_t)(blk >> 2) * 16, fl_out, lane < 8);
+        }
+        __syncthreads();  // the scratch is reused by the next block
+    }
+}
+
+// Epilogue inputs that do not depend on the GEMV, by the threads from 32 up while warp 0
+// starts the input staging: the residual rows of an EPI_RESID phase (flagged words of the
+// phase d.tag_res), the RoPE factors of an EPI_QKV phase (cosine at the even row of a q or k
+// pair, sine at the odd row). Rows [prow0, prow0 + nprow) -> outs_s.
+__device__ __noinline__ void prepare_epilogue(const StepParams& P, const StepPhase& d, int pos, uint32_t fepoch,
+                                              int prow0, int nprow, float* outs_s) {
+    const int tid = threadIdx.x;
+    if (d.epi == EPI_RESID) {
+        const uint32_t fl_res = step_flag(fepoch, d.tag_res);
+        for (int i = tid - 32; i < nprow; i += STEP_THREADS - 32) {
+            const int row = prow0 + i;
+            outs_s[i] = row < d.rows ? fval(wait_word(d.fres + row, ld_w(d.fres + row), fl_res, P.st, P.spin_limit)) : 0.f;
+        }
+    } else {
+        for (int i = tid - 32; i < nprow; i += STEP_THREADS - 32) {
+            const int row = prow0 + i;
+            if ((i & 1) == 0 && row < P.nq + P.nk) {
+                float cs, sn;
+                rope_pair(row < P.nq ? row : row - P.nq, pos, P.rope_base, P.head_dim, cs, sn);
+                outs_s[i] = cs;
+                outs_s[i + 1] = sn;
+            }
+        }
+    }
+}
+
+// The embedding row as flagged h words (the residual stream the first o phase adds to).
+__device__ __noinline__ void store_h_flag(const float* emb, int cols, u64w* fout_h, uint32_t flag) {
+    for (int i = threadIdx.x; i < cols / 2; i += STEP_THREADS) {
+        const float2 e = reinterpret_cast<const float2*>(emb)[i];
+        st_ll2(fout_h + 2 * (size_t)i, fword(e.x, flag), fword(e.y, flag));
+    }
+}
+
+// Tensor-parallel RMSNorm input: the h of phase d.tag_res plus the ranks' partials of exchange
+// point d.xin; the CTA that owns pair 0 stores the new h (flag fl_out).
+__device__ __noinline__ float stage_tp(const StepParams& P, const StepPhase& d, int t0, uint32_t fepoch,
+                                       uint32_t fl_out, uint8_t* xbase, float* misc) {
+    const unsigned long long ep = *(volatile unsigned long long*)P.xpeer[P.tp_rank];
+    return stage_x_tp(xchg_data(P, P.tp_rank, d.xin, (unsigned)(ep & 1ull), 0), (size_t)(P.x_slot / 8), P.tp_size,
+                      P.eps, P.spin_limit, d.fres, step_flag(fepoch, d.tag_res), t0 == 0 ? d.fout_h : nullptr, fl_out,
+                      d.norm_w, d.cols, (uint32_t)(ep + 1ull), xbase, misc, P.st);
+}
+
+// What a finished tile pair's epilogue needs besides the phase.
+struct EpiCtx {
+    float fac;        // 1 / rms of a normalised input, else 1
+    int pos;
+    uint32_t fepoch;  // the step's flag epoch
+    uint32_t fl_out;  // flag of this phase's words
+    int t0, prow0;    // the CTA's first pair and its first row
+    bool pre;         // the epilogue inputs were prepared into outs_s (prepare_epilogue)
+};
+
+// The running argmax of the LM-head rows this warp finished.
+struct ArgMax {
+    float v;
+    int i;
+};
+
+// The epilogue of a finished pair, by a whole warp: lanes q < 16 hold rows 2q, 2q + 1 (v0, v1,
+// before the input's norm factor).
+template <bool TP>
+__device__ __noinline__ void finish_pair(const StepParams& P, const StepPhase& d, const EpiCtx& ec, int pr, float v0,
+                                         float v1, float* outs_s, ArgMax& am) {
+    const int lane = threadIdx.x & 31, q = lane & 15, row = pr * Q4M_PAIR_ROWS + 2 * q;
+    v0 *= ec.fac;
+    v1 *= ec.fac;
+    if (TP && d.epi == EPI_PARTIAL) {
+        // this rank's partial rows into its slot of every rank's exchange area
+        if (lane < 16 && row < d.rows) {  // (rows: a multiple of 32)
+            const unsigned long long ep = *(volatile unsigned long long*)P.xpeer[P.tp_rank];
+            const uint32_t flag = (uint32_t)(ep + 1ull);
+            const unsigned long long w0 = ll_word(v0, flag), w1 = ll_word(v1, flag);
+            for (int r = 0; r < P.tp_size; ++r) st_ll2(xchg_data(P, r, d.xout, (unsigned)(ep & 1ull), P.tp_rank) + row, w0, w1);
+        }
+        return;
+    }
+    if (d.epi == EPI_GATEUP) {
+        // the activation goes to shared memory; whole blocks become records after the phase
+        if (lane < 16) outs_s[(pr - ec.t0) * 16 + q] = row < d.rows ? v0 / (1.0f + expf(-v0)) * v1 : 0.f;
+        return;
+    }
+    if (lane >= 16 || row >= d.rows) return;
+    if (d.epi == EPI_RESID) {
+        // h += W x, the reference's residual add (src/engine.cpp:470-472, 505-507)
+        float h0, h1;
+        if (ec.pre) {
+            h0 = outs_s[row - ec.prow0];
+            h1 = outs_s[row + 1 - ec.prow0];
+        } else {
+            const ulonglong2 w = wait_pair(d.fres + row, ld_ll2(d.fres + row), step_flag(ec.fepoch, d.tag_res), P.st,
+                                           P.spin_limit);
+            h0 = fval(w.x);
+            h1 = fval(w.y);
+        }
+        st_ll2(d.fout + row, fword(h0 + v0, ec.fl_out), fword(h1 + v1, ec.fl_out));
+    } else if (d.epi == EPI_QKV) {
+        // RoPE on q and k (reference cuda/rope_kernel.cu); q as flagged words, K and V into the
+        // fp16 cache at pos and as flagged words for this step's attention
+        float o0 = v0, o1 = v1;
+        if (row < P.nq + P.nk) {
+            float cs, sn;
+            if (ec.pre) {
+                cs = outs_s[row - ec.prow0];
+                sn = outs_s[row + 1 - ec.prow0];
+            } else {
+                rope_pair(row < P.nq ? row : row - P.nq, ec.pos, P.rope_base, P.head_dim, cs, sn);
+            }
+            o0 = v0 * cs - v1 * sn;
+            o1 = v0 * sn + v1 * cs;
+        }
+        if (row < P.nq) {
+            st_ll2(d.fout + row, fword(o0, ec.fl_out), fword(o1, ec.fl_out));
+        } else {
+            const bool isk = row < P.nq + P.nk;
+            const int rr = isk ? row - P.nq : row - P.nq - P.nk;
+            const int kvh = rr / P.head_dim, dd = rr % P.head_dim;
+            const __half2 hv = __floats2half2_rn(o0, o1);
+            *reinterpret_cast<__half2*>((isk ? d.kcache : d.vcache) + ((size_t)kvh * P.max_ctx + ec.pos) * P.head_dim + dd) =
+                hv;
+            st_w(d.fkv + (isk ? 0 : P.nk / 2) + rr / 2, fword_u(*reinterpret_cast<const uint32_t*>(&hv), ec.fl_out));
+        }
+    } else {  // EPI_LMHEAD: logits and the running argmax (first maximum)
+        d.y[row] = v0;
+        if (v0 > am.v) {
+            am.v = v0;
+            am.i = row;
+        }
+        if (row + 1 < d.rows) {
+            d.y[row + 1] = v1;
+            if (v1 > am.v) {
+                am.v = v1;
+                am.i = row + 1;
+            }
+        }
+    }
+}
+
+// The last CTA to leave finishes the step: the argmax (tensor parallel: exchanged with every
+// rank) becomes the next input token, the position and the flag epoch advance, the exit
+// counter is cleared for the next launch.
+template <bool TP>
+__device__ __noinline__ void finish_step(const StepParams& P, int pos, uint32_t fepoch) {
+    DeviceState* st = P.st;
+    __threadfence();
+    u64 b = P.with_argmax ? atomicAdd(&st->best, 0ull) : 0ull;
+    const bool tp = TP && P.tp_size > 1;
+    const unsigned long long ep = tp ? *(volatile unsigned long long*)P.xpeer[P.tp_rank] : 0ull;
+    const unsigned par = (unsigned)(ep & 1ull);
+    if (tp) {
+        // every rank's argmax key to every rank, then the largest (the key order puts the
+        // lower global index first on ties). Steps without an LM head exchange a zero key,
+        // so that every rank's step ends only after all writes into its area have landed.
+        u64* keys = reinterpret_cast<u64*>(P.xpeer[P.tp_rank] + P.x_keys) + par * STEP_MAX_TP;
+        for (int r = 0; r < P.tp_size; ++r)
+            reinterpret_cast<volatile u64*>(P.xpeer[r] + P.x_keys)[par * STEP_MAX_TP + P.tp_rank] = b;
+        __threadfence_system();
+        for (int r = 0; r < P.tp_size; ++r)
+            atomicAdd_system(reinterpret_cast<unsigned long long*>(P.xpeer[r] + P.x_keycnt), 1ull);
+        if (wait_ge_sys(reinterpret_cast<const unsigned long long*>(P.xpeer[P.tp_rank] + P.x_keycnt),
+                        (ep + 1ull) * (unsigned long long)P.tp_size, st, P.spin_limit)) {
+            for (int r = 0; r < P.tp_size; ++r) {
+                const u64 k = __ldcg(keys + r);
+                b = k > b ? k : b;
+            }
+        }
+    }
+    if (P.with_argmax) {
+        st->argmax_token = b ? (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull)) : 0;
+        st->token = st->argmax_token;
+        st->best = 0ull;
+    }
+    st->pos = pos + 1;
+    st->epoch = fepoch + 1u;
+    P.done[0] = 0u;
+    if (tp) *reinterpret_cast<volatile unsigned long long*>(P.xpeer[P.tp_rank]) = ep + 1ull;
+}
+
 }  // namespace
 
 template <int FMT, int NBUF, bool TP>
-__global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
+__global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const __grid_constant__ StepParams P) {
     constexpr int UB = q4m_unit_bytes(FMT);  // ring slot bytes (the largest unit of a mixed model)
     constexpr bool MIXED = FMT == Q4M_MIX;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -689,13 +1086,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     //                 outputs to convert 4 KB | phase descriptor 2 x 256 B | phase infos | rings]
     uint8_t* xbase = smem;
     float* misc = reinterpret_cast<float*>(smem + P.xstage_bytes);        // 64 floats of reductions
-    int* flags = reinterpret_cast<int*>(smem + P.xstage_bytes + 256);     // [0..1] go, [2] attention last
+    int* flags = reinterpret_cast<int*>(smem + P.xstage_bytes + 256);     // [0..1] go
     u64* wkeys = reinterpret_cast<u64*>(smem + P.xstage_bytes + 256 + 64);  // [NW] argmax keys
     int* ftile = reinterpret_cast<int*>(smem + P.xstage_bytes + 256 + 192);  // [NW] tile of a warp's first piece
     int* fmid = ftile + NW;                                                  // [NW] first piece starts mid-tile
     float* part_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768);   // [NW][2][32] partial rows
     float* outs_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768 + 4096);  // [1024] outputs to convert
-    const uint32_t mbar_rec = smem_u32(smem + P.xstage_bytes + 576);  // bulk copies of input records
     StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 8192);  // [2] descriptors
     PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 8192 + 512);
     const uint32_t ring_base = smem_u32(pinfo + ((P.n_phases + 1) & ~1));
@@ -704,10 +1100,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     const int C = gridDim.x;
     DeviceState* st = P.st;
     const int pos = *(volatile int*)&st->pos;
-    // tensor parallel: this step's epoch (steps finished so far, the same on every rank; only
-    // the finalizer advances it, after every CTA's last use). Re-read where needed rather
-    // than kept live through the kernel.
-    auto epoch = [&]() -> unsigned long long { return *(volatile unsigned long long*)P.xpeer[P.tp_rank]; };
+    // the flag epoch of this step (only the last CTA to leave advances it, after every CTA's
+    // last use)
+    const uint32_t fepoch = *(volatile unsigned*)&st->epoch;
 
     // stream geometry of every phase -> shared memory
     for (int i = tid; i < P.n_phases; i += STEP_THREADS) {
@@ -719,11 +1114,6 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         pi.fmts = P.phases[i].fmts;
         pinfo[i] = pi;
     }
-    if (tid == 0) {
-        mbar_init(mbar_rec);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    uint32_t par_rec = 0;  // next phase of the records mbarrier (the same in every thread)
     __syncthreads();
 
     // ---------------- weight stream: this warp's unit ranges of all GEMV phases, copied in
@@ -741,147 +1131,29 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     }
 
     const int c4 = lane & 3;
-    float lmax = -INFINITY;
-    int lidx = 0;
+    ArgMax am{-INFINITY, 0};
     constexpr int DWORDS = (int)(sizeof(StepPhase) / 4);
     static_assert(sizeof(StepPhase) <= 256 && sizeof(StepPhase) % 4 == 0, "descriptor slot");
     for (int ph = 0; ph < P.n_phases; ++ph) {
         StepPhase& d = dsm[ph & 1];
         JINF_TRACE(ph, 0);
         if (tid == 0) {
-            const StepPhase& g = P.phases[ph];
-            // (a tensor-parallel input waits in its staging: the flagged words are the signal)
-            flags[ph & 1] = g.dep < 0 || (TP && g.xin >= 0)
-                                ? 1
-                                : (wait_ge(P.done + g.dep, g.dep_target, st, P.spin_limit) ? 1 : 0);
-        } else if (tid >= 32 && tid < 32 + DWORDS) {  // descriptor -> shared memory while warp 0 polls
+            flags[ph & 1] = *(volatile int*)&st->error == DEV_OK ? 1 : 0;
+        } else if (tid >= 32 && tid < 32 + DWORDS) {  // descriptor -> shared memory
             reinterpret_cast<uint32_t*>(&d)[tid - 32] = reinterpret_cast<const uint32_t*>(P.phases + ph)[tid - 32];
-        } else if (tid >= 96) {
-            if (tid == 32 * 9) {  // L2 prefetch of later weights while warp 0 polls
-                for (int k = 0; k < 2; ++k) {
-                    const int j = P.phases[ph].pf[k];
-                    if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C, UB, MIXED);
-                }
+        } else if (tid == 32 * 9) {  // L2 prefetch of later weights
+            for (int k = 0; k < 2; ++k) {
+                const int j = P.phases[ph].pf[k];
+                if (j > ph && j < P.n_phases) prefetch_cta_range(pinfo[j], blockIdx.x, C, UB, MIXED);
             }
         }
         __syncthreads();  // also: every warp is done with the previous phase's shared data
         if (!flags[ph & 1]) break;
         JINF_TRACE(ph, 1);
+        const uint32_t fl_in = step_flag(fepoch, d.tag_in), fl_out = step_flag(fepoch, ph);
 
         if (d.kind == PH_ATTN) {
-            // ---------------- attention: CTA (kv head, split) of the context
-            AttnGeom a;
-            if (!attn_geom(pos, P.n_kv_heads, P.attn_smax, blockIdx.x, a)) continue;
-            const int hd = P.head_dim, gq = P.n_heads / P.n_kv_heads;
-            const float* qh = d.q + (size_t)a.kvh * gq * hd;
-            const __half* kb = d.kcache + (size_t)a.kvh * P.max_ctx * hd;
-            const __half* vb = d.vcache + (size_t)a.kvh * P.max_ctx * hd;
-            float* gpart =
-                a.S > 1 ? P.attn_part + ((size_t)a.kvh * ATTN_MAX_SPLIT + a.sp) * ATTN_MAX_GROUP * (hd + 2) : nullptr;
-#define JINF_ATTN_SPLIT(HD_, GQ_) attn_split<HD_, GQ_>(qh, kb, vb, a.p0, a.p1, xbase, gpart, outs_s)
-            if (hd == 64) {
-                if (gq == 8) JINF_ATTN_SPLIT(64, 8);
-                else if (gq == 4) JINF_ATTN_SPLIT(64, 4);
-                else if (gq == 2) JINF_ATTN_SPLIT(64, 2);
-                else JINF_ATTN_SPLIT(64, 1);
-            } else {
-                if (gq == 8) JINF_ATTN_SPLIT(128, 8);
-                else if (gq == 4) JINF_ATTN_SPLIT(128, 4);
-                else if (gq == 2) JINF_ATTN_SPLIT(128, 2);
-                else JINF_ATTN_SPLIT(128, 1);
-            }
-#undef JINF_ATTN_SPLIT
-            JINF_TRACE(ph, 2);
-            const int nblk = gq * hd / 32;  // 32-element output blocks of this kv head
-            if (a.S == 1) {
-                __syncthreads();
-                if (d.rec_out) {
-                    blocks_to_records(outs_s, a.kvh * nblk, nblk, d.groups_out, d.rec_out);
-                } else {
-                    for (int i = tid; i < gq * hd; i += STEP_THREADS) d.out[(size_t)a.kvh * gq * hd + i] = outs_s[i];
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    __threadfence();
-                    atomicAdd(P.done + ph, (unsigned)nblk);
-                }
-                JINF_TRACE(ph, 5);
-                continue;
-            }
-            // publish this split's partial; the splits that own output blocks (split sp owns
-            // blocks sp, sp + S, ...) wait for all S partials of the kv head, then each merges its
-            // blocks in split order (deterministic) and writes them as records
-            __syncthreads();
-            unsigned* cnt = P.attn_cnt + d.layer * P.n_kv_heads + a.kvh;
-            if (tid == 0) {
-                __threadfence();
-                atomicAdd(cnt, 1u);
-            }
-            JINF_TRACE(ph, 3);
-            if (a.sp >= nblk) continue;
-            if (tid == 0) flags[2] = wait_ge(cnt, (unsigned)a.S, st, P.spin_limit) ? 1 : 0;
-            __syncthreads();  // (a timeout is recorded in the device state; the step is then discarded)
-            JINF_TRACE(ph, 4);
-            const size_t stride = (size_t)ATTN_MAX_GROUP * (hd + 2);
-            const float* base = P.attn_part + (size_t)a.kvh * ATTN_MAX_SPLIT * stride;
-            float* ml = reinterpret_cast<float*>(xbase);  // [S][2] (m, l) of the block's query head
-            float* av = ml + 2 * ATTN_MAX_SPLIT;           // [S][32] accumulators of the block
-            float* ew = av + 32 * ATTN_MAX_SPLIT;          // [S] split weights e^(m_s - M)
-            unsigned mine = 0;
-            for (int b = a.sp; b < nblk; b += a.S, ++mine) {
-                const int g = b * 32 / hd, dd0 = b * 32 % hd;
-                {  // every partial load of the thread before any store (S <= 64: at most 4)
-                    float t4[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const int t = tid + k * STEP_THREADS;
-                        t4[k] = t < a.S * 32 ? __ldcg(base + (t >> 5) * stride + g * (hd + 2) + dd0 + (t & 31)) : 0.f;
-                    }
-                    const float m0 = tid < a.S ? __ldcg(base + tid * stride + g * (hd + 2) + hd) : 0.f;
-                    const float l0 = tid < a.S ? __ldcg(base + tid * stride + g * (hd + 2) + hd + 1) : 0.f;
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        if (tid + k * STEP_THREADS < a.S * 32) av[tid + k * STEP_THREADS] = t4[k];
-                    if (tid < a.S) {
-                        ml[2 * tid] = m0;
-                        ml[2 * tid + 1] = l0;
-                    }
-                }
-                __syncthreads();
-                if (warp == 0) {
-                    // lanes own splits lane, lane + 32: the max, the weights and their sum in parallel
-                    const float ma = lane < a.S ? ml[2 * lane] : -INFINITY;
-                    const float mb = lane + 32 < a.S ? ml[2 * (lane + 32)] : -INFINITY;
-                    const float M = warp_max(fmaxf(ma, mb));
-                    const float ea = ma == -INFINITY ? 0.f : expf(ma - M);  // 0: an empty split
-                    const float eb = mb == -INFINITY ? 0.f : expf(mb - M);
-                    const float L = warp_sum((lane < a.S ? ml[2 * lane + 1] * ea : 0.f) +
-                                             (lane + 32 < a.S ? ml[2 * (lane + 32) + 1] * eb : 0.f));
-                    if (lane < a.S) ew[lane] = ea;
-                    if (lane + 32 < a.S) ew[lane + 32] = eb;
-                    __syncwarp();
-                    float v = 0.f;
-                    for (int s2 = 0; s2 < a.S; ++s2) v = fmaf(ew[s2], av[s2 * 32 + lane], v);
-                    v /= L;
-                    const int blk = a.kvh * nblk + b;  // block of the o projection's input
-                    if (d.rec_out) {
-                        // octet layout: lane q < 8 takes elements 4q .. 4q+3
-                        const int src = 4 * (lane & 7);
-                        const float4 x = make_float4(__shfl_sync(JINF_FULL_MASK, v, src), __shfl_sync(JINF_FULL_MASK, v, src + 1),
-                                                     __shfl_sync(JINF_FULL_MASK, v, src + 2), __shfl_sync(JINF_FULL_MASK, v, src + 3));
-                        uint32_t* dig = reinterpret_cast<uint32_t*>(d.rec_out);
-                        float4* prm = reinterpret_cast<float4*>(d.rec_out + (size_t)d.groups_out * 256);
-                        octet_to_records(x, lane, blk & 3, dig + (blk >> 2) * 64, prm + (blk >> 2) * 4, lane < 8);
-                    } else {
-                        d.out[(size_t)blk * 32 + lane] = v;
-                    }
-                }
-                __syncthreads();  // the scratch is reused by the next block
-            }
-            if (tid == 0) {
-                __threadfence();
-                atomicAdd(P.done + ph, mine);
-            }
+            attn_phase(P, d, pos, fl_in, fl_out, xbase, outs_s);
             JINF_TRACE(ph, 5);
             continue;
         }
@@ -905,82 +1177,26 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
         // of an EPI_RESID phase, the RoPE factors of an EPI_QKV phase. The staging ends with
         // the CTA synchronised, before any epilogue reads them.
         const int prow0 = t0 * Q4M_PAIR_ROWS, nprow = (t1 - t0) * Q4M_PAIR_ROWS;
-        const bool pre = ((d.epi == EPI_RESID && !d.rec_out) || d.epi == EPI_QKV) && nprow <= 1024;
-        if (pre && tid >= 32) {
-            for (int i = tid - 32; i < nprow; i += STEP_THREADS - 32) {
-                const int row = prow0 + i;
-                if (d.epi == EPI_RESID) {
-                    outs_s[i] = row < d.rows ? __ldcg(d.y + row) : 0.f;
-                } else if ((i & 1) == 0 && row < P.nq + P.nk) {
-                    float cs, sn;
-                    rope_pair(row < P.nq ? row : row - P.nq, pos, P.rope_base, P.head_dim, cs, sn);
-                    outs_s[i] = cs;
-                    outs_s[i + 1] = sn;
-                }
-            }
-        }
+        const bool pre = (d.epi == EPI_RESID || d.epi == EPI_QKV) && nprow <= 1024;
+        if (pre && tid >= 32) prepare_epilogue(P, d, pos, fepoch, prow0, nprow, outs_s);
         float fac;
         if (d.xm == X_RECORDS) {
-            fac = stage_records(d.rec, d.ssp, d.n_ss, d.cols, P.eps, G, xbase, mbar_rec, par_rec, st, P.spin_limit);
-            par_rec ^= 1u;
+            stage_records_flag(d.fin, fl_in, G, d.cols / 32, xbase, st, P.spin_limit);
+            fac = 1.0f;
+        } else if (d.xm == X_EMBED_NORM) {
+            // the embedding row; the CTA that owns pair 0 also stores it as the residual stream
+            const float* emb = d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols;
+            fac = stage_x<STEP_THREADS>(X_EMBED_NORM, nullptr, emb, nullptr, nullptr, false, d.norm_w, P.eps, d.cols,
+                                        xbase, misc, true);
+            if (t0 == 0 && d.fout_h) store_h_flag(emb, d.cols, d.fout_h, fl_out);
+        } else if (TP && d.xm == X_RMSNORM_TP) {
+            fac = stage_tp(P, d, t0, fepoch, fl_out, xbase, misc);
         } else {
-            const float* hsrc =
-                d.xm == X_EMBED_NORM ? d.hsrc + (size_t)(*(volatile int*)&st->token) * d.cols : d.hsrc;
-            // the CTA that owns pair 0 stores the embedding row as the residual stream
-            if (TP && d.xm == X_RMSNORM_TP) {
-                const unsigned long long ep = epoch();
-                fac = stage_x_tp(xchg_data(P, P.tp_rank, d.xin, (unsigned)(ep & 1ull), 0), (size_t)(P.x_slot / 8),
-                                 P.tp_size, P.eps, P.spin_limit, hsrc, d.hout, t0 == 0 && d.hout, d.norm_w, d.cols,
-                                 (uint32_t)(ep + 1ull), xbase, misc, st);
-            } else
-                fac = stage_x<STEP_THREADS>(d.xm, d.x, hsrc, nullptr, d.hout, t0 == 0, d.norm_w, P.eps, d.cols,
-                                            xbase, misc, true);
+            fac = stage_x_flag(d.fin, fl_in, d.norm_w, P.eps, d.cols, xbase, misc, st, P.spin_limit);
         }
         JINF_TRACE(ph, 2);
         const XRecS xr{smem_u32(xbase), smem_u32(xbase + (size_t)G * 256)};
-        // epilogue arguments are read from the shared descriptor when a tile finishes
-        auto epilogue = [&](int row, float v0, float v1) {
-            EpiArgs ea;
-            ea.epi = d.epi;
-            ea.rows = d.rows;
-            ea.y = d.y;
-            ea.kcache = d.kcache;
-            ea.vcache = d.vcache;
-            ea.nq = P.nq;
-            ea.nk = P.nk;
-            ea.head_dim = P.head_dim;
-            ea.max_ctx = P.max_ctx;
-            ea.pos = pos;
-            ea.rope_base = P.rope_base;
-            ea.coherent = true;
-            ea.pre = pre ? outs_s : nullptr;
-            ea.pre_row0 = prow0;
-            epilogue_pair(ea, row, v0 * fac, v1 * fac, lmax, lidx);
-        };
-        // a finished pair, by the whole warp (lanes q < 16 hold rows 2q, 2q+1)
-        auto finish_pair = [&](int pr, float v0, float v1) {
-            const int q = lane & 15, row = pr * Q4M_PAIR_ROWS + 2 * q;
-            if (TP && d.epi == EPI_PARTIAL) {
-                // this rank's partial rows into its slot of every rank's exchange area
-                if (lane < 16 && row < d.rows) {  // (rows: a multiple of 32)
-                    const unsigned long long ep = epoch();
-                    const uint32_t flag = (uint32_t)(ep + 1ull);
-                    const unsigned long long w0 = ll_word(v0 * fac, flag), w1 = ll_word(v1 * fac, flag);
-                    for (int r = 0; r < P.tp_size; ++r)
-                        st_ll2(xchg_data(P, r, d.xout, (unsigned)(ep & 1ull), P.tp_rank) + row, w0, w1);
-                }
-            } else if (d.rec_out && d.epi == EPI_RESID) {
-                resid_records(d, pr, v0 * fac, v1 * fac);
-            } else if (d.rec_out && d.epi == EPI_GATEUP) {
-                // the activation goes to shared memory; whole blocks become records below
-                if (lane < 16) {
-                    const float g = v0 * fac, u = v1 * fac;
-                    outs_s[(pr - t0) * 16 + q] = row < d.rows ? g / (1.0f + expf(-g)) * u : 0.f;
-                }
-            } else if (lane < 16) {
-                epilogue(row, v0, v1);
-            }
-        };
+        const EpiCtx ec{fac, pos, fepoch, fl_out, t0, prow0, pre};
         int c, c1;
         warp_range(blockIdx.x, C, warp, d.pairs, d.gran, G, c, c1);
         if (lane == 0) {
@@ -1010,7 +1226,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
             if (gb == 0 && ge == G) {
                 const int q = lane & 15;
                 const float v0 = unit_row(ps.acc, 2 * q), v1 = unit_row(ps.acc, 2 * q + 1);
-                finish_pair(pair, v0, v1);
+                finish_pair<TP>(P, d, ec, pair, v0, v1, outs_s, am);
             } else {
                 // a piece of a pair shared with the neighbouring warps: partial rows to shared memory
                 const int sl = first_piece ? 0 : 1;
@@ -1054,17 +1270,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
                     v1 += p1[w2];
                 }
             }
-            finish_pair(own_pair, v0, v1);
+            finish_pair<TP>(P, d, ec, own_pair, v0, v1, outs_s, am);
         }
-        __syncthreads();  // every epilogue store of the CTA precedes the report
-        if (d.rec_out && d.epi == EPI_GATEUP) {
+        if (d.epi == EPI_GATEUP) {
+            __syncthreads();  // every activation of the CTA is in shared memory
             // pairs [t0, t1) hold activation blocks [t0 / 2, t1 / 2) (gran 2)
-            blocks_to_records(outs_s, t0 >> 1, (t1 - t0) >> 1, d.groups_out, d.rec_out);
-            __syncthreads();
-        }
-        if (tid == 0) {
-            __threadfence();
-            atomicAdd(P.done + ph, (unsigned)(t1 - t0));
+            blocks_to_records_flag(outs_s, t0 >> 1, (t1 - t0) >> 1, d.groups_out, d.fout, fl_out);
         }
         JINF_TRACE(ph, 5);
     }
@@ -1072,7 +1283,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
 
     // ---------------- leave: LM head argmax, then the last CTA finishes the step
     if (P.with_argmax) {
-        u64 key = lmax == -INFINITY ? 0ull : argmax_key(lmax, lidx + P.vocab_off);
+        u64 key = am.v == -INFINITY ? 0ull : argmax_key(am.v, am.i + P.vocab_off);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const u64 other = __shfl_xor_sync(JINF_FULL_MASK, key, o);
@@ -1082,47 +1293,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const StepParams P) {
     }
     __syncthreads();
     if (tid == 0) {
+        u64 best = 0ull;
         if (P.with_argmax) {
-            u64 best = 0ull;
             for (int w = 0; w < NW; ++w) best = wkeys[w] > best ? wkeys[w] : best;
             if (best) atomicMax(&st->best, best);
         }
         __threadfence();
-        const unsigned old = atomicAdd(P.done + P.n_phases, 1u);
-        if (old == gridDim.x - 1) {
-            __threadfence();
-            u64 b = P.with_argmax ? atomicAdd(&st->best, 0ull) : 0ull;
-            const bool tp = TP && P.tp_size > 1;
-            const unsigned long long ep = tp ? epoch() : 0ull;
-            const unsigned par = (unsigned)(ep & 1ull);
-            if (tp) {
-                // every rank's argmax key to every rank, then the largest (the key order puts the
-                // lower global index first on ties). Steps without an LM head exchange a zero key,
-                // so that every rank's step ends only after all writes into its area have landed.
-                u64* keys = reinterpret_cast<u64*>(P.xpeer[P.tp_rank] + P.x_keys) + par * STEP_MAX_TP;
-                for (int r = 0; r < P.tp_size; ++r)
-                    reinterpret_cast<volatile u64*>(P.xpeer[r] + P.x_keys)[par * STEP_MAX_TP + P.tp_rank] = b;
-                __threadfence_system();
-                for (int r = 0; r < P.tp_size; ++r)
-                    atomicAdd_system(reinterpret_cast<unsigned long long*>(P.xpeer[r] + P.x_keycnt), 1ull);
-                if (wait_ge_sys(reinterpret_cast<const unsigned long long*>(P.xpeer[P.tp_rank] + P.x_keycnt),
-                                (ep + 1ull) * (unsigned long long)P.tp_size, st, P.spin_limit)) {
-                    for (int r = 0; r < P.tp_size; ++r) {
-                        const u64 k = __ldcg(keys + r);
-                        b = k > b ? k : b;
-                    }
-                }
-            }
-            if (P.with_argmax) {
-                st->argmax_token = b ? (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull)) : 0;
-                st->token = st->argmax_token;
-                st->best = 0ull;
-            }
-            st->pos = pos + 1;
-            for (int i = 0; i <= P.n_phases; ++i) P.done[i] = 0u;
-            for (int i = 0; i < P.n_attn_cnt; ++i) P.attn_cnt[i] = 0u;
-            if (tp) *reinterpret_cast<volatile unsigned long long*>(P.xpeer[P.tp_rank]) = ep + 1ull;
-        }
+        const unsigned old = atomicAdd(P.done, 1u);
+        if (old == gridDim.x - 1) finish_step<TP>(P, pos, fepoch);
     }
 }
 
@@ -1198,6 +1376,14 @@ int step_occupancy(size_t smem, int fmt, int nbuf) {
     }
     return lo;
 }
+
+#ifdef JINF_STEP_TRACE
+extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
+    const size_t cap = (size_t)TRACE_MAX_PH * TRACE_MAX_CTA * TRACE_PTS;
+    if (n > cap) n = cap;
+    return cudaMemcpyFromSymbol(host, g_step_trace, n * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 #ifdef JINF_STEP_TRACE
 extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
