@@ -69,23 +69,6 @@ __device__ __forceinline__ void trace_at(int ph, int pt) {
 #define JINF_TRACE(ph, pt) ((void)0)
 #endif
 
-// Development timing (off unless built with -DJINF_STEP_TRACE): thread 0 of every CTA stamps
-// %globaltimer at fixed points of every phase into g_step_trace[phase][cta][point]; the last
-// launch's stamps are read with jinf_step_trace_read.
-#ifdef JINF_STEP_TRACE
-constexpr int TRACE_PTS = 6, TRACE_MAX_PH = 512, TRACE_MAX_CTA = 160;
-__device__ unsigned long long g_step_trace[TRACE_MAX_PH * TRACE_MAX_CTA * TRACE_PTS];
-__device__ __forceinline__ void trace_at(int ph, int pt) {
-    if (threadIdx.x == 0 && ph < TRACE_MAX_PH && blockIdx.x < TRACE_MAX_CTA) {
-        unsigned long long t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        g_step_trace[((size_t)ph * TRACE_MAX_CTA + blockIdx.x) * TRACE_PTS + pt] = t;
-    }
-}
-#define JINF_TRACE(ph, pt) trace_at(ph, pt)
-#else
-#define JINF_TRACE(ph, pt) ((void)0)
-#endif
 
 // ---------------------------------------------------------------- flagged words
 //
@@ -1376,14 +1359,6 @@ int step_occupancy(size_t smem, int fmt, int nbuf) {
     }
     return lo;
 }
-
-#ifdef JINF_STEP_TRACE
-extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
-    const size_t cap = (size_t)TRACE_MAX_PH * TRACE_MAX_CTA * TRACE_PTS;
-    if (n > cap) n = cap;
-    return cudaMemcpyFromSymbol(host, g_step_trace, n * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
-}
-#endif
 
 #ifdef JINF_STEP_TRACE
 extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
