@@ -166,6 +166,7 @@ SIGNATURES = {
     "jinf_b200_gemv_q4m": (i32, [vp, vp, i32, vp, i32, i32, vp, i32, vp]),
     "jinf_b200_gemv_q4m_rmsnorm": (i32, [vp, vp, vp, f32, vp, i32, i32, vp, i32, vp]),
     "jinf_b200_gemv_q4m_noalloc": (i32, [vp, vp, i32, vp, i32, i32, vp]),
+    "jinf_b200_prefill_gemm": (i32, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp]),
     "jinf_b200_attention_workspace_bytes": (sz, [i32, i32, i32]),
     "jinf_b200_attention_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     # gguf.h
