@@ -374,8 +374,25 @@ def run_ours(args, rank, world, local):
     stream = torch.cuda.ExternalStream(eng.h.contents.compute_stream, device=dev)
     prompt = prompt_ids(shape.n_vocab)
 
-    # ---- value: resident decode, K steps timed on the device
+    # ---- time to first token: the prompt through forward() (batched tensor-core prefill of all
+    # but its last token where the model allows it, then one decode step), and the same prompt
+    # one token per forward() as the reference runs it (src/engine.cpp:690-751)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
     eng.forward(prompt)
+    torch.cuda.synchronize()
+    prompt_s = time.perf_counter() - t0
+    eng.reset()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for t in prompt:
+        eng.forward([t])
+    torch.cuda.synchronize()
+    tokenwise_s = time.perf_counter() - t0
+    eng.reset()
+    eng.forward(prompt)
+
+    # ---- value: resident decode, K steps timed on the device
     eng.decode_resident(args.warmup)
     if dist:
         dist.barrier()
@@ -455,6 +472,11 @@ def run_ours(args, rank, world, local):
                                 "achieved_GBs": round(step_gbs, 1), "frac": round(step_gbs / peak, 4),
                                 "roofline_tok_s": round(peak * 1e9 / (wbytes + kv_bytes), 1)},
             "per_op_kernels_us": {k: round(v["us"], 2) for k, v in prof.items()},
+            "prompt": {"tokens": len(prompt), "forward_ms": round(1e3 * prompt_s, 2),
+                       "tok_s": round(len(prompt) / prompt_s, 1), "one_token_per_forward_ms": round(1e3 * tokenwise_s, 2),
+                       "note": "host wall time of forward(prompt) (batched tensor-core prefill of all but the last "
+                               "token where the model allows it, then one decode step) and of one forward() per "
+                               "prompt token"},
             "clocks": clk.summary(),
             "load_s": round(t_load, 1),
         }

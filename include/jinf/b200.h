@@ -75,12 +75,14 @@ jinf_status jinf_b200_gemv_q4m_noalloc(const void* q4m, const void* x, int x_typ
 // ---- batched prefill (new; replaces the reference's one-token-at-a-time prompt loop,
 // src/engine.cpp:690-751, with one tensor-core contraction per projection)
 //
-// y[t * ldy + m] = tok_scale[t] * sum_k x[t][k] W[m][k] for t < T: W a Q4M (Q4_0) matrix
-// [rows][cols], x fp16 [T][cols] (16-byte aligned, row stride cols), y fp32. tcgen05.mma with
-// the accumulator in tensor memory; x by TMA. `err` is a device int the caller zeroed: the
-// kernel sets it to 1 if a pipeline wait ran out (the output is then incomplete).
+// y[t * ldy + m] (+)= tok_scale[t] * sum_k x[t][k] W[m][k] for t < T: W a Q4M (Q4_0) matrix
+// [rows][cols], x fp16 [T][cols] (16-byte aligned, row stride cols), y fp32 (`accumulate`:
+// added to y). tcgen05.mma with the accumulator in tensor memory; x by TMA. `err` is a device
+// int the caller zeroed: the kernel sets it to 1 if a pipeline wait ran out (the output is
+// then incomplete).
 jinf_status jinf_b200_prefill_gemm(const void* q4m, int rows, int cols, const void* x_f16, int T,
-                                   const float* tok_scale, float* y, int ldy, int* err, cudaStream_t stream);
+                                   const float* tok_scale, float* y, int ldy, int accumulate, int* err,
+                                   cudaStream_t stream);
 
 // ---- sparse FFN (engine sparse modes; reference src/engine.cpp:339-415, src/activation_predictor.cpp)
 //

@@ -102,6 +102,9 @@ typedef struct jinf_b200_options {
     float sparse_keep;      // fraction of FFN neurons kept in sparse modes (default 0.15)
     uint64_t sparse_seed;   // seed of the predictor weights / fixed masks
     int   persistent;       // tp_size 1: run each token as one persistent kernel (default 1)
+    int   prefill;          // forward() of several tokens runs all but the last through the batched
+                            // prefill (tensor-core projections over all tokens at once) where the
+                            // model allows it: one GPU, Q4_0 weights, dense FFN (default 1)
 } jinf_b200_options;
 
 static inline jinf_b200_options jinf_b200_options_default(void) {
@@ -117,6 +120,7 @@ static inline jinf_b200_options jinf_b200_options_default(void) {
     o.sparse_keep = 0.15f;
     o.sparse_seed = 0;
     o.persistent = 1;
+    o.prefill = 1;
     return o;
 }
 

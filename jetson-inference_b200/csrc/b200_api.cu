@@ -245,10 +245,11 @@ extern "C" jinf_status jinf_b200_attention_f16(float* out, const float* q, const
 }
 
 extern "C" jinf_status jinf_b200_prefill_gemm(const void* q4m, int rows, int cols, const void* x_f16, int T,
-                                              const float* tok_scale, float* y, int ldy, int* err, cudaStream_t stream) {
+                                              const float* tok_scale, float* y, int ldy, int accumulate, int* err,
+                                              cudaStream_t stream) {
     if (!q4m || !x_f16 || !tok_scale || !y || !err || T <= 0) return JINF_ERR_INVALID;
     const cudaError_t e = prefill_gemm_launch((const uint8_t*)q4m, rows, cols, (const __half*)x_f16, T, tok_scale, y,
-                                              ldy, err, stream);
+                                              ldy, accumulate ? 1 : 0, err, stream);
     if (e == cudaErrorInvalidValue) return JINF_ERR_INVALID;
     return e == cudaSuccess ? JINF_OK : JINF_ERR_CUDA;
 }

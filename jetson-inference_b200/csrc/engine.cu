@@ -35,6 +35,7 @@
 #include "device_state.cuh"
 #include "gemv.h"
 #include "nccl_shim.h"
+#include "prefill.h"
 #include "q4m.cuh"
 #include "sparse_engine.h"
 #include "step.h"
@@ -431,6 +432,13 @@ struct jinf_engine_impl {
     unsigned long long *fx_h[2] = {nullptr, nullptr}, *fx_q = nullptr, *fx_kv = nullptr, *fx_arec = nullptr,
                        *fx_grec = nullptr;
     StepParams sp_full{}, sp_body{};
+    // batched prefill (prefill.h): enabled for one GPU, Q4_0 weights, dense FFN; buffers for a
+    // chunk of up to pf_cap tokens, allocated at the first long forward()
+    bool prefill = false;
+    int pf_cap = 0;
+    float *pf_h = nullptr, *pf_y = nullptr, *pf_att = nullptr, *pf_sc = nullptr;
+    __half *pf_x16 = nullptr, *pf_q16 = nullptr;
+    int* pf_err = nullptr;
     // ops and graphs
     std::vector<Op> ops_full, ops_body;
     cudaGraphExec_t exec_full = nullptr, exec_body = nullptr;
@@ -1180,7 +1188,8 @@ void free_impl(jinf_engine_impl* I) {
     }
     void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
                     I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
-                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_fx, I->bundles, I->pred_w1,
+                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_fx, I->pf_h, I->pf_y,
+                    I->pf_att, I->pf_sc, I->pf_x16, I->pf_q16, I->pf_err, I->bundles, I->pred_w1,
                     I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -1219,6 +1228,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     I->tp_rank = opt.tp_rank;
     I->tp_size = tp;
     I->use_graph = opt.use_graph != 0;
+    I->prefill = opt.prefill != 0;
     I->eos = opt.eos_token;
     I->d = (int)hp.n_embd;
     I->H = (int)hp.n_heads;
@@ -1730,6 +1740,83 @@ jinf_status step(jinf_engine* e, bool with_head) {
     return JINF_OK;
 }
 
+// ---------------------------------------------------------------- batched prefill
+//
+// The reference runs every prompt token through the whole model one at a time
+// (src/engine.cpp:690-751). Here the tokens [0, T) of a forward() (all but its last, whose
+// logits the caller reads) go through each layer together: the projections are tensor-core
+// contractions over all T tokens (prefill_gemm.cu), RMSNorm, RoPE, the KV store, a causal
+// attention and SiLU * up run once per layer over all rows (prefill.cu). Chunks of up to 512
+// tokens; each chunk's attention also sees the positions before it.
+constexpr int PF_CHUNK = 512;
+constexpr int PF_MIN_TOKENS = 8;  // shorter prompts run token by token
+
+bool prefill_usable(const jinf_engine* e, int T) {
+    const jinf_engine_impl* I = e->impl;
+    return I->prefill && T >= PF_MIN_TOKENS && I->persistent && I->tp_size == 1 && I->uniform &&
+           I->wfmt == Q4M_Q4_0 && !I->sparse_mode && !e->ffn_hook && !I->count_dev && (I->hd == 64 || I->hd == 128) &&
+           I->d % 64 == 0 && I->ffl % 64 == 0;
+}
+
+jinf_status prefill_alloc(jinf_engine_impl* I) {
+    if (I->pf_cap) return JINF_OK;
+    const size_t C = PF_CHUNK, nq = (size_t)I->Hl * I->hd, nk = (size_t)I->Hkvl * I->hd;
+    const size_t ny = std::max(nq + 2 * nk, 2 * (size_t)I->ffl), nx = std::max(std::max((size_t)I->d, (size_t)I->ffl), nq);
+    JINF_CUDA_CHECK(cudaMalloc(&I->pf_h, sizeof(float) * C * I->d));
+    JINF_CUDA_CHECK(cudaMalloc(&I->pf_y, sizeof(float) * C * ny));
+    JINF_CUDA_CHECK(cudaMalloc(&I->pf_att, sizeof(float) * C * nq));
+    JINF_CUDA_CHECK(cudaMalloc(&I->pf_sc, sizeof(float) * C));
+    JINF_CUDA_CHECK(cudaMalloc(&I->pf_x16, sizeof(__half) * C * nx));
+    JINF_CUDA_CHECK(cudaMalloc(&I->pf_q16, sizeof(__half) * C * nq));
+    JINF_CUDA_CHECK(cudaMalloc(&I->pf_err, sizeof(int)));
+    JINF_CUDA_CHECK(cudaMemset(I->pf_err, 0, sizeof(int)));
+    I->pf_cap = PF_CHUNK;
+    return JINF_OK;
+}
+
+// Tokens dev_tokens[0, T) at positions n_past .. n_past + T - 1; afterwards n_past += T and
+// the device position follows (the last token of the forward() then runs as a decode step).
+jinf_status prefill_tokens(jinf_engine* e, int T) {
+    jinf_engine_impl* I = e->impl;
+    JINF_CHECK(prefill_alloc(I), "prefill buffers");
+    cudaStream_t s = I->stream;
+    const int d = I->d, nq = I->Hl * I->hd, nk = I->Hkvl * I->hd, ff = I->ffl, nqkv = nq + 2 * nk;
+    for (int c0 = 0; c0 < T; c0 += PF_CHUNK) {
+        const int Tc = std::min(PF_CHUNK, T - c0), p0 = e->n_past + c0;
+        JINF_CUDA_CHECK(prefill_embed(I->embed, I->dev_tokens + c0, Tc, d, I->pf_h, s));
+        for (int L = 0; L < I->L; ++L) {
+            const auto& ly = I->layers[L];
+            __half* kc = I->kc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+            __half* vc = I->vc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+            JINF_CUDA_CHECK(prefill_rows_to_f16(I->pf_h, d, Tc, d, ly.attn_norm, I->eps, I->pf_x16, d, I->pf_sc, s));
+            JINF_CUDA_CHECK(prefill_gemm_launch(ly.qkv, nqkv, d, I->pf_x16, Tc, I->pf_sc, I->pf_y, nqkv, 0, I->pf_err, s));
+            JINF_CUDA_CHECK(prefill_rope_qkv(I->pf_y, nqkv, Tc, p0, nq, nk, I->hd, I->rope_base, I->pf_q16, kc, vc,
+                                             I->max_ctx, s));
+            JINF_CUDA_CHECK(prefill_attention(I->pf_q16, I->Hl, I->Hkvl, I->hd, Tc, p0, kc, vc, I->max_ctx, I->pf_att, s));
+            JINF_CUDA_CHECK(prefill_rows_to_f16(I->pf_att, nq, Tc, nq, nullptr, 0.f, I->pf_x16, nq, I->pf_sc, s));
+            JINF_CUDA_CHECK(prefill_gemm_launch(ly.o, d, nq, I->pf_x16, Tc, I->pf_sc, I->pf_h, d, 1, I->pf_err, s));
+            JINF_CUDA_CHECK(prefill_rows_to_f16(I->pf_h, d, Tc, d, ly.ffn_norm, I->eps, I->pf_x16, d, I->pf_sc, s));
+            JINF_CUDA_CHECK(
+                prefill_gemm_launch(ly.gu, 2 * ff, d, I->pf_x16, Tc, I->pf_sc, I->pf_y, 2 * ff, 0, I->pf_err, s));
+            JINF_CUDA_CHECK(prefill_silu_to_f16(I->pf_y, 2 * ff, Tc, ff, I->pf_x16, ff, I->pf_sc, s));
+            JINF_CUDA_CHECK(prefill_gemm_launch(ly.down, d, ff, I->pf_x16, Tc, I->pf_sc, I->pf_h, d, 1, I->pf_err, s));
+        }
+    }
+    e->n_past += T;
+    I->pinned[3] = e->n_past;
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->pos, &I->pinned[3], sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    // a pipeline wait of the tensor-core GEMM that ran out is reported like a step timeout
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->pinned[2], I->pf_err, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(s));
+    if (I->pinned[2] != 0) {
+        JINF_LOG("prefill: a tensor-core pipeline wait ran out");
+        cudaMemsetAsync(I->pf_err, 0, sizeof(int), s);
+        I->pinned[2] = DEV_ERR_TIMEOUT;
+        return JINF_ERR_TIMEOUT;
+    }
+    return JINF_OK;
+}
+
 // Device-side error recorded by a step (pinned[2], copied after the step): a dependency
 // wait of the persistent kernel that gave up.
 jinf_status device_error(jinf_engine_impl* I) {
@@ -1811,7 +1898,12 @@ extern "C" jinf_status jinf_engine_forward(jinf_engine* e, const int32_t* tokens
         JINF_CUDA_CHECK(cudaMemcpyAsync(I->dev_tokens, tokens, sizeof(int32_t) * (size_t)n_tokens,
                                         cudaMemcpyHostToDevice, I->stream));
     }
-    for (int t = 0; t < n_tokens; ++t) {
+    int t_first = 0;
+    if (n_tokens > 1 && prefill_usable(e, n_tokens - 1)) {
+        JINF_CHECK(prefill_tokens(e, n_tokens - 1), "prefill");
+        t_first = n_tokens - 1;
+    }
+    for (int t = t_first; t < n_tokens; ++t) {
         if (n_tokens > 1)
             JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->token, I->dev_tokens + t, sizeof(int32_t),
                                             cudaMemcpyDeviceToDevice, I->stream));

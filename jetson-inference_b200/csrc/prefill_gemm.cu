@@ -21,7 +21,7 @@
 //                      N 128, K 16, f16 x f16 -> f32) per stage and commits each stage's MMAs
 //                      to its `empty` mbarrier, which frees the stage for the next copies;
 //   warps 4..7         after the last stage, read the accumulator (tcgen05.ld, one TMEM lane
-//                      quarter per warp) and store Y.
+//                      quarter per warp) and store Y (or add it to Y: the residual add).
 // Every mbarrier wait is bounded: a wait that runs out records an error in *err, the CTA
 // stops issuing work, lets its copies and MMAs in flight finish (bounded again), frees its
 // tensor memory and returns.
@@ -162,7 +162,7 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* raw, uint8_t* A, in
 
 __global__ void __launch_bounds__(PG_THREADS, 1)
     k_prefill_gemm(const __grid_constant__ CUtensorMap tmx, const uint8_t* __restrict__ w, int rows, int pairs,
-                   int groups, int T, float* __restrict__ y, int ldy, const float* __restrict__ tok_scale, int* err) {
+                   int groups, int T, float* __restrict__ y, int ldy, const float* __restrict__ tok_scale, int accum, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem + PG_OFF_A;
@@ -289,7 +289,11 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
 #pragma unroll
                         for (int jj = 0; jj < 32; ++jj) {
                             const int tok = t0 + c0 + jj;
-                            if (tok < T) y[(size_t)tok * ldy + row] = __uint_as_float(v[jj]) * tok_scale[tok];
+                            if (tok < T) {
+                                float* py = y + (size_t)tok * ldy + row;
+                                const float val = __uint_as_float(v[jj]) * tok_scale[tok];
+                                *py = accum ? *py + val : val;
+                            }
                         }
                     }
                 }
@@ -334,7 +338,7 @@ EncodeTiledFn encode_tiled() {
 size_t prefill_gemm_smem_bytes() { return PG_SMEM; }
 
 cudaError_t prefill_gemm_launch(const uint8_t* w, int rows, int cols, const __half* x, int T, const float* tok_scale,
-                                float* y, int ldy, int* err, cudaStream_t s) {
+                                float* y, int ldy, int accum, int* err, cudaStream_t s) {
     Q4MShape sh;
     if (!w || !x || !y || !tok_scale || !err || T <= 0 || !q4m_shape(rows, cols, &sh) || ldy < rows)
         return cudaErrorInvalidValue;
@@ -358,7 +362,8 @@ cudaError_t prefill_gemm_launch(const uint8_t* w, int rows, int cols, const __ha
         configured = 1;
     }
     const dim3 grid((unsigned)((T + PG_BN - 1) / PG_BN), (unsigned)((sh.pairs + 3) / 4));
-    k_prefill_gemm<<<grid, PG_THREADS, PG_SMEM, s>>>(map, w, rows, sh.pairs, sh.groups, T, y, ldy, tok_scale, err);
+    k_prefill_gemm<<<grid, PG_THREADS, PG_SMEM, s>>>(map, w, rows, sh.pairs, sh.groups, T, y, ldy, tok_scale, accum,
+                                                     err);
     return cudaGetLastError();
 }
 

@@ -52,7 +52,7 @@ class EngineConfig(C.Structure):
 class B200Options(C.Structure):
     _fields_ = [("device", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int), ("nccl_id", C.c_void_p),
                 ("kv_type", C.c_int), ("use_graph", C.c_int), ("eos_token", C.c_int), ("sparse_mode", C.c_int),
-                ("sparse_keep", C.c_float), ("sparse_seed", C.c_uint64), ("persistent", C.c_int)]
+                ("sparse_keep", C.c_float), ("sparse_seed", C.c_uint64), ("persistent", C.c_int), ("prefill", C.c_int)]
 
 
 class PerfStats(C.Structure):
@@ -166,7 +166,7 @@ SIGNATURES = {
     "jinf_b200_gemv_q4m": (i32, [vp, vp, i32, vp, i32, i32, vp, i32, vp]),
     "jinf_b200_gemv_q4m_rmsnorm": (i32, [vp, vp, vp, f32, vp, i32, i32, vp, i32, vp]),
     "jinf_b200_gemv_q4m_noalloc": (i32, [vp, vp, i32, vp, i32, i32, vp]),
-    "jinf_b200_prefill_gemm": (i32, [vp, i32, i32, vp, i32, vp, vp, i32, vp, vp]),
+    "jinf_b200_prefill_gemm": (i32, [vp, i32, i32, vp, i32, vp, vp, i32, i32, vp, vp]),
     "jinf_b200_attention_workspace_bytes": (sz, [i32, i32, i32]),
     "jinf_b200_attention_f16": (i32, [vp, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]),
     # gguf.h

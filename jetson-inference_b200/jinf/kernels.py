@@ -144,9 +144,9 @@ def attention_f16(out, q, kc, vc, head_dim: int, n_heads: int, n_kv_heads: int, 
                                           max_ctx, _p(workspace), _s(stream)), "jinf_b200_attention_f16")
 
 
-def prefill_gemm(q4m, rows: int, cols: int, x16, tok_scale, y, err, stream=None) -> None:
-    """y[t][m] = tok_scale[t] * sum_k x16[t][k] W[m][k] over the T rows of x16 ([T][cols] fp16):
+def prefill_gemm(q4m, rows: int, cols: int, x16, tok_scale, y, err, accumulate: bool = False, stream=None) -> None:
+    """y[t][m] (+)= tok_scale[t] * sum_k x16[t][k] W[m][k] over the T rows of x16 ([T][cols] fp16):
     the tensor-core (tcgen05) contraction of the batched prefill. `err`: a zeroed device int32."""
     T = int(x16.shape[0])
     L.check(L.lib.jinf_b200_prefill_gemm(_p(q4m), rows, cols, _p(x16), T, _p(tok_scale), _p(y), int(y.shape[1]),
-                                         _p(err), _s(stream)), "jinf_b200_prefill_gemm")
+                                         1 if accumulate else 0, _p(err), _s(stream)), "jinf_b200_prefill_gemm")

@@ -125,13 +125,16 @@ class SynthModel:
 
 def b200_options(device: int = 0, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
                  use_graph: bool = True, eos_token: int = 2, persistent: bool = True, sparse_mode: int = 0,
-                 sparse_keep: float = 0.15, sparse_seed: int = 0) -> L.B200Options:
-    """sparse_mode: 0 dense FFN, 1 device predictor top-k, 2 fixed mask (runs of 8)."""
+                 sparse_keep: float = 0.15, sparse_seed: int = 0, prefill: bool = True) -> L.B200Options:
+    """sparse_mode: 0 dense FFN, 1 device predictor top-k, 2 fixed mask (runs of 8). prefill:
+    forward() of several tokens runs all but the last through the batched (tensor-core) prefill
+    where the model allows it."""
     o = L.B200Options()
     o.device, o.tp_rank, o.tp_size = device, tp_rank, tp_size
     o.kv_type, o.use_graph, o.eos_token = L.F16, int(use_graph), eos_token
     o.sparse_mode, o.sparse_keep, o.sparse_seed = sparse_mode, sparse_keep, sparse_seed
     o.persistent = int(persistent)
+    o.prefill = int(prefill)
     o._nccl_buf = None
     if nccl_id is not None:
         buf = C.create_string_buffer(bytes(nccl_id), 128)

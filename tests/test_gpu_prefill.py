@@ -66,3 +66,82 @@ def test_prefill_gemm_deterministic(cuda):
     K.prefill_gemm(q, rows, cols, x, s, b, err)
     torch.cuda.synchronize()
     assert torch.equal(a, b) and int(err.item()) == 0
+
+
+# ---------------------------------------------------------------- the engine's batched prefill
+
+def rel_logits(got, want):
+    return float(np.max(np.abs(np.asarray(got, np.float64) - want)) / max(np.max(np.abs(want)), 1e-30))
+
+
+def top_gap(v):
+    t = np.sort(v)[-2:]
+    return float(t[1] - t[0])
+
+
+def _prefill_vs_oracle(syn, prompt, n_greedy, max_ctx):
+    import jinf
+    eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=jinf.b200_options(eos_token=-1, prefill=True))
+    orc = oracle.OracleModel(syn, max_ctx=max_ctx, kv_f16=True)
+    want = None
+    for t in prompt:
+        want = orc.forward(t)
+    got = eng.logits_host(prompt)
+    assert eng.n_past == len(prompt)
+    worst, gap = rel_logits(got, want), top_gap(want)
+    assert worst < 1e-2
+    for step in range(n_greedy):
+        tok = oracle.argmax(want)
+        assert eng.last_argmax() == tok, f"step {step}"
+        want = orc.forward(tok)
+        got = eng.logits_host([tok])
+        e = rel_logits(got, want)
+        assert e < 1e-2, f"step {step}: {e:.3g}"
+        worst, gap = max(worst, e), min(gap, top_gap(want))
+    orc.close()
+    eng.close()
+    return worst, gap
+
+
+def test_engine_prefill_tiny_logits_and_32_greedy_tokens(cuda):
+    """C1 tiny model: the 16-token prompt's first 15 tokens through the batched prefill (tensor
+    cores, causal attention over all of them at once), the last as a decode step; the logits
+    and the following 32 greedy tokens against the oracle's token-by-token decode."""
+    import jinf
+    syn = jinf.SynthModel(jinf.TINY, seed=0)
+    prompt = [int(t) for t in np.random.default_rng(0).integers(0, 4096, size=16)]
+    worst, gap = _prefill_vs_oracle(syn, prompt, 32, 128)
+    print(f"tiny prefill: max logits rel err {worst:.3g}, min top-1/top-2 gap {gap:.3g}")
+
+
+def test_engine_prefill_8b_layer_two_chunks(cuda):
+    """One Llama-3-8B-shaped layer (d 4096, 32/8 heads of 128, ff 14336; vocabulary 32000) with
+    a 530-token prompt: prefill chunks of 512 and 17 tokens (the second chunk's attention reads
+    the first chunk's cache rows), then 8 greedy steps, against the oracle."""
+    import jinf
+    shape = jinf.LlamaShape(1, 4096, 32, 8, 14336, 32000, 5e5)
+    syn = jinf.SynthModel(shape, seed=6)
+    prompt = [int(t) for t in np.random.default_rng(5).integers(0, 32000, size=530)]
+    worst, gap = _prefill_vs_oracle(syn, prompt, 8, 560)
+    print(f"8B layer prefill (530 tokens): max logits rel err {worst:.3g}, min top-1/top-2 gap {gap:.3g}")
+
+
+def test_engine_prefill_matches_token_by_token(cuda):
+    """The batched prefill and the token-by-token prompt (prefill off) agree to the logits bar,
+    and the KV rows they leave in the cache agree to fp16 rounding."""
+    import jinf
+    shape = jinf.LlamaShape(2, 4096, 32, 8, 14336, 32000, 5e5)
+    syn = jinf.SynthModel(shape, seed=8)
+    prompt = [int(t) for t in np.random.default_rng(8).integers(0, 32000, size=64)]
+    a = jinf.Engine.from_synth(syn, max_context=80, options=jinf.b200_options(eos_token=-1, prefill=True))
+    b = jinf.Engine.from_synth(syn, max_context=80, options=jinf.b200_options(eos_token=-1, prefill=False))
+    la, lb = a.logits_host(prompt), b.logits_host(prompt)
+    assert rel_logits(la, lb) < 1e-2
+    assert a.last_argmax() == b.last_argmax()
+    ka, va = a.kv_read(len(prompt))
+    kb, vb = b.kv_read(len(prompt))
+    for x, y in ((ka, kb), (va, vb)):
+        x, y = x.astype(np.float32), y.astype(np.float32)
+        assert float(np.max(np.abs(x - y)) / np.max(np.abs(y))) < 1e-2
+    a.close()
+    b.close()
