@@ -180,13 +180,21 @@ def prompt_ids(n_vocab, n=PROMPT):
 
 # ------------------------------------------------------------------------- CPU decode
 
+def start_pos(args):
+    """Position of the first decode step: the prompt length, or --ctx (the KV cache filled with
+    seeded values up to it after the prompt: config C5's 8192-position cache)."""
+    return max(PROMPT, args.ctx)
+
+
 def bench_config(args, world):
     """The workload description both arms print (the same dict on both)."""
     shape = shape_for(args.config)
     wbytes = weight_bytes(shape, args.config)
-    return {"workload": f"{args.config} greedy decode batch 1, prompt {PROMPT}, positions "
-                        f"{PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
-            "model": f"llama3-{args.config}-shape", "global_batch": 1, "seq_len": PROMPT + args.steps,
+    p0 = start_pos(args)
+    kv = "" if p0 == PROMPT else f", KV cache filled to {p0} positions"
+    return {"workload": f"{args.config} greedy decode batch 1, prompt {PROMPT}{kv}, positions "
+                        f"{p0 + args.warmup}..{p0 + args.warmup + args.steps - 1}",
+            "model": f"llama3-{args.config}-shape", "global_batch": 1, "seq_len": p0 + args.steps,
             "parallelism": f"tp{world}",
             "ffn": ["dense", "sparse: device predictor top-k 15%", "sparse: fixed mask 15% (runs of 8)"][args.sparse],
             "l2": f"{wbytes / 1e9:.2f} GB of weights streamed per step >> 126 MB L2 (no flush needed)"}
@@ -206,7 +214,7 @@ def weight_bytes(shape, config):
     return tot
 
 
-def cpu_decode(shape, config, warmup: int, steps: int, max_seconds: float | None = None):
+def cpu_decode(shape, config, warmup: int, steps: int, max_seconds: float | None = None, p0: int = PROMPT):
     """The CPU implementation of the decode path (the oracle: the reference's dequant
     conventions and its kernels' math restated on the host, OpenMP over rows) timing WHOLE
     decode tokens: every layer and the LM head, positions PROMPT + warmup onwards over a KV
@@ -216,8 +224,8 @@ def cpu_decode(shape, config, warmup: int, steps: int, max_seconds: float | None
     Returns (tok/s, threads, tokens timed, seconds timed)."""
     from oracle import oracle
     src = oracle.SynthSource(shape, seed=0, weight_type=wtype_for(config), mix_type=mix_for(config))
-    om = oracle.OracleModel(src, max_ctx=PROMPT + warmup + steps + 8, kv_f16=True)
-    om.fill_kv_random(PROMPT, seed=1)
+    om = oracle.OracleModel(src, max_ctx=p0 + warmup + steps + 8, kv_f16=True)
+    om.fill_kv_random(p0, seed=1)
     tok = 1
     for _ in range(warmup):
         tok = oracle.argmax(om.forward(tok))
@@ -244,9 +252,10 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     shape = shape_for(args.config)
-    value, cores, n, secs = cpu_decode(shape, args.config, args.warmup, args.steps)
+    p0 = start_pos(args)
+    value, cores, n, secs = cpu_decode(shape, args.config, args.warmup, args.steps, p0=p0)
     sample = (f"{n} whole decode tokens (all {shape.n_layers} layers + LM head, greedy argmax) at positions "
-              f"{PROMPT + args.warmup}..{PROMPT + args.warmup + n - 1} after {args.warmup} untimed, "
+              f"{p0 + args.warmup}..{p0 + args.warmup + n - 1} after {args.warmup} untimed, "
               f"{secs:.1f} s timed")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * secs / n,
@@ -366,7 +375,8 @@ def run_ours(args, rank, world, local):
         nccl_id = buf[0]
     t_load = time.perf_counter()
     syn = jinf.SynthModel(shape.llama(), seed=0, weight_type=wtype_for(args.config), mix_type=mix_for(args.config))
-    max_ctx = PROMPT + args.warmup + args.steps + 8
+    p0 = start_pos(args)
+    max_ctx = p0 + args.warmup + args.steps + 8
     opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
                              sparse_mode=args.sparse)
     eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=opts)
@@ -391,6 +401,8 @@ def run_ours(args, rank, world, local):
     tokenwise_s = time.perf_counter() - t0
     eng.reset()
     eng.forward(prompt)
+    if p0 > PROMPT:
+        eng.fill_kv_random(p0, seed=1)
 
     # ---- value: resident decode, K steps timed on the device
     eng.decode_resident(args.warmup)
@@ -411,6 +423,8 @@ def run_ours(args, rank, world, local):
     # ---- e2e: the same window through jinf_engine_generate (host buffers)
     eng.reset()
     eng.forward(prompt)
+    if p0 > PROMPT:
+        eng.fill_kv_random(p0, seed=1)
     eng.generate([], args.warmup)  # emits W tokens, forwards them
     if dist:
         dist.barrier()
@@ -427,7 +441,7 @@ def run_ours(args, rank, world, local):
     persistent = eng.persistent
     prof = eng.profile_kernels(reps=max(32, shape.n_layers))  # kernel-per-operation form, each timed alone
     wbytes = eng.weight_bytes_per_token()
-    kv_bytes = 2 * 2 * shape.n_layers * (shape.n_heads_kv // world) * shape.head_dim * (PROMPT + args.warmup + args.steps / 2)
+    kv_bytes = 2 * 2 * shape.n_layers * (shape.n_heads_kv // world) * shape.head_dim * (p0 + args.warmup + args.steps / 2)
     step_gbs = (wbytes + kv_bytes) / (dev_s / args.steps) / 1e9
     if persistent:
         roof = {"bound": "hbm", "kernel": "k_step (persistent decode step, one launch per token)",
@@ -451,9 +465,9 @@ def run_ours(args, rank, world, local):
     if rank == 0:
         cpu, cpu_gemv = None, None
         if world == 1 and not args.no_cpu:
-            cv, cores, n, secs = cpu_decode(shape, args.config, 1, 64, max_seconds=args.cpu_seconds)
+            cv, cores, n, secs = cpu_decode(shape, args.config, 1, 64, max_seconds=args.cpu_seconds, p0=p0)
             desc = (f"{n} whole decode tokens (all {shape.n_layers} layers + LM head, greedy argmax) at positions "
-                    f"{PROMPT + 1}..{PROMPT + n} after 1 untimed, {secs:.1f} s timed; the same method as "
+                    f"{p0 + 1}..{p0 + n} after 1 untimed, {secs:.1f} s timed; the same method as "
                     f"--impl reference")
             cpu = {"value": cv, "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc}
             if gemv:
@@ -521,6 +535,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-gemv", action="store_true", help="skip the C2 GEMV shape sweep")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ctx", type=int, default=PROMPT,
+                    help="first decode position: the KV cache is filled with seeded values up to it after the prompt "
+                         "(config C5: 8192)")
     ap.add_argument("--sparse", type=int, default=0, choices=[0, 1, 2],
                     help="FFN: 0 dense, 1 device predictor top-k, 2 fixed mask (BASELINE config C4)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",

@@ -32,16 +32,16 @@ def top_gap(v):
     return float(t[1] - t[0])
 
 
-def run_from_cache(eng, orc, prompt, n_steps):
+def run_from_cache(eng, orc, prompt, n_steps, kv_pos=KV_POS):
     """The engine's cache -> the oracle, then the prompt, then n_steps greedy tokens on both;
     returns (max relative logits error, min top-1/top-2 gap)."""
-    k, v = eng.kv_read(KV_POS)
+    k, v = eng.kv_read(kv_pos)
     orc.load_kv_f16(k, v)
     want = None
     for t in prompt:
         want = orc.forward(t)
     got = eng.logits_host(prompt)
-    assert eng.n_past == KV_POS + len(prompt)
+    assert eng.n_past == kv_pos + len(prompt)
     worst, gap = rel_err(got, want), top_gap(want)
     assert worst < LOGIT_REL
     for step in range(n_steps):
@@ -89,5 +89,25 @@ def test_full_c3_model_at_bench_positions(cuda):
     worst, gap = run_from_cache(eng, orc, prompt, 8)
     print(f"C3 8B model, positions {KV_POS}..{KV_POS + 11}: max logits rel err {worst:.3g}, "
           f"min top-1/top-2 gap {gap:.3g}")
+    orc.close()
+    eng.close()
+
+
+def test_70b_shaped_layers_at_8192_positions(cuda):
+    """Two layers of the 70B shape (d 8192, 64/8 heads of 128, ff 28672, Q4_K weights;
+    vocabulary 32000) over a KV cache filled to 8192 positions (config C5's context): the
+    attention splits every kv head 18 ways over 513-position splits. 4 prompt tokens, then 8
+    greedy steps."""
+    import jinf
+    from jinf import _lib as L
+    shape = jinf.LlamaShape(2, 8192, 64, 8, 28672, 32000, 5e5)
+    syn = jinf.SynthModel(shape, seed=7, weight_type=L.Q4_K)
+    eng = jinf.Engine.from_synth(syn, max_context=8192 + 16, options=jinf.b200_options(eos_token=-1))
+    assert eng.persistent
+    eng.fill_kv_random(8192, seed=1)
+    orc = oracle.OracleModel(syn, max_ctx=8192 + 16, kv_f16=True)
+    prompt = [int(t) for t in np.random.default_rng(3).integers(0, shape.n_vocab, size=4)]
+    worst, gap = run_from_cache(eng, orc, prompt, 8, kv_pos=8192)
+    print(f"70B-shaped x2 layers, positions 8192..8203: max logits rel err {worst:.3g}, min top-1/top-2 gap {gap:.3g}")
     orc.close()
     eng.close()
