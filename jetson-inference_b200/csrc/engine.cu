@@ -429,6 +429,7 @@ struct jinf_engine_impl {
     // flagged words the phases hand on (step.h): h ping-pong [2][d], q [nq], the new K and V
     // rows [nk], the o input records and the down input records (xrec_bytes / 4 words each)
     unsigned long long* step_fx = nullptr;
+    unsigned long long* step_split = nullptr;  // [grid][2][64] partial rows of tiles shared between CTAs
     unsigned long long *fx_h[2] = {nullptr, nullptr}, *fx_q = nullptr, *fx_kv = nullptr, *fx_arec = nullptr,
                        *fx_grec = nullptr;
     StepParams sp_full{}, sp_body{};
@@ -936,9 +937,10 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     // input records: a tile pair of h is one 32-element block, a CTA's gate|up rows are whole
     // activation blocks and fit the 1024-float conversion buffer, as do a kv head's outputs
     const int gu_pairs = I->layers.empty() ? 0 : I->layers[0].gu_sh.pairs;
-    const int gu_per_cta = 2 * ((gu_pairs / 2 + I->num_sms - 1) / I->num_sms);
+    // gate|up pairs a CTA touches (its equal share of units starts and ends mid-pair at most)
+    const int gu_per_cta = (gu_pairs + I->num_sms - 1) / I->num_sms + 2;
     const bool records_ok = I->d % 32 == 0 && (I->Hl * I->hd) % 32 == 0 && gu_pairs % 2 == 0 &&
-                            gu_per_cta * 16 <= 1024 && G * I->hd <= 1024;
+                            gu_per_cta * 16 <= 1024 - 64 && G * I->hd <= 1024;
     if (G > ATTN_MAX_GROUP || (G & (G - 1)) || I->Hkvl > 64 || (I->hd != 64 && I->hd != 128) || smem > 227 * 1024 ||
         step_occupancy(smem, I->wfmt, nbuf) < 1 || !records_ok) {
         JINF_LOG("persistent step unavailable for this shape (%zu bytes of shared memory); using one kernel per "
@@ -976,11 +978,14 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     JINF_CUDA_CHECK(cudaMalloc(&I->step_done, sizeof(unsigned int)));
     JINF_CUDA_CHECK(cudaMalloc(&I->step_attn_part, sizeof(unsigned long long) * attn_words));
     JINF_CUDA_CHECK(cudaMemset(I->step_attn_part, 0, sizeof(unsigned long long) * attn_words));
+    JINF_CUDA_CHECK(cudaMalloc(&I->step_split, sizeof(unsigned long long) * (size_t)I->step_grid * 128));
+    JINF_CUDA_CHECK(cudaMemset(I->step_split, 0, sizeof(unsigned long long) * (size_t)I->step_grid * 128));
     JINF_CUDA_CHECK(cudaMemcpy(I->d_phases, all.data(), sizeof(StepPhase) * all.size(), cudaMemcpyHostToDevice));
     JINF_CUDA_CHECK(cudaMemset(I->step_done, 0, sizeof(unsigned int)));
     StepParams sp{};
     sp.done = I->step_done;
     sp.attn_part = I->step_attn_part;
+    sp.split_part = I->step_split;
     sp.st = I->st;
     sp.nq = I->Hl * I->hd;
     sp.nk = I->Hkvl * I->hd;
@@ -1188,7 +1193,7 @@ void free_impl(jinf_engine_impl* I) {
     }
     void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
                     I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
-                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_fx, I->pf_h, I->pf_y,
+                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_fx, I->step_split, I->pf_h, I->pf_y,
                     I->pf_att, I->pf_sc, I->pf_x16, I->pf_q16, I->pf_err, I->bundles, I->pred_w1,
                     I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp};
     for (void* p : ptrs)

@@ -82,6 +82,8 @@ struct StepParams {
     unsigned int* done;       // [1] CTAs that have left the step (zero at launch, cleared by the last)
     unsigned long long* attn_part;  // [Hkv][ATTN_MAX_SPLIT][ATTN_MAX_GROUP][hd + 2] flagged per-split
                                     // attention partials (acc, m, l)
+    unsigned long long* split_part;  // [grid][2][64] flagged partial rows of the (at most two) tiles a
+                                     // CTA shares with its neighbours in a GEMV phase
     DeviceState* st;
     int nq, nk, head_dim, max_ctx, n_heads, n_kv_heads;
     float rope_base, eps;
@@ -120,9 +122,12 @@ struct XchgLayout {
 };
 XchgLayout step_xchg_layout(int n_points, int tp_size, int d);
 
-// CTA c of C owns tile pairs [step_cta_tile(c), step_cta_tile(c + 1)) of every GEMV phase.
-// (c * T stays far below 2^32: at most a few hundred CTAs times tens of thousands of pairs.)
-__host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)((unsigned)(c * T) / (unsigned)C); }
+// CTA c of C owns units [step_cta_unit(c), step_cta_unit(c + 1)) of every GEMV phase of U
+// units (pair-major: unit p * groups + g), an equal share whatever the shape; a tile of
+// `gran` pairs that crosses a CTA boundary is merged by the CTA that holds its last unit.
+__host__ __device__ inline int step_cta_unit(int c, int C, int U) {
+    return (int)((unsigned long long)c * (unsigned long long)U / (unsigned long long)C);
+}
 
 // Shared bytes of the staged input for the widest GEMV phase, or of the attention scratch
 // (q of one kv head's query heads + per-warp partials), whichever is larger.

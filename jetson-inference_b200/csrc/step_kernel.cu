@@ -181,33 +181,13 @@ struct PhaseInfo {
     int fmts;  // StepPhase::fmts
 };
 
-// Byte offset of tile pair t in a phase's matrix (pairs below fmts >> 8 in format fmts & 15,
-// the rest in (fmts >> 4) & 15).
-__device__ __forceinline__ size_t pair_offset(int fmts, int groups, int t) {
-    const int ps = fmts >> 8;
-    const size_t ua = (size_t)groups * q4m_unit_bytes(fmts & 15);
-    return t <= ps ? (size_t)t * ua : (size_t)ps * ua + (size_t)(t - ps) * groups * q4m_unit_bytes((fmts >> 4) & 15);
-}
-
-// Tile pairs [t0, t1) of CTA `cta` (of C): balanced runs of `gran` pairs (T % gran == 0).
-__device__ __forceinline__ void cta_range(int cta, int C, int T, int gran, int& t0, int& t1) {
-    if (gran == 2) {
-        t0 = 2 * step_cta_tile(cta, C, T >> 1);
-        t1 = 2 * step_cta_tile(cta + 1, C, T >> 1);
-    } else {
-        t0 = step_cta_tile(cta, C, T);
-        t1 = step_cta_tile(cta + 1, C, T);
-    }
-}
-
-// Unit range [c0, c1) of warp `warp` of CTA `cta` (of C) in a pairs x groups matrix
-// (32-bit: a matrix has far fewer than 2^31 units).
-__device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int gran, int G, int& c0, int& c1) {
-    int t0, t1;
-    cta_range(cta, C, T, gran, t0, t1);
-    const int n = (t1 - t0) * G;
-    c0 = t0 * G + ((warp * n) >> 4);
-    c1 = t0 * G + (((warp + 1) * n) >> 4);
+// Unit range [c0, c1) of warp `warp` of CTA `cta` (of C) in a pairs x groups matrix: the
+// CTA's equal share of the T * G units, split evenly over its warps (32-bit: a matrix has far
+// fewer than 2^31 units).
+__device__ __forceinline__ void warp_range(int cta, int C, int warp, int T, int G, int& c0, int& c1) {
+    const int U = T * G, u0 = step_cta_unit(cta, C, U), n = step_cta_unit(cta + 1, C, U) - u0;
+    c0 = u0 + ((warp * n) >> 4);
+    c1 = u0 + (((warp + 1) * n) >> 4);
 }
 static_assert(NW == 16, "warp_range divides by the warp count with a shift");
 
@@ -235,7 +215,7 @@ __device__ __noinline__ StreamPosOf<M> stream_seek(const PhaseInfo* pinfo, int n
         const int G = pinfo[i].groups;
         if (!G) continue;
         int c0, c1;
-        warp_range(cta, C, warp, pinfo[i].pairs, pinfo[i].gran, G, c0, c1);
+        warp_range(cta, C, warp, pinfo[i].pairs, G, c0, c1);
         if (c0 < c1) {
             r.w = pinfo[i].w;
             r.ph = i;
@@ -267,15 +247,20 @@ __device__ __noinline__ StreamPosOf<M> stream_seek(const PhaseInfo* pinfo, int n
 // so that HBM keeps streaming weights through attention, input staging and merges.
 __device__ __noinline__ void prefetch_cta_range(const PhaseInfo& pi, int cta, int C, int ub, bool mixed) {
     if (!pi.groups) return;
-    int t0, t1;
-    cta_range(cta, C, pi.pairs, pi.gran, t0, t1);
-    if (t0 >= t1) return;
-    const size_t o0 = mixed ? pair_offset(pi.fmts, pi.groups, t0) : (size_t)t0 * pi.groups * ub;
-    const size_t o1 = mixed ? pair_offset(pi.fmts, pi.groups, t1) : (size_t)t1 * pi.groups * ub;
+    const int U = pi.pairs * pi.groups, u0 = step_cta_unit(cta, C, U), u1 = step_cta_unit(cta + 1, C, U);
+    if (u0 >= u1) return;
+    // byte offset of unit u: mixed matrices hold the pairs below the split in format fa
+    auto off = [&](int u) -> size_t {
+        if (!mixed) return (size_t)u * ub;
+        const int cs = (pi.fmts >> 8) * pi.groups;
+        const size_t ua = q4m_unit_bytes(pi.fmts & 15), uw = q4m_unit_bytes((pi.fmts >> 4) & 15);
+        return u <= cs ? (size_t)u * ua : (size_t)cs * ua + (size_t)(u - cs) * uw;
+    };
+    const size_t o0 = off(u0), o1 = off(u1);
     const uint8_t* b = pi.w + o0;
     const uint32_t bytes = (uint32_t)(o1 - o0);  // multiple of 16
-    for (uint32_t off = 0; off < bytes; off += (1u << 20))
-        prefetch_l2(b + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
+    for (uint32_t off2 = 0; off2 < bytes; off2 += (1u << 20))
+        prefetch_l2(b + off2, bytes - off2 < (1u << 20) ? bytes - off2 : (1u << 20));
 }
 
 // The weight stream of one warp between calls: ring slot of the next unit to consume and
@@ -1018,6 +1003,52 @@ __device__ __noinline__ void finish_pair(const StepParams& P, const StepPhase& d
     }
 }
 
+// A tile (gran pairs) whose units this CTA shares with neighbouring CTAs, by one warp: the CTA
+// that holds the tile's last unit merges it (its own rows plus the flagged partial rows the
+// earlier CTAs left in their slots, added in a fixed order) and runs the epilogue; the others
+// leave their rows in their slot `slot` (0: their first tile, 1: their last). own: this CTA's
+// rows of the tile ([gran][32], zero where it has no units).
+template <bool TP>
+__device__ __noinline__ void merge_split_tile(const StepParams& P, const StepPhase& d, const EpiCtx& ec, int t, int slot,
+                                              int U, int TG, const float* own, float* outs_s, ArgMax& am) {
+    const int lane = threadIdx.x & 31, C = gridDim.x, cta = blockIdx.x;
+    const int nr = d.gran * 32;  // rows of the tile
+    const int u1 = step_cta_unit(cta + 1, C, U);
+    if ((t + 1) * TG > u1) {  // not the merging CTA: leave the rows
+        u64w* dst = P.split_part + ((size_t)cta * 2 + slot) * 64;
+        for (int r = lane; r < nr; r += 32) st_w(dst + r, fword(own[r], ec.fl_out));
+        return;
+    }
+    float v[2] = {0.f, 0.f};  // rows lane, lane + 32
+    for (int k = 0; k < d.gran; ++k) v[k] = own[lane + 32 * k];
+    for (int c = cta - 1; c >= 0; --c) {  // the earlier CTAs that hold units of the tile
+        const int cu0 = step_cta_unit(c, C, U), cu1 = step_cta_unit(c + 1, C, U);
+        if (cu1 <= t * TG) break;
+        if (cu0 >= cu1) continue;
+        const u64w* src = P.split_part + ((size_t)c * 2 + (cu0 / TG == t ? 0 : 1)) * 64;
+        for (int k = 0; k < d.gran; ++k)
+            v[k] += fval(wait_word(src + lane + 32 * k, ld_w(src + lane + 32 * k), ec.fl_out, P.st, P.spin_limit));
+    }
+    if (d.epi == EPI_GATEUP) {
+        // both pairs of the activation block: neuron q of pair k from rows 2q (gate), 2q + 1 (up)
+        float* acts = outs_s + 1024 - 64 + 32 * slot;  // scratch past any pair's activations
+        const float g0 = __shfl_sync(JINF_FULL_MASK, v[0], (2 * lane) & 31), u0v = __shfl_sync(JINF_FULL_MASK, v[0], (2 * lane + 1) & 31);
+        const float g1 = __shfl_sync(JINF_FULL_MASK, v[1], (2 * lane) & 31), u1v = __shfl_sync(JINF_FULL_MASK, v[1], (2 * lane + 1) & 31);
+        const float g = (lane < 16 ? g0 : g1) * ec.fac, u = (lane < 16 ? u0v : u1v) * ec.fac;
+        const int nrow = 2 * (t * 32 + lane);  // the neuron's gate row
+        acts[lane] = nrow < d.rows ? g / (1.0f + expf(-g)) * u : 0.f;
+        __syncwarp();
+        const float4 x = reinterpret_cast<const float4*>(acts)[lane & 7];
+        octet_to_records_flag(x, lane, t & 3, d.fout + (size_t)(t >> 2) * 64,
+                              d.fout + (size_t)d.groups_out * 64 + (size_t)(t >> 2) * 16, ec.fl_out, lane < 8);
+        return;
+    }
+    // gran 1: lanes q < 16 take rows 2q, 2q + 1
+    const int q = lane & 15;
+    const float r0 = __shfl_sync(JINF_FULL_MASK, v[0], 2 * q), r1 = __shfl_sync(JINF_FULL_MASK, v[0], 2 * q + 1);
+    finish_pair<TP>(P, d, ec, t, r0, r1, outs_s, am);
+}
+
 // The last CTA to leave finishes the step: the argmax (tensor parallel: exchanged with every
 // rank) becomes the next input token, the position and the flag epoch advance, the exit
 // counter is cleared for the next launch.
@@ -1075,8 +1106,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const __grid_constant_
     int* fmid = ftile + NW;                                                  // [NW] first piece starts mid-tile
     float* part_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768);   // [NW][2][32] partial rows
     float* outs_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768 + 4096);  // [1024] outputs to convert
-    StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 8192);  // [2] descriptors
-    PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 8192 + 512);
+    float* split_s = reinterpret_cast<float*>(smem + P.xstage_bytes + 768 + 8192);   // [2 tiles][64] rows of
+                                                                                     // the shared tiles
+    StepPhase* dsm = reinterpret_cast<StepPhase*>(smem + P.xstage_bytes + 768 + 8192 + 512);  // [2] descriptors
+    PhaseInfo* pinfo = reinterpret_cast<PhaseInfo*>(smem + P.xstage_bytes + 768 + 8192 + 1024);
     const uint32_t ring_base = smem_u32(pinfo + ((P.n_phases + 1) & ~1));
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint32_t ring = ring_base + (uint32_t)(warp * NBUF * UB);
@@ -1152,9 +1185,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const __grid_constant_
                 prefetch_l2(reinterpret_cast<const uint8_t*>(base) + off, bytes - off < (1u << 20) ? bytes - off : (1u << 20));
         }
         const int G = d.groups;
-        int t0, t1;
-        cta_range(blockIdx.x, C, d.pairs, d.gran, t0, t1);
-        if (t0 >= t1) continue;
+        // this CTA's equal share [u0, u1) of the phase's units; the pairs [t0, t1) it touches; its
+        // first and last tile (gran pairs), which it may share with its neighbours
+        const int U = d.pairs * G, u0 = step_cta_unit(blockIdx.x, C, U), u1 = step_cta_unit(blockIdx.x + 1, C, U);
+        if (u0 >= u1) continue;
+        const int t0 = u0 / G, t1 = (u1 - 1) / G + 1, TG = d.gran * G;
+        const int tf = u0 / TG, tl = (u1 - 1) / TG;
+        const bool split_f = tf * TG < u0 || (tf + 1) * TG > u1;
+        const bool split_l = tl != tf && (tl + 1) * TG > u1;
+        if (tid < 128) split_s[tid] = 0.f;  // rows of a shared tile this CTA has no units of stay 0
         // Epilogue inputs that do not depend on this GEMV, prepared now by warps 1.. while
         // warp 0 starts the input staging (outs_s is free in these phases): the residual rows
         // of an EPI_RESID phase, the RoPE factors of an EPI_QKV phase. The staging ends with
@@ -1180,8 +1219,20 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const __grid_constant_
         JINF_TRACE(ph, 2);
         const XRecS xr{smem_u32(xbase), smem_u32(xbase + (size_t)G * 256)};
         const EpiCtx ec{fac, pos, fepoch, fl_out, t0, prow0, pre};
+        // a pair's rows: finished here when its tile lies inside this CTA's units, else kept in
+        // shared memory for the tile's merge with the neighbouring CTAs' partial rows
+        auto deliver = [&](int pr, float v0, float v1) {
+            const int t = pr / d.gran;
+            if (t * TG >= u0 && (t + 1) * TG <= u1) {
+                finish_pair<TP>(P, d, ec, pr, v0, v1, outs_s, am);
+            } else if (lane < 16) {
+                float* sp = split_s + (t == tf ? 0 : 64) + (pr - t * d.gran) * 32 + 2 * (lane & 15);
+                sp[0] = v0;
+                sp[1] = v1;
+            }
+        };
         int c, c1;
-        warp_range(blockIdx.x, C, warp, d.pairs, d.gran, G, c, c1);
+        warp_range(blockIdx.x, C, warp, d.pairs, G, c, c1);
         if (lane == 0) {
             ftile[warp] = -1;
             fmid[warp] = 0;
@@ -1209,7 +1260,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const __grid_constant_
             if (gb == 0 && ge == G) {
                 const int q = lane & 15;
                 const float v0 = unit_row(ps.acc, 2 * q), v1 = unit_row(ps.acc, 2 * q + 1);
-                finish_pair<TP>(P, d, ec, pair, v0, v1, outs_s, am);
+                deliver(pair, v0, v1);
             } else {
                 // a piece of a pair shared with the neighbouring warps: partial rows to shared memory
                 const int sl = first_piece ? 0 : 1;
@@ -1217,7 +1268,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const __grid_constant_
 #pragma unroll
                     for (int i = 0; i < 4; ++i) part_s[(warp * 2 + sl) * 32 + unit_row_of(i, lane)] = ps.acc[i];
                 }
-                if (gb == 0) {
+                if (gb == 0 || pair * G + gb == u0) {  // the piece starts the pair's units in this CTA
                     own_pair = pair;
                     own_slot = sl;
                 }
@@ -1253,12 +1304,16 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_step(const __grid_constant_
                     v1 += p1[w2];
                 }
             }
-            finish_pair<TP>(P, d, ec, own_pair, v0, v1, outs_s, am);
+            deliver(own_pair, v0, v1);
         }
+        if (split_f || split_l || d.epi == EPI_GATEUP) __syncthreads();  // split_s and outs_s are complete
+        if ((warp == 0 && split_f) || (warp == 1 && split_l))
+            merge_split_tile<TP>(P, d, ec, warp == 0 ? tf : tl, warp, U, TG, split_s + 64 * warp, outs_s, am);
         if (d.epi == EPI_GATEUP) {
-            __syncthreads();  // every activation of the CTA is in shared memory
-            // pairs [t0, t1) hold activation blocks [t0 / 2, t1 / 2) (gran 2)
-            blocks_to_records_flag(outs_s, t0 >> 1, (t1 - t0) >> 1, d.groups_out, d.fout, fl_out);
+            // tiles inside this CTA's units are whole activation blocks, their activations in
+            // outs_s from pair t0 on (the shared tiles' blocks are written by their merge)
+            const int b0 = (u0 + TG - 1) / TG, b1 = u1 / TG;
+            if (b1 > b0) blocks_to_records_flag(outs_s + (2 * b0 - t0) * 16, b0, b1 - b0, d.groups_out, d.fout, fl_out);
         }
         JINF_TRACE(ph, 5);
     }
@@ -1315,7 +1370,7 @@ XchgLayout step_xchg_layout(int n_points, int tp_size, int d) {
 
 size_t step_smem_bytes(unsigned int xstage_bytes, int n_phases, int fmt, int nbuf) {
     const size_t infos = sizeof(PhaseInfo) * (size_t)((n_phases + 1) & ~1);
-    return (size_t)xstage_bytes + 768 + 8192 + 512 + infos + (size_t)NW * nbuf * q4m_unit_bytes(fmt);
+    return (size_t)xstage_bytes + 768 + 8192 + 1024 + infos + (size_t)NW * nbuf * q4m_unit_bytes(fmt);
 }
 
 // The kernel instances: weight format x ring depth (STEP_NBUF, or 3 when a model's staged
