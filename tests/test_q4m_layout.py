@@ -193,3 +193,39 @@ def test_host_pack_matches_layout(qt, rows, cols):
     assert jinf.lib.jinf_b200_q4m_pack_host(w.ctypes.data_as(C.c_void_p), qt, out.ctypes.data_as(C.c_void_p),
                                             rows, cols) == 0
     assert np.array_equal(out, ref(w, rows, cols))
+
+
+def step_unit_offset(u, split_pairs, groups, unit_a, unit_b):
+    """Byte offset of unit u (pair-major: pair u // groups, group u % groups) in a persistent-step
+    phase whose first `split_pairs` pairs are in a format with unit_a-byte units and the rest
+    in one with unit_b-byte units (the step kernel's stream position and its L2 prefetch of a
+    CTA's unit range, csrc/step_kernel.cu)."""
+    cs = split_pairs * groups
+    return u * unit_a if u <= cs else cs * unit_a + (u - cs) * unit_b
+
+
+def test_split_phase_unit_offsets_match_the_packed_images():
+    """A QKV phase of a Q4_K_M-like layer streams [q | k] in Q4_K then v in Q6_K from one buffer:
+    the two host-packed images side by side. Every unit the offset rule addresses is that
+    image's unit (pair, group), at the packer's own offset ((pair * groups + group) * unit)."""
+    import jinf
+    rows_qk, rows_v, cols = 96, 32, 512
+    groups = cols // 128
+    wa = np.ascontiguousarray(q4_k_rows(rows_qk, cols, seed=1))
+    wb = np.ascontiguousarray(q4m_ref.random_q6k_rows(rows_v, cols, seed=2))
+    ia = np.zeros(jinf.lib.jinf_b200_q4m_bytes_qt(rows_qk, cols, 12), dtype=np.uint8)
+    ib = np.zeros(jinf.lib.jinf_b200_q4m_bytes_qt(rows_v, cols, 14), dtype=np.uint8)
+    assert jinf.lib.jinf_b200_q4m_pack_host(wa.ctypes.data_as(C.c_void_p), 12, ia.ctypes.data_as(C.c_void_p),
+                                            rows_qk, cols) == 0
+    assert jinf.lib.jinf_b200_q4m_pack_host(wb.ctypes.data_as(C.c_void_p), 14, ib.ctypes.data_as(C.c_void_p),
+                                            rows_v, cols) == 0
+    ua, ub = ia.size // (rows_qk // 32 * groups), ib.size // (rows_v // 32 * groups)
+    assert (ua, ub) == (2432, 3392)
+    buf = np.concatenate([ia, ib])
+    pa = rows_qk // 32
+    for u in range((pa + rows_v // 32) * groups):
+        o = step_unit_offset(u, pa, groups, ua, ub)
+        p, g = divmod(u, groups)
+        want = ia[(p * groups + g) * ua:][:ua] if p < pa else ib[((p - pa) * groups + g) * ub:][:ub]
+        assert np.array_equal(buf[o:o + want.size], want), u
+    assert step_unit_offset((pa + rows_v // 32) * groups, pa, groups, ua, ub) == buf.size
