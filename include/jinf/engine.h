@@ -105,6 +105,8 @@ typedef struct jinf_b200_options {
     int   prefill;          // forward() of several tokens runs all but the last through the batched
                             // prefill (tensor-core projections over all tokens at once) where the
                             // model allows it: one GPU, Q4_0 weights, dense FFN (default 1)
+    int   max_seqs;         // sequences with a KV cache of their own for jinf_engine_decode_batch
+                            // (1..8, default 1; sequence 0 is the one forward()/generate() use)
 } jinf_b200_options;
 
 static inline jinf_b200_options jinf_b200_options_default(void) {
@@ -121,6 +123,7 @@ static inline jinf_b200_options jinf_b200_options_default(void) {
     o.sparse_seed = 0;
     o.persistent = 1;
     o.prefill = 1;
+    o.max_seqs = 1;
     return o;
 }
 
@@ -196,6 +199,25 @@ uint64_t    jinf_engine_weight_bytes_per_token(const jinf_engine* e);
 // down, lm_head, sparse_ffn (sparse modes: the whole FFN of a layer; 0 in dense mode, where
 // gate_up and down are the FFN). bytes receives the algorithmic bytes of one launch of each.
 jinf_status jinf_engine_profile_kernels(jinf_engine* e, int reps, double* times_us, double* bytes);
+
+// ---- Multi-sequence decode (new; the reference decodes one sequence) ----
+// Sequences 0 .. max_seqs - 1 each have a KV cache and a position of their own; sequence 0 is
+// the one forward(), generate() and e->n_past describe. decode_batch advances n distinct
+// sequences (1 <= n <= max_seqs) by one token in one step, every projection's weights streamed
+// once for all of them: tokens[i] is fed to sequence seqs[i] at its position, next_tokens[i]
+// (host, may be NULL) receives that sequence's greedy argmax (first maximum wins) and logits
+// (host, may be NULL; one GPU only) the fp32 logits [n][n_vocab]. Dense FFN models. Under
+// tensor parallelism every rank makes the same call. The prompt of a sequence is fed the same
+// way, one token per call (its argmax ignored).
+jinf_status jinf_engine_decode_batch(jinf_engine* e, int n, const int32_t* seqs, const int32_t* tokens,
+                                     int32_t* next_tokens, float* logits);
+// Tokens in the KV cache of sequence `seq` (-1 for an invalid sequence).
+int         jinf_engine_seq_n_past(const jinf_engine* e, int seq);
+// Forget sequence `seq` (its position returns to 0).
+jinf_status jinf_engine_seq_reset(jinf_engine* e, int seq);
+// jinf_engine_fill_kv_random / jinf_engine_kv_read for the cache of sequence `seq`.
+jinf_status jinf_engine_seq_fill_kv_random(jinf_engine* e, int seq, int n_pos, uint64_t seed);
+jinf_status jinf_engine_seq_kv_read(jinf_engine* e, int seq, int n_pos, uint16_t* k_host, uint16_t* v_host);
 
 // nccl unique id (128 bytes) for tensor-parallel set-up; rank 0 creates it and the
 // caller distributes it. Returns JINF_ERR_CUDA if NCCL cannot be loaded.

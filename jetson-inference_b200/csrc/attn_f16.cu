@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "device_state.cuh"
 #include "attn_f16.h"
+#include "multi.h"
 
 #include <math.h>
 
@@ -61,14 +62,30 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
 
     pdl_wait();
     pdl_trigger();
-    const int n = p.st->pos + 1;
+    // one sequence (st), or vector blockIdx.y of a multi-sequence step (ms)
+    const int vec = blockIdx.y;
+    const float* qv = p.q;
+    float* outv = p.out;
+    float* partv = p.partial;
+    unsigned int* cntv = p.ms ? p.ms->attn_count + vec * MULTI_MAX_KV_HEADS : p.st->attn_count;
+    size_t so = 0;
+    int n;
+    if (p.ms) {
+        n = p.ms->pos[vec] + 1;
+        so = (size_t)p.ms->seq[vec] * p.seq_stride;
+        qv += (size_t)vec * p.q_stride;
+        outv += (size_t)vec * p.q_stride;
+        partv += (size_t)p.n_kv_heads * p.n_split * (AMAXG * HD + 2 * AMAXG) * vec;
+    } else {
+        n = p.st->pos + 1;
+    }
     const float scale = rsqrtf((float)HD);
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) sm.q[i] = p.q[(size_t)kvh * G * HD + i] * scale;
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) sm.q[i] = qv[(size_t)kvh * G * HD + i] * scale;
     __syncthreads();
 
     const int start = (int)((int64_t)n * split / p.n_split), end = (int)((int64_t)n * (split + 1) / p.n_split);
-    const __half* kb = p.kcache + (size_t)kvh * p.max_ctx * HD;
-    const __half* vb = p.vcache + (size_t)kvh * p.max_ctx * HD;
+    const __half* kb = p.kcache + so + (size_t)kvh * p.max_ctx * HD;
+    const __half* vb = p.vcache + so + (size_t)kvh * p.max_ctx * HD;
     __half* ksm = sm.k[wid];
     __half* vsm = sm.v[wid];
 
@@ -167,7 +184,7 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
     __syncthreads();
     // CTA partial -> global
     const size_t stride = AMAXG * HD + 2 * AMAXG;
-    float* part = p.partial + ((size_t)kvh * p.n_split + split) * stride;
+    float* part = partv + ((size_t)kvh * p.n_split + split) * stride;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int g = i / HD, d = i % HD;
         float M = -INFINITY;
@@ -190,14 +207,14 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&p.st->attn_count[kvh], 1u);
+        const unsigned prev = atomicAdd(&cntv[kvh], 1u);
         sm.is_last = prev == (unsigned)(p.n_split - 1);
     }
     __syncthreads();
     if (!sm.is_last) return;
     __threadfence();
     // merge the n_split partials of this kv head in split order
-    const float* base = p.partial + (size_t)kvh * p.n_split * stride;
+    const float* base = partv + (size_t)kvh * p.n_split * stride;
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
         const int g = i / HD, d = i % HD;
         float M = -INFINITY;
@@ -210,9 +227,9 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
             a = fmaf(__ldcg(base + s2 * stride + g * HD + d), f, a);
             L = fmaf(__ldcg(base + s2 * stride + AMAXG * HD + AMAXG + g), f, L);
         }
-        p.out[(size_t)(kvh * G + g) * HD + d] = a / L;
+        outv[(size_t)(kvh * G + g) * HD + d] = a / L;
     }
-    if (threadIdx.x == 0) p.st->attn_count[kvh] = 0u;
+    if (threadIdx.x == 0) cntv[kvh] = 0u;
 }
 
 size_t attn_partial_floats(int n_kv_heads, int n_split, int head_dim) {
@@ -221,6 +238,7 @@ size_t attn_partial_floats(int n_kv_heads, int n_split, int head_dim) {
 
 cudaError_t attn_launch(const AttnParams& p, cudaStream_t s, bool pdl) {
     if (p.n_heads % p.n_kv_heads || p.n_heads / p.n_kv_heads > AMAXG || p.n_kv_heads > 64) return cudaErrorInvalidValue;
+    if (p.ms && (p.n_vec < 1 || p.n_vec > MULTI_MAX || p.n_kv_heads > MULTI_MAX_KV_HEADS)) return cudaErrorInvalidValue;
     if (p.head_dim != 64 && p.head_dim != 128) return cudaErrorInvalidValue;
     const size_t smem = attn_smem_bytes(p.head_dim);
     static bool configured[2] = {false, false};
@@ -233,7 +251,7 @@ cudaError_t attn_launch(const AttnParams& p, cudaStream_t s, bool pdl) {
         configured[which] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.n_kv_heads * p.n_split);
+    cfg.gridDim = dim3(p.n_kv_heads * p.n_split, p.ms ? p.n_vec : 1);
     cfg.blockDim = dim3(AW * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;

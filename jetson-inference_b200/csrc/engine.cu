@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "device_state.cuh"
 #include "gemv.h"
+#include "multi.h"
 #include "nccl_shim.h"
 #include "prefill.h"
 #include "q4m.cuh"
@@ -316,7 +317,9 @@ __global__ void k_gather_blocks(const uint8_t* __restrict__ src, uint8_t* __rest
 
 
 enum OpKind { OP_GEMV = 0, OP_ATTN = 1, OP_ALLREDUCE_F32 = 2, OP_ALLREDUCE_MAXU64 = 3, OP_FINALIZE = 4,
-              OP_SPARSE_FFN = 5 };
+              OP_SPARSE_FFN = 5,
+              // multi-sequence step (multi.h)
+              OP_MGEMV = 6, OP_MEMBED = 7, OP_MRESID = 8, OP_MFINAL = 9 };
 enum GemvRole { ROLE_QKV = 0, ROLE_O = 1, ROLE_GATEUP = 2, ROLE_DOWN = 3, ROLE_LM = 4, ROLE_NONE = 5 };
 
 struct Op {
@@ -330,6 +333,8 @@ struct Op {
     size_t count = 0;
     int with_argmax = 0;
     uint64_t bytes = 0;  // algorithmic bytes of the op (weights + vectors)
+    MultiParams mp{};    // OP_MGEMV (xm, epi, grid as above)
+    int n_vec = 0;       // multi-sequence ops: vectors of the step
 };
 
 }  // namespace
@@ -440,6 +445,20 @@ struct jinf_engine_impl {
     float *pf_h = nullptr, *pf_y = nullptr, *pf_att = nullptr, *pf_sc = nullptr;
     __half *pf_x16 = nullptr, *pf_q16 = nullptr;
     int* pf_err = nullptr;
+    // multi-sequence decode (multi.h): n_seqs KV caches of seq_stride elements each (sequence
+    // 0 = the one-sequence cache), the positions of sequences 1.. (sequence 0's is e->n_past),
+    // the step's vectors [n_seqs][...], and one op list / graph per vector count
+    int n_seqs = 1;
+    size_t seq_stride = 0;
+    std::vector<int> seq_past;
+    MultiState* ms = nullptr;
+    int32_t* ms_pinned = nullptr;  // [3 * MULTI_MAX] step inputs (token, pos, seq), then [MULTI_MAX] outputs
+    float *m_h = nullptr, *m_y = nullptr, *m_q = nullptr, *m_attn = nullptr, *m_act = nullptr, *m_logits = nullptr,
+          *m_ssq = nullptr, *m_attn_part = nullptr, *m_part = nullptr;
+    unsigned int* m_cnt = nullptr;
+    int m_split = 1;  // attention splits of a multi step
+    std::vector<Op> m_ops[MULTI_MAX + 1];
+    cudaGraphExec_t m_exec[MULTI_MAX + 1] = {};
     // ops and graphs
     std::vector<Op> ops_full, ops_body;
     cudaGraphExec_t exec_full = nullptr, exec_body = nullptr;
@@ -456,6 +475,10 @@ jinf_status run_op(jinf_engine_impl* I, const Op& op, cudaStream_t s) {
         case OP_GEMV: e = gemvm_launch(op.gp, op.xm, op.epi, op.grid, s, true); break;
         case OP_ATTN: e = attn_launch(op.ap, s, true); break;
         case OP_FINALIZE: k_finalize<<<1, 1, 0, s>>>(I->st, op.with_argmax); e = cudaGetLastError(); break;
+        case OP_MGEMV: e = multi_gemv_launch(op.mp, op.xm, op.epi, op.grid, s, true); break;
+        case OP_MEMBED: e = multi_embed_launch(I->embed, I->ms, op.n_vec, I->d, I->m_h, I->m_ssq, s, true); break;
+        case OP_MRESID: e = multi_resid_launch(I->m_h, I->m_y, op.n_vec, I->d, I->m_ssq, s, true); break;
+        case OP_MFINAL: e = multi_finalize_launch(I->ms, op.n_vec, s); break;
         case OP_SPARSE_FFN: {
             // h = h + y_o; x = RMSNorm(h) * ffn_norm; [predictor]; y_down = FFN over the active
             // neurons (the next layer's QKV prologue adds y_down to h)
@@ -712,6 +735,181 @@ void build_ops(jinf_engine_impl* I, bool with_head, std::vector<Op>& ops) {
     }
     Op fin{OP_FINALIZE};
     fin.with_argmax = with_head ? 1 : 0;
+    ops.push_back(fin);
+}
+
+// Op list of one multi-sequence step over n vectors (vector v = a sequence's token). Per layer:
+//   [embedding rows (layer 0)] -> QKV (x = RMSNorm(h), RoPE at each vector's position, k/v
+//   into each vector's sequence cache) -> attention (vector v over its sequence's positions)
+//   -> o (h += W attn, and the new h's sums of squares for the next RMSNorm) -> gate|up
+//   (x = RMSNorm(h), SiLU(gate) up) -> down (h += W act)
+// then the LM head (x = RMSNorm(h), logits and each vector's argmax) and the finaliser. Tensor
+// parallel: o and down store their partial outputs, which an allreduce sums before the residual
+// add, and the argmax keys are reduced across the ranks.
+Op multi_gemv_op(jinf_engine_impl* I, int n, const uint8_t* w, const Q4MShape& sh, int xm, int epi) {
+    Op op{OP_MGEMV};
+    op.xm = xm;
+    op.epi = epi;
+    op.n_vec = n;
+    op.grid = multi_grid(I->num_sms);
+    MultiParams& p = op.mp;
+    p.w = w;
+    p.rows = sh.rows;
+    p.cols = sh.cols;
+    p.pairs = sh.pairs;
+    p.groups = sh.groups;
+    p.fmt = sh.fmt;
+    p.n = n;
+    p.kw = multi_pick_kw(sh.pairs, sh.groups, n, sh.fmt, op.grid);
+    p.gk = p.kw > 0 ? (sh.groups + p.kw - 1) / p.kw : 0;
+    p.part = I->m_part;
+    p.cnt = I->m_cnt;
+    p.ms = I->ms;
+    p.eps = I->eps;
+    p.ssq = I->m_ssq;
+    p.ssq_parts = I->d / 32;
+    op.bytes = (uint64_t)sh.rows * aos_row_bytes(sh.fmt, sh.cols);
+    return op;
+}
+
+void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
+    ops.clear();
+    const int d = I->d, nq = I->Hl * I->hd, nk = I->Hkvl * I->hd;
+    const bool tp = I->tp_size > 1;
+    auto resid = [&](Op& g) {  // o / down: residual add (one GPU) or partial + allreduce + add
+        if (!tp) {
+            g.epi = ME_RESID;
+            g.mp.y = I->m_h;
+            g.mp.ldy = d;
+            g.mp.ssq_out = I->m_ssq;
+            ops.push_back(g);
+            return;
+        }
+        g.epi = ME_STORE;
+        g.mp.y = I->m_y;
+        g.mp.ldy = d;
+        ops.push_back(g);
+        Op ar{OP_ALLREDUCE_F32};
+        ar.buf = I->m_y;
+        ar.count = (size_t)n * d;
+        ops.push_back(ar);
+        Op ad{OP_MRESID};
+        ad.n_vec = n;
+        ops.push_back(ad);
+    };
+    Op em{OP_MEMBED};
+    em.n_vec = n;
+    ops.push_back(em);
+    for (int L = 0; L < I->L; ++L) {
+        const auto& ly = I->layers[L];
+        __half* kc = I->kc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        __half* vc = I->vc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        Op qkv = multi_gemv_op(I, n, ly.qkv, ly.qkv_sh, MX_NORMED, ME_QKV);
+        qkv.role = ROLE_QKV;
+        qkv.layer = L;
+        MultiParams& qp = qkv.mp;
+        qp.x = I->m_h;
+        qp.ldx = d;
+        qp.norm_w = ly.attn_norm;
+        qp.y = I->m_q;
+        qp.ldy = nq;
+        qp.kcache = kc;
+        qp.vcache = vc;
+        qp.seq_stride = I->seq_stride;
+        qp.nq = nq;
+        qp.nk = nk;
+        qp.head_dim = I->hd;
+        qp.max_ctx = I->max_ctx;
+        qp.rope_base = I->rope_base;
+        qp.pf_ptr = ly.v ? ly.v : ly.o;
+        qp.pf_bytes = ly.v ? ly.v_sh.bytes : ly.o_sh.bytes;
+        ops.push_back(qkv);
+        if (ly.v) {  // v of another weight type: every row a v row
+            Op v = multi_gemv_op(I, n, ly.v, ly.v_sh, MX_NORMED, ME_QKV);
+            v.mp = qp;
+            v.mp.w = ly.v;
+            v.mp.rows = ly.v_sh.rows;
+            v.mp.pairs = ly.v_sh.pairs;
+            v.mp.groups = ly.v_sh.groups;
+            v.mp.fmt = ly.v_sh.fmt;
+            v.mp.kw = multi_pick_kw(ly.v_sh.pairs, ly.v_sh.groups, n, ly.v_sh.fmt, v.grid);
+            v.mp.gk = v.mp.kw > 0 ? (ly.v_sh.groups + v.mp.kw - 1) / v.mp.kw : 0;
+            v.mp.nq = 0;
+            v.mp.nk = 0;
+            v.mp.pf_ptr = ly.o;
+            v.mp.pf_bytes = ly.o_sh.bytes;
+            v.bytes = (uint64_t)ly.v_sh.rows * aos_row_bytes(ly.v_sh.fmt, ly.v_sh.cols);
+            ops.push_back(v);
+        }
+        Op at{OP_ATTN};
+        at.layer = L;
+        at.n_vec = n;
+        at.ap.q = I->m_q;
+        at.ap.kcache = kc;
+        at.ap.vcache = vc;
+        at.ap.out = I->m_attn;
+        at.ap.partial = I->m_attn_part;
+        at.ap.n_heads = I->Hl;
+        at.ap.n_kv_heads = I->Hkvl;
+        at.ap.head_dim = I->hd;
+        at.ap.max_ctx = I->max_ctx;
+        at.ap.n_split = I->m_split;
+        at.ap.st = I->st;
+        at.ap.ms = I->ms;
+        at.ap.n_vec = n;
+        at.ap.seq_stride = I->seq_stride;
+        at.ap.q_stride = nq;
+        ops.push_back(at);
+
+        Op o = multi_gemv_op(I, n, ly.o, ly.o_sh, MX_PLAIN_F32, ME_RESID);
+        o.role = ROLE_O;
+        o.layer = L;
+        o.mp.x = I->m_attn;
+        o.mp.ldx = nq;
+        o.mp.pf_ptr = ly.gu;
+        o.mp.pf_bytes = ly.gu_sh.bytes;
+        resid(o);
+
+        Op gu = multi_gemv_op(I, n, ly.gu, ly.gu_sh, MX_NORMED, ME_GATEUP);
+        gu.role = ROLE_GATEUP;
+        gu.layer = L;
+        gu.mp.x = I->m_h;
+        gu.mp.ldx = d;
+        gu.mp.norm_w = ly.ffn_norm;
+        gu.mp.y = I->m_act;
+        gu.mp.ldy = I->ffl;
+        gu.mp.pf_ptr = ly.down;
+        gu.mp.pf_bytes = ly.down_sh.bytes;
+        ops.push_back(gu);
+
+        Op dn = multi_gemv_op(I, n, ly.down, ly.down_sh, MX_PLAIN_F32, ME_RESID);
+        dn.role = ROLE_DOWN;
+        dn.layer = L;
+        dn.mp.x = I->m_act;
+        dn.mp.ldx = I->ffl;
+        dn.mp.pf_ptr = L + 1 < I->L ? I->layers[L + 1].qkv : I->lm;
+        dn.mp.pf_bytes = L + 1 < I->L ? I->layers[L + 1].qkv_sh.bytes : I->lm_sh.bytes;
+        resid(dn);
+    }
+    Op lm = multi_gemv_op(I, n, I->lm, I->lm_sh, MX_NORMED, ME_LMHEAD);
+    lm.role = ROLE_LM;
+    lm.mp.x = I->m_h;
+    lm.mp.ldx = d;
+    lm.mp.norm_w = I->out_norm;
+    lm.mp.y = I->m_logits;
+    lm.mp.ldy = I->Vl;
+    lm.mp.vocab_offset = I->vocab_off;
+    lm.mp.pf_ptr = I->layers[0].qkv;
+    lm.mp.pf_bytes = I->layers[0].qkv_sh.bytes;
+    ops.push_back(lm);
+    if (tp) {
+        Op ar{OP_ALLREDUCE_MAXU64};
+        ar.buf = I->ms->best;
+        ar.count = (size_t)n;
+        ops.push_back(ar);
+    }
+    Op fin{OP_MFINAL};
+    fin.n_vec = n;
     ops.push_back(fin);
 }
 
@@ -1185,6 +1383,8 @@ void free_impl(jinf_engine_impl* I) {
     if (I->device >= 0) cudaSetDevice(I->device);
     if (I->exec_full) cudaGraphExecDestroy(I->exec_full);
     if (I->exec_body) cudaGraphExecDestroy(I->exec_body);
+    for (cudaGraphExec_t& g : I->m_exec)
+        if (g) cudaGraphExecDestroy(g);
     if (I->stream) cudaStreamSynchronize(I->stream);
     free_exchange(I);  // every write of a peer into this area landed before our last step ended
     if (I->comm) {
@@ -1195,11 +1395,14 @@ void free_impl(jinf_engine_impl* I) {
                     I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
                     I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_fx, I->step_split, I->pf_h, I->pf_y,
                     I->pf_att, I->pf_sc, I->pf_x16, I->pf_q16, I->pf_err, I->bundles, I->pred_w1,
-                    I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp};
+                    I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp,
+                    I->ms, I->m_h, I->m_y, I->m_q, I->m_attn, I->m_act, I->m_logits, I->m_ssq, I->m_attn_part,
+                    I->m_part, I->m_cnt};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);
     if (I->pinned) cudaFreeHost(I->pinned);
+    if (I->ms_pinned) cudaFreeHost(I->ms_pinned);
     if (I->ev0) cudaEventDestroy(I->ev0);
     if (I->ev1) cudaEventDestroy(I->ev1);
     if (I->stream) cudaStreamDestroy(I->stream);
@@ -1429,15 +1632,22 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     I->lm = I->arena + (uintptr_t)I->lm;
 
     // ---- other buffers
-    const size_t kv_elems = (size_t)I->L * I->Hkvl * I->max_ctx * hd;
+    const size_t kv_elems = (size_t)I->L * I->Hkvl * I->max_ctx * hd;  // one sequence's cache
+    I->n_seqs = opt.max_seqs < 1 ? 1 : opt.max_seqs;
+    if (I->n_seqs > MULTI_MAX || (I->n_seqs > 1 && I->sparse_mode)) {
+        JINF_LOG("max_seqs must be 1..%d (dense FFN for more than one sequence)", MULTI_MAX);
+        return fail(JINF_ERR_INVALID);
+    }
+    I->seq_stride = kv_elems;
+    I->seq_past.assign(I->n_seqs, 0);
     I->n_split = (I->max_ctx + 63) / 64;
     const int max_split = (2 * I->num_sms) / I->Hkvl;
     if (I->n_split > max_split) I->n_split = max_split;
     if (I->n_split < 1) I->n_split = 1;
     bool ok = cudaMalloc(&I->norms, sizeof(float) * (size_t)(2 * I->L + 1) * d) == cudaSuccess &&
               cudaMalloc(&I->embed, sizeof(float) * (size_t)I->V * d) == cudaSuccess &&
-              cudaMalloc(&I->kc, sizeof(__half) * kv_elems) == cudaSuccess &&
-              cudaMalloc(&I->vc, sizeof(__half) * kv_elems) == cudaSuccess &&
+              cudaMalloc(&I->kc, sizeof(__half) * kv_elems * I->n_seqs) == cudaSuccess &&
+              cudaMalloc(&I->vc, sizeof(__half) * kv_elems * I->n_seqs) == cudaSuccess &&
               cudaMalloc(&I->hA, sizeof(float) * d) == cudaSuccess &&
               cudaMalloc(&I->hB, sizeof(float) * d) == cudaSuccess &&
               cudaMalloc(&I->y_o, sizeof(float) * d) == cudaSuccess &&
@@ -1454,8 +1664,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     if (ok && tp > 1) ok = cudaMalloc(&I->logits_full, sizeof(float) * (size_t)I->V) == cudaSuccess;
     if (!ok) return fail(JINF_ERR_OOM);
     if (tp == 1) I->logits_full = I->logits;
-    cudaMemset(I->kc, 0, sizeof(__half) * kv_elems);
-    cudaMemset(I->vc, 0, sizeof(__half) * kv_elems);
+    cudaMemset(I->kc, 0, sizeof(__half) * kv_elems * I->n_seqs);
+    cudaMemset(I->vc, 0, sizeof(__half) * kv_elems * I->n_seqs);
     cudaMemset(I->st, 0, sizeof(DeviceState));
     cudaMemset(I->y_o, 0, sizeof(float) * d);
     cudaMemset(I->y_down, 0, sizeof(float) * d);
@@ -1645,6 +1855,42 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             cudaMalloc(&I->gemv_cnt, sizeof(unsigned int) * pairs) != cudaSuccess)
             return fail(JINF_ERR_OOM);
         cudaMemset(I->gemv_cnt, 0, sizeof(unsigned int) * pairs);
+    }
+    // ---- multi-sequence step buffers (the GEMV workspace sized for the K splits every vector
+    // count picks; arrival counters zero, self-resetting)
+    if (!I->sparse_mode) {
+        const int S = I->n_seqs, nq = I->Hl * hd;
+        const int grid = multi_grid(I->num_sms);
+        size_t ws = 0, pairs = 0;
+        for (int n = 1; n <= S; ++n) {
+            auto need = [&](const Q4MShape& sh) {
+                if (!sh.rows) return;
+                const int kw = multi_pick_kw(sh.pairs, sh.groups, n, sh.fmt, grid);
+                ws = std::max(ws, (size_t)sh.pairs * std::max(kw, 1) * n * 32);
+                pairs = std::max(pairs, (size_t)sh.pairs);
+            };
+            need(I->lm_sh);
+            for (const auto& ly : I->layers)
+                for (const Q4MShape* sh : {&ly.qkv_sh, &ly.v_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) need(*sh);
+        }
+        // attention splits: about four CTAs per SM at one vector, whole 64-position spans
+        I->m_split = std::max(1, std::min((I->max_ctx + 63) / 64, (4 * I->num_sms + I->Hkvl - 1) / I->Hkvl));
+        const size_t attn_part = attn_partial_floats(I->Hkvl, I->m_split, hd) * S;
+        bool mok = cudaMalloc(&I->ms, sizeof(MultiState)) == cudaSuccess &&
+                   cudaHostAlloc(&I->ms_pinned, sizeof(int32_t) * 4 * MULTI_MAX, cudaHostAllocDefault) == cudaSuccess &&
+                   cudaMalloc(&I->m_h, sizeof(float) * (size_t)S * d) == cudaSuccess &&
+                   cudaMalloc(&I->m_y, sizeof(float) * (size_t)S * d) == cudaSuccess &&
+                   cudaMalloc(&I->m_q, sizeof(float) * (size_t)S * nq) == cudaSuccess &&
+                   cudaMalloc(&I->m_attn, sizeof(float) * (size_t)S * nq) == cudaSuccess &&
+                   cudaMalloc(&I->m_act, sizeof(float) * (size_t)S * I->ffl) == cudaSuccess &&
+                   cudaMalloc(&I->m_logits, sizeof(float) * (size_t)S * I->Vl) == cudaSuccess &&
+                   cudaMalloc(&I->m_ssq, sizeof(float) * (size_t)S * (d / 32)) == cudaSuccess &&
+                   cudaMalloc(&I->m_attn_part, sizeof(float) * attn_part) == cudaSuccess &&
+                   cudaMalloc(&I->m_part, sizeof(float) * std::max(ws, (size_t)1)) == cudaSuccess &&
+                   cudaMalloc(&I->m_cnt, sizeof(unsigned int) * std::max(pairs, (size_t)1)) == cudaSuccess;
+        if (!mok) return fail(JINF_ERR_OOM);
+        cudaMemset(I->ms, 0, sizeof(MultiState));
+        cudaMemset(I->m_cnt, 0, sizeof(unsigned int) * std::max(pairs, (size_t)1));
     }
     // mixed models in the persistent step: a v of its own type must follow its [q | k] rows
     // directly (one phase streams both) and start on a tile pair
@@ -1880,6 +2126,7 @@ extern "C" void jinf_engine_reset(jinf_engine* e) {
     cudaMemsetAsync(I->st, 0, offsetof(DeviceState, epoch), I->stream);  // the step epoch is kept
     cudaStreamSynchronize(I->stream);
     e->n_past = 0;
+    std::fill(I->seq_past.begin(), I->seq_past.end(), 0);
     I->logits_valid = false;
     memset(&e->perf, 0, sizeof e->perf);
 }
@@ -1987,32 +2234,128 @@ extern "C" jinf_status jinf_engine_decode_resident(jinf_engine* e, int n_steps, 
     return JINF_OK;
 }
 
-extern "C" jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uint64_t seed) {
-    if (!e || !e->impl || n_pos < 0 || n_pos > e->impl->max_ctx) return JINF_ERR_INVALID;
+extern "C" jinf_status jinf_engine_seq_fill_kv_random(jinf_engine* e, int seq, int n_pos, uint64_t seed) {
+    if (!e || !e->impl || n_pos < 0 || n_pos > e->impl->max_ctx || seq < 0 || seq >= e->impl->n_seqs)
+        return JINF_ERR_INVALID;
     jinf_engine_impl* I = e->impl;
     JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    const size_t so = (size_t)seq * I->seq_stride;
     if (n_pos > 0) {
-        k_fill_kv_random<<<4 * I->num_sms, 256, 0, I->stream>>>(I->kc, I->vc, I->L, I->Hkvl, I->max_ctx, I->hd, n_pos,
-                                                               (unsigned long long)seed);
+        k_fill_kv_random<<<4 * I->num_sms, 256, 0, I->stream>>>(I->kc + so, I->vc + so, I->L, I->Hkvl, I->max_ctx, I->hd,
+                                                               n_pos, (unsigned long long)seed);
         JINF_CUDA_CHECK(cudaGetLastError());
     }
-    // set the device position; the token stays whatever was last fed
-    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->pos, &n_pos, sizeof(int), cudaMemcpyHostToDevice, I->stream));
+    if (seq == 0) {  // set the device position; the token stays whatever was last fed
+        JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->pos, &n_pos, sizeof(int), cudaMemcpyHostToDevice, I->stream));
+        e->n_past = n_pos;
+    } else {
+        I->seq_past[seq] = n_pos;
+    }
     JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
-    e->n_past = n_pos;
+    return JINF_OK;
+}
+
+extern "C" jinf_status jinf_engine_fill_kv_random(jinf_engine* e, int n_pos, uint64_t seed) {
+    return jinf_engine_seq_fill_kv_random(e, 0, n_pos, seed);
+}
+
+extern "C" jinf_status jinf_engine_seq_kv_read(jinf_engine* e, int seq, int n_pos, uint16_t* k_host, uint16_t* v_host) {
+    if (!e || !e->impl || !k_host || !v_host || n_pos <= 0 || n_pos > e->impl->max_ctx || seq < 0 ||
+        seq >= e->impl->n_seqs)
+        return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    // the cache is [layer][kv head][max_ctx][hd]: one strided copy per cache, rows of n_pos * hd
+    const size_t so = (size_t)seq * I->seq_stride;
+    const size_t w = (size_t)n_pos * I->hd * sizeof(__half), pitch = (size_t)I->max_ctx * I->hd * sizeof(__half);
+    const size_t h = (size_t)I->L * I->Hkvl;
+    JINF_CUDA_CHECK(cudaMemcpy2DAsync(k_host, w, I->kc + so, pitch, w, h, cudaMemcpyDeviceToHost, I->stream));
+    JINF_CUDA_CHECK(cudaMemcpy2DAsync(v_host, w, I->vc + so, pitch, w, h, cudaMemcpyDeviceToHost, I->stream));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
     return JINF_OK;
 }
 
 extern "C" jinf_status jinf_engine_kv_read(jinf_engine* e, int n_pos, uint16_t* k_host, uint16_t* v_host) {
-    if (!e || !e->impl || !k_host || !v_host || n_pos <= 0 || n_pos > e->impl->max_ctx) return JINF_ERR_INVALID;
+    return jinf_engine_seq_kv_read(e, 0, n_pos, k_host, v_host);
+}
+
+extern "C" int jinf_engine_seq_n_past(const jinf_engine* e, int seq) {
+    if (!e || !e->impl || seq < 0 || seq >= e->impl->n_seqs) return -1;
+    return seq == 0 ? e->n_past : e->impl->seq_past[seq];
+}
+
+extern "C" jinf_status jinf_engine_seq_reset(jinf_engine* e, int seq) {
+    if (!e || !e->impl || seq < 0 || seq >= e->impl->n_seqs) return JINF_ERR_INVALID;
+    if (seq == 0) {
+        jinf_engine_reset(e);
+        return JINF_OK;
+    }
+    e->impl->seq_past[seq] = 0;
+    return JINF_OK;
+}
+
+// One multi-sequence step: the inputs go to the device state in one copy, the step's graph for
+// this vector count runs (captured at its first use), and the argmax ids (and, if asked, the
+// logits) come back. Sequence 0's new position is also written to the one-sequence state.
+extern "C" jinf_status jinf_engine_decode_batch(jinf_engine* e, int n, const int32_t* seqs, const int32_t* tokens,
+                                               int32_t* next_tokens, float* logits) {
+    if (!e || !e->impl || !seqs || !tokens || n < 1) return JINF_ERR_INVALID;
     jinf_engine_impl* I = e->impl;
+    if (!I->ms || n > I->n_seqs || (logits && I->tp_size > 1)) return JINF_ERR_INVALID;
+    int32_t* in = I->ms_pinned;
+    bool has0 = false;
+    for (int i = 0; i < n; ++i) {
+        const int sq = seqs[i];
+        if (sq < 0 || sq >= I->n_seqs || tokens[i] < 0 || tokens[i] >= I->V) return JINF_ERR_INVALID;
+        for (int j = 0; j < i; ++j)
+            if (seqs[j] == sq) return JINF_ERR_INVALID;
+        const int pos = sq == 0 ? e->n_past : I->seq_past[sq];
+        if (pos >= I->max_ctx) {
+            JINF_LOG("context full (%d positions) for sequence %d", I->max_ctx, sq);
+            return JINF_ERR_INVALID;
+        }
+        in[i] = tokens[i];
+        in[MULTI_MAX + i] = pos;
+        in[2 * MULTI_MAX + i] = sq;
+        has0 |= sq == 0;
+    }
     JINF_CUDA_CHECK(cudaSetDevice(I->device));
-    // the cache is [layer][kv head][max_ctx][hd]: one strided copy per cache, rows of n_pos * hd
-    const size_t w = (size_t)n_pos * I->hd * sizeof(__half), pitch = (size_t)I->max_ctx * I->hd * sizeof(__half);
-    const size_t h = (size_t)I->L * I->Hkvl;
-    JINF_CUDA_CHECK(cudaMemcpy2DAsync(k_host, w, I->kc, pitch, w, h, cudaMemcpyDeviceToHost, I->stream));
-    JINF_CUDA_CHECK(cudaMemcpy2DAsync(v_host, w, I->vc, pitch, w, h, cudaMemcpyDeviceToHost, I->stream));
+    if (!I->ev0) {
+        JINF_CUDA_CHECK(cudaEventCreate(&I->ev0));
+        JINF_CUDA_CHECK(cudaEventCreate(&I->ev1));
+    }
+    JINF_CUDA_CHECK(cudaEventRecord(I->ev0, I->stream));
+    JINF_CUDA_CHECK(cudaMemcpyAsync(I->ms, in, sizeof(int32_t) * 3 * MULTI_MAX, cudaMemcpyHostToDevice, I->stream));
+    if (I->m_ops[n].empty()) build_multi_ops(I, n, I->m_ops[n]);
+    if (I->use_graph) {
+        if (!I->m_exec[n]) JINF_CHECK(capture(I, I->m_ops[n], &I->m_exec[n]), "multi-sequence step capture");
+        JINF_CUDA_CHECK(cudaGraphLaunch(I->m_exec[n], I->stream));
+    } else {
+        JINF_CHECK(run_ops(I, I->m_ops[n], I->stream), "multi-sequence step");
+    }
+    JINF_CUDA_CHECK(cudaMemcpyAsync(in + 3 * MULTI_MAX, I->ms->out_token, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+                                    I->stream));
+    if (logits)  // one GPU: the vocabulary is whole, rows [n][n_vocab]
+        JINF_CUDA_CHECK(cudaMemcpyAsync(logits, I->m_logits, sizeof(float) * (size_t)n * I->Vl, cudaMemcpyDeviceToHost,
+                                        I->stream));
+    if (has0) {  // the one-sequence step keeps its position on the device
+        I->pinned[3] = e->n_past + 1;
+        JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->pos, &I->pinned[3], sizeof(int32_t), cudaMemcpyHostToDevice, I->stream));
+    }
+    JINF_CUDA_CHECK(cudaEventRecord(I->ev1, I->stream));
     JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, I->ev0, I->ev1) == cudaSuccess) e->perf.gpu_compute_ms += ms;
+    for (int i = 0; i < n; ++i) {
+        if (seqs[i] == 0) {
+            ++e->n_past;
+            I->logits_valid = false;
+        } else {
+            ++I->seq_past[seqs[i]];
+        }
+        if (next_tokens) next_tokens[i] = in[3 * MULTI_MAX + i];
+    }
+    e->perf.tokens_generated += n;
     return JINF_OK;
 }
 

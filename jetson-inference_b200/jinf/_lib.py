@@ -52,7 +52,8 @@ class EngineConfig(C.Structure):
 class B200Options(C.Structure):
     _fields_ = [("device", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int), ("nccl_id", C.c_void_p),
                 ("kv_type", C.c_int), ("use_graph", C.c_int), ("eos_token", C.c_int), ("sparse_mode", C.c_int),
-                ("sparse_keep", C.c_float), ("sparse_seed", C.c_uint64), ("persistent", C.c_int), ("prefill", C.c_int)]
+                ("sparse_keep", C.c_float), ("sparse_seed", C.c_uint64), ("persistent", C.c_int), ("prefill", C.c_int),
+                ("max_seqs", C.c_int)]
 
 
 class PerfStats(C.Structure):
@@ -160,6 +161,8 @@ SIGNATURES = {
     "jinf_b200_q4m_bytes_qt": (u64, [i32, i32, i32]),
     "jinf_b200_gemv_q4m_batch_workspace_bytes": (sz, [i32, i32, i32]),
     "jinf_b200_gemv_q4m_batch": (i32, [vp, vp, i32, vp, i32, i32, i32, vp, vp]),
+    "jinf_b200_gemv_q4m_batch_workspace_bytes_qt": (sz, [i32, i32, i32, i32]),
+    "jinf_b200_gemv_q4m_batch_qt": (i32, [vp, i32, vp, i32, vp, i32, i32, i32, vp, i32, vp]),
     "jinf_b200_q4m_pack_qt": (i32, [vp, i32, vp, i32, i32, vp]),
     "jinf_b200_gemv_q4m_qt": (i32, [vp, i32, vp, i32, vp, i32, i32, vp, i32, vp]),
     "jinf_b200_gemv_q4m_workspace_bytes": (sz, [i32, i32]),
@@ -230,6 +233,11 @@ SIGNATURES = {
     "jinf_engine_last_argmax": (i32, [C.POINTER(Engine), C.POINTER(C.c_int32)]),
     "jinf_engine_fill_kv_random": (i32, [C.POINTER(Engine), i32, u64]),
     "jinf_engine_kv_read": (i32, [C.POINTER(Engine), i32, vp, vp]),
+    "jinf_engine_decode_batch": (i32, [C.POINTER(Engine), i32, vp, vp, vp, vp]),
+    "jinf_engine_seq_n_past": (i32, [C.POINTER(Engine), i32]),
+    "jinf_engine_seq_reset": (i32, [C.POINTER(Engine), i32]),
+    "jinf_engine_seq_fill_kv_random": (i32, [C.POINTER(Engine), i32, i32, u64]),
+    "jinf_engine_seq_kv_read": (i32, [C.POINTER(Engine), i32, i32, vp, vp]),
     "jinf_engine_is_persistent": (i32, [vp]),
     "jinf_engine_sparse_ids": (i32, [vp, i32, vp, i32, vp]),
     "jinf_engine_count_activations": (i32, [vp, vp, i32, C.c_float, vp]),

@@ -96,6 +96,20 @@ def gemv_q4m_batch(q4m, x, y, rows: int, cols: int, batch: int, workspace=None, 
             "jinf_b200_gemv_q4m_batch")
 
 
+def gemv_q4m_batch_workspace_bytes_qt(rows: int, cols: int, batch: int, qtype: int) -> int:
+    return int(L.lib.jinf_b200_gemv_q4m_batch_workspace_bytes_qt(rows, cols, batch, qtype))
+
+
+def gemv_q4m_batch_qt(q4m, qtype: int, x, y, rows: int, cols: int, batch: int, workspace=None, kw: int = 0,
+                      stream=None) -> None:
+    """Y[b] = W . X[b] over a Q4M image of block type `qtype`; kw = 0 picks the K split."""
+    import torch
+    xt = L.F32 if x.dtype == torch.float32 else L.F16
+    ws = _p(workspace) if workspace is not None else None
+    L.check(L.lib.jinf_b200_gemv_q4m_batch_qt(_p(q4m), qtype, _p(x), xt, _p(y), rows, cols, batch, ws, kw,
+                                              _s(stream)), "jinf_b200_gemv_q4m_batch_qt")
+
+
 def q4m_bytes_qt(rows: int, cols: int, qtype: int) -> int:
     """Q4M image bytes for qtype Q4_0 (2), Q8_0 (8), Q4_K (12) or Q6_K (14); 0 for an
     unsupported type or shape."""

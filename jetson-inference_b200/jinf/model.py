@@ -125,16 +125,18 @@ class SynthModel:
 
 def b200_options(device: int = 0, tp_rank: int = 0, tp_size: int = 1, nccl_id: bytes | None = None,
                  use_graph: bool = True, eos_token: int = 2, persistent: bool = True, sparse_mode: int = 0,
-                 sparse_keep: float = 0.15, sparse_seed: int = 0, prefill: bool = True) -> L.B200Options:
+                 sparse_keep: float = 0.15, sparse_seed: int = 0, prefill: bool = True,
+                 max_seqs: int = 1) -> L.B200Options:
     """sparse_mode: 0 dense FFN, 1 device predictor top-k, 2 fixed mask (runs of 8). prefill:
     forward() of several tokens runs all but the last through the batched (tensor-core) prefill
-    where the model allows it."""
+    where the model allows it. max_seqs: sequences with their own KV cache for decode_batch."""
     o = L.B200Options()
     o.device, o.tp_rank, o.tp_size = device, tp_rank, tp_size
     o.kv_type, o.use_graph, o.eos_token = L.F16, int(use_graph), eos_token
     o.sparse_mode, o.sparse_keep, o.sparse_seed = sparse_mode, sparse_keep, sparse_seed
     o.persistent = int(persistent)
     o.prefill = int(prefill)
+    o.max_seqs = int(max_seqs)
     o._nccl_buf = None
     if nccl_id is not None:
         buf = C.create_string_buffer(bytes(nccl_id), 128)
@@ -258,6 +260,39 @@ class Engine:
         k, v = np.empty(shp, dtype=np.float16), np.empty(shp, dtype=np.float16)
         L.check(L.lib.jinf_engine_kv_read(self.h, n_pos, k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p)),
                 "kv_read")
+        return k, v
+
+    # ---- multi-sequence decode
+
+    def decode_batch(self, seqs, tokens, want_logits: bool = False):
+        """One step of len(seqs) sequences: tokens[i] fed to sequence seqs[i]. Returns the
+        greedy next tokens (and the logits [n][n_vocab] when want_logits)."""
+        n = len(seqs)
+        s = (C.c_int32 * n)(*[int(v) for v in seqs])
+        t = (C.c_int32 * n)(*[int(v) for v in tokens])
+        out = (C.c_int32 * n)()
+        lg = np.empty((n, self.n_vocab), dtype=np.float32) if want_logits else None
+        L.check(L.lib.jinf_engine_decode_batch(self.h, n, s, t, out,
+                                               lg.ctypes.data_as(C.c_void_p) if want_logits else None),
+                "decode_batch")
+        return (list(out), lg) if want_logits else list(out)
+
+    def seq_n_past(self, seq: int) -> int:
+        return int(L.lib.jinf_engine_seq_n_past(self.h, seq))
+
+    def seq_reset(self, seq: int) -> None:
+        L.check(L.lib.jinf_engine_seq_reset(self.h, seq), "seq_reset")
+
+    def seq_fill_kv_random(self, seq: int, n_pos: int, seed: int = 0) -> None:
+        L.check(L.lib.jinf_engine_seq_fill_kv_random(self.h, seq, n_pos, seed), "seq_fill_kv_random")
+
+    def seq_kv_read(self, seq: int, n_pos: int, tp_size: int = 1):
+        e = self.h.contents
+        hkv = e.n_heads_kv // max(1, tp_size)
+        shp = (e.n_layers, hkv, n_pos, e.n_embd // e.n_heads)
+        k, v = np.empty(shp, dtype=np.float16), np.empty(shp, dtype=np.float16)
+        L.check(L.lib.jinf_engine_seq_kv_read(self.h, seq, n_pos, k.ctypes.data_as(C.c_void_p),
+                                              v.ctypes.data_as(C.c_void_p)), "seq_kv_read")
         return k, v
 
     @property

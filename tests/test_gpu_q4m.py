@@ -279,3 +279,57 @@ def test_gemv_q4m_batch(cuda, rows, cols, batch):
         for b in range(min(batch, 2)):
             want = q4m_ref.emulate_gemv(q4m_ref.pack(w, rows, cols), x[b].astype(np.float32), rows, cols)
             assert rel_err(got[b], want) < 1e-5
+
+
+# ---------------------------------------------------------------- multi-vector GEMV, every format
+
+def _typed_rows(qt, rows, cols, seed):
+    from test_q4m_layout import q4_k_rows
+    if qt == 2:
+        return q4_0_rows(rows, cols, seed=seed)
+    if qt == 12:
+        return q4_k_rows(rows, cols, seed=seed)
+    return QT_HELPERS[qt][0](rows, cols, seed=seed)
+
+
+@pytest.mark.parametrize("qt", [2, 12, 14, 8])
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 8), (1024, 8192, 3), (3584, 8192, 8), (8192, 3584, 5),
+                                             (160, 1024, 1), (128256, 4096, 8)])
+def test_gemv_batch_every_format(cuda, qt, rows, cols, batch):
+    """Y[b] = W x[b] through the multi-vector kernel (the engine's multi-sequence GEMV) against
+    the oracle's matvec of each vector, for Q4_0, Q4_K, Q6_K and Q8_0 images; deterministic."""
+    from jinf import kernels as K
+    w = _typed_rows(qt, rows, cols, seed=rows + cols + qt)
+    q = packed_qt(w, qt, rows, cols, cuda) if qt != 12 else packed_k(w, rows, cols, cuda)
+    x = np.random.default_rng(batch + qt).standard_normal((batch, cols)).astype(np.float32)
+    ws = torch.zeros(K.gemv_q4m_batch_workspace_bytes_qt(rows, cols, batch, qt), dtype=torch.uint8, device=cuda)
+    xd = torch.from_numpy(x).to(cuda)
+    y = torch.empty((batch, rows), dtype=torch.float32, device=cuda)
+    y2 = torch.empty_like(y)
+    K.gemv_q4m_batch_qt(q, qt, xd, y, rows, cols, batch, workspace=ws)
+    K.gemv_q4m_batch_qt(q, qt, xd, y2, rows, cols, batch, workspace=ws)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    for b in range(batch):
+        assert rel_err(got[b], oracle.matvec(w, qt, x[b], rows, cols)) < REL, f"vector {b}"
+    assert torch.equal(y, y2)
+
+
+@pytest.mark.parametrize("qt", [2, 12, 14, 8])
+@pytest.mark.parametrize("kw", [1, 2, 5, 16])
+def test_gemv_batch_every_k_split(cuda, qt, kw):
+    """Every forced K split gives the same vectors (to the oracle bar) and matches kw = 1 to
+    fp32 summation order."""
+    from jinf import kernels as K
+    rows, cols, batch = 1024, 4096, 8
+    w = _typed_rows(qt, rows, cols, seed=7 * kw + qt)
+    q = packed_qt(w, qt, rows, cols, cuda) if qt != 12 else packed_k(w, rows, cols, cuda)
+    x = np.random.default_rng(kw).standard_normal((batch, cols)).astype(np.float32)
+    xd = torch.from_numpy(x).to(cuda)
+    ws = torch.zeros(K.gemv_q4m_batch_workspace_bytes_qt(rows, cols, batch, qt), dtype=torch.uint8, device=cuda)
+    y = torch.empty((batch, rows), dtype=torch.float32, device=cuda)
+    K.gemv_q4m_batch_qt(q, qt, xd, y, rows, cols, batch, workspace=ws, kw=kw)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    for b in range(batch):
+        assert rel_err(got[b], oracle.matvec(w, qt, x[b], rows, cols)) < REL, f"vector {b}"
