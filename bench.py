@@ -21,6 +21,9 @@ reference src/engine.cpp:684-804), after a 512-token prompt: positions 512+W .. 
          the seeded generator, so that arm loads no B200 code.
 Under torchrun (N > 1) the model is tensor parallel over the ranks (NCCL allreduce inside
 the captured step). --impl reference times the CPU implementation of the path.
+--batch B (config C5's batch 8) decodes B sequences per step (jinf_engine_decode_batch: every
+projection's weights streamed once for all B, each sequence with its own KV cache, filled with
+seeded values to the first decode position); value and e2e count the tokens of all B.
 Weights are synthetic N(0, 0.02) Q4_0 from seed 0 (no checkpoints): data "synthetic".
 """
 from __future__ import annotations
@@ -191,10 +194,13 @@ def bench_config(args, world):
     shape = shape_for(args.config)
     wbytes = weight_bytes(shape, args.config)
     p0 = start_pos(args)
-    kv = "" if p0 == PROMPT else f", KV cache filled to {p0} positions"
-    return {"workload": f"{args.config} greedy decode batch 1, prompt {PROMPT}{kv}, positions "
+    if args.batch > 1:
+        kv = f", {args.batch} sequences, each KV cache filled with seeded values to {p0} positions"
+    else:
+        kv = "" if p0 == PROMPT else f", KV cache filled to {p0} positions"
+    return {"workload": f"{args.config} greedy decode batch {args.batch}, prompt {PROMPT}{kv}, positions "
                         f"{p0 + args.warmup}..{p0 + args.warmup + args.steps - 1}",
-            "model": f"llama3-{args.config}-shape", "global_batch": 1, "seq_len": p0 + args.steps,
+            "model": f"llama3-{args.config}-shape", "global_batch": args.batch, "seq_len": p0 + args.steps,
             "parallelism": f"tp{world}",
             "ffn": ["dense", "sparse: device predictor top-k 15%", "sparse: fixed mask 15% (runs of 8)"][args.sparse],
             "l2": f"{wbytes / 1e9:.2f} GB of weights streamed per step >> 126 MB L2 (no flush needed)"}
@@ -507,6 +513,104 @@ def run_ours(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_ours_batch(args, rank, world, local):
+    """--batch B: B sequences per step through the multi-sequence decode."""
+    import torch
+    import jinf
+
+    dist = init_dist(world)
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    shape = shape_for(args.config)
+    peak, peak_kind = peaks()
+    B = args.batch
+    nccl_id = None
+    if world > 1:
+        buf = [jinf.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(buf, src=0)
+        nccl_id = buf[0]
+    t_load = time.perf_counter()
+    syn = jinf.SynthModel(shape.llama(), seed=0, weight_type=wtype_for(args.config), mix_type=mix_for(args.config))
+    p0 = start_pos(args)
+    max_ctx = p0 + args.warmup + args.steps + 8
+    opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
+                             max_seqs=B)
+    eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=opts)
+    t_load = time.perf_counter() - t_load
+    stream = torch.cuda.ExternalStream(eng.h.contents.compute_stream, device=dev)
+    seqs = list(range(B))
+    first = prompt_ids(shape.n_vocab, n=B)
+
+    def fill():
+        for s in seqs:
+            eng.seq_fill_kv_random(s, p0, seed=1 + s)
+
+    # ---- value: resident steps (argmax fed back on the device), K steps timed on the device
+    fill()
+    eng.decode_batch_resident(seqs, first, args.warmup)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        eng.decode_batch_resident(seqs, first, args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    dev_s = all_max(dist, e0.elapsed_time(e1) / 1000.0)
+    value = B * args.steps / dev_s
+
+    # ---- e2e: the same window through jinf_engine_decode_batch, host buffers every step
+    fill()
+    toks = first
+    for _ in range(args.warmup):
+        toks = eng.decode_batch(seqs, toks)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        toks = eng.decode_batch(seqs, toks)
+    t1 = time.perf_counter()
+    if dist:
+        dist.barrier()
+    e2e = B * args.steps / all_max(dist, t1 - t0)
+
+    wbytes = eng.weight_bytes_per_token()
+    kv_seq = 2 * 2 * shape.n_layers * (shape.n_heads_kv // world) * shape.head_dim * (p0 + args.warmup + args.steps / 2)
+    step_bytes = wbytes + B * kv_seq
+    step_gbs = step_bytes / (dev_s / args.steps) / 1e9
+    launches = 1 + 5 * shape.n_layers + 2 + (2 * shape.n_layers if world > 1 else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * dev_s / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": f"{wname_for(args.config)} weights, f32 activations, f16 KV",
+            "data": f"synthetic (seeded N(0,0.02) {wname_for(args.config).upper()} weights, seeded N(0,1) KV)",
+            "config": bench_config(args, world),
+            # per step: the 8-slot token / position / sequence arrays and sequence 0's position in,
+            # one argmax id per sequence out
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 3 * 8 * 4 + 4,
+                    "d2h_bytes_per_step": 4 * B},
+            "gpu_launches": launches * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "multi-sequence step (k_gemv_multi + k_attn_f16 graph)",
+                         "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                         "bytes_per_step": int(step_bytes), "us_per_step": round(1e6 * dev_s / args.steps, 2),
+                         "note": "weights once per step + every sequence's KV rows"},
+            "clocks": clk.summary(),
+            "load_s": round(t_load, 1),
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def profile_case(steps: int) -> None:
     """The small case of the persistent step for ncu captures: ~0.6 GB of weights plus a
     0.5 GB embedding table; with a 3-token prompt the captured launch `-s 3 -c 1` is the
@@ -538,6 +642,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=PROMPT,
                     help="first decode position: the KV cache is filled with seeded values up to it after the prompt "
                          "(config C5: 8192)")
+    ap.add_argument("--batch", type=int, default=1, choices=range(1, 9), metavar="B",
+                    help="sequences decoded per step (1..8; config C5: 8)")
     ap.add_argument("--sparse", type=int, default=0, choices=[0, 1, 2],
                     help="FFN: 0 dense, 1 device predictor top-k, 2 fixed mask (BASELINE config C4)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",
@@ -553,6 +659,11 @@ def main():
     rank, world, local = dist_env()
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.batch > 1:
+        if args.sparse:
+            ap.error("--batch needs the dense FFN")
+        run_ours_batch(args, rank, world, local)
         return
     run_ours(args, rank, world, local)
 

@@ -211,6 +211,12 @@ jinf_status jinf_engine_profile_kernels(jinf_engine* e, int reps, double* times_
 // way, one token per call (its argmax ignored).
 jinf_status jinf_engine_decode_batch(jinf_engine* e, int n, const int32_t* seqs, const int32_t* tokens,
                                      int32_t* next_tokens, float* logits);
+// n_steps greedy steps of the same n sequences without host round trips: step 0 feeds tokens,
+// every later step the previous step's argmax of each sequence (fed back on the device).
+// out_tokens (host, may be NULL) receives the ids [n_steps][n]. Used to measure resident
+// multi-sequence throughput.
+jinf_status jinf_engine_decode_batch_resident(jinf_engine* e, int n, const int32_t* seqs, const int32_t* tokens,
+                                              int n_steps, int32_t* out_tokens);
 // Tokens in the KV cache of sequence `seq` (-1 for an invalid sequence).
 int         jinf_engine_seq_n_past(const jinf_engine* e, int seq);
 // Forget sequence `seq` (its position returns to 0).

@@ -456,6 +456,7 @@ struct jinf_engine_impl {
     float *m_h = nullptr, *m_y = nullptr, *m_q = nullptr, *m_attn = nullptr, *m_act = nullptr, *m_logits = nullptr,
           *m_ssq = nullptr, *m_attn_part = nullptr, *m_part = nullptr;
     unsigned int* m_cnt = nullptr;
+    int32_t* m_out = nullptr;  // [max_ctx][MULTI_MAX] argmax ids of resident multi steps
     int m_split = 1;  // attention splits of a multi step
     std::vector<Op> m_ops[MULTI_MAX + 1];
     cudaGraphExec_t m_exec[MULTI_MAX + 1] = {};
@@ -1397,7 +1398,7 @@ void free_impl(jinf_engine_impl* I) {
                     I->pf_att, I->pf_sc, I->pf_x16, I->pf_q16, I->pf_err, I->bundles, I->pred_w1,
                     I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp,
                     I->ms, I->m_h, I->m_y, I->m_q, I->m_attn, I->m_act, I->m_logits, I->m_ssq, I->m_attn_part,
-                    I->m_part, I->m_cnt};
+                    I->m_part, I->m_cnt, I->m_out};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);
@@ -1887,7 +1888,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
                    cudaMalloc(&I->m_ssq, sizeof(float) * (size_t)S * (d / 32)) == cudaSuccess &&
                    cudaMalloc(&I->m_attn_part, sizeof(float) * attn_part) == cudaSuccess &&
                    cudaMalloc(&I->m_part, sizeof(float) * std::max(ws, (size_t)1)) == cudaSuccess &&
-                   cudaMalloc(&I->m_cnt, sizeof(unsigned int) * std::max(pairs, (size_t)1)) == cudaSuccess;
+                   cudaMalloc(&I->m_cnt, sizeof(unsigned int) * std::max(pairs, (size_t)1)) == cudaSuccess &&
+                   cudaMalloc(&I->m_out, sizeof(int32_t) * (size_t)I->max_ctx * MULTI_MAX) == cudaSuccess;
         if (!mok) return fail(JINF_ERR_OOM);
         cudaMemset(I->ms, 0, sizeof(MultiState));
         cudaMemset(I->m_cnt, 0, sizeof(unsigned int) * std::max(pairs, (size_t)1));
@@ -2294,38 +2296,35 @@ extern "C" jinf_status jinf_engine_seq_reset(jinf_engine* e, int seq) {
     return JINF_OK;
 }
 
-// One multi-sequence step: the inputs go to the device state in one copy, the step's graph for
-// this vector count runs (captured at its first use), and the argmax ids (and, if asked, the
-// logits) come back. Sequence 0's new position is also written to the one-sequence state.
-extern "C" jinf_status jinf_engine_decode_batch(jinf_engine* e, int n, const int32_t* seqs, const int32_t* tokens,
-                                               int32_t* next_tokens, float* logits) {
-    if (!e || !e->impl || !seqs || !tokens || n < 1) return JINF_ERR_INVALID;
+namespace {
+
+// Validate a multi-sequence call and stage its inputs (tokens, positions, sequences) in the
+// pinned buffer; n_steps positions must fit in every sequence's cache.
+jinf_status multi_inputs(jinf_engine* e, int n, const int32_t* seqs, const int32_t* tokens, int n_steps, bool* has0) {
     jinf_engine_impl* I = e->impl;
-    if (!I->ms || n > I->n_seqs || (logits && I->tp_size > 1)) return JINF_ERR_INVALID;
+    if (!I->ms || n < 1 || n > I->n_seqs || n_steps < 1) return JINF_ERR_INVALID;
     int32_t* in = I->ms_pinned;
-    bool has0 = false;
+    *has0 = false;
     for (int i = 0; i < n; ++i) {
         const int sq = seqs[i];
         if (sq < 0 || sq >= I->n_seqs || tokens[i] < 0 || tokens[i] >= I->V) return JINF_ERR_INVALID;
         for (int j = 0; j < i; ++j)
             if (seqs[j] == sq) return JINF_ERR_INVALID;
         const int pos = sq == 0 ? e->n_past : I->seq_past[sq];
-        if (pos >= I->max_ctx) {
+        if (pos + n_steps > I->max_ctx) {
             JINF_LOG("context full (%d positions) for sequence %d", I->max_ctx, sq);
             return JINF_ERR_INVALID;
         }
         in[i] = tokens[i];
         in[MULTI_MAX + i] = pos;
         in[2 * MULTI_MAX + i] = sq;
-        has0 |= sq == 0;
+        *has0 |= sq == 0;
     }
-    JINF_CUDA_CHECK(cudaSetDevice(I->device));
-    if (!I->ev0) {
-        JINF_CUDA_CHECK(cudaEventCreate(&I->ev0));
-        JINF_CUDA_CHECK(cudaEventCreate(&I->ev1));
-    }
-    JINF_CUDA_CHECK(cudaEventRecord(I->ev0, I->stream));
-    JINF_CUDA_CHECK(cudaMemcpyAsync(I->ms, in, sizeof(int32_t) * 3 * MULTI_MAX, cudaMemcpyHostToDevice, I->stream));
+    return JINF_OK;
+}
+
+// The graph of an n-vector step (captured at its first use) on the engine's stream.
+jinf_status multi_launch(jinf_engine_impl* I, int n) {
     if (I->m_ops[n].empty()) build_multi_ops(I, n, I->m_ops[n]);
     if (I->use_graph) {
         if (!I->m_exec[n]) JINF_CHECK(capture(I, I->m_ops[n], &I->m_exec[n]), "multi-sequence step capture");
@@ -2333,13 +2332,14 @@ extern "C" jinf_status jinf_engine_decode_batch(jinf_engine* e, int n, const int
     } else {
         JINF_CHECK(run_ops(I, I->m_ops[n], I->stream), "multi-sequence step");
     }
-    JINF_CUDA_CHECK(cudaMemcpyAsync(in + 3 * MULTI_MAX, I->ms->out_token, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
-                                    I->stream));
-    if (logits)  // one GPU: the vocabulary is whole, rows [n][n_vocab]
-        JINF_CUDA_CHECK(cudaMemcpyAsync(logits, I->m_logits, sizeof(float) * (size_t)n * I->Vl, cudaMemcpyDeviceToHost,
-                                        I->stream));
-    if (has0) {  // the one-sequence step keeps its position on the device
-        I->pinned[3] = e->n_past + 1;
+    return JINF_OK;
+}
+
+// After n_steps steps: positions advance; sequence 0's also on the one-sequence device state.
+jinf_status multi_advance(jinf_engine* e, int n, const int32_t* seqs, int n_steps, bool has0) {
+    jinf_engine_impl* I = e->impl;
+    if (has0) {
+        I->pinned[3] = e->n_past + n_steps;
         JINF_CUDA_CHECK(cudaMemcpyAsync(&I->st->pos, &I->pinned[3], sizeof(int32_t), cudaMemcpyHostToDevice, I->stream));
     }
     JINF_CUDA_CHECK(cudaEventRecord(I->ev1, I->stream));
@@ -2348,14 +2348,73 @@ extern "C" jinf_status jinf_engine_decode_batch(jinf_engine* e, int n, const int
     if (cudaEventElapsedTime(&ms, I->ev0, I->ev1) == cudaSuccess) e->perf.gpu_compute_ms += ms;
     for (int i = 0; i < n; ++i) {
         if (seqs[i] == 0) {
-            ++e->n_past;
+            e->n_past += n_steps;
             I->logits_valid = false;
         } else {
-            ++I->seq_past[seqs[i]];
+            I->seq_past[seqs[i]] += n_steps;
         }
-        if (next_tokens) next_tokens[i] = in[3 * MULTI_MAX + i];
     }
-    e->perf.tokens_generated += n;
+    e->perf.tokens_generated += n * n_steps;
+    return JINF_OK;
+}
+
+}  // namespace
+
+// One multi-sequence step: the inputs go to the device state in one copy, the step's graph for
+// this vector count runs, and the argmax ids (and, if asked, the logits) come back. Sequence
+// 0's new position is also written to the one-sequence state.
+extern "C" jinf_status jinf_engine_decode_batch(jinf_engine* e, int n, const int32_t* seqs, const int32_t* tokens,
+                                               int32_t* next_tokens, float* logits) {
+    if (!e || !e->impl || !seqs || !tokens) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    if (logits && I->tp_size > 1) return JINF_ERR_INVALID;
+    bool has0 = false;
+    JINF_CHECK(multi_inputs(e, n, seqs, tokens, 1, &has0), "decode_batch arguments");
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    int32_t* in = I->ms_pinned;
+    JINF_CUDA_CHECK(cudaEventRecord(I->ev0, I->stream));
+    JINF_CUDA_CHECK(cudaMemcpyAsync(I->ms, in, sizeof(int32_t) * 3 * MULTI_MAX, cudaMemcpyHostToDevice, I->stream));
+    JINF_CHECK(multi_launch(I, n), "decode_batch");
+    JINF_CUDA_CHECK(cudaMemcpyAsync(in + 3 * MULTI_MAX, I->ms->out_token, sizeof(int32_t) * n, cudaMemcpyDeviceToHost,
+                                    I->stream));
+    if (logits)  // one GPU: the vocabulary is whole, rows [n][n_vocab]
+        JINF_CUDA_CHECK(cudaMemcpyAsync(logits, I->m_logits, sizeof(float) * (size_t)n * I->Vl, cudaMemcpyDeviceToHost,
+                                        I->stream));
+    JINF_CHECK(multi_advance(e, n, seqs, 1, has0), "decode_batch");
+    if (next_tokens)
+        for (int i = 0; i < n; ++i) next_tokens[i] = in[3 * MULTI_MAX + i];
+    return JINF_OK;
+}
+
+// n_steps multi-sequence steps back to back with the argmax fed back on the device: the
+// host copies the inputs once and, at the end, the ids of every step.
+extern "C" jinf_status jinf_engine_decode_batch_resident(jinf_engine* e, int n, const int32_t* seqs,
+                                                        const int32_t* tokens, int n_steps, int32_t* out_tokens) {
+    if (!e || !e->impl || !seqs || !tokens) return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    bool has0 = false;
+    JINF_CHECK(multi_inputs(e, n, seqs, tokens, n_steps, &has0), "decode_batch_resident arguments");
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    int32_t* in = I->ms_pinned;
+    in[3 * MULTI_MAX] = 1;  // feedback on (the word after the three input arrays)
+    JINF_CUDA_CHECK(cudaEventRecord(I->ev0, I->stream));
+    JINF_CUDA_CHECK(cudaMemcpyAsync(I->ms, in, sizeof(int32_t) * (3 * MULTI_MAX + 1), cudaMemcpyHostToDevice, I->stream));
+    for (int t = 0; t < n_steps; ++t) {
+        JINF_CHECK(multi_launch(I, n), "decode_batch_resident");
+        if (out_tokens)
+            JINF_CUDA_CHECK(cudaMemcpyAsync(I->m_out + (size_t)t * MULTI_MAX, I->ms->out_token, sizeof(int32_t) * n,
+                                            cudaMemcpyDeviceToDevice, I->stream));
+    }
+    in[3 * MULTI_MAX] = 0;
+    JINF_CUDA_CHECK(cudaMemcpyAsync(&I->ms->feedback, in + 3 * MULTI_MAX, sizeof(int32_t), cudaMemcpyHostToDevice,
+                                    I->stream));
+    JINF_CHECK(multi_advance(e, n, seqs, n_steps, has0), "decode_batch_resident");
+    if (out_tokens) {
+        std::vector<int32_t> buf((size_t)n_steps * MULTI_MAX);
+        JINF_CUDA_CHECK(cudaMemcpy(buf.data(), I->m_out, sizeof(int32_t) * buf.size(), cudaMemcpyDeviceToHost));
+        for (int t = 0; t < n_steps; ++t)
+            for (int i = 0; i < n; ++i) out_tokens[(size_t)t * n + i] = buf[(size_t)t * MULTI_MAX + i];
+    }
     return JINF_OK;
 }
 

@@ -540,8 +540,13 @@ __global__ void k_multi_finalize(MultiState* ms, int n) {
     const int v = threadIdx.x;
     if (v >= n) return;
     const u64 key = ms->best[v];
-    ms->out_token[v] = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
+    const int tok = key ? (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull)) : 0;
+    ms->out_token[v] = tok;
     ms->best[v] = 0ull;
+    if (ms->feedback) {
+        ms->token[v] = tok;
+        ms->pos[v] += 1;
+    }
 }
 
 cudaError_t launch_rows(const float* table, const MultiState* ms, float* h, const float* y, int n, int d, float* ssq,

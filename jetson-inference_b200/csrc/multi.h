@@ -22,6 +22,8 @@ struct MultiState {
     int token[MULTI_MAX];  // input token of vector v
     int pos[MULTI_MAX];    // its position (the sequence's n_past)
     int seq[MULTI_MAX];    // its sequence (KV cache slot)
+    int feedback;          // 1: the finaliser feeds each argmax back as the vector's next token
+                           // and advances its position (resident decode, no host round trip)
     int out_token[MULTI_MAX];           // greedy argmax of the step (first maximum wins)
     unsigned long long best[MULTI_MAX];  // packed argmax keys of the LM head (reset by the finaliser)
     unsigned int attn_count[MULTI_MAX * MULTI_MAX_KV_HEADS];  // attention split arrivals (self-resetting)
@@ -79,7 +81,8 @@ cudaError_t multi_embed_launch(const float* table, const MultiState* ms, int n, 
 // h[v] += y[v] and the new sums of squares per 32 elements (tensor parallel: after the
 // allreduce of the row-split partial outputs).
 cudaError_t multi_resid_launch(float* h, const float* y, int n, int d, float* ssq, cudaStream_t s, bool pdl);
-// out_token[v] from the argmax keys, which are reset for the next step.
+// out_token[v] from the argmax keys, which are reset for the next step (and, with feedback,
+// fed back as the next step's tokens, positions advanced).
 cudaError_t multi_finalize_launch(MultiState* ms, int n, cudaStream_t s);
 
 }  // namespace jinf

@@ -234,6 +234,7 @@ SIGNATURES = {
     "jinf_engine_fill_kv_random": (i32, [C.POINTER(Engine), i32, u64]),
     "jinf_engine_kv_read": (i32, [C.POINTER(Engine), i32, vp, vp]),
     "jinf_engine_decode_batch": (i32, [C.POINTER(Engine), i32, vp, vp, vp, vp]),
+    "jinf_engine_decode_batch_resident": (i32, [C.POINTER(Engine), i32, vp, vp, i32, vp]),
     "jinf_engine_seq_n_past": (i32, [C.POINTER(Engine), i32]),
     "jinf_engine_seq_reset": (i32, [C.POINTER(Engine), i32]),
     "jinf_engine_seq_fill_kv_random": (i32, [C.POINTER(Engine), i32, i32, u64]),

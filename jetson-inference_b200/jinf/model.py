@@ -277,6 +277,16 @@ class Engine:
                 "decode_batch")
         return (list(out), lg) if want_logits else list(out)
 
+    def decode_batch_resident(self, seqs, tokens, n_steps: int, collect: bool = False):
+        """n_steps greedy steps of the sequences, argmax fed back on the device; returns the
+        ids [n_steps][len(seqs)] when collect."""
+        n = len(seqs)
+        s = (C.c_int32 * n)(*[int(v) for v in seqs])
+        t = (C.c_int32 * n)(*[int(v) for v in tokens])
+        out = (C.c_int32 * (n * n_steps))() if collect else None
+        L.check(L.lib.jinf_engine_decode_batch_resident(self.h, n, s, t, n_steps, out), "decode_batch_resident")
+        return [list(out[i * n:(i + 1) * n]) for i in range(n_steps)] if collect else None
+
     def seq_n_past(self, seq: int) -> int:
         return int(L.lib.jinf_engine_seq_n_past(self.h, seq))
 

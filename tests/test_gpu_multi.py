@@ -171,3 +171,27 @@ def test_decode_batch_rejects_bad_arguments(cuda):
     assert eng.seq_n_past(1) == 0
     eng.decode_batch([1], [5])
     eng.close()
+
+
+def test_resident_matches_host_fed_steps(cuda):
+    """decode_batch_resident (argmax fed back on the device) gives the tokens that host-fed
+    decode_batch steps give, and leaves the same positions."""
+    import jinf
+    shape = jinf.LlamaShape(2, 512, 8, 2, 1408, 4096, 1e4)
+    syn = jinf.SynthModel(shape, seed=5)
+    seqs = [3, 0, 1]
+    a = jinf.Engine.from_synth(syn, max_context=64, options=jinf.b200_options(eos_token=-1, max_seqs=4))
+    b = jinf.Engine.from_synth(syn, max_context=64, options=jinf.b200_options(eos_token=-1, max_seqs=4))
+    for eng in (a, b):
+        for s in seqs:
+            eng.seq_fill_kv_random(s, 10 + s, seed=s)
+    first = [7, 99, 2048]
+    got = a.decode_batch_resident(seqs, first, 20, collect=True)
+    toks, want = first, []
+    for _ in range(20):
+        toks = b.decode_batch(seqs, toks)
+        want.append(toks)
+    assert got == want
+    assert [a.seq_n_past(s) for s in seqs] == [b.seq_n_past(s) for s in seqs] == [10 + s + 20 for s in seqs]
+    a.close()
+    b.close()
