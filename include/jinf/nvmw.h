@@ -126,6 +126,10 @@ jinf_status jinf_prepare_model(const char* gguf_path, const char* nvmw_path, siz
 // engine copies it into HBM without repacking; the embedding and norms as in the GGUF. New:
 // no counterpart in the reference.
 jinf_status jinf_prepare_model_b200(const char* gguf_path, const char* nvmw_path);
+// The same for tensor parallelism over tp_size GPUs (1, 2, 4 or 8): every rank's shard of
+// every projection as an image of its own, named "tp<tp_size>.<rank>." + the one-GPU name;
+// an engine created with that tp_size reads its rank's images.
+jinf_status jinf_prepare_model_b200_tp(const char* gguf_path, const char* nvmw_path, int tp_size);
 jinf_status jinf_nvmw_writer_write_bundle_section(jinf_nvmw_writer* w,
                                                   const jinf_nvmw_bundle_header* bh,
                                                   const jinf_nvmw_bundle_layer_desc* layer_descs,

@@ -83,6 +83,9 @@ struct ModelSource {
     // B200-layout files (NVMW version 3): the projections are stored as the engine's Q4M
     // images; read_packed copies one into device memory (exactly `bytes` long).
     virtual bool prepacked() const { return false; }
+    // Select the images of tensor-parallel rank `rank` of `size` in a pre-packed file; false
+    // when the file holds none for that split.
+    virtual bool select_shard(int, int) const { return false; }
     virtual jinf_status read_packed(const char*, uint8_t*, uint64_t) const { return JINF_ERR_INVALID; }
     jinf_model_hparams hp{};
     int primary_type = JINF_TYPE_Q4_0;
@@ -140,7 +143,12 @@ struct NvmwSource : ModelSource {
         if (r) jinf_nvmw_close(r);
     }
     bool b200 = false;  // version 3: pre-packed projections
+    mutable std::string pfx;  // "tp<size>.<rank>." when a tensor-parallel rank reads its images
     bool prepacked() const override { return b200; }
+    bool select_shard(int rank, int size) const override {
+        pfx = size > 1 ? "tp" + std::to_string(size) + "." + std::to_string(rank) + "." : "";
+        return b200 && jinf_nvmw_find_tensor(r, (pfx + "output.q4m").c_str()) != nullptr;
+    }
     // In a B200-layout file a projection's type is that of the Q4M image that holds it.
     const jinf_nvmw_tensor_entry* packed_entry_for(const char* name) const {
         int l = -1;
@@ -157,7 +165,7 @@ struct NvmwSource : ModelSource {
         } else if (!strcmp(name, "output.weight")) {
             img = "output.q4m";
         }
-        return img.empty() ? nullptr : jinf_nvmw_find_tensor(r, img.c_str());
+        return img.empty() ? nullptr : jinf_nvmw_find_tensor(r, (pfx + img).c_str());
     }
     bool meta(const char* name, TensorMeta* t) const override {
         const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, name);
@@ -178,7 +186,7 @@ struct NvmwSource : ModelSource {
         return true;
     }
     jinf_status read_packed(const char* name, uint8_t* dst_dev, uint64_t bytes) const override {
-        const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, name);
+        const jinf_nvmw_tensor_entry* te = jinf_nvmw_find_tensor(r, (pfx + name).c_str());
         if (!te || (int)te->type < JINF_NVMW_TYPE_Q4M || te->n_bytes != bytes) {
             JINF_LOG("tensor %s: no pre-packed image of %llu bytes in this file", name, (unsigned long long)bytes);
             return JINF_ERR_INVALID;
@@ -1468,6 +1476,11 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     // matrices are all Q4_0 or all Q4_K; others run one kernel per operation.
     std::vector<std::array<int, 5>> lfmt((size_t)I->L);  // per layer: q|k, v, o, gate|up, down
     int lm_fmt = -1;
+    // a pre-packed file: this rank's images (a tensor-parallel file holds one set per rank)
+    if (src.prepacked() && tp > 1 && !src.select_shard(opt.tp_rank, tp)) {
+        JINF_LOG("this B200-layout model file holds no images for %d GPUs (jinf_prepare_model_b200_tp)", tp);
+        return fail(JINF_ERR_INVALID);
+    }
     {
         TensorMeta m;
         if (src.meta("blk.0.attn_q.weight", &m)) I->wtype = m.type;
@@ -1509,8 +1522,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         I->uniform = I->uniform && (lm_fmt == Q4M_Q4_0 || lm_fmt == Q4M_Q4_K);
         I->wfmt = I->uniform ? lm_fmt : Q4M_MIX;
         if (I->uniform) I->wtype = lm_fmt == Q4M_Q4_K ? JINF_TYPE_Q4_K : JINF_TYPE_Q4_0;
-        if (src.prepacked() && (tp > 1 || opt.sparse_mode)) {
-            JINF_LOG("a B200-layout model file is prepared for one GPU and the dense FFN");
+        if (src.prepacked() && opt.sparse_mode) {
+            JINF_LOG("a B200-layout model file is prepared for the dense FFN");
             return fail(JINF_ERR_INVALID);
         }
         if (!I->uniform && opt.sparse_mode) {

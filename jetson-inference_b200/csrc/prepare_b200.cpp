@@ -10,12 +10,17 @@
 // embedding table and the norm gains are copied as they are. Everything lies in the hot
 // region (on B200 the whole model is in HBM), 4 KB aligned; the cold regions are empty.
 // The engine copies each image into its arena without staging or repacking. The file is
-// prepared for one GPU and the dense FFN.
+// prepared for the dense FFN and for one GPU, or (jinf_prepare_model_b200_tp) for tensor
+// parallelism over tp_size GPUs: then every rank r has its own images, named
+// "tp<size>.<r>." + the one-GPU name, each the rank's slice in the engine's split
+// (jinf_tp_shard: q, k, v, gate, up and the output head by rows, o and down by whole column
+// blocks), so a rank reads exactly its shard.
 #include "jinf/b200.h"
 #include "jinf/common.h"
 #include "jinf/gguf.h"
 #include "jinf/nvmw.h"
 #include "jinf/quant.h"
+#include "jinf/splitter.h"
 
 #include <stdio.h>
 #include <string.h>
@@ -31,6 +36,7 @@ struct Item {
     // a copied tensor (src) or a packed matrix assembled from up to 3 sources
     const jinf_gguf_tensor_info* src = nullptr;
     const jinf_gguf_tensor_info* parts[3] = {nullptr, nullptr, nullptr};
+    int64_t r0[3] = {0, 0, 0}, nr[3] = {0, 0, 0}, c0[3] = {0, 0, 0};  // each part's slice (rows, first column)
     bool interleave = false;  // gate|up: rows alternate parts[0], parts[1]
     int qtype = 0;
     int64_t rows = 0, cols = 0;
@@ -49,8 +55,9 @@ bool read_at(FILE* in, uint64_t off, void* dst, size_t n) {
 
 }  // namespace
 
-extern "C" jinf_status jinf_prepare_model_b200(const char* gguf_path, const char* nvmw_path) {
-    if (!gguf_path || !nvmw_path) return JINF_ERR_INVALID;
+extern "C" jinf_status jinf_prepare_model_b200_tp(const char* gguf_path, const char* nvmw_path, int tp_size) {
+    if (!gguf_path || !nvmw_path || (tp_size != 1 && tp_size != 2 && tp_size != 4 && tp_size != 8))
+        return JINF_ERR_INVALID;
     jinf_gguf_file* g = nullptr;
     JINF_CHECK(jinf_gguf_open(&g, gguf_path), "gguf");
     const jinf_model_hparams hp = g->hparams;
@@ -71,24 +78,37 @@ extern "C" jinf_status jinf_prepare_model_b200(const char* gguf_path, const char
         it.bytes = t->n_bytes;
         items.push_back(it);
     };
+    // one image per rank: the fused slices of the sources
     auto packed_item = [&](const std::string& name, int layer, std::vector<std::string> srcs, bool interleave) {
-        Item it;
-        it.name = name;
-        it.layer = layer;
-        it.interleave = interleave;
-        for (size_t i = 0; i < srcs.size(); ++i) {
-            const jinf_gguf_tensor_info* t = find(g, srcs[i]);
-            if (!t || t->n_dims != 2) return fail("matrix missing", srcs[i]);
-            if (i > 0 && (t->type != it.parts[0]->type || t->shape[0] != it.parts[0]->shape[0]))
-                return fail("fused matrices of different types or widths", srcs[i]);
-            it.parts[i] = t;
-            it.rows += t->shape[1];
+        for (int rank = 0; rank < tp_size && st == JINF_OK; ++rank) {
+            Item it;
+            it.name = tp_size == 1 ? name : "tp" + std::to_string(tp_size) + "." + std::to_string(rank) + "." + name;
+            it.layer = layer;
+            it.interleave = interleave;
+            for (size_t i = 0; i < srcs.size(); ++i) {
+                const jinf_gguf_tensor_info* t = find(g, srcs[i]);
+                if (!t || t->n_dims != 2) return fail("matrix missing", srcs[i]);
+                if (i > 0 && (t->type != it.parts[0]->type || t->shape[0] != it.parts[0]->shape[0]))
+                    return fail("fused matrices of different types or widths", srcs[i]);
+                int64_t r0, nr, c0, nc;
+                if (jinf_tp_shard(srcs[i].c_str(), t->shape[1], t->shape[0], rank, tp_size, &r0, &nr, &c0, &nc) !=
+                    JINF_OK)
+                    return fail("no tensor-parallel split of this shape", srcs[i]);
+                if (c0 % jinf_qtype_block_size(t->type) || nc % jinf_qtype_block_size(t->type))
+                    return fail("column split inside a block", srcs[i]);
+                if (i > 0 && nc != it.cols) return fail("fused matrices split to different widths", srcs[i]);
+                it.parts[i] = t;
+                it.r0[i] = r0;
+                it.nr[i] = nr;
+                it.c0[i] = c0;
+                it.cols = nc;
+                it.rows += nr;
+            }
+            it.qtype = it.parts[0]->type;
+            it.bytes = jinf_b200_q4m_bytes_qt((int)it.rows, (int)it.cols, it.qtype);
+            if (!it.bytes) return fail("no Q4M form for this type or width", it.name);
+            items.push_back(it);
         }
-        it.qtype = it.parts[0]->type;
-        it.cols = it.parts[0]->shape[0];
-        it.bytes = jinf_b200_q4m_bytes_qt((int)it.rows, (int)it.cols, it.qtype);
-        if (!it.bytes) return fail("no Q4M form for this type or width", name);
-        items.push_back(it);
     };
     copy_item("token_embd.weight", -1);
     char b[160];
@@ -201,21 +221,27 @@ extern "C" jinf_status jinf_prepare_model_b200(const char* gguf_path, const char
             img.assign(JINF_ALIGN_4K(it.bytes), 0);
             if (!read_at(in, g->data_offset + it.src->offset, img.data(), it.bytes)) st = JINF_ERR_IO;
         } else {
-            // the fused matrix in the reference's blocks, then its Q4M image
-            const size_t rb = it.parts[0]->n_bytes / (size_t)it.parts[0]->shape[1];
+            // the fused slices in the reference's blocks, then their Q4M image
+            const jinf_qtype qt = (jinf_qtype)it.qtype;
+            const size_t bb = jinf_qtype_type_size(qt);
+            const int64_t bs = jinf_qtype_block_size(qt);
+            const size_t rb = (size_t)(it.cols / bs) * bb;  // bytes of one row of the slice
             aos.assign(rb * (size_t)it.rows, 0);
             size_t row0 = 0;
             for (int i = 0; i < 3 && it.parts[i] && st == JINF_OK; ++i) {
                 const jinf_gguf_tensor_info* t = it.parts[i];
-                if (it.interleave) {
-                    std::vector<uint8_t> tmp(t->n_bytes);
-                    if (!read_at(in, g->data_offset + t->offset, tmp.data(), t->n_bytes)) st = JINF_ERR_IO;
-                    for (int64_t r = 0; r < t->shape[1]; ++r)
-                        memcpy(aos.data() + (size_t)(2 * r + i) * rb, tmp.data() + (size_t)r * rb, rb);
-                } else {
-                    if (!read_at(in, g->data_offset + t->offset, aos.data() + row0 * rb, t->n_bytes)) st = JINF_ERR_IO;
-                    row0 += (size_t)t->shape[1];
+                const size_t srb = t->n_bytes / (size_t)t->shape[1];  // bytes of one source row
+                std::vector<uint8_t> tmp((size_t)it.nr[i] * srb);
+                if (!read_at(in, g->data_offset + t->offset + (uint64_t)it.r0[i] * srb, tmp.data(), tmp.size())) {
+                    st = JINF_ERR_IO;
+                    break;
                 }
+                const size_t coff = (size_t)(it.c0[i] / bs) * bb;
+                for (int64_t r = 0; r < it.nr[i]; ++r) {
+                    const size_t dst_row = it.interleave ? (size_t)(2 * r + i) : row0 + (size_t)r;
+                    memcpy(aos.data() + dst_row * rb, tmp.data() + (size_t)r * srb + coff, rb);
+                }
+                row0 += (size_t)it.nr[i];
             }
             img.assign(JINF_ALIGN_4K(it.bytes), 0);
             if (st == JINF_OK)
@@ -229,4 +255,8 @@ extern "C" jinf_status jinf_prepare_model_b200(const char* gguf_path, const char
     fclose(in);
     jinf_gguf_close(g);
     return st;
+}
+
+extern "C" jinf_status jinf_prepare_model_b200(const char* gguf_path, const char* nvmw_path) {
+    return jinf_prepare_model_b200_tp(gguf_path, nvmw_path, 1);
 }

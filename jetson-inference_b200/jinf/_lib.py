@@ -198,6 +198,7 @@ SIGNATURES = {
     "jinf_nvmw_writer_write_bundle_section": (i32, [vp, vp, vp, i32]),
     "jinf_prepare_model": (i32, [C.c_char_p, C.c_char_p, sz, i32]),
     "jinf_prepare_model_b200": (i32, [C.c_char_p, C.c_char_p]),
+    "jinf_prepare_model_b200_tp": (i32, [C.c_char_p, C.c_char_p, i32]),
     "jinf_nvmw_open": (i32, [C.POINTER(vp), C.c_char_p]),
     "jinf_nvmw_close": (None, [vp]),
     "jinf_nvmw_get_header": (C.POINTER(NvmwHeader), [vp]),

@@ -104,3 +104,64 @@ def test_tp2_matches_oracle(shape_args, kv_pos, persistent):
         assert rel_err(logits[step], want) < LOGIT_REL, f"step {step}"
         assert toks[step] == oracle.argmax(want), f"step {step}"
         want = orc.forward(toks[step])
+
+
+def _rank_nvmw_main(rank, world, nccl_id, nvmw, shape_args, prompt, persistent, out_q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "jetson-inference_b200"))
+    try:
+        import jinf
+        from jinf import _lib as L
+        torch.cuda.set_device(rank)
+        syn = jinf.SynthModel(jinf.LlamaShape(*shape_args), seed=2, weight_type=L.Q4_K, mix_type=L.Q6_K)
+        out = []
+        for src in ("nvmw", "synth"):
+            opts = jinf.b200_options(device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id[src], eos_token=-1,
+                                     persistent=persistent)
+            eng = (jinf.Engine.from_nvmw(nvmw, max_context=64, options=opts) if src == "nvmw"
+                   else jinf.Engine.from_synth(syn, max_context=64, options=opts))
+            logits = [eng.logits_host(prompt)]
+            for _ in range(4):
+                logits.append(eng.logits_host([eng.last_argmax()]))
+            eng.close()
+            out.append([l.copy() for l in logits])
+        out_q.put((rank, "ok", out))
+    except Exception as e:  # reported to the parent, which fails the test
+        out_q.put((rank, "error", repr(e)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+@pytest.mark.parametrize("persistent", [True, False], ids=["persistent", "per_op"])
+def test_tp2_from_b200_layout_shards(tmp_path, persistent):
+    """Each rank of a 2-GPU engine loads its own pre-packed shard images from a
+    jinf_prepare_model_b200_tp file (Q4_K with Q6_K v / down / output) and computes logits
+    bit-identical to the same engine built from the reference blocks."""
+    import jinf
+    from jinf import _lib as L
+    shape_args = (2, 1024, 16, 4, 2048, 4096, 1e4)
+    syn = jinf.SynthModel(jinf.LlamaShape(*shape_args), seed=2, weight_type=L.Q4_K, mix_type=L.Q6_K)
+    gguf, nvmw = str(tmp_path / "m.gguf"), str(tmp_path / "m.nvmw")
+    syn.write_gguf(gguf)
+    assert L.lib.jinf_prepare_model_b200_tp(gguf.encode(), nvmw.encode(), WORLD) == 0
+    prompt = [int(t) for t in np.random.default_rng(1).integers(0, 4096, size=6)]
+    ids = {"nvmw": jinf.nccl_unique_id(), "synth": jinf.nccl_unique_id()}
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_nvmw_main, args=(r, WORLD, ids, nvmw, shape_args, prompt, persistent, q))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    try:
+        for _ in range(WORLD):
+            rank, status, out = q.get(timeout=300)
+            assert status == "ok", f"rank {rank}: {out}"
+            for a, b in zip(out[0], out[1]):
+                assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), f"rank {rank}"
+    except queue.Empty:
+        pytest.fail("a tensor-parallel rank did not report within 300 s")
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
