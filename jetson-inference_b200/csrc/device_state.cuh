@@ -13,10 +13,6 @@ struct DeviceState {
     int argmax_token;         // decoded argmax of the last step
     int error;                // first device-side error code (DEV_OK = none)
     unsigned int attn_count[64];  // split-K arrival counters of the attention kernel (self-resetting)
-    // Steps the persistent kernel has finished (the flag epoch of its words, step.h). It is
-    // never reset, not even by jinf_engine_reset, so that no stale word matches a later step:
-    // it must stay the last field (a reset clears the state before it).
-    unsigned int epoch;
 };
 
 }  // namespace jinf

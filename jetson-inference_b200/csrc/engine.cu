@@ -438,13 +438,12 @@ struct jinf_engine_impl {
     int step_grid = 0;
     StepPhase* d_phases = nullptr;  // [n_full + n_body]
     unsigned int* step_done = nullptr;
-    unsigned long long* step_attn_part = nullptr;  // flagged per-split attention partials
-    // flagged words the phases hand on (step.h): h ping-pong [2][d], q [nq], the new K and V
-    // rows [nk], the o input records and the down input records (xrec_bytes / 4 words each)
-    unsigned long long* step_fx = nullptr;
-    unsigned long long* step_split = nullptr;  // [grid][2][64] partial rows of tiles shared between CTAs
-    unsigned long long *fx_h[2] = {nullptr, nullptr}, *fx_q = nullptr, *fx_kv = nullptr, *fx_arec = nullptr,
-                       *fx_grec = nullptr;
+    float* step_attn_part = nullptr;
+    // input records of the GEMV phases (inputs of o, gate|up, down, qkv / LM head), written by
+    // the producing phase, and the per-pair sums of h^2 behind the RMSNorm inputs
+    uint8_t* step_rec[4] = {nullptr, nullptr, nullptr, nullptr};
+    float* step_ss = nullptr;
+    unsigned int* step_attn_cnt = nullptr;  // [layers][Hkv] attention split arrival counters
     StepParams sp_full{}, sp_body{};
     // batched prefill (prefill.h): enabled for one GPU, Q4_0 weights, dense FFN; buffers for a
     // chunk of up to pf_cap tokens, allocated at the first long forward()
@@ -922,13 +921,9 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
     ops.push_back(fin);
 }
 
-// Phase table of the persistent step. Per layer L the phases are 5L (QKV), 5L + 1
-// (attention), 5L + 2 (o), 5L + 3 (gate|up), 5L + 4 (down), then the LM head; a phase's index
-// is the tag of the flagged words it writes, and each phase names the tags of its inputs.
-// One GPU: h ping-pongs between fx_h[0] (written by o) and fx_h[1] (written by down, and by
-// the first QKV phase from the embedding row). Tensor parallel: o and down store partials into
-// exchange points 2L and 2L + 1 of every rank; the next RMSNorm input adds them to the h that
-// the previous RMSNorm input stored (ping-pong again), so every rank holds the same h.
+// Phase table of the persistent step (tp_size == 1). Every phase
+// waits for the one before it; the residual stream is hA, updated in place by the o and
+// down epilogues.
 void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph) {
     ph.clear();
     auto add_gemv = [&](const uint8_t* w, const Q4MShape& sh, int xm, int epi) -> StepPhase& {
@@ -944,105 +939,88 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
         p.fmts = sh.fmt | (sh.fmt << 4) | (sh.pairs << 8);
         p.gran = 1;
         p.xin = p.xout = -1;
-        p.tag_in = p.tag_res = -1;
         ph.push_back(p);
         return ph.back();
     };
+    // tensor parallel: o and down store partials into exchange points 2L and 2L + 1 of every
+    // rank; the next RMSNorm input adds them up (h ping-pongs between hA and hB, so that no
+    // CTA overwrites the h another CTA is still reading)
     const bool tp = I->tp_size > 1;
-    // tensor parallel: where the last RMSNorm input stored h, and its tag
-    int hcur = 0, hcur_tag = 0;
+    float* hcur = I->hA;
     auto tp_input = [&](StepPhase& p, int point) {
         p.xm = X_RMSNORM_TP;
         p.xin = point;
-        p.fres = I->fx_h[hcur];
-        p.tag_res = hcur_tag;
-        p.fout_h = I->fx_h[hcur ^ 1];
-        hcur ^= 1;
-        hcur_tag = (int)ph.size() - 1;  // this phase
+        p.hsrc = hcur;
+        p.hout = hcur == I->hA ? I->hB : I->hA;
+        hcur = p.hout;
     };
     for (int L = 0; L < I->L; ++L) {
         const auto& ly = I->layers[L];
-        const int base = 5 * L;
         __half* kc = I->kc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
         __half* vc = I->vc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
+        // The attention output and the activation arrive as records from their producing
+        // phase (attention -> o: rec 0, gate|up -> down: rec 2). The RMSNorm inputs are staged
+        // by every CTA from h (records of h * gain would cost the o and down epilogues an
+        // extra dependent round trip each, more than they save; step_rec[1], [3] and
+        // step_ss stay available for that form).
         StepPhase& qkv = add_gemv(ly.qkv, ly.qkv_sh, L == 0 ? X_EMBED_NORM : X_RMSNORM, EPI_QKV);
         if (ly.v) {  // [q | k] rows, then the v rows of their own type right after them
             qkv.rows = ly.qkv_sh.rows + ly.v_sh.rows;
             qkv.pairs = ly.qkv_sh.pairs + ly.v_sh.pairs;
             qkv.fmts = ly.qkv_sh.fmt | (ly.v_sh.fmt << 4) | (ly.qkv_sh.pairs << 8);
         }
-        if (L == 0) {
-            qkv.hsrc = I->embed;
-            qkv.fout_h = tp ? I->fx_h[0] : I->fx_h[1];  // the embedding row as h (tag 0)
-        } else if (tp) {
-            tp_input(qkv, 2 * (L - 1) + 1);
-        } else {
-            qkv.fin = I->fx_h[1];
-            qkv.tag_in = base - 1;  // down of layer L - 1
-        }
+        qkv.hsrc = L == 0 ? I->embed : I->hA;
+        qkv.hout = L == 0 ? I->hA : nullptr;
+        if (tp && L > 0) tp_input(qkv, 2 * (L - 1) + 1);
         qkv.norm_w = ly.attn_norm;
-        qkv.fout = I->fx_q;
-        qkv.fkv = I->fx_kv;
+        qkv.y = I->q;
         qkv.kcache = kc;
         qkv.vcache = vc;
         StepPhase at{};
         at.kind = PH_ATTN;
         at.xin = at.xout = -1;
-        at.tag_res = -1;
-        at.fin = I->fx_q;
-        at.fkv = I->fx_kv;
-        at.tag_in = base;
+        at.q = I->q;
+        at.out = I->attn;
         at.kcache = kc;
         at.vcache = vc;
         at.layer = L;
-        at.fout = I->fx_arec;
+        at.rec_out = I->step_rec[0];
         at.groups_out = ly.o_sh.groups;
         ph.push_back(at);
         StepPhase& o = add_gemv(ly.o, ly.o_sh, X_RECORDS, tp ? EPI_PARTIAL : EPI_RESID);
-        o.fin = I->fx_arec;
-        o.tag_in = base + 1;
-        if (tp) {
-            o.xout = 2 * L;
-        } else {
-            o.fres = I->fx_h[1];
-            o.tag_res = L == 0 ? 0 : base - 1;
-            o.fout = I->fx_h[0];
-        }
+        o.rec = I->step_rec[0];
+        o.y = I->hA;
+        if (tp) o.xout = 2 * L;
         StepPhase& gu = add_gemv(ly.gu, ly.gu_sh, X_RMSNORM, EPI_GATEUP);
-        if (tp) {
-            tp_input(gu, 2 * L);
-        } else {
-            gu.fin = I->fx_h[0];
-            gu.tag_in = base + 2;
-        }
+        gu.hsrc = I->hA;
+        if (tp) tp_input(gu, 2 * L);
         gu.norm_w = ly.ffn_norm;
         gu.gran = 2;
-        gu.fout = I->fx_grec;
+        gu.rec_out = I->step_rec[2];
         gu.groups_out = ly.down_sh.groups;
         StepPhase& dn = add_gemv(ly.down, ly.down_sh, X_RECORDS, tp ? EPI_PARTIAL : EPI_RESID);
-        dn.fin = I->fx_grec;
-        dn.tag_in = base + 3;
-        if (tp) {
-            dn.xout = 2 * L + 1;
-        } else {
-            dn.fres = I->fx_h[0];
-            dn.tag_res = base + 2;
-            dn.fout = I->fx_h[1];
-        }
+        dn.rec = I->step_rec[2];
+        dn.y = I->hA;
+        if (tp) dn.xout = 2 * L + 1;
     }
     if (with_head) {
         StepPhase& lm = add_gemv(I->lm, I->lm_sh, X_RMSNORM, EPI_LMHEAD);
+        lm.hsrc = I->hA;
         if (tp) {
             tp_input(lm, 2 * (I->L - 1) + 1);
-            lm.fout_h = nullptr;  // the step's last h is not needed
-        } else {
-            lm.fin = I->fx_h[1];
-            lm.tag_in = 5 * I->L - 1;
+            lm.hout = nullptr;  // the step's last h is not needed
         }
         lm.norm_w = I->out_norm;
         lm.y = I->logits;
     }
-    for (auto& p : ph) p.pf[0] = p.pf[1] = -1;
+    for (size_t i = 0; i < ph.size(); ++i) {
+        ph[i].dep = (int)i - 1;
+        // GEMV phases report tile pairs, attention its 32-element output blocks
+        ph[i].dep_target = i == 0                      ? 0u
+                           : ph[i - 1].kind == PH_GEMV ? (unsigned)ph[i - 1].pairs
+                                                       : (unsigned)(I->Hl * I->hd / 32);
+        ph[i].pf[0] = ph[i].pf[1] = -1;
+    }
     // L2 prefetch schedule (phase order per layer: qkv, attention, o, gate|up, down). HBM
     // would idle while attention runs and while CTAs stage inputs and merge rows; in those
     // windows each CTA pulls the weights it owns in a later phase into L2, and the later
@@ -1057,7 +1035,7 @@ void build_step(jinf_engine_impl* I, bool with_head, std::vector<StepPhase>& ph)
             }
         } else if (ph[i].epi == EPI_GATEUP) {
             if (JINF_STEP_PF_MODE >= 2 && gemv_next) ph[i].pf[0] = i + 1;  // down
-        } else if ((ph[i].epi == EPI_RESID || ph[i].epi == EPI_PARTIAL) && i > 0 && ph[i - 1].epi == EPI_GATEUP) {
+        } else if (ph[i].epi == EPI_RESID && i > 0 && ph[i - 1].epi == EPI_GATEUP) {
             if (JINF_STEP_PF_MODE >= 3 && gemv_next && ph[i + 1].epi == EPI_QKV) ph[i].pf[0] = i + 1;  // next qkv
         }
     }
@@ -1144,10 +1122,9 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     // input records: a tile pair of h is one 32-element block, a CTA's gate|up rows are whole
     // activation blocks and fit the 1024-float conversion buffer, as do a kv head's outputs
     const int gu_pairs = I->layers.empty() ? 0 : I->layers[0].gu_sh.pairs;
-    // gate|up pairs a CTA touches (its equal share of units starts and ends mid-pair at most)
-    const int gu_per_cta = (gu_pairs + I->num_sms - 1) / I->num_sms + 2;
+    const int gu_per_cta = 2 * ((gu_pairs / 2 + I->num_sms - 1) / I->num_sms);
     const bool records_ok = I->d % 32 == 0 && (I->Hl * I->hd) % 32 == 0 && gu_pairs % 2 == 0 &&
-                            gu_per_cta * 16 <= 1024 - 64 && G * I->hd <= 1024;
+                            gu_per_cta * 16 <= 1024 && G * I->hd <= 1024;
     if (G > ATTN_MAX_GROUP || (G & (G - 1)) || I->Hkvl > 64 || (I->hd != 64 && I->hd != 128) || smem > 227 * 1024 ||
         step_occupancy(smem, I->wfmt, nbuf) < 1 || !records_ok) {
         JINF_LOG("persistent step unavailable for this shape (%zu bytes of shared memory); using one kernel per "
@@ -1156,43 +1133,34 @@ jinf_status setup_persistent(jinf_engine_impl* I) {
     }
     I->step_grid = I->num_sms;
     {
-        // the flagged words the phases hand on, zeroed once (a zero word carries no valid flag)
         const auto& ly = I->layers[0];
-        auto up = [](size_t w) { return (w + 31) & ~(size_t)31; };  // 256-byte aligned pieces
-        const size_t nh = up((size_t)I->d), nq = up((size_t)I->Hl * I->hd), nkv = up((size_t)I->Hkvl * I->hd);
-        const size_t na = up(xrec_bytes(ly.o_sh.groups) / 4), ng = up(xrec_bytes(ly.down_sh.groups) / 4);
-        const size_t words = 2 * nh + nq + nkv + na + ng;
-        JINF_CUDA_CHECK(cudaMalloc(&I->step_fx, sizeof(unsigned long long) * words));
-        JINF_CUDA_CHECK(cudaMemset(I->step_fx, 0, sizeof(unsigned long long) * words));
-        I->fx_h[0] = I->step_fx;
-        I->fx_h[1] = I->fx_h[0] + nh;
-        I->fx_q = I->fx_h[1] + nh;
-        I->fx_kv = I->fx_q + nq;
-        I->fx_arec = I->fx_kv + nkv;
-        I->fx_grec = I->fx_arec + na;
+        const int rec_groups[4] = {ly.o_sh.groups, ly.gu_sh.groups, ly.down_sh.groups,
+                                   std::max(ly.qkv_sh.groups, I->lm_sh.groups)};
+        for (int i = 0; i < 4; ++i) {
+            // zero once: padding blocks past the real columns are never written and stay zero
+            JINF_CUDA_CHECK(cudaMalloc(&I->step_rec[i], xrec_bytes(rec_groups[i])));
+            JINF_CUDA_CHECK(cudaMemset(I->step_rec[i], 0, xrec_bytes(rec_groups[i])));
+        }
+        JINF_CUDA_CHECK(cudaMalloc(&I->step_ss, sizeof(float) * (size_t)(I->d / 32)));
+        JINF_CUDA_CHECK(cudaMalloc(&I->step_attn_cnt, sizeof(unsigned int) * (size_t)I->L * I->Hkvl));
+        JINF_CUDA_CHECK(cudaMemset(I->step_attn_cnt, 0, sizeof(unsigned int) * (size_t)I->L * I->Hkvl));
     }
     std::vector<StepPhase> full, body;
     build_step(I, true, full);
     build_step(I, false, body);
-    const size_t attn_words = (size_t)I->Hkvl * ATTN_MAX_SPLIT * ATTN_MAX_GROUP * (I->hd + 2);
+    const size_t attn_floats = (size_t)I->Hkvl * ATTN_MAX_SPLIT * ATTN_MAX_GROUP * (I->hd + 2);
     std::vector<StepPhase> all(full);
     all.insert(all.end(), body.begin(), body.end());
-    if (full.size() > (size_t)STEP_MAX_PHASES) {
-        JINF_LOG("persistent step unavailable: %zu phases exceed the %d flag tags", full.size(), STEP_MAX_PHASES);
-        return JINF_OK;
-    }
     JINF_CUDA_CHECK(cudaMalloc(&I->d_phases, sizeof(StepPhase) * all.size()));
-    JINF_CUDA_CHECK(cudaMalloc(&I->step_done, sizeof(unsigned int)));
-    JINF_CUDA_CHECK(cudaMalloc(&I->step_attn_part, sizeof(unsigned long long) * attn_words));
-    JINF_CUDA_CHECK(cudaMemset(I->step_attn_part, 0, sizeof(unsigned long long) * attn_words));
-    JINF_CUDA_CHECK(cudaMalloc(&I->step_split, sizeof(unsigned long long) * (size_t)I->step_grid * 128));
-    JINF_CUDA_CHECK(cudaMemset(I->step_split, 0, sizeof(unsigned long long) * (size_t)I->step_grid * 128));
+    JINF_CUDA_CHECK(cudaMalloc(&I->step_done, sizeof(unsigned int) * (full.size() + 1)));
+    JINF_CUDA_CHECK(cudaMalloc(&I->step_attn_part, sizeof(float) * attn_floats));
     JINF_CUDA_CHECK(cudaMemcpy(I->d_phases, all.data(), sizeof(StepPhase) * all.size(), cudaMemcpyHostToDevice));
-    JINF_CUDA_CHECK(cudaMemset(I->step_done, 0, sizeof(unsigned int)));
+    JINF_CUDA_CHECK(cudaMemset(I->step_done, 0, sizeof(unsigned int) * (full.size() + 1)));
     StepParams sp{};
     sp.done = I->step_done;
     sp.attn_part = I->step_attn_part;
-    sp.split_part = I->step_split;
+    sp.attn_cnt = I->step_attn_cnt;
+    sp.n_attn_cnt = I->L * I->Hkvl;
     sp.st = I->st;
     sp.nq = I->Hl * I->hd;
     sp.nk = I->Hkvl * I->hd;
@@ -1402,7 +1370,7 @@ void free_impl(jinf_engine_impl* I) {
     }
     void* ptrs[] = {I->arena, I->norms, I->embed, I->kc, I->vc, I->hA, I->hB, I->y_o, I->y_down, I->q, I->attn,
                     I->act, I->gate_raw, I->logits, I->attn_partial, I->st, I->dev_tokens, I->gemv_part,
-                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_fx, I->step_split, I->pf_h, I->pf_y,
+                    I->gemv_cnt, I->d_phases, I->step_done, I->step_attn_part, I->step_rec[0], I->step_rec[1], I->step_rec[2], I->step_rec[3], I->step_ss, I->step_attn_cnt, I->pf_h, I->pf_y,
                     I->pf_att, I->pf_sc, I->pf_x16, I->pf_q16, I->pf_err, I->bundles, I->pred_w1,
                     I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp,
                     I->ms, I->m_h, I->m_y, I->m_q, I->m_attn, I->m_act, I->m_logits, I->m_ssq, I->m_attn_part,
@@ -2138,7 +2106,7 @@ extern "C" void jinf_engine_reset(jinf_engine* e) {
     const size_t kv_elems = (size_t)I->L * I->Hkvl * I->max_ctx * I->hd;
     cudaMemsetAsync(I->kc, 0, sizeof(__half) * kv_elems, I->stream);
     cudaMemsetAsync(I->vc, 0, sizeof(__half) * kv_elems, I->stream);
-    cudaMemsetAsync(I->st, 0, offsetof(DeviceState, epoch), I->stream);  // the step epoch is kept
+    cudaMemsetAsync(I->st, 0, sizeof(DeviceState), I->stream);
     cudaStreamSynchronize(I->stream);
     e->n_past = 0;
     std::fill(I->seq_past.begin(), I->seq_past.end(), 0);
@@ -2440,14 +2408,14 @@ extern "C" jinf_status jinf_engine_debug_step_timeout(jinf_engine* e, unsigned l
     jinf_engine_impl* I = e->impl;
     if (!I->persistent || I->tp_size != 1) return JINF_ERR_INVALID;
     cudaSetDevice(I->device);
-    // a copy of the phase table whose attention phase waits for q words with a tag that no
-    // phase writes: nothing ever sets what it waits for
+    // a copy of the phase table whose attention phase waits for more finished QKV tile
+    // pairs than exist: nothing ever sets what it waits for
     StepParams sp = I->sp_full;
     std::vector<StepPhase> ph((size_t)sp.n_phases);
     JINF_CUDA_CHECK(cudaMemcpy(ph.data(), sp.phases, sizeof(StepPhase) * ph.size(), cudaMemcpyDeviceToHost));
     for (auto& p : ph)
         if (p.kind == PH_ATTN) {
-            p.tag_in = STEP_MAX_PHASES;
+            p.dep_target = 0xFFFFFFFFu;
             break;
         }
     StepPhase* dph = nullptr;

@@ -367,16 +367,20 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     pdl_wait();
     pdl_trigger();
 
-    // ---------------- prologue: norm factors, then the part's records (one group of one vector
-    // per warp pass: lane l converts block l / 8, elements 4 (l % 8) .. +3)
-    if (tid < MULTI_MAX) {
+    // ---------------- prologue: norm factors (warp v < n adds vector v's partial sums of
+    // squares: lane l the parts l, l + 32, ..., then a fixed shuffle tree), then the part's
+    // records (one group of one vector per warp pass: lane l converts block l / 8, elements
+    // 4 (l % 8) .. +3)
+    if (warp < MULTI_MAX) {
         float f = 1.0f;
-        if (XM == MX_NORMED && tid < n) {
+        if (XM == MX_NORMED && warp < n) {
             float ss = 0.f;
-            for (int q = 0; q < p.ssq_parts; ++q) ss += p.ssq[(size_t)q * n + tid];
+            for (int q = lane; q < p.ssq_parts; q += 32) ss += p.ssq[(size_t)q * n + warp];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(JINF_FULL_MASK, ss, o);
             f = rsqrtf(ss / (float)p.cols + p.eps);
         }
-        fac[tid] = f;
+        if (lane == 0) fac[warp] = f;
     }
     const int n4 = p.cols / 4;
     for (int it = warp; it < n * ng; it += MNW) {
@@ -433,10 +437,18 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
             if (old != (unsigned)(kw - 1)) continue;  // another K part finishes this pair
             __threadfence();
             if (lane == 0) p.cnt[q] = 0u;  // ready for the next launch
+            // the parts in K order, eight loads in flight per lane
             const float* pb = p.part + (size_t)q * kw * n * 32;
+            const size_t kst = (size_t)n * 32;
             for (int e = lane; e < n * 32; e += 32) {
                 float s = 0.f;
-                for (int k2 = 0; k2 < kw; ++k2) s += __ldcg(pb + (size_t)k2 * n * 32 + e);
+                for (int k0 = 0; k0 < kw; k0 += 8) {
+                    float t[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) t[i] = k0 + i < kw ? __ldcg(pb + (size_t)(k0 + i) * kst + e) : 0.f;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) s += t[i];
+                }
                 eps_w[(e >> 5) * EP_STRIDE + (e & 31)] = s;
             }
             __syncwarp();

@@ -191,10 +191,19 @@ __global__ void __launch_bounds__(GEMV_M_THREADS) k_gemv_q4m(const GemvParams p)
             if (lane == 0) p.cnt[pair] = 0u;  // ready for the next launch
             v0 = 0.f;
             v1 = 0.f;
+            // the parts in K order, eight row pairs in flight per lane
             const float* pb = p.part + (size_t)pair * kw * Q4M_PAIR_ROWS;
-            for (int q = 0; q < kw; ++q) {
-                v0 += __ldcg(pb + q * Q4M_PAIR_ROWS + r0);
-                v1 += __ldcg(pb + q * Q4M_PAIR_ROWS + r0 + 1);
+            for (int q0 = 0; q0 < kw; q0 += 8) {
+                float2 t[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    t[i] = q0 + i < kw ? __ldcg(reinterpret_cast<const float2*>(pb + (q0 + i) * Q4M_PAIR_ROWS + r0))
+                                       : make_float2(0.f, 0.f);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    v0 += t[i].x;
+                    v1 += t[i].y;
+                }
             }
         }
         if (lane < 16) epilogue_pair(ea, pair * Q4M_PAIR_ROWS + r0, v0 * fac, v1 * fac, lmax, lidx);

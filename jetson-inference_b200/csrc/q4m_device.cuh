@@ -366,17 +366,14 @@ __device__ __forceinline__ float4 ld_f4(const float* p, int i, bool coherent) {
     return coherent ? __ldcg(reinterpret_cast<const float4*>(p) + i) : reinterpret_cast<const float4*>(p)[i];
 }
 
-// Digits of one 32-element block held by an octet of lanes (lane q = lane & 7 of the octet
-// holds elements 4q .. 4q+3 in v): the lane's hi and lo digit words (elements 4q .. 4q+3,
-// one byte each), the octet's digit sums and its block maximum. All 32 lanes of the warp call
-// it (the octet reductions shuffle). A block of zeros gives zero digits.
-struct OctetDigits {
-    uint32_t H, L;
-    int sh, sl;
-    float amax;
-};
-__device__ __forceinline__ OctetDigits octet_digits(float4 v) {
-    OctetDigits o;
+// Digit records of one 32-element block held by an octet of lanes (lane q = lane & 7 of the
+// octet holds elements 4q .. 4q+3 in v): `dig` is the group's 64 record words and `prm` its
+// 4 block params (shared or global memory), j the block within the group. All 32 lanes of
+// the warp call it (the octet reductions shuffle); only octets with `store` write. A block
+// of zeros gives zero records.
+__device__ __forceinline__ void octet_to_records(float4 v, int lane, int j, uint32_t* dig, float4* prm,
+                                                 bool store = true) {
+    const int q = lane & 7;
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     amax = fmaxf(amax, __shfl_xor_sync(JINF_FULL_MASK, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(JINF_FULL_MASK, amax, 2));
@@ -395,36 +392,18 @@ __device__ __forceinline__ OctetDigits octet_digits(float4 v) {
         sl += lo;
     }
 #pragma unroll
-    for (int o2 = 1; o2 < 8; o2 <<= 1) {
-        sh += __shfl_xor_sync(JINF_FULL_MASK, sh, o2);
-        sl += __shfl_xor_sync(JINF_FULL_MASK, sl, o2);
+    for (int o = 1; o < 8; o <<= 1) {
+        sh += __shfl_xor_sync(JINF_FULL_MASK, sh, o);
+        sl += __shfl_xor_sync(JINF_FULL_MASK, sl, o);
     }
-    o.H = H;
-    o.L = L;
-    o.sh = sh;
-    o.sl = sl;
-    o.amax = amax;
-    return o;
-}
-
-// Where the digit words of lane q of an octet go in a group's 64 record words (block j):
-// elements k = 4q .. 4q+3 are word r = q >> 2 of record lanes 4 (2j + h) + (q & 3).
-__device__ __forceinline__ int rec_word_hi(int j, int q) { return (8 * j + (q & 3)) * 2 + (q >> 2); }
-__device__ __forceinline__ int rec_word_lo(int j, int q) { return (8 * j + 4 + (q & 3)) * 2 + (q >> 2); }
-
-// Digit records of one 32-element block held by an octet of lanes (octet_digits): `dig` is
-// the group's 64 record words and `prm` its 4 block params (shared or global memory), j the
-// block within the group. All 32 lanes of the warp call it; only octets with `store` write.
-__device__ __forceinline__ void octet_to_records(float4 v, int lane, int j, uint32_t* dig, float4* prm,
-                                                 bool store = true) {
-    const int q = lane & 7;
-    const OctetDigits o = octet_digits(v);
+    // elements k = 4q .. 4q+3: word r = q >> 2 of record lanes 4 (2j + h) + (q & 3)
+    const int r = q >> 2, c = q & 3;
     if (!store) return;
-    dig[rec_word_hi(j, q)] = o.H;
-    dig[rec_word_lo(j, q)] = o.L;
+    dig[(8 * j + c) * 2 + r] = H;
+    dig[(8 * j + 4 + c) * 2 + r] = L;
     if (q == 0) {
-        const float ia = o.amax / XREC_DIGIT_MAX;
-        prm[j] = make_float4(__int_as_float(-8 * o.sh), __int_as_float(-8 * o.sl), ia, ia * 0.0625f);
+        const float ia = amax / XREC_DIGIT_MAX;
+        prm[j] = make_float4(__int_as_float(-8 * sh), __int_as_float(-8 * sl), ia, ia * 0.0625f);
     }
 }
 

@@ -33,22 +33,20 @@ constexpr int STEP_MAX_TP = 8;         // ranks of the tensor-parallel persisten
 
 enum PhaseKind { PH_GEMV = 0, PH_ATTN = 1 };
 
-// One phase of the decode step. Phases hand their outputs on as flagged words (8 bytes:
-// the value's 32 bits, then a 32-bit flag): the flag of a word written by phase `ph` during the
-// step with epoch e is step_flag(e, ph), so a consumer's load of the word is also its wait
-// (it reloads until the flag is the one it expects), with no counter and no fence on the way.
-// An aligned 8-byte word is written and read whole.
+// One phase of the decode step. A phase starts (on every CTA) once phase `dep` has
+// reported `dep_target` finished units: GEMV phases count finished 32-row tile pairs,
+// attention counts finished kv heads.
 struct StepPhase {
     int kind;
-    int tag_in;              // phase whose flagged output this phase's input is (-1: none)
-    int tag_res;             // EPI_RESID: phase that wrote the residual rows `fres`; tensor parallel:
-                             //   phase that wrote the h of `fres` the ranks' partials are added to
+    int dep;                 // -1: no dependency
+    unsigned int dep_target;
     int gran;                // a CTA owns whole runs of `gran` tile pairs (2: its gate|up rows
                              // make whole 32-element blocks of the activation)
-    int layer;               // layer index
+    int layer;               // PH_ATTN: layer index (selects its split arrival counters)
     int pf[2];               // GEMV phases (-1: none) whose weights this CTA owns are prefetched
-                             // into L2 when the CTA reaches this phase
-    int xin;                 // tensor parallel: exchange point this phase reads (X_RMSNORM_TP), -1: none
+                             // into L2 when the CTA reaches this phase (before its wait)
+    int xin;                 // tensor parallel: exchange point this phase reads (X_RMSNORM_TP; its
+                             // staging waits for the flagged words, in place of `dep`), -1: none
     int xout;                // exchange point this phase writes (EPI_PARTIAL), -1: none
     // PH_GEMV
     int xm, epi;
@@ -56,34 +54,37 @@ struct StepPhase {
                              // rest (fmts >> 4) & 15 (a QKV of [q|k] in one type, v in another)
     const uint8_t* w;        // Q4M matrix
     int rows, cols, pairs, groups;
-    const float* hsrc;       // X_EMBED_NORM: token_embd [V][cols]
+    const float* x;          // X_PLAIN_F32: input (written earlier in the step)
+    const float* hsrc;       // X_RMSNORM: residual stream; X_EMBED_NORM: token_embd [V][cols]
+    float* hout;             // X_EMBED_NORM: residual stream (CTA 0 stores the embedding row)
     const float* norm_w;     // RMSNorm gain
-    float* y;                // EPI_LMHEAD: logits
+    float* y;                // epilogue output; EPI_RESID: the residual stream (h += W x)
     __half* kcache;          // EPI_QKV and PH_ATTN: this layer's cache [Hkv][max_ctx][hd]
     __half* vcache;
-    // flagged words (step_flag): the input (X_RMSNORM: h [cols]; X_RECORDS: digit records as
-    // xrec_bytes(groups) / 4 words; PH_ATTN: q [n_heads * hd]), the residual rows EPI_RESID
-    // adds to (and the tensor-parallel h the partials are added to), the output (EPI_RESID:
-    // h [rows]; EPI_QKV: q; EPI_GATEUP and PH_ATTN: the next phase's records, groups_out
-    // groups), and the new K and V rows of the step's position (EPI_QKV writes, PH_ATTN
-    // reads: [nk / 2] K words then [nk / 2] V words, two halves per word)
-    const unsigned long long* fin;
-    const unsigned long long* fres;
-    unsigned long long* fout;
-    unsigned long long* fkv;
-    unsigned long long* fout_h;  // X_EMBED_NORM and X_RMSNORM_TP: the CTA that owns pair 0 stores
-                                 // the phase's h here (flag of this phase), or null
+    // X_RECORDS input: the digit records written by the producing phase and, for an RMSNorm
+    // input, the producer's per-pair sums of h^2 (n_ss of them) that give the norm factor
+    const uint8_t* rec;
+    const float* ssp;
+    int n_ss;
+    // records this phase writes for the next GEMV phase (null: none), that phase's group
+    // count, and for EPI_RESID the per-pair sums of h^2 and the next RMSNorm gain (the
+    // records then hold h * gain)
     int groups_out;
+    uint8_t* rec_out;
+    float* ss_out;
+    const float* gain_out;
+    // PH_ATTN
+    const float* q;          // [n_heads * hd], RoPE applied
+    float* out;              // [n_heads * hd]
 };
 
 struct StepParams {
     const StepPhase* phases;  // device array
     int n_phases;
-    unsigned int* done;       // [1] CTAs that have left the step (zero at launch, cleared by the last)
-    unsigned long long* attn_part;  // [Hkv][ATTN_MAX_SPLIT][ATTN_MAX_GROUP][hd + 2] flagged per-split
-                                    // attention partials (acc, m, l)
-    unsigned long long* split_part;  // [grid][2][64] flagged partial rows of the (at most two) tiles a
-                                     // CTA shares with its neighbours in a GEMV phase
+    unsigned int* done;       // [n_phases + 1] zero at launch; [n_phases] counts exiting CTAs
+    float* attn_part;         // [Hkv][ATTN_MAX_SPLIT][ATTN_MAX_GROUP][hd + 2] per-CTA attention partials
+    unsigned int* attn_cnt;   // [layers][Hkv] split arrival counters, zero at launch (cleared at the end)
+    int n_attn_cnt;
     DeviceState* st;
     int nq, nk, head_dim, max_ctx, n_heads, n_kv_heads;
     float rope_base, eps;
@@ -92,7 +93,7 @@ struct StepParams {
     int fmt;                  // Q4MFormat of every weight matrix of the step
     int nbuf;                 // weight ring slots per warp: STEP_NBUF, or 3 for wide models
     unsigned int xstage_bytes;  // shared bytes for the staged GEMV input / attention scratch
-    unsigned long long spin_limit;  // polls before a wait gives up (DEV_ERR_TIMEOUT)
+    unsigned long long spin_limit;  // polls before a dependency wait gives up (DEV_ERR_TIMEOUT)
     // tensor parallel (tp_size > 1): the exchange area of every rank, mapped into this
     // process (xpeer[tp_rank] is this rank's own), laid out as step_xchg_layout says
     int tp_rank, tp_size;
@@ -100,13 +101,6 @@ struct StepParams {
     uint8_t* xpeer[STEP_MAX_TP];
     unsigned long long x_keycnt, x_keys, x_data, x_point, x_slot;
 };
-
-// Flag of the words phase `ph` writes during the step whose epoch is `epoch` (steps the
-// engine's persistent kernel has finished; never reset, so no stale word of an earlier step
-// carries a current flag: the flag repeats only after 2^22 steps, and every word a step reads
-// is rewritten by that step). Never 0, so zeroed buffers hold no valid word.
-__host__ __device__ inline uint32_t step_flag(uint32_t epoch, int ph) { return epoch * 1024u + (uint32_t)ph + 1u; }
-constexpr int STEP_MAX_PHASES = 1023;  // phase indices (and tags) below 1024; 1023 is never written
 
 // Exchange area of one rank for the tensor-parallel persistent step (same layout on every
 // rank; all offsets 256-byte aligned):
@@ -122,12 +116,9 @@ struct XchgLayout {
 };
 XchgLayout step_xchg_layout(int n_points, int tp_size, int d);
 
-// CTA c of C owns units [step_cta_unit(c), step_cta_unit(c + 1)) of every GEMV phase of U
-// units (pair-major: unit p * groups + g), an equal share whatever the shape; a tile of
-// `gran` pairs that crosses a CTA boundary is merged by the CTA that holds its last unit.
-__host__ __device__ inline int step_cta_unit(int c, int C, int U) {
-    return (int)((unsigned long long)c * (unsigned long long)U / (unsigned long long)C);
-}
+// CTA c of C owns tile pairs [step_cta_tile(c), step_cta_tile(c + 1)) of every GEMV phase.
+// (c * T stays far below 2^32: at most a few hundred CTAs times tens of thousands of pairs.)
+__host__ __device__ inline int step_cta_tile(int c, int C, int T) { return (int)((unsigned)(c * T) / (unsigned)C); }
 
 // Shared bytes of the staged input for the widest GEMV phase, or of the attention scratch
 // (q of one kv head's query heads + per-warp partials), whichever is larger.
