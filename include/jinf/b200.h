@@ -58,7 +58,9 @@ size_t jinf_b200_gemv_q4m_batch_workspace_bytes(int rows, int cols, int batch);
 jinf_status jinf_b200_gemv_q4m_batch(const void* q4m, const void* x, int x_type, float* y, int rows, int cols,
                                      int batch, void* workspace, cudaStream_t stream);
 // The same for a Q4M image of reference block type `qtype` (Q4_0 = 2, Q8_0 = 8, Q4_K = 12,
-// Q6_K = 14); kw = 0 picks the K split, kw > 0 forces it (1..32, within shared memory).
+// Q6_K = 14); kw = 0 picks the K split and how it is shared out, kw > 0 forces kw parts with
+// each warp taking whole tile pairs, kw < 0 forces -kw parts with a CTA's warps splitting
+// each of its tile pairs (1..32 parts, within shared memory).
 size_t jinf_b200_gemv_q4m_batch_workspace_bytes_qt(int rows, int cols, int batch, int qtype);
 jinf_status jinf_b200_gemv_q4m_batch_qt(const void* q4m, int qtype, const void* x, int x_type, float* y, int rows,
                                         int cols, int batch, void* workspace, int kw, cudaStream_t stream);

@@ -2,15 +2,18 @@
 //
 // Math of reference cuda/attention_kernel.cu:45-98 (scores q.k / sqrt(hd), GQA head map
 // h -> h / (H/Hkv), max-subtracted softmax, P.V), restated as split-K flash-decoding:
-//   grid = n_kv_heads x n_split CTAs; CTA (h, s) covers positions [s*n/S, (s+1)*n/S)
-//   for ALL query heads of kv head h, so each K/V row is read from HBM once (the
-//   reference re-reads it once per query head).
+//   grid = n_kv_heads x n_split CTAs; of these, S = min(n_split, ceil(n / ATT_SPAN)) splits
+//   hold positions (n = pos + 1 read at run time), CTA (h, s < S) covering [s*n/S,
+//   (s+1)*n/S) for ALL query heads of kv head h, so each K/V row is read from HBM once (the
+//   reference re-reads it once per query head), and every split has enough positions to
+//   pay for its share of the merge.
 //   Each warp takes 32-position tiles: the tile's K and V rows are copied into the
 //   warp's shared memory with asynchronous 16-byte copies (all issued at once, one
 //   wait), K chunk-swizzled so that lane-per-position reads are bank-conflict free.
 //   Lanes own positions for q.k (online softmax per query head) and head dims for p.v.
 //   The CTA's (m, l, acc) goes to a partial buffer; the last CTA of a kv head (arrival
-//   counter, reset by that CTA for graph replay) merges the splits in fixed order.
+//   counter, reset by that CTA for graph replay) merges the S splits in fixed order, every
+//   load of a pass issued before the first is used.
 // Cache layout: [n_kv_heads][max_ctx][hd] fp16 per layer; n = pos + 1 is read from the
 // device state, so one captured graph serves every position.
 #include "common.cuh"
@@ -25,6 +28,7 @@ namespace jinf {
 constexpr int AW = 4;      // warps per CTA
 constexpr int AMAXG = 8;   // max query heads per kv head
 constexpr int TP = 32;     // positions per warp tile
+constexpr int ATT_SPAN = 256;  // fewest positions per split (more splits only for more positions)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -83,7 +87,9 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
     for (int i = threadIdx.x; i < G * HD; i += blockDim.x) sm.q[i] = qv[(size_t)kvh * G * HD + i] * scale;
     __syncthreads();
 
-    const int start = (int)((int64_t)n * split / p.n_split), end = (int)((int64_t)n * (split + 1) / p.n_split);
+    const int ns = min(p.n_split, max(1, (n + ATT_SPAN - 1) / ATT_SPAN));  // splits with positions
+    const int start = split < ns ? (int)((int64_t)n * split / ns) : n;
+    const int end = split < ns ? (int)((int64_t)n * (split + 1) / ns) : n;
     const __half* kb = p.kcache + so + (size_t)kvh * p.max_ctx * HD;
     const __half* vb = p.vcache + so + (size_t)kvh * p.max_ctx * HD;
     __half* ksm = sm.k[wid];
@@ -213,21 +219,55 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
     __syncthreads();
     if (!sm.is_last) return;
     __threadfence();
-    // merge the n_split partials of this kv head in split order
+    // merge the ns partials of this kv head in split order. First every split's (m, l) of every
+    // query head (one pass of loads), the weights f_s = exp(m_s - M) and L = sum f_s l_s; then
+    // each thread adds float4s of the accumulators, eight splits' loads in flight at a time.
     const float* base = partv + (size_t)kvh * p.n_split * stride;
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-        const int g = i / HD, d = i % HD;
+    float* fw = &sm.wacc[0][0][0];                  // [G][ns] m_s, then the weights
+    float* fl = fw + AMAXG * p.n_split;             // [G][ns] l_s
+    float* linv = &sm.wm[0][0];                     // [G] L
+    for (int i = threadIdx.x; i < G * ns; i += blockDim.x) {
+        const int g = i / ns, s2 = i % ns;
+        fw[g * ns + s2] = __ldcg(base + s2 * stride + AMAXG * HD + g);
+        fl[g * ns + s2] = __ldcg(base + s2 * stride + AMAXG * HD + AMAXG + g);
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
         float M = -INFINITY;
-        for (int s2 = 0; s2 < p.n_split; ++s2) M = fmaxf(M, __ldcg(base + s2 * stride + AMAXG * HD + g));
-        float a = 0.f, L = 0.f;
-        for (int s2 = 0; s2 < p.n_split; ++s2) {
-            const float ms = __ldcg(base + s2 * stride + AMAXG * HD + g);
-            if (ms == -INFINITY) continue;
-            const float f = expf(ms - M);
-            a = fmaf(__ldcg(base + s2 * stride + g * HD + d), f, a);
-            L = fmaf(__ldcg(base + s2 * stride + AMAXG * HD + AMAXG + g), f, L);
+        for (int s2 = 0; s2 < ns; ++s2) M = fmaxf(M, fw[g * ns + s2]);
+        float L = 0.f;
+        for (int s2 = 0; s2 < ns; ++s2) {
+            const float ms = fw[g * ns + s2];
+            const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+            fw[g * ns + s2] = f;
+            L = fmaf(fl[g * ns + s2], f, L);
         }
-        outv[(size_t)(kvh * G + g) * HD + d] = a / L;
+        linv[g] = L;
+    }
+    __syncthreads();
+    constexpr int D4 = HD / 4;
+    for (int i = threadIdx.x; i < G * D4; i += blockDim.x) {
+        const int g = i / D4, d4 = i % D4;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            float4 t[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                t[k] = s0 + k < ns ? __ldcg(reinterpret_cast<const float4*>(base + (s0 + k) * stride + g * HD) + d4)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float f = s0 + k < ns ? fw[g * ns + s0 + k] : 0.f;
+                a.x = fmaf(t[k].x, f, a.x);
+                a.y = fmaf(t[k].y, f, a.y);
+                a.z = fmaf(t[k].z, f, a.z);
+                a.w = fmaf(t[k].w, f, a.w);
+            }
+        }
+        const float L = linv[g];
+        *reinterpret_cast<float4*>(outv + (size_t)(kvh * G + g) * HD + 4 * d4) =
+            make_float4(a.x / L, a.y / L, a.z / L, a.w / L);
     }
     if (threadIdx.x == 0) cntv[kvh] = 0u;
 }
@@ -239,6 +279,8 @@ size_t attn_partial_floats(int n_kv_heads, int n_split, int head_dim) {
 cudaError_t attn_launch(const AttnParams& p, cudaStream_t s, bool pdl) {
     if (p.n_heads % p.n_kv_heads || p.n_heads / p.n_kv_heads > AMAXG || p.n_kv_heads > 64) return cudaErrorInvalidValue;
     if (p.ms && (p.n_vec < 1 || p.n_vec > MULTI_MAX || p.n_kv_heads > MULTI_MAX_KV_HEADS)) return cudaErrorInvalidValue;
+    // the merge keeps 2 x AMAXG x n_split floats in the CTA's accumulator scratch
+    if (p.n_split < 1 || 2 * AMAXG * p.n_split > AW * AMAXG * p.head_dim) return cudaErrorInvalidValue;
     if (p.head_dim != 64 && p.head_dim != 128) return cudaErrorInvalidValue;
     const size_t smem = attn_smem_bytes(p.head_dim);
     static bool configured[2] = {false, false};

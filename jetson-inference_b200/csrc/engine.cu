@@ -768,7 +768,7 @@ Op multi_gemv_op(jinf_engine_impl* I, int n, const uint8_t* w, const Q4MShape& s
     p.groups = sh.groups;
     p.fmt = sh.fmt;
     p.n = n;
-    p.kw = multi_pick_kw(sh.pairs, sh.groups, n, sh.fmt, op.grid);
+    multi_plan(sh.pairs, sh.groups, n, sh.fmt, op.grid, epi, &p.kw, &p.local);
     p.gk = p.kw > 0 ? (sh.groups + p.kw - 1) / p.kw : 0;
     p.part = I->m_part;
     p.cnt = I->m_cnt;
@@ -840,7 +840,7 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
             v.mp.pairs = ly.v_sh.pairs;
             v.mp.groups = ly.v_sh.groups;
             v.mp.fmt = ly.v_sh.fmt;
-            v.mp.kw = multi_pick_kw(ly.v_sh.pairs, ly.v_sh.groups, n, ly.v_sh.fmt, v.grid);
+            multi_plan(ly.v_sh.pairs, ly.v_sh.groups, n, ly.v_sh.fmt, v.grid, ME_QKV, &v.mp.kw, &v.mp.local);
             v.mp.gk = v.mp.kw > 0 ? (ly.v_sh.groups + v.mp.kw - 1) / v.mp.kw : 0;
             v.mp.nq = 0;
             v.mp.nk = 0;
@@ -1622,10 +1622,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     }
     I->seq_stride = kv_elems;
     I->seq_past.assign(I->n_seqs, 0);
-    I->n_split = (I->max_ctx + 63) / 64;
-    const int max_split = (2 * I->num_sms) / I->Hkvl;
-    if (I->n_split > max_split) I->n_split = max_split;
-    if (I->n_split < 1) I->n_split = 1;
+    // attention splits (the kernel uses one per 256 positions at run time, up to this many)
+    I->n_split = std::max(1, std::min(64, (I->max_ctx + 255) / 256));
     bool ok = cudaMalloc(&I->norms, sizeof(float) * (size_t)(2 * I->L + 1) * d) == cudaSuccess &&
               cudaMalloc(&I->embed, sizeof(float) * (size_t)I->V * d) == cudaSuccess &&
               cudaMalloc(&I->kc, sizeof(__half) * kv_elems * I->n_seqs) == cudaSuccess &&
@@ -1847,7 +1845,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         for (int n = 1; n <= S; ++n) {
             auto need = [&](const Q4MShape& sh) {
                 if (!sh.rows) return;
-                const int kw = multi_pick_kw(sh.pairs, sh.groups, n, sh.fmt, grid);
+                int kw = 0, local = 0;
+                multi_plan(sh.pairs, sh.groups, n, sh.fmt, grid, ME_STORE, &kw, &local);
                 ws = std::max(ws, (size_t)sh.pairs * std::max(kw, 1) * n * 32);
                 pairs = std::max(pairs, (size_t)sh.pairs);
             };
@@ -1855,8 +1854,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
             for (const auto& ly : I->layers)
                 for (const Q4MShape* sh : {&ly.qkv_sh, &ly.v_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) need(*sh);
         }
-        // attention splits: about four CTAs per SM at one vector, whole 64-position spans
-        I->m_split = std::max(1, std::min((I->max_ctx + 63) / 64, (4 * I->num_sms + I->Hkvl - 1) / I->Hkvl));
+        // attention splits: one per 256 positions at run time, up to this many
+        I->m_split = I->n_split;
         const size_t attn_part = attn_partial_floats(I->Hkvl, I->m_split, hd) * S;
         bool mok = cudaMalloc(&I->ms, sizeof(MultiState)) == cudaSuccess &&
                    cudaHostAlloc(&I->ms_pinned, sizeof(int32_t) * 4 * MULTI_MAX, cudaHostAllocDefault) == cudaSuccess &&

@@ -17,13 +17,18 @@
 // reduction is needed.
 //
 // Scheduling. CTA c works on K part kp = c % kw only, so it stages just that part's records
-// (n vectors x gk groups) in shared memory, and its warps take tile pairs; consecutive pairs
-// of a part go to different CTAs. Each warp streams its tasks' units through a private
-// cp.async ring that runs ahead across tasks; the first units are requested before the kernel
-// waits on its producer (programmatic dependent launch). With kw > 1 each task leaves its
-// n x 32 partial rows in the workspace and the last task of a pair (arrival counter, reset by
-// it) adds them in K order, so results are deterministic. The finishing warp stages the
-// pair's rows in shared memory and runs the epilogue on adjacent row pairs.
+// (n vectors x gk groups) in shared memory. Two ways to share out a part's work:
+//   per warp (many tile pairs, e.g. an LM head): the CTA's warps take tile pairs, each warp
+//     all of the part's groups of its pair; consecutive pairs go to different CTAs;
+//   per CTA (p.local: at most a few pairs per CTA, the projections of a layer): the CTA takes
+//     tile pairs and its 16 warps split the part's groups of each, meeting in shared memory in
+//     warp order, so no warp idles for want of a pair and few partials leave the CTA.
+// Each warp streams its units through a private cp.async ring that runs ahead across pairs;
+// the first units are requested before the kernel waits on its producer (programmatic
+// dependent launch). With kw > 1 each (pair, part) leaves its n x 32 partial rows in the
+// workspace and the last one of a pair (arrival counter, reset by it) adds them in K order,
+// so results are deterministic. The pair's rows are staged in shared memory and the
+// epilogue runs on adjacent row pairs.
 #include "common.cuh"
 #include "gemv.h"
 #include "jinf/b200.h"
@@ -45,6 +50,10 @@ constexpr int MNW = MT / 32;          // warps
 constexpr int kMultiMaxKw = 32;
 constexpr int EP_STRIDE = 33;         // floats per staged row block (32 rows, padded)
 
+// Ring slots per warp: 2 in flight per warp keep HBM busy with 16 warps per SM, and leave
+// room for the records of several vectors (the larger Q6_K and Q8_0 units: 1 in flight).
+__host__ __device__ constexpr inline int multi_nbuf(int fmt) { return fmt == Q4M_Q6_K || fmt == Q4M_Q8_0 ? 2 : 3; }
+
 // Staged records: digits [n][gk][256 B] then params [n][gk][4][16 B], each vector's run padded
 // (digits +64 B, params +16 B) so that the lanes of one load that read different vectors fall
 // in different shared-memory banks.
@@ -53,11 +62,13 @@ __host__ __device__ inline int multi_prm_stride(int gk) { return gk * 64 + 16; }
 __host__ __device__ inline size_t multi_rec_bytes(int n, int gk) {
     return (size_t)n * (multi_dig_stride(gk) + multi_prm_stride(gk));
 }
-// epilogue staging [MNW][MULTI_MAX][EP_STRIDE] floats, then 64 floats of factors / keys
-constexpr size_t MULTI_EP_BYTES = (size_t)MNW * MULTI_MAX * EP_STRIDE * 4 + 64 * 4 + MNW * MULTI_MAX * 8;
+// epilogue staging [MNW][MULTI_MAX][EP_STRIDE] floats, 64 floats of norm factors, the argmax
+// keys [MNW][MULTI_MAX], the merged rows [MULTI_MAX][EP_STRIDE] (per-CTA split) and a flag
+constexpr size_t MULTI_EP_BYTES =
+    (size_t)MNW * MULTI_MAX * EP_STRIDE * 4 + 64 * 4 + MNW * MULTI_MAX * 8 + MULTI_MAX * EP_STRIDE * 4 + 16;
 
 __host__ __device__ inline size_t multi_smem(int n, int gk, int fmt) {
-    return multi_rec_bytes(n, gk) + MULTI_EP_BYTES + (size_t)MNW * gemvm_nbuf(fmt) * q4m_unit_bytes(fmt);
+    return multi_rec_bytes(n, gk) + MULTI_EP_BYTES + (size_t)MNW * multi_nbuf(fmt) * q4m_unit_bytes(fmt);
 }
 
 __device__ __forceinline__ void lds128(uint32_t a, uint32_t (&r)[4]) {
@@ -321,10 +332,54 @@ __device__ __forceinline__ float4 multi_load(const MultiParams& p, int v, int i,
     return h;
 }
 
+// Epilogue of rows (row, row + 1) of tile pair q for vector v, values v0, v1 (valid: v < n).
+// Every lane of the warp calls it with its own row pair of 16 (qq = lane & 15, one vector per
+// half warp): ME_RESID adds the halves' sums of squares with shuffles.
+template <int EPI>
+__device__ __forceinline__ void multi_epilogue(const MultiParams& p, int q, int qq, int v, bool valid, float v0,
+                                               float v1, float& lmax, int& lidx) {
+    const int row = q * Q4M_PAIR_ROWS + 2 * qq;
+    if (EPI == ME_RESID) {
+        float s2 = 0.f;
+        if (valid) {  // rows = the residual width (a multiple of 32): every row exists
+            float* hy = p.y + (size_t)v * p.ldy + row;
+            const float h0 = hy[0] + v0, h1 = hy[1] + v1;
+            hy[0] = h0;
+            hy[1] = h1;
+            s2 = fmaf(h0, h0, h1 * h1);
+        }
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) s2 += __shfl_xor_sync(JINF_FULL_MASK, s2, o);
+        if (valid && qq == 0) p.ssq_out[(size_t)q * p.n + v] = s2;
+        return;
+    }
+    if (!valid) return;
+    EpiArgs ea;
+    ea.rows = p.rows;
+    ea.y = p.y + (size_t)v * p.ldy;
+    ea.coherent = false;
+    if (EPI == ME_QKV) {
+        const size_t so = (size_t)p.ms->seq[v] * p.seq_stride;
+        ea.epi = EPI_QKV;
+        ea.kcache = p.kcache + so;
+        ea.vcache = p.vcache + so;
+        ea.nq = p.nq;
+        ea.nk = p.nk;
+        ea.head_dim = p.head_dim;
+        ea.max_ctx = p.max_ctx;
+        ea.pos = p.ms->pos[v];
+        ea.rope_base = p.rope_base;
+    } else {
+        ea.epi = EPI == ME_GATEUP ? EPI_GATEUP : EPI == ME_LMHEAD ? EPI_LMHEAD : EPI_STORE;
+        ea.pos = 0;
+    }
+    epilogue_pair(ea, row, v0, v1, lmax, lidx);
+}
+
 template <int XM, int EPI, int FMT, int NVB>
 __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     constexpr int UB = q4m_unit_bytes(FMT);
-    constexpr int NB = gemvm_nbuf(FMT);  // ring slots per warp
+    constexpr int NB = multi_nbuf(FMT);  // ring slots per warp
     extern __shared__ __align__(16) uint8_t smem_m[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = p.groups, kw = p.kw, gk = p.gk, n = p.n;
@@ -337,17 +392,23 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     float* ep = reinterpret_cast<float*>(rec + multi_rec_bytes(n, gk));  // [MNW][MULTI_MAX][EP_STRIDE]
     float* fac = ep + MNW * MULTI_MAX * EP_STRIDE;                       // [MULTI_MAX] (64 floats)
     u64* keys = reinterpret_cast<u64*>(fac + 64);                        // [MNW][MULTI_MAX]
+    float* fin = reinterpret_cast<float*>(keys + MNW * MULTI_MAX);      // [MULTI_MAX][EP_STRIDE]
+    int* flag = reinterpret_cast<int*>(fin + MULTI_MAX * EP_STRIDE);
     const uint32_t ring = smem_u32(rec + multi_rec_bytes(n, gk) + MULTI_EP_BYTES) + (uint32_t)(warp * NB * UB);
     float* eps_w = ep + warp * MULTI_MAX * EP_STRIDE;
 
-    // ---------------- weight stream: pairs cidx + cg (warp + MNW i) of K part kp
-    const int wstep = cg * MNW;
-    int cq = cidx + cg * warp, cgl = 0;  // copy cursor
+    // ---------------- weight stream: per warp, pairs cidx + cg (warp + MNW i) of K part kp,
+    // groups [0, ng) of each; per CTA (local), pairs cidx + cg i, groups [lg0, lg1) of each
+    const bool local = p.local != 0;
+    const int lg0 = warp * ng / MNW, lg1 = (warp + 1) * ng / MNW;
+    const int wstep = local ? cg : cg * MNW;
+    const int cg0 = local ? lg0 : 0, cg1 = local ? lg1 : ng;
+    int cq = local ? cidx : cidx + cg * warp, cgl = cg0;  // copy cursor
     auto issue = [&](int slot) {
-        if (cq < p.pairs && ng > 0) {
+        if (cq < p.pairs && cg0 < cg1) {
             copy_unit_fmt<FMT>(ring + slot * UB, p.w + ((size_t)cq * G + g0 + cgl) * UB, lane);
-            if (++cgl == ng) {
-                cgl = 0;
+            if (++cgl == cg1) {
+                cgl = cg0;
                 cq += wstep;
             }
         }
@@ -402,7 +463,79 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         lidx[k] = 0;
     }
     int slot = 0;
-    for (int q = cidx + cg * warp; q < p.pairs && ng > 0; q += wstep) {
+    if (local) {
+        // ---------------- per CTA: all warps on one pair, each its groups [lg0, lg1)
+        for (int q = cidx; q < p.pairs; q += cg) {
+            float acc[NVB][4];
+#pragma unroll
+            for (int vb = 0; vb < NVB; ++vb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[vb][i] = 0.f;
+            for (int gl = lg0; gl < lg1; ++gl) {
+                issue(slot == 0 ? NB - 1 : slot - 1);
+                asm volatile("cp.async.wait_group %0;" ::"n"(NB - 1) : "memory");
+                __syncwarp();  // scale words are read across lanes
+                unit_multi<FMT, NVB>(ring + slot * UB, mr, gl, lane, acc);
+                __syncwarp();  // every lane's reads of the slot precede the next copy into it
+                slot = slot + 1 == NB ? 0 : slot + 1;
+            }
+#pragma unroll
+            for (int vb = 0; vb < NVB; ++vb) {
+                const int v = 4 * vb + c;
+                if (v < n)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) eps_w[v * EP_STRIDE + gr + 8 * i] = acc[vb][i];
+            }
+            __syncthreads();
+            // the warps' pieces in warp order (warps without groups wrote zeros)
+            if (tid < n * 32) {
+                const int v = tid >> 5, r = tid & 31;
+                float sum = 0.f;
+#pragma unroll
+                for (int w2 = 0; w2 < MNW; ++w2) sum += ep[(w2 * MULTI_MAX + v) * EP_STRIDE + r];
+                if (kw > 1) p.part[((size_t)q * kw + kp) * n * 32 + tid] = sum;
+                else fin[v * EP_STRIDE + r] = sum;
+            }
+            if (kw > 1) {
+                __threadfence();
+                __syncthreads();
+                if (tid == 0) {
+                    const unsigned old = atomicAdd(p.cnt + q, 1u);
+                    *flag = old == (unsigned)(kw - 1);
+                    if (*flag) p.cnt[q] = 0u;  // ready for the next launch
+                }
+                __syncthreads();
+                if (!*flag) continue;  // another K part finishes this pair
+                __threadfence();
+                if (tid < n * 32) {  // the parts in K order, eight loads in flight
+                    const float* pb = p.part + (size_t)q * kw * n * 32 + tid;
+                    const size_t kst = (size_t)n * 32;
+                    float sum = 0.f;
+                    for (int k0 = 0; k0 < kw; k0 += 8) {
+                        float t[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) t[i] = k0 + i < kw ? __ldcg(pb + (size_t)(k0 + i) * kst) : 0.f;
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) sum += t[i];
+                    }
+                    fin[(tid >> 5) * EP_STRIDE + (tid & 31)] = sum;
+                }
+            }
+            __syncthreads();
+            if (warp < (n + 1) / 2) {  // row pair qq of vector 2 warp + lane / 16
+                const int qq = lane & 15, v = 2 * warp + (lane >> 4);
+                const bool valid = v < n;
+                const float f = valid ? fac[v] : 0.f;
+                const float v0 = valid ? fin[v * EP_STRIDE + 2 * qq] * f : 0.f;
+                const float v1 = valid ? fin[v * EP_STRIDE + 2 * qq + 1] * f : 0.f;
+                float lm = -INFINITY;
+                int li = 0;
+                multi_epilogue<EPI>(p, q, qq, v, valid, v0, v1, lm, li);
+            }
+            __syncthreads();  // the staging blocks are rewritten by the next pair
+        }
+    }
+    for (int q = local ? p.pairs : cidx + cg * warp; q < p.pairs && ng > 0; q += wstep) {
         float acc[NVB][4];
 #pragma unroll
         for (int vb = 0; vb < NVB; ++vb)
@@ -455,7 +588,7 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         }
         // ---------------- epilogue: lane handles row pair (2 (lane & 15), +1) of vector
         // 2 k + lane / 16, k = 0 .. ceil(n / 2) - 1
-        const int qq = lane & 15, row = q * Q4M_PAIR_ROWS + 2 * qq;
+        const int qq = lane & 15;
 #pragma unroll
         for (int k = 0; k < 2 * NVB; ++k) {
             if (2 * k >= n) break;
@@ -464,41 +597,7 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
             const float f = valid ? fac[v] : 0.f;
             const float v0 = valid ? eps_w[v * EP_STRIDE + 2 * qq] * f : 0.f;
             const float v1 = valid ? eps_w[v * EP_STRIDE + 2 * qq + 1] * f : 0.f;
-            if (EPI == ME_RESID) {
-                float s2 = 0.f;
-                if (valid) {  // rows = the residual width (a multiple of 32): every row exists
-                    float* hy = p.y + (size_t)v * p.ldy + row;
-                    const float h0 = hy[0] + v0, h1 = hy[1] + v1;
-                    hy[0] = h0;
-                    hy[1] = h1;
-                    s2 = fmaf(h0, h0, h1 * h1);
-                }
-#pragma unroll
-                for (int o = 1; o < 16; o <<= 1) s2 += __shfl_xor_sync(JINF_FULL_MASK, s2, o);
-                if (valid && qq == 0) p.ssq_out[(size_t)q * n + v] = s2;
-                continue;
-            }
-            if (!valid) continue;
-            EpiArgs ea;
-            ea.rows = p.rows;
-            ea.y = p.y + (size_t)v * p.ldy;
-            ea.coherent = false;
-            if (EPI == ME_QKV) {
-                const size_t so = (size_t)p.ms->seq[v] * p.seq_stride;
-                ea.epi = EPI_QKV;
-                ea.kcache = p.kcache + so;
-                ea.vcache = p.vcache + so;
-                ea.nq = p.nq;
-                ea.nk = p.nk;
-                ea.head_dim = p.head_dim;
-                ea.max_ctx = p.max_ctx;
-                ea.pos = p.ms->pos[v];
-                ea.rope_base = p.rope_base;
-            } else {
-                ea.epi = EPI == ME_GATEUP ? EPI_GATEUP : EPI == ME_LMHEAD ? EPI_LMHEAD : EPI_STORE;
-                ea.pos = 0;
-            }
-            epilogue_pair(ea, row, v0, v1, lmax[k], lidx[k]);
+            multi_epilogue<EPI>(p, q, qq, v, valid, v0, v1, lmax[k], lidx[k]);
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -638,27 +737,46 @@ int device_sms() {
 
 int multi_grid(int num_sms) { return num_sms; }
 
-// The K split with the smallest estimated time: the busiest warp's units (ceil of its pairs
-// times the part's groups) plus a per-task cost of the partial rows and the final sums, among
-// the splits whose records fit in shared memory next to the weight ring.
-int multi_pick_kw(int pairs, int groups, int n, int fmt, int grid) {
-    if (pairs < 1 || groups < 1 || n < 1 || n > MULTI_MAX || grid < 1) return 0;
-    int best = 0;
-    double best_cost = 1e300;
+// Estimated time, in units of one unit's streaming time per warp (at full HBM rate a warp
+// streams one unit while the other 15 warps of its SM stream theirs; a dependent global round
+// trip costs about the same):
+//   per warp: the busiest warp's pairs x the part's groups, plus, with kw > 1, its partial rows,
+//     the arrival and the final sums (n loads per lane per part, eight in flight);
+//   per CTA: rounds of pairs x (the warp's share of the part's groups + the merge), plus, with
+//     kw > 1, the arrival and the final sums (one load per thread per part, eight in flight).
+void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int* kw_out, int* local_out) {
+    *kw_out = 0;
+    *local_out = 0;
+    if (pairs < 1 || groups < 1 || n < 1 || n > MULTI_MAX || grid < 1) return;
+    double best = 1e300;
     const int lim = groups < kMultiMaxKw ? groups : kMultiMaxKw;
     for (int kw = 1; kw <= lim; ++kw) {
         const int gk = (groups + kw - 1) / kw;
         if (multi_smem(n, gk, fmt) > 226 * 1024) continue;
         const int cg = grid / kw > 0 ? grid / kw : 1;  // CTAs of the least served part
         const long long warps = (long long)cg * MNW;
-        const double per_warp = (double)((pairs + warps - 1) / warps);
-        const double cost = per_warp * ((double)gk + (kw > 1 ? 0.5 + 0.03 * kw : 0.1));
-        if (cost < best_cost - 1e-9) {
-            best_cost = cost;
-            best = kw;
+        const double pw = (double)((pairs + warps - 1) / warps);
+        const double cost_w = pw * (gk + (kw > 1 ? 1.0 + n * ((kw + 7) / 8) : 0.0));
+        if (cost_w < best - 1e-9) {
+            best = cost_w;
+            *kw_out = kw;
+            *local_out = 0;
+        }
+        if (epi == ME_LMHEAD) continue;
+        const double rounds = (double)((pairs + cg - 1) / cg);
+        const double cost_l = rounds * ((gk + MNW - 1) / MNW + 0.5) + (kw > 1 ? 1.0 + (kw + 7) / 8 : 0.0);
+        if (cost_l < best - 1e-9) {
+            best = cost_l;
+            *kw_out = kw;
+            *local_out = 1;
         }
     }
-    return best;
+}
+
+int multi_pick_kw(int pairs, int groups, int n, int fmt, int grid) {
+    int kw, local;
+    multi_plan(pairs, groups, n, fmt, grid, ME_STORE, &kw, &local);
+    return kw;
 }
 
 size_t multi_workspace_bytes(int pairs, int kw, int n) {
@@ -674,6 +792,7 @@ cudaError_t multi_gemv_launch(const MultiParams& p, int xm, int epi, int grid, c
     if (xm == MX_NORMED && (!p.norm_w || !p.ssq || p.ssq_parts < 1)) return cudaErrorInvalidValue;
     if (epi == ME_RESID && (!p.ssq_out || p.rows % 32)) return cudaErrorInvalidValue;
     if ((epi == ME_QKV || epi == ME_LMHEAD) && !p.ms) return cudaErrorInvalidValue;
+    if (p.local && epi == ME_LMHEAD) return cudaErrorInvalidValue;
     if (epi == ME_QKV && (!p.kcache || !p.vcache)) return cudaErrorInvalidValue;
     switch (p.fmt) {
         case Q4M_Q4_0: return launch_multi_f<Q4M_Q4_0>(p, xm, epi, grid, s, pdl);
@@ -729,7 +848,13 @@ extern "C" jinf_status jinf_b200_gemv_q4m_batch_qt(const void* q4m, int qtype, c
         return JINF_ERR_INVALID;
     if (x_type != JINF_TYPE_F32 && x_type != JINF_TYPE_F16) return JINF_ERR_INVALID;
     const int grid = multi_grid(device_sms());
-    if (kw <= 0) kw = multi_pick_kw(sh.pairs, sh.groups, batch, fmt, grid);
+    int local = 0;
+    if (kw == 0) {
+        multi_plan(sh.pairs, sh.groups, batch, fmt, grid, ME_STORE, &kw, &local);
+    } else if (kw < 0) {  // a forced split with the per-CTA sharing
+        kw = -kw;
+        local = 1;
+    }
     if (kw < 1 || kw > sh.groups || kw > kMultiMaxKw || multi_smem(batch, (sh.groups + kw - 1) / kw, fmt) > 226 * 1024)
         return JINF_ERR_INVALID;
     if (kw > 1 && !workspace) return JINF_ERR_INVALID;
@@ -743,6 +868,7 @@ extern "C" jinf_status jinf_b200_gemv_q4m_batch_qt(const void* q4m, int qtype, c
     p.n = batch;
     p.kw = kw;
     p.gk = (sh.groups + kw - 1) / kw;
+    p.local = local;
     p.x = x;
     p.ldx = cols;
     p.y = y;

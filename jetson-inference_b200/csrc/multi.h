@@ -45,6 +45,7 @@ struct MultiParams {
     int rows, cols, pairs, groups, fmt;
     int n;             // vectors (1..MULTI_MAX)
     int kw, gk;        // K parts per tile pair; groups per part (the largest)
+    int local;         // 1: a CTA's 16 warps split each of its tile pairs (not with ME_LMHEAD)
     const void* x;     // [n][ldx]
     int ldx;
     const float* norm_w;  // MX_NORMED: gain [cols]
@@ -67,9 +68,10 @@ struct MultiParams {
     uint64_t pf_bytes;
 };
 
-// K parts for an n-vector GEMV of this shape on `grid` CTAs: enough (pair, part) tasks for
-// every warp, the part's records within shared memory next to the weight ring; 0 when no
-// split fits.
+// How an n-vector GEMV of this shape runs on `grid` CTAs: the K parts (the part's records
+// within shared memory next to the weight rings) and whether a CTA's warps split each tile
+// pair (*local), by the smallest estimated time; kw 0 when no split fits.
+void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int* kw, int* local);
 int multi_pick_kw(int pairs, int groups, int n, int fmt, int grid);
 int multi_grid(int num_sms);
 size_t multi_workspace_bytes(int pairs, int kw, int n);

@@ -316,11 +316,12 @@ def test_gemv_batch_every_format(cuda, qt, rows, cols, batch):
 
 
 @pytest.mark.parametrize("qt", [2, 12, 14, 8])
-@pytest.mark.parametrize("kw", [1, 2, 5, 16])
+@pytest.mark.parametrize("kw", [1, 2, 5, 16, -1, -2, -3, -16])
 def test_gemv_batch_every_k_split(cuda, qt, kw):
     """Every forced K split gives the same vectors (to the oracle bar) and matches kw = 1 to
-    fp32 summation order. (2048 columns: at 8 vectors the records of all 16 groups fit in
-    shared memory, so kw = 1 is a valid split for every format.)"""
+    fp32 summation order; kw < 0: -kw parts with a CTA's warps splitting each tile pair.
+    (2048 columns: at 8 vectors the records of all 16 groups fit in shared memory, so one
+    part is a valid split for every format.)"""
     from jinf import kernels as K
     rows, cols, batch = 1024, 2048, 8
     w = _typed_rows(qt, rows, cols, seed=7 * kw + qt)
