@@ -28,7 +28,7 @@ namespace jinf {
 constexpr int AW = 4;      // warps per CTA
 constexpr int AMAXG = 8;   // max query heads per kv head
 constexpr int TP = 32;     // positions per warp tile
-constexpr int ATT_SPAN = 256;  // fewest positions per split (more splits only for more positions)
+constexpr int ATT_SPAN = 64;  // fewest positions per split (more splits only for more positions)
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -84,7 +84,22 @@ __global__ void __launch_bounds__(AW * 32) k_attn_f16(const AttnParams p) {
         n = p.st->pos + 1;
     }
     const float scale = rsqrtf((float)HD);
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) sm.q[i] = qv[(size_t)kvh * G * HD + i] * scale;
+    {  // the kv head's query rows, float4 loads all in flight (G * HD / 4 <= 2 x 128 of them)
+        const float4* q4 = reinterpret_cast<const float4*>(qv + (size_t)kvh * G * HD);
+        float4 t[AMAXG * HD / 4 / (AW * 32)];
+#pragma unroll
+        for (int k = 0; k < AMAXG * HD / 4 / (AW * 32); ++k) {
+            const int i = threadIdx.x + k * AW * 32;
+            if (i < G * HD / 4) t[k] = q4[i];
+        }
+#pragma unroll
+        for (int k = 0; k < AMAXG * HD / 4 / (AW * 32); ++k) {
+            const int i = threadIdx.x + k * AW * 32;
+            if (i < G * HD / 4)
+                reinterpret_cast<float4*>(sm.q)[i] = make_float4(t[k].x * scale, t[k].y * scale, t[k].z * scale,
+                                                                 t[k].w * scale);
+        }
+    }
     __syncthreads();
 
     const int ns = min(p.n_split, max(1, (n + ATT_SPAN - 1) / ATT_SPAN));  // splits with positions

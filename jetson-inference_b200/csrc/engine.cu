@@ -463,6 +463,7 @@ struct jinf_engine_impl {
     float *m_h = nullptr, *m_y = nullptr, *m_q = nullptr, *m_attn = nullptr, *m_act = nullptr, *m_logits = nullptr,
           *m_ssq = nullptr, *m_attn_part = nullptr, *m_part = nullptr;
     unsigned int* m_cnt = nullptr;
+    size_t m_part_floats = 0, m_cnt_n = 0;  // their sizes
     int32_t* m_out = nullptr;  // [max_ctx][MULTI_MAX] argmax ids of resident multi steps
     int m_split = 1;  // attention splits of a multi step
     std::vector<Op> m_ops[MULTI_MAX + 1];
@@ -772,6 +773,8 @@ Op multi_gemv_op(jinf_engine_impl* I, int n, const uint8_t* w, const Q4MShape& s
     p.gk = p.kw > 0 ? (sh.groups + p.kw - 1) / p.kw : 0;
     p.part = I->m_part;
     p.cnt = I->m_cnt;
+    p.part_floats = I->m_part_floats;
+    p.cnt_n = I->m_cnt_n;
     p.ms = I->ms;
     p.eps = I->eps;
     p.ssq = I->m_ssq;
@@ -1622,8 +1625,8 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
     }
     I->seq_stride = kv_elems;
     I->seq_past.assign(I->n_seqs, 0);
-    // attention splits (the kernel uses one per 256 positions at run time, up to this many)
-    I->n_split = std::max(1, std::min(64, (I->max_ctx + 255) / 256));
+    // attention splits (the kernel uses one per 64 positions at run time, up to this many)
+    I->n_split = std::max(1, std::min(64, (I->max_ctx + 63) / 64));
     bool ok = cudaMalloc(&I->norms, sizeof(float) * (size_t)(2 * I->L + 1) * d) == cudaSuccess &&
               cudaMalloc(&I->embed, sizeof(float) * (size_t)I->V * d) == cudaSuccess &&
               cudaMalloc(&I->kc, sizeof(__half) * kv_elems * I->n_seqs) == cudaSuccess &&
@@ -1843,20 +1846,22 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         const int grid = multi_grid(I->num_sms);
         size_t ws = 0, pairs = 0;
         for (int n = 1; n <= S; ++n) {
-            auto need = [&](const Q4MShape& sh) {
+            auto need = [&](const Q4MShape& sh, int epi) {  // the plan the step's op will make
                 if (!sh.rows) return;
                 int kw = 0, local = 0;
-                multi_plan(sh.pairs, sh.groups, n, sh.fmt, grid, ME_STORE, &kw, &local);
+                multi_plan(sh.pairs, sh.groups, n, sh.fmt, grid, epi, &kw, &local);
                 ws = std::max(ws, (size_t)sh.pairs * std::max(kw, 1) * n * 32);
                 pairs = std::max(pairs, (size_t)sh.pairs);
             };
-            need(I->lm_sh);
+            need(I->lm_sh, ME_LMHEAD);
             for (const auto& ly : I->layers)
-                for (const Q4MShape* sh : {&ly.qkv_sh, &ly.v_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) need(*sh);
+                for (const Q4MShape* sh : {&ly.qkv_sh, &ly.v_sh, &ly.o_sh, &ly.gu_sh, &ly.down_sh}) need(*sh, ME_STORE);
         }
-        // attention splits: one per 256 positions at run time, up to this many
+        // attention splits: one per 64 positions at run time, up to this many
         I->m_split = I->n_split;
         const size_t attn_part = attn_partial_floats(I->Hkvl, I->m_split, hd) * S;
+        I->m_part_floats = std::max(ws, (size_t)1);
+        I->m_cnt_n = std::max(pairs, (size_t)1);
         bool mok = cudaMalloc(&I->ms, sizeof(MultiState)) == cudaSuccess &&
                    cudaHostAlloc(&I->ms_pinned, sizeof(int32_t) * 4 * MULTI_MAX, cudaHostAllocDefault) == cudaSuccess &&
                    cudaMalloc(&I->m_h, sizeof(float) * (size_t)S * d) == cudaSuccess &&

@@ -436,19 +436,40 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         float f = 1.0f;
         if (XM == MX_NORMED && warp < n) {
             float ss = 0.f;
-            for (int q = lane; q < p.ssq_parts; q += 32) ss += p.ssq[(size_t)q * n + warp];
+            for (int q0 = lane; q0 < p.ssq_parts; q0 += 8 * 32) {  // eight loads in flight
+                float t[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int q = q0 + 32 * i;
+                    t[i] = q < p.ssq_parts ? p.ssq[(size_t)q * n + warp] : 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) ss += t[i];
+            }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(JINF_FULL_MASK, ss, o);
             f = rsqrtf(ss / (float)p.cols + p.eps);
         }
         if (lane == 0) fac[warp] = f;
     }
-    const int n4 = p.cols / 4;
-    for (int it = warp; it < n * ng; it += MNW) {
-        const int v = it / ng, gl = it % ng;
-        const float4 x4 = multi_load<XM>(p, v, (g0 + gl) * 32 + lane, n4);
-        octet_to_records(x4, lane, lane >> 3, dig + (v * multi_dig_stride(gk) + gl * 256) / 4,
-                         prm + (v * multi_prm_stride(gk) + gl * 64) / 16);
+    // a warp issues the loads of up to 8 of its items before converting any, so it pays one
+    // L2 round trip per 8 items, not one per item
+    const int n4 = p.cols / 4, items = n * ng;
+    for (int base = warp; base < items; base += 8 * MNW) {
+        float4 x4[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const int it = base + b * MNW;
+            if (it < items) x4[b] = multi_load<XM>(p, it / ng, (g0 + it % ng) * 32 + lane, n4);
+        }
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            const int it = base + b * MNW;  // warp-uniform: the conversion's shuffles see every lane
+            if (it >= items) break;
+            const int v = it / ng, gl = it % ng;
+            octet_to_records(x4[b], lane, lane >> 3, dig + (v * multi_dig_stride(gk) + gl * 256) / 4,
+                             prm + (v * multi_prm_stride(gk) + gl * 64) / 16);
+        }
     }
     __syncthreads();
     const MultiRec mr{smem_u32(dig), smem_u32(prm), multi_dig_stride(gk), multi_prm_stride(gk), n};
@@ -787,7 +808,9 @@ cudaError_t multi_gemv_launch(const MultiParams& p, int xm, int epi, int grid, c
     if (!p.w || !p.x || !p.y || p.n < 1 || p.n > MULTI_MAX || p.kw < 1 || p.kw > p.groups || grid < p.kw)
         return cudaErrorInvalidValue;
     if (p.gk != (p.groups + p.kw - 1) / p.kw || multi_smem(p.n, p.gk, p.fmt) > 226 * 1024) return cudaErrorInvalidValue;
-    if (p.kw > 1 && (!p.part || !p.cnt)) return cudaErrorInvalidValue;
+    if (p.kw > 1 && (!p.part || !p.cnt || (size_t)p.pairs * p.kw * p.n * 32 > p.part_floats ||
+                     (size_t)p.pairs > p.cnt_n))
+        return cudaErrorInvalidValue;
     if (p.cols % 4 || p.ldx < p.cols) return cudaErrorInvalidValue;
     if (xm == MX_NORMED && (!p.norm_w || !p.ssq || p.ssq_parts < 1)) return cudaErrorInvalidValue;
     if (epi == ME_RESID && (!p.ssq_out || p.rows % 32)) return cudaErrorInvalidValue;
@@ -876,6 +899,8 @@ extern "C" jinf_status jinf_b200_gemv_q4m_batch_qt(const void* q4m, int qtype, c
     if (kw > 1) {
         p.part = (float*)workspace;
         p.cnt = (unsigned int*)((uint8_t*)workspace + (size_t)sh.pairs * kMultiMaxKw * batch * 32 * sizeof(float));
+        p.part_floats = (size_t)sh.pairs * kMultiMaxKw * batch * 32;
+        p.cnt_n = (size_t)sh.pairs;
     }
     const cudaError_t e =
         multi_gemv_launch(p, x_type == JINF_TYPE_F16 ? MX_PLAIN_F16 : MX_PLAIN_F32, ME_STORE, grid, stream, false);

@@ -64,6 +64,7 @@ struct MultiParams {
     MultiState* ms;    // ME_QKV (positions, sequences), ME_LMHEAD (argmax keys)
     float* part;       // kw > 1: [pairs][kw][n][32] partial rows
     unsigned int* cnt;  // kw > 1: [pairs] arrival counters, zero before the first launch (self-resetting)
+    size_t part_floats, cnt_n;  // their sizes (checked at launch)
     const uint8_t* pf_ptr;  // L2 prefetch of the next kernel's weights
     uint64_t pf_bytes;
 };

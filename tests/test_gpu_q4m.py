@@ -324,9 +324,9 @@ def test_gemv_batch_every_k_split(cuda, qt, kw):
     part is a valid split for every format.)"""
     from jinf import kernels as K
     rows, cols, batch = 1024, 2048, 8
-    w = _typed_rows(qt, rows, cols, seed=7 * kw + qt)
+    w = _typed_rows(qt, rows, cols, seed=7 * abs(kw) + qt)
     q = packed_qt(w, qt, rows, cols, cuda) if qt != 12 else packed_k(w, rows, cols, cuda)
-    x = np.random.default_rng(kw).standard_normal((batch, cols)).astype(np.float32)
+    x = np.random.default_rng(abs(kw)).standard_normal((batch, cols)).astype(np.float32)
     xd = torch.from_numpy(x).to(cuda)
     ws = torch.zeros(K.gemv_q4m_batch_workspace_bytes_qt(rows, cols, batch, qt), dtype=torch.uint8, device=cuda)
     y = torch.empty((batch, rows), dtype=torch.float32, device=cuda)
