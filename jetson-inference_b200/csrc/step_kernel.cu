@@ -436,7 +436,13 @@ __device__ __noinline__ float stage_records(const uint8_t* rec, const float* ssp
     }
     float s = 0.f;
     if (ssp)
-        for (int i = lane; i < n_ss; i += 32) s += __ldcg(ssp + i);
+        for (int i0 = lane; i0 < n_ss; i0 += 8 * 32) {  // eight loads in flight per lane
+            float t[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) t[k] = i0 + 32 * k < n_ss ? __ldcg(ssp + i0 + 32 * k) : 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s += t[k];
+        }
     float fac = 1.0f;
     if (ssp) {
 #pragma unroll
