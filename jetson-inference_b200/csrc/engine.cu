@@ -327,7 +327,7 @@ __global__ void k_gather_blocks(const uint8_t* __restrict__ src, uint8_t* __rest
 enum OpKind { OP_GEMV = 0, OP_ATTN = 1, OP_ALLREDUCE_F32 = 2, OP_ALLREDUCE_MAXU64 = 3, OP_FINALIZE = 4,
               OP_SPARSE_FFN = 5,
               // multi-sequence step (multi.h)
-              OP_MGEMV = 6, OP_MEMBED = 7, OP_MRESID = 8, OP_MFINAL = 9 };
+              OP_MGEMV = 6, OP_MEMBED = 7, OP_MRESID = 8, OP_MFINAL = 9, OP_MATTN = 10 };
 enum GemvRole { ROLE_QKV = 0, ROLE_O = 1, ROLE_GATEUP = 2, ROLE_DOWN = 3, ROLE_LM = 4, ROLE_NONE = 5 };
 
 struct Op {
@@ -342,6 +342,7 @@ struct Op {
     int with_argmax = 0;
     uint64_t bytes = 0;  // algorithmic bytes of the op (weights + vectors)
     MultiParams mp{};    // OP_MGEMV (xm, epi, grid as above)
+    MultiAttnParams map{};  // OP_MATTN
     int n_vec = 0;       // multi-sequence ops: vectors of the step
 };
 
@@ -488,6 +489,7 @@ jinf_status run_op(jinf_engine_impl* I, const Op& op, cudaStream_t s) {
         case OP_MEMBED: e = multi_embed_launch(I->embed, I->ms, op.n_vec, I->d, I->m_h, I->m_ssq, s, true); break;
         case OP_MRESID: e = multi_resid_launch(I->m_h, I->m_y, op.n_vec, I->d, I->m_ssq, s, true); break;
         case OP_MFINAL: e = multi_finalize_launch(I->ms, op.n_vec, s); break;
+        case OP_MATTN: e = multi_attn_launch(op.map, s, true); break;
         case OP_SPARSE_FFN: {
             // h = h + y_o; x = RMSNorm(h) * ffn_norm; [predictor]; y_down = FFN over the active
             // neurons (the next layer's QKV prologue adds y_down to h)
@@ -852,24 +854,23 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
             v.bytes = (uint64_t)ly.v_sh.rows * aos_row_bytes(ly.v_sh.fmt, ly.v_sh.cols);
             ops.push_back(v);
         }
-        Op at{OP_ATTN};
+        Op at{OP_MATTN};
         at.layer = L;
         at.n_vec = n;
-        at.ap.q = I->m_q;
-        at.ap.kcache = kc;
-        at.ap.vcache = vc;
-        at.ap.out = I->m_attn;
-        at.ap.partial = I->m_attn_part;
-        at.ap.n_heads = I->Hl;
-        at.ap.n_kv_heads = I->Hkvl;
-        at.ap.head_dim = I->hd;
-        at.ap.max_ctx = I->max_ctx;
-        at.ap.n_split = I->m_split;
-        at.ap.st = I->st;
-        at.ap.ms = I->ms;
-        at.ap.n_vec = n;
-        at.ap.seq_stride = I->seq_stride;
-        at.ap.q_stride = nq;
+        at.map.q = I->m_q;
+        at.map.q_stride = nq;
+        at.map.kcache = kc;
+        at.map.vcache = vc;
+        at.map.seq_stride = I->seq_stride;
+        at.map.out = I->m_attn;
+        at.map.part = I->m_attn_part;
+        at.map.n = n;
+        at.map.n_heads = I->Hl;
+        at.map.n_kv_heads = I->Hkvl;
+        at.map.head_dim = I->hd;
+        at.map.max_ctx = I->max_ctx;
+        at.map.s_max = I->m_split;
+        at.map.ms = I->ms;
         ops.push_back(at);
 
         Op o = multi_gemv_op(I, n, ly.o, ly.o_sh, MX_PLAIN_F32, ME_RESID);
@@ -1859,7 +1860,7 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         }
         // attention splits: one per 64 positions at run time, up to this many
         I->m_split = I->n_split;
-        const size_t attn_part = attn_partial_floats(I->Hkvl, I->m_split, hd) * S;
+        const size_t attn_part = multi_attn_part_floats(S, I->Hkvl, I->m_split, hd);
         I->m_part_floats = std::max(ws, (size_t)1);
         I->m_cnt_n = std::max(pairs, (size_t)1);
         bool mok = cudaMalloc(&I->ms, sizeof(MultiState)) == cudaSuccess &&

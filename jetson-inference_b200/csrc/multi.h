@@ -78,6 +78,27 @@ int multi_grid(int num_sms);
 size_t multi_workspace_bytes(int pairs, int kw, int n);
 cudaError_t multi_gemv_launch(const MultiParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
 
+// Decode attention of a multi-sequence step (step_kernel.cu: the persistent step's attention
+// split, one kernel per layer): vector v's query heads over positions 0 .. ms->pos[v] of
+// sequence ms->seq[v]'s cache, the positions of each (vector, kv head) split over up to s_max
+// CTAs of 16 warps (one per MULTI_ATTN_SPAN positions), the splits merged in order by the
+// last CTA to finish.
+constexpr int MULTI_ATTN_SPAN = 64;
+struct MultiAttnParams {
+    const float* q;         // [n][q_stride], RoPE applied
+    int q_stride;
+    const __half* kcache;   // this layer's cache of sequence 0: [n_kv_heads][max_ctx][head_dim]
+    const __half* vcache;
+    size_t seq_stride;      // elements from one sequence's cache to the next
+    float* out;             // [n][q_stride]
+    float* part;            // multi_attn_part_floats floats of scratch
+    int n, n_heads, n_kv_heads, head_dim, max_ctx, s_max;
+    MultiState* ms;
+};
+size_t multi_attn_part_floats(int n, int n_kv_heads, int s_max, int head_dim);
+size_t multi_attn_smem_bytes(int group, int head_dim);
+cudaError_t multi_attn_launch(const MultiAttnParams& p, cudaStream_t s, bool pdl);
+
 // h[v] = table[token_v] and its sums of squares per 32 elements (ssq [d / 32][n]).
 cudaError_t multi_embed_launch(const float* table, const MultiState* ms, int n, int d, float* h, float* ssq,
                                cudaStream_t s, bool pdl);

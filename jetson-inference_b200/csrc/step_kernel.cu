@@ -34,6 +34,7 @@
 // the next RMSNorm input adds all ranks' rows in rank order (stage_x_tp); the last CTA
 // exchanges the argmax keys.
 #include "common.cuh"
+#include "multi.h"
 #include "q4m_device.cuh"
 #include "step.h"
 
@@ -1212,6 +1213,143 @@ extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
     return cudaMemcpyFromSymbol(host, g_step_trace, n * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
 }
 #endif
+
+// ---------------------------------------------------------------- multi-sequence attention
+
+namespace {
+
+template <int HD, int GQ>
+__global__ void __launch_bounds__(STEP_THREADS) k_attn_multi(const MultiAttnParams p) {
+    extern __shared__ __align__(16) uint8_t smem_a[];
+    __shared__ int is_last;
+    const int tid = threadIdx.x;
+    const int v = blockIdx.y, kvh = blockIdx.x / p.s_max, sp = blockIdx.x % p.s_max;
+    pdl_wait();
+    pdl_trigger();
+    const int n_pos = p.ms->pos[v] + 1;
+    const int S = min(p.s_max, max(1, (n_pos + MULTI_ATTN_SPAN - 1) / MULTI_ATTN_SPAN));  // splits with positions
+    const size_t pst = (size_t)GQ * (HD + 2);
+    float* pbase = p.part + ((size_t)v * p.n_kv_heads + kvh) * p.s_max * pst;
+    if (sp < S) {
+        const int per = (n_pos + S - 1) / S;
+        const int p0 = min(n_pos, sp * per), p1 = min(n_pos, p0 + per);
+        const size_t so = (size_t)p.ms->seq[v] * p.seq_stride + (size_t)kvh * p.max_ctx * HD;
+        attn_split<HD, GQ>(p.q + (size_t)v * p.q_stride + (size_t)kvh * GQ * HD, p.kcache + so, p.vcache + so, p0, p1,
+                           smem_a, pbase + (size_t)sp * pst, nullptr);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(&p.ms->attn_count[v * MULTI_MAX_KV_HEADS + kvh], 1u);
+        is_last = prev == (unsigned)(p.s_max - 1);
+        if (is_last) p.ms->attn_count[v * MULTI_MAX_KV_HEADS + kvh] = 0u;  // ready for the next launch
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // merge the S splits in order: every split's (m, l) of every head in one pass of loads, the
+    // weights f_s = exp(m_s - M) and L = sum f_s l_s, then the outputs, eight splits' loads in
+    // flight per thread
+    float* fw = reinterpret_cast<float*>(smem_a);  // [GQ][S] m_s, then the weights
+    float* fl = fw + GQ * S;                        // [GQ][S] l_s
+    float* ls = fl + GQ * S;                        // [GQ] L
+    for (int i = tid; i < GQ * S; i += STEP_THREADS) {
+        const int g = i / S, s2 = i % S;
+        fw[i] = __ldcg(pbase + (size_t)s2 * pst + g * (HD + 2) + HD);
+        fl[i] = __ldcg(pbase + (size_t)s2 * pst + g * (HD + 2) + HD + 1);
+    }
+    __syncthreads();
+    if (tid < GQ) {
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, fw[tid * S + s2]);
+        float L = 0.f;
+        for (int s2 = 0; s2 < S; ++s2) {
+            const float ms = fw[tid * S + s2];
+            const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+            fw[tid * S + s2] = f;
+            L = fmaf(fl[tid * S + s2], f, L);
+        }
+        ls[tid] = L;
+    }
+    __syncthreads();
+    for (int o = tid; o < GQ * HD / 2; o += STEP_THREADS) {
+        const int g = o / (HD / 2), d2 = o % (HD / 2);
+        float2 a = make_float2(0.f, 0.f);
+        for (int s0 = 0; s0 < S; s0 += 8) {
+            float2 t[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                t[k] = s0 + k < S ? __ldcg(reinterpret_cast<const float2*>(pbase + (size_t)(s0 + k) * pst + g * (HD + 2)) + d2)
+                                  : make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float f = s0 + k < S ? fw[g * S + s0 + k] : 0.f;
+                a.x = fmaf(t[k].x, f, a.x);
+                a.y = fmaf(t[k].y, f, a.y);
+            }
+        }
+        const float L = ls[g];
+        *reinterpret_cast<float2*>(p.out + (size_t)v * p.q_stride + (size_t)(kvh * GQ + g) * HD + 2 * d2) =
+            make_float2(a.x / L, a.y / L);
+    }
+}
+
+template <int HD, int GQ>
+cudaError_t launch_attn_multi(const MultiAttnParams& p, cudaStream_t s, bool pdl) {
+    const size_t smem = multi_attn_smem_bytes(GQ, HD);
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(k_attn_multi<HD, GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.n_kv_heads * p.s_max), (unsigned)p.n);
+    cfg.blockDim = dim3(STEP_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_attn_multi<HD, GQ>, p);
+}
+
+}  // namespace
+
+size_t multi_attn_part_floats(int n, int n_kv_heads, int s_max, int head_dim) {
+    return (size_t)n * n_kv_heads * s_max * ATTN_MAX_GROUP * (head_dim + 2);
+}
+
+// the attention split's scratch, or the merge's (2 x group x s_max + group floats), whichever
+// is larger (s_max <= 64)
+size_t multi_attn_smem_bytes(int group, int head_dim) {
+    const size_t attn = sizeof(float) * ((size_t)group * NW * ATTN_PW + 4 * ATTN_MAX_GROUP + (size_t)NW * group * head_dim);
+    const size_t merge = sizeof(float) * ((size_t)2 * group * 64 + group);
+    return ((attn > merge ? attn : merge) + 15) & ~(size_t)15;
+}
+
+cudaError_t multi_attn_launch(const MultiAttnParams& p, cudaStream_t s, bool pdl) {
+    if (!p.q || !p.kcache || !p.vcache || !p.out || !p.part || !p.ms || p.n < 1 || p.n > MULTI_MAX ||
+        p.n_kv_heads < 1 || p.n_kv_heads > MULTI_MAX_KV_HEADS || p.n_heads % p.n_kv_heads || p.s_max < 1 ||
+        p.s_max > 64)
+        return cudaErrorInvalidValue;
+    const int gq = p.n_heads / p.n_kv_heads;
+    if (p.head_dim == 64) {
+        if (gq == 8) return launch_attn_multi<64, 8>(p, s, pdl);
+        if (gq == 4) return launch_attn_multi<64, 4>(p, s, pdl);
+        if (gq == 2) return launch_attn_multi<64, 2>(p, s, pdl);
+        if (gq == 1) return launch_attn_multi<64, 1>(p, s, pdl);
+    } else if (p.head_dim == 128) {
+        if (gq == 8) return launch_attn_multi<128, 8>(p, s, pdl);
+        if (gq == 4) return launch_attn_multi<128, 4>(p, s, pdl);
+        if (gq == 2) return launch_attn_multi<128, 2>(p, s, pdl);
+        if (gq == 1) return launch_attn_multi<128, 1>(p, s, pdl);
+    }
+    return cudaErrorInvalidValue;
+}
 
 cudaError_t step_launch(const StepParams& p, int grid, cudaStream_t s) {
     const size_t smem = step_smem_bytes(p.xstage_bytes, p.n_phases, p.fmt, p.nbuf);
