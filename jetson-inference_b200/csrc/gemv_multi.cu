@@ -6,20 +6,23 @@
 // its arithmetic is cuda/matmul_kernels.cu:8-43 (Q4_0) and :104-185 (Q4_K, Q6_K, Q8_0).
 //
 // Arithmetic. One mma.m16n8k16 (f16 x f16 -> f32) multiplies 16 rows by 16 columns of all 8
-// vectors at once: the vectors are the MMA's 8 columns, so the fp32 accumulator runs over the
-// whole K range and no per-block work follows the MMAs.
+// vectors at once: the vectors are the MMA's 8 columns.
 //   A (weights): each lane turns the 4-bit (6-, 8-bit) codes of its unit words straight into
-//     fp16 fragments: the byte code q becomes the fp16 1024 + q (0x64 as the high byte), minus
-//     the format's offset (exact), times the row's block scale (one rounding), or for Q4_K
-//     q * (d sc) - dmin m. A unit word holds columns 4c .. 4c + 3 of rows gr or gr + 8 (low
-//     nibbles: tile A, high: tile B); the MMA's logical columns (2c, 2c+1 | 2c+8, 2c+9) are
-//     mapped to them, and the B fragments follow the same map.
-//   B (inputs): the K part's columns of every vector as fp16 in shared memory, each vector
-//     scaled by a power of two that puts its largest magnitude in [2^13, 2^14) (undone
-//     exactly on the outputs), so fp16 keeps 11 significant bits whatever the range; lane
-//     (gr, c) reads columns 4c .. 4c + 3 of vector gr as one 8-byte load.
-// The weights enter the tensor cores rounded once to fp16 (relative 2^-11), the inputs with
-// 11 bits relative to their maximum; sums in fp32.
+//     fp16 fragments of the exact integer weights: the byte code q becomes the fp16 1024 + q
+//     (0x64 as the high byte) minus the format's offset, with no rounding. A unit word holds
+//     columns 4c .. 4c + 3 of rows gr or gr + 8 (low nibbles: tile A, high: tile B); the MMA's
+//     logical columns (2c, 2c+1 | 2c+8, 2c+9) are mapped to them, and the B fragments follow
+//     the same map.
+//   B (inputs): the K part's columns of every vector in shared memory as two fp16 terms,
+//     hi = fp16(x s) and lo = fp16(x s - hi) (about 22 significant bits together), each vector
+//     scaled by a power of two s that puts its largest magnitude in [2^13, 2^14) (undone
+//     exactly on the outputs); lane (gr, c) reads hi and lo of columns 4c .. 4c + 3 of
+//     vector gr as one 16-byte load, and the MMA runs once per term.
+//   The block's scale (per row, per 32 columns; Q6_K: per 16) multiplies its fp32 sums
+//     after its MMAs, as the reference applies d to each block's sum
+//     (cuda/matmul_kernels.cu:8-43); Q4_K subtracts dmin m times the block's input sum.
+// So the weights are exact, the inputs carry ~22 bits relative to their maximum, and every
+// sum is fp32.
 //
 // Scheduling. CTA c works on K part kp = c % kw only, so it stages just that part's inputs
 // (n vectors x gk groups) in shared memory. Two ways to share out a part's work:
@@ -59,10 +62,14 @@ constexpr int EP_STRIDE = 33;         // floats per staged row block (32 rows, p
 // room for the inputs (the larger Q6_K and Q8_0 units: 1 in flight).
 __host__ __device__ constexpr inline int multi_nbuf(int fmt) { return fmt == Q4M_Q6_K || fmt == Q4M_Q8_0 ? 2 : 3; }
 
-// Staged inputs: fp16 [n][gk * 128 + 16] (each vector's row padded by 32 bytes, so that the 8
-// rows of one fragment load fall in different shared-memory banks).
-__host__ __device__ inline int multi_xs_stride(int gk) { return gk * 256 + 32; }  // bytes per vector
-__host__ __device__ inline size_t multi_xs_bytes(int n, int gk) { return (size_t)n * multi_xs_stride(gk); }
+// Staged inputs: per vector a row of 16-byte records, one per 4 columns (hi of the 4, then lo),
+// padded by 64 bytes so that the two rows one quarter-warp load reads fall in different
+// banks; then the inputs' sums per 32-column block [gk * 4][MULTI_MAX] floats (Q4_K's min
+// term).
+__host__ __device__ inline int multi_xs_stride(int gk) { return gk * 512 + 64; }  // bytes per vector
+__host__ __device__ inline size_t multi_xs_bytes(int n, int gk) {
+    return (size_t)n * multi_xs_stride(gk) + (size_t)gk * 4 * MULTI_MAX * 4;
+}
 // epilogue staging [MNW][MULTI_MAX][EP_STRIDE] floats, 64 floats of per-vector factors (norm,
 // input scale, maximum), the argmax keys [MNW][MULTI_MAX], the merged rows
 // [MULTI_MAX][EP_STRIDE] (per-CTA split) and a flag
@@ -90,45 +97,49 @@ __device__ __forceinline__ uint32_t as_u(__half2 h) { return *reinterpret_cast<u
 // bytes 0, 1 (lo) or 2, 3 (hi) of a word of 8-bit codes as the fp16 pair (1024 + b, 1024 + b')
 __device__ __forceinline__ __half2 codes_lo(uint32_t t) { return as_h2(__byte_perm(t, 0x64646464u, 0x4140)); }
 __device__ __forceinline__ __half2 codes_hi(uint32_t t) { return as_h2(__byte_perm(t, 0x64646464u, 0x4342)); }
-// the low / high half of a word, in both halves
-__device__ __forceinline__ __half2 splat_lo(uint32_t u) { return as_h2(__byte_perm(u, 0u, 0x1010)); }
-__device__ __forceinline__ __half2 splat_hi(uint32_t u) { return as_h2(__byte_perm(u, 0u, 0x3232)); }
 
-// The A fragment of one 16-column step from the step's two code words (row gr: t0, row gr+8:
-// t1; bytes = codes of columns 4c .. 4c+3): (code - off) * scale, per row.
-__device__ __forceinline__ void frag_scaled(uint32_t t0, uint32_t t1, __half2 off, __half2 s0, __half2 s1,
-                                            uint32_t (&a)[4]) {
-    a[0] = as_u(__hmul2(__hsub2(codes_lo(t0), off), s0));
-    a[1] = as_u(__hmul2(__hsub2(codes_lo(t1), off), s1));
-    a[2] = as_u(__hmul2(__hsub2(codes_hi(t0), off), s0));
-    a[3] = as_u(__hmul2(__hsub2(codes_hi(t1), off), s1));
-}
-// the same as (code - 1024 offset) * mul - sub, per row (Q4_K)
-__device__ __forceinline__ void frag_affine(uint32_t t0, uint32_t t1, __half2 off, __half2 m0, __half2 m1, __half2 b0,
-                                            __half2 b1, uint32_t (&a)[4]) {
-    a[0] = as_u(__hfma2(__hsub2(codes_lo(t0), off), m0, b0));
-    a[1] = as_u(__hfma2(__hsub2(codes_lo(t1), off), m1, b1));
-    a[2] = as_u(__hfma2(__hsub2(codes_hi(t0), off), m0, b0));
-    a[3] = as_u(__hfma2(__hsub2(codes_hi(t1), off), m1, b1));
-}
-
-// Shared address of lane (gr, c)'s B fragment row: vector gr's staged inputs + 8 c bytes; the
-// lanes of vectors gr >= n take zeros.
+// Lane (gr, c)'s inputs: vector gr's row of records + 16 c bytes (the lanes of vectors gr >= n
+// take zeros), and its two vector columns' block sums (Q4_K).
 struct XFrag {
-    uint32_t row;  // shared address
+    uint32_t row;   // shared address
+    uint32_t sblk;  // shared address of block sums [block][MULTI_MAX] + vector 2c
     bool on;
 };
-__device__ __forceinline__ void xfrag(const XFrag& x, int col, uint32_t& b0, uint32_t& b1) {
-    b0 = 0u;
-    b1 = 0u;
-    if (x.on) asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(x.row + 2u * (uint32_t)col));
+// hi (b[0], b[1]) and lo (b[2], b[3]) terms of the B fragment of the 16 columns from `col`
+__device__ __forceinline__ void xfrag(const XFrag& x, int col, uint32_t (&b)[4]) {
+    b[0] = b[1] = b[2] = b[3] = 0u;
+    if (x.on)
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                     : "r"(x.row + 4u * (uint32_t)col));
 }
+// the block sums of vector columns 2c, 2c + 1 at block `blk` of the part
+__device__ __forceinline__ float2 xsums(const XFrag& x, int blk) {
+    float2 r;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(r.x), "=f"(r.y) : "r"(x.sblk + (uint32_t)blk * MULTI_MAX * 4));
+    return r;
+}
+// the A fragment of one 16-column step from its two code words (row gr: t0, row gr + 8: t1;
+// bytes = codes of columns 4c .. 4c + 3): code - off, exact
+__device__ __forceinline__ void frag_exact(uint32_t t0, uint32_t t1, __half2 off, uint32_t (&a)[4]) {
+    a[0] = as_u(__hsub2(codes_lo(t0), off));
+    a[1] = as_u(__hsub2(codes_lo(t1), off));
+    a[2] = as_u(__hsub2(codes_hi(t0), off));
+    a[3] = as_u(__hsub2(codes_hi(t1), off));
+}
+// A times both input terms, into d
+__device__ __forceinline__ void mma_hl(const uint32_t (&a)[4], const uint32_t (&b)[4], float (&d)[4]) {
+    mma_f16(a, b[0], b[1], d);
+    mma_f16(a, b[2], b[3], d);
+}
+// small non-negative integer -> float without the conversion unit (exact below 2^23)
+__device__ __forceinline__ float small_u2f(uint32_t u) { return __uint_as_float(0x4B000000u | u) - 8388608.0f; }
 
 // ---- one unit (32 rows x 128 columns) of local group gl against the 8 vector columns, per
 // weight format. accA: rows gr, gr + 8 (tile A), accB: 16 + gr, 24 + gr (tile B), vector
-// columns 2c, 2c + 1. The slot's scale words are read across lanes: the caller synchronises
-// the warp before (after its copies landed) and after (before a lane copies the next unit
-// into the slot).
+// columns 2c, 2c + 1 (c0, c1: the first row; c2, c3: the second). The slot's scale words are
+// read across lanes: the caller synchronises the warp before (after its copies landed) and
+// after (before a lane copies the next unit into the slot).
 
 __device__ __forceinline__ void unit_f16_q40(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
                                              float (&accB)[4]) {
@@ -143,25 +154,35 @@ __device__ __forceinline__ void unit_f16_q40(uint32_t sl, const XFrag& x, int gl
     }
     lds128(sl + Q4M_SCALES + 16 * gr, sa);  // words 4 gr + j: d of rows gr (low), gr + 8 (high), block j
     lds128(sl + Q4M_SCALES + 128 + 16 * gr, sb);
-    const __half2 off = __float2half2_rn(1032.f);  // 1024 + the zero point 8
+    const __half2 off = __float2half2_rn(1032.f);  // 1024 + the zero point 8: codes q - 8
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const __half2 a0 = splat_lo(sa[j]), a1 = splat_hi(sa[j]), b0s = splat_lo(sb[j]), b1s = splat_hi(sb[j]);
+        float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
             const uint32_t r0 = w[4 * j + 2 * s], r1 = w[4 * j + 2 * s + 1];
-            uint32_t fa[4], fb[4], x0, x1;
-            frag_scaled(r0 & 0x0F0F0F0Fu, r1 & 0x0F0F0F0Fu, off, a0, a1, fa);
-            frag_scaled((r0 >> 4) & 0x0F0F0F0Fu, (r1 >> 4) & 0x0F0F0F0Fu, off, b0s, b1s, fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, x0, x1);
-            mma_f16(fa, x0, x1, accA);
-            mma_f16(fb, x0, x1, accB);
+            uint32_t fa[4], fb[4], xb[4];
+            frag_exact(r0 & 0x0F0F0F0Fu, r1 & 0x0F0F0F0Fu, off, fa);
+            frag_exact((r0 >> 4) & 0x0F0F0F0Fu, (r1 >> 4) & 0x0F0F0F0Fu, off, fb);
+            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
+            mma_hl(fa, xb, bA);
+            mma_hl(fb, xb, bB);
         }
+        const float a0 = jinf_h2f((uint16_t)(sa[j] & 0xffffu)), a1 = jinf_h2f((uint16_t)(sa[j] >> 16));
+        const float b0 = jinf_h2f((uint16_t)(sb[j] & 0xffffu)), b1 = jinf_h2f((uint16_t)(sb[j] >> 16));
+        accA[0] = fmaf(a0, bA[0], accA[0]);
+        accA[1] = fmaf(a0, bA[1], accA[1]);
+        accA[2] = fmaf(a1, bA[2], accA[2]);
+        accA[3] = fmaf(a1, bA[3], accA[3]);
+        accB[0] = fmaf(b0, bB[0], accB[0]);
+        accB[1] = fmaf(b0, bB[1], accB[1]);
+        accB[2] = fmaf(b1, bB[2], accB[2]);
+        accB[3] = fmaf(b1, bB[3], accB[3]);
     }
 }
 
-// Q4_K: weight d sc q - dmin m (reference src/quant.cpp:71-77), per row and 32-column block j:
-// mul = d sc and sub = -dmin m, each rounded once to fp16.
+// Q4_K: weight d sc q - dmin m (reference src/quant.cpp:71-77): per row and 32-column block,
+// d sc times the block's sum of q x, minus dmin m times the block's sum of x.
 __device__ __forceinline__ void unit_f16_q4k(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
                                              float (&accB)[4]) {
     const int gr = lane >> 2;
@@ -179,38 +200,47 @@ __device__ __forceinline__ void unit_f16_q4k(uint32_t sl, const XFrag& x, int gl
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dm[1]) : "r"(sl + Q4M_DMIN_K + (gr + 8) * 4));
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dm[2]) : "r"(sl + Q4M_DMIN_K + 64 + gr * 4));
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dm[3]) : "r"(sl + Q4M_DMIN_K + 64 + (gr + 8) * 4));
-    // (d, d') and (dmin, dmin') of the tile's two rows
-    const __half2 dA = as_h2(__byte_perm(dm[0], dm[1], 0x5410)), mA = as_h2(__byte_perm(dm[0], dm[1], 0x7632));
-    const __half2 dB = as_h2(__byte_perm(dm[2], dm[3], 0x5410)), mB = as_h2(__byte_perm(dm[2], dm[3], 0x7632));
-    const __half2 off = __float2half2_rn(1024.f);
-    const __half2 neg = __float2half2_rn(-1.f);
+    float d[4], mn[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        d[i] = jinf_h2f((uint16_t)(dm[i] & 0xffffu));
+        mn[i] = jinf_h2f((uint16_t)(dm[i] >> 16));
+    }
+    const __half2 off = __float2half2_rn(1024.f);  // codes q
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        // the rows' 6-bit sc and m as exact fp16: bytes (sc, m, sc', m') of the scale word
-        const __half2 scA = __hsub2(as_h2(__byte_perm(sa[j], 0x64646464u, 0x4240)), off);
-        const __half2 miA = __hsub2(as_h2(__byte_perm(sa[j], 0x64646464u, 0x4341)), off);
-        const __half2 scB = __hsub2(as_h2(__byte_perm(sb[j], 0x64646464u, 0x4240)), off);
-        const __half2 miB = __hsub2(as_h2(__byte_perm(sb[j], 0x64646464u, 0x4341)), off);
-        const uint32_t mulA = as_u(__hmul2(dA, scA)), subA = as_u(__hmul2(__hmul2(mA, miA), neg));
-        const uint32_t mulB = as_u(__hmul2(dB, scB)), subB = as_u(__hmul2(__hmul2(mB, miB), neg));
-        const __half2 ma0 = splat_lo(mulA), ma1 = splat_hi(mulA), sa0 = splat_lo(subA), sa1 = splat_hi(subA);
-        const __half2 mb0 = splat_lo(mulB), mb1 = splat_hi(mulB), sb0 = splat_lo(subB), sb1 = splat_hi(subB);
+        float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
             const uint32_t r0 = w[4 * j + 2 * s], r1 = w[4 * j + 2 * s + 1];
-            uint32_t fa[4], fb[4], x0, x1;
-            frag_affine(r0 & 0x0F0F0F0Fu, r1 & 0x0F0F0F0Fu, off, ma0, ma1, sa0, sa1, fa);
-            frag_affine((r0 >> 4) & 0x0F0F0F0Fu, (r1 >> 4) & 0x0F0F0F0Fu, off, mb0, mb1, sb0, sb1, fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, x0, x1);
-            mma_f16(fa, x0, x1, accA);
-            mma_f16(fb, x0, x1, accB);
+            uint32_t fa[4], fb[4], xb[4];
+            frag_exact(r0 & 0x0F0F0F0Fu, r1 & 0x0F0F0F0Fu, off, fa);
+            frag_exact((r0 >> 4) & 0x0F0F0F0Fu, (r1 >> 4) & 0x0F0F0F0Fu, off, fb);
+            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
+            mma_hl(fa, xb, bA);
+            mma_hl(fb, xb, bB);
         }
+        const float2 S = xsums(x, gl * 4 + j);
+        // the four rows' (d sc, dmin m) of block j
+        const uint32_t qa = sa[j], qb = sb[j];
+        const float ka0 = d[0] * small_u2f(qa & 63u), ma0 = mn[0] * small_u2f((qa >> 8) & 63u);
+        const float ka1 = d[1] * small_u2f((qa >> 16) & 63u), ma1 = mn[1] * small_u2f((qa >> 24) & 63u);
+        const float kb0 = d[2] * small_u2f(qb & 63u), mb0 = mn[2] * small_u2f((qb >> 8) & 63u);
+        const float kb1 = d[3] * small_u2f((qb >> 16) & 63u), mb1 = mn[3] * small_u2f((qb >> 24) & 63u);
+        accA[0] = fmaf(ka0, bA[0], fmaf(-ma0, S.x, accA[0]));
+        accA[1] = fmaf(ka0, bA[1], fmaf(-ma0, S.y, accA[1]));
+        accA[2] = fmaf(ka1, bA[2], fmaf(-ma1, S.x, accA[2]));
+        accA[3] = fmaf(ka1, bA[3], fmaf(-ma1, S.y, accA[3]));
+        accB[0] = fmaf(kb0, bB[0], fmaf(-mb0, S.x, accB[0]));
+        accB[1] = fmaf(kb0, bB[1], fmaf(-mb0, S.y, accB[1]));
+        accB[2] = fmaf(kb1, bB[2], fmaf(-mb1, S.x, accB[2]));
+        accB[3] = fmaf(kb1, bB[3], fmaf(-mb1, S.y, accB[3]));
     }
 }
 
 // Q6_K: the 6-bit code as the int8 4 (q - 32) (nibble and flipped crumb, as the one-vector
-// path builds it), fp16 through the 0x80 flip, times d sc / 4 of its row and 16-column half
-// (reference cuda/dequant_kernels.cu:82-110).
+// path builds it), exact in fp16 through the 0x80 flip; each 16-column half has its own scale,
+// so a half's sums take d sc / 4 of their row (reference cuda/dequant_kernels.cu:82-110).
 __device__ __forceinline__ void unit_f16_q6k(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
                                              float (&accB)[4]) {
     const int gr = lane >> 2;
@@ -233,10 +263,11 @@ __device__ __forceinline__ void unit_f16_q6k(uint32_t sl, const XFrag& x, int gl
         for (int i = 0; i < 4; ++i) sc[4 * jj + i] = t[i];
     }
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(dlo), "=r"(dhi) : "r"(sl + Q4M_D_6 + gr * 8));
+    const float d0 = 0.25f * jinf_h2f((uint16_t)(dlo & 0xffffu)), d1 = 0.25f * jinf_h2f((uint16_t)(dlo >> 16));
+    const float d2 = 0.25f * jinf_h2f((uint16_t)(dhi & 0xffffu)), d3 = 0.25f * jinf_h2f((uint16_t)(dhi >> 16));
     const __half2 off = __float2half2_rn(1152.f);  // 1024 + the 0x80 flip
-    const __half2 quarter = __float2half2_rn(0.25f);
-    const __half2 dA = __hmul2(as_h2(dlo), quarter), dB = __hmul2(as_h2(dhi), quarter);
     constexpr uint32_t NM = 0x3C3C3C3Cu, CM = 0xC0C0C0C0u, FL = 0x80808080u;
+    auto scv = [](uint32_t v, int b) { return (float)(int8_t)(uint8_t)(v >> (8 * b)); };
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t* nw = w + 4 * j;
@@ -246,24 +277,31 @@ __device__ __forceinline__ void unit_f16_q6k(uint32_t sl, const XFrag& x, int gl
                                (((nw[2] << 2) & NM) | ((h1 << 6) & CM)) ^ FL, (((nw[3] << 2) & NM) | ((h1 << 2) & CM)) ^ FL};
         const uint32_t B[4] = {(((nw[0] >> 2) & NM) | ((h0 << 4) & CM)) ^ FL, (((nw[1] >> 2) & NM) | (h0 & CM)) ^ FL,
                                (((nw[2] >> 2) & NM) | ((h1 << 4) & CM)) ^ FL, (((nw[3] >> 2) & NM) | (h1 & CM)) ^ FL};
-        const uint32_t sca = sc[2 * j] ^ FL, scb = sc[2 * j + 1] ^ FL;  // int8 scales, flipped
+        const uint32_t sca = sc[2 * j], scb = sc[2 * j + 1];  // bytes 2u + h: row gr + 8u, half h
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
-            // the rows' scales of half s (bytes s and 2 + s), exact, times d / 4
-            const uint32_t sel = s ? 0x4341u : 0x4240u;
-            const __half2 mA = __hmul2(dA, __hsub2(as_h2(__byte_perm(sca, 0x64646464u, sel)), off));
-            const __half2 mB = __hmul2(dB, __hsub2(as_h2(__byte_perm(scb, 0x64646464u, sel)), off));
-            uint32_t fa[4], fb[4], x0, x1;
-            frag_scaled(A[2 * s], A[2 * s + 1], off, splat_lo(as_u(mA)), splat_hi(as_u(mA)), fa);
-            frag_scaled(B[2 * s], B[2 * s + 1], off, splat_lo(as_u(mB)), splat_hi(as_u(mB)), fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, x0, x1);
-            mma_f16(fa, x0, x1, accA);
-            mma_f16(fb, x0, x1, accB);
+            float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t fa[4], fb[4], xb[4];
+            frag_exact(A[2 * s], A[2 * s + 1], off, fa);
+            frag_exact(B[2 * s], B[2 * s + 1], off, fb);
+            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
+            mma_hl(fa, xb, bA);
+            mma_hl(fb, xb, bB);
+            const float ka0 = d0 * scv(sca, s), ka1 = d1 * scv(sca, 2 + s);
+            const float kb0 = d2 * scv(scb, s), kb1 = d3 * scv(scb, 2 + s);
+            accA[0] = fmaf(ka0, bA[0], accA[0]);
+            accA[1] = fmaf(ka0, bA[1], accA[1]);
+            accA[2] = fmaf(ka1, bA[2], accA[2]);
+            accA[3] = fmaf(ka1, bA[3], accA[3]);
+            accB[0] = fmaf(kb0, bB[0], accB[0]);
+            accB[1] = fmaf(kb0, bB[1], accB[1]);
+            accB[2] = fmaf(kb1, bB[2], accB[2]);
+            accB[3] = fmaf(kb1, bB[3], accB[3]);
         }
     }
 }
 
-// Q8_0: the int8 code, fp16 through the 0x80 flip, times the row's block d.
+// Q8_0: the int8 code, exact in fp16 through the 0x80 flip; the block's sums take the row's d.
 __device__ __forceinline__ void unit_f16_q80(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
                                              float (&accB)[4]) {
     const int gr = lane >> 2;
@@ -284,17 +322,26 @@ __device__ __forceinline__ void unit_f16_q80(uint32_t sl, const XFrag& x, int gl
         uint32_t wa[4], wb[4];
         lds128(sl + 1024 * j + lane * 16, wa);
         lds128(sl + 1024 * j + 512 + lane * 16, wb);
-        const __half2 a0 = splat_lo(dd[2 * j]), a1 = splat_hi(dd[2 * j]);
-        const __half2 b0s = splat_lo(dd[2 * j + 1]), b1s = splat_hi(dd[2 * j + 1]);
+        float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
-            uint32_t fa[4], fb[4], x0, x1;
-            frag_scaled(wa[2 * s] ^ FL, wa[2 * s + 1] ^ FL, off, a0, a1, fa);
-            frag_scaled(wb[2 * s] ^ FL, wb[2 * s + 1] ^ FL, off, b0s, b1s, fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, x0, x1);
-            mma_f16(fa, x0, x1, accA);
-            mma_f16(fb, x0, x1, accB);
+            uint32_t fa[4], fb[4], xb[4];
+            frag_exact(wa[2 * s] ^ FL, wa[2 * s + 1] ^ FL, off, fa);
+            frag_exact(wb[2 * s] ^ FL, wb[2 * s + 1] ^ FL, off, fb);
+            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
+            mma_hl(fa, xb, bA);
+            mma_hl(fb, xb, bB);
         }
+        const float e0 = jinf_h2f((uint16_t)(dd[2 * j] & 0xffffu)), e1 = jinf_h2f((uint16_t)(dd[2 * j] >> 16));
+        const float e2 = jinf_h2f((uint16_t)(dd[2 * j + 1] & 0xffffu)), e3 = jinf_h2f((uint16_t)(dd[2 * j + 1] >> 16));
+        accA[0] = fmaf(e0, bA[0], accA[0]);
+        accA[1] = fmaf(e0, bA[1], accA[1]);
+        accA[2] = fmaf(e1, bA[2], accA[2]);
+        accA[3] = fmaf(e1, bA[3], accA[3]);
+        accB[0] = fmaf(e2, bB[0], accB[0]);
+        accB[1] = fmaf(e2, bB[1], accB[1]);
+        accB[2] = fmaf(e3, bB[2], accB[2]);
+        accB[3] = fmaf(e3, bB[3], accB[3]);
     }
 }
 
@@ -392,7 +439,8 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     const int cg = ((int)gridDim.x - kp + kw - 1) / kw;  // CTAs of part kp
     const int g0 = kp * G / kw, g1 = (kp + 1) * G / kw, ng = g1 - g0;
     const int xsb = multi_xs_stride(gk);
-    uint8_t* xs = smem_m;                                                     // [n][xsb] fp16 inputs
+    uint8_t* xs = smem_m;                                                     // [n][xsb] fp16 input records
+    float* sblk = reinterpret_cast<float*>(xs + (size_t)n * xsb);             // [gk * 4][MULTI_MAX] block sums
     float* ep = reinterpret_cast<float*>(smem_m + multi_xs_bytes(n, gk));    // [MNW][MULTI_MAX][EP_STRIDE]
     float* fac = ep + MNW * MULTI_MAX * EP_STRIDE;  // [v] norm factor, [8 + v] 1 / s, [16 + v] max, [24 + v] s
     u64* keys = reinterpret_cast<u64*>(fac + 64);                            // [MNW][MULTI_MAX]
@@ -496,15 +544,23 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
             if (it >= items) break;
             const int v = it / ng, gl = it % ng;
             const float s = fac[24 + v];
-            const __half2 h01 = __floats2half2_rn(x4[b].x * s, x4[b].y * s);
-            const __half2 h23 = __floats2half2_rn(x4[b].z * s, x4[b].w * s);
-            *reinterpret_cast<uint2*>(xs + (size_t)v * xsb + (size_t)(gl * 128 + 4 * lane) * 2) =
-                make_uint2(as_u(h01), as_u(h23));
+            const float e0 = x4[b].x * s, e1 = x4[b].y * s, e2 = x4[b].z * s, e3 = x4[b].w * s;
+            const __half2 h01 = __floats2half2_rn(e0, e1), h23 = __floats2half2_rn(e2, e3);
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            const __half2 l01 = __floats2half2_rn(e0 - f01.x, e1 - f01.y), l23 = __floats2half2_rn(e2 - f23.x, e3 - f23.y);
+            *reinterpret_cast<uint4*>(xs + (size_t)v * xsb + (size_t)(gl * 32 + lane) * 16) =
+                make_uint4(as_u(h01), as_u(h23), as_u(l01), as_u(l23));
+            // the block's sum (lanes 8 i .. 8 i + 7 hold block i of the group)
+            float bs = (e0 + e1) + (e2 + e3);
+            bs += __shfl_xor_sync(JINF_FULL_MASK, bs, 1);
+            bs += __shfl_xor_sync(JINF_FULL_MASK, bs, 2);
+            bs += __shfl_xor_sync(JINF_FULL_MASK, bs, 4);
+            if ((lane & 7) == 0) sblk[(gl * 4 + (lane >> 3)) * MULTI_MAX + v] = bs;
         }
     }
     __syncthreads();
     const int gr = lane >> 2, c = lane & 3;
-    const XFrag xf{smem_u32(xs) + (uint32_t)(gr * xsb + 8 * c), gr < n};
+    const XFrag xf{smem_u32(xs) + (uint32_t)(gr * xsb + 16 * c), smem_u32(sblk) + (uint32_t)(8 * c), gr < n};
     // a lane's sums -> the warp's staging block (true scale): rows gr, gr + 8, 16 + gr, 24 + gr of
     // vector columns 2c, 2c + 1
     auto stage_rows = [&](const float (&aA)[4], const float (&aB)[4]) {
