@@ -5,26 +5,18 @@
 // (BASELINE config C2 at batch 4 and 8). The reference has no batched form; at one vector
 // its arithmetic is cuda/matmul_kernels.cu:8-43 (Q4_0) and :104-185 (Q4_K, Q6_K, Q8_0).
 //
-// Arithmetic. One mma.m16n8k16 (f16 x f16 -> f32) multiplies 16 rows by 16 columns of all 8
-// vectors at once: the vectors are the MMA's 8 columns.
-//   A (weights): each lane turns the 4-bit (6-, 8-bit) codes of its unit words straight into
-//     fp16 fragments of the exact integer weights: the byte code q becomes the fp16 1024 + q
-//     (0x64 as the high byte) minus the format's offset, with no rounding. A unit word holds
-//     columns 4c .. 4c + 3 of rows gr or gr + 8 (low nibbles: tile A, high: tile B); the MMA's
-//     logical columns (2c, 2c+1 | 2c+8, 2c+9) are mapped to them, and the B fragments follow
-//     the same map.
-//   B (inputs): the K part's columns of every vector in shared memory as two fp16 terms,
-//     hi = fp16(x s) and lo = fp16(x s - hi) (about 22 significant bits together), each vector
-//     scaled by a power of two s that puts its largest magnitude in [2^13, 2^14) (undone
-//     exactly on the outputs); lane (gr, c) reads hi and lo of columns 4c .. 4c + 3 of
-//     vector gr as one 16-byte load, and the MMA runs once per term.
-//   The block's scale (per row, per 32 columns; Q6_K: per 16) multiplies its fp32 sums
-//     after its MMAs, as the reference applies d to each block's sum
-//     (cuda/matmul_kernels.cu:8-43); Q4_K subtracts dmin m times the block's input sum.
-// So the weights are exact, the inputs carry ~22 bits relative to their maximum, and every
-// sum is fp32.
+// Arithmetic (q4m_device.cuh for one vector). The inputs are int8 digit records per
+// 32-element block (alpha = 32639 / max|x|, v = rint(x alpha) = 256 hi + lo). In one
+// m16n8k32 step the B operand's 8 columns hold digit h of vector 4 vb + c in column 2c + h,
+// so one step multiplies a block of 16 rows by four vectors' digits and the accumulator
+// columns (2c, 2c + 1) of a lane are vector c's hi and lo sums. Each block is finished on its
+// own (its scale differs per row, its digit scale per vector): the step starts from the
+// vector's zero-point offsets (Q4_0) and the block adds d (256 D_hi + D_lo) / alpha to the
+// lane's rows. Vectors 4..7 take a second step per block. A lane ends a task with complete
+// sums of rows gr, gr + 8, 16 + gr, 24 + gr of the tile pair for its vector(s); no lane
+// reduction is needed.
 //
-// Scheduling. CTA c works on K part kp = c % kw only, so it stages just that part's inputs
+// Scheduling. CTA c works on K part kp = c % kw only, so it stages just that part's records
 // (n vectors x gk groups) in shared memory. Two ways to share out a part's work:
 //   per warp (many tile pairs, e.g. an LM head): the CTA's warps take tile pairs, each warp
 //     all of the part's groups of its pair; consecutive pairs go to different CTAs;
@@ -59,90 +51,67 @@ constexpr int kMultiMaxKw = 32;
 constexpr int EP_STRIDE = 33;         // floats per staged row block (32 rows, padded)
 
 // Ring slots per warp: 2 in flight per warp keep HBM busy with 16 warps per SM, and leave
-// room for the inputs (the larger Q6_K and Q8_0 units: 1 in flight).
+// room for the records of several vectors (the larger Q6_K and Q8_0 units: 1 in flight).
 __host__ __device__ constexpr inline int multi_nbuf(int fmt) { return fmt == Q4M_Q6_K || fmt == Q4M_Q8_0 ? 2 : 3; }
 
-// Staged inputs: per vector a row of 16-byte records, one per 4 columns (hi of the 4, then lo),
-// padded by 64 bytes so that the two rows one quarter-warp load reads fall in different
-// banks; then the inputs' sums per 32-column block [gk * 4][MULTI_MAX] floats (Q4_K's min
-// term).
-__host__ __device__ inline int multi_xs_stride(int gk) { return gk * 512 + 64; }  // bytes per vector
-__host__ __device__ inline size_t multi_xs_bytes(int n, int gk) {
-    return (size_t)n * multi_xs_stride(gk) + (size_t)gk * 4 * MULTI_MAX * 4;
+// Staged records: digits [n][gk][256 B] then params [n][gk][4][16 B], each vector's run padded
+// (digits +64 B, params +16 B) so that the lanes of one load that read different vectors fall
+// in different shared-memory banks.
+__host__ __device__ inline int multi_dig_stride(int gk) { return gk * 256 + 64; }
+__host__ __device__ inline int multi_prm_stride(int gk) { return gk * 64 + 16; }
+__host__ __device__ inline size_t multi_rec_bytes(int n, int gk) {
+    return (size_t)n * (multi_dig_stride(gk) + multi_prm_stride(gk));
 }
-// epilogue staging [MNW][MULTI_MAX][EP_STRIDE] floats, 64 floats of per-vector factors (norm,
-// input scale, maximum), the argmax keys [MNW][MULTI_MAX], the merged rows
-// [MULTI_MAX][EP_STRIDE] (per-CTA split) and a flag
+// epilogue staging [MNW][MULTI_MAX][EP_STRIDE] floats, 64 floats of norm factors, the argmax
+// keys [MNW][MULTI_MAX], the merged rows [MULTI_MAX][EP_STRIDE] (per-CTA split) and a flag
 constexpr size_t MULTI_EP_BYTES =
     (size_t)MNW * MULTI_MAX * EP_STRIDE * 4 + 64 * 4 + MNW * MULTI_MAX * 8 + MULTI_MAX * EP_STRIDE * 4 + 16;
 
 __host__ __device__ inline size_t multi_smem(int n, int gk, int fmt) {
-    return multi_xs_bytes(n, gk) + MULTI_EP_BYTES + (size_t)MNW * multi_nbuf(fmt) * q4m_unit_bytes(fmt);
+    return multi_rec_bytes(n, gk) + MULTI_EP_BYTES + (size_t)MNW * multi_nbuf(fmt) * q4m_unit_bytes(fmt);
 }
 
 __device__ __forceinline__ void lds128(uint32_t a, uint32_t (&r)[4]) {
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
 }
 
-__device__ __forceinline__ void mma_f16(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, float (&d)[4]) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ __half2 as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
-__device__ __forceinline__ uint32_t as_u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-// bytes 0, 1 (lo) or 2, 3 (hi) of a word of 8-bit codes as the fp16 pair (1024 + b, 1024 + b')
-__device__ __forceinline__ __half2 codes_lo(uint32_t t) { return as_h2(__byte_perm(t, 0x64646464u, 0x4140)); }
-__device__ __forceinline__ __half2 codes_hi(uint32_t t) { return as_h2(__byte_perm(t, 0x64646464u, 0x4342)); }
-
-// Lane (gr, c)'s inputs: vector gr's row of records + 16 c bytes (the lanes of vectors gr >= n
-// take zeros), and its two vector columns' block sums (Q4_K).
-struct XFrag {
-    uint32_t row;   // shared address
-    uint32_t sblk;  // shared address of block sums [block][MULTI_MAX] + vector 2c
-    bool on;
+// Staged records of one vector block (4 vectors) for block j of local group gl: the lane's B
+// fragment (digit h = gr & 1 of vector 4 vb + gr / 2) and the params of its accumulator vector
+// 4 vb + c (zero-point offsets kh, kl and the digit scales ia, ia / 16).
+struct MultiRec {
+    uint32_t dig, prm;  // shared addresses
+    int dstride, pstride, n;
 };
-// hi (b[0], b[1]) and lo (b[2], b[3]) terms of the B fragment of the 16 columns from `col`
-__device__ __forceinline__ void xfrag(const XFrag& x, int col, uint32_t (&b)[4]) {
-    b[0] = b[1] = b[2] = b[3] = 0u;
-    if (x.on)
-        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                     : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
-                     : "r"(x.row + 4u * (uint32_t)col));
+__device__ __forceinline__ void rec_frag(const MultiRec& r, int vb, int j, int gl, int lane, uint32_t& b0,
+                                         uint32_t& b1) {
+    const int gr = lane >> 2, c = lane & 3;
+    const int v = 4 * vb + (gr >> 1), h = gr & 1;
+    b0 = 0u;
+    b1 = 0u;
+    if (v < r.n)
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                     : "=r"(b0), "=r"(b1)
+                     : "r"(r.dig + (uint32_t)(v * r.dstride + gl * 256 + ((2 * j + h) * 4 + c) * 8)));
 }
-// the block sums of vector columns 2c, 2c + 1 at block `blk` of the part
-__device__ __forceinline__ float2 xsums(const XFrag& x, int blk) {
-    float2 r;
-    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(r.x), "=f"(r.y) : "r"(x.sblk + (uint32_t)blk * MULTI_MAX * 4));
-    return r;
+__device__ __forceinline__ void rec_prm(const MultiRec& r, int vb, int j, int gl, int lane, int& kh, int& kl,
+                                        float& ia, float& ib) {
+    const int vo = 4 * vb + (lane & 3);
+    kh = 0;
+    kl = 0;
+    ia = 0.f;
+    ib = 0.f;
+    if (vo < r.n)
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(kh), "=r"(kl), "=f"(ia), "=f"(ib)
+                     : "r"(r.prm + (uint32_t)(vo * r.pstride + (gl * 4 + j) * 16)));
 }
-// the A fragment of one 16-column step from its two code words (row gr: t0, row gr + 8: t1;
-// bytes = codes of columns 4c .. 4c + 3): code - off, exact
-__device__ __forceinline__ void frag_exact(uint32_t t0, uint32_t t1, __half2 off, uint32_t (&a)[4]) {
-    a[0] = as_u(__hsub2(codes_lo(t0), off));
-    a[1] = as_u(__hsub2(codes_lo(t1), off));
-    a[2] = as_u(__hsub2(codes_hi(t0), off));
-    a[3] = as_u(__hsub2(codes_hi(t1), off));
-}
-// A times both input terms, into d
-__device__ __forceinline__ void mma_hl(const uint32_t (&a)[4], const uint32_t (&b)[4], float (&d)[4]) {
-    mma_f16(a, b[0], b[1], d);
-    mma_f16(a, b[2], b[3], d);
-}
-// small non-negative integer -> float without the conversion unit (exact below 2^23)
-__device__ __forceinline__ float small_u2f(uint32_t u) { return __uint_as_float(0x4B000000u | u) - 8388608.0f; }
 
-// ---- one unit (32 rows x 128 columns) of local group gl against the 8 vector columns, per
-// weight format. accA: rows gr, gr + 8 (tile A), accB: 16 + gr, 24 + gr (tile B), vector
-// columns 2c, 2c + 1 (c0, c1: the first row; c2, c3: the second). The slot's scale words are
-// read across lanes: the caller synchronises the warp before (after its copies landed) and
-// after (before a lane copies the next unit into the slot).
+// ---- one unit (32 rows x 128 columns) against NVB vector blocks, per weight format.
+// The slot's scale words are read across lanes: the caller synchronises the warp before
+// (after its copies landed) and after (before a lane copies the next unit into the slot).
 
-__device__ __forceinline__ void unit_f16_q40(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
-                                             float (&accB)[4]) {
+template <int NVB>
+__device__ __forceinline__ void unit_multi_q40(uint32_t sl, const MultiRec& r, int gl, int lane, float (&acc)[NVB][4]) {
     const int gr = lane >> 2;
     uint32_t w[16], sa[4], sb[4];
 #pragma unroll
@@ -152,39 +121,37 @@ __device__ __forceinline__ void unit_f16_q40(uint32_t sl, const XFrag& x, int gl
 #pragma unroll
         for (int i = 0; i < 4; ++i) w[4 * j + i] = t[i];
     }
-    lds128(sl + Q4M_SCALES + 16 * gr, sa);  // words 4 gr + j: d of rows gr (low), gr + 8 (high), block j
+    lds128(sl + Q4M_SCALES + 16 * gr, sa);        // words 4 gr + j: rows gr, gr + 8 of block j
     lds128(sl + Q4M_SCALES + 128 + 16 * gr, sb);
-    const __half2 off = __float2half2_rn(1032.f);  // 1024 + the zero point 8: codes q - 8
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
+        const float dA0 = jinf_h2f((uint16_t)(sa[j] & 0xffffu)), dA1 = jinf_h2f((uint16_t)(sa[j] >> 16));
+        const float dB0 = jinf_h2f((uint16_t)(sb[j] & 0xffffu)), dB1 = jinf_h2f((uint16_t)(sb[j] >> 16));
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            const uint32_t r0 = w[4 * j + 2 * s], r1 = w[4 * j + 2 * s + 1];
-            uint32_t fa[4], fb[4], xb[4];
-            frag_exact(r0 & 0x0F0F0F0Fu, r1 & 0x0F0F0F0Fu, off, fa);
-            frag_exact((r0 >> 4) & 0x0F0F0F0Fu, (r1 >> 4) & 0x0F0F0F0Fu, off, fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
-            mma_hl(fa, xb, bA);
-            mma_hl(fb, xb, bB);
+        for (int vb = 0; vb < NVB; ++vb) {
+            uint32_t b0, b1;
+            int kh, kl;
+            float ia, ib;
+            rec_frag(r, vb, j, gl, lane, b0, b1);
+            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
+            int da[4] = {kh, kl, kh, kl};
+            int db[4] = {kh * 16, kl * 16, kh * 16, kl * 16};
+            mma_u8s8(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), b0, b1, da);
+            mma_u8s8(nib_hi(w[4 * j]), nib_hi(w[4 * j + 1]), nib_hi(w[4 * j + 2]), nib_hi(w[4 * j + 3]), b0, b1, db);
+            acc[vb][0] = fmaf(dA0 * ia, (float)(da[0] * 256 + da[1]), acc[vb][0]);
+            acc[vb][1] = fmaf(dA1 * ia, (float)(da[2] * 256 + da[3]), acc[vb][1]);
+            acc[vb][2] = fmaf(dB0 * ib, (float)(db[0] * 256 + db[1]), acc[vb][2]);
+            acc[vb][3] = fmaf(dB1 * ib, (float)(db[2] * 256 + db[3]), acc[vb][3]);
         }
-        const float a0 = jinf_h2f((uint16_t)(sa[j] & 0xffffu)), a1 = jinf_h2f((uint16_t)(sa[j] >> 16));
-        const float b0 = jinf_h2f((uint16_t)(sb[j] & 0xffffu)), b1 = jinf_h2f((uint16_t)(sb[j] >> 16));
-        accA[0] = fmaf(a0, bA[0], accA[0]);
-        accA[1] = fmaf(a0, bA[1], accA[1]);
-        accA[2] = fmaf(a1, bA[2], accA[2]);
-        accA[3] = fmaf(a1, bA[3], accA[3]);
-        accB[0] = fmaf(b0, bB[0], accB[0]);
-        accB[1] = fmaf(b0, bB[1], accB[1]);
-        accB[2] = fmaf(b1, bB[2], accB[2]);
-        accB[3] = fmaf(b1, bB[3], accB[3]);
     }
 }
 
-// Q4_K: weight d sc q - dmin m (reference src/quant.cpp:71-77): per row and 32-column block,
-// d sc times the block's sum of q x, minus dmin m times the block's sum of x.
-__device__ __forceinline__ void unit_f16_q4k(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
-                                             float (&accB)[4]) {
+// Q4_K: no zero point; block j of row r contributes (d sc (256 D_hi + D_lo) -
+// dmin m (256 S_hi + S_lo)) / alpha, S the block's digit sums recovered from the record's
+// zero-point params (-8 S). Tile B's sums carry the 16 of its high-nibble operand, so its min
+// term is taken x16 and the row scaled by 1 / (16 alpha).
+template <int NVB>
+__device__ __forceinline__ void unit_multi_q4k(uint32_t sl, const MultiRec& r, int gl, int lane, float (&acc)[NVB][4]) {
     const int gr = lane >> 2;
     uint32_t w[16], sa[4], sb[4], dm[4];
 #pragma unroll
@@ -194,57 +161,54 @@ __device__ __forceinline__ void unit_f16_q4k(uint32_t sl, const XFrag& x, int gl
 #pragma unroll
         for (int i = 0; i < 4; ++i) w[4 * j + i] = t[i];
     }
-    lds128(sl + Q4M_SCALES + 16 * gr, sa);  // sc | m << 8 of rows gr (low half), gr + 8, block j
+    lds128(sl + Q4M_SCALES + 16 * gr, sa);        // sc | m << 8 of rows gr (low half), gr + 8, block j
     lds128(sl + Q4M_SCALES + 128 + 16 * gr, sb);
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dm[0]) : "r"(sl + Q4M_DMIN_K + gr * 4));
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dm[1]) : "r"(sl + Q4M_DMIN_K + (gr + 8) * 4));
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dm[2]) : "r"(sl + Q4M_DMIN_K + 64 + gr * 4));
     asm volatile("ld.shared.u32 %0, [%1];" : "=r"(dm[3]) : "r"(sl + Q4M_DMIN_K + 64 + (gr + 8) * 4));
-    float d[4], mn[4];
+    float d[4], m[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         d[i] = jinf_h2f((uint16_t)(dm[i] & 0xffffu));
-        mn[i] = jinf_h2f((uint16_t)(dm[i] >> 16));
+        m[i] = jinf_h2f((uint16_t)(dm[i] >> 16));
     }
-    const __half2 off = __float2half2_rn(1024.f);  // codes q
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t scm[4] = {sa[j] & 0xffffu, sa[j] >> 16, sb[j] & 0xffffu, sb[j] >> 16};
+        float sd[4], sm[4];
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            const uint32_t r0 = w[4 * j + 2 * s], r1 = w[4 * j + 2 * s + 1];
-            uint32_t fa[4], fb[4], xb[4];
-            frag_exact(r0 & 0x0F0F0F0Fu, r1 & 0x0F0F0F0Fu, off, fa);
-            frag_exact((r0 >> 4) & 0x0F0F0F0Fu, (r1 >> 4) & 0x0F0F0F0Fu, off, fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
-            mma_hl(fa, xb, bA);
-            mma_hl(fb, xb, bB);
+        for (int i = 0; i < 4; ++i) {
+            sd[i] = d[i] * (float)(scm[i] & 63u);
+            sm[i] = m[i] * (float)((scm[i] >> 8) & 63u);
         }
-        const float2 S = xsums(x, gl * 4 + j);
-        // the four rows' (d sc, dmin m) of block j
-        const uint32_t qa = sa[j], qb = sb[j];
-        const float ka0 = d[0] * small_u2f(qa & 63u), ma0 = mn[0] * small_u2f((qa >> 8) & 63u);
-        const float ka1 = d[1] * small_u2f((qa >> 16) & 63u), ma1 = mn[1] * small_u2f((qa >> 24) & 63u);
-        const float kb0 = d[2] * small_u2f(qb & 63u), mb0 = mn[2] * small_u2f((qb >> 8) & 63u);
-        const float kb1 = d[3] * small_u2f((qb >> 16) & 63u), mb1 = mn[3] * small_u2f((qb >> 24) & 63u);
-        accA[0] = fmaf(ka0, bA[0], fmaf(-ma0, S.x, accA[0]));
-        accA[1] = fmaf(ka0, bA[1], fmaf(-ma0, S.y, accA[1]));
-        accA[2] = fmaf(ka1, bA[2], fmaf(-ma1, S.x, accA[2]));
-        accA[3] = fmaf(ka1, bA[3], fmaf(-ma1, S.y, accA[3]));
-        accB[0] = fmaf(kb0, bB[0], fmaf(-mb0, S.x, accB[0]));
-        accB[1] = fmaf(kb0, bB[1], fmaf(-mb0, S.y, accB[1]));
-        accB[2] = fmaf(kb1, bB[2], fmaf(-mb1, S.x, accB[2]));
-        accB[3] = fmaf(kb1, bB[3], fmaf(-mb1, S.y, accB[3]));
+#pragma unroll
+        for (int vb = 0; vb < NVB; ++vb) {
+            uint32_t b0, b1;
+            int kh, kl;
+            float ia, ib;
+            rec_frag(r, vb, j, gl, lane, b0, b1);
+            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
+            int da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
+            mma_u8s8(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), b0, b1, da);
+            mma_u8s8(nib_hi(w[4 * j]), nib_hi(w[4 * j + 1]), nib_hi(w[4 * j + 2]), nib_hi(w[4 * j + 3]), b0, b1, db);
+            const float S = (float)(-((kh << 8) + kl) >> 3);  // 256 S_hi + S_lo of the block (exact)
+            acc[vb][0] = fmaf(fmaf(sd[0], (float)(da[0] * 256 + da[1]), -sm[0] * S), ia, acc[vb][0]);
+            acc[vb][1] = fmaf(fmaf(sd[1], (float)(da[2] * 256 + da[3]), -sm[1] * S), ia, acc[vb][1]);
+            acc[vb][2] = fmaf(fmaf(sd[2], (float)(db[0] * 256 + db[1]), -sm[2] * 16.0f * S), ib, acc[vb][2]);
+            acc[vb][3] = fmaf(fmaf(sd[3], (float)(db[2] * 256 + db[3]), -sm[3] * 16.0f * S), ib, acc[vb][3]);
+        }
     }
 }
 
-// Q6_K: the 6-bit code as the int8 4 (q - 32) (nibble and flipped crumb, as the one-vector
-// path builds it), exact in fp16 through the 0x80 flip; each 16-column half has its own scale,
-// so a half's sums take d sc / 4 of their row (reference cuda/dequant_kernels.cu:82-110).
-__device__ __forceinline__ void unit_f16_q6k(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
-                                             float (&accB)[4]) {
+// Q6_K: each weight byte is rebuilt as the int8 value 4 (q - 32) from its nibble and flipped
+// crumb; a scale covers 16 elements, so every block is two m16n8k16 steps per tile, one per
+// half, into their own accumulators; block j of row r contributes
+// d (sc_0 (256 D0_hi + D0_lo) + sc_1 (256 D1_hi + D1_lo)) / (4 alpha).
+template <int NVB>
+__device__ __forceinline__ void unit_multi_q6k(uint32_t sl, const MultiRec& r, int gl, int lane, float (&acc)[NVB][4]) {
     const int gr = lane >> 2;
-    uint32_t w[16], cr[8], sc[8], dlo, dhi;
+    uint32_t w[16], cr[8], sc[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         uint32_t t[4];
@@ -262,96 +226,92 @@ __device__ __forceinline__ void unit_f16_q6k(uint32_t sl, const XFrag& x, int gl
 #pragma unroll
         for (int i = 0; i < 4; ++i) sc[4 * jj + i] = t[i];
     }
+    uint32_t dlo, dhi;
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(dlo), "=r"(dhi) : "r"(sl + Q4M_D_6 + gr * 8));
-    const float d0 = 0.25f * jinf_h2f((uint16_t)(dlo & 0xffffu)), d1 = 0.25f * jinf_h2f((uint16_t)(dlo >> 16));
-    const float d2 = 0.25f * jinf_h2f((uint16_t)(dhi & 0xffffu)), d3 = 0.25f * jinf_h2f((uint16_t)(dhi >> 16));
-    const __half2 off = __float2half2_rn(1152.f);  // 1024 + the 0x80 flip
-    constexpr uint32_t NM = 0x3C3C3C3Cu, CM = 0xC0C0C0C0u, FL = 0x80808080u;
+    const float d0 = jinf_h2f((uint16_t)(dlo & 0xffffu)), d1 = jinf_h2f((uint16_t)(dlo >> 16));
+    const float d2 = jinf_h2f((uint16_t)(dhi & 0xffffu)), d3 = jinf_h2f((uint16_t)(dhi >> 16));
+    constexpr uint32_t NM = 0x3C3C3C3Cu, CM = 0xC0C0C0C0u;
     auto scv = [](uint32_t v, int b) { return (float)(int8_t)(uint8_t)(v >> (8 * b)); };
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t* nw = w + 4 * j;
         const uint32_t h0 = cr[2 * j], h1 = cr[2 * j + 1];
-        // int8 4 (q - 32) of tiles A (low nibbles) and B (high), words i = 0..3, flipped by 0x80
-        const uint32_t A[4] = {(((nw[0] << 2) & NM) | ((h0 << 6) & CM)) ^ FL, (((nw[1] << 2) & NM) | ((h0 << 2) & CM)) ^ FL,
-                               (((nw[2] << 2) & NM) | ((h1 << 6) & CM)) ^ FL, (((nw[3] << 2) & NM) | ((h1 << 2) & CM)) ^ FL};
-        const uint32_t B[4] = {(((nw[0] >> 2) & NM) | ((h0 << 4) & CM)) ^ FL, (((nw[1] >> 2) & NM) | (h0 & CM)) ^ FL,
-                               (((nw[2] >> 2) & NM) | ((h1 << 4) & CM)) ^ FL, (((nw[3] >> 2) & NM) | (h1 & CM)) ^ FL};
-        const uint32_t sca = sc[2 * j], scb = sc[2 * j + 1];  // bytes 2u + h: row gr + 8u, half h
+        const uint32_t A0 = ((nw[0] << 2) & NM) | ((h0 << 6) & CM), B0 = ((nw[0] >> 2) & NM) | ((h0 << 4) & CM);
+        const uint32_t A1 = ((nw[1] << 2) & NM) | ((h0 << 2) & CM), B1 = ((nw[1] >> 2) & NM) | (h0 & CM);
+        const uint32_t A2 = ((nw[2] << 2) & NM) | ((h1 << 6) & CM), B2 = ((nw[2] >> 2) & NM) | ((h1 << 4) & CM);
+        const uint32_t A3 = ((nw[3] << 2) & NM) | ((h1 << 2) & CM), B3 = ((nw[3] >> 2) & NM) | (h1 & CM);
+        const uint32_t sca = sc[2 * j], scb = sc[2 * j + 1];
+        // per row: the two half-block scales times d
+        const float a00 = d0 * scv(sca, 0), a01 = d0 * scv(sca, 1), a10 = d1 * scv(sca, 2), a11 = d1 * scv(sca, 3);
+        const float b00 = d2 * scv(scb, 0), b01 = d2 * scv(scb, 1), b10 = d3 * scv(scb, 2), b11 = d3 * scv(scb, 3);
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t fa[4], fb[4], xb[4];
-            frag_exact(A[2 * s], A[2 * s + 1], off, fa);
-            frag_exact(B[2 * s], B[2 * s + 1], off, fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
-            mma_hl(fa, xb, bA);
-            mma_hl(fb, xb, bB);
-            const float ka0 = d0 * scv(sca, s), ka1 = d1 * scv(sca, 2 + s);
-            const float kb0 = d2 * scv(scb, s), kb1 = d3 * scv(scb, 2 + s);
-            accA[0] = fmaf(ka0, bA[0], accA[0]);
-            accA[1] = fmaf(ka0, bA[1], accA[1]);
-            accA[2] = fmaf(ka1, bA[2], accA[2]);
-            accA[3] = fmaf(ka1, bA[3], accA[3]);
-            accB[0] = fmaf(kb0, bB[0], accB[0]);
-            accB[1] = fmaf(kb0, bB[1], accB[1]);
-            accB[2] = fmaf(kb1, bB[2], accB[2]);
-            accB[3] = fmaf(kb1, bB[3], accB[3]);
+        for (int vb = 0; vb < NVB; ++vb) {
+            uint32_t x0, x1;
+            int kh, kl;
+            float ia, ib;
+            rec_frag(r, vb, j, gl, lane, x0, x1);
+            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
+            int p0[4] = {0, 0, 0, 0}, p1[4] = {0, 0, 0, 0}, q0[4] = {0, 0, 0, 0}, q1[4] = {0, 0, 0, 0};
+            mma_s8s8_k16(A0, A1, x0, p0);
+            mma_s8s8_k16(A2, A3, x1, p1);
+            mma_s8s8_k16(B0, B1, x0, q0);
+            mma_s8s8_k16(B2, B3, x1, q1);
+            const float s = 0.25f * ia;
+            auto dsum = [](const int (&h)[4], int rr) { return (float)(h[2 * rr] * 256 + h[2 * rr + 1]); };
+            acc[vb][0] = fmaf(fmaf(a00, dsum(p0, 0), a01 * dsum(p1, 0)), s, acc[vb][0]);
+            acc[vb][1] = fmaf(fmaf(a10, dsum(p0, 1), a11 * dsum(p1, 1)), s, acc[vb][1]);
+            acc[vb][2] = fmaf(fmaf(b00, dsum(q0, 0), b01 * dsum(q1, 0)), s, acc[vb][2]);
+            acc[vb][3] = fmaf(fmaf(b10, dsum(q0, 1), b11 * dsum(q1, 1)), s, acc[vb][3]);
         }
     }
 }
 
-// Q8_0: the int8 code, exact in fp16 through the 0x80 flip; the block's sums take the row's d.
-__device__ __forceinline__ void unit_f16_q80(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
-                                             float (&accB)[4]) {
+// Q8_0: the weight words are the int8 q themselves, one m16n8k32 step per block and tile, no
+// zero point; block j of row r contributes d (256 D_hi + D_lo) / alpha.
+template <int NVB>
+__device__ __forceinline__ void unit_multi_q80(uint32_t sl, const MultiRec& r, int gl, int lane, float (&acc)[NVB][4]) {
     const int gr = lane >> 2;
     uint32_t dd[8];
     {
         uint32_t t[4];
-        lds128(sl + Q4M_D_8 + 32 * gr, t);  // blocks 0, 1: (d of rows gr, gr + 8), (16 + gr, 24 + gr)
+        lds128(sl + Q4M_D_8 + 32 * gr, t);  // blocks 0, 1: (rows gr, gr + 8), (16 + gr, 24 + gr)
 #pragma unroll
         for (int i = 0; i < 4; ++i) dd[i] = t[i];
         lds128(sl + Q4M_D_8 + 32 * gr + 16, t);
 #pragma unroll
         for (int i = 0; i < 4; ++i) dd[4 + i] = t[i];
     }
-    const __half2 off = __float2half2_rn(1152.f);
-    constexpr uint32_t FL = 0x80808080u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         uint32_t wa[4], wb[4];
         lds128(sl + 1024 * j + lane * 16, wa);
         lds128(sl + 1024 * j + 512 + lane * 16, wb);
-        float bA[4] = {0.f, 0.f, 0.f, 0.f}, bB[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-            uint32_t fa[4], fb[4], xb[4];
-            frag_exact(wa[2 * s] ^ FL, wa[2 * s + 1] ^ FL, off, fa);
-            frag_exact(wb[2 * s] ^ FL, wb[2 * s + 1] ^ FL, off, fb);
-            xfrag(x, gl * 128 + 32 * j + 16 * s, xb);
-            mma_hl(fa, xb, bA);
-            mma_hl(fb, xb, bB);
-        }
         const float e0 = jinf_h2f((uint16_t)(dd[2 * j] & 0xffffu)), e1 = jinf_h2f((uint16_t)(dd[2 * j] >> 16));
         const float e2 = jinf_h2f((uint16_t)(dd[2 * j + 1] & 0xffffu)), e3 = jinf_h2f((uint16_t)(dd[2 * j + 1] >> 16));
-        accA[0] = fmaf(e0, bA[0], accA[0]);
-        accA[1] = fmaf(e0, bA[1], accA[1]);
-        accA[2] = fmaf(e1, bA[2], accA[2]);
-        accA[3] = fmaf(e1, bA[3], accA[3]);
-        accB[0] = fmaf(e2, bB[0], accB[0]);
-        accB[1] = fmaf(e2, bB[1], accB[1]);
-        accB[2] = fmaf(e3, bB[2], accB[2]);
-        accB[3] = fmaf(e3, bB[3], accB[3]);
+#pragma unroll
+        for (int vb = 0; vb < NVB; ++vb) {
+            uint32_t x0, x1;
+            int kh, kl;
+            float ia, ib;
+            rec_frag(r, vb, j, gl, lane, x0, x1);
+            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
+            int da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
+            mma_s8s8(wa[0], wa[1], wa[2], wa[3], x0, x1, da);
+            mma_s8s8(wb[0], wb[1], wb[2], wb[3], x0, x1, db);
+            acc[vb][0] = fmaf(e0 * ia, (float)(da[0] * 256 + da[1]), acc[vb][0]);
+            acc[vb][1] = fmaf(e1 * ia, (float)(da[2] * 256 + da[3]), acc[vb][1]);
+            acc[vb][2] = fmaf(e2 * ia, (float)(db[0] * 256 + db[1]), acc[vb][2]);
+            acc[vb][3] = fmaf(e3 * ia, (float)(db[2] * 256 + db[3]), acc[vb][3]);
+        }
     }
 }
 
-template <int FMT>
-__device__ __forceinline__ void unit_f16(uint32_t sl, const XFrag& x, int gl, int lane, float (&accA)[4],
-                                         float (&accB)[4]) {
-    if (FMT == Q4M_Q4_K) unit_f16_q4k(sl, x, gl, lane, accA, accB);
-    else if (FMT == Q4M_Q6_K) unit_f16_q6k(sl, x, gl, lane, accA, accB);
-    else if (FMT == Q4M_Q8_0) unit_f16_q80(sl, x, gl, lane, accA, accB);
-    else unit_f16_q40(sl, x, gl, lane, accA, accB);
+template <int FMT, int NVB>
+__device__ __forceinline__ void unit_multi(uint32_t sl, const MultiRec& r, int gl, int lane, float (&acc)[NVB][4]) {
+    if (FMT == Q4M_Q4_K) unit_multi_q4k<NVB>(sl, r, gl, lane, acc);
+    else if (FMT == Q4M_Q6_K) unit_multi_q6k<NVB>(sl, r, gl, lane, acc);
+    else if (FMT == Q4M_Q8_0) unit_multi_q80<NVB>(sl, r, gl, lane, acc);
+    else unit_multi_q40<NVB>(sl, r, gl, lane, acc);
 }
 
 // Input of vector v at elements 4 i .. 4 i + 3 (zero past cols).
@@ -370,17 +330,6 @@ __device__ __forceinline__ float4 multi_load(const MultiParams& p, int v, int i,
         h = make_float4(h.x * g.x, h.y * g.y, h.z * g.z, h.w * g.w);
     }
     return h;
-}
-
-// The power of two s that puts a positive maximum in [2^13, 2^14) (1 for a zero maximum):
-// scaled by s, the vector's fp16 values keep 11 significant bits and stay far below the
-// fp16 maximum.
-__device__ __forceinline__ float pow2_scale(float amax) {
-    if (!(amax > 0.f)) return 1.0f;
-    int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu) - 127;  // amax in [2^e, 2^(e+1)) (normal)
-    e = 13 - e;
-    e = e > 126 ? 126 : e < -126 ? -126 : e;
-    return __uint_as_float((uint32_t)(e + 127) << 23);
 }
 
 // Epilogue of rows (row, row + 1) of tile pair q for vector v, values v0, v1 (valid: v < n).
@@ -427,8 +376,7 @@ __device__ __forceinline__ void multi_epilogue(const MultiParams& p, int q, int 
     epilogue_pair(ea, row, v0, v1, lmax, lidx);
 }
 
-
-template <int XM, int EPI, int FMT>
+template <int XM, int EPI, int FMT, int NVB>
 __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     constexpr int UB = q4m_unit_bytes(FMT);
     constexpr int NB = multi_nbuf(FMT);  // ring slots per warp
@@ -438,15 +386,15 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     const int kp = blockIdx.x % kw, cidx = blockIdx.x / kw;
     const int cg = ((int)gridDim.x - kp + kw - 1) / kw;  // CTAs of part kp
     const int g0 = kp * G / kw, g1 = (kp + 1) * G / kw, ng = g1 - g0;
-    const int xsb = multi_xs_stride(gk);
-    uint8_t* xs = smem_m;                                                     // [n][xsb] fp16 input records
-    float* sblk = reinterpret_cast<float*>(xs + (size_t)n * xsb);             // [gk * 4][MULTI_MAX] block sums
-    float* ep = reinterpret_cast<float*>(smem_m + multi_xs_bytes(n, gk));    // [MNW][MULTI_MAX][EP_STRIDE]
-    float* fac = ep + MNW * MULTI_MAX * EP_STRIDE;  // [v] norm factor, [8 + v] 1 / s, [16 + v] max, [24 + v] s
-    u64* keys = reinterpret_cast<u64*>(fac + 64);                            // [MNW][MULTI_MAX]
-    float* fin = reinterpret_cast<float*>(keys + MNW * MULTI_MAX);          // [MULTI_MAX][EP_STRIDE]
+    uint8_t* rec = smem_m;
+    uint32_t* dig = reinterpret_cast<uint32_t*>(rec);
+    float4* prm = reinterpret_cast<float4*>(rec + (size_t)n * multi_dig_stride(gk));
+    float* ep = reinterpret_cast<float*>(rec + multi_rec_bytes(n, gk));  // [MNW][MULTI_MAX][EP_STRIDE]
+    float* fac = ep + MNW * MULTI_MAX * EP_STRIDE;                       // [MULTI_MAX] (64 floats)
+    u64* keys = reinterpret_cast<u64*>(fac + 64);                        // [MNW][MULTI_MAX]
+    float* fin = reinterpret_cast<float*>(keys + MNW * MULTI_MAX);      // [MULTI_MAX][EP_STRIDE]
     int* flag = reinterpret_cast<int*>(fin + MULTI_MAX * EP_STRIDE);
-    const uint32_t ring = smem_u32(smem_m + multi_xs_bytes(n, gk) + MULTI_EP_BYTES) + (uint32_t)(warp * NB * UB);
+    const uint32_t ring = smem_u32(rec + multi_rec_bytes(n, gk) + MULTI_EP_BYTES) + (uint32_t)(warp * NB * UB);
     float* eps_w = ep + warp * MULTI_MAX * EP_STRIDE;
 
     // ---------------- weight stream: per warp, pairs cidx + cg (warp + MNW i) of K part kp,
@@ -481,15 +429,14 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     pdl_trigger();
 
     // ---------------- prologue: norm factors (warp v < n adds vector v's partial sums of
-    // squares, eight loads in flight per lane, then a fixed shuffle tree); the part's inputs as
-    // fp16, each vector scaled by the power of two of its part's maximum (two passes over the
-    // items (vector, group), a warp's loads of up to 8 items issued before any is used)
-    if (tid < MULTI_MAX) reinterpret_cast<int*>(fac)[16 + tid] = 0;
+    // squares: lane l the parts l, l + 32, ..., then a fixed shuffle tree), then the part's
+    // records (one group of one vector per warp pass: lane l converts block l / 8, elements
+    // 4 (l % 8) .. +3)
     if (warp < MULTI_MAX) {
         float f = 1.0f;
         if (XM == MX_NORMED && warp < n) {
             float ss = 0.f;
-            for (int q0 = lane; q0 < p.ssq_parts; q0 += 8 * 32) {
+            for (int q0 = lane; q0 < p.ssq_parts; q0 += 8 * 32) {  // eight loads in flight
                 float t[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -505,9 +452,10 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         }
         if (lane == 0) fac[warp] = f;
     }
-    __syncthreads();
+    // a warp issues the loads of up to 8 of its items before converting any, so it pays one
+    // L2 round trip per 8 items, not one per item
     const int n4 = p.cols / 4, items = n * ng;
-    for (int base = warp; base < items; base += 8 * MNW) {  // pass 1: the maxima
+    for (int base = warp; base < items; base += 8 * MNW) {
         float4 x4[8];
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
@@ -516,71 +464,22 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         }
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
-            const int it = base + b * MNW;  // warp-uniform
-            if (it >= items) break;
-            float m = fmaxf(fmaxf(fabsf(x4[b].x), fabsf(x4[b].y)), fmaxf(fabsf(x4[b].z), fabsf(x4[b].w)));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(JINF_FULL_MASK, m, o));
-            if (lane == 0) atomicMax(reinterpret_cast<int*>(fac) + 16 + it / ng, __float_as_int(m));
-        }
-    }
-    __syncthreads();
-    if (tid < n) {
-        const float s = pow2_scale(__int_as_float(reinterpret_cast<int*>(fac)[16 + tid]));
-        fac[24 + tid] = s;
-        fac[8 + tid] = 1.0f / s;  // a power of two: exact
-    }
-    __syncthreads();
-    for (int base = warp; base < items; base += 8 * MNW) {  // pass 2: scaled fp16 inputs
-        float4 x4[8];
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            const int it = base + b * MNW;
-            if (it < items) x4[b] = multi_load<XM>(p, it / ng, (g0 + it % ng) * 32 + lane, n4);
-        }
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            const int it = base + b * MNW;
+            const int it = base + b * MNW;  // warp-uniform: the conversion's shuffles see every lane
             if (it >= items) break;
             const int v = it / ng, gl = it % ng;
-            const float s = fac[24 + v];
-            const float e0 = x4[b].x * s, e1 = x4[b].y * s, e2 = x4[b].z * s, e3 = x4[b].w * s;
-            const __half2 h01 = __floats2half2_rn(e0, e1), h23 = __floats2half2_rn(e2, e3);
-            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-            const __half2 l01 = __floats2half2_rn(e0 - f01.x, e1 - f01.y), l23 = __floats2half2_rn(e2 - f23.x, e3 - f23.y);
-            *reinterpret_cast<uint4*>(xs + (size_t)v * xsb + (size_t)(gl * 32 + lane) * 16) =
-                make_uint4(as_u(h01), as_u(h23), as_u(l01), as_u(l23));
-            // the block's sum (lanes 8 i .. 8 i + 7 hold block i of the group)
-            float bs = (e0 + e1) + (e2 + e3);
-            bs += __shfl_xor_sync(JINF_FULL_MASK, bs, 1);
-            bs += __shfl_xor_sync(JINF_FULL_MASK, bs, 2);
-            bs += __shfl_xor_sync(JINF_FULL_MASK, bs, 4);
-            if ((lane & 7) == 0) sblk[(gl * 4 + (lane >> 3)) * MULTI_MAX + v] = bs;
+            octet_to_records(x4[b], lane, lane >> 3, dig + (v * multi_dig_stride(gk) + gl * 256) / 4,
+                             prm + (v * multi_prm_stride(gk) + gl * 64) / 16);
         }
     }
     __syncthreads();
-    const int gr = lane >> 2, c = lane & 3;
-    const XFrag xf{smem_u32(xs) + (uint32_t)(gr * xsb + 16 * c), smem_u32(sblk) + (uint32_t)(8 * c), gr < n};
-    // a lane's sums -> the warp's staging block (true scale): rows gr, gr + 8, 16 + gr, 24 + gr of
-    // vector columns 2c, 2c + 1
-    auto stage_rows = [&](const float (&aA)[4], const float (&aB)[4]) {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int v = 2 * c + h;
-            if (v < n) {
-                const float is = fac[8 + v];
-                eps_w[v * EP_STRIDE + gr] = aA[h] * is;
-                eps_w[v * EP_STRIDE + gr + 8] = aA[2 + h] * is;
-                eps_w[v * EP_STRIDE + gr + 16] = aB[h] * is;
-                eps_w[v * EP_STRIDE + gr + 24] = aB[2 + h] * is;
-            }
-        }
-    };
+    const MultiRec mr{smem_u32(dig), smem_u32(prm), multi_dig_stride(gk), multi_prm_stride(gk), n};
+
     // ---------------- main loop
-    float lmax[4];
-    int lidx[4];
+    const int gr = lane >> 2, c = lane & 3;
+    float lmax[2 * NVB];
+    int lidx[2 * NVB];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < 2 * NVB; ++k) {
         lmax[k] = -INFINITY;
         lidx[k] = 0;
     }
@@ -588,16 +487,26 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     if (local) {
         // ---------------- per CTA: all warps on one pair, each its groups [lg0, lg1)
         for (int q = cidx; q < p.pairs; q += cg) {
-            float accA[4] = {0.f, 0.f, 0.f, 0.f}, accB[4] = {0.f, 0.f, 0.f, 0.f};
+            float acc[NVB][4];
+#pragma unroll
+            for (int vb = 0; vb < NVB; ++vb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[vb][i] = 0.f;
             for (int gl = lg0; gl < lg1; ++gl) {
                 issue(slot == 0 ? NB - 1 : slot - 1);
                 asm volatile("cp.async.wait_group %0;" ::"n"(NB - 1) : "memory");
                 __syncwarp();  // scale words are read across lanes
-                unit_f16<FMT>(ring + slot * UB, xf, gl, lane, accA, accB);
+                unit_multi<FMT, NVB>(ring + slot * UB, mr, gl, lane, acc);
                 __syncwarp();  // every lane's reads of the slot precede the next copy into it
                 slot = slot + 1 == NB ? 0 : slot + 1;
             }
-            stage_rows(accA, accB);
+#pragma unroll
+            for (int vb = 0; vb < NVB; ++vb) {
+                const int v = 4 * vb + c;
+                if (v < n)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) eps_w[v * EP_STRIDE + gr + 8 * i] = acc[vb][i];
+            }
             __syncthreads();
             // the warps' pieces in warp order (warps without groups wrote zeros)
             if (tid < n * 32) {
@@ -648,16 +557,28 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         }
     }
     for (int q = local ? p.pairs : cidx + cg * warp; q < p.pairs && ng > 0; q += wstep) {
-        float accA[4] = {0.f, 0.f, 0.f, 0.f}, accB[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc[NVB][4];
+#pragma unroll
+        for (int vb = 0; vb < NVB; ++vb)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[vb][i] = 0.f;
         for (int gl = 0; gl < ng; ++gl) {
             issue(slot == 0 ? NB - 1 : slot - 1);
             asm volatile("cp.async.wait_group %0;" ::"n"(NB - 1) : "memory");
             __syncwarp();  // scale words are read across lanes
-            unit_f16<FMT>(ring + slot * UB, xf, gl, lane, accA, accB);
+            unit_multi<FMT, NVB>(ring + slot * UB, mr, gl, lane, acc);
             __syncwarp();  // every lane's reads of the slot precede the next copy into it
             slot = slot + 1 == NB ? 0 : slot + 1;
         }
-        stage_rows(accA, accB);
+        // the pair's rows to the warp's staging block: lane (gr, c) holds vector 4 vb + c,
+        // rows gr + 8 i
+#pragma unroll
+        for (int vb = 0; vb < NVB; ++vb) {
+            const int v = 4 * vb + c;
+            if (v < n)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) eps_w[v * EP_STRIDE + gr + 8 * i] = acc[vb][i];
+        }
         __syncwarp();
         if (kw > 1) {
             float* pt = p.part + ((size_t)q * kw + kp) * n * 32;
@@ -690,7 +611,7 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         // 2 k + lane / 16, k = 0 .. ceil(n / 2) - 1
         const int qq = lane & 15;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 2 * NVB; ++k) {
             if (2 * k >= n) break;
             const int v = 2 * k + (lane >> 4);
             const bool valid = v < n;
@@ -706,7 +627,7 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         // per vector: the warp's argmax (first index wins on ties), then the CTA's, then one
         // atomicMax per CTA and vector
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 2 * NVB; ++k) {
             if (2 * k >= n) break;
             const int v = 2 * k + (lane >> 4);
             u64 key = lmax[k] == -INFINITY ? 0ull : argmax_key(lmax[k], lidx[k] + p.vocab_offset);
@@ -779,13 +700,13 @@ cudaError_t launch_rows(const float* table, const MultiState* ms, float* h, cons
 
 // ---------------------------------------------------------------- dispatch
 
-template <int XM, int EPI, int FMT>
+template <int XM, int EPI, int FMT, int NVB>
 cudaError_t launch_multi_t(const MultiParams& p, int grid, cudaStream_t s, bool pdl) {
     const size_t smem = multi_smem(p.n, p.gk, FMT);
     static size_t configured = 0;
     if (smem > configured) {
         const cudaError_t e =
-            cudaFuncSetAttribute(k_gemv_multi<XM, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            cudaFuncSetAttribute(k_gemv_multi<XM, EPI, FMT, NVB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         configured = smem;
     }
@@ -799,18 +720,23 @@ cudaError_t launch_multi_t(const MultiParams& p, int grid, cudaStream_t s, bool 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_gemv_multi<XM, EPI, FMT>, p);
+    return cudaLaunchKernelEx(&cfg, k_gemv_multi<XM, EPI, FMT, NVB>, p);
+}
+
+template <int XM, int EPI, int FMT>
+cudaError_t launch_multi_n(const MultiParams& p, int grid, cudaStream_t s, bool pdl) {
+    return p.n <= 4 ? launch_multi_t<XM, EPI, FMT, 1>(p, grid, s, pdl) : launch_multi_t<XM, EPI, FMT, 2>(p, grid, s, pdl);
 }
 
 template <int FMT>
 cudaError_t launch_multi_f(const MultiParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl) {
     switch (xm * 16 + epi) {
-        case MX_PLAIN_F32 * 16 + ME_STORE: return launch_multi_t<MX_PLAIN_F32, ME_STORE, FMT>(p, grid, s, pdl);
-        case MX_PLAIN_F16 * 16 + ME_STORE: return launch_multi_t<MX_PLAIN_F16, ME_STORE, FMT>(p, grid, s, pdl);
-        case MX_PLAIN_F32 * 16 + ME_RESID: return launch_multi_t<MX_PLAIN_F32, ME_RESID, FMT>(p, grid, s, pdl);
-        case MX_NORMED * 16 + ME_QKV: return launch_multi_t<MX_NORMED, ME_QKV, FMT>(p, grid, s, pdl);
-        case MX_NORMED * 16 + ME_GATEUP: return launch_multi_t<MX_NORMED, ME_GATEUP, FMT>(p, grid, s, pdl);
-        case MX_NORMED * 16 + ME_LMHEAD: return launch_multi_t<MX_NORMED, ME_LMHEAD, FMT>(p, grid, s, pdl);
+        case MX_PLAIN_F32 * 16 + ME_STORE: return launch_multi_n<MX_PLAIN_F32, ME_STORE, FMT>(p, grid, s, pdl);
+        case MX_PLAIN_F16 * 16 + ME_STORE: return launch_multi_n<MX_PLAIN_F16, ME_STORE, FMT>(p, grid, s, pdl);
+        case MX_PLAIN_F32 * 16 + ME_RESID: return launch_multi_n<MX_PLAIN_F32, ME_RESID, FMT>(p, grid, s, pdl);
+        case MX_NORMED * 16 + ME_QKV: return launch_multi_n<MX_NORMED, ME_QKV, FMT>(p, grid, s, pdl);
+        case MX_NORMED * 16 + ME_GATEUP: return launch_multi_n<MX_NORMED, ME_GATEUP, FMT>(p, grid, s, pdl);
+        case MX_NORMED * 16 + ME_LMHEAD: return launch_multi_n<MX_NORMED, ME_LMHEAD, FMT>(p, grid, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -69,7 +69,7 @@ struct MultiParams {
     uint64_t pf_bytes;
 };
 
-// How an n-vector GEMV of this shape runs on `grid` CTAs: the K parts (the part's inputs
+// How an n-vector GEMV of this shape runs on `grid` CTAs: the K parts (the part's records
 // within shared memory next to the weight rings) and whether a CTA's warps split each tile
 // pair (*local), by the smallest estimated time; kw 0 when no split fits.
 void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int* kw, int* local);
