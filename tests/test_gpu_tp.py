@@ -165,3 +165,71 @@ def test_tp2_from_b200_layout_shards(tmp_path, persistent):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
+
+
+def _rank_multi_main(rank, world, nccl_id, shape_args, prompts, n_greedy, out_q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "jetson-inference_b200"))
+    try:
+        import jinf
+        torch.cuda.set_device(rank)
+        syn = jinf.SynthModel(jinf.LlamaShape(*shape_args), seed=0)
+        opts = jinf.b200_options(device=rank, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
+                                 max_seqs=len(prompts))
+        eng = jinf.Engine.from_synth(syn, max_context=64, options=opts)
+        seqs = list(range(len(prompts)))
+        toks = []
+        for t in range(len(prompts[0])):
+            toks.append(eng.decode_batch(seqs, [p[t] for p in prompts]))
+        for _ in range(n_greedy):
+            toks.append(eng.decode_batch(seqs, toks[-1]))
+        eng.close()
+        out_q.put((rank, "ok", toks))
+    except Exception as e:  # reported to the parent, which fails the test
+        out_q.put((rank, "error", repr(e)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_tp2_multi_sequence_greedy_tokens():
+    """The multi-sequence step on 2 GPUs (row-split partial outputs summed by NCCL, argmax keys
+    max-reduced): three sequences' greedy tokens, identical on both ranks and equal to each
+    sequence's own oracle decode."""
+    import jinf
+    shape_args = (2, 512, 8, 2, 1408, 4096, 1e4)
+    rng = np.random.default_rng(7)
+    prompts = [[int(t) for t in rng.integers(0, 4096, size=6)] for _ in range(3)]
+    n_greedy = 8
+    nccl_id = jinf.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_multi_main, args=(r, WORLD, nccl_id, shape_args, prompts, n_greedy, q))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(WORLD):
+            rank, status, toks = q.get(timeout=300)
+            assert status == "ok", f"rank {rank}: {toks}"
+            res[rank] = toks
+    except queue.Empty:
+        pytest.fail("a tensor-parallel rank did not report within 300 s")
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[0] == res[1]
+    syn = jinf.SynthModel(jinf.LlamaShape(*shape_args), seed=0)
+    for i, pr in enumerate(prompts):
+        orc = oracle.OracleModel(syn, max_ctx=64, kv_f16=True)
+        want = None
+        for t in pr:
+            want = orc.forward(t)
+        steps = len(pr) - 1
+        assert res[0][steps][i] == oracle.argmax(want), f"sequence {i} after its prompt"
+        for k in range(n_greedy):
+            want = orc.forward(res[0][steps + k][i])
+            assert res[0][steps + k + 1][i] == oracle.argmax(want), f"sequence {i} step {k}"
+        orc.close()
