@@ -15,7 +15,7 @@
 //   warp 0 (one lane)  copies the stage's four raw 2304-byte Q4M units (cp.async.bulk) and
 //                      the two 64-column boxes of X (TMA tiled load, 128B swizzle) into
 //                      shared memory, completing on the stage's `full` mbarrier;
-//   warps 2..7         dequantise the raw units into the fp16 A tile (K-major, 128B swizzle,
+//   warps 2..15        dequantise the raw units into the fp16 A tile (K-major, 128B swizzle,
 //                      the canonical UMMA layout), then arrive on `aready`;
 //   warp 1             allocates 128 TMEM columns; one lane issues 8 tcgen05.mma (M 128,
 //                      N 128, K 16, f16 x f16 -> f32) per stage and commits each stage's MMAs
@@ -35,12 +35,12 @@
 namespace jinf {
 namespace {
 
-constexpr int PG_BM = 128, PG_BN = 128, PG_BK = 128, PG_STAGES = 3, PG_THREADS = 256;
+constexpr int PG_BM = 128, PG_BN = 128, PG_BK = 128, PG_STAGES = 3, PG_THREADS = 512;
 constexpr int PG_ATOM = 16384;                        // one 64-column swizzle atom of a 128-row tile
 constexpr int PG_A_BYTES = 2 * PG_ATOM;               // 128 rows x 128 columns fp16
 constexpr int PG_B_BYTES = 2 * PG_ATOM;               // 128 tokens x 128 columns fp16
 constexpr int PG_RAW_BYTES = 4 * Q4M_UNIT;            // four tile pairs of one group
-constexpr int PG_DQ_THREADS = 192;                    // warps 2..7
+constexpr int PG_DQ_THREADS = 448;                    // warps 2..15
 constexpr unsigned long long PG_SPIN = 1ull << 22;    // polls of a wait before it gives up
 
 // shared memory offsets from the 1024-aligned base
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
             }
         }
     } else {
-        // ---- dequantisation (warps 2..7)
+        // ---- dequantisation (warps 2..15)
         const int t = tid - 64;
         for (int kt = 0; kt < groups; ++kt) {
             const int s = kt % PG_STAGES;
@@ -263,7 +263,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1)
             mb_arrive(b_aready + 8 * s);
         }
         // ---- epilogue (warps 4..7: TMEM lane quarter warp % 4)
-        if (warp >= 4) {
+        if (warp >= 4 && warp < 8) {
             const bool ok = !*(volatile int*)abort_flag && mb_wait(b_acc, 0);
             if (!ok) {
                 fail();
