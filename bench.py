@@ -120,6 +120,9 @@ def dist_env():
 def init_dist(world):
     if world == 1:
         return None
+    # the engine's communicator is NCCL's: keep its version banner off stdout, where rank 0's
+    # JSON line is the only output
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     import datetime
     import torch.distributed as dist
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))

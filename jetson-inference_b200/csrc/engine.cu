@@ -158,7 +158,7 @@ struct NvmwSource : ModelSource {
             const std::string p(part);
             const std::string pre = "blk." + std::to_string(l) + ".";
             if (p == "attn_q" || p == "attn_k") img = pre + "qkv.q4m";
-            else if (p == "attn_v") img = jinf_nvmw_find_tensor(r, (pre + "v.q4m").c_str()) ? pre + "v.q4m" : pre + "qkv.q4m";
+            else if (p == "attn_v") img = jinf_nvmw_find_tensor(r, (pfx + pre + "v.q4m").c_str()) ? pre + "v.q4m" : pre + "qkv.q4m";
             else if (p == "attn_output") img = pre + "o.q4m";
             else if (p == "ffn_gate" || p == "ffn_up") img = pre + "gu.q4m";
             else if (p == "ffn_down") img = pre + "down.q4m";
