@@ -81,8 +81,8 @@ cudaError_t multi_gemv_launch(const MultiParams& p, int xm, int epi, int grid, c
 // Decode attention of a multi-sequence step (step_kernel.cu: the persistent step's attention
 // split, one kernel per layer): vector v's query heads over positions 0 .. ms->pos[v] of
 // sequence ms->seq[v]'s cache, the positions of each (vector, kv head) split over up to s_max
-// CTAs of 16 warps (one per MULTI_ATTN_SPAN positions: enough blocks of 64 per CTA to pay for its fixed cost), the splits merged in order by the
-// last CTA to finish.
+// CTAs of 16 warps (one per MULTI_ATTN_SPAN positions: enough 64-position blocks per CTA to
+// pay for its fixed cost), the splits merged in order by the last CTA to finish.
 constexpr int MULTI_ATTN_SPAN = 256;
 struct MultiAttnParams {
     const float* q;         // [n][q_stride], RoPE applied
