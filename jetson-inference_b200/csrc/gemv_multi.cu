@@ -425,6 +425,20 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
                 prefetch_l2(p.pf_ptr + off + o, (uint32_t)(len - o < (1ull << 20) ? len - o : (1ull << 20)));
         }
     }
+    if (EPI == ME_QKV && tid == 32 && p.nk > 0) {
+        // the attention after this GEMV reads every vector's cache rows 0 .. pos - 1 of this
+        // layer: bring them into L2 now, one (vector, kv head, K or V) region per CTA. The
+        // positions and sequences of the step were written before the step began.
+        const int nkvh = p.nk / p.head_dim;
+        for (int r = blockIdx.x; r < n * nkvh * 2; r += gridDim.x) {
+            const int v = r / (nkvh * 2), kvh = (r >> 1) % nkvh;
+            const __half* base = ((r & 1) ? p.vcache : p.kcache) + (size_t)p.ms->seq[v] * p.seq_stride +
+                                 (size_t)kvh * p.max_ctx * p.head_dim;
+            const uint32_t bytes = (uint32_t)p.ms->pos[v] * (uint32_t)p.head_dim * 2u;
+            for (uint32_t o = 0; o < bytes; o += (1u << 20))
+                prefetch_l2(reinterpret_cast<const uint8_t*>(base) + o, bytes - o < (1u << 20) ? bytes - o : (1u << 20));
+        }
+    }
     pdl_wait();
     pdl_trigger();
 
