@@ -344,6 +344,8 @@ struct Op {
     MultiParams mp{};    // OP_MGEMV (xm, epi, grid as above)
     MultiAttnParams map{};  // OP_MATTN
     int n_vec = 0;       // multi-sequence ops: vectors of the step
+    uint8_t* rec = nullptr;      // OP_MEMBED, OP_MRESID: records of h * gain for the next GEMV
+    const float* gain = nullptr;
 };
 
 }  // namespace
@@ -463,6 +465,10 @@ struct jinf_engine_impl {
     int32_t* ms_pinned = nullptr;  // [3 * MULTI_MAX] step inputs (token, pos, seq), then [MULTI_MAX] outputs
     float *m_h = nullptr, *m_y = nullptr, *m_q = nullptr, *m_attn = nullptr, *m_act = nullptr, *m_logits = nullptr,
           *m_ssq = nullptr, *m_attn_part = nullptr, *m_part = nullptr;
+    // the GEMV inputs as digit records, written by their producers (n_seqs vectors each): h *
+    // the next norm's gain, and the attention output; null when a width is not a whole number
+    // of 128-element groups (the GEMVs then convert their inputs themselves)
+    uint8_t *m_rec_h = nullptr, *m_rec_a = nullptr;
     unsigned int* m_cnt = nullptr;
     size_t m_part_floats = 0, m_cnt_n = 0;  // their sizes
     int32_t* m_out = nullptr;  // [max_ctx][MULTI_MAX] argmax ids of resident multi steps
@@ -486,8 +492,12 @@ jinf_status run_op(jinf_engine_impl* I, const Op& op, cudaStream_t s) {
         case OP_ATTN: e = attn_launch(op.ap, s, true); break;
         case OP_FINALIZE: k_finalize<<<1, 1, 0, s>>>(I->st, op.with_argmax); e = cudaGetLastError(); break;
         case OP_MGEMV: e = multi_gemv_launch(op.mp, op.xm, op.epi, op.grid, s, true); break;
-        case OP_MEMBED: e = multi_embed_launch(I->embed, I->ms, op.n_vec, I->d, I->m_h, I->m_ssq, s, true); break;
-        case OP_MRESID: e = multi_resid_launch(I->m_h, I->m_y, op.n_vec, I->d, I->m_ssq, s, true); break;
+        case OP_MEMBED:
+            e = multi_embed_launch(I->embed, I->ms, op.n_vec, I->d, I->m_h, I->m_ssq, op.rec, op.gain, s, true);
+            break;
+        case OP_MRESID:
+            e = multi_resid_launch(I->m_h, I->m_y, op.n_vec, I->d, I->m_ssq, op.rec, op.gain, s, true);
+            break;
         case OP_MFINAL: e = multi_finalize_launch(I->ms, op.n_vec, s); break;
         case OP_MATTN: e = multi_attn_launch(op.map, s, true); break;
         case OP_SPARSE_FFN: {
@@ -789,12 +799,25 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
     ops.clear();
     const int d = I->d, nq = I->Hl * I->hd, nk = I->Hkvl * I->hd;
     const bool tp = I->tp_size > 1;
-    auto resid = [&](Op& g) {  // o / down: residual add (one GPU) or partial + allreduce + add
+    const bool rec = I->m_rec_h != nullptr;
+    const int xm_h = rec ? MX_RECORDS : MX_NORMED;  // inputs normalised from h
+    auto from_h = [&](Op& g, const float* gain) {
+        g.mp.x = rec ? static_cast<const void*>(I->m_rec_h) : static_cast<const void*>(I->m_h);
+        g.mp.ldx = d;
+        g.mp.norm_w = gain;
+    };
+    // o / down: residual add (one GPU) or partial + allreduce + add; the new h's records with
+    // the gain of the norm after it
+    auto resid = [&](Op& g, const float* next_gain) {
         if (!tp) {
             g.epi = ME_RESID;
             g.mp.y = I->m_h;
             g.mp.ldy = d;
             g.mp.ssq_out = I->m_ssq;
+            if (rec) {
+                g.mp.rec_out = I->m_rec_h;
+                g.mp.gain_out = next_gain;
+            }
             ops.push_back(g);
             return;
         }
@@ -808,22 +831,28 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
         ops.push_back(ar);
         Op ad{OP_MRESID};
         ad.n_vec = n;
+        if (rec) {
+            ad.rec = I->m_rec_h;
+            ad.gain = next_gain;
+        }
         ops.push_back(ad);
     };
     Op em{OP_MEMBED};
     em.n_vec = n;
+    if (rec) {
+        em.rec = I->m_rec_h;
+        em.gain = I->layers[0].attn_norm;
+    }
     ops.push_back(em);
     for (int L = 0; L < I->L; ++L) {
         const auto& ly = I->layers[L];
         __half* kc = I->kc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
         __half* vc = I->vc + (size_t)L * I->Hkvl * I->max_ctx * I->hd;
-        Op qkv = multi_gemv_op(I, n, ly.qkv, ly.qkv_sh, MX_NORMED, ME_QKV);
+        Op qkv = multi_gemv_op(I, n, ly.qkv, ly.qkv_sh, xm_h, ME_QKV);
         qkv.role = ROLE_QKV;
         qkv.layer = L;
         MultiParams& qp = qkv.mp;
-        qp.x = I->m_h;
-        qp.ldx = d;
-        qp.norm_w = ly.attn_norm;
+        from_h(qkv, ly.attn_norm);
         qp.y = I->m_q;
         qp.ldy = nq;
         qp.kcache = kc;
@@ -838,7 +867,7 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
         qp.pf_bytes = ly.v ? ly.v_sh.bytes : ly.o_sh.bytes;
         ops.push_back(qkv);
         if (ly.v) {  // v of another weight type: every row a v row
-            Op v = multi_gemv_op(I, n, ly.v, ly.v_sh, MX_NORMED, ME_QKV);
+            Op v = multi_gemv_op(I, n, ly.v, ly.v_sh, xm_h, ME_QKV);
             v.mp = qp;
             v.mp.w = ly.v;
             v.mp.rows = ly.v_sh.rows;
@@ -871,23 +900,23 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
         at.map.max_ctx = I->max_ctx;
         at.map.s_max = I->m_split;
         at.map.ms = I->ms;
+        at.map.rec = rec ? I->m_rec_a : nullptr;
         ops.push_back(at);
 
-        Op o = multi_gemv_op(I, n, ly.o, ly.o_sh, MX_PLAIN_F32, ME_RESID);
+        Op o = multi_gemv_op(I, n, ly.o, ly.o_sh, rec ? MX_RECORDS : MX_PLAIN_F32, ME_RESID);
         o.role = ROLE_O;
         o.layer = L;
-        o.mp.x = I->m_attn;
+        o.mp.x = rec ? static_cast<const void*>(I->m_rec_a) : static_cast<const void*>(I->m_attn);
         o.mp.ldx = nq;
+        o.mp.ssq = nullptr;  // plain values: no norm factor
         o.mp.pf_ptr = ly.gu;
         o.mp.pf_bytes = ly.gu_sh.bytes;
-        resid(o);
+        resid(o, ly.ffn_norm);
 
-        Op gu = multi_gemv_op(I, n, ly.gu, ly.gu_sh, MX_NORMED, ME_GATEUP);
+        Op gu = multi_gemv_op(I, n, ly.gu, ly.gu_sh, xm_h, ME_GATEUP);
         gu.role = ROLE_GATEUP;
         gu.layer = L;
-        gu.mp.x = I->m_h;
-        gu.mp.ldx = d;
-        gu.mp.norm_w = ly.ffn_norm;
+        from_h(gu, ly.ffn_norm);
         gu.mp.y = I->m_act;
         gu.mp.ldy = I->ffl;
         gu.mp.pf_ptr = ly.down;
@@ -901,13 +930,11 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
         dn.mp.ldx = I->ffl;
         dn.mp.pf_ptr = L + 1 < I->L ? I->layers[L + 1].qkv : I->lm;
         dn.mp.pf_bytes = L + 1 < I->L ? I->layers[L + 1].qkv_sh.bytes : I->lm_sh.bytes;
-        resid(dn);
+        resid(dn, L + 1 < I->L ? I->layers[L + 1].attn_norm : I->out_norm);
     }
-    Op lm = multi_gemv_op(I, n, I->lm, I->lm_sh, MX_NORMED, ME_LMHEAD);
+    Op lm = multi_gemv_op(I, n, I->lm, I->lm_sh, xm_h, ME_LMHEAD);
     lm.role = ROLE_LM;
-    lm.mp.x = I->m_h;
-    lm.mp.ldx = d;
-    lm.mp.norm_w = I->out_norm;
+    from_h(lm, I->out_norm);
     lm.mp.y = I->m_logits;
     lm.mp.ldy = I->Vl;
     lm.mp.vocab_offset = I->vocab_off;
@@ -1378,7 +1405,7 @@ void free_impl(jinf_engine_impl* I) {
                     I->pf_att, I->pf_sc, I->pf_x16, I->pf_q16, I->pf_err, I->bundles, I->pred_w1,
                     I->pred_w2, I->sparse_ids, I->sparse_offs, I->sparse_x, I->sparse_scratch, I->gate_up_tmp,
                     I->ms, I->m_h, I->m_y, I->m_q, I->m_attn, I->m_act, I->m_logits, I->m_ssq, I->m_attn_part,
-                    I->m_part, I->m_cnt, I->m_out};
+                    I->m_part, I->m_cnt, I->m_out, I->m_rec_h, I->m_rec_a};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     if (I->logits_full && I->logits_full != I->logits) cudaFree(I->logits_full);
@@ -1876,6 +1903,9 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
                    cudaMalloc(&I->m_part, sizeof(float) * std::max(ws, (size_t)1)) == cudaSuccess &&
                    cudaMalloc(&I->m_cnt, sizeof(unsigned int) * std::max(pairs, (size_t)1)) == cudaSuccess &&
                    cudaMalloc(&I->m_out, sizeof(int32_t) * (size_t)I->max_ctx * MULTI_MAX) == cudaSuccess;
+        if (mok && d % Q4M_KG == 0 && nq % Q4M_KG == 0)
+            mok = cudaMalloc(&I->m_rec_h, (size_t)S * xrec_bytes(d / Q4M_KG)) == cudaSuccess &&
+                  cudaMalloc(&I->m_rec_a, (size_t)S * xrec_bytes(nq / Q4M_KG)) == cudaSuccess;
         if (!mok) return fail(JINF_ERR_OOM);
         cudaMemset(I->ms, 0, sizeof(MultiState));
         cudaMemset(I->m_cnt, 0, sizeof(unsigned int) * std::max(pairs, (size_t)1));

@@ -340,17 +340,36 @@ __device__ __forceinline__ void multi_epilogue(const MultiParams& p, int q, int 
                                                float v1, float& lmax, int& lidx) {
     const int row = q * Q4M_PAIR_ROWS + 2 * qq;
     if (EPI == ME_RESID) {
-        float s2 = 0.f;
+        float s2 = 0.f, h0v = 0.f, h1v = 0.f;
         if (valid) {  // rows = the residual width (a multiple of 32): every row exists
             float* hy = p.y + (size_t)v * p.ldy + row;
-            const float h0 = hy[0] + v0, h1 = hy[1] + v1;
-            hy[0] = h0;
-            hy[1] = h1;
-            s2 = fmaf(h0, h0, h1 * h1);
+            h0v = hy[0] + v0;
+            h1v = hy[1] + v1;
+            hy[0] = h0v;
+            hy[1] = h1v;
+            s2 = fmaf(h0v, h0v, h1v * h1v);
         }
 #pragma unroll
         for (int o = 1; o < 16; o <<= 1) s2 += __shfl_xor_sync(JINF_FULL_MASK, s2, o);
         if (valid && qq == 0) p.ssq_out[(size_t)q * p.n + v] = s2;
+        if (p.rec_out) {
+            // the pair is block q of the next GEMV's input: its records of h * gain_out. Octet
+            // lane L of lanes 0..7 (vector 2k) and 8..15 (vector 2k + 1) takes elements 4L .. 4L+3,
+            // the rows of half-warp lanes 2L and 2L + 1
+            const int lane = threadIdx.x & 31, hh = (lane >> 3) & 1, L = lane & 7;
+            const int src = 16 * hh + 2 * L;
+            const float e0 = __shfl_sync(JINF_FULL_MASK, h0v, src), e1 = __shfl_sync(JINF_FULL_MASK, h1v, src);
+            const float e2 = __shfl_sync(JINF_FULL_MASK, h0v, src + 1), e3 = __shfl_sync(JINF_FULL_MASK, h1v, src + 1);
+            const int vv = v - (lane >> 4) + hh;  // v of lane 0 is 2k
+            const bool st = lane < 16 && vv < p.n;
+            float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (st) g = reinterpret_cast<const float4*>(p.gain_out + (size_t)q * Q4M_PAIR_ROWS)[L];
+            const int gout = p.rows / Q4M_KG;
+            uint8_t* base = p.rec_out + (size_t)(st ? vv : 0) * xrec_bytes(gout);
+            octet_to_records(make_float4(e0 * g.x, e1 * g.y, e2 * g.z, e3 * g.w), lane, q & 3,
+                             reinterpret_cast<uint32_t*>(base) + (q >> 2) * 64,
+                             reinterpret_cast<float4*>(base + (size_t)gout * 256) + (q >> 2) * 4, st);
+        }
         return;
     }
     if (!valid) return;
@@ -448,7 +467,7 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     // 4 (l % 8) .. +3)
     if (warp < MULTI_MAX) {
         float f = 1.0f;
-        if (XM == MX_NORMED && warp < n) {
+        if ((XM == MX_NORMED || (XM == MX_RECORDS && p.ssq)) && warp < n) {
             float ss = 0.f;
             for (int q0 = lane; q0 < p.ssq_parts; q0 += 8 * 32) {  // eight loads in flight
                 float t[8];
@@ -466,9 +485,30 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
         }
         if (lane == 0) fac[warp] = f;
     }
+    if (XM == MX_RECORDS) {
+        // records written by the producer (xrec layout per vector, xrec_bytes(G) apart): the
+        // part's digit words and params, 16 bytes per thread and copy
+        const uint8_t* src = reinterpret_cast<const uint8_t*>(p.x);
+        const size_t vstride = xrec_bytes(G);
+        const int dchunks = ng * 16, pchunks = ng * 4;  // 16-byte pieces per vector
+        for (int i = tid; i < n * (dchunks + pchunks); i += MT) {
+            const int v = i / (dchunks + pchunks), r = i % (dchunks + pchunks);
+            const uint8_t* g = src + (size_t)v * vstride;
+            uint32_t dst;
+            if (r < dchunks) {
+                g += (size_t)g0 * 256 + (size_t)r * 16;
+                dst = smem_u32(dig) + (uint32_t)(v * multi_dig_stride(gk) + r * 16);
+            } else {
+                g += (size_t)G * 256 + (size_t)g0 * 64 + (size_t)(r - dchunks) * 16;
+                dst = smem_u32(prm) + (uint32_t)(v * multi_prm_stride(gk) + (r - dchunks) * 16);
+            }
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(g) : "memory");
+        }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+    }
     // a warp issues the loads of up to 8 of its items before converting any, so it pays one
     // L2 round trip per 8 items, not one per item
-    const int n4 = p.cols / 4, items = n * ng;
+    const int n4 = p.cols / 4, items = XM == MX_RECORDS ? 0 : n * ng;
     for (int base = warp; base < items; base += 8 * MNW) {
         float4 x4[8];
 #pragma unroll
@@ -663,15 +703,18 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
 
 // ---------------------------------------------------------------- small steps of the multi step
 
-// One warp per 32-element chunk of a vector: h (+)= source, and the chunk's sum of squares.
+// One warp per 32-element chunk of a vector: h (+)= source, and the chunk's sum of squares;
+// with rec, the chunk is block ch of the next GEMV's input: its digit records of h * gain
+// (octet lane L of lanes 0..7 converts elements 4L .. 4L+3, the values of lanes 4L .. 4L+3).
 __global__ void k_multi_rows(const float* __restrict__ table, const MultiState* __restrict__ ms, float* h,
-                             const float* __restrict__ y, int n, int d, float* __restrict__ ssq) {
+                             const float* __restrict__ y, int n, int d, float* __restrict__ ssq, uint8_t* rec,
+                             const float* __restrict__ gain) {
     pdl_wait();
     pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int chunks = d / 32;
     const int wid = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (wid >= n * chunks) return;
+    if (wid >= n * chunks) return;  // whole warps: the shuffles below see every lane
     const int v = wid / chunks, ch = wid % chunks;
     const size_t i = (size_t)v * d + ch * 32 + lane;
     float val;
@@ -680,6 +723,16 @@ __global__ void k_multi_rows(const float* __restrict__ table, const MultiState* 
     h[i] = val;
     const float s = warp_sum(val * val);
     if (lane == 0) ssq[(size_t)ch * n + v] = s;
+    if (rec) {
+        const float gv = val * gain[ch * 32 + lane];
+        const int src = 4 * (lane & 7);
+        const float4 e = make_float4(__shfl_sync(JINF_FULL_MASK, gv, src), __shfl_sync(JINF_FULL_MASK, gv, src + 1),
+                                     __shfl_sync(JINF_FULL_MASK, gv, src + 2), __shfl_sync(JINF_FULL_MASK, gv, src + 3));
+        const int G = d / Q4M_KG;
+        uint8_t* base = rec + (size_t)v * xrec_bytes(G);
+        octet_to_records(e, lane, ch & 3, reinterpret_cast<uint32_t*>(base) + (ch >> 2) * 64,
+                         reinterpret_cast<float4*>(base + (size_t)G * 256) + (ch >> 2) * 4, lane < 8);
+    }
 }
 
 __global__ void k_multi_finalize(MultiState* ms, int n) {
@@ -696,9 +749,10 @@ __global__ void k_multi_finalize(MultiState* ms, int n) {
 }
 
 cudaError_t launch_rows(const float* table, const MultiState* ms, float* h, const float* y, int n, int d, float* ssq,
-                        cudaStream_t s, bool pdl) {
+                        uint8_t* rec, const float* gain, cudaStream_t s, bool pdl) {
     if (n < 1 || n > MULTI_MAX || d % 32 || !h || !ssq || (!table && !y) || (table && !ms))
         return cudaErrorInvalidValue;
+    if (rec && (!gain || d % Q4M_KG)) return cudaErrorInvalidValue;
     const int warps = n * (d / 32);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((warps + 7) / 8));
@@ -709,7 +763,7 @@ cudaError_t launch_rows(const float* table, const MultiState* ms, float* h, cons
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_multi_rows, table, ms, h, y, n, d, ssq);
+    return cudaLaunchKernelEx(&cfg, k_multi_rows, table, ms, h, y, n, d, ssq, rec, gain);
 }
 
 // ---------------------------------------------------------------- dispatch
@@ -751,6 +805,10 @@ cudaError_t launch_multi_f(const MultiParams& p, int xm, int epi, int grid, cuda
         case MX_NORMED * 16 + ME_QKV: return launch_multi_n<MX_NORMED, ME_QKV, FMT>(p, grid, s, pdl);
         case MX_NORMED * 16 + ME_GATEUP: return launch_multi_n<MX_NORMED, ME_GATEUP, FMT>(p, grid, s, pdl);
         case MX_NORMED * 16 + ME_LMHEAD: return launch_multi_n<MX_NORMED, ME_LMHEAD, FMT>(p, grid, s, pdl);
+        case MX_RECORDS * 16 + ME_QKV: return launch_multi_n<MX_RECORDS, ME_QKV, FMT>(p, grid, s, pdl);
+        case MX_RECORDS * 16 + ME_GATEUP: return launch_multi_n<MX_RECORDS, ME_GATEUP, FMT>(p, grid, s, pdl);
+        case MX_RECORDS * 16 + ME_LMHEAD: return launch_multi_n<MX_RECORDS, ME_LMHEAD, FMT>(p, grid, s, pdl);
+        case MX_RECORDS * 16 + ME_RESID: return launch_multi_n<MX_RECORDS, ME_RESID, FMT>(p, grid, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -827,7 +885,9 @@ cudaError_t multi_gemv_launch(const MultiParams& p, int xm, int epi, int grid, c
         return cudaErrorInvalidValue;
     if (p.cols % 4 || p.ldx < p.cols) return cudaErrorInvalidValue;
     if (xm == MX_NORMED && (!p.norm_w || !p.ssq || p.ssq_parts < 1)) return cudaErrorInvalidValue;
+    if (xm == MX_RECORDS && (p.cols % Q4M_KG || (p.ssq && p.ssq_parts < 1))) return cudaErrorInvalidValue;
     if (epi == ME_RESID && (!p.ssq_out || p.rows % 32)) return cudaErrorInvalidValue;
+    if (p.rec_out && (epi != ME_RESID || !p.gain_out || p.rows % Q4M_KG)) return cudaErrorInvalidValue;
     if ((epi == ME_QKV || epi == ME_LMHEAD) && !p.ms) return cudaErrorInvalidValue;
     if (p.local && epi == ME_LMHEAD) return cudaErrorInvalidValue;
     if (epi == ME_QKV && (!p.kcache || !p.vcache)) return cudaErrorInvalidValue;
@@ -841,14 +901,15 @@ cudaError_t multi_gemv_launch(const MultiParams& p, int xm, int epi, int grid, c
 }
 
 cudaError_t multi_embed_launch(const float* table, const MultiState* ms, int n, int d, float* h, float* ssq,
-                               cudaStream_t s, bool pdl) {
+                               uint8_t* rec, const float* gain, cudaStream_t s, bool pdl) {
     if (!table) return cudaErrorInvalidValue;
-    return launch_rows(table, ms, h, nullptr, n, d, ssq, s, pdl);
+    return launch_rows(table, ms, h, nullptr, n, d, ssq, rec, gain, s, pdl);
 }
 
-cudaError_t multi_resid_launch(float* h, const float* y, int n, int d, float* ssq, cudaStream_t s, bool pdl) {
+cudaError_t multi_resid_launch(float* h, const float* y, int n, int d, float* ssq, uint8_t* rec, const float* gain,
+                               cudaStream_t s, bool pdl) {
     if (!y) return cudaErrorInvalidValue;
-    return launch_rows(nullptr, nullptr, h, y, n, d, ssq, s, pdl);
+    return launch_rows(nullptr, nullptr, h, y, n, d, ssq, rec, gain, s, pdl);
 }
 
 cudaError_t multi_finalize_launch(MultiState* ms, int n, cudaStream_t s) {

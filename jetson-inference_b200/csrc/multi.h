@@ -32,7 +32,10 @@ struct MultiState {
 // Input of a multi GEMV: fp32 or fp16 vectors x[v][ldx], or MX_NORMED: x = h * gain with the
 // RMSNorm factor of vector v, 1 / sqrt(sum of its ssq partials / cols + eps), applied to the
 // outputs (W (h g r) = r W (h g)).
-enum MultiX { MX_PLAIN_F32 = 0, MX_PLAIN_F16 = 1, MX_NORMED = 2 };
+// MX_RECORDS: x holds the inputs already as digit records (q4m_device.cuh, xrec_bytes(groups)
+// bytes per vector, written by the producer: records of h * gain with ssq set, the RMSNorm
+// factor then applied as for MX_NORMED; of plain values with ssq null).
+enum MultiX { MX_PLAIN_F32 = 0, MX_PLAIN_F16 = 1, MX_NORMED = 2, MX_RECORDS = 3 };
 // Output: ME_STORE y[v][row]; ME_QKV RoPE on the q and k rows at the vector's position, q to
 // y[v], k and v rows into its sequence's cache; ME_GATEUP rows interleaved (gate_n, up_n):
 // y[v][n] = SiLU(gate_n) up_n; ME_LMHEAD y[v][row] and the vector's argmax key; ME_RESID
@@ -55,6 +58,8 @@ struct MultiParams {
     float* y;          // [n][ldy]
     int ldy;
     float* ssq_out;    // ME_RESID: [pairs][n]
+    uint8_t* rec_out;  // ME_RESID, optional: records of h * gain_out for the next GEMV (per vector
+    const float* gain_out;  //   xrec_bytes(rows / 128) bytes apart; one 32-row pair is one block)
     __half* kcache;    // ME_QKV: this layer's K cache of sequence 0 ([n_kv_heads][max_ctx][hd])
     __half* vcache;
     size_t seq_stride;  // elements from one sequence's cache to the next
@@ -92,6 +97,7 @@ struct MultiAttnParams {
     size_t seq_stride;      // elements from one sequence's cache to the next
     float* out;             // [n][q_stride]
     float* part;            // multi_attn_part_floats floats of scratch
+    uint8_t* rec;           // optional: the output's digit records (xrec_bytes(q_stride / 128) per vector)
     int n, n_heads, n_kv_heads, head_dim, max_ctx, s_max;
     MultiState* ms;
 };
@@ -100,11 +106,13 @@ size_t multi_attn_smem_bytes(int group, int head_dim);
 cudaError_t multi_attn_launch(const MultiAttnParams& p, cudaStream_t s, bool pdl);
 
 // h[v] = table[token_v] and its sums of squares per 32 elements (ssq [d / 32][n]).
+// rec (optional): the digit records of h * gain (xrec_bytes(d / 128) bytes per vector).
 cudaError_t multi_embed_launch(const float* table, const MultiState* ms, int n, int d, float* h, float* ssq,
-                               cudaStream_t s, bool pdl);
+                               uint8_t* rec, const float* gain, cudaStream_t s, bool pdl);
 // h[v] += y[v] and the new sums of squares per 32 elements (tensor parallel: after the
 // allreduce of the row-split partial outputs).
-cudaError_t multi_resid_launch(float* h, const float* y, int n, int d, float* ssq, cudaStream_t s, bool pdl);
+cudaError_t multi_resid_launch(float* h, const float* y, int n, int d, float* ssq, uint8_t* rec, const float* gain,
+                               cudaStream_t s, bool pdl);
 // out_token[v] from the argmax keys, which are reset for the next step (and, with feedback,
 // fed back as the next step's tokens, positions advanced).
 cudaError_t multi_finalize_launch(MultiState* ms, int n, cudaStream_t s);

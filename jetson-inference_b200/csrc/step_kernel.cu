@@ -1289,8 +1289,22 @@ __global__ void __launch_bounds__(STEP_THREADS) k_attn_multi(const MultiAttnPara
             }
         }
         const float L = ls[g];
+        const float ox = a.x / L, oy = a.y / L;
         *reinterpret_cast<float2*>(p.out + (size_t)v * p.q_stride + (size_t)(kvh * GQ + g) * HD + 2 * d2) =
-            make_float2(a.x / L, a.y / L);
+            make_float2(ox, oy);
+        if (p.rec) {
+            // a warp holds 64 consecutive outputs (GQ * HD / 2 is a multiple of 32, so whole warps
+            // take each pass), lane l elements 2l, 2l + 1: blocks 2w and 2w + 1, octet lane L of
+            // lanes 0..7 and 8..15 takes elements 4L .. 4L+3 of its block
+            const int lane = tid & 31, hh = (lane >> 3) & 1, src = 16 * hh + 2 * (lane & 7);
+            const float4 e = make_float4(__shfl_sync(JINF_FULL_MASK, ox, src), __shfl_sync(JINF_FULL_MASK, oy, src),
+                                         __shfl_sync(JINF_FULL_MASK, ox, src + 1), __shfl_sync(JINF_FULL_MASK, oy, src + 1));
+            const int G = p.q_stride / Q4M_KG;
+            const int blk = (kvh * GQ * HD + 2 * (o - lane)) / 32 + hh;
+            uint8_t* base = p.rec + (size_t)v * xrec_bytes(G);
+            octet_to_records(e, lane, blk & 3, reinterpret_cast<uint32_t*>(base) + (blk >> 2) * 64,
+                             reinterpret_cast<float4*>(base + (size_t)G * 256) + (blk >> 2) * 4, lane < 16);
+        }
     }
 }
 
@@ -1336,6 +1350,7 @@ cudaError_t multi_attn_launch(const MultiAttnParams& p, cudaStream_t s, bool pdl
         p.n_kv_heads < 1 || p.n_kv_heads > MULTI_MAX_KV_HEADS || p.n_heads % p.n_kv_heads || p.s_max < 1 ||
         p.s_max > 64)
         return cudaErrorInvalidValue;
+    if (p.rec && (p.q_stride % Q4M_KG || p.q_stride < p.n_heads * p.head_dim)) return cudaErrorInvalidValue;
     const int gq = p.n_heads / p.n_kv_heads;
     if (p.head_dim == 64) {
         if (gq == 8) return launch_attn_multi<64, 8>(p, s, pdl);
