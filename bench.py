@@ -29,6 +29,7 @@ Weights are synthetic N(0, 0.02) Q4_0 from seed 0 (no checkpoints): data "synthe
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import subprocess
@@ -117,12 +118,24 @@ def dist_env():
     return rank, world, local
 
 
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """File descriptor 1 points at stderr meanwhile: NCCL prints its version banner on stdout
+    when the engine creates its communicator, and rank 0's JSON line must be the only output."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def init_dist(world):
     if world == 1:
         return None
-    # the engine's communicator is NCCL's: keep its version banner off stdout, where rank 0's
-    # JSON line is the only output
-    os.environ.setdefault("NCCL_DEBUG", "WARN")
     import datetime
     import torch.distributed as dist
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
@@ -388,7 +401,8 @@ def run_ours(args, rank, world, local):
     max_ctx = p0 + args.warmup + args.steps + 8
     opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
                              sparse_mode=args.sparse)
-    eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=opts)
+    with stdout_to_stderr():
+        eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=opts)
     t_load = time.perf_counter() - t_load
     stream = torch.cuda.ExternalStream(eng.h.contents.compute_stream, device=dev)
     prompt = prompt_ids(shape.n_vocab)
@@ -538,7 +552,8 @@ def run_ours_batch(args, rank, world, local):
     max_ctx = p0 + args.warmup + args.steps + 8
     opts = jinf.b200_options(device=local, tp_rank=rank, tp_size=world, nccl_id=nccl_id, eos_token=-1,
                              max_seqs=B)
-    eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=opts)
+    with stdout_to_stderr():
+        eng = jinf.Engine.from_synth(syn, max_context=max_ctx, options=opts)
     t_load = time.perf_counter() - t_load
     stream = torch.cuda.ExternalStream(eng.h.contents.compute_stream, device=dev)
     seqs = list(range(B))
@@ -580,6 +595,8 @@ def run_ours_batch(args, rank, world, local):
     if dist:
         dist.barrier()
     e2e = B * args.steps / all_max(dist, t1 - t0)
+    # per-kernel times of the step (each kind back to back over the layers, after the timed runs)
+    prof = eng.profile_multi(B, reps=2 * shape.n_layers)
 
     wbytes = eng.weight_bytes_per_token()
     kv_seq = 2 * 2 * shape.n_layers * (shape.n_heads_kv // world) * shape.head_dim * (p0 + args.warmup + args.steps / 2)
@@ -599,11 +616,12 @@ def run_ours_batch(args, rank, world, local):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 3 * 8 * 4 + 4,
                     "d2h_bytes_per_step": 4 * B},
             "gpu_launches": launches * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "multi-sequence step (k_gemv_multi + k_attn_f16 graph)",
+            "roofline": {"bound": "hbm", "kernel": "multi-sequence step (k_gemv_multi + k_attn_multi graph)",
                          "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind, "traffic": None,
                          "bytes_per_step": int(step_bytes), "us_per_step": round(1e6 * dev_s / args.steps, 2),
                          "note": "weights once per step + every sequence's KV rows"},
+            "per_op_kernels_us": {k: round(v["us"], 2) for k, v in prof.items()},
             "clocks": clk.summary(),
             "load_s": round(t_load, 1),
         }
@@ -614,13 +632,27 @@ def run_ours_batch(args, rank, world, local):
         dist.destroy_process_group()
 
 
-def profile_case(steps: int) -> None:
+def profile_case(steps: int, batch: int = 1) -> None:
     """The small case of the persistent step for ncu captures: ~0.6 GB of weights plus a
     0.5 GB embedding table; with a 3-token prompt the captured launch `-s 3 -c 1` is the
-    first decode step at position 513."""
+    first decode step at position 513. With batch > 1: the same model's multi-sequence step,
+    `batch` sequences each with its KV cache filled to 512 positions, `steps` resident steps
+    (per step one k_multi_rows, per layer QKV, attention, o, gate|up, down, then the LM head
+    and the finaliser: 4 x 4 + 1 k_gemv_multi launches)."""
     import torch
     import jinf
     shape = jinf.LlamaShape(4, 4096, 32, 8, 14336, 32000, 5e5)
+    if batch > 1:
+        eng = jinf.Engine.from_synth(jinf.SynthModel(shape, seed=0), max_context=600,
+                                     options=jinf.b200_options(eos_token=-1, max_seqs=batch))
+        seqs = list(range(batch))
+        for s in seqs:
+            eng.seq_fill_kv_random(s, 512, seed=1 + s)
+        eng.decode_batch_resident(seqs, [1 + s for s in seqs], steps)
+        torch.cuda.synchronize()
+        eng.close()
+        print("profile case ok")
+        return
     eng = jinf.Engine.from_synth(jinf.SynthModel(shape, seed=0), max_context=600,
                                  options=jinf.b200_options(eos_token=-1))
     eng.forward([1, 2, 3])
@@ -652,10 +684,11 @@ def main():
     ap.add_argument("--profile-case", type=int, default=0, metavar="STEPS",
                     help="run only the small case used for ncu captures of the step kernel and exit: a 4-layer "
                          "8B-shaped model (vocabulary 32000), KV filled to position 512, one forwarded token, "
-                         "then STEPS resident decode steps")
+                         "then STEPS resident decode steps (with --batch B: B sequences through the "
+                         "multi-sequence step)")
     args = ap.parse_args()
     if args.profile_case:
-        profile_case(args.profile_case)
+        profile_case(args.profile_case, args.batch)
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

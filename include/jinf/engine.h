@@ -199,6 +199,10 @@ uint64_t    jinf_engine_weight_bytes_per_token(const jinf_engine* e);
 // down, lm_head, sparse_ffn (sparse modes: the whole FFN of a layer; 0 in dense mode, where
 // gate_up and down are the FFN). bytes receives the algorithmic bytes of one launch of each.
 jinf_status jinf_engine_profile_kernels(jinf_engine* e, int reps, double* times_us, double* bytes);
+// The same for the kernels of an n-vector multi-sequence step (times_us, bytes: 8 entries:
+// QKV, attention, o, gate|up, down, LM head, embedding/residual rows, finaliser). Leaves the
+// sequences' state undefined.
+jinf_status jinf_engine_profile_multi(jinf_engine* e, int n, int reps, double* times_us, double* bytes);
 
 // ---- Multi-sequence decode (new; the reference decodes one sequence) ----
 // Sequences 0 .. max_seqs - 1 each have a KV cache and a position of their own; sequence 0 is

@@ -2516,6 +2516,57 @@ extern "C" uint64_t jinf_engine_weight_bytes_per_token(const jinf_engine* e) {
     return e && e->impl ? e->impl->weight_bytes_token : 0;
 }
 
+// The kernels of an n-vector multi-sequence step, each kind launched back to back over the
+// layers (as jinf_engine_profile_kernels): QKV, attention, o, gate|up, down, LM head, the
+// embedding / residual rows and the finaliser; the exchange steps of tensor parallelism are not
+// timed. Leaves the multi-sequence state undefined (callers reset the sequences afterwards).
+extern "C" jinf_status jinf_engine_profile_multi(jinf_engine* e, int n, int reps, double* times_us, double* bytes) {
+    if (!e || !e->impl || reps <= 0 || !times_us || !bytes || n < 1 || n > e->impl->n_seqs || e->impl->sparse_mode)
+        return JINF_ERR_INVALID;
+    jinf_engine_impl* I = e->impl;
+    JINF_CUDA_CHECK(cudaSetDevice(I->device));
+    if (I->m_ops[n].empty()) build_multi_ops(I, n, I->m_ops[n]);
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    const int roles[6] = {ROLE_QKV, -1, ROLE_O, ROLE_GATEUP, ROLE_DOWN, ROLE_LM};
+    for (int k = 0; k < 8; ++k) {
+        std::vector<const Op*> sel;
+        for (const Op& op : I->m_ops[n]) {
+            const bool pick = k == 1   ? op.kind == OP_MATTN
+                              : k == 6 ? (op.kind == OP_MEMBED || op.kind == OP_MRESID)
+                              : k == 7 ? op.kind == OP_MFINAL
+                                       : (op.kind == OP_MGEMV && op.role == roles[k]);
+            if (pick) sel.push_back(&op);
+        }
+        times_us[k] = 0;
+        bytes[k] = 0;
+        if (sel.empty()) continue;
+        // each GEMV streams its own weights only (no L2 prefetch of the next matrix, which the
+        // next launch here would not use)
+        auto launch = [&](int r) {
+            Op op = *sel[r % sel.size()];
+            if (op.kind == OP_MGEMV) op.mp.pf_bytes = 0;
+            run_op(I, op, I->stream);
+        };
+        for (int r = 0; r < 3; ++r) launch(r);
+        cudaEventRecord(a, I->stream);
+        for (int r = 0; r < reps; ++r) launch(r);
+        cudaEventRecord(b, I->stream);
+        cudaEventSynchronize(b);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, a, b);
+        times_us[k] = 1000.0 * ms / reps;
+        bytes[k] = (double)sel[0]->bytes;
+    }
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    JINF_CUDA_CHECK(cudaMemsetAsync(I->ms->best, 0, sizeof(I->ms->best), I->stream));
+    JINF_CUDA_CHECK(cudaStreamSynchronize(I->stream));
+    JINF_CUDA_CHECK(cudaGetLastError());
+    return JINF_OK;
+}
+
 extern "C" jinf_status jinf_engine_profile_kernels(jinf_engine* e, int reps, double* times_us, double* bytes) {
     if (!e || !e->impl || reps <= 0 || !times_us || !bytes) return JINF_ERR_INVALID;
     jinf_engine_impl* I = e->impl;

@@ -809,6 +809,7 @@ cudaError_t launch_multi_f(const MultiParams& p, int xm, int epi, int grid, cuda
         case MX_RECORDS * 16 + ME_GATEUP: return launch_multi_n<MX_RECORDS, ME_GATEUP, FMT>(p, grid, s, pdl);
         case MX_RECORDS * 16 + ME_LMHEAD: return launch_multi_n<MX_RECORDS, ME_LMHEAD, FMT>(p, grid, s, pdl);
         case MX_RECORDS * 16 + ME_RESID: return launch_multi_n<MX_RECORDS, ME_RESID, FMT>(p, grid, s, pdl);
+        case MX_RECORDS * 16 + ME_STORE: return launch_multi_n<MX_RECORDS, ME_STORE, FMT>(p, grid, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -83,12 +83,12 @@ int multi_grid(int num_sms);
 size_t multi_workspace_bytes(int pairs, int kw, int n);
 cudaError_t multi_gemv_launch(const MultiParams& p, int xm, int epi, int grid, cudaStream_t s, bool pdl);
 
-// Decode attention of a multi-sequence step (step_kernel.cu: the persistent step's attention
-// split, one kernel per layer): vector v's query heads over positions 0 .. ms->pos[v] of
-// sequence ms->seq[v]'s cache, the positions of each (vector, kv head) split over up to s_max
-// CTAs of 16 warps (one per MULTI_ATTN_SPAN positions: enough 64-position blocks per CTA to
-// pay for its fixed cost), the splits merged in order by the last CTA to finish.
-constexpr int MULTI_ATTN_SPAN = 256;
+// Decode attention of a multi-sequence step (step_kernel.cu, one kernel per layer): vector v's
+// query heads over positions 0 .. ms->pos[v] of sequence ms->seq[v]'s cache, the positions of
+// each (vector, kv head) split over S = min(G, position blocks) CTAs of 16 warps, G = the
+// resident CTA slots / (n x n_kv_heads) (at least 1, at most s_max): one wave of CTAs, each
+// with one contiguous range of positions, the next block's K and V rows requested before the
+// current block's arithmetic. The last CTA of each (vector, kv head) merges the splits in order.
 struct MultiAttnParams {
     const float* q;         // [n][q_stride], RoPE applied
     int q_stride;
@@ -102,7 +102,6 @@ struct MultiAttnParams {
     MultiState* ms;
 };
 size_t multi_attn_part_floats(int n, int n_kv_heads, int s_max, int head_dim);
-size_t multi_attn_smem_bytes(int group, int head_dim);
 cudaError_t multi_attn_launch(const MultiAttnParams& p, cudaStream_t s, bool pdl);
 
 // h[v] = table[token_v] and its sums of squares per 32 elements (ssq [d / 32][n]).

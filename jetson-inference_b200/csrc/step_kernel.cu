@@ -558,7 +558,9 @@ struct HalfVec<2> {
 // GQ heads of the kv head at `q`, cache rows at kb / vb. Leaves either the normalised output
 // in `outs` ([GQ][HD], shared memory; `part` null) or the split's partial (acc, m, l) in
 // `part` ([GQ][HD + 2], global). Shared scratch at `xbase`: step_xstage_bytes covers it.
-template <int HD, int GQ>
+// PIPE: the next block's K and V rows are requested before this block's arithmetic (splits of
+// several blocks; a split of one block, the persistent step's usual case, gains nothing).
+template <int HD, int GQ, bool PIPE = false>
 __device__ __noinline__ void attn_split(const float* q, const __half* kb, const __half* vb, int p0, int p1,
                                         uint8_t* xbase, float* part, float* outs) {
     constexpr int VD = HD / 32;                               // head dims per lane
@@ -589,20 +591,34 @@ __device__ __noinline__ void attn_split(const float* q, const __half* kb, const 
     for (int g = 0; g < GQ; ++g)
 #pragma unroll
         for (int d = 0; d < VD; ++d) acc[g][d] = 0.f;
-    for (int b0 = p0; b0 < p1; b0 += BLK) {
-        const int n = min(BLK, p1 - b0);
-        // every K and V row piece of this warp's positions warp, warp + 16, ... at once
-        HalfVec<VD> kr[PW], vr[PW];
+    // every K and V row piece of this warp's positions warp, warp + 16, ... of a block at once
+    HalfVec<VD> kr[PW], vr[PW], kn[PW], vn[PW];
+    auto fetch = [&](int b, HalfVec<VD>(&kk)[PW], HalfVec<VD>(&vv)[PW]) {
+        const int nb = min(BLK, p1 - b);
 #pragma unroll
         for (int k = 0; k < PW; ++k) {
             const int j = warp + NW * k;
-            if (j < n) {
-                kr[k].load(kb + (size_t)(b0 + j) * HD + lane * VD);
-                vr[k].load(vb + (size_t)(b0 + j) * HD + lane * VD);
+            if (j < nb) {
+                kk[k].load(kb + (size_t)(b + j) * HD + lane * VD);
+                vv[k].load(vb + (size_t)(b + j) * HD + lane * VD);
             } else {
-                kr[k].zero();
-                vr[k].zero();
+                kk[k].zero();
+                vv[k].zero();
             }
+        }
+    };
+    if (PIPE && p0 < p1) fetch(p0, kn, vn);
+    for (int b0 = p0; b0 < p1; b0 += BLK) {
+        const int n = min(BLK, p1 - b0);
+        if (PIPE) {
+#pragma unroll
+            for (int k = 0; k < PW; ++k) {
+                kr[k] = kn[k];
+                vr[k] = vn[k];
+            }
+            if (b0 + BLK < p1) fetch(b0 + BLK, kn, vn);
+        } else {
+            fetch(b0, kr, vr);
         }
         // scores: each lane's dims, summed over the warp
 #pragma unroll
@@ -1223,25 +1239,27 @@ __global__ void __launch_bounds__(STEP_THREADS) k_attn_multi(const MultiAttnPara
     extern __shared__ __align__(16) uint8_t smem_a[];
     __shared__ int is_last;
     const int tid = threadIdx.x;
-    const int v = blockIdx.y, kvh = blockIdx.x / p.s_max, sp = blockIdx.x % p.s_max;
+    const int G = (int)gridDim.x / p.n_kv_heads;  // CTAs per (vector, kv head)
+    const int v = blockIdx.y, kvh = blockIdx.x / G, sp = blockIdx.x % G;
     pdl_wait();
     pdl_trigger();
     const int n_pos = p.ms->pos[v] + 1;
-    const int S = min(p.s_max, max(1, (n_pos + MULTI_ATTN_SPAN - 1) / MULTI_ATTN_SPAN));  // splits with positions
+    constexpr int BLK = NW * (GQ * (HD / 32) >= 32 ? ATTN_PW / 2 : ATTN_PW);  // attn_split's block
+    const int S = min(G, (n_pos + BLK - 1) / BLK);                             // splits with positions
     const size_t pst = (size_t)GQ * (HD + 2);
     float* pbase = p.part + ((size_t)v * p.n_kv_heads + kvh) * p.s_max * pst;
     if (sp < S) {
         const int per = (n_pos + S - 1) / S;
         const int p0 = min(n_pos, sp * per), p1 = min(n_pos, p0 + per);
         const size_t so = (size_t)p.ms->seq[v] * p.seq_stride + (size_t)kvh * p.max_ctx * HD;
-        attn_split<HD, GQ>(p.q + (size_t)v * p.q_stride + (size_t)kvh * GQ * HD, p.kcache + so, p.vcache + so, p0, p1,
-                           smem_a, pbase + (size_t)sp * pst, nullptr);
+        attn_split<HD, GQ, true>(p.q + (size_t)v * p.q_stride + (size_t)kvh * GQ * HD, p.kcache + so, p.vcache + so,
+                                 p0, p1, smem_a, pbase + (size_t)sp * pst, nullptr);
     }
     __threadfence();
     __syncthreads();
     if (tid == 0) {
         const unsigned prev = atomicAdd(&p.ms->attn_count[v * MULTI_MAX_KV_HEADS + kvh], 1u);
-        is_last = prev == (unsigned)(p.s_max - 1);
+        is_last = prev == (unsigned)(G - 1);
         if (is_last) p.ms->attn_count[v * MULTI_MAX_KV_HEADS + kvh] = 0u;  // ready for the next launch
     }
     __syncthreads();
@@ -1309,17 +1327,29 @@ __global__ void __launch_bounds__(STEP_THREADS) k_attn_multi(const MultiAttnPara
 }
 
 template <int HD, int GQ>
-cudaError_t launch_attn_multi(const MultiAttnParams& p, cudaStream_t s, bool pdl) {
-    const size_t smem = multi_attn_smem_bytes(GQ, HD);
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(k_attn_multi<HD, GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+cudaError_t launch_attn_multi(const MultiAttnParams& p0, cudaStream_t s, bool pdl) {
+    // the split's scratch (attn_split) or the merge's (2 x group x s_max + group floats)
+    const size_t split = sizeof(float) * ((size_t)GQ * NW * ATTN_PW + 4 * ATTN_MAX_GROUP + (size_t)NW * GQ * HD);
+    const size_t merge = sizeof(float) * ((size_t)2 * GQ * 64 + GQ);
+    const size_t smem = (std::max(split, merge) + 15) & ~(size_t)15;
+    static int per_sm[64] = {0};  // resident CTAs per SM, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!per_sm[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_multi<HD, GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
-        configured = true;
+        int k = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, k_attn_multi<HD, GQ>, STEP_THREADS, smem);
+        if (e != cudaSuccess) return e;
+        per_sm[dev] = k > 0 ? k : 1;
     }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const MultiAttnParams& p = p0;
+    const int G = std::max(1, std::min(p.s_max, per_sm[dev] * sms / (p.n * p.n_kv_heads)));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(p.n_kv_heads * p.s_max), (unsigned)p.n);
+    cfg.gridDim = dim3((unsigned)(p.n_kv_heads * G), (unsigned)p.n);
     cfg.blockDim = dim3(STEP_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -1335,14 +1365,6 @@ cudaError_t launch_attn_multi(const MultiAttnParams& p, cudaStream_t s, bool pdl
 
 size_t multi_attn_part_floats(int n, int n_kv_heads, int s_max, int head_dim) {
     return (size_t)n * n_kv_heads * s_max * ATTN_MAX_GROUP * (head_dim + 2);
-}
-
-// the attention split's scratch, or the merge's (2 x group x s_max + group floats), whichever
-// is larger (s_max <= 64)
-size_t multi_attn_smem_bytes(int group, int head_dim) {
-    const size_t attn = sizeof(float) * ((size_t)group * NW * ATTN_PW + 4 * ATTN_MAX_GROUP + (size_t)NW * group * head_dim);
-    const size_t merge = sizeof(float) * ((size_t)2 * group * 64 + group);
-    return ((attn > merge ? attn : merge) + 15) & ~(size_t)15;
 }
 
 cudaError_t multi_attn_launch(const MultiAttnParams& p, cudaStream_t s, bool pdl) {

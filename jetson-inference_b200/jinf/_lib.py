@@ -251,6 +251,7 @@ SIGNATURES = {
     "jinf_b200_sparse_predict": (i32, [vp, vp, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp]),
     "jinf_engine_weight_bytes_per_token": (u64, [C.POINTER(Engine)]),
     "jinf_engine_profile_kernels": (i32, [C.POINTER(Engine), i32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "jinf_engine_profile_multi": (i32, [C.POINTER(Engine), i32, i32, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "jinf_nccl_get_unique_id": (i32, [vp]),
     "jinf_synth_create": (i32, [C.POINTER(vp), C.POINTER(SynthConfig)]),
     "jinf_synth_destroy": (None, [vp]),

@@ -337,6 +337,15 @@ class Engine:
         names = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "sparse_ffn"]
         return {n: {"us": t[i], "bytes": b[i]} for i, n in enumerate(names)}
 
+    def profile_multi(self, n: int, reps: int = 32) -> dict:
+        """Per-kernel times of an n-vector multi-sequence step (the sequences' state is left
+        undefined)."""
+        t = (C.c_double * 8)()
+        b = (C.c_double * 8)()
+        L.check(L.lib.jinf_engine_profile_multi(self.h, n, reps, t, b), "profile_multi")
+        names = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "rows", "finalize"]
+        return {k: {"us": t[i], "bytes": b[i]} for i, k in enumerate(names)}
+
     def stats(self) -> L.PerfStats:
         return L.lib.jinf_engine_get_stats(self.h).contents
 
