@@ -17,6 +17,7 @@
 //   silu_to_f16   SiLU(gate) * up (cuda/silu_kernel.cu:15-17) as fp16 rows
 //   [down GEMM, residual add in its epilogue]
 #include "common.cuh"
+#include "mma_f16.cuh"
 #include "prefill.h"
 #include "q4m_device.cuh"
 
@@ -144,29 +145,6 @@ __global__ void k_rope_qkv(const float* __restrict__ y, int ldy, int T, int p0, 
 // tensor cores (m16n8k16, fp16 in, fp32 out), the online softmax in fp32 registers. Query
 // token t (position p0 + t) sees positions 0 .. p0 + t.
 constexpr int AQ = 64, AK = 64;
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                        uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-        "{%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
 
 template <int HD>
 __global__ void __launch_bounds__(128) k_prefill_attn(const __half* __restrict__ q16, int nq, int T, int p0,

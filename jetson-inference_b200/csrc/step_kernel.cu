@@ -34,6 +34,7 @@
 // the next RMSNorm input adds all ranks' rows in rank order (stage_x_tp); the last CTA
 // exchanges the argmax keys.
 #include "common.cuh"
+#include "mma_f16.cuh"
 #include "multi.h"
 #include "q4m_device.cuh"
 #include "step.h"
@@ -1234,8 +1235,191 @@ extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
 
 namespace {
 
+// The multi-sequence attention's split [p0, p1) of one kv head on the tensor cores
+// (mma.sync m16n8k16, fp16 operands, fp32 accumulation). Blocks of TA_BLK positions: their K
+// and V rows are copied into shared memory (cp.async, rows padded to HD + 8 halves so that
+// ldmatrix reads no bank twice), TA_NST - 1 blocks ahead of the arithmetic. Per block:
+//   scores S^T = K Q^T with the query heads as the MMA's 8 columns (rows of q past GQ zero):
+//     warp w takes positions 8 (w & 7) .. +7 and half the head dims (w >> 3); q enters as
+//     fp16 hi + lo (q = hi + lo to about 22 bits), so two MMAs per step;
+//   an online softmax per head (one warp each), in fp32, over the two halves' sums;
+//   O^T += V^T P^T with the heads as columns again: warp w takes head dims 16 (w & 7) .. +15
+//     and positions 32 (w >> 3) .. +31; p enters as fp16 hi + lo.
+// K and V are the cache's fp16 values, so the products are those of the fp32 arithmetic to
+// the hi + lo rounding; sums are fp32. Leaves the split's partial (acc, m, l) in `part`
+// ([GQ][HD + 2]), as attn_split does.
+constexpr int TA_BLK = 64;
+constexpr int TA_NST = 4;
+template <int HD>
+__host__ __device__ constexpr size_t ta_smem() {
+    return (size_t)TA_NST * 2 * TA_BLK * (HD + 8) * 2  // K and V stages
+           + 2 * 8 * TA_BLK * 4                        // scores of the two halves [2][8][TA_BLK]
+           + 2 * 8 * (TA_BLK + 8) * 2                  // p hi, lo [8][TA_BLK + 8]
+           + 8 * 4 * 4;                                // m, l, correction per head
+}
+
 template <int HD, int GQ>
-__global__ void __launch_bounds__(STEP_THREADS) k_attn_multi(const MultiAttnParams p) {
+__device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, const __half* vb, int p0, int p1,
+                                              uint8_t* sm, float* part) {
+    static_assert(GQ <= 8 && HD % 32 == 0 && HD <= 128, "heads are the MMA's 8 columns");
+    constexpr int LD = HD + 8;                 // padded row, halves
+    constexpr int STH = 2 * TA_BLK * LD;        // halves per stage
+    constexpr int PST = TA_BLK + 8;             // p row, halves
+    constexpr int KH = HD / 32;                 // score k-steps per warp (half the head dims)
+    constexpr int MTL = HD / 16;                // p.v m-tiles (16 head dims)
+    constexpr int CH = HD / 8;                  // 16-byte chunks per cache row
+    static_assert((size_t)2 * HD * 8 * 4 <= (size_t)TA_NST * STH * 2, "the final sums reuse the stages");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gid = lane >> 2, tig = lane & 3;
+    __half* stages = reinterpret_cast<__half*>(sm);
+    float* s_part = reinterpret_cast<float*>(sm + (size_t)TA_NST * STH * 2);
+    __half* p_hi = reinterpret_cast<__half*>(s_part + 2 * 8 * TA_BLK);
+    __half* p_lo = p_hi + 8 * PST;
+    float* ml = reinterpret_cast<float*>(p_lo + 8 * PST);
+    const int nb = (p1 - p0 + TA_BLK - 1) / TA_BLK;
+
+    // block b's K and V rows into stage b % TA_NST; rows past p1 are zero-filled
+    auto load_block = [&](int b) {
+        __half* sk = stages + (b % TA_NST) * STH;
+        const int pos0 = p0 + b * TA_BLK;
+        for (int i = tid; i < 2 * TA_BLK * CH; i += STEP_THREADS) {
+            const int isv = i / (TA_BLK * CH), r = (i / CH) % TA_BLK, c = i % CH;
+            const bool in = pos0 + r < p1;
+            const __half* src = (isv ? vb : kb) + (size_t)(in ? pos0 + r : p0) * HD + c * 8;
+            const uint32_t dst = smem_u32(sk + isv * TA_BLK * LD + r * LD + c * 8);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(in ? 16 : 0)
+                         : "memory");
+        }
+    };
+#pragma unroll
+    for (int b = 0; b < TA_NST - 1; ++b) {
+        if (b < nb) load_block(b);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+
+    // the query fragments of this warp's score half: head gid (zero past GQ), dims
+    // 16 (kh KH + s) + 8 h + 2 tig, +1, scaled by 1 / sqrt(HD)
+    const int nt = warp & 7, kh = warp >> 3;
+    uint32_t qh[KH][2], ql[KH][2];
+    {
+        const float scale = rsqrtf((float)HD);
+#pragma unroll
+        for (int st = 0; st < KH; ++st)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float2 t = make_float2(0.f, 0.f);
+                if (gid < GQ) t = __ldcg(reinterpret_cast<const float2*>(q + gid * HD + (kh * KH + st) * 16 + h * 8 + tig * 2));
+                split_h2(t.x * scale, t.y * scale, qh[st][h], ql[st][h]);
+            }
+    }
+    for (int i = tid; i < 8 * PST; i += STEP_THREADS) {  // rows of heads past GQ stay zero
+        p_hi[i] = __float2half_rn(0.f);
+        p_lo[i] = __float2half_rn(0.f);
+    }
+    if (tid < 8) {
+        ml[tid * 4] = -INFINITY;
+        ml[tid * 4 + 1] = 0.f;
+        ml[tid * 4 + 2] = 0.f;
+    }
+    const int mt = warp & 7, ph = warp >> 3;  // p.v: head dims 16 mt .. +15, positions 32 ph .. +31
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int b = 0; b < nb; ++b) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(TA_NST - 2) : "memory");
+        __syncthreads();  // block b landed for every thread; block b - 1's stage is free
+        if (b + TA_NST - 1 < nb) load_block(b + TA_NST - 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const int n = min(TA_BLK, p1 - (p0 + b * TA_BLK));
+        const __half* sk = stages + (b % TA_NST) * STH;
+        const __half* sv = sk + TA_BLK * LD;
+        {
+            // scores of positions 8 nt .. +7 over head dims [32 kh KH / 2 ...): lane l addresses
+            // row 8 nt + (l & 7) of matrix l >> 3 (8 dims each)
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int st = 0; st < KH; st += 2) {
+                uint32_t b0, b1, b2, b3;
+                const int dim = (kh * KH + st) * 16 + (lane >> 3) * 8;
+                ldsm_x4(smem_u32(sk + (8 * nt + (lane & 7)) * LD + dim), b0, b1, b2, b3);
+                mma_f16(c, qh[st][0], 0u, qh[st][1], 0u, b0, b1);
+                mma_f16(c, ql[st][0], 0u, ql[st][1], 0u, b0, b1);
+                mma_f16(c, qh[st + 1][0], 0u, qh[st + 1][1], 0u, b2, b3);
+                mma_f16(c, ql[st + 1][0], 0u, ql[st + 1][1], 0u, b2, b3);
+            }
+            if (gid < GQ)
+                *reinterpret_cast<float2*>(s_part + (kh * 8 + gid) * TA_BLK + 8 * nt + 2 * tig) = make_float2(c[0], c[1]);
+        }
+        __syncthreads();
+        if (warp < GQ) {  // online softmax of head `warp`: lanes own positions lane, lane + 32
+            float sc[2], e[2];
+            float mb = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const int j = lane + 32 * t;
+                sc[t] = j < n ? s_part[warp * TA_BLK + j] + s_part[(8 + warp) * TA_BLK + j] : -INFINITY;
+                mb = fmaxf(mb, sc[t]);
+            }
+            const float mo = ml[warp * 4], mn = fmaxf(mo, warp_max(mb));
+#pragma unroll
+            for (int t = 0; t < 2; ++t) e[t] = lane + 32 * t < n ? expf(sc[t] - mn) : 0.f;
+            const float corr = mo == -INFINITY ? 0.f : expf(mo - mn);
+            const float ln = fmaf(ml[warp * 4 + 1], corr, warp_sum(e[0] + e[1]));
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+                const __half h = __float2half_rn(e[t]);
+                p_hi[warp * PST + lane + 32 * t] = h;
+                p_lo[warp * PST + lane + 32 * t] = __float2half_rn(e[t] - __half2float(h));
+            }
+            __syncwarp();
+            if (lane == 0) {
+                ml[warp * 4] = mn;
+                ml[warp * 4 + 1] = ln;
+                ml[warp * 4 + 2] = corr;
+            }
+        }
+        __syncthreads();
+        if (mt < MTL) {
+            const float c0 = ml[(2 * tig) * 4 + 2], c1 = ml[(2 * tig + 1) * 4 + 2];  // columns = heads 2 tig, +1
+            acc[0] *= c0;
+            acc[1] *= c1;
+            acc[2] *= c0;
+            acc[3] *= c1;
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks) {
+                const int k0 = 32 * ph + 16 * ks;  // positions
+                // V^T fragments: matrix l >> 3 = (positions +8 if bit 1, dims +8 if bit 0)
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_t(smem_u32(sv + (k0 + (lane & 7) + ((lane >> 4) & 1) * 8) * LD + 16 * mt + ((lane >> 3) & 1) * 8),
+                          a0, a1, a2, a3);
+                const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(p_hi + gid * PST + k0 + 2 * tig);
+                const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(p_hi + gid * PST + k0 + 8 + 2 * tig);
+                const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(p_lo + gid * PST + k0 + 2 * tig);
+                const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(p_lo + gid * PST + k0 + 8 + 2 * tig);
+                mma_f16(acc, a0, a1, a2, a3, bh0, bh1);
+                mma_f16(acc, a0, a1, a2, a3, bl0, bl1);
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // the trailing groups are empty
+    __syncthreads();
+    // the two position halves summed in order: red [2][HD][8] over the stages
+    float* red = reinterpret_cast<float*>(sm);
+    if (mt < MTL) {
+        float* r0 = red + ((size_t)ph * HD + 16 * mt + gid) * 8 + 2 * tig;
+        *reinterpret_cast<float2*>(r0) = make_float2(acc[0], acc[1]);
+        *reinterpret_cast<float2*>(r0 + 8 * 8) = make_float2(acc[2], acc[3]);
+    }
+    __syncthreads();
+    for (int o = tid; o < GQ * HD; o += STEP_THREADS) {
+        const int g = o / HD, dd = o % HD;
+        part[g * (HD + 2) + dd] = red[(size_t)dd * 8 + g] + red[((size_t)HD + dd) * 8 + g];
+        if (dd == 0) {
+            part[g * (HD + 2) + HD] = p1 > p0 ? ml[g * 4] : -INFINITY;  // an empty split
+            part[g * (HD + 2) + HD + 1] = ml[g * 4 + 1];
+        }
+    }
+}
+
+template <int HD, int GQ>
+__global__ void __launch_bounds__(STEP_THREADS, 1) k_attn_multi(const MultiAttnParams p) {
     extern __shared__ __align__(16) uint8_t smem_a[];
     __shared__ int is_last;
     const int tid = threadIdx.x;
@@ -1244,16 +1428,15 @@ __global__ void __launch_bounds__(STEP_THREADS) k_attn_multi(const MultiAttnPara
     pdl_wait();
     pdl_trigger();
     const int n_pos = p.ms->pos[v] + 1;
-    constexpr int BLK = NW * (GQ * (HD / 32) >= 32 ? ATTN_PW / 2 : ATTN_PW);  // attn_split's block
-    const int S = min(G, (n_pos + BLK - 1) / BLK);                             // splits with positions
+    const int S = min(G, (n_pos + TA_BLK - 1) / TA_BLK);  // splits with positions
     const size_t pst = (size_t)GQ * (HD + 2);
     float* pbase = p.part + ((size_t)v * p.n_kv_heads + kvh) * p.s_max * pst;
     if (sp < S) {
         const int per = (n_pos + S - 1) / S;
         const int p0 = min(n_pos, sp * per), p1 = min(n_pos, p0 + per);
         const size_t so = (size_t)p.ms->seq[v] * p.seq_stride + (size_t)kvh * p.max_ctx * HD;
-        attn_split<HD, GQ, true>(p.q + (size_t)v * p.q_stride + (size_t)kvh * GQ * HD, p.kcache + so, p.vcache + so,
-                                 p0, p1, smem_a, pbase + (size_t)sp * pst, nullptr);
+        attn_split_tc<HD, GQ>(p.q + (size_t)v * p.q_stride + (size_t)kvh * GQ * HD, p.kcache + so, p.vcache + so, p0,
+                              p1, smem_a, pbase + (size_t)sp * pst);
     }
     __threadfence();
     __syncthreads();
@@ -1328,10 +1511,9 @@ __global__ void __launch_bounds__(STEP_THREADS) k_attn_multi(const MultiAttnPara
 
 template <int HD, int GQ>
 cudaError_t launch_attn_multi(const MultiAttnParams& p0, cudaStream_t s, bool pdl) {
-    // the split's scratch (attn_split) or the merge's (2 x group x s_max + group floats)
-    const size_t split = sizeof(float) * ((size_t)GQ * NW * ATTN_PW + 4 * ATTN_MAX_GROUP + (size_t)NW * GQ * HD);
+    // the split's scratch (attn_split_tc) or the merge's (2 x group x s_max + group floats)
     const size_t merge = sizeof(float) * ((size_t)2 * GQ * 64 + GQ);
-    const size_t smem = (std::max(split, merge) + 15) & ~(size_t)15;
+    const size_t smem = (std::max(ta_smem<HD>(), merge) + 15) & ~(size_t)15;
     static int per_sm[64] = {0};  // resident CTAs per SM, per device
     int dev = 0;
     cudaGetDevice(&dev);

@@ -100,6 +100,34 @@ def test_8b_layers_eight_sequences_at_512(cuda, qtype):
     eng.close()
 
 
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_eight_query_heads_per_kv_head_ragged_caches(cuda, head_dim):
+    """Eight query heads per kv head (the 70B grouping) at head dims 64 and 128, four sequences
+    whose caches hold 63, 64, 700 and 1500 seeded positions (one short of a 64-position block,
+    exactly one block, and many blocks over several splits), then 1 prompt token and 3 greedy
+    steps each, against each sequence's oracle."""
+    import jinf
+    shape = jinf.LlamaShape(2, 16 * head_dim, 16, 2, 2816, 4096, 5e5)
+    syn = jinf.SynthModel(shape, seed=21 + head_dim)
+    fills = [63, 64, 700, 1500]
+    ctx = max(fills) + 8
+    eng = jinf.Engine.from_synth(syn, max_context=ctx, options=jinf.b200_options(eos_token=-1, max_seqs=4))
+    seqs = [0, 1, 2, 3]
+    orcs = []
+    for s, f in zip(seqs, fills):
+        eng.seq_fill_kv_random(s, f, seed=300 + s)
+        o = oracle.OracleModel(syn, max_ctx=ctx, kv_f16=True)
+        o.load_kv_f16(*eng.seq_kv_read(s, f))
+        orcs.append(o)
+    rng = np.random.default_rng(head_dim)
+    prompts = [[int(rng.integers(0, shape.n_vocab))] for _ in seqs]
+    worst, gap = run_lockstep(eng, orcs, seqs, prompts, 3)
+    print(f"GQA 8, head dim {head_dim}, caches {fills}: max logits rel err {worst:.3g}, min top-1/top-2 gap {gap:.3g}")
+    for o in orcs:
+        o.close()
+    eng.close()
+
+
 def test_ragged_positions_and_counts(cuda):
     """Sequences at different positions, stepped in changing subsets (1, 2, 3 and 5 vectors:
     one captured graph per count), each against its own oracle."""
