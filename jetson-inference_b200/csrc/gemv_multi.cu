@@ -59,8 +59,9 @@ __host__ __device__ constexpr inline int multi_nbuf(int fmt) { return fmt == Q4M
 // in different shared-memory banks.
 __host__ __device__ inline int multi_dig_stride(int gk) { return gk * 256 + 64; }
 __host__ __device__ inline int multi_prm_stride(int gk) { return gk * 64 + 16; }
+__host__ __device__ inline int multi_pad(int n) { return (n + 3) & ~3; }  // staged vectors: whole blocks of 4
 __host__ __device__ inline size_t multi_rec_bytes(int n, int gk) {
-    return (size_t)n * (multi_dig_stride(gk) + multi_prm_stride(gk));
+    return (size_t)multi_pad(n) * (multi_dig_stride(gk) + multi_prm_stride(gk));
 }
 // epilogue staging [MNW][MULTI_MAX][EP_STRIDE] floats, 64 floats of norm factors, the argmax
 // keys [MNW][MULTI_MAX], the merged rows [MULTI_MAX][EP_STRIDE] (per-CTA split) and a flag
@@ -77,33 +78,51 @@ __device__ __forceinline__ void lds128(uint32_t a, uint32_t (&r)[4]) {
 
 // Staged records of one vector block (4 vectors) for block j of local group gl: the lane's B
 // fragment (digit h = gr & 1 of vector 4 vb + gr / 2) and the params of its accumulator vector
-// 4 vb + c (zero-point offsets kh, kl and the digit scales ia, ia / 16).
+// 4 vb + c (zero-point offsets kh, kl and the digit scales ia, ia / 16). The staged vectors are
+// padded to a multiple of 4 with zero records, so every lane loads unconditionally; the lane's
+// addresses for group 0, block 0 are computed once per kernel.
 struct MultiRec {
-    uint32_t dig, prm;  // shared addresses
-    int dstride, pstride, n;
+    uint32_t dig[2], prm[2];  // shared addresses of vector blocks 0 and 1
 };
-__device__ __forceinline__ void rec_frag(const MultiRec& r, int vb, int j, int gl, int lane, uint32_t& b0,
-                                         uint32_t& b1) {
+__device__ __forceinline__ MultiRec multi_rec(uint32_t dig, uint32_t prm, int dstride, int pstride, int lane) {
     const int gr = lane >> 2, c = lane & 3;
-    const int v = 4 * vb + (gr >> 1), h = gr & 1;
-    b0 = 0u;
-    b1 = 0u;
-    if (v < r.n)
-        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
-                     : "=r"(b0), "=r"(b1)
-                     : "r"(r.dig + (uint32_t)(v * r.dstride + gl * 256 + ((2 * j + h) * 4 + c) * 8)));
+    MultiRec r;
+#pragma unroll
+    for (int vb = 0; vb < 2; ++vb) {
+        r.dig[vb] = dig + (uint32_t)((4 * vb + (gr >> 1)) * dstride + ((gr & 1) * 4 + c) * 8);
+        r.prm[vb] = prm + (uint32_t)((4 * vb + c) * pstride);
+    }
+    return r;
 }
-__device__ __forceinline__ void rec_prm(const MultiRec& r, int vb, int j, int gl, int lane, int& kh, int& kl,
-                                        float& ia, float& ib) {
-    const int vo = 4 * vb + (lane & 3);
-    kh = 0;
-    kl = 0;
-    ia = 0.f;
-    ib = 0.f;
-    if (vo < r.n)
-        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                     : "=r"(kh), "=r"(kl), "=f"(ia), "=f"(ib)
-                     : "r"(r.prm + (uint32_t)(vo * r.pstride + (gl * 4 + j) * 16)));
+__device__ __forceinline__ void rec_frag(const MultiRec& r, int vb, int j, int gl, uint32_t& b0, uint32_t& b1) {
+    asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(r.dig[vb] + (uint32_t)(gl * 256 + j * 64)));
+}
+__device__ __forceinline__ void rec_prm(const MultiRec& r, int vb, int j, int gl, int& kh, int& kl, float& ia,
+                                        float& ib) {
+    asm("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(kh), "=r"(kl), "=f"(ia), "=f"(ib)
+        : "r"(r.prm[vb] + (uint32_t)(gl * 64 + j * 16)));
+}
+
+// Integer MMAs with a zero accumulator input (no register initialisation per step).
+__device__ __forceinline__ void mma_u8s8_z(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                                           int (&d)[4]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_s8s8_z(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                                           int (&d)[4]) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %10, %10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_s8s8_k16_z(uint32_t a0, uint32_t a1, uint32_t b0, int (&d)[4]) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%7, %7, %7, %7};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
 
 // ---- one unit (32 rows x 128 columns) against NVB vector blocks, per weight format.
@@ -132,16 +151,18 @@ __device__ __forceinline__ void unit_multi_q40(uint32_t sl, const MultiRec& r, i
             uint32_t b0, b1;
             int kh, kl;
             float ia, ib;
-            rec_frag(r, vb, j, gl, lane, b0, b1);
-            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
-            int da[4] = {kh, kl, kh, kl};
-            int db[4] = {kh * 16, kl * 16, kh * 16, kl * 16};
-            mma_u8s8(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), b0, b1, da);
-            mma_u8s8(nib_hi(w[4 * j]), nib_hi(w[4 * j + 1]), nib_hi(w[4 * j + 2]), nib_hi(w[4 * j + 3]), b0, b1, db);
-            acc[vb][0] = fmaf(dA0 * ia, (float)(da[0] * 256 + da[1]), acc[vb][0]);
-            acc[vb][1] = fmaf(dA1 * ia, (float)(da[2] * 256 + da[3]), acc[vb][1]);
-            acc[vb][2] = fmaf(dB0 * ib, (float)(db[0] * 256 + db[1]), acc[vb][2]);
-            acc[vb][3] = fmaf(dB1 * ib, (float)(db[2] * 256 + db[3]), acc[vb][3]);
+            rec_frag(r, vb, j, gl, b0, b1);
+            rec_prm(r, vb, j, gl, kh, kl, ia, ib);
+            // the zero-point offsets (kh, kl: -8 x the digit sums) added after the MMAs: the
+            // (hi, lo) pair of tile A gets 256 kh + kl, tile B's (its operand carries 16 q) 16 x that
+            const int k = kh * 256 + kl, k16 = k * 16;
+            int da[4], db[4];
+            mma_u8s8_z(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), b0, b1, da);
+            mma_u8s8_z(nib_hi(w[4 * j]), nib_hi(w[4 * j + 1]), nib_hi(w[4 * j + 2]), nib_hi(w[4 * j + 3]), b0, b1, db);
+            acc[vb][0] = fmaf(dA0 * ia, (float)(da[0] * 256 + da[1] + k), acc[vb][0]);
+            acc[vb][1] = fmaf(dA1 * ia, (float)(da[2] * 256 + da[3] + k), acc[vb][1]);
+            acc[vb][2] = fmaf(dB0 * ib, (float)(db[0] * 256 + db[1] + k16), acc[vb][2]);
+            acc[vb][3] = fmaf(dB1 * ib, (float)(db[2] * 256 + db[3] + k16), acc[vb][3]);
         }
     }
 }
@@ -187,11 +208,11 @@ __device__ __forceinline__ void unit_multi_q4k(uint32_t sl, const MultiRec& r, i
             uint32_t b0, b1;
             int kh, kl;
             float ia, ib;
-            rec_frag(r, vb, j, gl, lane, b0, b1);
-            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
-            int da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
-            mma_u8s8(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), b0, b1, da);
-            mma_u8s8(nib_hi(w[4 * j]), nib_hi(w[4 * j + 1]), nib_hi(w[4 * j + 2]), nib_hi(w[4 * j + 3]), b0, b1, db);
+            rec_frag(r, vb, j, gl, b0, b1);
+            rec_prm(r, vb, j, gl, kh, kl, ia, ib);
+            int da[4], db[4];
+            mma_u8s8_z(nib_lo(w[4 * j]), nib_lo(w[4 * j + 1]), nib_lo(w[4 * j + 2]), nib_lo(w[4 * j + 3]), b0, b1, da);
+            mma_u8s8_z(nib_hi(w[4 * j]), nib_hi(w[4 * j + 1]), nib_hi(w[4 * j + 2]), nib_hi(w[4 * j + 3]), b0, b1, db);
             const float S = (float)(-((kh << 8) + kl) >> 3);  // 256 S_hi + S_lo of the block (exact)
             acc[vb][0] = fmaf(fmaf(sd[0], (float)(da[0] * 256 + da[1]), -sm[0] * S), ia, acc[vb][0]);
             acc[vb][1] = fmaf(fmaf(sd[1], (float)(da[2] * 256 + da[3]), -sm[1] * S), ia, acc[vb][1]);
@@ -249,13 +270,13 @@ __device__ __forceinline__ void unit_multi_q6k(uint32_t sl, const MultiRec& r, i
             uint32_t x0, x1;
             int kh, kl;
             float ia, ib;
-            rec_frag(r, vb, j, gl, lane, x0, x1);
-            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
-            int p0[4] = {0, 0, 0, 0}, p1[4] = {0, 0, 0, 0}, q0[4] = {0, 0, 0, 0}, q1[4] = {0, 0, 0, 0};
-            mma_s8s8_k16(A0, A1, x0, p0);
-            mma_s8s8_k16(A2, A3, x1, p1);
-            mma_s8s8_k16(B0, B1, x0, q0);
-            mma_s8s8_k16(B2, B3, x1, q1);
+            rec_frag(r, vb, j, gl, x0, x1);
+            rec_prm(r, vb, j, gl, kh, kl, ia, ib);
+            int p0[4], p1[4], q0[4], q1[4];
+            mma_s8s8_k16_z(A0, A1, x0, p0);
+            mma_s8s8_k16_z(A2, A3, x1, p1);
+            mma_s8s8_k16_z(B0, B1, x0, q0);
+            mma_s8s8_k16_z(B2, B3, x1, q1);
             const float s = 0.25f * ia;
             auto dsum = [](const int (&h)[4], int rr) { return (float)(h[2 * rr] * 256 + h[2 * rr + 1]); };
             acc[vb][0] = fmaf(fmaf(a00, dsum(p0, 0), a01 * dsum(p1, 0)), s, acc[vb][0]);
@@ -293,11 +314,11 @@ __device__ __forceinline__ void unit_multi_q80(uint32_t sl, const MultiRec& r, i
             uint32_t x0, x1;
             int kh, kl;
             float ia, ib;
-            rec_frag(r, vb, j, gl, lane, x0, x1);
-            rec_prm(r, vb, j, gl, lane, kh, kl, ia, ib);
-            int da[4] = {0, 0, 0, 0}, db[4] = {0, 0, 0, 0};
-            mma_s8s8(wa[0], wa[1], wa[2], wa[3], x0, x1, da);
-            mma_s8s8(wb[0], wb[1], wb[2], wb[3], x0, x1, db);
+            rec_frag(r, vb, j, gl, x0, x1);
+            rec_prm(r, vb, j, gl, kh, kl, ia, ib);
+            int da[4], db[4];
+            mma_s8s8_z(wa[0], wa[1], wa[2], wa[3], x0, x1, da);
+            mma_s8s8_z(wb[0], wb[1], wb[2], wb[3], x0, x1, db);
             acc[vb][0] = fmaf(e0 * ia, (float)(da[0] * 256 + da[1]), acc[vb][0]);
             acc[vb][1] = fmaf(e1 * ia, (float)(da[2] * 256 + da[3]), acc[vb][1]);
             acc[vb][2] = fmaf(e2 * ia, (float)(db[0] * 256 + db[1]), acc[vb][2]);
@@ -407,7 +428,7 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
     const int g0 = kp * G / kw, g1 = (kp + 1) * G / kw, ng = g1 - g0;
     uint8_t* rec = smem_m;
     uint32_t* dig = reinterpret_cast<uint32_t*>(rec);
-    float4* prm = reinterpret_cast<float4*>(rec + (size_t)n * multi_dig_stride(gk));
+    float4* prm = reinterpret_cast<float4*>(rec + (size_t)multi_pad(n) * multi_dig_stride(gk));
     float* ep = reinterpret_cast<float*>(rec + multi_rec_bytes(n, gk));  // [MNW][MULTI_MAX][EP_STRIDE]
     float* fac = ep + MNW * MULTI_MAX * EP_STRIDE;                       // [MULTI_MAX] (64 floats)
     u64* keys = reinterpret_cast<u64*>(fac + 64);                        // [MNW][MULTI_MAX]
@@ -525,8 +546,16 @@ __global__ void __launch_bounds__(MT, 1) k_gemv_multi(const MultiParams p) {
                              prm + (v * multi_prm_stride(gk) + gl * 64) / 16);
         }
     }
+    // zero records for the padding vectors n .. multi_pad(n) - 1 (they contribute nothing)
+    for (int i = tid; i < (multi_pad(n) - n) * (multi_dig_stride(gk) + multi_prm_stride(gk)) / 16; i += MT) {
+        const int per_d = (multi_pad(n) - n) * multi_dig_stride(gk) / 16;
+        uint4* dst = i < per_d ? reinterpret_cast<uint4*>(rec + (size_t)n * multi_dig_stride(gk)) + i
+                               : reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(prm) + (size_t)n * multi_prm_stride(gk)) +
+                                     (i - per_d);
+        *dst = make_uint4(0u, 0u, 0u, 0u);
+    }
     __syncthreads();
-    const MultiRec mr{smem_u32(dig), smem_u32(prm), multi_dig_stride(gk), multi_prm_stride(gk), n};
+    const MultiRec mr = multi_rec(smem_u32(dig), smem_u32(prm), multi_dig_stride(gk), multi_prm_stride(gk), lane);
 
     // ---------------- main loop
     const int gr = lane >> 2, c = lane & 3;
