@@ -781,7 +781,7 @@ Op multi_gemv_op(jinf_engine_impl* I, int n, const uint8_t* w, const Q4MShape& s
     p.groups = sh.groups;
     p.fmt = sh.fmt;
     p.n = n;
-    multi_plan(sh.pairs, sh.groups, n, sh.fmt, op.grid, epi, &p.kw, &p.local);
+    multi_plan(sh.pairs, sh.groups, n, sh.fmt, op.grid, epi, xm, &p.kw, &p.local);
     p.gk = p.kw > 0 ? (sh.groups + p.kw - 1) / p.kw : 0;
     p.part = I->m_part;
     p.cnt = I->m_cnt;
@@ -874,7 +874,7 @@ void build_multi_ops(jinf_engine_impl* I, int n, std::vector<Op>& ops) {
             v.mp.pairs = ly.v_sh.pairs;
             v.mp.groups = ly.v_sh.groups;
             v.mp.fmt = ly.v_sh.fmt;
-            multi_plan(ly.v_sh.pairs, ly.v_sh.groups, n, ly.v_sh.fmt, v.grid, ME_QKV, &v.mp.kw, &v.mp.local);
+            multi_plan(ly.v_sh.pairs, ly.v_sh.groups, n, ly.v_sh.fmt, v.grid, ME_QKV, xm_h, &v.mp.kw, &v.mp.local);
             v.mp.gk = v.mp.kw > 0 ? (ly.v_sh.groups + v.mp.kw - 1) / v.mp.kw : 0;
             v.mp.nq = 0;
             v.mp.nk = 0;
@@ -1874,11 +1874,13 @@ jinf_status create_from_source(jinf_engine** out, const jinf_engine_config* cfg,
         const int grid = multi_grid(I->num_sms);
         size_t ws = 0, pairs = 0;
         for (int n = 1; n <= S; ++n) {
-            auto need = [&](const Q4MShape& sh, int epi) {  // the plan the step's op will make
+            auto need = [&](const Q4MShape& sh, int epi) {  // the plans the step's op can make
                 if (!sh.rows) return;
-                int kw = 0, local = 0;
-                multi_plan(sh.pairs, sh.groups, n, sh.fmt, grid, epi, &kw, &local);
-                ws = std::max(ws, (size_t)sh.pairs * std::max(kw, 1) * n * 32);
+                for (int xm : {MX_PLAIN_F32, MX_RECORDS}) {
+                    int kw = 0, local = 0;
+                    multi_plan(sh.pairs, sh.groups, n, sh.fmt, grid, epi, xm, &kw, &local);
+                    ws = std::max(ws, (size_t)sh.pairs * std::max(kw, 1) * n * 32);
+                }
                 pairs = std::max(pairs, (size_t)sh.pairs);
             };
             need(I->lm_sh, ME_LMHEAD);

@@ -862,15 +862,23 @@ int multi_grid(int num_sms) { return num_sms; }
 
 // Estimated time, in units of one unit's streaming time per warp (at full HBM rate a warp
 // streams one unit while the other 15 warps of its SM stream theirs; a dependent global round
-// trip costs about the same):
-//   per warp: the busiest warp's pairs x the part's groups, plus, with kw > 1, its partial rows,
-//     the arrival and the final sums (n loads per lane per part, eight in flight);
-//   per CTA: rounds of pairs x (the warp's share of the part's groups + the merge), plus, with
-//     kw > 1, the arrival and the final sums (one load per thread per part, eight in flight).
-void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int* kw_out, int* local_out) {
+// trip costs about the same), fitted to B200 measurements of the 8B and 70B layer shapes at
+// 2, 4 and 8 vectors:
+//   per warp: the busiest warp's pairs x (the part's groups, plus, with kw > 1, its partial
+//     rows, the arrival and the final sums: n loads per lane per part, eight in flight, 1.2
+//     units per round of loads);
+//   per CTA, one K part only: 2.5 + rounds of pairs x (the warp's share of the groups + 0.9
+//     for the three barriers and the 16-warp merge of each pair);
+// both plus the CTA's input staging spread over its 16 warps (n x the part's groups: 0.45
+// units each when converted from fp32, 0.15 when copied as records). The per-CTA form wins
+// where the pairs are about as many as the CTAs and one part holds every group (the 8B QKV,
+// o and gate|up projections); with several K parts it lost every measured case, so it is
+// not considered there; the per-warp form with several K parts wins elsewhere.
+void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int xm, int* kw_out, int* local_out) {
     *kw_out = 0;
     *local_out = 0;
     if (pairs < 1 || groups < 1 || n < 1 || n > MULTI_MAX || grid < 1) return;
+    const double stage = xm == MX_RECORDS ? 0.15 : 0.45;
     double best = 1e300;
     const int lim = groups < kMultiMaxKw ? groups : kMultiMaxKw;
     for (int kw = 1; kw <= lim; ++kw) {
@@ -879,15 +887,16 @@ void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int* k
         const int cg = grid / kw > 0 ? grid / kw : 1;  // CTAs of the least served part
         const long long warps = (long long)cg * MNW;
         const double pw = (double)((pairs + warps - 1) / warps);
-        const double cost_w = pw * (gk + (kw > 1 ? 1.0 + n * ((kw + 7) / 8) : 0.0));
+        const double st = stage * n * gk / MNW;
+        const double cost_w = pw * (gk + (kw > 1 ? 1.0 + 1.2 * n * ((kw + 7) / 8) : 0.0)) + st;
         if (cost_w < best - 1e-9) {
             best = cost_w;
             *kw_out = kw;
             *local_out = 0;
         }
-        if (epi == ME_LMHEAD) continue;
+        if (epi == ME_LMHEAD || kw > 1) continue;
         const double rounds = (double)((pairs + cg - 1) / cg);
-        const double cost_l = rounds * ((gk + MNW - 1) / MNW + 0.5) + (kw > 1 ? 1.0 + (kw + 7) / 8 : 0.0);
+        const double cost_l = 2.5 + rounds * ((gk + MNW - 1) / MNW + 0.9) + st;
         if (cost_l < best - 1e-9) {
             best = cost_l;
             *kw_out = kw;
@@ -898,7 +907,7 @@ void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int* k
 
 int multi_pick_kw(int pairs, int groups, int n, int fmt, int grid) {
     int kw, local;
-    multi_plan(pairs, groups, n, fmt, grid, ME_STORE, &kw, &local);
+    multi_plan(pairs, groups, n, fmt, grid, ME_STORE, MX_PLAIN_F32, &kw, &local);
     return kw;
 }
 
@@ -978,7 +987,7 @@ extern "C" jinf_status jinf_b200_gemv_q4m_batch_qt(const void* q4m, int qtype, c
     const int grid = multi_grid(device_sms());
     int local = 0;
     if (kw == 0) {
-        multi_plan(sh.pairs, sh.groups, batch, fmt, grid, ME_STORE, &kw, &local);
+        multi_plan(sh.pairs, sh.groups, batch, fmt, grid, ME_STORE, MX_PLAIN_F32, &kw, &local);
     } else if (kw < 0) {  // a forced split with the per-CTA sharing
         kw = -kw;
         local = 1;

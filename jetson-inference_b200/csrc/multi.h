@@ -74,10 +74,10 @@ struct MultiParams {
     uint64_t pf_bytes;
 };
 
-// How an n-vector GEMV of this shape runs on `grid` CTAs: the K parts (the part's records
-// within shared memory next to the weight rings) and whether a CTA's warps split each tile
-// pair (*local), by the smallest estimated time; kw 0 when no split fits.
-void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int* kw, int* local);
+// How an n-vector GEMV of this shape and input kind (xm) runs on `grid` CTAs: the K parts (the
+// part's records within shared memory next to the weight rings) and whether a CTA's warps
+// split each tile pair (*local), by the smallest estimated time; kw 0 when no split fits.
+void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int xm, int* kw, int* local);
 int multi_pick_kw(int pairs, int groups, int n, int fmt, int grid);
 int multi_grid(int num_sms);
 size_t multi_workspace_bytes(int pairs, int kw, int n);
