@@ -869,7 +869,7 @@ int multi_grid(int num_sms) { return num_sms; }
 //     units per round of loads);
 //   per CTA, one K part only: 2.5 + rounds of pairs x (the warp's share of the groups + 0.9
 //     for the three barriers and the 16-warp merge of each pair);
-// both plus the CTA's input staging spread over its 16 warps (n x the part's groups: 0.45
+// both plus the CTA's input staging spread over its 16 warps (n x the part's groups: 0.7
 // units each when converted from fp32, 0.15 when copied as records). The per-CTA form wins
 // where the pairs are about as many as the CTAs and one part holds every group (the 8B QKV,
 // o and gate|up projections); with several K parts it lost every measured case, so it is
@@ -878,7 +878,7 @@ void multi_plan(int pairs, int groups, int n, int fmt, int grid, int epi, int xm
     *kw_out = 0;
     *local_out = 0;
     if (pairs < 1 || groups < 1 || n < 1 || n > MULTI_MAX || grid < 1) return;
-    const double stage = xm == MX_RECORDS ? 0.15 : 0.45;
+    const double stage = xm == MX_RECORDS ? 0.15 : 0.7;
     double best = 1e300;
     const int lim = groups < kMultiMaxKw ? groups : kMultiMaxKw;
     for (int kw = 1; kw <= lim; ++kw) {
