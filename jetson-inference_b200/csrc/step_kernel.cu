@@ -1238,24 +1238,29 @@ namespace {
 // The multi-sequence attention's split [p0, p1) of one kv head on the tensor cores
 // (mma.sync m16n8k16, fp16 operands, fp32 accumulation). Blocks of TA_BLK positions: their K
 // and V rows are copied into shared memory (cp.async, rows padded to HD + 8 halves so that
-// ldmatrix reads no bank twice), TA_NST - 1 blocks ahead of the arithmetic. Per block:
+// ldmatrix reads no bank twice), TA_NST - 1 blocks ahead of the arithmetic. CTAs of 8 warps,
+// two per SM (one CTA of 16 warps per SM left the copies of one block per SM in flight too
+// few to stream long caches). Per block:
 //   scores S^T = K Q^T with the query heads as the MMA's 8 columns (rows of q past GQ zero):
-//     warp w takes positions 8 (w & 7) .. +7 and half the head dims (w >> 3); q enters as
-//     fp16 hi + lo (q = hi + lo to about 22 bits), so two MMAs per step;
-//   an online softmax per head (one warp each), in fp32, over the two halves' sums;
-//   O^T += V^T P^T with the heads as columns again: warp w takes head dims 16 (w & 7) .. +15
-//     and positions 32 (w >> 3) .. +31; p enters as fp16 hi + lo.
+//     warp w takes positions 8 w .. +7 over all head dims; q enters as fp16 hi + lo
+//     (q = hi + lo to about 22 bits), so two MMAs per step;
+//   an online softmax per head (one warp each), in fp32;
+//   O^T += V^T P^T with the heads as columns again: warp w takes head dims 16 (w % (HD / 16))
+//     .. +15 and, at head dim 64, half the positions; p enters as fp16 hi + lo.
 // K and V are the cache's fp16 values, so the products are those of the fp32 arithmetic to
 // the hi + lo rounding; sums are fp32. Leaves the split's partial (acc, m, l) in `part`
 // ([GQ][HD + 2]), as attn_split does.
 constexpr int TA_BLK = 64;
-constexpr int TA_NST = 4;
+constexpr int TA_NST = 3;
+constexpr int TA_THREADS = 256;
+constexpr int TA_NW = TA_THREADS / 32;
 template <int HD>
 __host__ __device__ constexpr size_t ta_smem() {
     return (size_t)TA_NST * 2 * TA_BLK * (HD + 8) * 2  // K and V stages
-           + 2 * 8 * TA_BLK * 4                        // scores of the two halves [2][8][TA_BLK]
+           + 8 * TA_BLK * 4                            // scores [8][TA_BLK]
            + 2 * 8 * (TA_BLK + 8) * 2                  // p hi, lo [8][TA_BLK + 8]
-           + 8 * 4 * 4;                                // m, l, correction per head
+           + 8 * 4 * 4                                 // m, l, correction per head
+           + (size_t)(HD / 16) * 32 * 16;              // q fragments [k-step][lane]
 }
 
 template <int HD, int GQ>
@@ -1265,23 +1270,27 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
     constexpr int LD = HD + 8;                 // padded row, halves
     constexpr int STH = 2 * TA_BLK * LD;        // halves per stage
     constexpr int PST = TA_BLK + 8;             // p row, halves
-    constexpr int KH = HD / 32;                 // score k-steps per warp (half the head dims)
+    constexpr int KS = HD / 16;                 // score k-steps (all head dims)
     constexpr int MTL = HD / 16;                // p.v m-tiles (16 head dims)
+    constexpr int PH = TA_NW / MTL;             // p.v position parts (1 at head dim 128, 2 at 64)
+    constexpr int PP = TA_BLK / PH;             // positions per part
     constexpr int CH = HD / 8;                  // 16-byte chunks per cache row
-    static_assert((size_t)2 * HD * 8 * 4 <= (size_t)TA_NST * STH * 2, "the final sums reuse the stages");
+    static_assert(KS % 2 == 0 && TA_NW % MTL == 0 && PP % 16 == 0, "fragment tiling");
+    static_assert((size_t)PH * HD * 8 * 4 <= (size_t)TA_NST * STH * 2, "the final sums reuse the stages");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gid = lane >> 2, tig = lane & 3;
     __half* stages = reinterpret_cast<__half*>(sm);
     float* s_part = reinterpret_cast<float*>(sm + (size_t)TA_NST * STH * 2);
-    __half* p_hi = reinterpret_cast<__half*>(s_part + 2 * 8 * TA_BLK);
+    __half* p_hi = reinterpret_cast<__half*>(s_part + 8 * TA_BLK);
     __half* p_lo = p_hi + 8 * PST;
     float* ml = reinterpret_cast<float*>(p_lo + 8 * PST);
+    uint4* qf = reinterpret_cast<uint4*>(ml + 8 * 4);  // per k-step and lane: q hi (2 words), q lo (2)
     const int nb = (p1 - p0 + TA_BLK - 1) / TA_BLK;
 
     // block b's K and V rows into stage b % TA_NST; rows past p1 are zero-filled
     auto load_block = [&](int b) {
         __half* sk = stages + (b % TA_NST) * STH;
         const int pos0 = p0 + b * TA_BLK;
-        for (int i = tid; i < 2 * TA_BLK * CH; i += STEP_THREADS) {
+        for (int i = tid; i < 2 * TA_BLK * CH; i += TA_THREADS) {
             const int isv = i / (TA_BLK * CH), r = (i / CH) % TA_BLK, c = i % CH;
             const bool in = pos0 + r < p1;
             const __half* src = (isv ? vb : kb) + (size_t)(in ? pos0 + r : p0) * HD + c * 8;
@@ -1296,22 +1305,26 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
 
-    // the query fragments of this warp's score half: head gid (zero past GQ), dims
-    // 16 (kh KH + s) + 8 h + 2 tig, +1, scaled by 1 / sqrt(HD)
-    const int nt = warp & 7, kh = warp >> 3;
-    uint32_t qh[KH][2], ql[KH][2];
-    {
+    // the query fragments: head gid (zero past GQ), dims 16 s + 8 h + 2 tig, +1, scaled by
+    // 1 / sqrt(HD)
+    // (the same for every warp: warp 0 stores them once, shared, and each warp reloads them
+    // per block rather than holding 4 KS registers)
+    const int nt = warp;
+    if (warp == 0) {
         const float scale = rsqrtf((float)HD);
 #pragma unroll
-        for (int st = 0; st < KH; ++st)
+        for (int st = 0; st < KS; ++st) {
+            uint32_t hi[2], lo[2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float2 t = make_float2(0.f, 0.f);
-                if (gid < GQ) t = __ldcg(reinterpret_cast<const float2*>(q + gid * HD + (kh * KH + st) * 16 + h * 8 + tig * 2));
-                split_h2(t.x * scale, t.y * scale, qh[st][h], ql[st][h]);
+                if (gid < GQ) t = __ldcg(reinterpret_cast<const float2*>(q + gid * HD + st * 16 + h * 8 + tig * 2));
+                split_h2(t.x * scale, t.y * scale, hi[h], lo[h]);
             }
+            qf[st * 32 + lane] = make_uint4(hi[0], hi[1], lo[0], lo[1]);
+        }
     }
-    for (int i = tid; i < 8 * PST; i += STEP_THREADS) {  // rows of heads past GQ stay zero
+    for (int i = tid; i < 8 * PST; i += TA_THREADS) {  // rows of heads past GQ stay zero
         p_hi[i] = __float2half_rn(0.f);
         p_lo[i] = __float2half_rn(0.f);
     }
@@ -1320,7 +1333,7 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
         ml[tid * 4 + 1] = 0.f;
         ml[tid * 4 + 2] = 0.f;
     }
-    const int mt = warp & 7, ph = warp >> 3;  // p.v: head dims 16 mt .. +15, positions 32 ph .. +31
+    const int mt = warp % MTL, ph = warp / MTL;  // p.v: head dims 16 mt .. +15, positions PP ph .. +PP-1
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int b = 0; b < nb; ++b) {
         asm volatile("cp.async.wait_group %0;" ::"n"(TA_NST - 2) : "memory");
@@ -1331,21 +1344,22 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
         const __half* sk = stages + (b % TA_NST) * STH;
         const __half* sv = sk + TA_BLK * LD;
         {
-            // scores of positions 8 nt .. +7 over head dims [32 kh KH / 2 ...): lane l addresses
-            // row 8 nt + (l & 7) of matrix l >> 3 (8 dims each)
+            // scores of positions 8 nt .. +7: lane l addresses row 8 nt + (l & 7) of matrix
+            // l >> 3 (8 dims each)
             float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int st = 0; st < KH; st += 2) {
+            for (int st = 0; st < KS; st += 2) {
                 uint32_t b0, b1, b2, b3;
-                const int dim = (kh * KH + st) * 16 + (lane >> 3) * 8;
+                const int dim = st * 16 + (lane >> 3) * 8;
                 ldsm_x4(smem_u32(sk + (8 * nt + (lane & 7)) * LD + dim), b0, b1, b2, b3);
-                mma_f16(c, qh[st][0], 0u, qh[st][1], 0u, b0, b1);
-                mma_f16(c, ql[st][0], 0u, ql[st][1], 0u, b0, b1);
-                mma_f16(c, qh[st + 1][0], 0u, qh[st + 1][1], 0u, b2, b3);
-                mma_f16(c, ql[st + 1][0], 0u, ql[st + 1][1], 0u, b2, b3);
+                const uint4 f0 = qf[st * 32 + lane], f1 = qf[(st + 1) * 32 + lane];
+                mma_f16(c, f0.x, 0u, f0.y, 0u, b0, b1);
+                mma_f16(c, f0.z, 0u, f0.w, 0u, b0, b1);
+                mma_f16(c, f1.x, 0u, f1.y, 0u, b2, b3);
+                mma_f16(c, f1.z, 0u, f1.w, 0u, b2, b3);
             }
             if (gid < GQ)
-                *reinterpret_cast<float2*>(s_part + (kh * 8 + gid) * TA_BLK + 8 * nt + 2 * tig) = make_float2(c[0], c[1]);
+                *reinterpret_cast<float2*>(s_part + gid * TA_BLK + 8 * nt + 2 * tig) = make_float2(c[0], c[1]);
         }
         __syncthreads();
         if (warp < GQ) {  // online softmax of head `warp`: lanes own positions lane, lane + 32
@@ -1354,7 +1368,7 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
                 const int j = lane + 32 * t;
-                sc[t] = j < n ? s_part[warp * TA_BLK + j] + s_part[(8 + warp) * TA_BLK + j] : -INFINITY;
+                sc[t] = j < n ? s_part[warp * TA_BLK + j] : -INFINITY;
                 mb = fmaxf(mb, sc[t]);
             }
             const float mo = ml[warp * 4], mn = fmaxf(mo, warp_max(mb));
@@ -1376,15 +1390,15 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
             }
         }
         __syncthreads();
-        if (mt < MTL) {
+        {
             const float c0 = ml[(2 * tig) * 4 + 2], c1 = ml[(2 * tig + 1) * 4 + 2];  // columns = heads 2 tig, +1
             acc[0] *= c0;
             acc[1] *= c1;
             acc[2] *= c0;
             acc[3] *= c1;
 #pragma unroll
-            for (int ks = 0; ks < 2; ++ks) {
-                const int k0 = 32 * ph + 16 * ks;  // positions
+            for (int ks = 0; ks < PP / 16; ++ks) {
+                const int k0 = PP * ph + 16 * ks;  // positions
                 // V^T fragments: matrix l >> 3 = (positions +8 if bit 1, dims +8 if bit 0)
                 uint32_t a0, a1, a2, a3;
                 ldsm_x4_t(smem_u32(sv + (k0 + (lane & 7) + ((lane >> 4) & 1) * 8) * LD + 16 * mt + ((lane >> 3) & 1) * 8),
@@ -1400,17 +1414,20 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");  // the trailing groups are empty
     __syncthreads();
-    // the two position halves summed in order: red [2][HD][8] over the stages
+    // the position parts summed in order: red [PH][HD][8] over the stages
     float* red = reinterpret_cast<float*>(sm);
-    if (mt < MTL) {
+    {
         float* r0 = red + ((size_t)ph * HD + 16 * mt + gid) * 8 + 2 * tig;
         *reinterpret_cast<float2*>(r0) = make_float2(acc[0], acc[1]);
         *reinterpret_cast<float2*>(r0 + 8 * 8) = make_float2(acc[2], acc[3]);
     }
     __syncthreads();
-    for (int o = tid; o < GQ * HD; o += STEP_THREADS) {
+    for (int o = tid; o < GQ * HD; o += TA_THREADS) {
         const int g = o / HD, dd = o % HD;
-        part[g * (HD + 2) + dd] = red[(size_t)dd * 8 + g] + red[((size_t)HD + dd) * 8 + g];
+        float a = red[(size_t)dd * 8 + g];
+#pragma unroll
+        for (int h = 1; h < PH; ++h) a += red[((size_t)h * HD + dd) * 8 + g];
+        part[g * (HD + 2) + dd] = a;
         if (dd == 0) {
             part[g * (HD + 2) + HD] = p1 > p0 ? ml[g * 4] : -INFINITY;  // an empty split
             part[g * (HD + 2) + HD + 1] = ml[g * 4 + 1];
@@ -1419,7 +1436,7 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
 }
 
 template <int HD, int GQ>
-__global__ void __launch_bounds__(STEP_THREADS, 1) k_attn_multi(const MultiAttnParams p) {
+__global__ void __launch_bounds__(TA_THREADS, 2) k_attn_multi(const MultiAttnParams p) {
     extern __shared__ __align__(16) uint8_t smem_a[];
     __shared__ int is_last;
     const int tid = threadIdx.x;
@@ -1454,7 +1471,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_attn_multi(const MultiAttnP
     float* fw = reinterpret_cast<float*>(smem_a);  // [GQ][S] m_s, then the weights
     float* fl = fw + GQ * S;                        // [GQ][S] l_s
     float* ls = fl + GQ * S;                        // [GQ] L
-    for (int i = tid; i < GQ * S; i += STEP_THREADS) {
+    for (int i = tid; i < GQ * S; i += TA_THREADS) {
         const int g = i / S, s2 = i % S;
         fw[i] = __ldcg(pbase + (size_t)s2 * pst + g * (HD + 2) + HD);
         fl[i] = __ldcg(pbase + (size_t)s2 * pst + g * (HD + 2) + HD + 1);
@@ -1473,7 +1490,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) k_attn_multi(const MultiAttnP
         ls[tid] = L;
     }
     __syncthreads();
-    for (int o = tid; o < GQ * HD / 2; o += STEP_THREADS) {
+    for (int o = tid; o < GQ * HD / 2; o += TA_THREADS) {
         const int g = o / (HD / 2), d2 = o % (HD / 2);
         float2 a = make_float2(0.f, 0.f);
         for (int s0 = 0; s0 < S; s0 += 8) {
@@ -1522,7 +1539,7 @@ cudaError_t launch_attn_multi(const MultiAttnParams& p0, cudaStream_t s, bool pd
         cudaError_t e = cudaFuncSetAttribute(k_attn_multi<HD, GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         int k = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, k_attn_multi<HD, GQ>, STEP_THREADS, smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k, k_attn_multi<HD, GQ>, TA_THREADS, smem);
         if (e != cudaSuccess) return e;
         per_sm[dev] = k > 0 ? k : 1;
     }
@@ -1532,7 +1549,7 @@ cudaError_t launch_attn_multi(const MultiAttnParams& p0, cudaStream_t s, bool pd
     const int G = std::max(1, std::min(p.s_max, per_sm[dev] * sms / (p.n * p.n_kv_heads)));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(p.n_kv_heads * G), (unsigned)p.n);
-    cfg.blockDim = dim3(STEP_THREADS);
+    cfg.blockDim = dim3(TA_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
