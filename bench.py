@@ -64,6 +64,7 @@ class ClockSampler:
         self.idx = gpu_index
         self.proc = None
         self.lines = []
+        self.n0 = 0
 
     def __enter__(self):
         try:
@@ -72,7 +73,12 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
-            time.sleep(0.05)
+            # nvidia-smi takes a while to start: wait for its first sample, so that it samples
+            # while the timed region runs; samples taken before the region are not counted
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0:
+                time.sleep(0.005)
+            self.n0 = len(self.lines)
         except Exception:
             self.proc = None
         return self
@@ -83,7 +89,10 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
-            time.sleep(0.03)
+            # a region shorter than the sampling period: the first sample after it ends
+            t0 = time.time()
+            while len(self.lines) <= self.n0 and time.time() - t0 < 0.2:
+                time.sleep(0.002)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -93,7 +102,7 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.n0:]:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
