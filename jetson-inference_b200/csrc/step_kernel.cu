@@ -78,16 +78,20 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 }
 
 // Wait until *c >= target. Gives up after `limit` polls, or as soon as another CTA has
-// recorded an error; a timeout records DEV_ERR_TIMEOUT.
+// recorded an error; a timeout records DEV_ERR_TIMEOUT. The counter is polled back to back
+// (one L2 round trip per poll, so a phase hand-off is seen within about one round trip);
+// every 64th poll also reads the error word, checks the limit and sleeps briefly.
 __device__ bool wait_ge(const unsigned* c, unsigned target, DeviceState* st, unsigned long long limit) {
     for (unsigned long long it = 0;; ++it) {
         if (ld_acquire(c) >= target) return true;
-        if (*(volatile int*)&st->error != DEV_OK) return false;
-        if (it >= limit) {
-            atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
-            return false;
+        if ((it & 63) == 63) {
+            if (*(volatile int*)&st->error != DEV_OK) return false;
+            if (it >= limit) {
+                atomicCAS(&st->error, DEV_OK, DEV_ERR_TIMEOUT);
+                return false;
+            }
+            __nanosleep(32);
         }
-        __nanosleep(32);
     }
 }
 
