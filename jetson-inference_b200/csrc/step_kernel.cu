@@ -1240,81 +1240,77 @@ extern "C" int jinf_step_trace_read(unsigned long long* host, size_t n) {
 namespace {
 
 // The multi-sequence attention's split [p0, p1) of one kv head on the tensor cores
-// (mma.sync m16n8k16, fp16 operands, fp32 accumulation). Blocks of TA_BLK positions: their K
-// and V rows are copied into shared memory (cp.async, rows padded to HD + 8 halves so that
-// ldmatrix reads no bank twice), TA_NST - 1 blocks ahead of the arithmetic. CTAs of 8 warps,
-// two per SM (one CTA of 16 warps per SM left the copies of one block per SM in flight too
-// few to stream long caches). Per block:
-//   scores S^T = K Q^T with the query heads as the MMA's 8 columns (rows of q past GQ zero):
-//     warp w takes positions 8 w .. +7 over all head dims; q enters as fp16 hi + lo
-//     (q = hi + lo to about 22 bits), so two MMAs per step;
-//   an online softmax per head (one warp each), in fp32;
-//   O^T += V^T P^T with the heads as columns again: warp w takes head dims 16 (w % (HD / 16))
-//     .. +15 and, at head dim 64, half the positions; p enters as fp16 hi + lo.
-// K and V are the cache's fp16 values, so the products are those of the fp32 arithmetic to
-// the hi + lo rounding; sums are fp32. Leaves the split's partial (acc, m, l) in `part`
-// ([GQ][HD + 2]), as attn_split does.
+// (mma.sync, fp16 operands, fp32 accumulation), in CTAs of 8 warps, two per SM. K and V are
+// the cache's fp16 values; q and the softmax weights p enter as fp16 hi + lo pairs (x = hi +
+// lo to about 22 bits), so every product is the fp32 one to that rounding, and sums are fp32.
+// The split is cut into 64-position blocks only to size the splits (TA_BLK); each warp
+// streams chunks of 8 positions (attn_split_w). Leaves the split's partial (acc, m, l) in
+// `part` ([GQ][HD + 2]), as attn_split does.
 constexpr int TA_BLK = 64;
-constexpr int TA_NST = 3;
 constexpr int TA_THREADS = 256;
 constexpr int TA_NW = TA_THREADS / 32;
+constexpr int TW_NST = 3;  // chunks in each warp's ring (attn_split_w)
+
+// The split computed warp by warp, with no CTA barrier per chunk: warp w streams its own
+// chunks of 8 positions (chunks w, w + 8, ... of the split) through a private cp.async ring of
+// TW_NST chunks in shared memory, and keeps its own online softmax (m, l per head) and output
+// accumulator; the 8 warps are merged once at the end, in warp order. Per chunk:
+//   scores S = Q K^T (m16n8k16: the query heads as the MMA's rows, q hi + lo, the chunk's 8
+//     positions as its columns), masked past p1;
+//   the chunk's softmax weights stay in the registers that hold the scores: their layout
+//     (head gid, positions 2 tig, 2 tig + 1) is the B fragment of the next MMA;
+//   O^T += V^T P^T (m16n8k8: head dims as rows, the 8 positions as k, the heads as columns;
+//     p hi + lo), V^T fragments by ldmatrix .trans.
 template <int HD>
-__host__ __device__ constexpr size_t ta_smem() {
-    return (size_t)TA_NST * 2 * TA_BLK * (HD + 8) * 2  // K and V stages
-           + 8 * TA_BLK * 4                            // scores [8][TA_BLK]
-           + 2 * 8 * (TA_BLK + 8) * 2                  // p hi, lo [8][TA_BLK + 8]
-           + 8 * 4 * 4                                 // m, l, correction per head
+__host__ __device__ constexpr size_t tw_smem() {
+    return (size_t)TA_NW * TW_NST * 16 * (HD + 8) * 2  // per warp: TW_NST chunks of K and V rows
            + (size_t)(HD / 16) * 32 * 16;              // q fragments [k-step][lane]
 }
 
-template <int HD, int GQ>
-__device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, const __half* vb, int p0, int p1,
-                                              uint8_t* sm, float* part) {
-    static_assert(GQ <= 8 && HD % 32 == 0 && HD <= 128, "heads are the MMA's 8 columns");
-    constexpr int LD = HD + 8;                 // padded row, halves
-    constexpr int STH = 2 * TA_BLK * LD;        // halves per stage
-    constexpr int PST = TA_BLK + 8;             // p row, halves
-    constexpr int KS = HD / 16;                 // score k-steps (all head dims)
-    constexpr int MTL = HD / 16;                // p.v m-tiles (16 head dims)
-    constexpr int PH = TA_NW / MTL;             // p.v position parts (1 at head dim 128, 2 at 64)
-    constexpr int PP = TA_BLK / PH;             // positions per part
-    constexpr int CH = HD / 8;                  // 16-byte chunks per cache row
-    static_assert(KS % 2 == 0 && TA_NW % MTL == 0 && PP % 16 == 0, "fragment tiling");
-    static_assert((size_t)PH * HD * 8 * 4 <= (size_t)TA_NST * STH * 2, "the final sums reuse the stages");
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gid = lane >> 2, tig = lane & 3;
-    __half* stages = reinterpret_cast<__half*>(sm);
-    float* s_part = reinterpret_cast<float*>(sm + (size_t)TA_NST * STH * 2);
-    __half* p_hi = reinterpret_cast<__half*>(s_part + 8 * TA_BLK);
-    __half* p_lo = p_hi + 8 * PST;
-    float* ml = reinterpret_cast<float*>(p_lo + 8 * PST);
-    uint4* qf = reinterpret_cast<uint4*>(ml + 8 * 4);  // per k-step and lane: q hi (2 words), q lo (2)
-    const int nb = (p1 - p0 + TA_BLK - 1) / TA_BLK;
+__device__ __forceinline__ void mma_f16_k8(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(b0));
+}
 
-    // block b's K and V rows into stage b % TA_NST; rows past p1 are zero-filled
-    auto load_block = [&](int b) {
-        __half* sk = stages + (b % TA_NST) * STH;
-        const int pos0 = p0 + b * TA_BLK;
-        for (int i = tid; i < 2 * TA_BLK * CH; i += TA_THREADS) {
-            const int isv = i / (TA_BLK * CH), r = (i / CH) % TA_BLK, c = i % CH;
-            const bool in = pos0 + r < p1;
-            const __half* src = (isv ? vb : kb) + (size_t)(in ? pos0 + r : p0) * HD + c * 8;
-            const uint32_t dst = smem_u32(sk + isv * TA_BLK * LD + r * LD + c * 8);
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(in ? 16 : 0)
+template <int HD, int GQ>
+__device__ __forceinline__ void attn_split_w(const float* q, const __half* kb, const __half* vb, int p0, int p1,
+                                             uint8_t* sm, float* part) {
+    static_assert(GQ <= 8 && HD % 32 == 0 && HD <= 128, "heads are the MMA's 8 columns");
+    constexpr int LD = HD + 8;               // padded row, halves
+    constexpr int CHW = 16 * LD;             // halves per chunk: K rows 0..7, V rows 8..15
+    constexpr int KS = HD / 16;              // score k-steps
+    constexpr int MTL = HD / 16;             // p.v m-tiles
+    constexpr int CH = HD / 8;               // 16-byte pieces per cache row
+    static_assert((size_t)TA_NW * GQ * HD * 4 <= (size_t)TA_NW * TW_NST * CHW * 2, "the merge reuses the rings");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, gid = lane >> 2, tig = lane & 3;
+    __half* ring = reinterpret_cast<__half*>(sm) + (size_t)warp * TW_NST * CHW;
+    uint4* qf = reinterpret_cast<uint4*>(sm + (size_t)TA_NW * TW_NST * CHW * 2);
+    const int nc = (p1 - p0 + 7) / 8;                     // chunks of the split
+    const int mine = nc > warp ? (nc - warp + TA_NW - 1) / TA_NW : 0;  // this warp's chunks
+
+    // chunk k of this warp (positions p0 + 8 (warp + 8 k) ..) into ring slot k % TW_NST; rows
+    // past p1 are zero-filled
+    auto load_chunk = [&](int k) {
+        __half* dst = ring + (k % TW_NST) * CHW;
+        const int pos0 = p0 + 8 * (warp + TA_NW * k);
+#pragma unroll
+        for (int i = lane; i < 16 * CH; i += 32) {
+            const int r = i / CH, c = i % CH, pr = r & 7;
+            const bool in = pos0 + pr < p1;
+            const __half* src = (r < 8 ? kb : vb) + (size_t)(in ? pos0 + pr : p0) * HD + c * 8;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + r * LD + c * 8)),
+                         "l"(src), "r"(in ? 16 : 0)
                          : "memory");
         }
     };
 #pragma unroll
-    for (int b = 0; b < TA_NST - 1; ++b) {
-        if (b < nb) load_block(b);
+    for (int k = 0; k < TW_NST - 1; ++k) {
+        if (k < mine) load_chunk(k);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
-
-    // the query fragments: head gid (zero past GQ), dims 16 s + 8 h + 2 tig, +1, scaled by
-    // 1 / sqrt(HD)
-    // (the same for every warp: warp 0 stores them once, shared, and each warp reloads them
-    // per block rather than holding 4 KS registers)
-    const int nt = warp;
-    if (warp == 0) {
+    if (warp == 0) {  // the query fragments (the same for every warp): head gid, zero past GQ
         const float scale = rsqrtf((float)HD);
 #pragma unroll
         for (int st = 0; st < KS; ++st) {
@@ -1328,113 +1324,103 @@ __device__ __forceinline__ void attn_split_tc(const float* q, const __half* kb, 
             qf[st * 32 + lane] = make_uint4(hi[0], hi[1], lo[0], lo[1]);
         }
     }
-    for (int i = tid; i < 8 * PST; i += TA_THREADS) {  // rows of heads past GQ stay zero
-        p_hi[i] = __float2half_rn(0.f);
-        p_lo[i] = __float2half_rn(0.f);
-    }
-    if (tid < 8) {
-        ml[tid * 4] = -INFINITY;
-        ml[tid * 4 + 1] = 0.f;
-        ml[tid * 4 + 2] = 0.f;
-    }
-    const int mt = warp % MTL, ph = warp / MTL;  // p.v: head dims 16 mt .. +15, positions PP ph .. +PP-1
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int b = 0; b < nb; ++b) {
-        asm volatile("cp.async.wait_group %0;" ::"n"(TA_NST - 2) : "memory");
-        __syncthreads();  // block b landed for every thread; block b - 1's stage is free
-        if (b + TA_NST - 1 < nb) load_block(b + TA_NST - 1);
+    __syncthreads();  // the query fragments
+
+    float m = -INFINITY, l = 0.f;  // head gid's running max and sum (the same in its 4 lanes)
+    float acc[MTL][4];
+#pragma unroll
+    for (int t = 0; t < MTL; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[t][i] = 0.f;
+    for (int k = 0; k < mine; ++k) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(TW_NST - 2) : "memory");
+        __syncwarp();  // every lane's copies of chunk k landed; chunk k - 1's slot is free
+        if (k + TW_NST - 1 < mine) load_chunk(k + TW_NST - 1);
         asm volatile("cp.async.commit_group;" ::: "memory");
-        const int n = min(TA_BLK, p1 - (p0 + b * TA_BLK));
-        const __half* sk = stages + (b % TA_NST) * STH;
-        const __half* sv = sk + TA_BLK * LD;
-        {
-            // scores of positions 8 nt .. +7: lane l addresses row 8 nt + (l & 7) of matrix
-            // l >> 3 (8 dims each)
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
+        const __half* ck = ring + (k % TW_NST) * CHW;
+        const __half* cv = ck + 8 * LD;
+        const int pos0 = p0 + 8 * (warp + TA_NW * k);
+        // scores: lane l addresses row (l & 7) of matrix l >> 3 (8 head dims each)
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int st = 0; st < KS; st += 2) {
-                uint32_t b0, b1, b2, b3;
-                const int dim = st * 16 + (lane >> 3) * 8;
-                ldsm_x4(smem_u32(sk + (8 * nt + (lane & 7)) * LD + dim), b0, b1, b2, b3);
-                const uint4 f0 = qf[st * 32 + lane], f1 = qf[(st + 1) * 32 + lane];
-                mma_f16(c, f0.x, 0u, f0.y, 0u, b0, b1);
-                mma_f16(c, f0.z, 0u, f0.w, 0u, b0, b1);
-                mma_f16(c, f1.x, 0u, f1.y, 0u, b2, b3);
-                mma_f16(c, f1.z, 0u, f1.w, 0u, b2, b3);
-            }
-            if (gid < GQ)
-                *reinterpret_cast<float2*>(s_part + gid * TA_BLK + 8 * nt + 2 * tig) = make_float2(c[0], c[1]);
+        for (int st = 0; st < KS; st += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(smem_u32(ck + (lane & 7) * LD + st * 16 + (lane >> 3) * 8), b0, b1, b2, b3);
+            const uint4 f0 = qf[st * 32 + lane], f1 = qf[(st + 1) * 32 + lane];
+            mma_f16(c, f0.x, 0u, f0.y, 0u, b0, b1);
+            mma_f16(c, f0.z, 0u, f0.w, 0u, b0, b1);
+            mma_f16(c, f1.x, 0u, f1.y, 0u, b2, b3);
+            mma_f16(c, f1.z, 0u, f1.w, 0u, b2, b3);
         }
-        __syncthreads();
-        if (warp < GQ) {  // online softmax of head `warp`: lanes own positions lane, lane + 32
-            float sc[2], e[2];
-            float mb = -INFINITY;
+        // online softmax of head gid over the chunk's positions 2 tig, 2 tig + 1
+        const float s0 = pos0 + 2 * tig < p1 ? c[0] : -INFINITY, s1 = pos0 + 2 * tig + 1 < p1 ? c[1] : -INFINITY;
+        float mc = fmaxf(s0, s1);
+        mc = fmaxf(mc, __shfl_xor_sync(JINF_FULL_MASK, mc, 1));
+        mc = fmaxf(mc, __shfl_xor_sync(JINF_FULL_MASK, mc, 2));
+        const float mn = fmaxf(m, mc);  // finite: a chunk holds at least one position
+        const float corr = m == -INFINITY ? 0.f : expf(m - mn);
+        float e0 = expf(s0 - mn), e1 = expf(s1 - mn);
+        if (gid >= GQ) e0 = e1 = 0.f;
+        float es = e0 + e1;
+        es += __shfl_xor_sync(JINF_FULL_MASK, es, 1);
+        es += __shfl_xor_sync(JINF_FULL_MASK, es, 2);
+        l = fmaf(l, corr, es);
+        m = mn;
+        uint32_t ph, pl;
+        split_h2(e0, e1, ph, pl);
+        // the accumulator's columns are heads 2 tig, 2 tig + 1: their corrections
+        const float ca = __shfl_sync(JINF_FULL_MASK, corr, 8 * tig), cb = __shfl_sync(JINF_FULL_MASK, corr, 8 * tig + 4);
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                const int j = lane + 32 * t;
-                sc[t] = j < n ? s_part[warp * TA_BLK + j] : -INFINITY;
-                mb = fmaxf(mb, sc[t]);
-            }
-            const float mo = ml[warp * 4], mn = fmaxf(mo, warp_max(mb));
+        for (int t = 0; t < MTL; t += 2) {
+            // V^T fragments of head dims 16 t .. 16 t + 31: matrix l >> 3 covers dims 8 (l >> 3) ..
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_t(smem_u32(cv + (lane & 7) * LD + t * 16 + (lane >> 3) * 8), a0, a1, a2, a3);
 #pragma unroll
-            for (int t = 0; t < 2; ++t) e[t] = lane + 32 * t < n ? expf(sc[t] - mn) : 0.f;
-            const float corr = mo == -INFINITY ? 0.f : expf(mo - mn);
-            const float ln = fmaf(ml[warp * 4 + 1], corr, warp_sum(e[0] + e[1]));
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                const __half h = __float2half_rn(e[t]);
-                p_hi[warp * PST + lane + 32 * t] = h;
-                p_lo[warp * PST + lane + 32 * t] = __float2half_rn(e[t] - __half2float(h));
-            }
-            __syncwarp();
-            if (lane == 0) {
-                ml[warp * 4] = mn;
-                ml[warp * 4 + 1] = ln;
-                ml[warp * 4 + 2] = corr;
-            }
-        }
-        __syncthreads();
-        {
-            const float c0 = ml[(2 * tig) * 4 + 2], c1 = ml[(2 * tig + 1) * 4 + 2];  // columns = heads 2 tig, +1
-            acc[0] *= c0;
-            acc[1] *= c1;
-            acc[2] *= c0;
-            acc[3] *= c1;
-#pragma unroll
-            for (int ks = 0; ks < PP / 16; ++ks) {
-                const int k0 = PP * ph + 16 * ks;  // positions
-                // V^T fragments: matrix l >> 3 = (positions +8 if bit 1, dims +8 if bit 0)
-                uint32_t a0, a1, a2, a3;
-                ldsm_x4_t(smem_u32(sv + (k0 + (lane & 7) + ((lane >> 4) & 1) * 8) * LD + 16 * mt + ((lane >> 3) & 1) * 8),
-                          a0, a1, a2, a3);
-                const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(p_hi + gid * PST + k0 + 2 * tig);
-                const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(p_hi + gid * PST + k0 + 8 + 2 * tig);
-                const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(p_lo + gid * PST + k0 + 2 * tig);
-                const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(p_lo + gid * PST + k0 + 8 + 2 * tig);
-                mma_f16(acc, a0, a1, a2, a3, bh0, bh1);
-                mma_f16(acc, a0, a1, a2, a3, bl0, bl1);
+            for (int u = 0; u < 2; ++u) {
+                float (&o)[4] = acc[t + u];
+                o[0] *= ca;
+                o[1] *= cb;
+                o[2] *= ca;
+                o[3] *= cb;
+                mma_f16_k8(o, u ? a2 : a0, u ? a3 : a1, ph);
+                mma_f16_k8(o, u ? a2 : a0, u ? a3 : a1, pl);
             }
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");  // the trailing groups are empty
-    __syncthreads();
-    // the position parts summed in order: red [PH][HD][8] over the stages
-    float* red = reinterpret_cast<float*>(sm);
-    {
-        float* r0 = red + ((size_t)ph * HD + 16 * mt + gid) * 8 + 2 * tig;
-        *reinterpret_cast<float2*>(r0) = make_float2(acc[0], acc[1]);
-        *reinterpret_cast<float2*>(r0 + 8 * 8) = make_float2(acc[2], acc[3]);
+    __syncthreads();  // every warp is done with its ring: the merge reuses them
+    // per warp: m, l of each head, and its accumulator [GQ][HD], then merged in warp order
+    float* wacc = reinterpret_cast<float*>(sm);                            // [TA_NW][GQ][HD]
+    float* wml = reinterpret_cast<float*>(sm) + (size_t)TA_NW * GQ * HD;   // [TA_NW][GQ][2]
+    if (tig == 0 && gid < GQ) {
+        wml[(warp * GQ + gid) * 2] = m;
+        wml[(warp * GQ + gid) * 2 + 1] = l;
     }
+#pragma unroll
+    for (int t = 0; t < MTL; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int g = 2 * tig + (i & 1), d = 16 * t + gid + 8 * (i >> 1);
+            if (g < GQ) wacc[((size_t)warp * GQ + g) * HD + d] = acc[t][i];
+        }
     __syncthreads();
     for (int o = tid; o < GQ * HD; o += TA_THREADS) {
         const int g = o / HD, dd = o % HD;
-        float a = red[(size_t)dd * 8 + g];
+        float M = -INFINITY;
 #pragma unroll
-        for (int h = 1; h < PH; ++h) a += red[((size_t)h * HD + dd) * 8 + g];
+        for (int w = 0; w < TA_NW; ++w) M = fmaxf(M, wml[(w * GQ + g) * 2]);
+        float a = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < TA_NW; ++w) {
+            const float mw = wml[(w * GQ + g) * 2];
+            const float f = mw == -INFINITY ? 0.f : expf(mw - M);
+            a = fmaf(f, wacc[((size_t)w * GQ + g) * HD + dd], a);
+            L = fmaf(f, wml[(w * GQ + g) * 2 + 1], L);
+        }
         part[g * (HD + 2) + dd] = a;
         if (dd == 0) {
-            part[g * (HD + 2) + HD] = p1 > p0 ? ml[g * 4] : -INFINITY;  // an empty split
-            part[g * (HD + 2) + HD + 1] = ml[g * 4 + 1];
+            part[g * (HD + 2) + HD] = p1 > p0 ? M : -INFINITY;  // an empty split
+            part[g * (HD + 2) + HD + 1] = L;
         }
     }
 }
@@ -1456,7 +1442,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) k_attn_multi(const MultiAttnPar
         const int per = (n_pos + S - 1) / S;
         const int p0 = min(n_pos, sp * per), p1 = min(n_pos, p0 + per);
         const size_t so = (size_t)p.ms->seq[v] * p.seq_stride + (size_t)kvh * p.max_ctx * HD;
-        attn_split_tc<HD, GQ>(p.q + (size_t)v * p.q_stride + (size_t)kvh * GQ * HD, p.kcache + so, p.vcache + so, p0,
+        attn_split_w<HD, GQ>(p.q + (size_t)v * p.q_stride + (size_t)kvh * GQ * HD, p.kcache + so, p.vcache + so, p0,
                               p1, smem_a, pbase + (size_t)sp * pst);
     }
     __threadfence();
@@ -1532,9 +1518,9 @@ __global__ void __launch_bounds__(TA_THREADS, 2) k_attn_multi(const MultiAttnPar
 
 template <int HD, int GQ>
 cudaError_t launch_attn_multi(const MultiAttnParams& p0, cudaStream_t s, bool pdl) {
-    // the split's scratch (attn_split_tc) or the merge's (2 x group x s_max + group floats)
+    // the split's scratch (attn_split_w) or the merge's (2 x group x s_max + group floats)
     const size_t merge = sizeof(float) * ((size_t)2 * GQ * 64 + GQ);
-    const size_t smem = (std::max(ta_smem<HD>(), merge) + 15) & ~(size_t)15;
+    const size_t smem = (std::max(tw_smem<HD>(), merge) + 15) & ~(size_t)15;
     static int per_sm[64] = {0};  // resident CTAs per SM, per device
     int dev = 0;
     cudaGetDevice(&dev);
